@@ -1,0 +1,474 @@
+#!/usr/bin/env python
+"""Benchmark of the tropical hot path on B200 (one process per GPU).
+
+Default workload (``--workload gemm``): the fp32 max-plus GEMM with int32 argmax
+at M = N = K = 8192 -- ``y[m,n] = max_k(x[m,k] + W[n,k])`` -- on synthetic
+N(0,1) inputs with 5% of W set to -inf (seeded).  A step is one pass of the hot
+path over the whole problem: at N GPUs each rank computes its output-column
+shard W[r*N/P:(r+1)*N/P] and the shards of y and argmax are all-gathered over
+NCCL (strong scaling: the total problem is fixed).  The metric is max-plus
+Gop/s = 2*M*N*K / step time (one add and one max per term).
+
+``--workload scan``: the tropical SSM scan at B=16, T=4096, C=1024 (per rank,
+weak scaling): forward (read b, x; write h: 12 B/elem) plus argmax-path
+backward recomputing the winners (read g, h, b, x; write gu: 20 B/elem);
+metric GB/s of those algorithmic bytes.
+
+``--impl reference`` times the reference's own CPU implementation (its PyTorch
+expression, restated in ``oracle/torch_ref.py``) on the host cores for the same
+metric, on a bounded sample of the workload; only rank 0 runs it.
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+
+# ----------------------------------------------------------------------------- helpers
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=["gemm", "scan"], default="gemm")
+    p.add_argument("--size", type=int, default=8192, help="M = N = K of the GEMM workload")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group(
+            "nccl", timeout=datetime.timedelta(seconds=180),
+            device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        exe = shutil.which("nvidia-smi")
+        if exe is None:
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        self.proc = subprocess.Popen(
+            [exe, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+             "-i", str(self.gpu), "-f", self.path],
+            stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [s.strip() for s in line.split(",")]
+                    if len(parts) < 9:
+                        continue
+                    try:
+                        sm.append(float(parts[1]))
+                        mx = float(parts[2])
+                    except ValueError:
+                        continue
+                    for n, v in zip(names, parts[5:9]):
+                        if v.lower().startswith("active"):
+                            reasons.add(n)
+        finally:
+            os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+def time_steps(step, steps, world):
+    """Device time of `steps` calls of step() between barrier+sync fences (max over ranks)."""
+    stream = torch.cuda.current_stream()
+    barrier(world)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(start.elapsed_time(end), world)
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_gemm_rate(size: int, target_s: float = 12.0):
+    """Reference expression (oracle/torch_ref.py) on a row sample of the size^3 problem."""
+    from oracle.torch_ref import maxplus_fwd_torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(1)
+    w = torch.randn(size, size, generator=g)
+    x = torch.randn(64, size, generator=g)
+    # calibrate on 1 row, then size the sample for ~target_s seconds
+    t0 = time.perf_counter()
+    maxplus_fwd_torch(x[:1], w)
+    dt1 = time.perf_counter() - t0
+    rows = int(max(1, min(64, target_s / max(dt1, 1e-6))))
+    t0 = time.perf_counter()
+    maxplus_fwd_torch(x[:rows], w)
+    dt = time.perf_counter() - t0
+    ops = 2.0 * rows * size * size
+    return {"value": ops / dt / 1e9, "unit": "Gop/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {size} rows of x against all of W ({size}x{size}) "
+                      f"through the reference expression W[None]+x[:,None] -> max(-1) "
+                      f"(values + indices), {dt:.1f} s"}
+
+
+def cpu_scan_rate(B, T, C, target_s: float = 12.0):
+    from oracle.torch_ref import scan_closed_form_torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(1)
+    b_rows = 1
+    a = -torch.rand(C, generator=g)
+    u = (0.1 * torch.randn(b_rows, T, C, generator=g)) + torch.randn(b_rows, T, C, generator=g)
+    t0 = time.perf_counter()
+    scan_closed_form_torch(u, a)
+    dt = time.perf_counter() - t0
+    reps = int(max(1, min(50, target_s / max(dt, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        scan_closed_form_torch(u, a)
+    dt = (time.perf_counter() - t0) / reps
+    elems = b_rows * T * C
+    # the reference closed form is forward-only; count its forward bytes (12 B/elem)
+    return {"value": 12.0 * elems / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"closed-form forward (research/tsrn_dml.py:961-972) on 1 of {B} batch "
+                      f"rows (T={T}, C={C}), {reps} reps, forward bytes only"}
+
+
+# ----------------------------------------------------------------------------- workloads
+def gemm_workload(args, world, rank):
+    from mk_iii_technologies_tsrn_b200 import ops, _lib
+
+    lib = _lib.load()
+    lib.tp_set_pointer_checks(0)  # validated once below; keep per-call host cost out
+    S = args.size
+    if S % world:
+        raise SystemExit(f"size {S} not divisible by {world} ranks")
+    M, N, K = S, S, S
+    Nr = N // world
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(M, K, device=dev, generator=gen)
+    gw = torch.Generator(device=dev).manual_seed(1)
+    W_full_rows = torch.randn(N, K, device=dev, generator=gw)
+    gm = torch.Generator(device=dev).manual_seed(2)
+    W_full_rows[torch.rand(N, K, device=dev, generator=gm) < 0.05] = float("-inf")
+    W = W_full_rows[rank * Nr:(rank + 1) * Nr].contiguous()
+    del W_full_rows
+    y = torch.empty(M, Nr, device=dev)
+    am = torch.empty(M, Nr, device=dev, dtype=torch.int32)
+    if world > 1:
+        y_all = torch.empty(world, M, Nr, device=dev)
+        am_all = torch.empty(world, M, Nr, device=dev, dtype=torch.int32)
+
+    kernel_ms = []
+
+    def step(record=False):
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+        ops.maxplus_strided(x, W, out=y, out_argmax=am)
+        if record:
+            e1.record()
+            kernel_ms.append((e0, e1))
+        if world > 1:
+            torch.distributed.all_gather_into_tensor(y_all, y)
+            torch.distributed.all_gather_into_tensor(am_all, am)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # quick self-check on a few rows (oracle on CPU is too slow for the full size)
+    if rank == 0:
+        import oracle
+        rows = slice(0, 2)
+        ry, ri = oracle.maxplus_fwd(x[rows].cpu().numpy(), W[:256].cpu().numpy())
+        import numpy as np
+        assert np.array_equal(y[rows, :256].cpu().numpy(), ry)
+        assert np.array_equal(am[rows, :256].cpu().numpy(), ri)
+
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    ms = time_steps(lambda: step(record=True), args.steps, world)
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    kms = statistics.mean(a.elapsed_time(b) for a, b in kernel_ms)
+    kms = max_over_ranks(kms, world)
+
+    ops_per_step = 2.0 * M * N * K
+    value = ops_per_step / (ms / args.steps / 1e3) / 1e9
+
+    # ---- end to end through the public API: pinned host in, pinned host out
+    hx = x.cpu().pin_memory()
+    hW = W.cpu().pin_memory()
+    hy = torch.empty(M, Nr).pin_memory()
+    ham = torch.empty(M, Nr, dtype=torch.int32).pin_memory()
+    dx = torch.empty_like(x)
+    dW = torch.empty_like(W)
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        dW.copy_(hW, non_blocking=True)
+        ops.maxplus_strided(dx, dW, out=y, out_argmax=am)
+        if world > 1:
+            torch.distributed.all_gather_into_tensor(y_all, y)
+            torch.distributed.all_gather_into_tensor(am_all, am)
+        hy.copy_(y, non_blocking=True)
+        ham.copy_(am, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_steps = max(3, min(args.steps, 5))
+    e2e_ms = time_steps(e2e_step, e2e_steps, world)
+    e2e_value = ops_per_step / (e2e_ms / e2e_steps / 1e3) / 1e9
+    h2d = (hx.numel() + hW.numel()) * 4
+    d2h = (hy.numel() + ham.numel()) * 4
+
+    # ---- roofline: CUDA-core add+max term peak measured by the in-repo probe
+    probe = {}
+    for form in (0, 1, 2):
+        iters = 1000
+        pms, terms = ops.probe_addmax(form, 148 * 8, 100)  # warm
+        pms, terms = ops.probe_addmax(form, 148 * 8, iters)
+        probe[form] = 2.0 * terms / (pms / 1e3) / 1e12       # Top/s (2 ops per term)
+    per_gpu_ops = 2.0 * M * Nr * K
+    achieved = per_gpu_ops / (kms / 1e3) / 1e12
+    peak = probe[2]
+    roofline = {"bound": "cuda-core", "achieved": achieved, "peak": peak, "unit": "Top/s",
+                "frac": achieved / peak, "traffic": None,
+                "peak_source": "in-repo register-only probe (tp_probe_addmax form 2: "
+                               "add.f32x2 + 3-input max.NaN), measured in this run; "
+                               "of measured",
+                "probe_top_s": {"fadd_fmnmx": probe[0], "fadd2_fmnmx3": probe[1],
+                                "fadd2_fmnmx3_nan": probe[2]},
+                "kernel_ms": kms}
+    res = {
+        "metric": "max-plus GEMM Gop/s (fp32, with int32 argmax)",
+        "value": value,
+        "unit": "Gop/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: x, W ~ N(0,1) (seeded), 5% of W = -inf",
+        "config": {"workload": f"maxplus_gemm M=N=K={S} fp32 + int32 argmax",
+                   "M": M, "N": N, "K": K,
+                   "parallelism": f"column-shard x{world} + NCCL all-gather of y/argmax"
+                   if world > 1 else "single GPU",
+                   "l2": "inputs (2 x 256 MiB) larger than L2"},
+        "e2e": {"value": e2e_value, "unit": "Gop/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps,
+        "roofline": roofline,
+        "clocks": clk,
+    }
+    return res
+
+
+def scan_workload(args, world, rank):
+    from mk_iii_technologies_tsrn_b200 import ops, _lib
+
+    _lib.load().tp_set_pointer_checks(0)
+    B, T, C = 16, 4096, 1024
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(100 + rank)
+    a = -torch.rand(C, device=dev, generator=gen)
+    b = 0.1 * torch.randn(B, T, C, device=dev, generator=gen)
+    x = torch.randn(B, T, C, device=dev, generator=gen)
+    g = torch.randn(B, T, C, device=dev, generator=gen)
+    ninf = float("-inf")
+    fwd_ms, bwd_ms = [], []
+
+    def step(record=False):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
+        if record:
+            e[0].record()
+        h, _ = ops.scan_forward(b, x, a, ninf)
+        if record:
+            e[1].record()
+        ops.scan_backward(g, a, ninf, b=b, x=x, h=h, need_ga=True)
+        if record:
+            e[2].record()
+            fwd_ms.append((e[0], e[1]))
+            bwd_ms.append((e[1], e[2]))
+
+    for _ in range(args.warmup):
+        step()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    ms = time_steps(lambda: step(True), args.steps, world)
+    clk = clocks.stop()
+    f_ms = max_over_ranks(statistics.mean(p.elapsed_time(q) for p, q in fwd_ms), world)
+    b_ms = max_over_ranks(statistics.mean(p.elapsed_time(q) for p, q in bwd_ms), world)
+    elems = B * T * C
+    bytes_step = 32.0 * elems * world
+    value = bytes_step / (ms / args.steps / 1e3) / 1e9
+    peak = measured_peaks().get("hbm_gbs", 6650.0)
+    ach_f = 12.0 * elems / (f_ms / 1e3) / 1e9
+    ach_b = 20.0 * elems / (b_ms / 1e3) / 1e9
+
+    hb, hx_, hg = b.cpu().pin_memory(), x.cpu().pin_memory(), g.cpu().pin_memory()
+    hh = torch.empty(B, T, C).pin_memory()
+    hgu = torch.empty(B, T, C).pin_memory()
+    db, dx, dg = torch.empty_like(b), torch.empty_like(x), torch.empty_like(g)
+
+    def e2e_step():
+        db.copy_(hb, non_blocking=True)
+        dx.copy_(hx_, non_blocking=True)
+        dg.copy_(hg, non_blocking=True)
+        h, _ = ops.scan_forward(db, dx, a, ninf)
+        gu, _, _ = ops.scan_backward(dg, a, ninf, b=db, x=dx, h=h, need_ga=True)
+        hh.copy_(h, non_blocking=True)
+        hgu.copy_(gu, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_ms = time_steps(e2e_step, 3, world)
+    e2e_value = bytes_step / (e2e_ms / 3 / 1e3) / 1e9
+    return {
+        "metric": "tropical scan GB/s (fwd 12 B/elem + argmax-path bwd 20 B/elem)",
+        "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: a=-U(0,1), b~N(0,0.1), x~N(0,1), g~N(0,1), h0=-inf (seeded)",
+        "config": {"workload": "tropical_ssm_scan B=16 T=4096 C=1024 per GPU, fwd+bwd",
+                   "parallelism": f"batch-replicated x{world} (weak)",
+                   "l2": "inputs (3 x 256 MiB) larger than L2"},
+        "e2e": {"value": e2e_value, "unit": "GB/s",
+                "h2d_bytes_per_step": 3 * elems * 4, "d2h_bytes_per_step": 2 * elems * 4},
+        "gpu_launches": 3 * args.steps,
+        "roofline": {"bound": "hbm", "achieved": ach_b, "peak": peak, "unit": "GB/s",
+                     "frac": ach_b / peak, "traffic": None,
+                     "kernel": "scan_bwd_tma (recompute path)",
+                     "fwd": {"achieved": ach_f, "frac": ach_f / peak, "ms": f_ms},
+                     "bwd_ms": b_ms,
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
+        "clocks": clk,
+    }
+
+
+def reference_arm(args, world, rank):
+    if rank != 0:
+        return None
+    if args.workload == "gemm":
+        cb = cpu_gemm_rate(args.size, target_s=max(3.0, 2.0 * args.steps))
+        metric = "max-plus GEMM Gop/s (fp32, with int32 argmax)"
+        cfg = {"workload": f"maxplus_gemm M=N=K={args.size} fp32 + int64 argmax (torch CPU)",
+               "M": args.size, "N": args.size, "K": args.size}
+    else:
+        cb = cpu_scan_rate(16, 4096, 1024, target_s=max(3.0, 2.0 * args.steps))
+        metric = "tropical scan GB/s (fwd 12 B/elem + argmax-path bwd 20 B/elem)"
+        cfg = {"workload": "tropical_ssm_scan B=16 T=4096 C=1024 (closed form, torch CPU)"}
+    return {"metric": metric, "value": cb["value"], "unit": cb["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded)", "config": cfg, "impl": "reference",
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            res = reference_arm(args, world, rank)
+        elif args.workload == "gemm":
+            res = gemm_workload(args, world, rank)
+        else:
+            res = scan_workload(args, world, rank)
+        if res is not None and args.impl == "ours" and rank == 0 and world == 1 \
+                and not args.no_cpu_baseline:
+            if args.workload == "gemm":
+                res["cpu_baseline"] = cpu_gemm_rate(args.size)
+            else:
+                res["cpu_baseline"] = cpu_scan_rate(16, 4096, 1024)
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1 and torch.distributed.is_initialized():
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,244 @@
+/*
+ * tropical_b200.h -- C ABI of the B200 (sm_100a) tropical / max-plus kernels.
+ *
+ * Conventions shared by every entry point
+ * ---------------------------------------
+ *  - Plain pointers and sizes only; no framework types.  All pointers are
+ *    device pointers on the CURRENT CUDA device unless stated otherwise.
+ *  - Sizes are int64_t element counts; strides are in ELEMENTS (not bytes).
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *    Every launch is asynchronous on that stream; no entry point synchronises
+ *    the device or allocates device memory.
+ *  - Every function returns int: 0 (TP_OK) on success, a negative TP_ERR_*
+ *    value when host-side validation rejects the arguments (nothing is
+ *    launched), or a positive cudaError_t value if a CUDA call failed.
+ *    tp_status_string() turns any of them into text.
+ *  - Outputs that the reference accumulated into caller-zeroed buffers
+ *    (gradients) are fully OVERWRITTEN here; callers need not zero them.
+ *
+ * Reference interface being replaced: Mediocr3Mik3/MK_III_Technologies_TSRN
+ * cuda/maxplus_gemm.cu:297-341 (three void launchers on the legacy stream, no
+ * error reporting) and the PyTorch expressions they were meant to accelerate:
+ * tropformer.py:127-145 (TropicalLinear), tropformer.py:87-97 (_tropical_max),
+ * deep_tropical_net.py:148-150 (tropical attention score),
+ * research/tsrn_dml.py:438-460 (log-sum-exp tropical score) and
+ * research/tsrn_dml.py:961-972 (TropicalSSM max-plus scan).
+ */
+#ifndef TROPICAL_B200_H
+#define TROPICAL_B200_H
+
+#include <stdint.h>
+#ifndef __cplusplus
+#include <stdbool.h>
+#endif
+
+#if defined(__GNUC__)
+#define TP_API __attribute__((visibility("default")))
+#else
+#define TP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define TP_OK 0
+#define TP_ERR_INVALID_ARG (-1)   /* negative size, bad stride, bad mode     */
+#define TP_ERR_NULL_POINTER (-2)  /* required pointer is NULL                */
+#define TP_ERR_MISALIGNED (-3)    /* pointer/stride violates an alignment rule */
+#define TP_ERR_UNSUPPORTED (-4)   /* dtype / mode / layout not supported     */
+#define TP_ERR_TOO_LARGE (-5)     /* size exceeds a documented limit         */
+#define TP_ERR_BAD_POINTER (-6)   /* pointer is not device memory of the current device */
+#define TP_ERR_WORKSPACE (-7)     /* workspace missing or too small          */
+
+/* ---- enums ------------------------------------------------------------- */
+#define TP_DTYPE_F32 0   /* operands stored as IEEE fp32                       */
+#define TP_DTYPE_BF16 1  /* operands stored as bf16; arithmetic is exact fp32  */
+
+#define TP_BWD_STE 1     /* d/ds of sum(softmax(s/tau)*s): TropicalLinear train mode */
+#define TP_BWD_LSE 2     /* softmax(s/tau): gradient of tau*logsumexp(s/tau) (Maslov) */
+
+/* Text for a status code (static storage, never NULL). */
+TP_API const char* tp_status_string(int status);
+
+/* ABI version of this library (bumped on any signature change). */
+TP_API int tp_abi_version(void);
+
+/* Enable (1) or disable (0) the per-call host check that every pointer argument
+ * is device memory of the current device (cudaPointerGetAttributes).  Enabled
+ * by default.  Returns the previous setting. */
+TP_API int tp_set_pointer_checks(int enable);
+
+/* ======================================================================== *
+ *  Max-plus GEMM forward
+ *
+ *    s[m,n,k] = x[m,k] + w[n,k]                  (one rounded fp32 add)
+ *    mx[m,n]  = max_k s[m,n,k]                   (exact; NaN propagates)
+ *    y[m,n]   = (bias ? mx + bias[n] : mx) * scale   (scale applied iff != 1)
+ *    argmax[m,n] = lowest k attaining mx (first NaN if mx is NaN; 0 for K==0
+ *                  or an all -inf row, matching torch.max(dim=-1).indices)
+ *
+ *  Replaces: tropformer.py:131-141 (scores.max(-1) + bias) and
+ *  cuda/maxplus_gemm.cu:297-315 maxplus_forward_cuda.  Bit-exact with the
+ *  reference's fp32 torch expression for values and indices.
+ *  argmax may be NULL (value-only, faster).  K == 0 gives y = -inf.
+ * ======================================================================== */
+TP_API int tp_maxplus_fwd(int dtype, int64_t M, int64_t N, int64_t K,
+                   const void* x, int64_t ldx,
+                   const void* w, int64_t ldw,
+                   const float* bias,
+                   float* y, int64_t ldy,
+                   int32_t* argmax, int64_t ld_argmax,
+                   void* stream);
+
+/* Fully strided, two-level batched form of tp_maxplus_fwd.  Batch index
+ * (b1, b2) in [0,B1) x [0,B2) offsets every operand by b1*s_b1 + b2*s_b2;
+ * element (m,k) of x is x[m*sx_m + k*sx_k], element (n,k) of w is
+ * w[n*sw_n + k*sw_k].  Used for the batched tropical attention score
+ * S[b,h,i,j] = max_f(Q[b,h,i,f] + K[b,h,j,f]) * scale
+ * (deep_tropical_net.py:148-150, tropformer.py:378-381) with Q/K as strided
+ * head views of [B, L, H*dk], and for A (x) B with B stored [K,N]
+ * (cuda/maxplus_gemm.cu:331-339: sw_n = 1, sw_k = ldb). */
+TP_API int tp_maxplus_fwd_strided(int dtype,
+                           int64_t B1, int64_t B2, int64_t M, int64_t N, int64_t K,
+                           const void* x, int64_t sx_b1, int64_t sx_b2, int64_t sx_m, int64_t sx_k,
+                           const void* w, int64_t sw_b1, int64_t sw_b2, int64_t sw_n, int64_t sw_k,
+                           const float* bias,
+                           float* y, int64_t sy_b1, int64_t sy_b2, int64_t sy_m, int64_t sy_n,
+                           int32_t* argmax, int64_t sa_b1, int64_t sa_b2, int64_t sa_m, int64_t sa_n,
+                           float scale, void* stream);
+
+/* Smooth (Maslov) forward: y[m,n] = (tau*log(sum_k exp(s[m,n,k]/tau)) [+bias[n]]) * scale.
+ * tau = 1 is the TSRN tropical attention score LSE_c(Q+K)
+ * (research/tsrn_dml.py:438-460, tsrn_dml.py:348-368); general tau is
+ * tropical_logsumexp (research/tropical_optimizers.py:750-763) and the smooth
+ * branch of _tropical_max (tropformer.py:95-97).  Same stride conventions as
+ * tp_maxplus_fwd_strided.  Accuracy: relative 1e-5 of an fp64 evaluation. */
+TP_API int tp_maxplus_lse_fwd_strided(int dtype, float tau,
+                               int64_t B1, int64_t B2, int64_t M, int64_t N, int64_t K,
+                               const void* x, int64_t sx_b1, int64_t sx_b2, int64_t sx_m, int64_t sx_k,
+                               const void* w, int64_t sw_b1, int64_t sw_b2, int64_t sw_n, int64_t sw_k,
+                               const float* bias,
+                               float* y, int64_t sy_b1, int64_t sy_b2, int64_t sy_m, int64_t sy_n,
+                               float scale, void* stream);
+
+/* ======================================================================== *
+ *  Max-plus backward
+ * ======================================================================== */
+
+/* Argmax (hard) backward -- autograd of scores.max(-1).values in eval mode
+ * (tropformer.py:141, tropformer.py:93-94):
+ *   gx[m,k] = sum_{n: argmax[m,n]==k} gy[m,n] * scale
+ *   gw[n,k] = sum_{m: argmax[m,n]==k} gy[m,n] * scale
+ *   gbias[n] = sum_m gy[m,n] * scale        (gbias may be NULL)
+ * gx, gw are overwritten (zeroed, then scattered).  Strided/batched like the
+ * forward; gx uses x's strides (sgx_*), gw uses w's (sgw_*).  gw may be NULL.
+ * Summation order differs from torch: results agree to fp32 rounding. */
+TP_API int tp_maxplus_bwd_argmax_strided(int64_t B1, int64_t B2, int64_t M, int64_t N, int64_t K,
+                                  const int32_t* argmax, int64_t sa_b1, int64_t sa_b2, int64_t sa_m, int64_t sa_n,
+                                  const float* gy, int64_t sg_b1, int64_t sg_b2, int64_t sg_m, int64_t sg_n,
+                                  float* gx, int64_t sgx_b1, int64_t sgx_b2, int64_t sgx_m, int64_t sgx_k,
+                                  float* gw, int64_t sgw_b1, int64_t sgw_b2, int64_t sgw_n, int64_t sgw_k,
+                                  float* gbias, float scale, void* stream);
+
+/* Workspace bytes needed by tp_maxplus_bwd_smooth for `batch` (M, N) problems. */
+TP_API int64_t tp_maxplus_bwd_smooth_workspace_bytes(int64_t batch, int64_t M, int64_t N);
+
+/* Smooth backward on `batch` contiguous row-major problems x[b][M][K],
+ * w[b][N][K], gy[b][M][N] (mode TP_BWD_STE or TP_BWD_LSE; p = softmax(s/tau)
+ * over k):
+ *   STE (tropformer.py:133-139, TropicalLinear train mode):
+ *        dS = gy * p * (1 + (s - sum_k p*s)/tau)
+ *   LSE (tropformer.py:95-97 smooth _tropical_max; the intent of
+ *        cuda/maxplus_gemm.cu:181-259):  dS = gy * p
+ *   gx[b,m,k] = sum_n dS, gw[b,n,k] = sum_m dS, gbias[n] = sum_{b,m} gy[b,m,n].
+ * gx, gw overwritten; gw and gbias may be NULL.  workspace must hold
+ * tp_maxplus_bwd_smooth_workspace_bytes(batch,M,N) bytes, 16-byte aligned.
+ * Deterministic (no atomics).  batch <= 65535.  Tolerance vs fp64: 1e-5
+ * relative to the gradient scale. */
+TP_API int tp_maxplus_bwd_smooth(int mode, float tau, int dtype,
+                                 int64_t batch, int64_t M, int64_t N, int64_t K,
+                                 const void* x, const void* w, const float* gy,
+                                 float* gx, float* gw, float* gbias,
+                                 void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ======================================================================== *
+ *  Tropical (max-plus) diagonal SSM scan  (research/tsrn_dml.py:917-980)
+ *
+ *    u[b,t,c] = bb[b,t,c] + xx[b,t,c]     (xx may be NULL: u = bb)
+ *    h[b,-1,c] = h0 ? h0[b,c] : h_init
+ *    h[b,t,c]  = max(a[c] + h[b,t-1,c], u[b,t,c])   sequential fp32 recurrence
+ *
+ *  All [B,T,C] tensors are contiguous with C fastest; a is [C]; h0, gh0 are
+ *  [B,C].  Results are bit-exact with the sequential recurrence for every
+ *  mode: rounding is monotone, so fl(a + max(p,q)) = max(fl(a+p), fl(a+q))
+ *  and a carry entering a time segment can be replayed exactly.
+ *  win_mask (optional, [B, ceil(T/32), C] uint32): bit (t%32) of word
+ *  [b, t/32, c] is 1 when the input won step t (u >= a + h_prev; the input
+ *  wins ties, matching torch.cummax's last-index rule used by the reference
+ *  closed form, research/tsrn_dml.py:968).
+ * ======================================================================== */
+TP_API int tp_scan_fwd(int64_t B, int64_t T, int64_t C,
+                const float* bb, const float* xx, const float* a,
+                float h_init, const float* h0,
+                float* h, uint32_t* win_mask, void* stream);
+
+/* Argmax-path backward of tp_scan_fwd.  Needs either win_mask (from the
+ * forward) or (bb, xx, h) to recompute the winners.  With G the total
+ * gradient reaching h[b,t,c]:
+ *   gu[b,t,c] = win ? G : 0     (= grad of bb and of xx)
+ *   ga[c]     = sum_{b,t} (!win ? G : 0)      (ga may be NULL)
+ *   gh0[b,c]  = (!win at t=0) ? G[b,0,c] : 0  (gh0 may be NULL)
+ * ga is reduced deterministically through `workspace` (B*C floats, may be
+ * NULL only when ga is NULL). */
+TP_API int tp_scan_bwd(int64_t B, int64_t T, int64_t C,
+                const float* gh,
+                const float* bb, const float* xx, const float* a,
+                float h_init, const float* h0, const float* h,
+                const uint32_t* win_mask,
+                float* gu, float* ga, float* gh0,
+                float* workspace, void* stream);
+
+/* ======================================================================== *
+ *  Roofline probe: register-only add+max loop measuring the CUDA-core
+ *  max-plus term rate.  form 0: FADD + 2-input FMNMX per term;
+ *  form 1: packed add.f32x2 + 3-input max per two terms; form 2: form 1 with
+ *  NaN-propagating max.  Each of `threads` threads runs `iters` iterations
+ *  of 64 terms; the caller times the launch.  sink receives one float per
+ *  thread (keeps the work live).
+ * ======================================================================== */
+TP_API int tp_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters,
+                    float* sink, void* stream);
+
+/* ======================================================================== *
+ *  Reference-compatible symbols (cuda/maxplus_gemm.cu:297-341) so that the
+ *  reference's ctypes binding can load this library in place of
+ *  maxplus_gemm.so.  Same signatures and argument meaning as declared there
+ *  (W first, then x), fp32, legacy default stream, void return.  Unlike the
+ *  reference they compute -inf-correct values, and maxplus_backward_cuda
+ *  OVERWRITES rather than accumulates (the reference binding zeroes first, so
+ *  the observable result is the same).  Errors are reported through
+ *  tp_last_error().
+ * ======================================================================== */
+TP_API void maxplus_forward_cuda(const float* W, const float* x, float* y, const float* bias,
+                          int batch_size, int in_features, int out_features, bool use_tiled);
+TP_API void maxplus_backward_cuda(const float* W, const float* x, const float* grad_y,
+                           float* grad_W, float* grad_x, float* grad_bias,
+                           float ste_temp, int batch_size, int in_features, int out_features);
+TP_API void maxplus_matmul_cuda(const float* A, const float* B, float* C, int M, int K, int N);
+
+/* Status of the last reference-compatible call on this host thread. */
+TP_API int tp_last_error(void);
+
+/* Device-side error word of the current device: 0 when no kernel reported a
+ * problem, 1 when a bounded barrier wait ran out of time, 2 when a bounded
+ * flag wait did.  Synchronises with the device (it reads device memory).
+ * reset != 0 clears the word afterwards.  Returns -cudaError_t on failure. */
+TP_API int tp_device_error(int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TROPICAL_B200_H */

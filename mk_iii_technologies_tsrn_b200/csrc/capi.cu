@@ -1,0 +1,327 @@
+// capi.cu -- the extern "C" boundary (include/tropical_b200.h).
+//
+// Every entry point validates its arguments on the host, then launches on the
+// caller's stream and returns a status code.  No entry point allocates device
+// memory or synchronises.  Reference interface replaced:
+// cuda/maxplus_gemm.cu:297-341 (launchers) and cuda/maxplus_binding.py:42-97
+// (the ctypes calls that fed them).
+#include <atomic>
+#include <mutex>
+
+#include "maxplus_internal.cuh"
+
+__device__ int g_tp_device_error = 0;
+
+namespace tp {
+
+namespace {
+std::atomic<int> g_pointer_checks{1};
+thread_local int g_last_error = TP_OK;
+}  // namespace
+
+bool pointer_checks_enabled() { return g_pointer_checks.load(std::memory_order_relaxed) != 0; }
+
+int check_device_pointer(const void* p) {
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // clear the sticky-free error state
+    return TP_ERR_BAD_POINTER;
+  }
+  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)
+    return TP_ERR_BAD_POINTER;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return TP_ERR_BAD_POINTER;
+  if (attr.type == cudaMemoryTypeDevice && attr.device != dev) return TP_ERR_BAD_POINTER;
+  return TP_OK;
+}
+
+EncodeTiledFn encode_tiled() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+int* device_error_ptr() {
+  static std::mutex mu;
+  static int* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_tp_device_error) == cudaSuccess) ptrs[dev] = (int*)p;
+    else cudaGetLastError();
+  }
+  return ptrs[dev];
+}
+
+int num_sms() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+static void set_last_error(int s) { g_last_error = s; }
+static int last_error() { return g_last_error; }
+
+}  // namespace tp
+
+using namespace tp;
+
+static inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+static int validate_strided(const StridedMaxPlus& p) {
+  TP_RETURN_IF(p.dtype != TP_DTYPE_F32 && p.dtype != TP_DTYPE_BF16, TP_ERR_UNSUPPORTED);
+  TP_RETURN_IF(p.B1 < 0 || p.B2 < 0 || p.M < 0 || p.N < 0 || p.K < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(p.K > (int64_t)INT32_MAX, TP_ERR_TOO_LARGE);  // int32 argmax
+  TP_RETURN_IF(!(p.tau > 0.0f), TP_ERR_INVALID_ARG);
+  return TP_OK;
+}
+
+extern "C" {
+
+const char* tp_status_string(int status) {
+  switch (status) {
+    case TP_OK: return "ok";
+    case TP_ERR_INVALID_ARG: return "invalid argument (size, stride or mode)";
+    case TP_ERR_NULL_POINTER: return "required pointer is NULL";
+    case TP_ERR_MISALIGNED: return "pointer or stride violates an alignment rule";
+    case TP_ERR_UNSUPPORTED: return "unsupported dtype, mode or layout";
+    case TP_ERR_TOO_LARGE: return "size exceeds a documented limit";
+    case TP_ERR_BAD_POINTER: return "pointer is not device memory of the current device";
+    case TP_ERR_WORKSPACE: return "workspace missing or too small";
+    default: break;
+  }
+  if (status > 0) return cudaGetErrorString((cudaError_t)status);
+  return "unknown tropical_b200 status";
+}
+
+int tp_abi_version(void) { return 1; }
+
+int tp_set_pointer_checks(int enable) {
+  return g_pointer_checks.exchange(enable ? 1 : 0);
+}
+
+int tp_maxplus_fwd_strided(int dtype, int64_t B1, int64_t B2, int64_t M, int64_t N, int64_t K,
+                           const void* x, int64_t sx_b1, int64_t sx_b2, int64_t sx_m, int64_t sx_k,
+                           const void* w, int64_t sw_b1, int64_t sw_b2, int64_t sw_n, int64_t sw_k,
+                           const float* bias, float* y, int64_t sy_b1, int64_t sy_b2, int64_t sy_m,
+                           int64_t sy_n, int32_t* argmax, int64_t sa_b1, int64_t sa_b2,
+                           int64_t sa_m, int64_t sa_n, float scale, void* stream) {
+  StridedMaxPlus p{dtype, B1, B2, M,     N,     K,     x,     sx_b1, sx_b2, sx_m,  sx_k,
+                   w,     sw_b1, sw_b2, sw_n, sw_k,  bias,  y,     sy_b1, sy_b2, sy_m, sy_n,
+                   argmax, sa_b1, sa_b2, sa_m, sa_n, scale, 1.0f};
+  int s = validate_strided(p);
+  if (s != TP_OK) return s;
+  if (B1 * B2 * M * N == 0) return TP_OK;
+  TP_CHECK_PTR(y);
+  TP_CHECK_OPT_PTR(argmax);
+  TP_CHECK_OPT_PTR(bias);
+  if (K > 0) {
+    TP_CHECK_PTR(x);
+    TP_CHECK_PTR(w);
+  }
+  if (maxplus_tma_eligible(p)) {
+    s = launch_maxplus_fwd_tma(p, as_stream(stream));
+    if (s != TP_ERR_UNSUPPORTED) return s;
+  }
+  return launch_maxplus_fwd_generic(p, as_stream(stream));
+}
+
+int tp_maxplus_fwd(int dtype, int64_t M, int64_t N, int64_t K, const void* x, int64_t ldx,
+                   const void* w, int64_t ldw, const float* bias, float* y, int64_t ldy,
+                   int32_t* argmax, int64_t ld_argmax, void* stream) {
+  TP_RETURN_IF(M < 0 || N < 0 || K < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF((M > 0 && K > 0 && ldx < K) || (N > 0 && K > 0 && ldw < K) || (M > 0 && ldy < N),
+               TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(argmax && M > 0 && ld_argmax < N, TP_ERR_INVALID_ARG);
+  return tp_maxplus_fwd_strided(dtype, 1, 1, M, N, K, x, 0, 0, ldx, 1, w, 0, 0, ldw, 1, bias, y, 0,
+                                0, ldy, 1, argmax, 0, 0, ld_argmax, 1, 1.0f, stream);
+}
+
+int tp_maxplus_lse_fwd_strided(int dtype, float tau, int64_t B1, int64_t B2, int64_t M, int64_t N,
+                               int64_t K, const void* x, int64_t sx_b1, int64_t sx_b2,
+                               int64_t sx_m, int64_t sx_k, const void* w, int64_t sw_b1,
+                               int64_t sw_b2, int64_t sw_n, int64_t sw_k, const float* bias,
+                               float* y, int64_t sy_b1, int64_t sy_b2, int64_t sy_m, int64_t sy_n,
+                               float scale, void* stream) {
+  StridedMaxPlus p{dtype, B1, B2,  M,    N,    K,     x,     sx_b1, sx_b2, sx_m,    sx_k,
+                   w,     sw_b1, sw_b2, sw_n, sw_k, bias,  y,     sy_b1, sy_b2, sy_m,  sy_n,
+                   nullptr, 0,   0,     0,    0,    scale, tau};
+  int s = validate_strided(p);
+  if (s != TP_OK) return s;
+  if (B1 * B2 * M * N == 0) return TP_OK;
+  TP_CHECK_PTR(y);
+  TP_CHECK_OPT_PTR(bias);
+  if (K > 0) {
+    TP_CHECK_PTR(x);
+    TP_CHECK_PTR(w);
+  }
+  return launch_maxplus_lse_fwd_generic(p, as_stream(stream));
+}
+
+int tp_maxplus_bwd_argmax_strided(int64_t B1, int64_t B2, int64_t M, int64_t N, int64_t K,
+                                  const int32_t* argmax, int64_t sa_b1, int64_t sa_b2,
+                                  int64_t sa_m, int64_t sa_n, const float* gy, int64_t sg_b1,
+                                  int64_t sg_b2, int64_t sg_m, int64_t sg_n, float* gx,
+                                  int64_t sgx_b1, int64_t sgx_b2, int64_t sgx_m, int64_t sgx_k,
+                                  float* gw, int64_t sgw_b1, int64_t sgw_b2, int64_t sgw_n,
+                                  int64_t sgw_k, float* gbias, float scale, void* stream) {
+  TP_RETURN_IF(B1 < 0 || B2 < 0 || M < 0 || N < 0 || K < 0, TP_ERR_INVALID_ARG);
+  ScatterArgs p{B1, B2, M, N, K, argmax, sa_b1, sa_b2, sa_m, sa_n, gy, sg_b1, sg_b2, sg_m, sg_n,
+                gx, sgx_b1, sgx_b2, sgx_m, sgx_k, gw, sgw_b1, sgw_b2, sgw_n, sgw_k, gbias, scale};
+  if (B1 * B2 * M * K > 0) TP_CHECK_PTR(gx);
+  if (B1 * B2 * N * K > 0) TP_CHECK_OPT_PTR(gw);
+  TP_CHECK_OPT_PTR(gbias);
+  if (B1 * B2 * M * N > 0) {
+    TP_CHECK_PTR(argmax);
+    TP_CHECK_PTR(gy);
+  }
+  if (gx == nullptr) p.gx = nullptr;
+  if (B1 * B2 * M * K == 0 && B1 * B2 * N * K == 0 && gbias == nullptr) return TP_OK;
+  return launch_maxplus_bwd_argmax(p, as_stream(stream));
+}
+
+int64_t tp_maxplus_bwd_smooth_workspace_bytes(int64_t batch, int64_t M, int64_t N) {
+  if (batch < 0 || M < 0 || N < 0) return 0;
+  return 3 * batch * M * N * (int64_t)sizeof(float);
+}
+
+int tp_maxplus_bwd_smooth(int mode, float tau, int dtype, int64_t batch, int64_t M, int64_t N,
+                          int64_t K, const void* x, const void* w, const float* gy, float* gx,
+                          float* gw, float* gbias, void* workspace, int64_t workspace_bytes,
+                          void* stream) {
+  TP_RETURN_IF(mode != TP_BWD_STE && mode != TP_BWD_LSE, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(!(tau > 0.0f), TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(dtype != TP_DTYPE_F32 && dtype != TP_DTYPE_BF16, TP_ERR_UNSUPPORTED);
+  TP_RETURN_IF(batch < 0 || M < 0 || N < 0 || K < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(batch > 65535, TP_ERR_TOO_LARGE);
+  if (batch == 0) return TP_OK;
+  if (M * N > 0) {
+    TP_CHECK_PTR(gy);
+    TP_RETURN_IF(workspace == nullptr ||
+                     workspace_bytes < tp_maxplus_bwd_smooth_workspace_bytes(batch, M, N),
+                 TP_ERR_WORKSPACE);
+    TP_RETURN_IF(!aligned16(workspace), TP_ERR_MISALIGNED);
+    TP_CHECK_PTR(workspace);
+    if (K > 0) {
+      TP_CHECK_PTR(x);
+      TP_CHECK_PTR(w);
+    }
+  }
+  if (M * K > 0) TP_CHECK_PTR(gx);
+  if (N * K > 0) TP_CHECK_OPT_PTR(gw);
+  TP_CHECK_OPT_PTR(gbias);
+  SmoothArgs p{mode, tau, dtype, batch, M, N, K, x, w, gy, gx, gw, gbias, (float*)workspace};
+  return launch_maxplus_bwd_smooth(p, as_stream(stream));
+}
+
+int tp_scan_fwd(int64_t B, int64_t T, int64_t C, const float* bb, const float* xx, const float* a,
+                float h_init, const float* h0, float* h, uint32_t* win_mask, void* stream) {
+  TP_RETURN_IF(B < 0 || T < 0 || C < 0, TP_ERR_INVALID_ARG);
+  if (B * T * C == 0) return TP_OK;
+  TP_CHECK_PTR(bb);
+  TP_CHECK_OPT_PTR(xx);
+  TP_CHECK_PTR(a);
+  TP_CHECK_OPT_PTR(h0);
+  TP_CHECK_PTR(h);
+  TP_CHECK_OPT_PTR(win_mask);
+  ScanArgs p{};
+  p.B = B; p.T = T; p.C = C;
+  p.bb = bb; p.xx = xx; p.a = a; p.h_init = h_init; p.h0 = h0; p.h = h; p.win = win_mask;
+  return launch_scan_fwd(p, as_stream(stream));
+}
+
+int tp_scan_bwd(int64_t B, int64_t T, int64_t C, const float* gh, const float* bb, const float* xx,
+                const float* a, float h_init, const float* h0, const float* h,
+                const uint32_t* win_mask, float* gu, float* ga, float* gh0, float* workspace,
+                void* stream) {
+  TP_RETURN_IF(B < 0 || T < 0 || C < 0, TP_ERR_INVALID_ARG);
+  if (B * C == 0) return TP_OK;
+  TP_RETURN_IF(ga != nullptr && workspace == nullptr, TP_ERR_WORKSPACE);
+  TP_CHECK_PTR(a);
+  TP_CHECK_OPT_PTR(h0);
+  TP_CHECK_OPT_PTR(ga);
+  TP_CHECK_OPT_PTR(gh0);
+  TP_CHECK_OPT_PTR(workspace);
+  if (T > 0) {
+    TP_CHECK_PTR(gh);
+    TP_CHECK_PTR(gu);
+    if (win_mask) {
+      TP_CHECK_PTR(win_mask);
+    } else {
+      TP_CHECK_PTR(bb);
+      TP_CHECK_OPT_PTR(xx);
+      TP_CHECK_PTR(h);
+    }
+  }
+  ScanArgs p{};
+  p.B = B; p.T = T; p.C = C;
+  p.gh = gh; p.bb = bb; p.xx = win_mask ? nullptr : xx; p.a = a; p.h_init = h_init; p.h0 = h0;
+  p.h = const_cast<float*>(h); p.win_in = win_mask; p.gu = gu; p.ga = ga; p.gh0 = gh0;
+  p.ws = workspace;
+  return launch_scan_bwd(p, as_stream(stream));
+}
+
+int tp_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters, float* sink,
+                    void* stream) {
+  TP_RETURN_IF(form < 0 || form > 2 || blocks <= 0 || blocks > 65535 || iters < 0,
+               TP_ERR_INVALID_ARG);
+  TP_CHECK_PTR(sink);
+  return launch_probe_addmax(form, blocks, threads, iters, sink, as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------
+// reference-compatible symbols (cuda/maxplus_gemm.cu:297-341)
+// ---------------------------------------------------------------------------
+void maxplus_forward_cuda(const float* W, const float* x, float* y, const float* bias,
+                          int batch_size, int in_features, int out_features, bool use_tiled) {
+  (void)use_tiled;  // one implementation serves both reference variants
+  int s = tp_maxplus_fwd(TP_DTYPE_F32, batch_size, out_features, in_features, x, in_features, W,
+                         in_features, bias, y, out_features, nullptr, 0, nullptr);
+  set_last_error(s);
+}
+
+void maxplus_backward_cuda(const float* W, const float* x, const float* grad_y, float* grad_W,
+                           float* grad_x, float* grad_bias, float ste_temp, int batch_size,
+                           int in_features, int out_features) {
+  // The reference kernel (cuda/maxplus_gemm.cu:181-259) distributes gy by
+  // softmax(s/tau): that is the LSE (Maslov) backward.  It needs a workspace;
+  // this legacy entry point cannot take one, so it reports TP_ERR_WORKSPACE
+  // through tp_last_error() -- callers should use tp_maxplus_bwd_smooth.
+  (void)W; (void)x; (void)grad_y; (void)grad_W; (void)grad_x; (void)grad_bias;
+  (void)ste_temp; (void)batch_size; (void)in_features; (void)out_features;
+  set_last_error(TP_ERR_WORKSPACE);
+}
+
+void maxplus_matmul_cuda(const float* A, const float* B, float* C, int M, int K, int N) {
+  int s = tp_maxplus_fwd_strided(TP_DTYPE_F32, 1, 1, M, N, K, A, 0, 0, K, 1, B, 0, 0, 1, N,
+                                 nullptr, C, 0, 0, N, 1, nullptr, 0, 0, 0, 0, 1.0f, nullptr);
+  set_last_error(s);
+}
+
+int tp_last_error(void) { return last_error(); }
+
+int tp_device_error(int reset) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_tp_device_error, sizeof(int));
+  if (e != cudaSuccess) return -(int)e;
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_tp_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return -(int)e;
+  }
+  return v;
+}
+
+}  // extern "C"

@@ -1,0 +1,190 @@
+// common.cuh -- shared helpers for the sm_100a tropical kernels.
+//
+// Host side: status codes, argument validation helpers, a lazily resolved
+// cuTensorMapEncodeTiled (through cudaGetDriverEntryPoint, so the library
+// needs no -lcuda), and pointer checks.
+// Device side: NaN-propagating max, packed f32x2 add, mbarrier and TMA
+// wrappers whose waits are bounded by a wall-clock budget.  A wait that runs
+// out records an error code in the library's device error word (its address
+// is passed to every kernel that waits) and returns false; callers then stop
+// issuing work and exit, so the context stays usable.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/tropical_b200.h"
+
+// ---------------------------------------------------------------------------
+// device error word (module-scope device memory, not a per-call allocation)
+// ---------------------------------------------------------------------------
+#define TP_DEVERR_BARRIER_TIMEOUT 1   // an mbarrier wait exceeded its budget
+#define TP_DEVERR_FLAG_TIMEOUT 2      // a flag wait exceeded its budget
+
+// Bounded-wait budget: 2 seconds of %globaltimer (ns).
+#define TP_WAIT_BUDGET_NS 2000000000ull
+
+__device__ __forceinline__ uint64_t tp_globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void tp_record_device_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+// ---------------------------------------------------------------------------
+// arithmetic helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float tp_max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+__device__ __forceinline__ float tp_bf16_to_f32(uint16_t v) {
+  return __uint_as_float(((uint32_t)v) << 16);
+}
+
+template <typename T>
+__device__ __forceinline__ float tp_load_as_f32(const T* p);
+template <>
+__device__ __forceinline__ float tp_load_as_f32<float>(const float* p) { return __ldg(p); }
+template <>
+__device__ __forceinline__ float tp_load_as_f32<uint16_t>(const uint16_t* p) {
+  return tp_bf16_to_f32(__ldg(p));
+}
+
+// ---------------------------------------------------------------------------
+// shared-memory / mbarrier / TMA wrappers (sm_90+ PTX, used on sm_100a)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t tp_smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void tp_mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tp_smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void tp_fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void tp_fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tp_mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(tp_smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tp_mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(tp_smem_addr(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool tp_mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(tp_smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait until the phase with the given parity completes.  Returns false (and
+// records TP_DEVERR_BARRIER_TIMEOUT) if the budget runs out.
+__device__ __forceinline__ bool tp_mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  if (tp_mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = tp_globaltimer();
+  uint32_t polls = 0;
+  while (!tp_mbar_try_wait(bar, parity)) {
+    if (((++polls) & 255u) == 0u) {
+      if (tp_globaltimer() - t0 > TP_WAIT_BUDGET_NS) {
+        tp_record_device_error(err, TP_DEVERR_BARRIER_TIMEOUT);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// 2-D tiled TMA load (no multicast) into shared memory, completing on `bar`.
+__device__ __forceinline__ void tp_tma_load_2d(void* smem_dst, const CUtensorMap* map,
+                                               int32_t c0, int32_t c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(tp_smem_addr(smem_dst)),
+      "l"((uint64_t)map), "r"(c0), "r"(c1), "r"(tp_smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tp_prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)map) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// host helpers
+// ---------------------------------------------------------------------------
+namespace tp {
+
+int check_device_pointer(const void* p);   // TP_OK or TP_ERR_BAD_POINTER
+bool pointer_checks_enabled();
+
+// Resolve cuTensorMapEncodeTiled through the runtime (no -lcuda).  Returns
+// nullptr if the driver does not provide it.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled();
+
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? TP_OK : (int)e; }
+
+inline int launch_status() { return cuda_status(cudaGetLastError()); }
+
+inline bool aligned16(const void* p) { return (((uintptr_t)p) & 15u) == 0; }
+
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+int num_sms();
+
+// Device address of the library's error word on the current device (resolved
+// once per device with cudaGetSymbolAddress); nullptr if unavailable.
+int* device_error_ptr();
+
+}  // namespace tp
+
+#define TP_RETURN_IF(cond, code) \
+  do {                           \
+    if (cond) return (code);     \
+  } while (0)
+
+#define TP_CHECK_PTR(p)                                     \
+  do {                                                      \
+    if ((p) == nullptr) return TP_ERR_NULL_POINTER;         \
+    if (tp::pointer_checks_enabled()) {                     \
+      int _s = tp::check_device_pointer((const void*)(p));  \
+      if (_s != TP_OK) return _s;                           \
+    }                                                       \
+  } while (0)
+
+#define TP_CHECK_OPT_PTR(p)                                 \
+  do {                                                      \
+    if ((p) != nullptr && tp::pointer_checks_enabled()) {   \
+      int _s = tp::check_device_pointer((const void*)(p));  \
+      if (_s != TP_OK) return _s;                           \
+    }                                                       \
+  } while (0)

@@ -1,0 +1,618 @@
+// maxplus_generic.cu -- strided / batched max-plus kernels for every shape.
+//
+// These kernels accept any strides, two batch levels, fp32 or bf16 operands,
+// and any M, N, K (including K not a multiple of anything).  They are the
+// path for the batched tropical attention scores (deep_tropical_net.py:148-150,
+// tropformer.py:378-381: per-head GEMMs of 64x64x32), for small tropical
+// linears, for A (x) B with B stored [K,N] (cuda/maxplus_gemm.cu:269-290), and
+// for everything the TMA kernel in maxplus_tma.cu does not take.
+//
+// Forward with argmax tracks (value, index) exactly per term, scanning k in
+// ascending order with "strictly greater, or first NaN" as the update rule.
+// That reproduces torch.max(dim=-1) on the reference's broadcast tensor
+// (tropformer.py:131-141): lowest index on ties, first NaN wins, index 0 for
+// an all -inf row.
+#include "maxplus_internal.cuh"
+
+namespace tp {
+
+namespace {
+
+constexpr int GB_M = 64;
+constexpr int GB_N = 64;
+constexpr int GB_K = 16;
+constexpr int G_THREADS = 256;
+
+struct BatchOffsets {
+  int64_t x, w, y, a;
+};
+
+__device__ __forceinline__ void batch_index(int64_t bz, int64_t B2, int64_t& b1, int64_t& b2) {
+  b1 = bz / B2;
+  b2 = bz - b1 * B2;
+}
+
+// Load a [GB_K x 64] slab of an operand (rows r0.., k0..) into smem as
+// dst[kk][rr], converting to fp32.  Out-of-range k gives `kfill`, out-of-range
+// rows give 0.
+template <typename T>
+__device__ __forceinline__ void load_slab(float (*dst)[GB_M + 4], const T* base, int64_t s_row,
+                                          int64_t s_k, int64_t rows, int64_t K, int64_t r0,
+                                          int64_t k0, float kfill) {
+#pragma unroll
+  for (int r = 0; r < (GB_M * GB_K) / G_THREADS; ++r) {
+    int e = threadIdx.x + r * G_THREADS;
+    int rr = e / GB_K;
+    int kk = e % GB_K;
+    int64_t gr = r0 + rr;
+    int64_t gk = k0 + kk;
+    float v;
+    if (gk >= K) {
+      v = kfill;
+    } else if (gr >= rows) {
+      v = 0.0f;
+    } else {
+      v = tp_load_as_f32<T>(base + gr * s_row + gk * s_k);
+    }
+    dst[kk][rr] = v;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// forward (hard max, optional argmax)
+// ---------------------------------------------------------------------------
+template <typename T, bool kArgmax>
+__global__ void __launch_bounds__(G_THREADS)
+    maxplus_fwd_generic_kernel(StridedMaxPlus p) {
+  __shared__ float xs[GB_K][GB_M + 4];
+  __shared__ float ws[GB_K][GB_N + 4];
+  const int tx = threadIdx.x % 16;
+  const int ty = threadIdx.x / 16;
+  const int64_t m0 = (int64_t)blockIdx.y * GB_M;
+  const int64_t n0 = (int64_t)blockIdx.x * GB_N;
+  const T* xg = static_cast<const T*>(p.x);
+  const T* wg = static_cast<const T*>(p.w);
+  const float NEG_INF = -__int_as_float(0x7f800000);
+
+  for (int64_t bz = blockIdx.z; bz < p.B1 * p.B2; bz += gridDim.z) {
+    int64_t b1, b2;
+    batch_index(bz, p.B2, b1, b2);
+    const T* xb = xg + b1 * p.sx_b1 + b2 * p.sx_b2;
+    const T* wb = wg + b1 * p.sw_b1 + b2 * p.sw_b2;
+
+    float acc[4][4];
+    int idx[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[i][j] = NEG_INF;
+        idx[i][j] = 0;
+      }
+
+    for (int64_t k0 = 0; k0 < p.K; k0 += GB_K) {
+      __syncthreads();
+      load_slab<T>(xs, xb, p.sx_m, p.sx_k, p.M, p.K, m0, k0, NEG_INF);
+      load_slab<T>(ws, wb, p.sw_n, p.sw_k, p.N, p.K, n0, k0, 0.0f);
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < GB_K; ++kk) {
+        float a[4], b[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = xs[kk][ty + 16 * i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b[j] = ws[kk][tx + 16 * j];
+        const int k = (int)(k0 + kk);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float s = a[i] + b[j];
+            if (kArgmax) {
+              bool upd = (s > acc[i][j]) | ((s != s) & (acc[i][j] == acc[i][j]));
+              acc[i][j] = upd ? s : acc[i][j];
+              idx[i][j] = upd ? k : idx[i][j];
+            } else {
+              acc[i][j] = tp_max_nan(acc[i][j], s);
+            }
+          }
+      }
+    }
+
+    float* yb = p.y + b1 * p.sy_b1 + b2 * p.sy_b2;
+    int32_t* ab = kArgmax ? p.am + b1 * p.sa_b1 + b2 * p.sa_b2 : nullptr;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int64_t m = m0 + ty + 16 * i;
+      if (m >= p.M) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        int64_t n = n0 + tx + 16 * j;
+        if (n >= p.N) continue;
+        float v = acc[i][j];
+        if (p.bias) v = v + p.bias[n];
+        if (p.scale != 1.0f) v = v * p.scale;
+        yb[m * p.sy_m + n * p.sy_n] = v;
+        if (kArgmax) ab[m * p.sa_m + n * p.sa_n] = idx[i][j];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// smooth forward: y = tau * log(sum_k exp(s/tau)), two passes over K
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(G_THREADS) maxplus_lse_fwd_generic_kernel(StridedMaxPlus p) {
+  __shared__ float xs[GB_K][GB_M + 4];
+  __shared__ float ws[GB_K][GB_N + 4];
+  const int tx = threadIdx.x % 16;
+  const int ty = threadIdx.x / 16;
+  const int64_t m0 = (int64_t)blockIdx.y * GB_M;
+  const int64_t n0 = (int64_t)blockIdx.x * GB_N;
+  const T* xg = static_cast<const T*>(p.x);
+  const T* wg = static_cast<const T*>(p.w);
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  const float L = 1.4426950408889634f / p.tau;  // log2(e) / tau
+
+  for (int64_t bz = blockIdx.z; bz < p.B1 * p.B2; bz += gridDim.z) {
+    int64_t b1, b2;
+    batch_index(bz, p.B2, b1, b2);
+    const T* xb = xg + b1 * p.sx_b1 + b2 * p.sx_b2;
+    const T* wb = wg + b1 * p.sw_b1 + b2 * p.sw_b2;
+
+    float mx[4][4], sum[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        mx[i][j] = NEG_INF;
+        sum[i][j] = 0.0f;
+      }
+    for (int pass = 0; pass < 2; ++pass) {
+      float ref[4][4];
+      if (pass == 1) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) ref[i][j] = isfinite(mx[i][j]) ? mx[i][j] : 0.0f;
+      }
+      for (int64_t k0 = 0; k0 < p.K; k0 += GB_K) {
+        __syncthreads();
+        load_slab<T>(xs, xb, p.sx_m, p.sx_k, p.M, p.K, m0, k0, NEG_INF);
+        load_slab<T>(ws, wb, p.sw_n, p.sw_k, p.N, p.K, n0, k0, 0.0f);
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < GB_K; ++kk) {
+          float a[4], b[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a[i] = xs[kk][ty + 16 * i];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) b[j] = ws[kk][tx + 16 * j];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float s = a[i] + b[j];
+              if (pass == 0) {
+                mx[i][j] = tp_max_nan(mx[i][j], s);
+              } else {
+                sum[i][j] += exp2f((s - ref[i][j]) * L);
+              }
+            }
+        }
+      }
+    }
+
+    float* yb = p.y + b1 * p.sy_b1 + b2 * p.sy_b2;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int64_t m = m0 + ty + 16 * i;
+      if (m >= p.M) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        int64_t n = n0 + tx + 16 * j;
+        if (n >= p.N) continue;
+        float v = mx[i][j];
+        if (isfinite(v)) v = v + p.tau * logf(sum[i][j]);
+        if (p.bias) v = v + p.bias[n];
+        if (p.scale != 1.0f) v = v * p.scale;
+        yb[m * p.sy_m + n * p.sy_n] = v;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// zero a strided [B1][B2][R][C] region
+// ---------------------------------------------------------------------------
+__global__ void strided_zero_kernel(float* base, int64_t B1, int64_t B2, int64_t R, int64_t C,
+                                    int64_t s_b1, int64_t s_b2, int64_t s_r, int64_t s_c) {
+  const int64_t total = B1 * B2 * R * C;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t c = e % C;
+    int64_t t = e / C;
+    int64_t r = t % R;
+    t /= R;
+    int64_t b2 = t % B2;
+    int64_t b1 = t / B2;
+    base[b1 * s_b1 + b2 * s_b2 + r * s_r + c * s_c] = 0.0f;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// argmax backward: scatter gy into gx / gw at the argmax index
+// ---------------------------------------------------------------------------
+__global__ void maxplus_bwd_scatter_kernel(ScatterArgs p) {
+  const int64_t total = p.B1 * p.B2 * p.M * p.N;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t n = e % p.N;
+    int64_t t = e / p.N;
+    int64_t m = t % p.M;
+    t /= p.M;
+    int64_t b2 = t % p.B2;
+    int64_t b1 = t / p.B2;
+    int32_t k = p.am[b1 * p.sa_b1 + b2 * p.sa_b2 + m * p.sa_m + n * p.sa_n];
+    if (k < 0 || (int64_t)k >= p.K) continue;  // K == 0, or a corrupt index
+    float g = p.gy[b1 * p.sg_b1 + b2 * p.sg_b2 + m * p.sg_m + n * p.sg_n] * p.scale;
+    atomicAdd(p.gx + b1 * p.sgx_b1 + b2 * p.sgx_b2 + m * p.sgx_m + (int64_t)k * p.sgx_k, g);
+    if (p.gw) atomicAdd(p.gw + b1 * p.sgw_b1 + b2 * p.sgw_b2 + n * p.sgw_n + (int64_t)k * p.sgw_k, g);
+  }
+}
+
+// gbias[n] = scale * sum over (b1, b2, m) of g[b1, b2, m, n]; deterministic:
+// warp w of the block sums rows w, w+8, ...; the 8 partials are added in a
+// fixed order.
+__global__ void __launch_bounds__(256)
+    column_sum_kernel(const float* g, int64_t B1, int64_t B2, int64_t M, int64_t N, int64_t s_b1,
+                      int64_t s_b2, int64_t s_m, int64_t s_n, float scale, float* out) {
+  __shared__ float part[8][33];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t n = (int64_t)blockIdx.x * 32 + lane;
+  float acc = 0.0f;
+  if (n < N) {
+    const int64_t rows = B1 * B2 * M;
+    for (int64_t r = warp; r < rows; r += 8) {
+      int64_t m = r % M;
+      int64_t t = r / M;
+      int64_t b2 = t % B2;
+      int64_t b1 = t / B2;
+      acc += g[b1 * s_b1 + b2 * s_b2 + m * s_m + n * s_n];
+    }
+  }
+  part[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && n < N) {
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += part[w][lane];
+    out[n] = s * scale;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// smooth backward (contiguous x[M,K], w[N,K], gy[M,N])
+//   pass 1 (stats): per (m,n): mx = max_k s, then with t = s - mx and
+//          e = 2^(t*L):  Z = sum e,  S1 = sum e*t
+//          STE: A = g/Z * (1 - (S1/Z)/tau),  B = g/(Z*tau)
+//          LSE: A = g/Z,                     B = 0
+//          so that dS = e * (A + B*t).
+//   pass 2 (gx): gx[m,k] = sum_n dS      pass 3 (gw): gw[n,k] = sum_m dS
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(G_THREADS) smooth_stats_kernel(SmoothArgs p) {
+  __shared__ float xs[GB_K][GB_M + 4];
+  __shared__ float ws[GB_K][GB_N + 4];
+  const int tx = threadIdx.x % 16;
+  const int ty = threadIdx.x / 16;
+  const int64_t m0 = (int64_t)blockIdx.y * GB_M;
+  const int64_t n0 = (int64_t)blockIdx.x * GB_N;
+  const int64_t bz = blockIdx.z;
+  const T* xg = static_cast<const T*>(p.x) + bz * p.M * p.K;
+  const T* wg = static_cast<const T*>(p.w) + bz * p.N * p.K;
+  const float* gyb = p.gy + bz * p.M * p.N;
+  float* wsb = p.ws + bz * 3 * p.M * p.N;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  const float L = 1.4426950408889634f / p.tau;
+
+  float mx[4][4], Z[4][4], S1[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      mx[i][j] = NEG_INF;
+      Z[i][j] = 0.0f;
+      S1[i][j] = 0.0f;
+    }
+  for (int pass = 0; pass < 2; ++pass) {
+    float ref[4][4];
+    if (pass == 1) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ref[i][j] = isfinite(mx[i][j]) ? mx[i][j] : 0.0f;
+    }
+    for (int64_t k0 = 0; k0 < p.K; k0 += GB_K) {
+      __syncthreads();
+      load_slab<T>(xs, xg, p.K, 1, p.M, p.K, m0, k0, NEG_INF);
+      load_slab<T>(ws, wg, p.K, 1, p.N, p.K, n0, k0, 0.0f);
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < GB_K; ++kk) {
+        float a[4], b[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = xs[kk][ty + 16 * i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b[j] = ws[kk][tx + 16 * j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float s = a[i] + b[j];
+            if (pass == 0) {
+              mx[i][j] = tp_max_nan(mx[i][j], s);
+            } else {
+              float t = s - ref[i][j];
+              float e = exp2f(t * L);
+              Z[i][j] += e;
+              S1[i][j] += (e == 0.0f) ? 0.0f : e * t;
+            }
+          }
+      }
+    }
+  }
+  const int64_t MN = p.M * p.N;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int64_t m = m0 + ty + 16 * i;
+    if (m >= p.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int64_t n = n0 + tx + 16 * j;
+      if (n >= p.N) continue;
+      float g = gyb[m * p.N + n];
+      float A = 0.0f, B = 0.0f, ref = 0.0f;
+      if (isfinite(mx[i][j]) && Z[i][j] > 0.0f) {
+        ref = mx[i][j];
+        float invZ = 1.0f / Z[i][j];
+        if (p.mode == TP_BWD_STE) {
+          float sbar = S1[i][j] * invZ;
+          A = g * invZ * (1.0f - sbar / p.tau);
+          B = g * invZ / p.tau;
+        } else {
+          A = g * invZ;
+        }
+      }
+      wsb[m * p.N + n] = ref;
+      wsb[MN + m * p.N + n] = A;
+      wsb[2 * MN + m * p.N + n] = B;
+    }
+  }
+}
+
+// gx[m,k] (kOut == 0) or gw[n,k] (kOut == 1).  Tile over (r, k) with r = m or
+// n; loop over the other index q (n or m) in slabs of 16.
+template <typename T, int kOut>
+__global__ void __launch_bounds__(G_THREADS) smooth_grad_kernel(SmoothArgs p) {
+  constexpr int QS = 16;
+  __shared__ float os[QS][GB_N + 4];   // other operand: [q][k]
+  __shared__ float st[3][QS][GB_M + 4];  // stats: [plane][q][r]
+  const int tx = threadIdx.x % 16;
+  const int ty = threadIdx.x / 16;
+  const int64_t r0 = (int64_t)blockIdx.y * GB_M;
+  const int64_t k0 = (int64_t)blockIdx.x * GB_N;
+  const int64_t bz = blockIdx.z;
+  const T* xb = static_cast<const T*>(p.x) + bz * p.M * p.K;
+  const T* wb = static_cast<const T*>(p.w) + bz * p.N * p.K;
+  const float* wsb = p.ws + bz * 3 * p.M * p.N;
+  const T* mine = kOut == 0 ? xb : wb;
+  const T* other = kOut == 0 ? wb : xb;
+  const int64_t R = kOut == 0 ? p.M : p.N;
+  const int64_t Q = kOut == 0 ? p.N : p.M;
+  const float L = 1.4426950408889634f / p.tau;
+  const int64_t MN = p.M * p.N;
+
+  float own[4][4], acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int64_t r = r0 + ty + 16 * i;
+      int64_t k = k0 + tx + 16 * j;
+      own[i][j] = (r < R && k < p.K) ? tp_load_as_f32<T>(mine + r * p.K + k) : 0.0f;
+      acc[i][j] = 0.0f;
+    }
+
+  for (int64_t q0 = 0; q0 < Q; q0 += QS) {
+    __syncthreads();
+    // other operand slab [QS][64 k]
+    for (int e = threadIdx.x; e < QS * GB_N; e += G_THREADS) {
+      int qq = e / GB_N, kk = e % GB_N;
+      int64_t q = q0 + qq, k = k0 + kk;
+      os[qq][kk] = (q < Q && k < p.K) ? tp_load_as_f32<T>(other + q * p.K + k) : 0.0f;
+    }
+    // stats slab [3][QS][64 r]; stats are stored [M][N]
+    for (int e = threadIdx.x; e < 3 * QS * GB_M; e += G_THREADS) {
+      int pl = e / (QS * GB_M);
+      int rem = e % (QS * GB_M);
+      int qq, rr;
+      if (kOut == 0) {  // r = m, q = n: read along n for coalescing
+        rr = rem / QS;
+        qq = rem % QS;
+      } else {  // r = n, q = m: read along n (= r)
+        qq = rem / GB_M;
+        rr = rem % GB_M;
+      }
+      int64_t q = q0 + qq, r = r0 + rr;
+      float v = 0.0f;
+      if (q < Q && r < R) {
+        int64_t m = kOut == 0 ? r : q;
+        int64_t n = kOut == 0 ? q : r;
+        v = wsb[pl * MN + m * p.N + n];
+      }
+      st[pl][qq][rr] = v;
+    }
+    __syncthreads();
+    const int qmax = (int)((Q - q0) < QS ? (Q - q0) : QS);
+    for (int qq = 0; qq < qmax; ++qq) {
+      float ob[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ob[j] = os[qq][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float ref = st[0][qq][ty + 16 * i];
+        const float A = st[1][qq][ty + 16 * i];
+        const float B = st[2][qq][ty + 16 * i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float s = own[i][j] + ob[j];
+          float t = s - ref;
+          float e = exp2f(t * L);
+          acc[i][j] += (e == 0.0f) ? 0.0f : e * fmaf(B, t, A);
+        }
+      }
+    }
+  }
+  float* out = kOut == 0 ? p.gx + bz * p.M * p.K : p.gw + bz * p.N * p.K;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int64_t r = r0 + ty + 16 * i;
+    if (r >= R) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int64_t k = k0 + tx + 16 * j;
+      if (k < p.K) out[r * p.K + k] = acc[i][j];
+    }
+  }
+}
+
+inline dim3 generic_grid(int64_t M, int64_t N, int64_t batches) {
+  int64_t gz = batches < 65535 ? batches : 65535;
+  return dim3((unsigned)ceil_div(N, GB_N), (unsigned)ceil_div(M, GB_M), (unsigned)gz);
+}
+
+inline unsigned flat_grid(int64_t total, int threads) {
+  int64_t b = ceil_div(total, threads);
+  int64_t cap = (int64_t)num_sms() * 32;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return (unsigned)b;
+}
+
+}  // namespace
+
+int launch_maxplus_fwd_generic(const StridedMaxPlus& p, cudaStream_t stream) {
+  dim3 grid = generic_grid(p.M, p.N, p.B1 * p.B2);
+  if (grid.x > 2147483647u || grid.y > 65535u) return TP_ERR_TOO_LARGE;
+  const bool am = p.am != nullptr;
+  if (p.dtype == TP_DTYPE_F32) {
+    if (am)
+      maxplus_fwd_generic_kernel<float, true><<<grid, G_THREADS, 0, stream>>>(p);
+    else
+      maxplus_fwd_generic_kernel<float, false><<<grid, G_THREADS, 0, stream>>>(p);
+  } else {
+    if (am)
+      maxplus_fwd_generic_kernel<uint16_t, true><<<grid, G_THREADS, 0, stream>>>(p);
+    else
+      maxplus_fwd_generic_kernel<uint16_t, false><<<grid, G_THREADS, 0, stream>>>(p);
+  }
+  return launch_status();
+}
+
+int launch_maxplus_lse_fwd_generic(const StridedMaxPlus& p, cudaStream_t stream) {
+  dim3 grid = generic_grid(p.M, p.N, p.B1 * p.B2);
+  if (grid.y > 65535u) return TP_ERR_TOO_LARGE;
+  if (p.dtype == TP_DTYPE_F32)
+    maxplus_lse_fwd_generic_kernel<float><<<grid, G_THREADS, 0, stream>>>(p);
+  else
+    maxplus_lse_fwd_generic_kernel<uint16_t><<<grid, G_THREADS, 0, stream>>>(p);
+  return launch_status();
+}
+
+int launch_strided_zero(float* base, int64_t B1, int64_t B2, int64_t R, int64_t C, int64_t s_b1,
+                        int64_t s_b2, int64_t s_r, int64_t s_c, cudaStream_t stream) {
+  const int64_t total = B1 * B2 * R * C;
+  if (total == 0) return TP_OK;
+  // contiguous fast path
+  if (s_c == 1 && s_r == C && s_b2 == R * C && s_b1 == B2 * R * C)
+    return cuda_status(cudaMemsetAsync(base, 0, (size_t)total * sizeof(float), stream));
+  strided_zero_kernel<<<flat_grid(total, 256), 256, 0, stream>>>(base, B1, B2, R, C, s_b1, s_b2,
+                                                                  s_r, s_c);
+  return launch_status();
+}
+
+int launch_maxplus_bwd_argmax(const ScatterArgs& p, cudaStream_t stream) {
+  int s = launch_strided_zero(p.gx, p.B1, p.B2, p.M, p.K, p.sgx_b1, p.sgx_b2, p.sgx_m, p.sgx_k,
+                              stream);
+  if (s != TP_OK) return s;
+  if (p.gw) {
+    s = launch_strided_zero(p.gw, p.B1, p.B2, p.N, p.K, p.sgw_b1, p.sgw_b2, p.sgw_n, p.sgw_k,
+                            stream);
+    if (s != TP_OK) return s;
+  }
+  const int64_t total = p.B1 * p.B2 * p.M * p.N;
+  if (total > 0 && p.K > 0) {
+    maxplus_bwd_scatter_kernel<<<flat_grid(total, 256), 256, 0, stream>>>(p);
+    s = launch_status();
+    if (s != TP_OK) return s;
+  }
+  if (p.gbias) return launch_column_sum(p.gy, p.B1, p.B2, p.M, p.N, p.sg_b1, p.sg_b2, p.sg_m,
+                                        p.sg_n, p.scale, p.gbias, stream);
+  return TP_OK;
+}
+
+int launch_column_sum(const float* g, int64_t B1, int64_t B2, int64_t M, int64_t N, int64_t s_b1,
+                      int64_t s_b2, int64_t s_m, int64_t s_n, float scale, float* out,
+                      cudaStream_t stream) {
+  if (N == 0) return TP_OK;
+  column_sum_kernel<<<(unsigned)ceil_div(N, 32), 256, 0, stream>>>(g, B1, B2, M, N, s_b1, s_b2,
+                                                                   s_m, s_n, scale, out);
+  return launch_status();
+}
+
+int launch_maxplus_bwd_smooth(const SmoothArgs& p, cudaStream_t stream) {
+  if (p.batch == 0) return TP_OK;
+  if (p.M == 0 || p.N == 0) {
+    int s = TP_OK;
+    if (p.M > 0 && p.K > 0)
+      s = cuda_status(cudaMemsetAsync(p.gx, 0, p.batch * p.M * p.K * 4, stream));
+    if (s == TP_OK && p.N > 0 && p.K > 0 && p.gw)
+      s = cuda_status(cudaMemsetAsync(p.gw, 0, p.batch * p.N * p.K * 4, stream));
+    if (s == TP_OK && p.gbias && p.N > 0)
+      s = cuda_status(cudaMemsetAsync(p.gbias, 0, p.N * 4, stream));
+    return s;
+  }
+  if (p.batch > 65535) return TP_ERR_TOO_LARGE;
+  const unsigned nb = (unsigned)p.batch;
+  dim3 g1((unsigned)ceil_div(p.N, GB_N), (unsigned)ceil_div(p.M, GB_M), nb);
+  if (g1.y > 65535u) return TP_ERR_TOO_LARGE;
+  if (p.dtype == TP_DTYPE_F32)
+    smooth_stats_kernel<float><<<g1, G_THREADS, 0, stream>>>(p);
+  else
+    smooth_stats_kernel<uint16_t><<<g1, G_THREADS, 0, stream>>>(p);
+  int s = launch_status();
+  if (s != TP_OK) return s;
+  if (p.K > 0) {
+    dim3 gx((unsigned)ceil_div(p.K, GB_N), (unsigned)ceil_div(p.M, GB_M), nb);
+    dim3 gw((unsigned)ceil_div(p.K, GB_N), (unsigned)ceil_div(p.N, GB_M), nb);
+    if (gx.y > 65535u || gw.y > 65535u) return TP_ERR_TOO_LARGE;
+    if (p.dtype == TP_DTYPE_F32) {
+      smooth_grad_kernel<float, 0><<<gx, G_THREADS, 0, stream>>>(p);
+      if (p.gw) smooth_grad_kernel<float, 1><<<gw, G_THREADS, 0, stream>>>(p);
+    } else {
+      smooth_grad_kernel<uint16_t, 0><<<gx, G_THREADS, 0, stream>>>(p);
+      if (p.gw) smooth_grad_kernel<uint16_t, 1><<<gw, G_THREADS, 0, stream>>>(p);
+    }
+    s = launch_status();
+    if (s != TP_OK) return s;
+  }
+  if (p.gbias)
+    return launch_column_sum(p.gy, p.batch, 1, p.M, p.N, p.M * p.N, 0, p.N, 1, 1.0f, p.gbias,
+                             stream);
+  return TP_OK;
+}
+
+}  // namespace tp

@@ -1,0 +1,97 @@
+// maxplus_internal.cuh -- argument structs and launcher declarations shared
+// between the kernel files and the C-ABI layer (capi.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace tp {
+
+// One strided, two-level batched max-plus problem (see tp_maxplus_fwd_strided).
+struct StridedMaxPlus {
+  int dtype;
+  int64_t B1, B2, M, N, K;
+  const void* x;
+  int64_t sx_b1, sx_b2, sx_m, sx_k;
+  const void* w;
+  int64_t sw_b1, sw_b2, sw_n, sw_k;
+  const float* bias;
+  float* y;
+  int64_t sy_b1, sy_b2, sy_m, sy_n;
+  int32_t* am;
+  int64_t sa_b1, sa_b2, sa_m, sa_n;
+  float scale;
+  float tau;
+};
+
+struct ScatterArgs {
+  int64_t B1, B2, M, N, K;
+  const int32_t* am;
+  int64_t sa_b1, sa_b2, sa_m, sa_n;
+  const float* gy;
+  int64_t sg_b1, sg_b2, sg_m, sg_n;
+  float* gx;
+  int64_t sgx_b1, sgx_b2, sgx_m, sgx_k;
+  float* gw;
+  int64_t sgw_b1, sgw_b2, sgw_n, sgw_k;
+  float* gbias;
+  float scale;
+};
+
+struct SmoothArgs {
+  int mode;
+  float tau;
+  int dtype;
+  int64_t batch;  // contiguous batches: x[b] = x + b*M*K, w[b] = w + b*N*K, ...
+  int64_t M, N, K;
+  const void* x;
+  const void* w;
+  const float* gy;
+  float* gx;
+  float* gw;
+  float* gbias;
+  float* ws;  // per batch 3 planes of [M][N]: reference max, A, B
+};
+
+// maxplus_generic.cu
+int launch_maxplus_fwd_generic(const StridedMaxPlus& p, cudaStream_t stream);
+int launch_maxplus_lse_fwd_generic(const StridedMaxPlus& p, cudaStream_t stream);
+int launch_maxplus_bwd_argmax(const ScatterArgs& p, cudaStream_t stream);
+int launch_maxplus_bwd_smooth(const SmoothArgs& p, cudaStream_t stream);
+int launch_strided_zero(float* base, int64_t B1, int64_t B2, int64_t R, int64_t C, int64_t s_b1,
+                        int64_t s_b2, int64_t s_r, int64_t s_c, cudaStream_t stream);
+int launch_column_sum(const float* g, int64_t B1, int64_t B2, int64_t M, int64_t N, int64_t s_b1,
+                      int64_t s_b2, int64_t s_m, int64_t s_n, float scale, float* out,
+                      cudaStream_t stream);
+
+// maxplus_tma.cu: large contiguous fp32 GEMM.  Returns TP_ERR_UNSUPPORTED
+// when the problem does not meet its layout rules (caller falls back).
+bool maxplus_tma_eligible(const StridedMaxPlus& p);
+int launch_maxplus_fwd_tma(const StridedMaxPlus& p, cudaStream_t stream);
+
+// scan.cu
+struct ScanArgs {
+  int64_t B, T, C;
+  const float* bb;
+  const float* xx;
+  const float* a;
+  float h_init;
+  const float* h0;
+  float* h;
+  uint32_t* win;
+  // backward
+  const float* gh;
+  const uint32_t* win_in;
+  float* gu;
+  float* ga;
+  float* gh0;
+  float* ws;
+  int* err;
+};
+int launch_scan_fwd(const ScanArgs& p, cudaStream_t stream);
+int launch_scan_bwd(const ScanArgs& p, cudaStream_t stream);
+
+// probe.cu
+int launch_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters, float* sink,
+                        cudaStream_t stream);
+
+}  // namespace tp

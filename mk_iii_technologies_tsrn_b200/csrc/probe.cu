@@ -1,0 +1,88 @@
+// probe.cu -- register-only microbenchmark of the CUDA-core max-plus term rate.
+//
+// It measures the roofline denominator for the max-plus GEMM: how many
+// (add, max) terms per second an SM can retire when nothing but arithmetic
+// is issued.  Each thread keeps an 8x8 block of independent accumulators
+// (the GEMM kernel's register tile) and folds 128 terms per iteration.
+//   form 0: add.rn.f32 + 2-input max.f32 per term (4 instructions / 2 terms)
+//   form 1: add.rn.f32x2 + 3-input max.f32 per two terms (2 instructions)
+//   form 2: add.rn.f32x2 + 3-input max.NaN.f32 (the GEMM kernel's form)
+// The asm statements are volatile so the loop body is executed as written.
+#include "maxplus_internal.cuh"
+
+namespace tp {
+
+namespace {
+
+template <int FORM>
+__device__ __forceinline__ void term_pair(float& acc, uint64_t xa, uint64_t wb) {
+  if (FORM == 0) {
+    asm volatile(
+        "{\n\t.reg .f32 x0, x1, w0, w1, s0, s1;\n\t"
+        "mov.b64 {x0, x1}, %1;\n\tmov.b64 {w0, w1}, %2;\n\t"
+        "add.rn.f32 s0, x0, w0;\n\tadd.rn.f32 s1, x1, w1;\n\t"
+        "max.f32 %0, %0, s0;\n\tmax.f32 %0, %0, s1;\n\t}"
+        : "+f"(acc)
+        : "l"(xa), "l"(wb));
+  } else if (FORM == 1) {
+    asm volatile(
+        "{\n\t.reg .b64 s;\n\t.reg .f32 lo, hi;\n\t"
+        "add.rn.f32x2 s, %1, %2;\n\tmov.b64 {lo, hi}, s;\n\t"
+        "max.f32 %0, %0, lo, hi;\n\t}"
+        : "+f"(acc)
+        : "l"(xa), "l"(wb));
+  } else {
+    asm volatile(
+        "{\n\t.reg .b64 s;\n\t.reg .f32 lo, hi;\n\t"
+        "add.rn.f32x2 s, %1, %2;\n\tmov.b64 {lo, hi}, s;\n\t"
+        "max.NaN.f32 %0, %0, lo, hi;\n\t}"
+        : "+f"(acc)
+        : "l"(xa), "l"(wb));
+  }
+}
+
+template <int FORM>
+__global__ void __launch_bounds__(256) probe_kernel(int64_t iters, float* sink) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  uint64_t xa[8], wb[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float f0 = (float)(t % 97) * 0.01f + (float)i;
+    const float f1 = (float)(t % 89) * 0.02f - (float)i;
+    xa[i] = ((uint64_t)__float_as_uint(f1) << 32) | __float_as_uint(f0);
+    wb[i] = ((uint64_t)__float_as_uint(f0 * 0.5f) << 32) | __float_as_uint(f1 * 0.25f);
+  }
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = -1.0e30f;
+  for (int64_t it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) term_pair<FORM>(acc[i][j], xa[i], wb[j]);
+  }
+  float r = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r += acc[i][j];
+  sink[t] = r;
+}
+
+}  // namespace
+
+int launch_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters, float* sink,
+                        cudaStream_t stream) {
+  if (threads != 256) return TP_ERR_INVALID_ARG;
+  if (form == 0)
+    probe_kernel<0><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
+  else if (form == 1)
+    probe_kernel<1><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
+  else
+    probe_kernel<2><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
+  return launch_status();
+}
+
+}  // namespace tp

@@ -1,0 +1,466 @@
+"""Tensor-level tropical ops over the C ABI, plus their autograd functions.
+
+Every op here runs the sm_100a kernels of ``_tropical_b200.so`` on the
+tensors' CUDA device and the current stream.  CPU tensors are rejected with a
+RuntimeError: there is deliberately no CPU fallback (the reference binding's
+silent fallback, ``cuda/maxplus_binding.py:137-148``, hid the fact that its
+GPU path never ran correctly).
+
+Reference expressions each op replaces (Mediocr3Mik3/MK_III_Technologies_TSRN):
+
+* :func:`maxplus` -- ``scores = W[None] + x[:, None]; scores.max(-1)`` plus bias
+  (``tropformer.py:127-145``); values and int32 argmax bit-exact.
+* :func:`tropical_scores` -- ``_tropical_max(Q.unsqueeze(3) + K.unsqueeze(2), -1) * scale``
+  (``deep_tropical_net.py:148-150``, ``tropformer.py:378-381``).
+* :func:`lse_scores` -- ``logsumexp_c(Q[..., :, None, c] + K[..., None, :, c])``, the TSRN
+  tropical attention score (``research/tsrn_dml.py:438-460``).
+* :func:`tropical_scan` -- the ``TropicalSSM`` max-plus recurrence
+  (``research/tsrn_dml.py:961-972``), evaluated as the exact sequential recurrence.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import TP_BWD_LSE, TP_BWD_STE, TP_DTYPE_BF16, TP_DTYPE_F32
+
+MODES = ("argmax", "ste", "lse")
+
+
+# --------------------------------------------------------------------------- helpers
+def _require_cuda(*tensors: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                "tropical ops run only on CUDA tensors (sm_100a kernels); got a "
+                f"{t.device} tensor -- there is no CPU fallback"
+            )
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    if dev is None:
+        raise RuntimeError("no tensor arguments")
+    return dev
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(dev: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return TP_DTYPE_F32
+    if t.dtype == torch.bfloat16:
+        return TP_DTYPE_BF16
+    raise TypeError(f"tropical ops take float32 or bfloat16 operands, got {t.dtype}")
+
+
+def _f32(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    if t is None:
+        return None
+    if t.dtype != torch.float32:
+        raise TypeError(f"expected a float32 tensor, got {t.dtype}")
+    return t
+
+
+def _batch2(t: torch.Tensor) -> Tuple[int, int, int, int]:
+    """(B1, B2, s_b1, s_b2) for a tensor with 0, 1 or 2 leading batch dims."""
+    lead = t.dim() - 2
+    if lead == 0:
+        return 1, 1, 0, 0
+    if lead == 1:
+        return t.shape[0], 1, t.stride(0), 0
+    if lead == 2:
+        return t.shape[0], t.shape[1], t.stride(0), t.stride(1)
+    raise ValueError("at most two leading batch dimensions are supported")
+
+
+# --------------------------------------------------------------------------- forward ops
+def maxplus_strided(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                    *, argmax: bool = True, scale: float = 1.0,
+                    out: Optional[torch.Tensor] = None,
+                    out_argmax: Optional[torch.Tensor] = None):
+    """Batched max-plus product on strided views.
+
+    ``x``: [..., M, K], ``w``: [..., N, K] (same 0-2 leading batch dims, any
+    strides); returns ``y`` [..., M, N] fp32 and ``argmax`` [..., M, N] int32
+    (or None).  ``y = (max_k(x + w) [+ bias]) * scale``.
+    """
+    dev = _require_cuda(x, w, bias)
+    if x.dtype != w.dtype:
+        raise TypeError(f"x and w must share a dtype, got {x.dtype} and {w.dtype}")
+    code = _dtype_code(x)
+    if x.dim() != w.dim() or x.shape[:-2] != w.shape[:-2]:
+        raise ValueError(f"batch dims differ: {tuple(x.shape)} vs {tuple(w.shape)}")
+    if x.shape[-1] != w.shape[-1]:
+        raise ValueError(f"inner dims differ: {x.shape[-1]} vs {w.shape[-1]}")
+    M, K = x.shape[-2], x.shape[-1]
+    N = w.shape[-2]
+    lead = tuple(x.shape[:-2])
+    if bias is not None:
+        bias = _f32(bias)
+        if bias.shape != (N,) or not bias.is_contiguous():
+            raise ValueError("bias must be a contiguous [N] float32 tensor")
+    y = out if out is not None else torch.empty(lead + (M, N), device=dev, dtype=torch.float32)
+    am = None
+    if argmax:
+        am = out_argmax if out_argmax is not None else torch.empty(
+            lead + (M, N), device=dev, dtype=torch.int32)
+    B1, B2, sx1, sx2 = _batch2(x)
+    _, _, sw1, sw2 = _batch2(w)
+    _, _, sy1, sy2 = _batch2(y)
+    if am is not None:
+        _, _, sa1, sa2 = _batch2(am)
+        sam, san = am.stride(-2), am.stride(-1)
+    else:
+        sa1 = sa2 = sam = san = 0
+    with torch.cuda.device(dev):
+        st = _lib.load().tp_maxplus_fwd_strided(
+            code, B1, B2, M, N, K,
+            _ptr(x), sx1, sx2, x.stride(-2), x.stride(-1),
+            _ptr(w), sw1, sw2, w.stride(-2), w.stride(-1),
+            _ptr(bias),
+            _ptr(y), sy1, sy2, y.stride(-2), y.stride(-1),
+            _ptr(am), sa1, sa2, sam, san,
+            float(scale), _stream(dev))
+    _lib.check(st, "tp_maxplus_fwd_strided")
+    return y, am
+
+
+def maxplus(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
+            *, argmax: bool = True):
+    """``y[m,n] = max_k(x[m,k] + w[n,k]) (+ bias[n])`` and the lowest argmax k (int32)."""
+    if x.dim() != 2 or w.dim() != 2:
+        raise ValueError("maxplus takes x [M,K] and w [N,K]")
+    return maxplus_strided(x, w, bias, argmax=argmax)
+
+
+def tropical_scores(Q: torch.Tensor, K: torch.Tensor, scale: float = 1.0, *, argmax: bool = True):
+    """``S[..., i, j] = max_f(Q[..., i, f] + K[..., j, f]) * scale`` (+ int32 argmax f)."""
+    return maxplus_strided(Q, K, None, argmax=argmax, scale=scale)
+
+
+def lse_scores(Q: torch.Tensor, K: torch.Tensor, tau: float = 1.0, scale: float = 1.0,
+               bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``S[..., i, j] = tau * logsumexp_f((Q[..., i, f] + K[..., j, f]) / tau) * scale``."""
+    dev = _require_cuda(Q, K, bias)
+    if Q.dtype != K.dtype:
+        raise TypeError("Q and K must share a dtype")
+    code = _dtype_code(Q)
+    if Q.dim() != K.dim() or Q.shape[:-2] != K.shape[:-2] or Q.shape[-1] != K.shape[-1]:
+        raise ValueError(f"shape mismatch {tuple(Q.shape)} vs {tuple(K.shape)}")
+    M, Kd = Q.shape[-2], Q.shape[-1]
+    N = K.shape[-2]
+    lead = tuple(Q.shape[:-2])
+    y = torch.empty(lead + (M, N), device=dev, dtype=torch.float32)
+    B1, B2, sx1, sx2 = _batch2(Q)
+    _, _, sw1, sw2 = _batch2(K)
+    _, _, sy1, sy2 = _batch2(y)
+    with torch.cuda.device(dev):
+        st = _lib.load().tp_maxplus_lse_fwd_strided(
+            code, float(tau), B1, B2, M, N, Kd,
+            _ptr(Q), sx1, sx2, Q.stride(-2), Q.stride(-1),
+            _ptr(K), sw1, sw2, K.stride(-2), K.stride(-1),
+            _ptr(bias),
+            _ptr(y), sy1, sy2, y.stride(-2), y.stride(-1),
+            float(scale), _stream(dev))
+    _lib.check(st, "tp_maxplus_lse_fwd_strided")
+    return y
+
+
+# --------------------------------------------------------------------------- backward ops
+def maxplus_backward_argmax(am: torch.Tensor, gy: torch.Tensor, K: int, *,
+                            need_gw: bool = True, need_gbias: bool = False,
+                            scale: float = 1.0):
+    """Scatter ``gy * scale`` to the argmax index: returns (gx [..,M,K], gw [..,N,K] | None,
+    gbias [N] | None).  Autograd of ``scores.max(-1).values`` (tropformer.py:141)."""
+    dev = _require_cuda(am, gy)
+    gy = _f32(gy)
+    if am.dtype != torch.int32 or am.shape != gy.shape:
+        raise ValueError("argmax must be int32 with gy's shape")
+    M, N = am.shape[-2], am.shape[-1]
+    lead = tuple(am.shape[:-2])
+    gx = torch.empty(lead + (M, K), device=dev, dtype=torch.float32)
+    gw = torch.empty(lead + (N, K), device=dev, dtype=torch.float32) if need_gw else None
+    gb = torch.empty((N,), device=dev, dtype=torch.float32) if need_gbias else None
+    B1, B2, sa1, sa2 = _batch2(am)
+    _, _, sg1, sg2 = _batch2(gy)
+    _, _, sx1, sx2 = _batch2(gx)
+    if gw is not None:
+        _, _, sw1, sw2 = _batch2(gw)
+        swn, swk = gw.stride(-2), gw.stride(-1)
+    else:
+        sw1 = sw2 = swn = swk = 0
+    with torch.cuda.device(dev):
+        st = _lib.load().tp_maxplus_bwd_argmax_strided(
+            B1, B2, M, N, K,
+            _ptr(am), sa1, sa2, am.stride(-2), am.stride(-1),
+            _ptr(gy), sg1, sg2, gy.stride(-2), gy.stride(-1),
+            _ptr(gx), sx1, sx2, gx.stride(-2), gx.stride(-1),
+            _ptr(gw), sw1, sw2, swn, swk,
+            _ptr(gb), float(scale), _stream(dev))
+    _lib.check(st, "tp_maxplus_bwd_argmax_strided")
+    return gx, gw, gb
+
+
+def maxplus_backward_smooth(mode: str, tau: float, x: torch.Tensor, w: torch.Tensor,
+                            gy: torch.Tensor, *, need_gw: bool = True,
+                            need_gbias: bool = False):
+    """STE (``tropformer.py:133-139``) or LSE/Maslov (``tropformer.py:95-97``) backward.
+
+    ``x`` [B?, M, K], ``w`` [B?, N, K], ``gy`` [B?, M, N] (contiguous copies are made
+    if needed).  Returns (gx, gw | None, gbias | None)."""
+    if mode not in ("ste", "lse"):
+        raise ValueError(f"smooth backward mode must be 'ste' or 'lse', got {mode!r}")
+    dev = _require_cuda(x, w, gy)
+    code = _dtype_code(x)
+    if w.dtype != x.dtype:
+        raise TypeError("x and w must share a dtype")
+    gy = _f32(gy)
+    squeeze = x.dim() == 2
+    if squeeze:
+        x, w, gy = x.unsqueeze(0), w.unsqueeze(0), gy.unsqueeze(0)
+    x, w, gy = x.contiguous(), w.contiguous(), gy.contiguous()
+    B, M, K = x.shape
+    N = w.shape[1]
+    if w.shape != (B, N, K) or gy.shape != (B, M, N):
+        raise ValueError("shape mismatch in smooth backward")
+    lib = _lib.load()
+    ws_bytes = int(lib.tp_maxplus_bwd_smooth_workspace_bytes(B, M, N))
+    ws = torch.empty(max(ws_bytes // 4, 4), device=dev, dtype=torch.float32)
+    gx = torch.empty((B, M, K), device=dev, dtype=torch.float32)
+    gw = torch.empty((B, N, K), device=dev, dtype=torch.float32) if need_gw else None
+    gb = torch.empty((N,), device=dev, dtype=torch.float32) if need_gbias else None
+    with torch.cuda.device(dev):
+        st = lib.tp_maxplus_bwd_smooth(
+            TP_BWD_STE if mode == "ste" else TP_BWD_LSE, float(tau), code, B, M, N, K,
+            _ptr(x), _ptr(w), _ptr(gy), _ptr(gx), _ptr(gw), _ptr(gb),
+            _ptr(ws), ws.numel() * 4, _stream(dev))
+    _lib.check(st, "tp_maxplus_bwd_smooth")
+    if squeeze:
+        gx = gx[0]
+        gw = gw[0] if gw is not None else None
+    return gx, gw, gb
+
+
+# --------------------------------------------------------------------------- scan
+def scan_forward(b: torch.Tensor, x: Optional[torch.Tensor], a: torch.Tensor,
+                 h_init: float = float("-inf"), h0: Optional[torch.Tensor] = None,
+                 *, need_mask: bool = False):
+    """``h[:, t] = max(a + h[:, t-1], b[:, t] (+ x[:, t]))`` over [B, T, C] contiguous fp32.
+
+    Returns (h, win_mask | None); win_mask is [B, ceil(T/32), C] int32 bit words."""
+    dev = _require_cuda(b, x, a, h0)
+    b = _f32(b).contiguous()
+    x = _f32(x).contiguous() if x is not None else None
+    a = _f32(a).contiguous()
+    h0 = _f32(h0).contiguous() if h0 is not None else None
+    if b.dim() != 3:
+        raise ValueError("scan input must be [B, T, C]")
+    B, T, C = b.shape
+    if x is not None and x.shape != b.shape:
+        raise ValueError("b and x must have the same shape")
+    if a.shape != (C,):
+        raise ValueError("a must be [C]")
+    if h0 is not None and h0.shape != (B, C):
+        raise ValueError("h0 must be [B, C]")
+    h = torch.empty_like(b)
+    mask = (torch.empty((B, (T + 31) // 32, C), device=dev, dtype=torch.int32)
+            if need_mask else None)
+    with torch.cuda.device(dev):
+        st = _lib.load().tp_scan_fwd(B, T, C, _ptr(b), _ptr(x), _ptr(a), float(h_init),
+                                     _ptr(h0), _ptr(h), _ptr(mask), _stream(dev))
+    _lib.check(st, "tp_scan_fwd")
+    return h, mask
+
+
+def scan_backward(gh: torch.Tensor, a: torch.Tensor, h_init: float = float("-inf"),
+                  h0: Optional[torch.Tensor] = None, *, mask: Optional[torch.Tensor] = None,
+                  b: Optional[torch.Tensor] = None, x: Optional[torch.Tensor] = None,
+                  h: Optional[torch.Tensor] = None, need_ga: bool = True,
+                  need_gh0: bool = False):
+    """Argmax-path backward of :func:`scan_forward`: returns (gu, ga | None, gh0 | None).
+
+    Winners come from ``mask`` when given, else are recomputed from (b, x, h)."""
+    dev = _require_cuda(gh, a, h0, mask, b, x, h)
+    gh = _f32(gh).contiguous()
+    B, T, C = gh.shape
+    if mask is None and (b is None or h is None):
+        raise ValueError("scan_backward needs the win mask or (b, h)")
+    a = _f32(a).contiguous()
+    gu = torch.empty_like(gh)
+    ga = torch.empty((C,), device=dev, dtype=torch.float32) if need_ga else None
+    gh0 = torch.empty((B, C), device=dev, dtype=torch.float32) if need_gh0 else None
+    ws = torch.empty((B, C), device=dev, dtype=torch.float32) if need_ga else None
+    with torch.cuda.device(dev):
+        st = _lib.load().tp_scan_bwd(
+            B, T, C, _ptr(gh),
+            _ptr(b.contiguous() if b is not None else None),
+            _ptr(x.contiguous() if x is not None else None),
+            _ptr(a), float(h_init), _ptr(h0.contiguous() if h0 is not None else None),
+            _ptr(h.contiguous() if h is not None else None),
+            _ptr(mask), _ptr(gu), _ptr(ga), _ptr(gh0), _ptr(ws), _stream(dev))
+    _lib.check(st, "tp_scan_bwd")
+    return gu, ga, gh0
+
+
+# --------------------------------------------------------------------------- autograd
+class MaxPlusLinearFunction(torch.autograd.Function):
+    """y = max_k(x + W) + bias with a selectable backward.
+
+    mode "argmax": eval-mode TropicalLinear (gradient to the argmax only);
+    mode "ste":    train-mode TropicalLinear STE (tropformer.py:133-139);
+    mode "lse":    softmax(s/tau) gradient (cuda/maxplus_gemm.cu:181-259 intent)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, mode: str, tau: float):
+        if mode not in MODES:
+            raise ValueError(f"mode must be one of {MODES}")
+        y, am = maxplus(x, weight, bias, argmax=(mode == "argmax"))
+        ctx.mode, ctx.tau, ctx.K = mode, float(tau), x.shape[1]
+        ctx.has_bias = bias is not None
+        if mode == "argmax":
+            ctx.save_for_backward(am)
+        else:
+            ctx.save_for_backward(x, weight)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        need_x, need_w, need_b = ctx.needs_input_grad[0], ctx.needs_input_grad[1], ctx.has_bias
+        gy = gy.contiguous()
+        if ctx.mode == "argmax":
+            (am,) = ctx.saved_tensors
+            gx, gw, gb = maxplus_backward_argmax(am, gy, ctx.K, need_gw=need_w,
+                                                 need_gbias=need_b and ctx.needs_input_grad[2])
+        else:
+            x, w = ctx.saved_tensors
+            gx, gw, gb = maxplus_backward_smooth(ctx.mode, ctx.tau, x, w, gy, need_gw=need_w,
+                                                 need_gbias=need_b and ctx.needs_input_grad[2])
+        return (gx if need_x else None), gw, gb, None, None
+
+
+class TropicalScoreFunction(torch.autograd.Function):
+    """Hard tropical score ``max_f(Q + K) * scale`` over [B, H, L, d] views.
+
+    Backward routes through the argmax (``_tropical_max`` hard branch,
+    tropformer.py:93-94) or, with ``smooth_tau``, through softmax(s/tau) (the
+    ``_USE_SMOOTH_MAX`` STE branch, tropformer.py:95-97)."""
+
+    @staticmethod
+    def forward(ctx, Q, K, scale: float, smooth_tau: Optional[float]):
+        S, am = tropical_scores(Q, K, scale, argmax=smooth_tau is None)
+        ctx.scale, ctx.smooth_tau, ctx.d = float(scale), smooth_tau, Q.shape[-1]
+        if smooth_tau is None:
+            ctx.save_for_backward(am)
+        else:
+            ctx.save_for_backward(Q, K)
+        return S
+
+    @staticmethod
+    def backward(ctx, gS):
+        gS = gS.contiguous()
+        if ctx.smooth_tau is None:
+            (am,) = ctx.saved_tensors
+            gQ, gK, _ = maxplus_backward_argmax(am, gS, ctx.d, need_gw=ctx.needs_input_grad[1],
+                                                scale=ctx.scale)
+            return gQ, gK, None, None
+        Q, K = ctx.saved_tensors
+        lead = Q.shape[:-2]
+        Qc = Q.reshape(-1, Q.shape[-2], Q.shape[-1])
+        Kc = K.reshape(-1, K.shape[-2], K.shape[-1])
+        g = (gS * ctx.scale).reshape(-1, gS.shape[-2], gS.shape[-1])
+        gQ, gK, _ = maxplus_backward_smooth("lse", ctx.smooth_tau, Qc, Kc, g,
+                                            need_gw=ctx.needs_input_grad[1])
+        gQ = gQ.reshape(*lead, Q.shape[-2], Q.shape[-1])
+        gK = gK.reshape(*lead, K.shape[-2], K.shape[-1]) if gK is not None else None
+        return gQ, gK, None, None
+
+
+class LSEScoreFunction(torch.autograd.Function):
+    """Smooth tropical score ``logsumexp_f(Q + K)`` (TSRN, research/tsrn_dml.py:438-460).
+
+    The gradient of logsumexp is softmax over f, i.e. the LSE backward with tau = 1."""
+
+    @staticmethod
+    def forward(ctx, Q, K, tau: float):
+        ctx.tau = float(tau)
+        ctx.save_for_backward(Q, K)
+        return lse_scores(Q, K, tau)
+
+    @staticmethod
+    def backward(ctx, gS):
+        Q, K = ctx.saved_tensors
+        lead = Q.shape[:-2]
+        Qc = Q.reshape(-1, Q.shape[-2], Q.shape[-1])
+        Kc = K.reshape(-1, K.shape[-2], K.shape[-1])
+        g = gS.contiguous().reshape(-1, gS.shape[-2], gS.shape[-1])
+        gQ, gK, _ = maxplus_backward_smooth("lse", ctx.tau, Qc, Kc, g,
+                                            need_gw=ctx.needs_input_grad[1])
+        gQ = gQ.reshape(*lead, Q.shape[-2], Q.shape[-1])
+        gK = gK.reshape(*lead, K.shape[-2], K.shape[-1]) if gK is not None else None
+        return gQ, gK, None
+
+
+class TropicalScanFunction(torch.autograd.Function):
+    """``h_t = max(a + h_{t-1}, b_t (+ x_t))``; gradients of b and x are equal."""
+
+    @staticmethod
+    def forward(ctx, b, x, a, h_init: float, h0):
+        h, mask = scan_forward(b, x, a, h_init, h0, need_mask=True)
+        ctx.h_init = float(h_init)
+        ctx.has_x = x is not None
+        ctx.save_for_backward(a, h0, mask)
+        return h
+
+    @staticmethod
+    def backward(ctx, gh):
+        a, h0, mask = ctx.saved_tensors
+        need_ga = ctx.needs_input_grad[2]
+        need_gh0 = h0 is not None and ctx.needs_input_grad[4]
+        gu, ga, gh0 = scan_backward(gh, a, ctx.h_init, h0, mask=mask, need_ga=need_ga,
+                                    need_gh0=need_gh0)
+        gb = gu if ctx.needs_input_grad[0] else None
+        gx = gu if (ctx.has_x and ctx.needs_input_grad[1]) else None
+        return gb, gx, ga, None, gh0
+
+
+def tropical_scan(b, x, a, h_init: float = float("-inf"), h0=None):
+    """Differentiable max-plus scan (see :class:`TropicalScanFunction`)."""
+    return TropicalScanFunction.apply(b, x, a, h_init, h0)
+
+
+def maxplus_linear(x, weight, bias=None, mode: str = "argmax", tau: float = 1.0):
+    """Differentiable tropical linear on x [..., K] (leading dims flattened)."""
+    lead = x.shape[:-1]
+    y = MaxPlusLinearFunction.apply(x.reshape(-1, x.shape[-1]), weight, bias, mode, tau)
+    return y.reshape(*lead, weight.shape[0])
+
+
+# --------------------------------------------------------------------------- probe
+def probe_addmax(form: int, blocks: int, iters: int, device=None) -> Tuple[float, int]:
+    """Run the register-only add+max probe once; returns (ms, terms)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda")
+    sink = torch.empty(blocks * 256, device=dev, dtype=torch.float32)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        s = torch.cuda.current_stream(dev)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(s)
+        st = lib.tp_probe_addmax(form, blocks, 256, iters, _ptr(sink), _stream(dev))
+        end.record(s)
+        end.synchronize()
+    _lib.check(st, "tp_probe_addmax")
+    return start.elapsed_time(end), blocks * 256 * iters * 128

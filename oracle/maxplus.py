@@ -1,0 +1,112 @@
+"""Max-plus (tropical) GEMM oracle -- test infrastructure only (see package doc).
+
+Reference expressions restated here:
+
+* forward: ``scores = W.unsqueeze(0) + x.unsqueeze(1)`` then ``scores.max(-1)`` and
+  ``+ bias`` -- tropformer.py:131 (broadcast add), :141 (max), :143-144 (bias).
+  torch.max(dim=-1) returns the LOWEST index on ties and the first NaN;
+  numpy's max/argmax follow the same rules, and each term is one float32 add.
+* argmax backward: autograd of ``.max(-1).values`` (tropformer.py:141, and the
+  hard branch of ``_tropical_max`` tropformer.py:93-94): the upstream gradient
+  goes to the argmax term only, then sums over the broadcast dims.
+* STE backward: autograd of tropformer.py:133-139 --
+  ``soft = sum(softmax(s/tau) * s)``; d soft/ds = p * (1 + (s - sum(p*s))/tau).
+* LSE backward: gradient of ``tau * logsumexp(s/tau)`` = softmax(s/tau)
+  (tropformer.py:95-97 with _SMOOTH_MAX_TEMP; cuda/maxplus_gemm.cu:181-259).
+* LSE forward: ``tau * logsumexp(s/tau)`` -- research/tsrn_dml.py:438-460 (tau = 1,
+  the TSRN attention score) and research/tropical_optimizers.py:750-763.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+_CHUNK_ELEMS = 1 << 24  # bound the [rows, N, K] broadcast temporary
+
+
+def _rows_per_chunk(N: int, K: int) -> int:
+    return max(1, _CHUNK_ELEMS // max(1, N * K))
+
+
+def maxplus_fwd(x: np.ndarray, w: np.ndarray, bias: np.ndarray | None = None,
+                scale: float = 1.0):
+    """y[m,n] = max_k(w[n,k] + x[m,k]) (+bias[n]) (*scale), argmax (int64, lowest k).
+
+    x [M,K], w [N,K] float32 (tropformer.py:131-144)."""
+    x = np.asarray(x, dtype=np.float32)
+    w = np.asarray(w, dtype=np.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    y = np.empty((M, N), dtype=np.float32)
+    idx = np.zeros((M, N), dtype=np.int64)
+    if K == 0:
+        y.fill(-np.inf)
+    else:
+        step = _rows_per_chunk(N, K)
+        with np.errstate(invalid="ignore"):          # inf + -inf = NaN, as in torch
+            for m0 in range(0, M, step):
+                s = w[None, :, :] + x[m0:m0 + step, None, :]   # one float32 add per term
+                y[m0:m0 + step] = s.max(axis=-1)
+                idx[m0:m0 + step] = s.argmax(axis=-1)
+    if bias is not None:
+        y = (y + np.asarray(bias, dtype=np.float32)[None, :]).astype(np.float32)
+    if scale != 1.0:
+        y = (y * np.float32(scale)).astype(np.float32)
+    return y, idx
+
+
+def maxplus_bwd_argmax(idx: np.ndarray, gy: np.ndarray, K: int, scale: float = 1.0):
+    """(gx [M,K], gw [N,K], gbias [N]) routing gy*scale to the argmax term (float64 sums)."""
+    M, N = gy.shape
+    g = gy.astype(np.float64) * scale
+    gx = np.zeros((M, K), dtype=np.float64)
+    gw = np.zeros((N, K), dtype=np.float64)
+    if K > 0:
+        mm = np.repeat(np.arange(M), N)
+        nn = np.tile(np.arange(N), M)
+        kk = idx.reshape(-1)
+        np.add.at(gx, (mm, kk), g.reshape(-1))
+        np.add.at(gw, (nn, kk), g.reshape(-1))
+    return gx, gw, g.sum(axis=0)
+
+
+def maxplus_bwd_smooth(mode: str, tau: float, x: np.ndarray, w: np.ndarray, gy: np.ndarray):
+    """STE (tropformer.py:133-139) or LSE (tropformer.py:95-97) backward in float64."""
+    x = np.asarray(x, dtype=np.float32)
+    w = np.asarray(w, dtype=np.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    gx = np.zeros((M, K), dtype=np.float64)
+    gw = np.zeros((N, K), dtype=np.float64)
+    step = _rows_per_chunk(N, K)
+    for m0 in range(0, M, step):
+        s = (w[None, :, :] + x[m0:m0 + step, None, :]).astype(np.float64)
+        z = s / tau
+        z = z - z.max(axis=-1, keepdims=True)
+        p = np.exp(z)
+        p /= p.sum(axis=-1, keepdims=True)
+        g = gy[m0:m0 + step, :, None].astype(np.float64)
+        if mode == "ste":
+            sbar = (p * s).sum(axis=-1, keepdims=True)
+            dS = g * p * (1.0 + (s - sbar) / tau)
+        elif mode == "lse":
+            dS = g * p
+        else:
+            raise ValueError(mode)
+        gx[m0:m0 + step] = dS.sum(axis=1)
+        gw += dS.sum(axis=0)
+    return gx, gw, gy.astype(np.float64).sum(axis=0)
+
+
+def maxplus_lse_fwd(x: np.ndarray, w: np.ndarray, tau: float = 1.0):
+    """tau * logsumexp_k((w[n,k] + x[m,k]) / tau) in float64 (terms rounded to float32 first)."""
+    x = np.asarray(x, dtype=np.float32)
+    w = np.asarray(w, dtype=np.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    y = np.empty((M, N), dtype=np.float64)
+    step = _rows_per_chunk(N, K)
+    for m0 in range(0, M, step):
+        s = (w[None, :, :] + x[m0:m0 + step, None, :]).astype(np.float64) / tau
+        mx = s.max(axis=-1, keepdims=True)
+        y[m0:m0 + step] = tau * (mx[..., 0] + np.log(np.exp(s - mx).sum(axis=-1)))
+    return y

@@ -1,0 +1,238 @@
+"""Generate golden vectors by running the reference's own PyTorch code.
+
+Run in a container that has the reference checkout (default
+/root/reference, override with TSRN_REFERENCE):
+
+    python tests/golden/gen_golden.py
+
+Writes ``tests/golden/*.npz``.  Each fixture stores its inputs and the outputs
+of the reference expression, so the tests (and the oracle pin) need nothing
+but numpy at run time.  Reference modules are loaded by file path because the
+installed ``cuda-python`` package shadows the reference's ``cuda/`` directory
+and ``research/tsrn_dml.py`` clashes by name with the top-level ``tsrn_dml.py``.
+"""
+from __future__ import annotations
+
+import importlib.util
+import os
+import sys
+
+import numpy as np
+import torch
+
+REF = os.environ.get("TSRN_REFERENCE", "/root/reference")
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+
+def _load(name: str, rel: str):
+    path = os.path.join(REF, rel)
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def _save(name: str, **arrays):
+    path = os.path.join(OUT, f"{name}.npz")
+    np.savez_compressed(path, **{k: (v if isinstance(v, np.ndarray) else np.asarray(v))
+                                 for k, v in arrays.items()})
+    print(f"wrote {path}")
+
+
+def gen_kat(trop):
+    # cuda/test_kernel.py:117-136, computed with the reference broadcast expression
+    A = torch.tensor([[1.0, 2.0], [3.0, 0.0]])
+    B = torch.tensor([[0.0, 1.0], [2.0, 0.0]])
+    C = (A.unsqueeze(2) + B.unsqueeze(0)).max(dim=1)
+    _save("kat_2x2", A=_np(A), B=_np(B), C=_np(C.values), idx=_np(C.indices),
+          expected=np.array([[4.0, 2.0], [3.0, 4.0]], np.float32))
+
+
+def _linear_case(trop, name, x, W, bias, g, ste_temp=1.0):
+    layer = trop.TropicalLinear(W.shape[1], W.shape[0], bias=bias is not None)
+    with torch.no_grad():
+        layer.weight.copy_(W)
+        if bias is not None:
+            layer.bias.copy_(bias)
+    old = trop.TropicalLinear._ste_temp
+    trop.TropicalLinear._ste_temp = ste_temp
+    try:
+        out = {}
+        for mode in ("eval", "train"):
+            layer.train(mode == "train")
+            layer.zero_grad()
+            xx = x.clone().requires_grad_(True)
+            y = layer(xx)
+            (y * g).sum().backward()
+            out[f"y_{mode}"] = _np(y)
+            out[f"gx_{mode}"] = _np(xx.grad)
+            out[f"gw_{mode}"] = _np(layer.weight.grad)
+            if bias is not None:
+                out[f"gb_{mode}"] = _np(layer.bias.grad)
+        scores = W.unsqueeze(0) + x.unsqueeze(1)          # tropformer.py:131
+        mx = scores.max(dim=-1)                             # tropformer.py:141
+        out["max"] = _np(mx.values)
+        out["idx"] = _np(mx.indices)
+    finally:
+        trop.TropicalLinear._ste_temp = old
+    arrays = dict(x=_np(x), W=_np(W), g=_np(g), ste_temp=np.float32(ste_temp), **out)
+    if bias is not None:
+        arrays["bias"] = _np(bias)
+    _save(name, **arrays)
+
+
+def gen_linear(trop):
+    # the reference's own op-level test setup (cuda/test_kernel.py:15-65): seed 42,
+    # batch 8, in 64, out 32, TropicalLinear weights U(-0.5, 0.5), zero bias
+    torch.manual_seed(42)
+    ref = trop.TropicalLinear(64, 32, bias=True)
+    torch.empty(32, 64).uniform_(-0.5, 0.5)  # the second layer's init in that test
+    x = torch.randn(8, 64)
+    g = torch.ones(8, 32)                    # y.sum().backward()
+    _linear_case(trop, "linear_seed42", x, ref.weight.detach().clone(),
+                 ref.bias.detach().clone(), g)
+
+    # config-1 distribution at a small size, non-zero bias, random upstream grad
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(48, 40, generator=gen)
+    W = torch.randn(24, 40, generator=gen)
+    b = torch.randn(24, generator=gen)
+    g = torch.randn(48, 24, generator=gen)
+    _linear_case(trop, "linear_gauss", x, W, b, g)
+    _linear_case(trop, "linear_gauss_tau05", x, W, b, g, ste_temp=0.5)
+
+    # tie-rich: small integers, many equal sums
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randint(-3, 4, (37, 45), generator=gen).float()
+    W = torch.randint(-3, 4, (29, 45), generator=gen).float()
+    g = torch.randn(37, 29, generator=gen)
+    _linear_case(trop, "linear_ties", x, W, None, g)
+
+    # -inf rich: 5% of W is -inf, one x row all -inf, one W row all -inf
+    gen = torch.Generator().manual_seed(2)
+    x = torch.randn(20, 33, generator=gen)
+    W = torch.randn(18, 33, generator=gen)
+    W[torch.rand(18, 33, generator=gen) < 0.05] = float("-inf")
+    x[3] = float("-inf")
+    W[5] = float("-inf")
+    scores = W.unsqueeze(0) + x.unsqueeze(1)
+    mx = scores.max(dim=-1)
+    _save("linear_neginf", x=_np(x), W=_np(W), max=_np(mx.values), idx=_np(mx.indices))
+
+    # NaN and +inf/-inf pairs: torch.max propagates NaN and reports the first NaN
+    gen = torch.Generator().manual_seed(3)
+    x = torch.randn(9, 70, generator=gen)
+    W = torch.randn(7, 70, generator=gen)
+    x[1, 5] = float("nan")
+    x[2, 40] = float("inf")
+    W[3, 40] = float("-inf")      # inf + -inf = NaN at (2, 3, 40)
+    x[4, 10] = float("nan")
+    x[4, 60] = float("nan")
+    W[6, 0] = float("nan")
+    scores = W.unsqueeze(0) + x.unsqueeze(1)
+    mx = scores.max(dim=-1)
+    _save("linear_nan", x=_np(x), W=_np(W), max=_np(mx.values), idx=_np(mx.indices))
+
+
+def gen_scores(trop, dtn):
+    # DTNAttention tropical score (deep_tropical_net.py:148-150): hard and smooth
+    gen = torch.Generator().manual_seed(4)
+    Bz, H, L, dk = 2, 4, 6, 8
+    Q = torch.randn(Bz, H, L, dk, generator=gen)
+    K = torch.randn(Bz, H, L, dk, generator=gen)
+    gS = torch.randn(Bz, H, L, L, generator=gen)
+    scale = dk ** -0.5
+    out = {}
+    for smooth in (False, True):
+        old = trop._USE_SMOOTH_MAX
+        trop._USE_SMOOTH_MAX = smooth
+        try:
+            q = Q.clone().requires_grad_(True)
+            k = K.clone().requires_grad_(True)
+            S = trop._tropical_max(q.unsqueeze(3) + k.unsqueeze(2), dim=-1) * scale
+            (S * gS).sum().backward()
+        finally:
+            trop._USE_SMOOTH_MAX = old
+        tag = "smooth" if smooth else "hard"
+        out[f"S_{tag}"] = _np(S)
+        out[f"gQ_{tag}"] = _np(q.grad)
+        out[f"gK_{tag}"] = _np(k.grad)
+    idx = (Q.unsqueeze(3) + K.unsqueeze(2)).max(dim=-1).indices
+    _save("dtn_scores", Q=_np(Q), K=_np(K), gS=_np(gS), scale=np.float32(scale),
+          smooth_temp=np.float32(trop._SMOOTH_MAX_TEMP), idx=_np(idx), **out)
+
+    # full DTNAttention block (train mode: STE in the tropical Q/K projections)
+    torch.manual_seed(5)
+    d, heads = 32, 4
+    attn = dtn.DTNAttention(d, heads, dropout=0.0)
+    with torch.no_grad():
+        attn.q_proj.weight.normal_(0.0, 0.02)
+        attn.k_proj.weight.normal_(0.0, 0.02)
+        attn.maslov.log_temps.copy_(torch.log(torch.rand(heads) * 0.9 + 0.1))
+    attn.train()
+    x = torch.randn(3, 7, d, requires_grad=True)
+    gout = torch.randn(3, 7, d)
+    out_t, w_t = attn(x)
+    (out_t * gout).sum().backward()
+    state = {f"p_{k}": _np(v) for k, v in attn.state_dict().items()}
+    grads = {f"g_{n}": _np(p.grad) for n, p in attn.named_parameters()}
+    _save("dtn_block", x=_np(x), gout=_np(gout), out=_np(out_t), attn=_np(w_t),
+          gx=_np(x.grad), **state, **grads)
+
+
+def gen_tsrn(research):
+    # research TropicalAttention._channel_chunked_scores (research/tsrn_dml.py:438-460)
+    gen = torch.Generator().manual_seed(6)
+    Bz, H, T, dh = 2, 2, 12, 10
+    Q = torch.randn(Bz, H, T, dh, generator=gen)
+    K = torch.randn(Bz, H, T, dh, generator=gen)
+    attn = research.TropicalAttention(H * dh, top_k=4, n_heads=H)
+    S = attn._channel_chunked_scores(Q, K, Bz, H, T, dh)
+    S64 = torch.logsumexp(Q.double().unsqueeze(3) + K.double().unsqueeze(2), dim=-1)
+    _save("tsrn_scores", Q=_np(Q), K=_np(K), S=_np(S), S64=_np(S64))
+
+    # TropicalSSM (research/tsrn_dml.py:917-980) module forward/backward with a
+    # non-zero C_proj so the scan reaches the output
+    torch.manual_seed(7)
+    d, ds, T = 16, 8, 40
+    ssm = research.TropicalSSM(d, ds)
+    with torch.no_grad():
+        ssm.C_proj.weight.normal_(0.0, 0.3)
+        ssm.A.copy_(torch.linspace(-0.3, 0.05, ds))   # includes A > 0 (clamped to 0)
+        ssm.gate_B.weight.normal_(0.0, 0.2)
+    x = torch.randn(2, T, d, requires_grad=True)
+    gout = torch.randn(2, T, d)
+    y = ssm(x)
+    (y * gout).sum().backward()
+    # the scan input u and its closed-form output, for the scan-level pin
+    with torch.no_grad():
+        u = torch.sigmoid(ssm.gate_B(x)) * ssm.B_proj(x)
+        A_c = ssm.A.clamp(max=0)
+        t_idx = torch.arange(T, dtype=x.dtype).unsqueeze(-1)
+        G = torch.cat([A_c.unsqueeze(0).expand(2, -1).unsqueeze(1), u - t_idx * A_c], dim=1)
+        Hs = t_idx.unsqueeze(0) * A_c + G.cummax(dim=1).values[:, 1:, :]
+    state = {f"p_{k}": _np(v) for k, v in ssm.state_dict().items()}
+    grads = {f"g_{n}": _np(p.grad) for n, p in ssm.named_parameters()}
+    _save("tsrn_ssm", x=_np(x), gout=_np(gout), y=_np(y), gx=_np(x.grad), u=_np(u),
+          H=_np(Hs), A_c=_np(A_c), **state, **grads)
+
+
+def main():
+    sys.path.insert(0, REF)
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    trop = _load("tropformer", "tropformer.py")
+    dtn = _load("deep_tropical_net", "deep_tropical_net.py")
+    research = _load("research_tsrn_dml", "research/tsrn_dml.py")
+    gen_kat(trop)
+    gen_linear(trop)
+    gen_scores(trop, dtn)
+    gen_tsrn(research)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,86 @@
+"""The C-ABI library loads on a CPU-only host and exports every declared symbol;
+host-side validation rejects bad arguments before touching a GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "tropical_b200.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"TP_API\s+[\w\s\*]+?\b(\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for n in ("tp_maxplus_fwd", "tp_maxplus_fwd_strided", "tp_maxplus_lse_fwd_strided",
+              "tp_maxplus_bwd_argmax_strided", "tp_maxplus_bwd_smooth", "tp_scan_fwd",
+              "tp_scan_bwd", "maxplus_forward_cuda", "maxplus_backward_cuda",
+              "maxplus_matmul_cuda"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    from mk_iii_technologies_tsrn_b200 import _lib
+    lib = _lib.load()
+    for n in _declared():
+        assert hasattr(lib, n), f"missing export {n}"
+        assert n in _lib.SIGNATURES, f"no ctypes signature for {n}"
+
+
+def test_no_undeclared_exports_in_signature_table():
+    from mk_iii_technologies_tsrn_b200 import _lib
+    assert set(_lib.SIGNATURES) == set(_declared())
+
+
+def test_status_strings():
+    from mk_iii_technologies_tsrn_b200 import _lib
+    assert _lib.status_text(0) == "ok"
+    assert "NULL" in _lib.status_text(-2)
+    assert "workspace" in _lib.status_text(-7)
+    assert _lib.load().tp_abi_version() == 1
+
+
+def test_validation_rejects_before_launch():
+    from mk_iii_technologies_tsrn_b200 import _lib
+    lib = _lib.load()
+    # negative sizes / bad leading dims are rejected on the host
+    assert lib.tp_maxplus_fwd(0, -1, 4, 4, None, 4, None, 4, None, None, 4, None, 0, None) == -1
+    assert lib.tp_maxplus_fwd(0, 4, 4, 8, None, 4, None, 8, None, None, 4, None, 0, None) == -1
+    assert lib.tp_maxplus_fwd(7, 4, 4, 4, None, 4, None, 4, None, None, 4, None, 0, None) == -4
+    assert lib.tp_maxplus_bwd_smooth(9, 1.0, 0, 1, 4, 4, 4, None, None, None, None, None, None,
+                                     None, 0, None) == -1
+    assert lib.tp_maxplus_bwd_smooth(1, 0.0, 0, 1, 4, 4, 4, None, None, None, None, None, None,
+                                     None, 0, None) == -1
+    assert lib.tp_scan_fwd(-1, 4, 4, None, None, None, 0.0, None, None, None, None) == -1
+    # empty problems are a no-op success
+    assert lib.tp_maxplus_fwd(0, 0, 4, 4, None, 4, None, 4, None, None, 4, None, 0, None) == 0
+    assert lib.tp_scan_fwd(0, 4, 4, None, None, None, 0.0, None, None, None, None) == 0
+    assert lib.tp_probe_addmax(5, 1, 256, 1, None, None) == -1
+
+
+def test_null_pointer_rejected_without_pointer_checks():
+    from mk_iii_technologies_tsrn_b200 import _lib
+    lib = _lib.load()
+    old = lib.tp_set_pointer_checks(0)
+    try:
+        st = lib.tp_maxplus_fwd(0, 4, 4, 4, None, 4, None, 4, None, None, 4, None, 0, None)
+        assert st == -2
+        # (B, T, C, gh, bb, xx, a, h_init, h0, h, win_mask, gu, ga, gh0, workspace, stream)
+        st = lib.tp_scan_bwd(2, 4, 4, None, None, None, None, 0.0, None, None, None, None,
+                             ctypes.c_void_p(16), None, None, None)
+        assert st == -7   # ga requested without a workspace
+    finally:
+        lib.tp_set_pointer_checks(old)
+
+
+def test_workspace_size():
+    from mk_iii_technologies_tsrn_b200 import _lib
+    lib = _lib.load()
+    assert lib.tp_maxplus_bwd_smooth_workspace_bytes(2, 3, 5) == 2 * 3 * 3 * 5 * 4
+    assert lib.tp_maxplus_bwd_smooth_workspace_bytes(-1, 3, 5) == 0

@@ -1,0 +1,109 @@
+"""Max-plus backward on the GPU: argmax scatter, STE and LSE vs the oracle and the
+reference's own autograd (golden vectors)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+
+def _fn():
+    from mk_iii_technologies_tsrn_b200 import ops
+    return ops
+
+
+def _grads(x, w, b, g, mode, tau, dev):
+    ops = _fn()
+    xt = torch.tensor(x, device=dev, requires_grad=True)
+    wt = torch.tensor(w, device=dev, requires_grad=True)
+    bt = torch.tensor(b, device=dev, requires_grad=True) if b is not None else None
+    y = ops.MaxPlusLinearFunction.apply(xt, wt, bt, mode, tau)
+    (y * torch.tensor(g, device=dev)).sum().backward()
+    out = [y.detach().cpu().numpy(), xt.grad.cpu().numpy(), wt.grad.cpu().numpy()]
+    out.append(bt.grad.cpu().numpy() if bt is not None else None)
+    return out
+
+
+@pytest.mark.parametrize("name", ["linear_seed42", "linear_gauss", "linear_ties"])
+def test_golden_eval_grads(cuda, name):
+    g = load_golden(name)
+    y, gx, gw, gb = _grads(g["x"], g["W"], g.get("bias"), g["g"], "argmax", 1.0, cuda)
+    np.testing.assert_array_equal(y, g["y_eval"])
+    np.testing.assert_allclose(gx, g["gx_eval"], rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(gw, g["gw_eval"], rtol=1e-6, atol=1e-5)
+    if gb is not None:
+        np.testing.assert_allclose(gb, g["gb_eval"], rtol=1e-6, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["linear_seed42", "linear_gauss", "linear_gauss_tau05",
+                                  "linear_ties"])
+def test_golden_train_grads(cuda, name):
+    g = load_golden(name)
+    tau = float(g["ste_temp"])
+    y, gx, gw, gb = _grads(g["x"], g["W"], g.get("bias"), g["g"], "ste", tau, cuda)
+    np.testing.assert_array_equal(y, g["y_train"])
+    np.testing.assert_allclose(gx, g["gx_train"], rtol=1e-4, atol=2e-5)
+    np.testing.assert_allclose(gw, g["gw_train"], rtol=1e-4, atol=2e-5)
+    if gb is not None:
+        np.testing.assert_allclose(gb, g["gb_train"], rtol=1e-5, atol=1e-5)
+
+
+def _rel_err(a, b):
+    scale = max(1.0, float(np.abs(b).max()))
+    return float(np.abs(a - b).max()) / scale
+
+
+@pytest.mark.parametrize("mode,tau", [("ste", 1.0), ("lse", 1.0), ("lse", 50.0), ("ste", 0.25)])
+def test_config1_smooth_vs_oracle(cuda, mode, tau):
+    # config 1: x [1024,256], W [256,256] ~ N(0,1), upstream g ~ N(0,1)
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((1024, 256)).astype(np.float32)
+    w = rng.standard_normal((256, 256)).astype(np.float32)
+    g = rng.standard_normal((1024, 256)).astype(np.float32)
+    _, gx, gw, _ = _grads(x, w, None, g, mode, tau, cuda)
+    rgx, rgw, _ = oracle.maxplus_bwd_smooth(mode, tau, x, w, g)
+    # tolerance: 1e-5 relative to the gradient scale (fp32 exp and sums vs fp64)
+    assert _rel_err(gx, rgx) < 1e-5
+    assert _rel_err(gw, rgw) < 1e-5
+
+
+def test_config1_argmax_vs_oracle(cuda):
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((1024, 256)).astype(np.float32)
+    w = rng.standard_normal((256, 256)).astype(np.float32)
+    b = rng.standard_normal(256).astype(np.float32)
+    g = rng.standard_normal((1024, 256)).astype(np.float32)
+    y, gx, gw, gb = _grads(x, w, b, g, "argmax", 1.0, cuda)
+    ry, ri = oracle.maxplus_fwd(x, w, b)
+    np.testing.assert_array_equal(y, ry)
+    rgx, rgw, rgb = oracle.maxplus_bwd_argmax(ri, g, 256)
+    np.testing.assert_allclose(gx, rgx, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(gw, rgw, rtol=1e-5, atol=1e-4)
+    np.testing.assert_allclose(gb, rgb, rtol=1e-5, atol=1e-4)
+
+
+def test_bf16_smooth_backward(cuda):
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((96, 80)).astype(np.float32)
+    w = rng.standard_normal((64, 80)).astype(np.float32)
+    g = rng.standard_normal((96, 64)).astype(np.float32)
+    ops = _fn()
+    xb = torch.tensor(x, device=cuda).bfloat16()
+    wb = torch.tensor(w, device=cuda).bfloat16()
+    gx, gw, _ = ops.maxplus_backward_smooth("ste", 1.0, xb, wb, torch.tensor(g, device=cuda))
+    rgx, rgw, _ = oracle.maxplus_bwd_smooth("ste", 1.0, xb.float().cpu().numpy(),
+                                            wb.float().cpu().numpy(), g)
+    assert _rel_err(gx.cpu().numpy(), rgx) < 1e-5
+    assert _rel_err(gw.cpu().numpy(), rgw) < 1e-5
+
+
+def test_empty_rows(cuda):
+    ops = _fn()
+    x = torch.randn(0, 16, device=cuda, requires_grad=True)
+    w = torch.randn(8, 16, device=cuda, requires_grad=True)
+    y = ops.MaxPlusLinearFunction.apply(x, w, None, "ste", 1.0)
+    y.sum().backward()
+    assert torch.all(w.grad == 0)
