@@ -63,17 +63,25 @@ def needs_build() -> bool:
     return any(os.path.getmtime(p) > lib_mtime for p in _deps())
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> str:
-    """Compile the library if needed and return its path."""
-    if not force and not needs_build():
+def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False,
+          extra_flags: list[str] | None = None, lib_path: str | None = None,
+          build_dir: str | None = None) -> str:
+    """Compile the library if needed and return its path.
+
+    ``extra_flags`` (e.g. ``-DTP_TMA_TM=8``) and ``lib_path``/``build_dir`` build a
+    variant library elsewhere without touching the in-tree one."""
+    out_path = lib_path or LIB_PATH
+    bdir = build_dir or BUILD_DIR
+    if lib_path is None and not force and not needs_build():
         return LIB_PATH
     nvcc = _nvcc()
-    os.makedirs(BUILD_DIR, exist_ok=True)
+    os.makedirs(bdir, exist_ok=True)
     objs = []
     procs = []
     for src in _sources():
-        obj = os.path.join(BUILD_DIR, os.path.basename(src)[:-3] + ".o")
-        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, "-I", INCLUDE, "-c", src, "-o", obj]
+        obj = os.path.join(bdir, os.path.basename(src)[:-3] + ".o")
+        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, *(extra_flags or []), "-I", INCLUDE, "-c", src,
+               "-o", obj]
         if ptxas_verbose:
             cmd[1:1] = ["-Xptxas", "-v"]
         if verbose:
@@ -91,15 +99,15 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     if failed:
         msg = "\n".join(f"--- {s}\n{t}" for s, t in failed)
         raise RuntimeError(f"nvcc failed:\n{msg}")
-    tmp = LIB_PATH + ".tmp"
+    tmp = out_path + ".tmp"
     link = [nvcc, *ARCH_FLAGS, "-shared", "-o", tmp, *objs, "-lcudart"]
     if verbose:
         print(" ".join(link), flush=True)
     res = subprocess.run(link, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, out_path)
+    return out_path
 
 
 if __name__ == "__main__":

@@ -15,7 +15,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
-#include "../../include/tropical_b200.h"
+#include "tropical_b200.h"
 
 // ---------------------------------------------------------------------------
 // device error word (module-scope device memory, not a per-call allocation)

@@ -10,10 +10,10 @@
 // add) and one 3-input max.NaN.f32 folding both sums into the accumulator.
 //
 // CTA (one per SM, persistent over 128x128 output tiles, grouped raster):
-//   warps 0-7   compute: 16x16 threads, 8x8 outputs per thread
-//   warp  8     producer: one lane issues TMA loads of 128x32 fp32 x/w tiles
-//               (128-byte swizzle) into a 4-stage full/empty mbarrier ring
-//   warps 9-11  argmax recovery (only when argmax is requested)
+//   compute warps   TY x TX threads, TM x TN outputs per thread (template)
+//   producer warp   one lane issues TMA loads of 128x32 fp32 x/w tiles
+//                   (128-byte swizzle) into a 4-stage full/empty mbarrier ring
+//   recovery warps  argmax recovery (only when argmax is requested)
 //
 // Exact argmax without per-term index tracking.  The running max only grows,
 // so the lowest k attaining the final max lies in the LAST 64-wide k-chunk in
@@ -35,22 +35,53 @@ namespace tp {
 
 namespace {
 
+#ifndef TP_TMA_TM
+#define TP_TMA_TM 4
+#endif
+#ifndef TP_TMA_TN
+#define TP_TMA_TN 8
+#endif
+#ifndef TP_TMA_CHUNK
+#define TP_TMA_CHUNK 64
+#endif
+#ifndef TP_TMA_QUNROLL
+#define TP_TMA_QUNROLL 8
+#endif
+
+constexpr int QUNROLL = TP_TMA_QUNROLL;
 constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int BK = 32;           // fp32 per TMA row: 128 bytes (one swizzle atom)
 constexpr int STAGES = 4;
-constexpr int CHUNK = 64;        // argmax tracking granularity in k
-constexpr int KT_PER_CHUNK = CHUNK / BK;
-constexpr int N_COMPUTE_WARPS = 8;
-constexpr int N_RECOVERY_WARPS = 3;
-constexpr int PRODUCER_WARP = N_COMPUTE_WARPS;
-constexpr int THREADS = 32 * (N_COMPUTE_WARPS + 1 + N_RECOVERY_WARPS);  // 384
 constexpr int TILE_BYTES = BM * BK * 4;                                  // 16 KB
 constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-constexpr int SNAP_BYTES = 256 * 64 * 4;                                 // 64 KB
-constexpr int CIDX_BYTES = 256 * 64 * 2;                                 // 32 KB
+constexpr int SNAP_BYTES = BM * BN * 4;                                  // 64 KB
+constexpr int CIDX_BYTES = BM * BN * 2;                                  // 32 KB
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + SNAP_BYTES + CIDX_BYTES + 256 + 1024;
-constexpr int64_t MAX_K = (int64_t)CHUNK * 65535;  // 16-bit chunk index
+
+template <int TM_, int TN_, int CHUNK_>
+struct Cfg {
+  static constexpr int TM = TM_, TN = TN_, CHUNK = CHUNK_;
+  static constexpr int TX = BN / TN;       // threads along n
+  static constexpr int TY = BM / TM;       // threads along m
+  static constexpr int CT = TX * TY;       // compute threads
+  static constexpr int CW = CT / 32;       // compute warps
+  static constexpr int PRODUCER_WARP = CW;
+  static constexpr int RW = 3;             // recovery warps (CW + 1 + RW: multiple of 4)
+  static constexpr int THREADS = 32 * (CW + 1 + RW);
+  static constexpr int OUTS = TM * TN;     // outputs per compute thread
+  static constexpr int KT_PER_CHUNK = CHUNK / BK;
+  static constexpr int LANES_PER_OUT = CHUNK / 4;   // recovery: 4 k per lane
+  static constexpr int OUT_PER_STEP = 32 / LANES_PER_OUT;
+  static constexpr int U = CW >= 16 ? 4 : 8;        // recovery steps in flight
+  static constexpr int64_t MAX_K = (int64_t)CHUNK * 65535;  // 16-bit chunk index
+  static_assert(CT % 32 == 0, "compute threads must fill warps");
+  static_assert(OUTS % 4 == 0, "snapshot uses float4");
+  static_assert((TX % 8) == 0 && (TY % 8) == 0, "swizzle phase must be per-thread constant");
+  static_assert(CHUNK % BK == 0 && LANES_PER_OUT <= 32, "chunk");
+};
+
+using DefaultCfg = Cfg<TP_TMA_TM, TP_TMA_TN, TP_TMA_CHUNK>;
 
 struct TmaParams {
   int64_t M, N, K;
@@ -100,17 +131,100 @@ __device__ __forceinline__ uint64_t mask_pair(uint64_t v, bool lo_bad, bool hi_b
   return v;
 }
 
-template <bool kArgmax>
-__global__ void __launch_bounds__(THREADS, 1)
+// ---------------------------------------------------------------------------
+// argmax recovery for one finished tile: for each output, find the first k of
+// its recorded chunk whose sum equals the raw max (first NaN when the max is
+// NaN); write the index and the epilogue value.  A group of LANES_PER_OUT lanes
+// handles one output (4 consecutive k per lane, 16-byte loads); U steps of
+// loads are issued before any compare so that the gathers overlap.
+// ---------------------------------------------------------------------------
+template <class C>
+__device__ __forceinline__ void recover_tile(const TmaParams& p, int mt, int nt, int rw, int lane) {
+  constexpr int G = C::LANES_PER_OUT;
+  constexpr int OPS = C::OUT_PER_STEP;
+  constexpr int U = C::U;
+  const int grp = lane / G;       // output slot within a warp step
+  const int gl = lane % G;        // lane within the group
+  const int64_t m0 = (int64_t)mt * BM, n0 = (int64_t)nt * BN;
+  const int64_t mend = min((int64_t)BM, p.M - m0);
+  const int64_t nend = min((int64_t)BN, p.N - n0);
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  const int64_t total = mend * BN;
+  for (int64_t base = (int64_t)rw * OPS * U; base < total; base += (int64_t)C::RW * OPS * U) {
+    int32_t cj[U];
+    float tv[U];
+    int64_t orow[U], ocol[U];
+    bool valid[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t o = base + (int64_t)u * OPS + grp;
+      const int64_t r = o / BN, c = o % BN;
+      valid[u] = (o < total) && (c < nend);
+      orow[u] = m0 + (valid[u] ? r : 0);
+      ocol[u] = n0 + (valid[u] ? c : 0);
+      cj[u] = valid[u] ? __ldcg(p.am + orow[u] * p.lda + ocol[u]) : 0;
+      tv[u] = valid[u] ? __ldcg(p.y + orow[u] * p.ldy + ocol[u]) : 0.0f;
+    }
+    float4 xv[U], wv[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t kb = (int64_t)cj[u] * C::CHUNK + 4 * gl;
+      const bool full = valid[u] && (kb + 3 < p.K);
+      const int64_t kq = full ? kb : 0;   // in-bounds dummy address otherwise
+      xv[u] = __ldg((const float4*)(p.x + orow[u] * p.ldx + kq));
+      wv[u] = __ldg((const float4*)(p.w + ocol[u] * p.ldw + kq));
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t kb = (int64_t)cj[u] * C::CHUNK + 4 * gl;
+      float xs[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
+      float ws[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+      if (valid[u] && kb < p.K && kb + 3 >= p.K) {   // quad straddling K (K % 4 != 0)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const bool in = kb + e < p.K;
+          xs[e] = in ? __ldg(p.x + orow[u] * p.ldx + kb + e) : NEG_INF;
+          ws[e] = in ? __ldg(p.w + ocol[u] * p.ldw + kb + e) : 0.0f;
+        }
+      }
+      const bool tnan = tv[u] != tv[u];
+      int first = 4;
+#pragma unroll
+      for (int e = 3; e >= 0; --e) {
+        const float s = xs[e] + ws[e];
+        const bool hit = valid[u] && (kb + e < p.K) && (tnan ? (s != s) : (s == tv[u]));
+        if (hit) first = e;
+      }
+      const unsigned ball = __ballot_sync(0xffffffffu, first < 4);
+      const unsigned mine = (ball >> (grp * G)) & ((G == 32) ? 0xffffffffu : ((1u << G) - 1u));
+      const int wl = mine ? (__ffs(mine) - 1) : 0;
+      const int fe = __shfl_sync(0xffffffffu, first, grp * G + wl);
+      if (valid[u] && gl == 0) {
+        const int64_t k = (int64_t)cj[u] * C::CHUNK + (mine ? (4 * wl + fe) : 0);
+        p.am[orow[u] * p.lda + ocol[u]] = (int32_t)k;
+        if (p.bias != nullptr || p.scale != 1.0f) {
+          float v = tv[u];
+          if (p.bias) v = v + p.bias[ocol[u]];
+          if (p.scale != 1.0f) v = v * p.scale;
+          p.y[orow[u] * p.ldy + ocol[u]] = v;
+        }
+      }
+    }
+  }
+}
+
+template <class C, bool kArgmax>
+__global__ void __launch_bounds__(C::THREADS, 1)
     maxplus_tma_kernel(const __grid_constant__ CUtensorMap xmap,
                        const __grid_constant__ CUtensorMap wmap, const TmaParams p) {
+  constexpr int TM = C::TM, TN = C::TN, TX = C::TX, TY = C::TY, CT = C::CT;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle pattern
   unsigned char* smem =
       (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* stage_base = smem;                                  // STAGES x (x tile, w tile)
-  float4* snap = (float4*)(smem + STAGES * STAGE_BYTES);             // [16][256]
-  uint16_t* cid = (uint16_t*)(smem + STAGES * STAGE_BYTES + SNAP_BYTES);  // [64][256]
+  float4* snap = (float4*)(smem + STAGES * STAGE_BYTES);             // [OUTS/4][CT]
+  uint16_t* cid = (uint16_t*)(smem + STAGES * STAGE_BYTES + SNAP_BYTES);  // [OUTS][CT]
   uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES + SNAP_BYTES + CIDX_BYTES);
   uint64_t* full = bars;                 // [STAGES]
   uint64_t* empty = bars + STAGES;       // [STAGES]
@@ -119,22 +233,21 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  constexpr bool with_argmax = kArgmax;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       tp_mbar_init(&full[s], 1);
-      tp_mbar_init(&empty[s], N_COMPUTE_WARPS);
+      tp_mbar_init(&empty[s], C::CW);
     }
     for (int b = 0; b < 2; ++b) {
-      tp_mbar_init(&done[b], N_COMPUTE_WARPS);
-      tp_mbar_init(&freeb[b], N_RECOVERY_WARPS);
+      tp_mbar_init(&done[b], C::CW);
+      tp_mbar_init(&freeb[b], C::RW);
     }
     tp_fence_mbar_init();
   }
   __syncthreads();
 
-  if (warp == PRODUCER_WARP) {
+  if (warp == C::PRODUCER_WARP) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tp_prefetch_tensormap(&xmap);
@@ -157,95 +270,17 @@ __global__ void __launch_bounds__(THREADS, 1)
     return;
   }
 
-  if (warp > PRODUCER_WARP) {
+  if (warp > C::PRODUCER_WARP) {
     // ------------------------------------------------------------ recovery
-    if (!with_argmax) return;
-    const int rw = warp - PRODUCER_WARP - 1;  // 0..2
-    const int half = lane >> 4;               // which of the two outputs of a step
-    const int hl = lane & 15;                 // 4 consecutive k per lane
+    if (!kArgmax) return;
+    const int rw = warp - C::PRODUCER_WARP - 1;
     int lt = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
       int mt, nt;
       tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
       const int b = lt & 1;
       if (!tp_mbar_wait(&done[b], (uint32_t)((lt >> 1) & 1), p.err)) return;
-      const int64_t m0 = (int64_t)mt * BM, n0 = (int64_t)nt * BN;
-      const int64_t mend = min((int64_t)BM, p.M - m0);
-      const int64_t nend = min((int64_t)BN, p.N - n0);
-      for (int64_t r = rw; r < mend; r += N_RECOVERY_WARPS) {
-        const int64_t m = m0 + r;
-        // this lane's 4 outputs of the row: n = n0 + 4*lane + c
-        int32_t cidx[4];
-        float tgt[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int64_t nn = 4 * lane + c;
-          if (nn < nend) {
-            cidx[c] = __ldcg(p.am + m * p.lda + n0 + nn);
-            tgt[c] = __ldcg(p.y + m * p.ldy + n0 + nn);
-          } else {
-            cidx[c] = 0;
-            tgt[c] = 0.0f;
-          }
-        }
-        const float* xrow = p.x + m * p.ldx;
-        // 64 steps of two outputs each (one per half-warp)
-#pragma unroll 4
-        for (int st = 0; st < BN / 2; ++st) {
-          const int nn = 2 * st + half;           // output column within the tile
-          const int src = nn >> 2, comp = nn & 3;  // lane/slot holding its chunk
-          int32_t cj = __shfl_sync(0xffffffffu, cidx[0], src);
-          float tv = __shfl_sync(0xffffffffu, tgt[0], src);
-          const int32_t c1 = __shfl_sync(0xffffffffu, cidx[1], src);
-          const float t1 = __shfl_sync(0xffffffffu, tgt[1], src);
-          const int32_t c2 = __shfl_sync(0xffffffffu, cidx[2], src);
-          const float t2 = __shfl_sync(0xffffffffu, tgt[2], src);
-          const int32_t c3 = __shfl_sync(0xffffffffu, cidx[3], src);
-          const float t3 = __shfl_sync(0xffffffffu, tgt[3], src);
-          if (comp == 1) { cj = c1; tv = t1; }
-          if (comp == 2) { cj = c2; tv = t2; }
-          if (comp == 3) { cj = c3; tv = t3; }
-          const bool valid = nn < nend;
-          const int64_t n = n0 + nn;
-          const int64_t kb = (int64_t)cj * CHUNK + 4 * hl;
-          float xs4[4], ws4[4];
-          if (valid && kb + 3 < p.K) {
-            const float4 xv = __ldg((const float4*)(xrow + kb));
-            const float4 wv = __ldg((const float4*)(p.w + n * p.ldw + kb));
-            xs4[0] = xv.x; xs4[1] = xv.y; xs4[2] = xv.z; xs4[3] = xv.w;
-            ws4[0] = wv.x; ws4[1] = wv.y; ws4[2] = wv.z; ws4[3] = wv.w;
-          } else {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const bool in = valid && (kb + e < p.K);
-              xs4[e] = in ? __ldg(xrow + kb + e) : -__int_as_float(0x7f800000);
-              ws4[e] = in ? __ldg(p.w + n * p.ldw + kb + e) : 0.0f;
-            }
-          }
-          const bool tnan = tv != tv;
-          int first = 4;
-#pragma unroll
-          for (int e = 3; e >= 0; --e) {
-            const float s = xs4[e] + ws4[e];
-            const bool hit = (kb + e < p.K) && (tnan ? (s != s) : (s == tv));
-            if (hit) first = e;
-          }
-          const unsigned ball = __ballot_sync(0xffffffffu, first < 4);
-          const unsigned mine = (ball >> (16 * half)) & 0xffffu;
-          const int wl = mine ? (__ffs(mine) - 1) : 0;
-          const int fe = __shfl_sync(0xffffffffu, first, 16 * half + wl);
-          if (valid && hl == 0) {
-            const int64_t k = mine ? ((int64_t)cj * CHUNK + 4 * wl + fe) : (int64_t)cj * CHUNK;
-            p.am[m * p.lda + n] = (int32_t)k;
-            if (p.bias != nullptr || p.scale != 1.0f) {
-              float v = tv;
-              if (p.bias) v = v + p.bias[n];
-              if (p.scale != 1.0f) v = v * p.scale;
-              p.y[m * p.ldy + n] = v;
-            }
-          }
-        }
-      }
+      recover_tile<C>(p, mt, nt, rw, lane);
       __syncwarp();
       if (lane == 0) tp_mbar_arrive(&freeb[b]);
     }
@@ -253,9 +288,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 
   // -------------------------------------------------------------- compute
-  const int t = threadIdx.x;  // 0..255
-  const int tx = t & 15;
-  const int ty = t >> 4;
+  const int t = threadIdx.x;  // 0..CT-1
+  const int tx = t % TX;
+  const int ty = t / TX;
   const uint32_t stage_addr = tp_smem_addr(stage_base);
   const uint32_t xsw = (uint32_t)(ty & 7);
   const uint32_t wsw = (uint32_t)(tx & 7);
@@ -265,16 +300,17 @@ __global__ void __launch_bounds__(THREADS, 1)
   for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
     int mt, nt;
     tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
-    float acc[8][8];
+    float acc[TM][TN];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < TM; ++i)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] = NEG_INF;
-    if (with_argmax) {
+      for (int j = 0; j < TN; ++j) acc[i][j] = NEG_INF;
+    if (kArgmax) {
 #pragma unroll
-      for (int q = 0; q < 16; ++q) snap[q * 256 + t] = make_float4(NEG_INF, NEG_INF, NEG_INF, NEG_INF);
+      for (int q = 0; q < C::OUTS / 4; ++q)
+        snap[q * CT + t] = make_float4(NEG_INF, NEG_INF, NEG_INF, NEG_INF);
 #pragma unroll
-      for (int o = 0; o < 64; ++o) cid[o * 256 + t] = 0;
+      for (int o = 0; o < C::OUTS; ++o) cid[o * CT + t] = 0;
     }
 
     for (int kt = 0; kt < p.k_tiles; ++kt, ++it) {
@@ -285,28 +321,28 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t wbase = xbase + TILE_BYTES;
       const int64_t k0 = (int64_t)kt * BK;
       const bool tail = k0 + BK > p.K;
-#pragma unroll
+#pragma unroll QUNROLL
       for (int q = 0; q < BK / 4; ++q) {
-        uint64_t xa[8][2];
+        uint64_t xa[TM][2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          lds128(xbase + (uint32_t)(ty + 16 * i) * 128u + (((uint32_t)q ^ xsw) << 4), xa[i][0],
+        for (int i = 0; i < TM; ++i)
+          lds128(xbase + (uint32_t)(ty + TY * i) * 128u + (((uint32_t)q ^ xsw) << 4), xa[i][0],
                  xa[i][1]);
         if (tail) {
           const int64_t kq = k0 + 4 * q;
           const bool b0 = kq >= p.K, b1 = kq + 1 >= p.K, b2 = kq + 2 >= p.K, b3 = kq + 3 >= p.K;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
+          for (int i = 0; i < TM; ++i) {
             xa[i][0] = mask_pair(xa[i][0], b0, b1);
             xa[i][1] = mask_pair(xa[i][1], b2, b3);
           }
         }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < TN; ++j) {
           uint64_t wb0, wb1;
-          lds128(wbase + (uint32_t)(tx + 16 * j) * 128u + (((uint32_t)q ^ wsw) << 4), wb0, wb1);
+          lds128(wbase + (uint32_t)(tx + TX * j) * 128u + (((uint32_t)q ^ wsw) << 4), wb0, wb1);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
+          for (int i = 0; i < TM; ++i) {
             mp_pair(acc[i][j], xa[i][0], wb0);
             mp_pair(acc[i][j], xa[i][1], wb1);
           }
@@ -315,21 +351,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) tp_mbar_arrive(&empty[s]);
 
-      if (with_argmax && (((kt + 1) % KT_PER_CHUNK) == 0 || kt == p.k_tiles - 1)) {
-        const uint16_t chunk = (uint16_t)(kt / KT_PER_CHUNK);
+      if (kArgmax && (((kt + 1) % C::KT_PER_CHUNK) == 0 || kt == p.k_tiles - 1)) {
+        const uint16_t chunk = (uint16_t)(kt / C::KT_PER_CHUNK);
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          float4 sv = snap[q * 256 + t];
+        for (int q = 0; q < C::OUTS / 4; ++q) {
+          float4 sv = snap[q * CT + t];
           const float* svp = reinterpret_cast<const float*>(&sv);
           float nv[4];
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             const int o = 4 * q + c;
-            const float a = acc[o >> 3][o & 7];
+            const float a = acc[o / TN][o % TN];
             nv[c] = a;
-            if (__float_as_uint(a) != __float_as_uint(svp[c])) cid[o * 256 + t] = chunk;
+            if (__float_as_uint(a) != __float_as_uint(svp[c])) cid[o * CT + t] = chunk;
           }
-          snap[q * 256 + t] = make_float4(nv[0], nv[1], nv[2], nv[3]);
+          snap[q * CT + t] = make_float4(nv[0], nv[1], nv[2], nv[3]);
         }
       }
     }
@@ -337,23 +373,22 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---- epilogue
     const int64_t m0 = (int64_t)mt * BM, n0 = (int64_t)nt * BN;
     const int b = lt & 1;
-    if (with_argmax) {
+    if (kArgmax) {
       // recovery must have released this done/free slot (tile lt-2)
       if (!tp_mbar_wait(&freeb[b], (uint32_t)(((lt >> 1) & 1) ^ 1), p.err)) return;
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int64_t m = m0 + ty + 16 * i;
+    for (int i = 0; i < TM; ++i) {
+      const int64_t m = m0 + ty + TY * i;
       if (m >= p.M) continue;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int64_t n = n0 + tx + 16 * j;
+      for (int j = 0; j < TN; ++j) {
+        const int64_t n = n0 + tx + TX * j;
         if (n >= p.N) continue;
         float v = acc[i][j];
-        if (with_argmax) {
-          const int o = i * 8 + j;
+        if (kArgmax) {
           p.y[m * p.ldy + n] = v;  // raw max; recovery applies bias/scale
-          p.am[m * p.lda + n] = (int32_t)cid[o * 256 + t];
+          p.am[m * p.lda + n] = (int32_t)cid[(i * TN + j) * CT + t];
         } else {
           if (p.bias) v = v + p.bias[n];
           if (p.scale != 1.0f) v = v * p.scale;
@@ -361,7 +396,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-    if (with_argmax) {
+    if (kArgmax) {
       __threadfence_block();
       __syncwarp();
       if (lane == 0) tp_mbar_arrive(&done[b]);
@@ -382,6 +417,18 @@ bool make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t K, int6
   return r == CUDA_SUCCESS;
 }
 
+template <class C, bool kArgmax>
+int launch_cfg(const CUtensorMap& xmap, const CUtensorMap& wmap, const TmaParams& tp_,
+               cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(maxplus_tma_kernel<C, kArgmax>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e != cudaSuccess) return (int)e;
+  int grid = num_sms();
+  if (grid > tp_.num_tiles) grid = tp_.num_tiles;
+  maxplus_tma_kernel<C, kArgmax><<<grid, C::THREADS, SMEM_BYTES, stream>>>(xmap, wmap, tp_);
+  return launch_status();
+}
+
 }  // namespace
 
 bool maxplus_tma_eligible(const StridedMaxPlus& p) {
@@ -389,7 +436,7 @@ bool maxplus_tma_eligible(const StridedMaxPlus& p) {
   if (p.B1 * p.B2 != 1) return false;
   if (p.sx_k != 1 || p.sw_k != 1 || p.sy_n != 1) return false;
   if (p.am && p.sa_n != 1) return false;
-  if (p.M < BM || p.N < BN || p.K < 2 * BK || p.K > MAX_K) return false;
+  if (p.M < BM || p.N < BN || p.K < 2 * BK || p.K > DefaultCfg::MAX_K) return false;
   if ((p.sx_m % 4) != 0 || (p.sw_n % 4) != 0) return false;
   if (!aligned16(p.x) || !aligned16(p.w)) return false;
   if (p.M > (int64_t)INT32_MAX || p.N > (int64_t)INT32_MAX) return false;
@@ -421,20 +468,8 @@ int launch_maxplus_fwd_tma(const StridedMaxPlus& p, cudaStream_t stream) {
   tp_.k_tiles = (int)ceil_div(p.K, BK);
   tp_.num_tiles = tp_.m_tiles * tp_.n_tiles;
   tp_.err = device_error_ptr();
-  // The attribute is per function and per device; setting it is cheap.
-  cudaError_t e = cudaFuncSetAttribute(maxplus_tma_kernel<true>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(maxplus_tma_kernel<false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  if (e != cudaSuccess) return (int)e;
-  int grid = num_sms();
-  if (grid > tp_.num_tiles) grid = tp_.num_tiles;
-  if (p.am)
-    maxplus_tma_kernel<true><<<grid, THREADS, SMEM_BYTES, stream>>>(xmap, wmap, tp_);
-  else
-    maxplus_tma_kernel<false><<<grid, THREADS, SMEM_BYTES, stream>>>(xmap, wmap, tp_);
-  return launch_status();
+  if (p.am) return launch_cfg<DefaultCfg, true>(xmap, wmap, tp_, stream);
+  return launch_cfg<DefaultCfg, false>(xmap, wmap, tp_, stream);
 }
 
 }  // namespace tp

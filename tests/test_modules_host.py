@@ -1,0 +1,58 @@
+"""Host-side checks of the drop-in modules (no GPU): names, parameters and
+state-dict layout match the reference's (from the golden fixtures), and CPU
+inputs are refused rather than silently computed on the CPU."""
+import pytest
+import torch
+
+from conftest import load_golden
+
+
+def _golden_state(name):
+    g = load_golden(name)
+    return {k[2:]: v for k, v in g.items() if k.startswith("p_")}
+
+
+def test_dtn_state_dict_matches_reference():
+    from mk_iii_technologies_tsrn_b200.dtn import DTNAttention
+    ref = _golden_state("dtn_block")
+    mod = DTNAttention(32, 4, dropout=0.0)
+    ours = mod.state_dict()
+    assert set(ours) == set(ref)
+    for k, v in ref.items():
+        assert tuple(ours[k].shape) == v.shape, k
+    mod.load_state_dict({k: torch.tensor(v) for k, v in ref.items()})
+
+
+def test_ssm_state_dict_matches_reference():
+    from mk_iii_technologies_tsrn_b200.ssm import TropicalSSM
+    ref = _golden_state("tsrn_ssm")
+    mod = TropicalSSM(16, 8)
+    ours = mod.state_dict()
+    assert set(ours) == set(ref)
+    for k, v in ref.items():
+        assert tuple(ours[k].shape) == v.shape, k
+
+
+def test_tropical_linear_surface():
+    from mk_iii_technologies_tsrn_b200.tropical import TropicalLinear
+    from mk_iii_technologies_tsrn_b200.maxplus_binding import CUDATropicalLinear
+    assert TropicalLinear._ste_temp == 1.0
+    for cls, kw in ((TropicalLinear, {}), (CUDATropicalLinear, {"ste_temp": 1.0})):
+        layer = cls(64, 32, bias=True, **kw)
+        assert set(layer.state_dict()) == {"weight", "bias"}
+        assert layer.weight.shape == (32, 64) and layer.bias.shape == (32,)
+        assert float(layer.weight.min()) >= -0.5 and float(layer.weight.max()) <= 0.5
+        assert torch.all(layer.bias == 0)
+        assert cls(8, 4, bias=False).bias is None
+
+
+def test_cpu_inputs_are_refused():
+    from mk_iii_technologies_tsrn_b200.tropical import TropicalLinear
+    layer = TropicalLinear(8, 4)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        layer(torch.randn(2, 8))
+
+
+def test_is_cuda_kernel_available_without_gpu():
+    from mk_iii_technologies_tsrn_b200.maxplus_binding import is_cuda_kernel_available
+    assert is_cuda_kernel_available() == torch.cuda.is_available()
