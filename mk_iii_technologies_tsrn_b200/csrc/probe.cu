@@ -1,13 +1,16 @@
 // probe.cu -- register-only microbenchmark of the CUDA-core max-plus term rate.
 //
-// It measures the roofline denominator for the max-plus GEMM: how many
-// (add, max) terms per second an SM can retire when nothing but arithmetic
-// is issued.  Each thread keeps an 8x8 block of independent accumulators
-// (the GEMM kernel's register tile) and folds 128 terms per iteration.
+// It measures how close a loop of nothing but max-plus arithmetic gets to the
+// issue limit of the GEMM kernel's instruction form (one add.f32x2 and one
+// 3-input max per two terms: 128 terms per clock per SM).  Each thread keeps
+// an 8x8 block of independent accumulators (the GEMM's register tile) and
+// folds 128 terms per iteration.  The x operands are advanced by one packed
+// add each per iteration (8 extra adds per 128 terms) so that no sum is loop
+// invariant -- otherwise the compiler hoists every add out of the loop and
+// the loop measures the max instruction alone.
 //   form 0: add.rn.f32 + 2-input max.f32 per term (4 instructions / 2 terms)
 //   form 1: add.rn.f32x2 + 3-input max.f32 per two terms (2 instructions)
 //   form 2: add.rn.f32x2 + 3-input max.NaN.f32 (the GEMM kernel's form)
-// The asm statements are volatile so the loop body is executed as written.
 #include "maxplus_internal.cuh"
 
 namespace tp {
@@ -57,7 +60,11 @@ __global__ void __launch_bounds__(256) probe_kernel(int64_t iters, float* sink) 
   for (int i = 0; i < 8; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[i][j] = -1.0e30f;
+  const uint64_t step = ((uint64_t)__float_as_uint(1.0e-3f) << 32) | __float_as_uint(-1.0e-3f);
   for (int64_t it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      asm volatile("add.rn.f32x2 %0, %0, %1;" : "+l"(xa[i]) : "l"(step));
 #pragma unroll
     for (int j = 0; j < 8; ++j)
 #pragma unroll
