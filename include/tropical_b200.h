@@ -200,6 +200,31 @@ TP_API int tp_scan_bwd(int64_t B, int64_t T, int64_t C,
                 float* gu, float* ga, float* gh0,
                 float* workspace, void* stream);
 
+/* Allocation-free form of tp_scan_bwd, for callers that cannot allocate
+ * device memory themselves: a thin FFI binding that only forwards pointers of
+ * buffers some other runtime already owns, or a process whose device memory
+ * belongs entirely to another framework's pool, where a raw cudaMalloc would
+ * synchronise the device and fragment that pool.  There is no counterpart in
+ * the reference.
+ *
+ * Same arguments, results and validation as tp_scan_bwd, without the
+ * workspace: the [B, C] partial sums behind ga live in one fixed array of this
+ * library's device memory (1 MiB per GPU that loads the library, held until
+ * the process exits).  Limit: when ga is requested, B*C <= 262144, else the
+ * call returns TP_ERR_TOO_LARGE and launches nothing.  No allocation or free
+ * happens in this call.  The first call on a device looks up that device's
+ * array address (cudaGetSymbolAddress) -- make that first call outside any
+ * stream capture.  Every entry of the array that a call reads it has written
+ * first, so nothing needs clearing, but all calls share the one array: calls
+ * whose kernels overlap on the GPU (other streams, other host threads) race
+ * and must be serialised by the caller. */
+TP_API int tp_scan_bwd_noalloc(int64_t B, int64_t T, int64_t C,
+                               const float* gh,
+                               const float* bb, const float* xx, const float* a,
+                               float h_init, const float* h0, const float* h,
+                               const uint32_t* win_mask,
+                               float* gu, float* ga, float* gh0, void* stream);
+
 /* ======================================================================== *
  *  Roofline probe: register-only add+max loop measuring the CUDA-core
  *  max-plus term rate.  form 0: FADD + 2-input FMNMX per term;

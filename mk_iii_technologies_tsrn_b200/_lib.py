@@ -73,6 +73,11 @@ SIGNATURES: dict[str, tuple] = {
         [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
          _c_p, _c_p],
     ),
+    "tp_scan_bwd_noalloc": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
+         _c_p],
+    ),
     "tp_probe_addmax": (_c_int, [_c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_p]),
     "maxplus_forward_cuda": (None, [_c_p, _c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_bool]),
     "maxplus_backward_cuda": (

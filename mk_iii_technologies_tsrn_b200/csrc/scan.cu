@@ -19,6 +19,8 @@
 // staged by TMA into a ring of shared-memory stages (mbarrier per stage) so
 // that each warp keeps several KB of loads in flight -- the kernel is bound
 // by HBM bandwidth, not by the dependency chain (~12 cycles/step/warp).
+#include <mutex>
+
 #include "maxplus_internal.cuh"
 
 namespace tp {
@@ -353,3 +355,53 @@ int launch_scan_bwd(const ScanArgs& p_in, cudaStream_t stream) {
 }
 
 }  // namespace tp
+
+// ---------------------------------------------------------------------------
+// Allocation-free backward: tp_scan_bwd with its [B, C] partial-sum workspace
+// taken from a fixed array in this library's device memory instead of from
+// the caller.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kScanNoAllocMaxLanes = 262144;  // B*C limit (1 MiB of fp32 partials)
+
+// One array per GPU that loads the library, kept until the process exits.
+static __device__ __align__(256) float g_scan_ga_scratch[kScanNoAllocMaxLanes];
+
+// Device address of g_scan_ga_scratch on the current device.  The name of the
+// array in host code is only a host-side stand-in, so the address is fetched
+// with cudaGetSymbolAddress once per device (with that device current) and
+// cached.
+int scan_scratch_address(float** out) {
+  static std::mutex mu;
+  static float* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= 64) return TP_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_scan_ga_scratch);
+    if (e != cudaSuccess) return (int)e;
+    addr[dev] = static_cast<float*>(ptr);
+  }
+  *out = addr[dev];
+  return TP_OK;
+}
+
+}  // namespace
+
+extern "C" int tp_scan_bwd_noalloc(int64_t B, int64_t T, int64_t C, const float* gh,
+                                   const float* bb, const float* xx, const float* a,
+                                   float h_init, const float* h0, const float* h,
+                                   const uint32_t* win_mask, float* gu, float* ga, float* gh0,
+                                   void* stream) {
+  float* ws = nullptr;
+  if (ga != nullptr && B > 0 && C > 0) {
+    if (B > kScanNoAllocMaxLanes / C) return TP_ERR_TOO_LARGE;
+    const int s = scan_scratch_address(&ws);
+    if (s != TP_OK) return s;
+  }
+  return tp_scan_bwd(B, T, C, gh, bb, xx, a, h_init, h0, h, win_mask, gu, ga, gh0, ws, stream);
+}
