@@ -299,30 +299,31 @@ def gemm_workload(args, world, rank):
     h2d = (hx.numel() + hW.numel()) * 4
     d2h = (hy.numel() + ham.numel()) * 4
 
-    # ---- roofline.  Max-plus is CUDA-core work: per two terms one add.f32x2
-    # (FMA pipe) and one 3-input max (ALU pipe); at one instruction per clock
-    # per SM sub-partition that is 128 terms (256 ops) per clock per SM.  The
-    # peak is that issue limit at the SM clock sampled during the timed region
-    # (max clock if no sample); the register-only probe shows how close a loop
-    # of pure arithmetic gets to it.
+    # ---- roofline.  Max-plus is CUDA-core work (one add and one max per term;
+    # tensor cores do not apply).  The peak is the fastest rate any form of the
+    # add+max instruction mix reaches in the register-only probe, measured in
+    # this run (forms: scalar, packed add.f32x2, 3-input max, mixes).  For
+    # context, the nominal issue limit of the packed form is 128 terms per
+    # clock per SM; measured forms reach about half of it.
     probe = {}
-    for form in (0, 1, 2):
+    for form in range(5):
         ops.probe_addmax(form, 148 * 8, 50)                      # warm
         pms, terms = ops.probe_addmax(form, 148 * 8, 400)
         probe[form] = 2.0 * terms / (pms / 1e3) / 1e12           # Top/s (2 ops per term)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     mhz = (clk or {}).get("sm_mhz") or measured_peaks().get("sm_max_mhz", 1965.0)
-    peak = 256.0 * sms * mhz * 1e6 / 1e12
+    issue_limit = 256.0 * sms * mhz * 1e6 / 1e12
+    peak = max(probe.values())
     per_gpu_ops = 2.0 * M * Nr * K
     achieved = per_gpu_ops / (kms / 1e3) / 1e12
     roofline = {"bound": "cuda-core", "achieved": achieved, "peak": peak, "unit": "Top/s",
                 "frac": achieved / peak, "traffic": None,
-                "peak_source": f"issue limit of add.f32x2 + 3-input max (128 terms/clk/SM) x "
-                               f"{sms} SMs x {mhz:.0f} MHz (sampled SM clock)",
+                "peak_source": "in-repo register-only add+max probe (tp_probe_addmax), best of "
+                               "5 instruction forms, measured in this run; of measured",
                 "probe_top_s": {"fadd_fmnmx": probe[0], "fadd2_fmnmx3": probe[1],
-                                "fadd2_fmnmx3_nan": probe[2],
-                                "note": "register-only loop incl. 8 operand-advance adds per "
-                                        "128 terms"},
+                                "fadd2_fmnmx3_nan": probe[2], "2fadd_fmnmx3_nan": probe[3],
+                                "mixed": probe[4]},
+                "nominal_issue_limit_top_s": issue_limit,
                 "kernel_ms": kms}
     res = {
         "metric": "max-plus GEMM Gop/s (fp32, with int32 argmax)",

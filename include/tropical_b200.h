@@ -229,7 +229,8 @@ TP_API int tp_scan_bwd_noalloc(int64_t B, int64_t T, int64_t C,
  *  Roofline probe: register-only add+max loop measuring the CUDA-core
  *  max-plus term rate.  form 0: FADD + 2-input FMNMX per term;
  *  form 1: packed add.f32x2 + 3-input max per two terms; form 2: form 1 with
- *  NaN-propagating max.  Each of `threads` threads runs `iters` iterations
+ *  NaN-propagating max; form 3: two scalar adds + 3-input NaN max per two
+ *  terms; form 4: forms 2 and 3 alternating.  Each of `threads` threads runs `iters` iterations
  *  of 64 terms; the caller times the launch.  sink receives one float per
  *  thread (keeps the work live).
  * ======================================================================== */

@@ -275,7 +275,7 @@ int tp_scan_bwd(int64_t B, int64_t T, int64_t C, const float* gh, const float* b
 
 int tp_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters, float* sink,
                     void* stream) {
-  TP_RETURN_IF(form < 0 || form > 2 || blocks <= 0 || blocks > 65535 || iters < 0,
+  TP_RETURN_IF(form < 0 || form > 4 || blocks <= 0 || blocks > 65535 || iters < 0,
                TP_ERR_INVALID_ARG);
   TP_CHECK_PTR(sink);
   return launch_probe_addmax(form, blocks, threads, iters, sink, as_stream(stream));

@@ -5,27 +5,29 @@
 // This is the large-problem path of tp_maxplus_fwd (the tropical linear of
 // tropformer.py:127-145 at GEMM scale, and the M=N=K sweep).  Max-plus is not
 // a multiply-add, so tensor cores do not apply; the kernel is bound by the
-// CUDA-core issue rate.  Per two k-terms of one output it issues exactly two
+// CUDA-core add and max rates.  Per two k-terms of one output it issues two
 // instructions: one packed add.rn.f32x2 (both sums, each one rounded fp32
 // add) and one 3-input max.NaN.f32 folding both sums into the accumulator.
 //
 // CTA (one per SM, persistent over 128x128 output tiles, grouped raster):
 //   compute warps   TY x TX threads, TM x TN outputs per thread (template)
 //   producer warp   one lane issues TMA loads of 128x32 fp32 x/w tiles
-//                   (128-byte swizzle) into a 4-stage full/empty mbarrier ring
-//   recovery warps  argmax recovery (only when argmax is requested)
+//                   (128-byte swizzle, no multicast) into a 4-stage
+//                   full/empty mbarrier ring
 //
 // Exact argmax without per-term index tracking.  The running max only grows,
-// so the lowest k attaining the final max lies in the LAST 64-wide k-chunk in
-// which the accumulator changed.  Every 64 k the compute threads compare
-// their accumulators with a snapshot kept in shared memory (bitwise, so NaN
-// counts once) and record the chunk index (16-bit, in shared memory).  At the end of a tile they store the raw max and
-// the chunk index to y/argmax and hand the tile to the recovery warps, which,
-// while the compute warps already run the next tile, re-read the 64 terms of
-// each output's chunk from global memory (L2), find the first k whose sum
-// equals the max (or is NaN when the max is NaN), and write the final argmax
-// and the epilogue value.  The result equals torch.max(dim=-1) on the
-// reference's broadcast tensor, bit for bit, in values and indices.
+// so the lowest k attaining the final max lies in the LAST CHUNK-wide k-range
+// in which the accumulator changed.  At each chunk boundary the compute
+// threads compare their accumulators with a snapshot kept in shared memory
+// (bitwise, so NaN counts once) and record the chunk index (16-bit, shared
+// memory).  After the main pass over K the producer streams the tile's
+// k-tiles through the ring a second time (the data is mostly still in L2).
+// The outputs are first bucketed by chunk (a counting sort in shared memory),
+// so that each chunk's outputs are searched by all compute warps evenly,
+// straight from shared memory: the first k whose sum equals the output's max
+// (or is NaN when the max is NaN) is its argmax.  The
+// result equals torch.max(dim=-1) on the reference's broadcast tensor, bit
+// for bit, in values and indices.
 //
 // Every mbarrier wait is bounded (common.cuh); a timeout records a device
 // error and the kernel returns.
@@ -57,7 +59,10 @@ constexpr int TILE_BYTES = BM * BK * 4;                                  // 16 K
 constexpr int STAGE_BYTES = 2 * TILE_BYTES;
 constexpr int SNAP_BYTES = BM * BN * 4;                                  // 64 KB
 constexpr int CIDX_BYTES = BM * BN * 2;                                  // 32 KB
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + SNAP_BYTES + CIDX_BYTES + 256 + 1024;
+constexpr int MAX_ARGMAX_CHUNKS = 512;                                   // argmax path: K <= 512*CHUNK
+constexpr int OFFS_BYTES = (MAX_ARGMAX_CHUNKS + 8) * 2;                  // u16 bucket offsets
+constexpr int SMEM_BYTES =
+    STAGES * STAGE_BYTES + SNAP_BYTES + CIDX_BYTES + OFFS_BYTES + 128 + 1024;
 
 template <int TM_, int TN_, int CHUNK_>
 struct Cfg {
@@ -67,28 +72,20 @@ struct Cfg {
   static constexpr int CT = TX * TY;       // compute threads
   static constexpr int CW = CT / 32;       // compute warps
   static constexpr int PRODUCER_WARP = CW;
-  static constexpr int RW = 3;             // recovery warps (CW + 1 + RW: multiple of 4)
-  static constexpr int THREADS = 32 * (CW + 1 + RW);
+  static constexpr int THREADS = 32 * (CW + 1);
   static constexpr int OUTS = TM * TN;     // outputs per compute thread
   static constexpr int KT_PER_CHUNK = CHUNK / BK;
-  static constexpr int LANES_PER_OUT = CHUNK / 4;   // recovery: 4 k per lane
-  static constexpr int OUT_PER_STEP = 32 / LANES_PER_OUT;
-  static constexpr int U = CW >= 16 ? 4 : 8;        // recovery steps in flight
   static constexpr int64_t MAX_K = (int64_t)CHUNK * 65535;  // 16-bit chunk index
   static_assert(CT % 32 == 0, "compute threads must fill warps");
   static_assert(OUTS % 4 == 0, "snapshot uses float4");
   static_assert((TX % 8) == 0 && (TY % 8) == 0, "swizzle phase must be per-thread constant");
-  static_assert(CHUNK % BK == 0 && LANES_PER_OUT <= 32, "chunk");
+  static_assert(CHUNK % BK == 0 && KT_PER_CHUNK <= STAGES, "a chunk must fit the ring");
 };
 
 using DefaultCfg = Cfg<TP_TMA_TM, TP_TMA_TN, TP_TMA_CHUNK>;
 
 struct TmaParams {
   int64_t M, N, K;
-  const float* x;
-  int64_t ldx;
-  const float* w;
-  int64_t ldw;
   const float* bias;
   float* y;
   int64_t ldy;
@@ -124,6 +121,12 @@ __device__ __forceinline__ void lds128(uint32_t addr, uint64_t& a, uint64_t& b) 
   asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr));
 }
 
+__device__ __forceinline__ float lds32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+
 __device__ __forceinline__ uint64_t mask_pair(uint64_t v, bool lo_bad, bool hi_bad) {
   const uint64_t NEG = 0xff800000ull;
   if (lo_bad) v = (v & 0xffffffff00000000ull) | NEG;
@@ -131,86 +134,29 @@ __device__ __forceinline__ uint64_t mask_pair(uint64_t v, bool lo_bad, bool hi_b
   return v;
 }
 
-// ---------------------------------------------------------------------------
-// argmax recovery for one finished tile: for each output, find the first k of
-// its recorded chunk whose sum equals the raw max (first NaN when the max is
-// NaN); write the index and the epilogue value.  A group of LANES_PER_OUT lanes
-// handles one output (4 consecutive k per lane, 16-byte loads); U steps of
-// loads are issued before any compare so that the gathers overlap.
-// ---------------------------------------------------------------------------
-template <class C>
-__device__ __forceinline__ void recover_tile(const TmaParams& p, int mt, int nt, int rw, int lane) {
-  constexpr int G = C::LANES_PER_OUT;
-  constexpr int OPS = C::OUT_PER_STEP;
-  constexpr int U = C::U;
-  const int grp = lane / G;       // output slot within a warp step
-  const int gl = lane % G;        // lane within the group
-  const int64_t m0 = (int64_t)mt * BM, n0 = (int64_t)nt * BN;
-  const int64_t mend = min((int64_t)BM, p.M - m0);
-  const int64_t nend = min((int64_t)BN, p.N - n0);
-  const float NEG_INF = -__int_as_float(0x7f800000);
-  const int64_t total = mend * BN;
-  for (int64_t base = (int64_t)rw * OPS * U; base < total; base += (int64_t)C::RW * OPS * U) {
-    int32_t cj[U];
-    float tv[U];
-    int64_t orow[U], ocol[U];
-    bool valid[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t o = base + (int64_t)u * OPS + grp;
-      const int64_t r = o / BN, c = o % BN;
-      valid[u] = (o < total) && (c < nend);
-      orow[u] = m0 + (valid[u] ? r : 0);
-      ocol[u] = n0 + (valid[u] ? c : 0);
-      cj[u] = valid[u] ? __ldcg(p.am + orow[u] * p.lda + ocol[u]) : 0;
-      tv[u] = valid[u] ? __ldcg(p.y + orow[u] * p.ldy + ocol[u]) : 0.0f;
-    }
-    float4 xv[U], wv[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t kb = (int64_t)cj[u] * C::CHUNK + 4 * gl;
-      const bool full = valid[u] && (kb + 3 < p.K);
-      const int64_t kq = full ? kb : 0;   // in-bounds dummy address otherwise
-      xv[u] = __ldg((const float4*)(p.x + orow[u] * p.ldx + kq));
-      wv[u] = __ldg((const float4*)(p.w + ocol[u] * p.ldw + kq));
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t kb = (int64_t)cj[u] * C::CHUNK + 4 * gl;
-      float xs[4] = {xv[u].x, xv[u].y, xv[u].z, xv[u].w};
-      float ws[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
-      if (valid[u] && kb < p.K && kb + 3 >= p.K) {   // quad straddling K (K % 4 != 0)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const bool in = kb + e < p.K;
-          xs[e] = in ? __ldg(p.x + orow[u] * p.ldx + kb + e) : NEG_INF;
-          ws[e] = in ? __ldg(p.w + ocol[u] * p.ldw + kb + e) : 0.0f;
-        }
-      }
-      const bool tnan = tv[u] != tv[u];
-      int first = 4;
-#pragma unroll
-      for (int e = 3; e >= 0; --e) {
-        const float s = xs[e] + ws[e];
-        const bool hit = valid[u] && (kb + e < p.K) && (tnan ? (s != s) : (s == tv[u]));
-        if (hit) first = e;
-      }
-      const unsigned ball = __ballot_sync(0xffffffffu, first < 4);
-      const unsigned mine = (ball >> (grp * G)) & ((G == 32) ? 0xffffffffu : ((1u << G) - 1u));
-      const int wl = mine ? (__ffs(mine) - 1) : 0;
-      const int fe = __shfl_sync(0xffffffffu, first, grp * G + wl);
-      if (valid[u] && gl == 0) {
-        const int64_t k = (int64_t)cj[u] * C::CHUNK + (mine ? (4 * wl + fe) : 0);
-        p.am[orow[u] * p.lda + ocol[u]] = (int32_t)k;
-        if (p.bias != nullptr || p.scale != 1.0f) {
-          float v = tv[u];
-          if (p.bias) v = v + p.bias[ocol[u]];
-          if (p.scale != 1.0f) v = v * p.scale;
-          p.y[orow[u] * p.ldy + ocol[u]] = v;
-        }
-      }
-    }
-  }
+// Barrier among the compute threads only (the producer warp never takes
+// part), on an mbarrier so that the wait is bounded like every other wait:
+// every compute thread arrives, then waits for the phase to complete.
+__device__ __forceinline__ bool compute_sync(uint64_t* bar, uint32_t& phase, int* err) {
+  tp_mbar_arrive(bar);
+  const bool ok = tp_mbar_wait(bar, phase, err);
+  phase ^= 1u;
+  return ok;
+}
+
+// atomic post-increment of a 16-bit shared counter (through its aligned word)
+__device__ __forceinline__ uint32_t atomicAdd_u16(uint16_t* p) {
+  uint32_t* w = (uint32_t*)((uintptr_t)p & ~(uintptr_t)3);
+  const uint32_t sh = ((uintptr_t)p & 2) ? 16u : 0u;
+  const uint32_t old = atomicAdd(w, 1u << sh);
+  return (old >> sh) & 0xffffu;
+}
+
+// shared-memory address of element (row, k) of a 128 x 32 fp32 tile stored
+// with the 128-byte TMA swizzle (16-byte chunk c of row r sits at c ^ (r & 7))
+__device__ __forceinline__ uint32_t swz(uint32_t base, int row, int k) {
+  return base + (uint32_t)row * 128u + ((((uint32_t)k >> 2) ^ ((uint32_t)row & 7u)) << 4) +
+         ((uint32_t)k & 3u) * 4u;
 }
 
 template <class C, bool kArgmax>
@@ -225,24 +171,24 @@ __global__ void __launch_bounds__(C::THREADS, 1)
   unsigned char* stage_base = smem;                                  // STAGES x (x tile, w tile)
   float4* snap = (float4*)(smem + STAGES * STAGE_BYTES);             // [OUTS/4][CT]
   uint16_t* cid = (uint16_t*)(smem + STAGES * STAGE_BYTES + SNAP_BYTES);  // [OUTS][CT]
-  uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES + SNAP_BYTES + CIDX_BYTES);
+  uint16_t* offs = (uint16_t*)(smem + STAGES * STAGE_BYTES + SNAP_BYTES + CIDX_BYTES);
+  uint64_t* bars =
+      (uint64_t*)(smem + STAGES * STAGE_BYTES + SNAP_BYTES + CIDX_BYTES + OFFS_BYTES);
   uint64_t* full = bars;                 // [STAGES]
   uint64_t* empty = bars + STAGES;       // [STAGES]
-  uint64_t* done = bars + 2 * STAGES;    // [2] compute -> recovery
-  uint64_t* freeb = bars + 2 * STAGES + 2;  // [2] recovery -> compute
+  uint64_t* cbar = bars + 2 * STAGES;    // compute-thread barrier
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // k-tile passes per output tile: the main pass, plus the argmax pass
+  constexpr int PASSES = kArgmax ? 2 : 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       tp_mbar_init(&full[s], 1);
       tp_mbar_init(&empty[s], C::CW);
     }
-    for (int b = 0; b < 2; ++b) {
-      tp_mbar_init(&done[b], C::CW);
-      tp_mbar_init(&freeb[b], C::RW);
-    }
+    tp_mbar_init(cbar, CT);
     tp_fence_mbar_init();
   }
   __syncthreads();
@@ -256,33 +202,35 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
         int mt, nt;
         tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
-        for (int kt = 0; kt < p.k_tiles; ++kt, ++it) {
-          const uint32_t s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1u;
-          if (!tp_mbar_wait(&empty[s], ph ^ 1u, p.err)) return;
-          unsigned char* dst = stage_base + s * STAGE_BYTES;
-          tp_mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-          tp_tma_load_2d(dst, &xmap, kt * BK, mt * BM, &full[s]);
-          tp_tma_load_2d(dst + TILE_BYTES, &wmap, kt * BK, nt * BN, &full[s]);
+        for (int pass = 0; pass < PASSES; ++pass) {
+          // main pass in k order; the argmax pass chunk by chunk from the last
+          // chunk back (its k-tiles were read most recently: likelier L2 hits)
+          const int nchunks = (p.k_tiles + C::KT_PER_CHUNK - 1) / C::KT_PER_CHUNK;
+          for (int i = 0; i < p.k_tiles; ++i, ++it) {
+            int kt = i;
+            if (pass == 1) {
+              const int c = nchunks - 1 - i / C::KT_PER_CHUNK;   // valid: chunks are full
+              kt = c * C::KT_PER_CHUNK + i % C::KT_PER_CHUNK;    // except the last one,
+              if (nchunks * C::KT_PER_CHUNK != p.k_tiles) {       // which comes first
+                const int last = p.k_tiles - (nchunks - 1) * C::KT_PER_CHUNK;  // its size
+                if (i < last) {
+                  kt = (nchunks - 1) * C::KT_PER_CHUNK + i;
+                } else {
+                  const int j = i - last;
+                  kt = (nchunks - 2 - j / C::KT_PER_CHUNK) * C::KT_PER_CHUNK + j % C::KT_PER_CHUNK;
+                }
+              }
+            }
+            const uint32_t s = it % STAGES;
+            const uint32_t ph = (it / STAGES) & 1u;
+            if (!tp_mbar_wait(&empty[s], ph ^ 1u, p.err)) return;
+            unsigned char* dst = stage_base + s * STAGE_BYTES;
+            tp_mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+            tp_tma_load_2d(dst, &xmap, kt * BK, mt * BM, &full[s]);
+            tp_tma_load_2d(dst + TILE_BYTES, &wmap, kt * BK, nt * BN, &full[s]);
+          }
         }
       }
-    }
-    return;
-  }
-
-  if (warp > C::PRODUCER_WARP) {
-    // ------------------------------------------------------------ recovery
-    if (!kArgmax) return;
-    const int rw = warp - C::PRODUCER_WARP - 1;
-    int lt = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
-      int mt, nt;
-      tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
-      const int b = lt & 1;
-      if (!tp_mbar_wait(&done[b], (uint32_t)((lt >> 1) & 1), p.err)) return;
-      recover_tile<C>(p, mt, nt, rw, lane);
-      __syncwarp();
-      if (lane == 0) tp_mbar_arrive(&freeb[b]);
     }
     return;
   }
@@ -292,14 +240,16 @@ __global__ void __launch_bounds__(C::THREADS, 1)
   const int tx = t % TX;
   const int ty = t / TX;
   const uint32_t stage_addr = tp_smem_addr(stage_base);
+  const uint32_t snap_addr = tp_smem_addr(snap);
   const uint32_t xsw = (uint32_t)(ty & 7);
   const uint32_t wsw = (uint32_t)(tx & 7);
   const float NEG_INF = -__int_as_float(0x7f800000);
   uint32_t it = 0;
-  int lt = 0;
-  for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
+  uint32_t cphase = 0;
+  for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
     int mt, nt;
     tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+    const int64_t m0 = (int64_t)mt * BM, n0 = (int64_t)nt * BN;
     float acc[TM][TN];
 #pragma unroll
     for (int i = 0; i < TM; ++i)
@@ -313,6 +263,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       for (int o = 0; o < C::OUTS; ++o) cid[o * CT + t] = 0;
     }
 
+    // ---- main pass: values (+ chunk tracking)
     for (int kt = 0; kt < p.k_tiles; ++kt, ++it) {
       const uint32_t s = it % STAGES;
       const uint32_t ph = (it / STAGES) & 1u;
@@ -370,37 +321,184 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       }
     }
 
-    // ---- epilogue
-    const int64_t m0 = (int64_t)mt * BM, n0 = (int64_t)nt * BN;
-    const int b = lt & 1;
-    if (kArgmax) {
-      // recovery must have released this done/free slot (tile lt-2)
-      if (!tp_mbar_wait(&freeb[b], (uint32_t)(((lt >> 1) & 1) ^ 1), p.err)) return;
-    }
+    if (!kArgmax) {
+      // ---- value-only epilogue
 #pragma unroll
-    for (int i = 0; i < TM; ++i) {
-      const int64_t m = m0 + ty + TY * i;
-      if (m >= p.M) continue;
+      for (int i = 0; i < TM; ++i) {
+        const int64_t m = m0 + ty + TY * i;
+        if (m >= p.M) continue;
 #pragma unroll
-      for (int j = 0; j < TN; ++j) {
-        const int64_t n = n0 + tx + TX * j;
-        if (n >= p.N) continue;
-        float v = acc[i][j];
-        if (kArgmax) {
-          p.y[m * p.ldy + n] = v;  // raw max; recovery applies bias/scale
-          p.am[m * p.lda + n] = (int32_t)cid[(i * TN + j) * CT + t];
-        } else {
+        for (int j = 0; j < TN; ++j) {
+          const int64_t n = n0 + tx + TX * j;
+          if (n >= p.N) continue;
+          float v = acc[i][j];
           if (p.bias) v = v + p.bias[n];
           if (p.scale != 1.0f) v = v * p.scale;
           p.y[m * p.ldy + n] = v;
         }
       }
+      continue;
     }
-    if (kArgmax) {
-      __threadfence_block();
-      __syncwarp();
-      if (lane == 0) tp_mbar_arrive(&done[b]);
+
+    // ---- argmax pass.  The snapshot holds each output's final max and cid its
+    // last-change chunk.  First bucket the tile's outputs by chunk (counting
+    // sort in shared memory; the list overwrites cid), then stream the tile's
+    // k-tiles through the ring again; each chunk's outputs are shared evenly
+    // by the CTA's 4-lane groups, which search 8 k per lane and k-tile with
+    // 16-byte shared loads and write the argmax and the final value.
+    const int nchunks = (p.k_tiles + C::KT_PER_CHUNK - 1) / C::KT_PER_CHUNK;
+    for (int c = t; c <= nchunks; c += CT) offs[c] = 0;
+    if (!compute_sync(cbar, cphase, p.err)) return;
+#pragma unroll 4
+    for (int o = 0; o < C::OUTS; ++o) {                   // count per chunk (in offs[c+1])
+      const bool valid = (m0 + ty + TY * (o / TN) < p.M) && (n0 + tx + TX * (o % TN) < p.N);
+      if (valid) atomicAdd_u16(&offs[cid[o * CT + t] + 1]);
     }
+    if (!compute_sync(cbar, cphase, p.err)) return;
+    if (warp == 0) {                              // prefix sum: offs[c] = start of chunk c
+      uint32_t carry = 0;
+      for (int base = 0; base <= nchunks; base += 32) {
+        const int c = base + lane;
+        uint32_t v = c <= nchunks ? offs[c] : 0u;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const uint32_t up = __shfl_up_sync(0xffffffffu, v, d);
+          if (lane >= d) v += up;
+        }
+        if (c <= nchunks) offs[c] = (uint16_t)(v + carry);
+        carry += __shfl_sync(0xffffffffu, v, 31);
+      }
+    }
+    {
+      // my outputs' chunk ids, two per register (0xFFFF: not an output); read
+      // before the barrier, because the list below overwrites cid
+      uint32_t cr[C::OUTS / 2];
+#pragma unroll
+      for (int q = 0; q < C::OUTS / 2; ++q) {
+        uint32_t v[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int o = 2 * q + h;
+          const bool valid = (m0 + ty + TY * (o / TN) < p.M) && (n0 + tx + TX * (o % TN) < p.N);
+          v[h] = valid ? (uint32_t)cid[o * CT + t] : 0xFFFFu;
+        }
+        cr[q] = v[0] | (v[1] << 16);
+      }
+      if (!compute_sync(cbar, cphase, p.err)) return;
+      // scatter: the counter of each chunk walks from its start to its end, so
+      // afterwards offs[c] is the end of chunk c (= start of chunk c+1)
+#pragma unroll
+      for (int q = 0; q < C::OUTS / 2; ++q) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t c = h ? (cr[q] >> 16) : (cr[q] & 0xffffu);
+          if (c != 0xFFFFu) {
+            const uint32_t pos = atomicAdd_u16(&offs[c]);
+            cid[pos] = (uint16_t)((2 * q + h) * CT + t);   // list entry: output slot
+          }
+        }
+      }
+    }
+    if (!compute_sync(cbar, cphase, p.err)) return;
+
+    // 4 lanes per output: lane gl covers k = 8*gl .. 8*gl+7 of each k-tile.
+    // The stages of a chunk are held only for the shared loads and compares:
+    // the items' metadata is fetched before the chunk's wait, and the group
+    // reductions and global stores happen after the stages are released.
+    const int g = lane >> 2, gl = lane & 3;
+    const int group = warp * 8 + g;                  // 0 .. 8*CW-1
+    constexpr int NGROUPS = 8 * C::CW;
+    constexpr int R = 1;                             // rounds prepared per chunk
+    for (int c = nchunks - 1; c >= 0; --c) {
+      const int kt0 = c * C::KT_PER_CHUNK;
+      const int nkt = min(C::KT_PER_CHUNK, p.k_tiles - kt0);
+      const int kbase = kt0 * BK, kmax = (int)p.K;
+      const int lo = c > 0 ? offs[c - 1] : 0, hi = offs[c];
+      for (int base0 = lo; base0 < hi; base0 += R * NGROUPS) {   // warp-uniform
+        bool active[R];
+        int mr[R], nr[R];
+        float tv[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int item = base0 + r * NGROUPS + group;
+          active[r] = item < hi;
+          const int slot = active[r] ? cid[item] : 0;
+          const int o = slot / CT, tl = slot % CT;
+          mr[r] = tl / TX + TY * (o / TN);
+          nr[r] = tl % TX + TX * (o % TN);
+          tv[r] = lds32(snap_addr + ((uint32_t)((o >> 2) * CT + tl) * 4u + (o & 3)) * 4u);
+        }
+        const bool last_batch = base0 + R * NGROUPS >= hi;
+        if (base0 == lo) {
+          for (int u = 0; u < nkt; ++u) {
+            const uint32_t s = (it + u) % STAGES;
+            if (!tp_mbar_wait(&full[s], ((it + u) / STAGES) & 1u, p.err)) return;
+          }
+        }
+        int best[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          best[r] = 1 << 30;
+          const bool tnan = tv[r] != tv[r];
+#pragma unroll
+          for (int u = 0; u < C::KT_PER_CHUNK; ++u) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              if (u < nkt) {
+                const uint32_t xb = stage_addr + ((it + u) % STAGES) * STAGE_BYTES;
+                const uint32_t q = (uint32_t)(2 * gl + h);       // 16-byte chunk of the row
+                uint64_t xv0, xv1, wv0, wv1;
+                lds128(xb + (uint32_t)mr[r] * 128u + ((q ^ ((uint32_t)mr[r] & 7u)) << 4), xv0, xv1);
+                lds128(xb + TILE_BYTES + (uint32_t)nr[r] * 128u +
+                           ((q ^ ((uint32_t)nr[r] & 7u)) << 4),
+                       wv0, wv1);
+                const float sum[4] = {
+                    __uint_as_float((uint32_t)xv0) + __uint_as_float((uint32_t)wv0),
+                    __uint_as_float((uint32_t)(xv0 >> 32)) + __uint_as_float((uint32_t)(wv0 >> 32)),
+                    __uint_as_float((uint32_t)xv1) + __uint_as_float((uint32_t)wv1),
+                    __uint_as_float((uint32_t)(xv1 >> 32)) + __uint_as_float((uint32_t)(wv1 >> 32))};
+                const int kl = u * BK + 4 * (int)q;               // chunk-local k of sum[0]
+#pragma unroll
+                for (int e = 3; e >= 0; --e) {
+                  const bool hit = (kbase + kl + e < kmax) &&
+                                   (tnan ? (sum[e] != sum[e]) : (sum[e] == tv[r]));
+                  if (hit) best[r] = min(best[r], kl + e);
+                }
+              }
+            }
+          }
+        }
+        if (last_batch) {                             // release the chunk's stages
+          __syncwarp();
+          if (lane == 0)
+            for (int u = 0; u < nkt; ++u) tp_mbar_arrive(&empty[(it + u) % STAGES]);
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          int b = min(best[r], __shfl_xor_sync(0xffffffffu, best[r], 1));
+          b = min(b, __shfl_xor_sync(0xffffffffu, b, 2));
+          if (active[r] && gl == 0) {
+            const int64_t m = m0 + mr[r], n = n0 + nr[r];
+            p.am[m * p.lda + n] = b < (1 << 30) ? kbase + b : kbase;
+            float v = tv[r];
+            if (p.bias) v = v + p.bias[n];
+            if (p.scale != 1.0f) v = v * p.scale;
+            p.y[m * p.ldy + n] = v;
+          }
+        }
+      }
+      if (lo == hi) {                                 // an empty chunk still holds stages
+        for (int u = 0; u < nkt; ++u) {
+          const uint32_t s = (it + u) % STAGES;
+          if (!tp_mbar_wait(&full[s], ((it + u) / STAGES) & 1u, p.err)) return;
+        }
+        __syncwarp();
+        if (lane == 0)
+          for (int u = 0; u < nkt; ++u) tp_mbar_arrive(&empty[(it + u) % STAGES]);
+      }
+      it += nkt;
+    }
+    if (!compute_sync(cbar, cphase, p.err)) return;   // the list (in cid) is read until here
   }
 }
 
@@ -436,6 +534,7 @@ bool maxplus_tma_eligible(const StridedMaxPlus& p) {
   if (p.B1 * p.B2 != 1) return false;
   if (p.sx_k != 1 || p.sw_k != 1 || p.sy_n != 1) return false;
   if (p.am && p.sa_n != 1) return false;
+  if (p.am && ceil_div(p.K, DefaultCfg::CHUNK) > MAX_ARGMAX_CHUNKS) return false;
   if (p.M < BM || p.N < BN || p.K < 2 * BK || p.K > DefaultCfg::MAX_K) return false;
   if ((p.sx_m % 4) != 0 || (p.sw_n % 4) != 0) return false;
   if (!aligned16(p.x) || !aligned16(p.w)) return false;
@@ -453,10 +552,6 @@ int launch_maxplus_fwd_tma(const StridedMaxPlus& p, cudaStream_t stream) {
   tp_.M = p.M;
   tp_.N = p.N;
   tp_.K = p.K;
-  tp_.x = (const float*)p.x;
-  tp_.ldx = p.sx_m;
-  tp_.w = (const float*)p.w;
-  tp_.ldw = p.sw_n;
   tp_.bias = p.bias;
   tp_.y = p.y;
   tp_.ldy = p.sy_m;

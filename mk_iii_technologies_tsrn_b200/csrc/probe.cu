@@ -10,7 +10,9 @@
 // the loop measures the max instruction alone.
 //   form 0: add.rn.f32 + 2-input max.f32 per term (4 instructions / 2 terms)
 //   form 1: add.rn.f32x2 + 3-input max.f32 per two terms (2 instructions)
-//   form 2: add.rn.f32x2 + 3-input max.NaN.f32 (the GEMM kernel's form)
+//   form 2: add.rn.f32x2 + 3-input max.NaN.f32
+//   form 3: two add.rn.f32 + 3-input max.NaN.f32 per two terms (3 instructions)
+//   form 4: forms 2 and 3 alternating over the outputs
 #include "maxplus_internal.cuh"
 
 namespace tp {
@@ -34,11 +36,19 @@ __device__ __forceinline__ void term_pair(float& acc, uint64_t xa, uint64_t wb) 
         "max.f32 %0, %0, lo, hi;\n\t}"
         : "+f"(acc)
         : "l"(xa), "l"(wb));
-  } else {
+  } else if (FORM == 2) {
     asm volatile(
         "{\n\t.reg .b64 s;\n\t.reg .f32 lo, hi;\n\t"
         "add.rn.f32x2 s, %1, %2;\n\tmov.b64 {lo, hi}, s;\n\t"
         "max.NaN.f32 %0, %0, lo, hi;\n\t}"
+        : "+f"(acc)
+        : "l"(xa), "l"(wb));
+  } else {
+    asm volatile(
+        "{\n\t.reg .f32 x0, x1, w0, w1, s0, s1;\n\t"
+        "mov.b64 {x0, x1}, %1;\n\tmov.b64 {w0, w1}, %2;\n\t"
+        "add.rn.f32 s0, x0, w0;\n\tadd.rn.f32 s1, x1, w1;\n\t"
+        "max.NaN.f32 %0, %0, s0, s1;\n\t}"
         : "+f"(acc)
         : "l"(xa), "l"(wb));
   }
@@ -68,7 +78,14 @@ __global__ void __launch_bounds__(256) probe_kernel(int64_t iters, float* sink) 
 #pragma unroll
     for (int j = 0; j < 8; ++j)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) term_pair<FORM>(acc[i][j], xa[i], wb[j]);
+      for (int i = 0; i < 8; ++i) {
+        if (FORM == 4) {
+          if ((i + j) & 1) term_pair<2>(acc[i][j], xa[i], wb[j]);
+          else term_pair<3>(acc[i][j], xa[i], wb[j]);
+        } else {
+          term_pair<FORM>(acc[i][j], xa[i], wb[j]);
+        }
+      }
   }
   float r = 0.0f;
 #pragma unroll
@@ -87,8 +104,12 @@ int launch_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters
     probe_kernel<0><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
   else if (form == 1)
     probe_kernel<1><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
-  else
+  else if (form == 2)
     probe_kernel<2><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
+  else if (form == 3)
+    probe_kernel<3><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
+  else
+    probe_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
   return launch_status();
 }
 
