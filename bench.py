@@ -51,6 +51,8 @@ def parse_args():
     p.add_argument("--workload", choices=["gemm", "scan"], default="gemm")
     p.add_argument("--size", type=int, default=8192, help="M = N = K of the GEMM workload")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                   help="N>1 GEMM: fused peer-store epilogue (p2p) or NCCL all-gather")
     return p.parse_args()
 
 
@@ -231,9 +233,10 @@ def gemm_workload(args, world, rank):
     del W_full_rows
     y = torch.empty(M, Nr, device=dev)
     am = torch.empty(M, Nr, device=dev, dtype=torch.int32)
+    sharded = None
     if world > 1:
-        y_all = torch.empty(world, M, Nr, device=dev)
-        am_all = torch.empty(world, M, Nr, device=dev, dtype=torch.int32)
+        from mk_iii_technologies_tsrn_b200.dist import ShardedMaxPlus
+        sharded = ShardedMaxPlus(M, N, K, mode=args.exchange, device=dev)
 
     kernel_ms = []
 
@@ -242,13 +245,13 @@ def gemm_workload(args, world, rank):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-        ops.maxplus_strided(x, W, out=y, out_argmax=am)
+        if sharded is None:
+            ops.maxplus_strided(x, W, out=y, out_argmax=am)
+        else:
+            sharded(x, W)          # shard GEMM + exchange (fused or NCCL)
         if record:
             e1.record()
             kernel_ms.append((e0, e1))
-        if world > 1:
-            torch.distributed.all_gather_into_tensor(y_all, y)
-            torch.distributed.all_gather_into_tensor(am_all, am)
 
     for _ in range(args.warmup):
         step()
@@ -256,11 +259,19 @@ def gemm_workload(args, world, rank):
     # quick self-check on a few rows (oracle on CPU is too slow for the full size)
     if rank == 0:
         import oracle
+        import numpy as np
         rows = slice(0, 2)
         ry, ri = oracle.maxplus_fwd(x[rows].cpu().numpy(), W[:256].cpu().numpy())
-        import numpy as np
-        assert np.array_equal(y[rows, :256].cpu().numpy(), ry)
-        assert np.array_equal(am[rows, :256].cpu().numpy(), ri)
+        if sharded is None:
+            yc, ac = y[rows, :256], am[rows, :256]
+        else:
+            yo, ao = sharded(x, W)
+            torch.cuda.synchronize()
+            yc, ac = yo[rows, :256], ao[rows, :256]
+        assert np.array_equal(yc.cpu().numpy(), ry)
+        assert np.array_equal(ac.cpu().numpy(), ri)
+    elif sharded is not None:
+        sharded(x, W)              # every rank takes the same collective steps
 
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
@@ -284,12 +295,13 @@ def gemm_workload(args, world, rank):
     def e2e_step():
         dx.copy_(hx, non_blocking=True)
         dW.copy_(hW, non_blocking=True)
-        ops.maxplus_strided(dx, dW, out=y, out_argmax=am)
-        if world > 1:
-            torch.distributed.all_gather_into_tensor(y_all, y)
-            torch.distributed.all_gather_into_tensor(am_all, am)
-        hy.copy_(y, non_blocking=True)
-        ham.copy_(am, non_blocking=True)
+        if sharded is None:
+            ys, ams = ops.maxplus_strided(dx, dW, out=y, out_argmax=am)
+        else:
+            yf, af = sharded(dx, dW)
+            ys, ams = yf[:, rank * Nr:(rank + 1) * Nr], af[:, rank * Nr:(rank + 1) * Nr]
+        hy.copy_(ys, non_blocking=True)   # this rank's columns of the result
+        ham.copy_(ams, non_blocking=True)
 
     for _ in range(2):
         e2e_step()
@@ -340,12 +352,14 @@ def gemm_workload(args, world, rank):
         "data": "synthetic: x, W ~ N(0,1) (seeded), 5% of W = -inf",
         "config": {"workload": f"maxplus_gemm M=N=K={S} fp32 + int32 argmax",
                    "M": M, "N": N, "K": K,
-                   "parallelism": f"column-shard x{world} + NCCL all-gather of y/argmax"
-                   if world > 1 else "single GPU",
+                   "parallelism": (f"column-shard x{world}, " + (
+                       "all-gather fused into the GEMM epilogue (peer stores into "
+                       "symmetric memory over NVLink)" if args.exchange == "p2p" else
+                       "NCCL all-gather of y/argmax")) if world > 1 else "single GPU",
                    "l2": "inputs (2 x 256 MiB) larger than L2"},
         "e2e": {"value": e2e_value, "unit": "Gop/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps,   # one max-plus kernel per step (plus 2 barrier kernels at N>1)
         "roofline": roofline,
         "clocks": clk,
     }

@@ -109,6 +109,27 @@ TP_API int tp_maxplus_fwd_strided(int dtype,
                            int32_t* argmax, int64_t sa_b1, int64_t sa_b2, int64_t sa_m, int64_t sa_n,
                            float scale, void* stream);
 
+/* Column-sharded max-plus GEMM with the all-gather fused into the epilogue.
+ * This rank computes the columns [col0, col0 + N_shard) of y = max_k(x + w):
+ * x [M,K] (row stride ldx), w_shard [N_shard,K] (row stride ldw), optional
+ * bias_shard [N_shard].  Every output (and its int32 argmax, when argmax_dst is
+ * not NULL) is stored into each of the n_dst (1..8) full-size row-major
+ * buffers y_dst[d] [M, ldy] (argmax_dst[d] [M, ldy]) at column col0 + n.
+ * y_dst[0] / argmax_dst[0] must be this device's memory; the others may be
+ * peer buffers of the other ranks of one NVLink domain (P2P-mapped), so one
+ * launch per rank fills every rank's full output -- no separate all-gather.
+ * Synchronising the ranks around the launch is the caller's job.  Same
+ * numerics as tp_maxplus_fwd (bit-exact values and argmax).  Needs the TMA
+ * path's layout (fp32, 16-byte aligned, ldx/ldw multiples of 4, M and N_shard
+ * >= 128); otherwise returns TP_ERR_UNSUPPORTED.  Replaces the reference's
+ * single-device forward (tropformer.py:127-145) for the multi-GPU sweep. */
+TP_API int tp_maxplus_fwd_sharded(int64_t M, int64_t N_shard, int64_t K,
+                                  const float* x, int64_t ldx,
+                                  const float* w_shard, int64_t ldw,
+                                  const float* bias_shard,
+                                  float* const* y_dst, int32_t* const* argmax_dst, int n_dst,
+                                  int64_t ldy, int64_t col0, void* stream);
+
 /* Smooth (Maslov) forward: y[m,n] = (tau*log(sum_k exp(s[m,n,k]/tau)) [+bias[n]]) * scale.
  * tau = 1 is the TSRN tropical attention score LSE_c(Q+K)
  * (research/tsrn_dml.py:438-460, tsrn_dml.py:348-368); general tau is

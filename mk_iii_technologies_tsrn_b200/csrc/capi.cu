@@ -149,6 +149,35 @@ int tp_maxplus_fwd(int dtype, int64_t M, int64_t N, int64_t K, const void* x, in
                                 0, ldy, 1, argmax, 0, 0, ld_argmax, 1, 1.0f, stream);
 }
 
+int tp_maxplus_fwd_sharded(int64_t M, int64_t N_shard, int64_t K, const float* x, int64_t ldx,
+                           const float* w_shard, int64_t ldw, const float* bias_shard,
+                           float* const* y_dst, int32_t* const* argmax_dst, int n_dst,
+                           int64_t ldy, int64_t col0, void* stream) {
+  TP_RETURN_IF(M < 0 || N_shard < 0 || K < 0 || col0 < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(n_dst < 1 || n_dst > 8, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(y_dst == nullptr, TP_ERR_NULL_POINTER);
+  TP_RETURN_IF(M > 0 && (ldy < col0 + N_shard || ldx < K || ldw < K), TP_ERR_INVALID_ARG);
+  if (M * N_shard == 0) return TP_OK;
+  for (int d = 0; d < n_dst; ++d) {
+    TP_RETURN_IF(y_dst[d] == nullptr, TP_ERR_NULL_POINTER);
+    TP_RETURN_IF(argmax_dst != nullptr && argmax_dst[d] == nullptr, TP_ERR_NULL_POINTER);
+  }
+  TP_CHECK_PTR(x);
+  TP_CHECK_PTR(w_shard);
+  TP_CHECK_OPT_PTR(bias_shard);
+  // destination 0 is this device's own output; the others may be peer memory
+  // (mapped through CUDA IPC / symmetric memory), which the pointer check
+  // below accepts as device memory of another device.
+  TP_CHECK_PTR(y_dst[0]);
+  if (argmax_dst) TP_CHECK_PTR(argmax_dst[0]);
+  StridedMaxPlus p{TP_DTYPE_F32, 1, 1, M, N_shard, K, x, 0, 0, ldx, 1, w_shard, 0, 0, ldw, 1,
+                   bias_shard, y_dst[0] + col0, 0, 0, ldy, 1,
+                   argmax_dst ? argmax_dst[0] + col0 : nullptr, 0, 0, ldy, 1, 1.0f, 1.0f};
+  if (!maxplus_tma_eligible(p)) return TP_ERR_UNSUPPORTED;
+  return launch_maxplus_fwd_tma_dests(p, y_dst + 1, argmax_dst ? argmax_dst + 1 : nullptr,
+                                      n_dst - 1, col0, as_stream(stream));
+}
+
 int tp_maxplus_lse_fwd_strided(int dtype, float tau, int64_t B1, int64_t B2, int64_t M, int64_t N,
                                int64_t K, const void* x, int64_t sx_b1, int64_t sx_b2,
                                int64_t sx_m, int64_t sx_k, const void* w, int64_t sw_b1,

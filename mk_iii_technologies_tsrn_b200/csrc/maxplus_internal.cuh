@@ -67,6 +67,11 @@ int launch_column_sum(const float* g, int64_t B1, int64_t B2, int64_t M, int64_t
 // when the problem does not meet its layout rules (caller falls back).
 bool maxplus_tma_eligible(const StridedMaxPlus& p);
 int launch_maxplus_fwd_tma(const StridedMaxPlus& p, cudaStream_t stream);
+// Same, additionally storing every output into ndst (<= 8) further buffers
+// at column offset col0 (same row strides as y / argmax).
+int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
+                                 int32_t* const* adst, int ndst, int64_t col0,
+                                 cudaStream_t stream);
 
 // scan.cu
 struct ScanArgs {

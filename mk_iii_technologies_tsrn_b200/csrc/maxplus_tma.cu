@@ -84,6 +84,8 @@ struct Cfg {
 
 using DefaultCfg = Cfg<TP_TMA_TM, TP_TMA_TN, TP_TMA_CHUNK>;
 
+constexpr int MAX_DESTS = 8;   // output copies (the ranks of one NVLink domain)
+
 struct TmaParams {
   int64_t M, N, K;
   const float* bias;
@@ -92,6 +94,14 @@ struct TmaParams {
   int32_t* am;
   int64_t lda;
   float scale;
+  // Extra output copies: every (m, n) is also stored at ydst[d][m*ldy + col0 + n]
+  // (and adst[d][m*lda + col0 + n]) for d < ndst.  Used by the column-sharded
+  // multi-GPU GEMM to write each rank's shard straight into every rank's full
+  // output over NVLink (peer pointers), fusing the all-gather into the epilogue.
+  float* ydst[MAX_DESTS];
+  int32_t* adst[MAX_DESTS];
+  int ndst;
+  int64_t col0;
   int m_tiles, n_tiles, k_tiles, num_tiles;
   int* err;
 };
@@ -335,6 +345,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
           if (p.bias) v = v + p.bias[n];
           if (p.scale != 1.0f) v = v * p.scale;
           p.y[m * p.ldy + n] = v;
+          for (int d = 0; d < p.ndst; ++d) p.ydst[d][m * p.ldy + p.col0 + n] = v;
         }
       }
       continue;
@@ -479,11 +490,16 @@ __global__ void __launch_bounds__(C::THREADS, 1)
           b = min(b, __shfl_xor_sync(0xffffffffu, b, 2));
           if (active[r] && gl == 0) {
             const int64_t m = m0 + mr[r], n = n0 + nr[r];
-            p.am[m * p.lda + n] = b < (1 << 30) ? kbase + b : kbase;
+            const int32_t k = b < (1 << 30) ? kbase + b : kbase;
+            p.am[m * p.lda + n] = k;
             float v = tv[r];
             if (p.bias) v = v + p.bias[n];
             if (p.scale != 1.0f) v = v * p.scale;
             p.y[m * p.ldy + n] = v;
+            for (int d = 0; d < p.ndst; ++d) {
+              p.ydst[d][m * p.ldy + p.col0 + n] = v;
+              p.adst[d][m * p.lda + p.col0 + n] = k;
+            }
           }
         }
       }
@@ -544,7 +560,14 @@ bool maxplus_tma_eligible(const StridedMaxPlus& p) {
 }
 
 int launch_maxplus_fwd_tma(const StridedMaxPlus& p, cudaStream_t stream) {
+  return launch_maxplus_fwd_tma_dests(p, nullptr, nullptr, 0, 0, stream);
+}
+
+int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
+                                 int32_t* const* adst, int ndst, int64_t col0,
+                                 cudaStream_t stream) {
   if (!maxplus_tma_eligible(p)) return TP_ERR_UNSUPPORTED;
+  if (ndst < 0 || ndst > MAX_DESTS) return TP_ERR_TOO_LARGE;
   CUtensorMap xmap, wmap;
   if (!make_map(&xmap, (const float*)p.x, p.M, p.K, p.sx_m)) return TP_ERR_UNSUPPORTED;
   if (!make_map(&wmap, (const float*)p.w, p.N, p.K, p.sw_n)) return TP_ERR_UNSUPPORTED;
@@ -563,6 +586,12 @@ int launch_maxplus_fwd_tma(const StridedMaxPlus& p, cudaStream_t stream) {
   tp_.k_tiles = (int)ceil_div(p.K, BK);
   tp_.num_tiles = tp_.m_tiles * tp_.n_tiles;
   tp_.err = device_error_ptr();
+  tp_.ndst = ndst;
+  tp_.col0 = col0;
+  for (int d = 0; d < MAX_DESTS; ++d) {
+    tp_.ydst[d] = d < ndst ? ydst[d] : nullptr;
+    tp_.adst[d] = (d < ndst && adst) ? adst[d] : nullptr;
+  }
   if (p.am) return launch_cfg<DefaultCfg, true>(xmap, wmap, tp_, stream);
   return launch_cfg<DefaultCfg, false>(xmap, wmap, tp_, stream);
 }
