@@ -119,10 +119,10 @@ TP_API int tp_maxplus_fwd_strided(int dtype,
  * peer buffers of the other ranks of one NVLink domain (P2P-mapped), so one
  * launch per rank fills every rank's full output -- no separate all-gather.
  * Synchronising the ranks around the launch is the caller's job.  Same
- * numerics as tp_maxplus_fwd (bit-exact values and argmax).  Needs the TMA
- * path's layout (fp32, 16-byte aligned, ldx/ldw multiples of 4, M and N_shard
- * >= 128); otherwise returns TP_ERR_UNSUPPORTED.  Replaces the reference's
- * single-device forward (tropformer.py:127-145) for the multi-GPU sweep. */
+ * numerics as tp_maxplus_fwd (bit-exact values and argmax).  Shards that the
+ * TMA kernel does not take (small or unaligned) are computed locally and then
+ * copied into the other destinations.  Replaces the reference's single-device
+ * forward (tropformer.py:127-145) for the multi-GPU sweep. */
 TP_API int tp_maxplus_fwd_sharded(int64_t M, int64_t N_shard, int64_t K,
                                   const float* x, int64_t ldx,
                                   const float* w_shard, int64_t ldw,

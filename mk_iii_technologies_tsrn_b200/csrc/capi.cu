@@ -173,9 +173,22 @@ int tp_maxplus_fwd_sharded(int64_t M, int64_t N_shard, int64_t K, const float* x
   StridedMaxPlus p{TP_DTYPE_F32, 1, 1, M, N_shard, K, x, 0, 0, ldx, 1, w_shard, 0, 0, ldw, 1,
                    bias_shard, y_dst[0] + col0, 0, 0, ldy, 1,
                    argmax_dst ? argmax_dst[0] + col0 : nullptr, 0, 0, ldy, 1, 1.0f, 1.0f};
-  if (!maxplus_tma_eligible(p)) return TP_ERR_UNSUPPORTED;
-  return launch_maxplus_fwd_tma_dests(p, y_dst + 1, argmax_dst ? argmax_dst + 1 : nullptr,
-                                      n_dst - 1, col0, as_stream(stream));
+  if (maxplus_tma_eligible(p))
+    return launch_maxplus_fwd_tma_dests(p, y_dst + 1, argmax_dst ? argmax_dst + 1 : nullptr,
+                                        n_dst - 1, col0, as_stream(stream));
+  // small or unaligned shards: compute into the local copy, then copy the
+  // block into the other destinations (peer copies through unified addressing)
+  int s = launch_maxplus_fwd_generic(p, as_stream(stream));
+  if (s != TP_OK) return s;
+  for (int d = 1; d < n_dst; ++d) {
+    cudaError_t e = cudaMemcpy2DAsync(y_dst[d] + col0, ldy * 4, y_dst[0] + col0, ldy * 4,
+                                      N_shard * 4, M, cudaMemcpyDeviceToDevice, as_stream(stream));
+    if (e == cudaSuccess && argmax_dst)
+      e = cudaMemcpy2DAsync(argmax_dst[d] + col0, ldy * 4, argmax_dst[0] + col0, ldy * 4,
+                            N_shard * 4, M, cudaMemcpyDeviceToDevice, as_stream(stream));
+    if (e != cudaSuccess) return (int)e;
+  }
+  return TP_OK;
 }
 
 int tp_maxplus_lse_fwd_strided(int dtype, float tau, int64_t B1, int64_t B2, int64_t M, int64_t N,

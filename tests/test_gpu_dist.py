@@ -17,11 +17,11 @@ import oracle
 pytestmark = pytest.mark.gpu
 
 
-def test_sharded_entry_two_local_destinations(cuda):
+@pytest.mark.parametrize("M,N,K,Ns,col0", [(512, 1024, 192, 512, 256),   # fused TMA epilogue
+                                           (96, 300, 50, 100, 150)])     # generic + copies
+def test_sharded_entry_two_local_destinations(cuda, M, N, K, Ns, col0):
     from mk_iii_technologies_tsrn_b200 import _lib
     lib = _lib.load()
-    M, N, K = 256, 512, 192
-    Ns, col0 = 256, 128
     g = torch.Generator(device=cuda).manual_seed(0)
     x = torch.randn(M, K, device=cuda, generator=g)
     w = torch.randn(Ns, K, device=cuda, generator=g)
