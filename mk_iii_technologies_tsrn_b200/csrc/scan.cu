@@ -81,31 +81,14 @@ __global__ void __launch_bounds__(32)
     if (!tp_mbar_wait(&full[s], (uint32_t)((ch / STAGES) & 1), p.err)) return;
     const int64_t t0 = (int64_t)ch * TS;
     const int rows = (int)((p.T - t0) < TS ? (p.T - t0) : TS);
-    uint32_t bits = 0;
-    float* hout = p.h + (row0 + t0) * p.C + c;
-    if (rows == TS) {
-#pragma unroll 8
-      for (int r = 0; r < TS; ++r) {
-        float u = buf[s][0][r][lane];
-        if (kHasX) u = u + buf[s][NBOX - 1][r][lane];
-        const float d = a + h;
-        const bool win = u >= d;
-        h = win ? u : d;
-        bits |= (uint32_t)win << r;
-        if (cv) hout[(int64_t)r * p.C] = h;
-      }
-    } else {
-      for (int r = 0; r < rows; ++r) {
-        float u = buf[s][0][r][lane];
-        if (kHasX) u = u + buf[s][NBOX - 1][r][lane];
-        const float d = a + h;
-        const bool win = u >= d;
-        h = win ? u : d;
-        bits |= (uint32_t)win << r;
-        if (cv) hout[(int64_t)r * p.C] = h;
-      }
+    // 1) the chunk's inputs into registers (independent loads), 2) hand the
+    // stage back to the TMA right away, 3) run the recurrence on registers
+    float u[TS];
+#pragma unroll
+    for (int r = 0; r < TS; ++r) {
+      u[r] = buf[s][0][r][lane];
+      if (kHasX) u[r] = u[r] + buf[s][NBOX - 1][r][lane];
     }
-    if (kMask && cv) p.win[(b * nchunks + ch) * p.C + c] = bits;
     __syncwarp();
     if (lane == 0 && ch + STAGES < nchunks) {
       const int64_t nr = row0 + (int64_t)(ch + STAGES) * TS;
@@ -113,6 +96,30 @@ __global__ void __launch_bounds__(32)
       tp_tma_load_2d(&buf[s][0][0][0], &bmap, (int32_t)c0, (int32_t)nr, &full[s]);
       if (kHasX) tp_tma_load_2d(&buf[s][NBOX - 1][0][0], &xmap, (int32_t)c0, (int32_t)nr, &full[s]);
     }
+    uint32_t bits = 0;
+    float* hout = p.h + (row0 + t0) * p.C + c;
+    if (rows == TS && cv) {
+#pragma unroll
+      for (int r = 0; r < TS; ++r) {
+        const float d = a + h;
+        const bool win = u[r] >= d;
+        h = win ? u[r] : d;
+        bits |= (uint32_t)win << r;
+        hout[(int64_t)r * p.C] = h;
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < TS; ++r) {
+        if (r < rows) {
+          const float d = a + h;
+          const bool win = u[r] >= d;
+          h = win ? u[r] : d;
+          bits |= (uint32_t)win << r;
+          if (cv) hout[(int64_t)r * p.C] = h;
+        }
+      }
+    }
+    if (kMask && cv) p.win[(b * nchunks + ch) * p.C + c] = bits;
   }
 }
 
