@@ -146,6 +146,19 @@ def measured_peaks():
     return {}
 
 
+def profiled_traffic(key):
+    """DRAM bytes per launch of a kernel from a committed ncu capture (profiles/traffic.txt)."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == key:
+                return int(parts[1])
+    return None
+
+
 def time_steps(step, steps, world):
     """Device time of `steps` calls of step() between barrier+sync fences (max over ranks)."""
     stream = torch.cuda.current_stream()
@@ -329,7 +342,8 @@ def gemm_workload(args, world, rank):
     per_gpu_ops = 2.0 * M * Nr * K
     achieved = per_gpu_ops / (kms / 1e3) / 1e12
     roofline = {"bound": "cuda-core", "achieved": achieved, "peak": peak, "unit": "Top/s",
-                "frac": achieved / peak, "traffic": None,
+                "frac": achieved / peak,
+                "traffic": profiled_traffic(f"maxplus_tma_gemm{S}") if world == 1 else None,
                 "peak_source": "in-repo register-only add+max probe (tp_probe_addmax), best of "
                                "5 instruction forms, measured in this run; of measured",
                 "probe_top_s": {"fadd_fmnmx": probe[0], "fadd2_fmnmx3": probe[1],
@@ -439,7 +453,8 @@ def scan_workload(args, world, rank):
                 "h2d_bytes_per_step": 3 * elems * 4, "d2h_bytes_per_step": 2 * elems * 4},
         "gpu_launches": 3 * args.steps,
         "roofline": {"bound": "hbm", "achieved": ach_b, "peak": peak, "unit": "GB/s",
-                     "frac": ach_b / peak, "traffic": None,
+                     "frac": ach_b / peak, "traffic": profiled_traffic("scan_bwd_tma_config3"),
+                     "algorithmic_bytes": 20 * elems,
                      "kernel": "scan_bwd_tma (recompute path)",
                      "fwd": {"achieved": ach_f, "frac": ach_f / peak, "ms": f_ms},
                      "bwd_ms": b_ms,
