@@ -14,6 +14,13 @@ weak scaling): forward (read b, x; write h: 12 B/elem) plus argmax-path
 backward recomputing the winners (read g, h, b, x; write gu: 20 B/elem);
 metric GB/s of those algorithmic bytes.
 
+``--workload dtn``: config 2, the drop-in DTNAttention(256, 8) block
+(tropical Q/K projections with the STE backward, tropical score, Maslov
+softmax) forward + backward at B=128, L=64 per rank; metric tokens/s.
+
+``--dtype bf16`` stores the GEMM operands in bf16 (widened exactly on the GPU;
+the arithmetic stays fp32).
+
 ``--impl reference`` times the reference's own CPU implementation (its PyTorch
 expression, restated in ``oracle/torch_ref.py``) on the host cores for the same
 metric, on a bounded sample of the workload; only rank 0 runs it.
@@ -48,8 +55,10 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["gemm", "scan"], default="gemm")
+    p.add_argument("--workload", choices=["gemm", "scan", "dtn"], default="gemm")
     p.add_argument("--size", type=int, default=8192, help="M = N = K of the GEMM workload")
+    p.add_argument("--dtype", choices=["f32", "bf16"], default="f32",
+                   help="GEMM operand storage (bf16 is widened exactly; arithmetic is fp32)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                    help="N>1 GEMM: fused peer-store epilogue (p2p) or NCCL all-gather")
@@ -244,6 +253,8 @@ def gemm_workload(args, world, rank):
     W_full_rows[torch.rand(N, K, device=dev, generator=gm) < 0.05] = float("-inf")
     W = W_full_rows[rank * Nr:(rank + 1) * Nr].contiguous()
     del W_full_rows
+    if args.dtype == "bf16":
+        x, W = x.to(torch.bfloat16), W.to(torch.bfloat16)
     y = torch.empty(M, Nr, device=dev)
     am = torch.empty(M, Nr, device=dev, dtype=torch.int32)
     sharded = None
@@ -260,6 +271,8 @@ def gemm_workload(args, world, rank):
             e0.record()
         if sharded is None:
             ops.maxplus_strided(x, W, out=y, out_argmax=am)
+        elif args.dtype == "bf16":
+            sharded(ops.widen_bf16(x), ops.widen_bf16(W))
         else:
             sharded(x, W)          # shard GEMM + exchange (fused or NCCL)
         if record:
@@ -274,17 +287,17 @@ def gemm_workload(args, world, rank):
         import oracle
         import numpy as np
         rows = slice(0, 2)
-        ry, ri = oracle.maxplus_fwd(x[rows].cpu().numpy(), W[:256].cpu().numpy())
+        ry, ri = oracle.maxplus_fwd(x[rows].float().cpu().numpy(), W[:256].float().cpu().numpy())
         if sharded is None:
             yc, ac = y[rows, :256], am[rows, :256]
         else:
-            yo, ao = sharded(x, W)
+            yo, ao = sharded(x.float(), W.float())
             torch.cuda.synchronize()
             yc, ac = yo[rows, :256], ao[rows, :256]
         assert np.array_equal(yc.cpu().numpy(), ry)
         assert np.array_equal(ac.cpu().numpy(), ri)
     elif sharded is not None:
-        sharded(x, W)              # every rank takes the same collective steps
+        sharded(x.float(), W.float())   # every rank takes the same collective steps
 
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
@@ -311,7 +324,10 @@ def gemm_workload(args, world, rank):
         if sharded is None:
             ys, ams = ops.maxplus_strided(dx, dW, out=y, out_argmax=am)
         else:
-            yf, af = sharded(dx, dW)
+            if args.dtype == "bf16":
+                yf, af = sharded(ops.widen_bf16(dx), ops.widen_bf16(dW))
+            else:
+                yf, af = sharded(dx, dW)
             ys, ams = yf[:, rank * Nr:(rank + 1) * Nr], af[:, rank * Nr:(rank + 1) * Nr]
         hy.copy_(ys, non_blocking=True)   # this rank's columns of the result
         ham.copy_(ams, non_blocking=True)
@@ -321,7 +337,7 @@ def gemm_workload(args, world, rank):
     e2e_steps = max(3, min(args.steps, 5))
     e2e_ms = time_steps(e2e_step, e2e_steps, world)
     e2e_value = ops_per_step / (e2e_ms / e2e_steps / 1e3) / 1e9
-    h2d = (hx.numel() + hW.numel()) * 4
+    h2d = hx.numel() * hx.element_size() + hW.numel() * hW.element_size()
     d2h = (hy.numel() + ham.numel()) * 4
 
     # ---- roofline.  Max-plus is CUDA-core work (one add and one max per term;
@@ -352,7 +368,8 @@ def gemm_workload(args, world, rank):
                 "nominal_issue_limit_top_s": issue_limit,
                 "kernel_ms": kms}
     res = {
-        "metric": "max-plus GEMM Gop/s (fp32, with int32 argmax)",
+        "metric": "max-plus GEMM Gop/s (fp32, with int32 argmax)" if args.dtype == "f32" else
+                  "max-plus GEMM Gop/s (bf16 operands, fp32 arithmetic, with int32 argmax)",
         "value": value,
         "unit": "Gop/s",
         "n_gpus": world,
@@ -364,7 +381,8 @@ def gemm_workload(args, world, rank):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic: x, W ~ N(0,1) (seeded), 5% of W = -inf",
-        "config": {"workload": f"maxplus_gemm M=N=K={S} fp32 + int32 argmax",
+        "config": {"workload": f"maxplus_gemm M=N=K={S} {args.dtype} operands + int32 argmax",
+                   "operand_storage": args.dtype,
                    "M": M, "N": N, "K": K,
                    "parallelism": (f"column-shard x{world}, " + (
                        "all-gather fused into the GEMM epilogue (peer stores into "
@@ -463,10 +481,143 @@ def scan_workload(args, world, rank):
     }
 
 
+def count_library_kernels(fn) -> int:
+    """Number of this library's kernels (namespace tp::) one call of fn launches."""
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return sum(1 for e in prof.events()
+               if e.device_type == torch.autograd.DeviceType.CUDA and "tp::" in e.name)
+
+
+def dtn_workload(args, world, rank):
+    """Config 2: DTNAttention(256, 8) forward + backward at B=128 (per rank), L=64."""
+    from mk_iii_technologies_tsrn_b200 import ops, _lib
+    from mk_iii_technologies_tsrn_b200.dtn import DTNAttention
+
+    _lib.load().tp_set_pointer_checks(0)
+    B, L, D, H = 128, 64, 256, 8
+    dev = torch.device("cuda")
+    torch.manual_seed(1 + rank)
+    attn = DTNAttention(D, H, dropout=0.0).to(dev)
+    with torch.no_grad():
+        attn.q_proj.weight.normal_(0.0, 0.02)
+        attn.k_proj.weight.normal_(0.0, 0.02)
+        attn.maslov.log_temps.copy_(torch.log(torch.rand(H, device=dev) * 0.9 + 0.1))
+    attn.train()
+    gen = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(B, L, D, device=dev, generator=gen, requires_grad=True)
+    g = torch.randn(B, L, D, device=dev, generator=gen)
+
+    def step():
+        out, _ = attn(x)
+        out.backward(g)
+
+    for _ in range(args.warmup):
+        step()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    ms = time_steps(step, args.steps, world)
+    clk = clocks.stop()
+    tokens = B * L * world
+    value = tokens / (ms / args.steps / 1e3)
+    # dominant tropical kernel: the Q-projection max-plus forward (M=8192, N=K=256)
+    xf = x.detach().reshape(-1, D)
+    wq = attn.q_proj.weight.detach()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ops.maxplus(xf, wq, argmax=False)
+    s0.record()
+    for _ in range(20):
+        ops.maxplus(xf, wq, argmax=False)
+    s1.record()
+    torch.cuda.synchronize()
+    kms = s0.elapsed_time(s1) / 20
+    achieved = 2.0 * xf.shape[0] * D * D / (kms / 1e3) / 1e12
+    probe = []
+    for form in range(5):
+        ops.probe_addmax(form, 148 * 8, 50)
+        pms, terms = ops.probe_addmax(form, 148 * 8, 400)
+        probe.append(2.0 * terms / (pms / 1e3) / 1e12)
+    peak = max(probe)
+    # end to end: activations from pinned host, input gradient back
+    hx = x.detach().cpu().pin_memory()
+    hgx = torch.empty_like(hx).pin_memory()
+    dx = torch.empty_like(x.detach())
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        xi = dx.requires_grad_(True)
+        out, _ = attn(xi)
+        out.backward(g)
+        hgx.copy_(xi.grad, non_blocking=True)
+        xi.grad = None
+        dx.requires_grad_(False)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_ms = time_steps(e2e_step, 3, world)
+    try:
+        per_step = count_library_kernels(step)
+    except Exception:   # profiler unavailable: leave the count out rather than guess
+        per_step = None
+    return {
+        "metric": "DTN tropical attention block tokens/s (fwd+bwd, train mode)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: x ~ N(0,1), upstream grad ~ N(0,1), Q/K weights N(0,0.02), "
+                "tau_h ~ U(0.1,1) (seeded)",
+        "config": {"workload": "DTNAttention d_model=256 heads=8 B=128 L=64 fwd+bwd (STE)",
+                   "parallelism": f"batch-replicated x{world} (weak)" if world > 1 else "single GPU",
+                   "l2": "activations 8 MiB (fit L2); the tropical kernels are compute-bound"},
+        "e2e": {"value": tokens / (e2e_ms / 3 / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hgx.numel() * 4},
+        "gpu_launches": per_step * args.steps if per_step is not None else None,
+        "roofline": {"bound": "cuda-core", "achieved": achieved, "peak": peak, "unit": "Top/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "kernel": "max-plus forward (value only, train mode) of the Q projection "
+                               "(M=8192, N=K=256)",
+                     "kernel_ms": kms,
+                     "peak_source": "in-repo add+max probe, best form, this run; of measured"},
+        "clocks": clk,
+    }
+
+
+def cpu_dtn_rate(target_s: float = 10.0):
+    from oracle.torch_ref import DTNAttentionRef
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    torch.manual_seed(1)
+    ref = DTNAttentionRef(256, 8)
+    B = 2
+    x = torch.randn(B, 64, 256, requires_grad=True)
+    t0 = time.perf_counter()
+    out, _ = ref(x)
+    out.sum().backward()
+    dt = time.perf_counter() - t0
+    reps = int(max(1, min(20, target_s / max(dt, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        out, _ = ref(x)
+        out.sum().backward()
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": B * 64 / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"reference DTNAttention expressions (oracle/torch_ref.py) fwd+bwd at "
+                      f"B={B} of 128, L=64, d=256, H=8; {reps} reps"}
+
+
 def reference_arm(args, world, rank):
     if rank != 0:
         return None
-    if args.workload == "gemm":
+    if args.workload == "dtn":
+        cb = cpu_dtn_rate(target_s=max(3.0, 2.0 * args.steps))
+        metric = "DTN tropical attention block tokens/s (fwd+bwd, train mode)"
+        cfg = {"workload": "DTNAttention d_model=256 heads=8 L=64 fwd+bwd (torch CPU)"}
+    elif args.workload == "gemm":
         cb = cpu_gemm_rate(args.size, target_s=max(3.0, 2.0 * args.steps))
         metric = "max-plus GEMM Gop/s (fp32, with int32 argmax)"
         cfg = {"workload": f"maxplus_gemm M=N=K={args.size} fp32 + int64 argmax (torch CPU)",
@@ -492,12 +643,16 @@ def main():
             res = reference_arm(args, world, rank)
         elif args.workload == "gemm":
             res = gemm_workload(args, world, rank)
+        elif args.workload == "dtn":
+            res = dtn_workload(args, world, rank)
         else:
             res = scan_workload(args, world, rank)
         if res is not None and args.impl == "ours" and rank == 0 and world == 1 \
                 and not args.no_cpu_baseline:
             if args.workload == "gemm":
                 res["cpu_baseline"] = cpu_gemm_rate(args.size)
+            elif args.workload == "dtn":
+                res["cpu_baseline"] = cpu_dtn_rate()
             else:
                 res["cpu_baseline"] = cpu_scan_rate(16, 4096, 1024)
         if rank == 0 and res is not None:

@@ -246,6 +246,13 @@ TP_API int tp_scan_bwd_noalloc(int64_t B, int64_t T, int64_t C,
                                const uint32_t* win_mask,
                                float* gu, float* ga, float* gh0, void* stream);
 
+/* Exact bf16 -> fp32 widening of n contiguous elements (dst may not overlap
+ * src).  Lets bf16-stored GEMM operands (the bf16 half of the M=N=K sweep)
+ * run on the fp32 TMA kernel: the results equal fp32 max-plus on the upcast
+ * inputs bit for bit.  No reference counterpart (the reference's fp16 kernel
+ * template, cuda/maxplus_gemm.cu:18, was never instantiated). */
+TP_API int tp_convert_bf16_to_f32(int64_t n, const void* src, float* dst, void* stream);
+
 /* ======================================================================== *
  *  Roofline probe: register-only add+max loop measuring the CUDA-core
  *  max-plus term rate.  form 0: FADD + 2-input FMNMX per term;

@@ -315,6 +315,14 @@ int tp_scan_bwd(int64_t B, int64_t T, int64_t C, const float* gh, const float* b
   return launch_scan_bwd(p, as_stream(stream));
 }
 
+int tp_convert_bf16_to_f32(int64_t n, const void* src, float* dst, void* stream) {
+  TP_RETURN_IF(n < 0, TP_ERR_INVALID_ARG);
+  if (n == 0) return TP_OK;
+  TP_CHECK_PTR(src);
+  TP_CHECK_PTR(dst);
+  return launch_bf16_to_f32(src, dst, n, as_stream(stream));
+}
+
 int tp_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters, float* sink,
                     void* stream) {
   TP_RETURN_IF(form < 0 || form > 4 || blocks <= 0 || blocks > 65535 || iters < 0,

@@ -616,3 +616,47 @@ int launch_maxplus_bwd_smooth(const SmoothArgs& p, cudaStream_t stream) {
 }
 
 }  // namespace tp
+
+// ---------------------------------------------------------------------------
+// bf16 -> fp32 widening (exact): 8 elements (16 bytes in, 32 bytes out) per
+// thread step when both pointers allow it, scalar otherwise.
+// ---------------------------------------------------------------------------
+namespace tp {
+namespace {
+__global__ void bf16_to_f32_kernel(const uint16_t* __restrict__ src, float* __restrict__ dst,
+                                   int64_t n, bool vec) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t done = 0;
+  if (vec) {
+    const int64_t n8 = n / 8;
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    for (int64_t i = tid; i < n8; i += stride) {
+      const uint4 v = __ldg(s4 + i);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      float f[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        f[2 * j] = __uint_as_float(w[j] << 16);
+        f[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+      }
+      d4[2 * i] = make_float4(f[0], f[1], f[2], f[3]);
+      d4[2 * i + 1] = make_float4(f[4], f[5], f[6], f[7]);
+    }
+    done = n8 * 8;
+  }
+  for (int64_t i = done + tid; i < n; i += stride) dst[i] = tp_bf16_to_f32(src[i]);
+}
+}  // namespace
+
+int launch_bf16_to_f32(const void* src, float* dst, int64_t n, cudaStream_t stream) {
+  if (n == 0) return TP_OK;
+  const bool vec = aligned16(src) && aligned16(dst);
+  int64_t blocks = ceil_div(n, 256 * 8);
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  bf16_to_f32_kernel<<<(unsigned)blocks, 256, 0, stream>>>((const uint16_t*)src, dst, n, vec);
+  return launch_status();
+}
+}  // namespace tp

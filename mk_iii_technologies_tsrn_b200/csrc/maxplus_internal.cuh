@@ -57,6 +57,7 @@ int launch_maxplus_fwd_generic(const StridedMaxPlus& p, cudaStream_t stream);
 int launch_maxplus_lse_fwd_generic(const StridedMaxPlus& p, cudaStream_t stream);
 int launch_maxplus_bwd_argmax(const ScatterArgs& p, cudaStream_t stream);
 int launch_maxplus_bwd_smooth(const SmoothArgs& p, cudaStream_t stream);
+int launch_bf16_to_f32(const void* src, float* dst, int64_t n, cudaStream_t stream);
 int launch_strided_zero(float* base, int64_t B1, int64_t B2, int64_t R, int64_t C, int64_t s_b1,
                         int64_t s_b2, int64_t s_r, int64_t s_c, cudaStream_t stream);
 int launch_column_sum(const float* g, int64_t B1, int64_t B2, int64_t M, int64_t N, int64_t s_b1,

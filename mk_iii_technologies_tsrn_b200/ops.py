@@ -86,6 +86,23 @@ def _batch2(t: torch.Tensor) -> Tuple[int, int, int, int]:
     raise ValueError("at most two leading batch dimensions are supported")
 
 
+def widen_bf16(t: torch.Tensor) -> torch.Tensor:
+    """Exact bf16 -> fp32 copy of a tensor by the library's kernel."""
+    dev = _require_cuda(t)
+    t = t.contiguous()
+    out = torch.empty(t.shape, device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        st = _lib.load().tp_convert_bf16_to_f32(t.numel(), _ptr(t), _ptr(out), _stream(dev))
+    _lib.check(st, "tp_convert_bf16_to_f32")
+    return out
+
+
+def _widen_pays(x: torch.Tensor, w: torch.Tensor) -> bool:
+    # 2-D operands big enough for the TMA kernel: widening costs < 1% there
+    return (x.dim() == 2 and w.dim() == 2 and x.shape[0] >= 128 and w.shape[0] >= 128
+            and x.shape[1] >= 64 and x.shape[0] * w.shape[0] >= 16 * 128 * 128)
+
+
 # --------------------------------------------------------------------------- forward ops
 def maxplus_strided(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
                     *, argmax: bool = True, scale: float = 1.0,
@@ -101,6 +118,10 @@ def maxplus_strided(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tenso
     if x.dtype != w.dtype:
         raise TypeError(f"x and w must share a dtype, got {x.dtype} and {w.dtype}")
     code = _dtype_code(x)
+    if code == TP_DTYPE_BF16 and _widen_pays(x, w):
+        # large bf16 problems: widen exactly to fp32 scratch, run the fp32 TMA kernel
+        x, w = widen_bf16(x), widen_bf16(w)
+        code = TP_DTYPE_F32
     if x.dim() != w.dim() or x.shape[:-2] != w.shape[:-2]:
         raise ValueError(f"batch dims differ: {tuple(x.shape)} vs {tuple(w.shape)}")
     if x.shape[-1] != w.shape[-1]:

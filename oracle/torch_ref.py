@@ -34,3 +34,51 @@ def scan_closed_form_torch(u: torch.Tensor, A_c: torch.Tensor):
     G = torch.cat([A_c.unsqueeze(0).expand(B, -1).unsqueeze(1), shifted], dim=1)
     cm, _ = G.cummax(dim=1)
     return t_idx.unsqueeze(0) * A_c + cm[:, 1:, :]
+
+
+class DTNAttentionRef(torch.nn.Module):
+    """deep_tropical_net.py:90-165 (DTNAttention) on the reference's own torch
+    expressions: TropicalLinear Q/K (tropformer.py:127-145, train-mode STE),
+    classical V/out projections, the gated tropical/classical score
+    (deep_tropical_net.py:145-155) and MaslovTemperature (tropformer.py:206-212).
+    For CPU timing only."""
+
+    def __init__(self, d_model: int, num_heads: int, ste_temp: float = 1.0):
+        super().__init__()
+        import math
+        self.h, self.dk = num_heads, d_model // num_heads
+        self.scale = self.dk ** -0.5
+        self.ste_temp = ste_temp
+        self.q_w = torch.nn.Parameter(torch.empty(d_model, d_model).uniform_(-0.5, 0.5))
+        self.q_b = torch.nn.Parameter(torch.zeros(d_model))
+        self.k_w = torch.nn.Parameter(torch.empty(d_model, d_model).uniform_(-0.5, 0.5))
+        self.k_b = torch.nn.Parameter(torch.zeros(d_model))
+        self.v = torch.nn.Linear(d_model, d_model)
+        self.o = torch.nn.Linear(d_model, d_model)
+        self.gate = torch.nn.Linear(d_model, num_heads)
+        self.log_temps = torch.nn.Parameter(torch.full((num_heads,), math.log(1.0)))
+
+    def _trop_linear(self, x, w, b):
+        lead = x.shape[:-1]
+        xf = x.reshape(-1, x.shape[-1])
+        scores = w.unsqueeze(0) + xf.unsqueeze(1)
+        hard = scores.detach().max(dim=-1).values
+        soft_w = torch.softmax(scores / self.ste_temp, dim=-1)
+        soft = (soft_w * scores).sum(dim=-1)
+        out = hard + (soft - soft.detach()) + b
+        return out.reshape(*lead, w.shape[0])
+
+    def forward(self, x):
+        B, L, D = x.shape
+        split = lambda t: t.view(B, L, self.h, self.dk).transpose(1, 2)
+        Q = split(self._trop_linear(x, self.q_w, self.q_b))
+        K = split(self._trop_linear(x, self.k_w, self.k_b))
+        V = split(self.v(x))
+        cls = torch.matmul(Q, K.transpose(-2, -1)) * self.scale
+        trop = (Q.unsqueeze(3) + K.unsqueeze(2)).max(dim=-1).values * self.scale
+        g = torch.sigmoid(self.gate(x)).permute(0, 2, 1).unsqueeze(-1)
+        scores = g * trop + (1.0 - g) * cls
+        tau = self.log_temps.exp().clamp(min=0.02, max=10.0).view(1, -1, 1, 1)
+        attn = torch.softmax(scores / tau, dim=-1)
+        out = torch.matmul(attn, V).transpose(1, 2).contiguous().view(B, L, D)
+        return self.o(out), attn

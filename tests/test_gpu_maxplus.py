@@ -135,7 +135,7 @@ def test_forward_nan_inf(cuda, M, N, K):
     _check(x, w)
 
 
-@pytest.mark.parametrize("M,N,K", [(512, 256, 320), (33, 20, 50)])
+@pytest.mark.parametrize("M,N,K", [(512, 256, 320), (33, 20, 50), (1024, 640, 200)])
 def test_forward_bf16_inputs(cuda, M, N, K):
     x, w = _gauss(M, N, K, seed=21)
     _check(x, w, dtype=torch.bfloat16)
@@ -197,3 +197,13 @@ def test_bad_pointer_is_reported(cuda):
                             ctypes.c_void_p(y.data_ptr()), 4, None, 0, None)
     assert st == -6  # TP_ERR_BAD_POINTER
     assert lib.tp_device_error(0) == 0
+
+
+def test_bf16_widening_exact(cuda):
+    from mk_iii_technologies_tsrn_b200 import ops
+    bits = torch.randint(0, 1 << 16, (100003,), dtype=torch.int32).to(torch.int16)
+    src = bits.view(torch.bfloat16).to(cuda)
+    out = ops.widen_bf16(src)
+    assert torch.equal(out.view(torch.int32), src.float().view(torch.int32))
+    odd = src[1:]                      # unaligned start: scalar path
+    assert torch.equal(ops.widen_bf16(odd).view(torch.int32), odd.float().view(torch.int32))
