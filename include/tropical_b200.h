@@ -163,8 +163,12 @@ TP_API int tp_maxplus_bwd_argmax_strided(int64_t B1, int64_t B2, int64_t M, int6
                                   float* gw, int64_t sgw_b1, int64_t sgw_b2, int64_t sgw_n, int64_t sgw_k,
                                   float* gbias, float scale, void* stream);
 
-/* Workspace bytes needed by tp_maxplus_bwd_smooth for `batch` (M, N) problems. */
-TP_API int64_t tp_maxplus_bwd_smooth_workspace_bytes(int64_t batch, int64_t M, int64_t N);
+/* Workspace bytes needed by tp_maxplus_bwd_smooth for `batch` (M, N, K)
+ * problems: three [M][N] stat planes per batch, plus per-slice partial sums
+ * when the gradient outputs are too small to fill the GPU and the reduced
+ * index is cut into slices (a function of the shapes only). */
+TP_API int64_t tp_maxplus_bwd_smooth_workspace_bytes(int64_t batch, int64_t M, int64_t N,
+                                                     int64_t K);
 
 /* Smooth backward on `batch` contiguous row-major problems x[b][M][K],
  * w[b][N][K], gy[b][M][N] (mode TP_BWD_STE or TP_BWD_LSE; p = softmax(s/tau)
@@ -175,7 +179,7 @@ TP_API int64_t tp_maxplus_bwd_smooth_workspace_bytes(int64_t batch, int64_t M, i
  *        cuda/maxplus_gemm.cu:181-259):  dS = gy * p
  *   gx[b,m,k] = sum_n dS, gw[b,n,k] = sum_m dS, gbias[n] = sum_{b,m} gy[b,m,n].
  * gx, gw overwritten; gw and gbias may be NULL.  workspace must hold
- * tp_maxplus_bwd_smooth_workspace_bytes(batch,M,N) bytes, 16-byte aligned.
+ * tp_maxplus_bwd_smooth_workspace_bytes(batch,M,N,K) bytes, 16-byte aligned.
  * Deterministic (no atomics).  batch <= 65535.  Tolerance vs fp64: 1e-5
  * relative to the gradient scale. */
 TP_API int tp_maxplus_bwd_smooth(int mode, float tau, int dtype,

@@ -63,7 +63,7 @@ SIGNATURES: dict[str, tuple] = {
          _c_p, _c_i64, _c_i64, _c_i64, _c_i64,
          _c_p, _c_f, _c_p],
     ),
-    "tp_maxplus_bwd_smooth_workspace_bytes": (_c_i64, [_c_i64, _c_i64, _c_i64]),
+    "tp_maxplus_bwd_smooth_workspace_bytes": (_c_i64, [_c_i64, _c_i64, _c_i64, _c_i64]),
     "tp_maxplus_bwd_smooth": (
         _c_int,
         [_c_int, _c_f, _c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,

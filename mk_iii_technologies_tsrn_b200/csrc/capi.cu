@@ -234,9 +234,9 @@ int tp_maxplus_bwd_argmax_strided(int64_t B1, int64_t B2, int64_t M, int64_t N, 
   return launch_maxplus_bwd_argmax(p, as_stream(stream));
 }
 
-int64_t tp_maxplus_bwd_smooth_workspace_bytes(int64_t batch, int64_t M, int64_t N) {
-  if (batch < 0 || M < 0 || N < 0) return 0;
-  return 3 * batch * M * N * (int64_t)sizeof(float);
+int64_t tp_maxplus_bwd_smooth_workspace_bytes(int64_t batch, int64_t M, int64_t N, int64_t K) {
+  if (batch < 0 || M < 0 || N < 0 || K < 0) return 0;
+  return tp::smooth_workspace_floats(batch, M, N, K) * (int64_t)sizeof(float);
 }
 
 int tp_maxplus_bwd_smooth(int mode, float tau, int dtype, int64_t batch, int64_t M, int64_t N,
@@ -252,7 +252,7 @@ int tp_maxplus_bwd_smooth(int mode, float tau, int dtype, int64_t batch, int64_t
   if (M * N > 0) {
     TP_CHECK_PTR(gy);
     TP_RETURN_IF(workspace == nullptr ||
-                     workspace_bytes < tp_maxplus_bwd_smooth_workspace_bytes(batch, M, N),
+                     workspace_bytes < tp_maxplus_bwd_smooth_workspace_bytes(batch, M, N, K),
                  TP_ERR_WORKSPACE);
     TP_RETURN_IF(!aligned16(workspace), TP_ERR_MISALIGNED);
     TP_CHECK_PTR(workspace);
@@ -264,7 +264,9 @@ int tp_maxplus_bwd_smooth(int mode, float tau, int dtype, int64_t batch, int64_t
   if (M * K > 0) TP_CHECK_PTR(gx);
   if (N * K > 0) TP_CHECK_OPT_PTR(gw);
   TP_CHECK_OPT_PTR(gbias);
-  SmoothArgs p{mode, tau, dtype, batch, M, N, K, x, w, gy, gx, gw, gbias, (float*)workspace};
+  SmoothArgs p{mode, tau, dtype, batch, M, N, K, x, w, gy, gx, gw, gbias, (float*)workspace,
+               tp::smooth_splits(batch, M, N, K), tp::smooth_splits(batch, N, M, K),
+               (float*)workspace + 3 * batch * M * N};
   return launch_maxplus_bwd_smooth(p, as_stream(stream));
 }
 

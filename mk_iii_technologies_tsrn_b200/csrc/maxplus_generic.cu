@@ -262,33 +262,47 @@ __global__ void maxplus_bwd_scatter_kernel(ScatterArgs p) {
   }
 }
 
-// gbias[n] = scale * sum over (b1, b2, m) of g[b1, b2, m, n]; deterministic:
-// warp w of the block sums rows w, w+8, ...; the 8 partials are added in a
-// fixed order.
-__global__ void __launch_bounds__(256)
+// gbias[n] = scale * sum over (b1, b2, m) of g[b1, b2, m, n]; deterministic.
+// One block per 32 columns, CS_WARPS warps: warp w sums rows w, w+CS_WARPS, ...
+// into 4 interleaved accumulators (independent loads in flight), and the
+// partials are added in a fixed order.  Rows are walked with an incremental
+// (b1, b2, m) counter, no division in the loop.
+constexpr int CS_WARPS = 32;
+__global__ void __launch_bounds__(CS_WARPS * 32)
     column_sum_kernel(const float* g, int64_t B1, int64_t B2, int64_t M, int64_t N, int64_t s_b1,
                       int64_t s_b2, int64_t s_m, int64_t s_n, float scale, float* out) {
-  __shared__ float part[8][33];
+  __shared__ float part[CS_WARPS][33];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int64_t n = (int64_t)blockIdx.x * 32 + lane;
-  float acc = 0.0f;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   if (n < N) {
+    const float* gn = g + n * s_n;
+    // rows are (b1, b2, m) in row-major order; when they collapse to one
+    // stride the loop is a plain strided walk
+    const bool flat = (B2 == 1 || s_b2 == M * s_m) && (B1 == 1 || s_b1 == B2 * M * s_m);
     const int64_t rows = B1 * B2 * M;
-    for (int64_t r = warp; r < rows; r += 8) {
-      int64_t m = r % M;
-      int64_t t = r / M;
-      int64_t b2 = t % B2;
-      int64_t b1 = t / B2;
-      acc += g[b1 * s_b1 + b2 * s_b2 + m * s_m + n * s_n];
+    if (flat) {
+      int64_t r = warp;
+      for (; r + 3 * CS_WARPS < rows; r += 4 * CS_WARPS) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[u] += gn[(r + u * CS_WARPS) * s_m];
+      }
+      for (; r < rows; r += CS_WARPS) acc[0] += gn[r * s_m];
+    } else {
+      for (int64_t b1 = 0; b1 < B1; ++b1)
+        for (int64_t b2 = 0; b2 < B2; ++b2) {
+          const float* gb = gn + b1 * s_b1 + b2 * s_b2;
+          for (int64_t m = warp; m < M; m += CS_WARPS) acc[0] += gb[m * s_m];
+        }
     }
   }
-  part[warp][lane] = acc;
+  part[warp][lane] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   __syncthreads();
   if (warp == 0 && n < N) {
     float s = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += part[w][lane];
+    for (int w = 0; w < CS_WARPS; ++w) s += part[w][lane];
     out[n] = s * scale;
   }
 }
@@ -404,7 +418,9 @@ __global__ void __launch_bounds__(G_THREADS) smooth_grad_kernel(SmoothArgs p) {
   const int ty = threadIdx.x / 16;
   const int64_t r0 = (int64_t)blockIdx.y * GB_M;
   const int64_t k0 = (int64_t)blockIdx.x * GB_N;
-  const int64_t bz = blockIdx.z;
+  const int64_t S = kOut == 0 ? p.splits_x : p.splits_w;
+  const int64_t bz = blockIdx.z / S;
+  const int64_t split = blockIdx.z % S;
   const T* xb = static_cast<const T*>(p.x) + bz * p.M * p.K;
   const T* wb = static_cast<const T*>(p.w) + bz * p.N * p.K;
   const float* wsb = p.ws + bz * 3 * p.M * p.N;
@@ -414,6 +430,10 @@ __global__ void __launch_bounds__(G_THREADS) smooth_grad_kernel(SmoothArgs p) {
   const int64_t Q = kOut == 0 ? p.N : p.M;
   const float L = 1.4426950408889634f / p.tau;
   const int64_t MN = p.M * p.N;
+  // this block's slice [qbeg, qend) of the reduced index, in whole slabs
+  const int64_t qchunk = ceil_div(ceil_div(Q, S), (int64_t)QS) * QS;
+  const int64_t qbeg = split * qchunk;
+  const int64_t qend = (qbeg + qchunk < Q) ? qbeg + qchunk : Q;
 
   float own[4][4], acc[4][4];
 #pragma unroll
@@ -426,13 +446,13 @@ __global__ void __launch_bounds__(G_THREADS) smooth_grad_kernel(SmoothArgs p) {
       acc[i][j] = 0.0f;
     }
 
-  for (int64_t q0 = 0; q0 < Q; q0 += QS) {
+  for (int64_t q0 = qbeg; q0 < qend; q0 += QS) {
     __syncthreads();
     // other operand slab [QS][64 k]
     for (int e = threadIdx.x; e < QS * GB_N; e += G_THREADS) {
       int qq = e / GB_N, kk = e % GB_N;
       int64_t q = q0 + qq, k = k0 + kk;
-      os[qq][kk] = (q < Q && k < p.K) ? tp_load_as_f32<T>(other + q * p.K + k) : 0.0f;
+      os[qq][kk] = (q < qend && k < p.K) ? tp_load_as_f32<T>(other + q * p.K + k) : 0.0f;
     }
     // stats slab [3][QS][64 r]; stats are stored [M][N]
     for (int e = threadIdx.x; e < 3 * QS * GB_M; e += G_THREADS) {
@@ -448,7 +468,7 @@ __global__ void __launch_bounds__(G_THREADS) smooth_grad_kernel(SmoothArgs p) {
       }
       int64_t q = q0 + qq, r = r0 + rr;
       float v = 0.0f;
-      if (q < Q && r < R) {
+      if (q < qend && r < R) {
         int64_t m = kOut == 0 ? r : q;
         int64_t n = kOut == 0 ? q : r;
         v = wsb[pl * MN + m * p.N + n];
@@ -456,7 +476,7 @@ __global__ void __launch_bounds__(G_THREADS) smooth_grad_kernel(SmoothArgs p) {
       st[pl][qq][rr] = v;
     }
     __syncthreads();
-    const int qmax = (int)((Q - q0) < QS ? (Q - q0) : QS);
+    const int qmax = (int)((qend - q0) < QS ? (qend - q0) : QS);
     for (int qq = 0; qq < qmax; ++qq) {
       float ob[4];
 #pragma unroll
@@ -476,7 +496,8 @@ __global__ void __launch_bounds__(G_THREADS) smooth_grad_kernel(SmoothArgs p) {
       }
     }
   }
-  float* out = kOut == 0 ? p.gx + bz * p.M * p.K : p.gw + bz * p.N * p.K;
+  float* out = S > 1 ? p.part + ((int64_t)blockIdx.z) * R * p.K
+                     : (kOut == 0 ? p.gx + bz * p.M * p.K : p.gw + bz * p.N * p.K);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     int64_t r = r0 + ty + 16 * i;
@@ -486,6 +507,20 @@ __global__ void __launch_bounds__(G_THREADS) smooth_grad_kernel(SmoothArgs p) {
       int64_t k = k0 + tx + 16 * j;
       if (k < p.K) out[r * p.K + k] = acc[i][j];
     }
+  }
+}
+
+// out[b][i] = sum_s part[b][s][i], s in increasing order (deterministic).
+__global__ void split_sum_kernel(const float* __restrict__ part, int64_t batch, int64_t S,
+                                 int64_t n, float* __restrict__ out) {
+  const int64_t total = batch * n;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = e / n, i = e % n;
+    const float* src = part + b * S * n + i;
+    float acc = 0.0f;
+    for (int64_t s = 0; s < S; ++s) acc += src[s * n];
+    out[e] = acc;
   }
 }
 
@@ -568,9 +603,32 @@ int launch_column_sum(const float* g, int64_t B1, int64_t B2, int64_t M, int64_t
                       int64_t s_b2, int64_t s_m, int64_t s_n, float scale, float* out,
                       cudaStream_t stream) {
   if (N == 0) return TP_OK;
-  column_sum_kernel<<<(unsigned)ceil_div(N, 32), 256, 0, stream>>>(g, B1, B2, M, N, s_b1, s_b2,
-                                                                   s_m, s_n, scale, out);
+  column_sum_kernel<<<(unsigned)ceil_div(N, 32), CS_WARPS * 32, 0, stream>>>(
+      g, B1, B2, M, N, s_b1, s_b2, s_m, s_n, scale, out);
   return launch_status();
+}
+
+// Split the reduced index when the output tiles (64 x 64) give fewer blocks
+// than two per SM of a B200 (148 SMs); aim for about four per SM, with at
+// least 256 reduced elements per slice.
+int64_t smooth_splits(int64_t batch, int64_t rows, int64_t Q, int64_t K) {
+  constexpr int64_t kFewBlocks = 2 * 148, kTargetBlocks = 4 * 148, kMinSlice = 256;
+  if (batch <= 0 || rows <= 0 || K <= 0 || Q < 2 * kMinSlice) return 1;
+  const int64_t tiles = batch * ceil_div(rows, (int64_t)GB_M) * ceil_div(K, (int64_t)GB_N);
+  if (tiles >= kFewBlocks) return 1;
+  int64_t s = ceil_div(kTargetBlocks, tiles);
+  const int64_t by_len = ceil_div(Q, kMinSlice);
+  if (s > by_len) s = by_len;
+  if (s > 65535 / batch) s = 65535 / batch;
+  return s < 1 ? 1 : s;
+}
+
+int64_t smooth_workspace_floats(int64_t batch, int64_t M, int64_t N, int64_t K) {
+  const int64_t sx = smooth_splits(batch, M, N, K), sw = smooth_splits(batch, N, M, K);
+  int64_t part = 0;
+  if (sx > 1) part = batch * sx * M * K;
+  if (sw > 1 && batch * sw * N * K > part) part = batch * sw * N * K;
+  return 3 * batch * M * N + part;
 }
 
 int launch_maxplus_bwd_smooth(const SmoothArgs& p, cudaStream_t stream) {
@@ -596,18 +654,31 @@ int launch_maxplus_bwd_smooth(const SmoothArgs& p, cudaStream_t stream) {
   int s = launch_status();
   if (s != TP_OK) return s;
   if (p.K > 0) {
-    dim3 gx((unsigned)ceil_div(p.K, GB_N), (unsigned)ceil_div(p.M, GB_M), nb);
-    dim3 gw((unsigned)ceil_div(p.K, GB_N), (unsigned)ceil_div(p.N, GB_M), nb);
+    const int64_t sx = p.splits_x, sw = p.splits_w;
+    if (sx < 1 || sw < 1 || nb * sx > 65535 || nb * sw > 65535) return TP_ERR_INVALID_ARG;
+    dim3 gx((unsigned)ceil_div(p.K, GB_N), (unsigned)ceil_div(p.M, GB_M), (unsigned)(nb * sx));
+    dim3 gw((unsigned)ceil_div(p.K, GB_N), (unsigned)ceil_div(p.N, GB_M), (unsigned)(nb * sw));
     if (gx.y > 65535u || gw.y > 65535u) return TP_ERR_TOO_LARGE;
-    if (p.dtype == TP_DTYPE_F32) {
+    if (p.dtype == TP_DTYPE_F32)
       smooth_grad_kernel<float, 0><<<gx, G_THREADS, 0, stream>>>(p);
-      if (p.gw) smooth_grad_kernel<float, 1><<<gw, G_THREADS, 0, stream>>>(p);
-    } else {
+    else
       smooth_grad_kernel<uint16_t, 0><<<gx, G_THREADS, 0, stream>>>(p);
-      if (p.gw) smooth_grad_kernel<uint16_t, 1><<<gw, G_THREADS, 0, stream>>>(p);
-    }
+    if (sx > 1)
+      split_sum_kernel<<<flat_grid(p.batch * p.M * p.K, 256), 256, 0, stream>>>(
+          p.part, p.batch, sx, p.M * p.K, p.gx);
     s = launch_status();
     if (s != TP_OK) return s;
+    if (p.gw) {
+      if (p.dtype == TP_DTYPE_F32)
+        smooth_grad_kernel<float, 1><<<gw, G_THREADS, 0, stream>>>(p);
+      else
+        smooth_grad_kernel<uint16_t, 1><<<gw, G_THREADS, 0, stream>>>(p);
+      if (sw > 1)
+        split_sum_kernel<<<flat_grid(p.batch * p.N * p.K, 256), 256, 0, stream>>>(
+            p.part, p.batch, sw, p.N * p.K, p.gw);
+      s = launch_status();
+      if (s != TP_OK) return s;
+    }
   }
   if (p.gbias)
     return launch_column_sum(p.gy, p.batch, 1, p.M, p.N, p.M * p.N, 0, p.N, 1, 1.0f, p.gbias,

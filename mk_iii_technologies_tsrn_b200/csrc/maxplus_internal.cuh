@@ -50,7 +50,20 @@ struct SmoothArgs {
   float* gw;
   float* gbias;
   float* ws;  // per batch 3 planes of [M][N]: reference max, A, B
+  // Splits of the reduced index for gx (over n) and gw (over m); > 1 only when
+  // the output tiles alone cannot fill the GPU.  Partial sums then go to
+  // `part` ([batch][splits][rows][K], after the stat planes in the workspace)
+  // and are added in split order.
+  int64_t splits_x, splits_w;
+  float* part;
 };
+
+// Number of slices the smooth backward cuts the reduced index Q into for an
+// output of `rows` x K per batch.  Depends on the shapes only, so the
+// workspace size is known before the call.
+int64_t smooth_splits(int64_t batch, int64_t rows, int64_t Q, int64_t K);
+// Workspace floats of the smooth backward (stat planes + split partials).
+int64_t smooth_workspace_floats(int64_t batch, int64_t M, int64_t N, int64_t K);
 
 // maxplus_generic.cu
 int launch_maxplus_fwd_generic(const StridedMaxPlus& p, cudaStream_t stream);

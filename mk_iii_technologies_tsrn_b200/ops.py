@@ -258,7 +258,7 @@ def maxplus_backward_smooth(mode: str, tau: float, x: torch.Tensor, w: torch.Ten
     if w.shape != (B, N, K) or gy.shape != (B, M, N):
         raise ValueError("shape mismatch in smooth backward")
     lib = _lib.load()
-    ws_bytes = int(lib.tp_maxplus_bwd_smooth_workspace_bytes(B, M, N))
+    ws_bytes = int(lib.tp_maxplus_bwd_smooth_workspace_bytes(B, M, N, K))
     ws = torch.empty(max(ws_bytes // 4, 4), device=dev, dtype=torch.float32)
     gx = torch.empty((B, M, K), device=dev, dtype=torch.float32)
     gw = torch.empty((B, N, K), device=dev, dtype=torch.float32) if need_gw else None

@@ -107,3 +107,24 @@ def test_empty_rows(cuda):
     y = ops.MaxPlusLinearFunction.apply(x, w, None, "ste", 1.0)
     y.sum().backward()
     assert torch.all(w.grad == 0)
+
+
+@pytest.mark.parametrize("batch,M,N,K", [(1, 64, 4096, 128), (3, 2048, 64, 64), (1, 8, 1500, 40)])
+def test_smooth_split_reduction(cuda, batch, M, N, K):
+    # shapes whose gradient outputs are too small to fill the GPU: the reduced
+    # index (n for gx, m for gw) is cut into slices whose partials are added in
+    # slice order -- same tolerance as the unsplit path, and bitwise repeatable
+    ops = _fn()
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((batch, M, K)).astype(np.float32)
+    w = rng.standard_normal((batch, N, K)).astype(np.float32)
+    g = rng.standard_normal((batch, M, N)).astype(np.float32)
+    xt, wt, gt = (torch.tensor(a, device=cuda) for a in (x, w, g))
+    gx, gw, gb = ops.maxplus_backward_smooth("ste", 0.5, xt, wt, gt, need_gbias=True)
+    gx2, gw2, gb2 = ops.maxplus_backward_smooth("ste", 0.5, xt, wt, gt, need_gbias=True)
+    assert torch.equal(gx, gx2) and torch.equal(gw, gw2) and torch.equal(gb, gb2)
+    for b in range(batch):
+        rgx, rgw, rgb = oracle.maxplus_bwd_smooth("ste", 0.5, x[b], w[b], g[b])
+        assert _rel_err(gx[b].cpu().numpy(), rgx) < 1e-5
+        assert _rel_err(gw[b].cpu().numpy(), rgw) < 1e-5
+    np.testing.assert_allclose(gb.cpu().numpy(), g.sum(axis=(0, 1)), rtol=1e-5, atol=1e-4)
