@@ -45,6 +45,36 @@ __device__ __forceinline__ float tp_max_nan(float a, float b) {
   return r;
 }
 
+// Packed fp32 pairs (sm_100a add/fma .f32x2): each half is an ordinary
+// round-to-nearest fp32 add / fused multiply-add, two per instruction.
+__device__ __forceinline__ float2 tp_add2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 pa, pb, pr;\n\t"
+      "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "add.rn.f32x2 pr, pa, pb;\n\tmov.b64 {%0, %1}, pr;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+__device__ __forceinline__ float2 tp_fma2(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 pa, pb, pc, pr;\n\t"
+      "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\tmov.b64 pc, {%6, %7};\n\t"
+      "fma.rn.f32x2 pr, pa, pb, pc;\n\tmov.b64 {%0, %1}, pr;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+
+// 2^x with the hardware approximation (PTX ex2.approx.ftz.f32: relative error
+// about 2^-22, subnormal results flushed to zero, 2^-inf = 0).
+__device__ __forceinline__ float tp_ex2(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 __device__ __forceinline__ float tp_bf16_to_f32(uint16_t v) {
   return __uint_as_float(((uint32_t)v) << 16);
 }

@@ -308,18 +308,58 @@ __global__ void __launch_bounds__(CS_WARPS * 32)
 }
 
 // ---------------------------------------------------------------------------
-// smooth backward (contiguous x[M,K], w[N,K], gy[M,N])
-//   pass 1 (stats): per (m,n): mx = max_k s, then with t = s - mx and
-//          e = 2^(t*L):  Z = sum e,  S1 = sum e*t
-//          STE: A = g/Z * (1 - (S1/Z)/tau),  B = g/(Z*tau)
-//          LSE: A = g/Z,                     B = 0
-//          so that dS = e * (A + B*t).
+// smooth backward (contiguous x[M,K], w[N,K], gy[M,N]).
+//
+// Everything runs in the base-2 domain scaled by L = log2(e)/tau: operands
+// are multiplied by L when staged, so a term is sL = xL + wL and its weight
+// 2^(sL - refL) = exp((s - ref)/tau) costs one ex2.approx.
+//   pass 1 (stats): per (m,n): refL = max_k sL; with tL = sL - refL and
+//          e = 2^tL:  Z = sum e,  S1 = sum e*tL
+//          STE: Bp = g / (Z*log2e),  A = g/Z - Bp*S1/Z
+//          LSE: Bp = 0,              A = g/Z
+//          so that dS = e * (A + Bp*tL)  [= g p (1 + (s - sbar)/tau) for STE].
 //   pass 2 (gx): gx[m,k] = sum_n dS      pass 3 (gw): gw[n,k] = sum_m dS
+// A term whose tL is -inf (an operand of -inf) contributes nothing: tL is
+// clamped at -256, where 2^tL is already 0, so e*(A + Bp*tL) is 0 and not
+// 0*inf; the clamp keeps NaN (max.NaN), so NaN operands still give NaN.
+// Thread (tx, ty) of a 64 x 64 tile owns rows 4*ty..4*ty+3 and columns
+// 4*tx..4*tx+3: both operand fragments are one 16-byte shared load.
 // ---------------------------------------------------------------------------
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kClampL = -256.0f;
+
+// load_slab with every staged value multiplied by `mul` (fills unscaled)
 template <typename T>
-__global__ void __launch_bounds__(G_THREADS) smooth_stats_kernel(SmoothArgs p) {
-  __shared__ float xs[GB_K][GB_M + 4];
-  __shared__ float ws[GB_K][GB_N + 4];
+__device__ __forceinline__ void load_slab_scaled(float (*dst)[GB_M + 4], const T* base,
+                                                 int64_t rows, int64_t K, int64_t r0, int64_t k0,
+                                                 float kfill, float mul) {
+#pragma unroll
+  for (int r = 0; r < (GB_M * GB_K) / G_THREADS; ++r) {
+    int e = threadIdx.x + r * G_THREADS;
+    int rr = e / GB_K;
+    int kk = e % GB_K;
+    int64_t gr = r0 + rr;
+    int64_t gk = k0 + kk;
+    float v;
+    if (gk >= K) {
+      v = kfill;
+    } else if (gr >= rows) {
+      v = 0.0f;
+    } else {
+      v = tp_load_as_f32<T>(base + gr * K + gk) * mul;
+    }
+    dst[kk][rr] = v;
+  }
+}
+
+__device__ __forceinline__ float4 lds_f4(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(G_THREADS, 3) smooth_stats_kernel(SmoothArgs p) {
+  __shared__ __align__(16) float xs[GB_K][GB_M + 4];
+  __shared__ __align__(16) float ws[GB_K][GB_N + 4];
   const int tx = threadIdx.x % 16;
   const int ty = threadIdx.x / 16;
   const int64_t m0 = (int64_t)blockIdx.y * GB_M;
@@ -330,90 +370,115 @@ __global__ void __launch_bounds__(G_THREADS) smooth_stats_kernel(SmoothArgs p) {
   const float* gyb = p.gy + bz * p.M * p.N;
   float* wsb = p.ws + bz * 3 * p.M * p.N;
   const float NEG_INF = -__int_as_float(0x7f800000);
-  const float L = 1.4426950408889634f / p.tau;
+  const float L = kLog2e / p.tau;
 
-  float mx[4][4], Z[4][4], S1[4][4];
+  // pass 0: refL = max_k (xL + wL)
+  float mx[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      mx[i][j] = NEG_INF;
-      Z[i][j] = 0.0f;
-      S1[i][j] = 0.0f;
-    }
-  for (int pass = 0; pass < 2; ++pass) {
-    float ref[4][4];
-    if (pass == 1) {
+    for (int j = 0; j < 4; ++j) mx[i][j] = NEG_INF;
+  for (int64_t k0 = 0; k0 < p.K; k0 += GB_K) {
+    __syncthreads();
+    load_slab_scaled<T>(xs, xg, p.M, p.K, m0, k0, NEG_INF, L);
+    load_slab_scaled<T>(ws, wg, p.N, p.K, n0, k0, 0.0f, L);
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < GB_K; ++kk) {
+      const float4 a4 = lds_f4(&xs[kk][4 * ty]);
+      const float4 b4 = lds_f4(&ws[kk][4 * tx]);
+      const float a[4] = {a4.x, a4.y, a4.z, a4.w};
+      const float b[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) ref[i][j] = isfinite(mx[i][j]) ? mx[i][j] : 0.0f;
+        for (int j = 0; j < 4; ++j) mx[i][j] = tp_max_nan(mx[i][j], a[i] + b[j]);
     }
-    for (int64_t k0 = 0; k0 < p.K; k0 += GB_K) {
-      __syncthreads();
-      load_slab<T>(xs, xg, p.K, 1, p.M, p.K, m0, k0, NEG_INF);
-      load_slab<T>(ws, wg, p.K, 1, p.N, p.K, n0, k0, 0.0f);
-      __syncthreads();
+  }
+
+  // pass 1: Z and S1 relative to refL, two columns per packed instruction.
+  // Outputs whose max is not finite use refL = 0 and get zero weights (bit
+  // 4*i+j of `finite` clear).
+  float2 nref[4][2], Z[4][2], S1[4][2];
+  uint32_t finite = 0;
 #pragma unroll
-      for (int kk = 0; kk < GB_K; ++kk) {
-        float a[4], b[4];
+  for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) a[i] = xs[kk][ty + 16 * i];
+    for (int h = 0; h < 2; ++h) {
+      const bool f0 = isfinite(mx[i][2 * h]), f1 = isfinite(mx[i][2 * h + 1]);
+      finite |= (f0 ? 1u : 0u) << (4 * i + 2 * h);
+      finite |= (f1 ? 1u : 0u) << (4 * i + 2 * h + 1);
+      nref[i][h] = make_float2(f0 ? -mx[i][2 * h] : 0.0f, f1 ? -mx[i][2 * h + 1] : 0.0f);
+      Z[i][h] = make_float2(0.0f, 0.0f);
+      S1[i][h] = make_float2(0.0f, 0.0f);
+    }
+  for (int64_t k0 = 0; k0 < p.K; k0 += GB_K) {
+    __syncthreads();
+    load_slab_scaled<T>(xs, xg, p.M, p.K, m0, k0, NEG_INF, L);
+    load_slab_scaled<T>(ws, wg, p.N, p.K, n0, k0, 0.0f, L);
+    __syncthreads();
+#pragma unroll 4
+    for (int kk = 0; kk < GB_K; ++kk) {
+      const float4 a4 = lds_f4(&xs[kk][4 * ty]);
+      const float4 b4 = lds_f4(&ws[kk][4 * tx]);
+      const float a[4] = {a4.x, a4.y, a4.z, a4.w};
+      const float2 bp[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) b[j] = ws[kk][tx + 16 * j];
+      for (int i = 0; i < 4; ++i) {
+        const float2 ap = make_float2(a[i], a[i]);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float s = a[i] + b[j];
-            if (pass == 0) {
-              mx[i][j] = tp_max_nan(mx[i][j], s);
-            } else {
-              float t = s - ref[i][j];
-              float e = exp2f(t * L);
-              Z[i][j] += e;
-              S1[i][j] += (e == 0.0f) ? 0.0f : e * t;
-            }
-          }
+        for (int h = 0; h < 2; ++h) {
+          float2 t = tp_add2(tp_add2(ap, bp[h]), nref[i][h]);
+          t.x = tp_max_nan(t.x, kClampL);
+          t.y = tp_max_nan(t.y, kClampL);
+          const float2 e = make_float2(tp_ex2(t.x), tp_ex2(t.y));
+          Z[i][h] = tp_add2(Z[i][h], e);
+          S1[i][h] = tp_fma2(e, t, S1[i][h]);
+        }
       }
     }
   }
+
   const int64_t MN = p.M * p.N;
+  const float inv_log2e = 1.0f / kLog2e;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    int64_t m = m0 + ty + 16 * i;
+    const int64_t m = m0 + 4 * ty + i;
     if (m >= p.M) continue;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      int64_t n = n0 + tx + 16 * j;
+      const int64_t n = n0 + 4 * tx + j;
       if (n >= p.N) continue;
-      float g = gyb[m * p.N + n];
-      float A = 0.0f, B = 0.0f, ref = 0.0f;
-      if (isfinite(mx[i][j]) && Z[i][j] > 0.0f) {
-        ref = mx[i][j];
-        float invZ = 1.0f / Z[i][j];
+      const float z = j & 1 ? Z[i][j >> 1].y : Z[i][j >> 1].x;
+      const float s1 = j & 1 ? S1[i][j >> 1].y : S1[i][j >> 1].x;
+      const float g = gyb[m * p.N + n];
+      float A = 0.0f, Bp = 0.0f, ref = 0.0f;
+      if (((finite >> (4 * i + j)) & 1u) && z > 0.0f) {
+        ref = -(j & 1 ? nref[i][j >> 1].y : nref[i][j >> 1].x);
+        const float invZ = 1.0f / z;
         if (p.mode == TP_BWD_STE) {
-          float sbar = S1[i][j] * invZ;
-          A = g * invZ * (1.0f - sbar / p.tau);
-          B = g * invZ / p.tau;
+          Bp = g * invZ * inv_log2e;
+          A = g * invZ - Bp * s1 * invZ;
         } else {
           A = g * invZ;
         }
       }
       wsb[m * p.N + n] = ref;
       wsb[MN + m * p.N + n] = A;
-      wsb[2 * MN + m * p.N + n] = B;
+      wsb[2 * MN + m * p.N + n] = Bp;
     }
   }
 }
 
 // gx[m,k] (kOut == 0) or gw[n,k] (kOut == 1).  Tile over (r, k) with r = m or
-// n; loop over the other index q (n or m) in slabs of 16.
+// n; loop over this block's slice of the other index q (n or m) in slabs of
+// QS.  The three stat planes are staged interleaved ({refL, A, Bp} per (q, r))
+// so that a row's stats are one 16-byte shared load.
 template <typename T, int kOut>
-__global__ void __launch_bounds__(G_THREADS) smooth_grad_kernel(SmoothArgs p) {
-  constexpr int QS = 16;
-  __shared__ float os[QS][GB_N + 4];   // other operand: [q][k]
-  __shared__ float st[3][QS][GB_M + 4];  // stats: [plane][q][r]
+__global__ void __launch_bounds__(G_THREADS, 3) smooth_grad_kernel(SmoothArgs p) {
+  constexpr int QS = 32;
+  __shared__ __align__(16) float os[QS][GB_N];      // other operand, scaled: [q][k]
+  __shared__ __align__(16) float4 st[QS][GB_M];     // stats: [q][r] {refL, A, Bp, -}
   const int tx = threadIdx.x % 16;
   const int ty = threadIdx.x / 16;
   const int64_t r0 = (int64_t)blockIdx.y * GB_M;
@@ -428,70 +493,76 @@ __global__ void __launch_bounds__(G_THREADS) smooth_grad_kernel(SmoothArgs p) {
   const T* other = kOut == 0 ? wb : xb;
   const int64_t R = kOut == 0 ? p.M : p.N;
   const int64_t Q = kOut == 0 ? p.N : p.M;
-  const float L = 1.4426950408889634f / p.tau;
+  const float L = kLog2e / p.tau;
   const int64_t MN = p.M * p.N;
   // this block's slice [qbeg, qend) of the reduced index, in whole slabs
   const int64_t qchunk = ceil_div(ceil_div(Q, S), (int64_t)QS) * QS;
   const int64_t qbeg = split * qchunk;
   const int64_t qend = (qbeg + qchunk < Q) ? qbeg + qchunk : Q;
 
-  float own[4][4], acc[4][4];
+  float2 own[4][2], acc[4][2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = r0 + 4 * ty + i;
+    float v[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      int64_t r = r0 + ty + 16 * i;
-      int64_t k = k0 + tx + 16 * j;
-      own[i][j] = (r < R && k < p.K) ? tp_load_as_f32<T>(mine + r * p.K + k) : 0.0f;
-      acc[i][j] = 0.0f;
+      const int64_t k = k0 + 4 * tx + j;
+      v[j] = (r < R && k < p.K) ? tp_load_as_f32<T>(mine + r * p.K + k) * L : 0.0f;
     }
+    own[i][0] = make_float2(v[0], v[1]);
+    own[i][1] = make_float2(v[2], v[3]);
+    acc[i][0] = make_float2(0.0f, 0.0f);
+    acc[i][1] = make_float2(0.0f, 0.0f);
+  }
 
   for (int64_t q0 = qbeg; q0 < qend; q0 += QS) {
     __syncthreads();
-    // other operand slab [QS][64 k]
     for (int e = threadIdx.x; e < QS * GB_N; e += G_THREADS) {
-      int qq = e / GB_N, kk = e % GB_N;
-      int64_t q = q0 + qq, k = k0 + kk;
-      os[qq][kk] = (q < qend && k < p.K) ? tp_load_as_f32<T>(other + q * p.K + k) : 0.0f;
+      const int qq = e / GB_N, kk = e % GB_N;
+      const int64_t q = q0 + qq, k = k0 + kk;
+      os[qq][kk] = (q < qend && k < p.K) ? tp_load_as_f32<T>(other + q * p.K + k) * L : 0.0f;
     }
-    // stats slab [3][QS][64 r]; stats are stored [M][N]
+    // stats are stored [M][N]: read along n for coalescing
     for (int e = threadIdx.x; e < 3 * QS * GB_M; e += G_THREADS) {
-      int pl = e / (QS * GB_M);
-      int rem = e % (QS * GB_M);
+      const int pl = e / (QS * GB_M);
+      const int rem = e % (QS * GB_M);
       int qq, rr;
-      if (kOut == 0) {  // r = m, q = n: read along n for coalescing
+      if (kOut == 0) {  // r = m, q = n
         rr = rem / QS;
         qq = rem % QS;
-      } else {  // r = n, q = m: read along n (= r)
+      } else {          // r = n, q = m
         qq = rem / GB_M;
         rr = rem % GB_M;
       }
-      int64_t q = q0 + qq, r = r0 + rr;
+      const int64_t q = q0 + qq, r = r0 + rr;
       float v = 0.0f;
       if (q < qend && r < R) {
-        int64_t m = kOut == 0 ? r : q;
-        int64_t n = kOut == 0 ? q : r;
+        const int64_t m = kOut == 0 ? r : q;
+        const int64_t n = kOut == 0 ? q : r;
         v = wsb[pl * MN + m * p.N + n];
       }
-      st[pl][qq][rr] = v;
+      reinterpret_cast<float*>(&st[qq][rr])[pl] = v;
     }
     __syncthreads();
     const int qmax = (int)((qend - q0) < QS ? (qend - q0) : QS);
+#pragma unroll 2
     for (int qq = 0; qq < qmax; ++qq) {
-      float ob[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) ob[j] = os[qq][tx + 16 * j];
+      const float4 o4 = *reinterpret_cast<const float4*>(&os[qq][4 * tx]);
+      const float2 ob[2] = {make_float2(o4.x, o4.y), make_float2(o4.z, o4.w)};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float ref = st[0][qq][ty + 16 * i];
-        const float A = st[1][qq][ty + 16 * i];
-        const float B = st[2][qq][ty + 16 * i];
+        const float4 sv = st[qq][4 * ty + i];
+        const float2 nref = make_float2(-sv.x, -sv.x);
+        const float2 A = make_float2(sv.y, sv.y);
+        const float2 Bp = make_float2(sv.z, sv.z);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float s = own[i][j] + ob[j];
-          float t = s - ref;
-          float e = exp2f(t * L);
-          acc[i][j] += (e == 0.0f) ? 0.0f : e * fmaf(B, t, A);
+        for (int h = 0; h < 2; ++h) {
+          float2 t = tp_add2(tp_add2(own[i][h], ob[h]), nref);
+          t.x = tp_max_nan(t.x, kClampL);
+          t.y = tp_max_nan(t.y, kClampL);
+          const float2 e = make_float2(tp_ex2(t.x), tp_ex2(t.y));
+          acc[i][h] = tp_fma2(e, tp_fma2(Bp, t, A), acc[i][h]);
         }
       }
     }
@@ -500,12 +571,13 @@ __global__ void __launch_bounds__(G_THREADS) smooth_grad_kernel(SmoothArgs p) {
                      : (kOut == 0 ? p.gx + bz * p.M * p.K : p.gw + bz * p.N * p.K);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    int64_t r = r0 + ty + 16 * i;
+    const int64_t r = r0 + 4 * ty + i;
     if (r >= R) continue;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      int64_t k = k0 + tx + 16 * j;
-      if (k < p.K) out[r * p.K + k] = acc[i][j];
+      const int64_t k = k0 + 4 * tx + j;
+      const float v = j & 1 ? acc[i][j >> 1].y : acc[i][j >> 1].x;
+      if (k < p.K) out[r * p.K + k] = v;
     }
   }
 }
