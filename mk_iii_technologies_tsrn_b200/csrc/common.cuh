@@ -45,6 +45,13 @@ __device__ __forceinline__ float tp_max_nan(float a, float b) {
   return r;
 }
 
+// 3-input NaN-propagating max (one instruction on sm_100a)
+__device__ __forceinline__ float tp_max3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Packed fp32 pairs (sm_100a add/fma .f32x2): each half is an ordinary
 // round-to-nearest fp32 add / fused multiply-add, two per instruction.
 __device__ __forceinline__ float2 tp_add2(float2 a, float2 b) {

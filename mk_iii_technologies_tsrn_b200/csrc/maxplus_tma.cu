@@ -11,23 +11,27 @@
 //
 // CTA (one per SM, persistent over 128x128 output tiles, grouped raster):
 //   compute warps   TY x TX threads, TM x TN outputs per thread (template)
-//   producer warp   one lane issues TMA loads of 128x32 fp32 x/w tiles
-//                   (128-byte swizzle, no multicast) into a 4-stage
-//                   full/empty mbarrier ring
+//   TMA loads       128x32 fp32 x/w tiles (128-byte swizzle, no multicast)
+//                   into a full/empty mbarrier ring.  The value-only kernel
+//                   has a producer warp and 4 stages; the argmax kernel lets
+//                   its thread 0 issue the loads (16 warps: 128 registers per
+//                   thread) and uses 3 stages (more L1 for the search below).
 //
 // Exact argmax without per-term index tracking.  The running max only grows,
 // so the lowest k attaining the final max lies in the LAST CHUNK-wide k-range
 // in which the accumulator changed.  At each chunk boundary the compute
 // threads compare their accumulators with a snapshot kept in shared memory
 // (bitwise, so NaN counts once) and record the chunk index (16-bit, shared
-// memory).  After the main pass over K the producer streams the tile's
-// k-tiles through the ring a second time (the data is mostly still in L2).
-// The outputs are first bucketed by chunk (a counting sort in shared memory),
-// so that each chunk's outputs are searched by all compute warps evenly,
-// straight from shared memory: the first k whose sum equals the output's max
-// (or is NaN when the max is NaN) is its argmax.  The
-// result equals torch.max(dim=-1) on the reference's broadcast tensor, bit
-// for bit, in values and indices.
+// memory).  At the end of a tile each thread stores its outputs' raw maxima
+// in y and their chunk indices in argmax; while the CTA computes its NEXT
+// tile, each thread searches its previous tile's outputs, 8 k at a time: the
+// x and w quads of a unit are loaded (through L1/L2) at one k-tile and tested
+// at the next, so the loads hide behind the tile's arithmetic.  The first k
+// of the chunk whose sum equals the output's max (or is NaN when the max is
+// NaN) is its argmax; then the final y (bias, scale) and the argmax are
+// stored.  The CTA's last tile is searched after its main loop.  The result
+// equals torch.max(dim=-1) on the reference's broadcast tensor, bit for bit,
+// in values and indices.
 //
 // Every mbarrier wait is bounded (common.cuh); a timeout records a device
 // error and the kernel returns.
@@ -54,15 +58,19 @@ constexpr int QUNROLL = TP_TMA_QUNROLL;
 constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int BK = 32;           // fp32 per TMA row: 128 bytes (one swizzle atom)
-constexpr int STAGES = 4;
+// Ring depth: the value-only kernel keeps 4 stages; the argmax kernel uses 3,
+// which leaves more of the SM's L1 to the argmax search's global loads (the
+// search re-reads x and w row chunks that neighbouring outputs share).
+template <bool kArgmax>
+constexpr int stages() { return kArgmax ? 3 : 4; }
 constexpr int TILE_BYTES = BM * BK * 4;                                  // 16 KB
 constexpr int STAGE_BYTES = 2 * TILE_BYTES;
 constexpr int SNAP_BYTES = BM * BN * 4;                                  // 64 KB
 constexpr int CIDX_BYTES = BM * BN * 2;                                  // 32 KB
-constexpr int MAX_ARGMAX_CHUNKS = 512;                                   // argmax path: K <= 512*CHUNK
-constexpr int OFFS_BYTES = (MAX_ARGMAX_CHUNKS + 8) * 2;                  // u16 bucket offsets
-constexpr int SMEM_BYTES =
-    STAGES * STAGE_BYTES + SNAP_BYTES + CIDX_BYTES + OFFS_BYTES + 128 + 1024;
+template <bool kArgmax>
+constexpr int smem_bytes() {
+  return stages<kArgmax>() * STAGE_BYTES + (kArgmax ? SNAP_BYTES + CIDX_BYTES : 0) + 128 + 1024;
+}
 
 template <int TM_, int TN_, int CHUNK_>
 struct Cfg {
@@ -71,15 +79,19 @@ struct Cfg {
   static constexpr int TY = BM / TM;       // threads along m
   static constexpr int CT = TX * TY;       // compute threads
   static constexpr int CW = CT / 32;       // compute warps
-  static constexpr int PRODUCER_WARP = CW;
+  static constexpr int PRODUCER_WARP = CW;           // value-only kernel: a TMA warp
   static constexpr int THREADS = 32 * (CW + 1);
+  // The argmax kernel has no producer warp (its thread 0 issues the TMA loads):
+  // 16 warps leave 128 registers per thread, room for the search's loads.
+  template <bool kArgmax>
+  static constexpr int threads() { return kArgmax ? CT : THREADS; }
   static constexpr int OUTS = TM * TN;     // outputs per compute thread
   static constexpr int KT_PER_CHUNK = CHUNK / BK;
   static constexpr int64_t MAX_K = (int64_t)CHUNK * 65535;  // 16-bit chunk index
   static_assert(CT % 32 == 0, "compute threads must fill warps");
   static_assert(OUTS % 4 == 0, "snapshot uses float4");
   static_assert((TX % 8) == 0 && (TY % 8) == 0, "swizzle phase must be per-thread constant");
-  static_assert(CHUNK % BK == 0 && KT_PER_CHUNK <= STAGES, "a chunk must fit the ring");
+  static_assert(CHUNK % BK == 0 && CHUNK % 8 == 0, "chunks are whole k-tiles and search units");
 };
 
 using DefaultCfg = Cfg<TP_TMA_TM, TP_TMA_TN, TP_TMA_CHUNK>;
@@ -88,6 +100,10 @@ constexpr int MAX_DESTS = 8;   // output copies (the ranks of one NVLink domain)
 
 struct TmaParams {
   int64_t M, N, K;
+  const float* x;   // the operands again, for the argmax search's global loads
+  int64_t ldx;
+  const float* w;
+  int64_t ldw;
   const float* bias;
   float* y;
   int64_t ldy;
@@ -131,12 +147,6 @@ __device__ __forceinline__ void lds128(uint32_t addr, uint64_t& a, uint64_t& b) 
   asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr));
 }
 
-__device__ __forceinline__ float lds32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
-  return v;
-}
-
 __device__ __forceinline__ uint64_t mask_pair(uint64_t v, bool lo_bad, bool hi_bad) {
   const uint64_t NEG = 0xff800000ull;
   if (lo_bad) v = (v & 0xffffffff00000000ull) | NEG;
@@ -144,33 +154,76 @@ __device__ __forceinline__ uint64_t mask_pair(uint64_t v, bool lo_bad, bool hi_b
   return v;
 }
 
-// Barrier among the compute threads only (the producer warp never takes
-// part), on an mbarrier so that the wait is bounded like every other wait:
-// every compute thread arrives, then waits for the phase to complete.
-__device__ __forceinline__ bool compute_sync(uint64_t* bar, uint32_t& phase, int* err) {
-  tp_mbar_arrive(bar);
-  const bool ok = tp_mbar_wait(bar, phase, err);
-  phase ^= 1u;
-  return ok;
+// Argmax search helpers.  A unit is 8 consecutive k of one output: x and w
+// quads (a0 a1, b0 b1).  unit_first_hit returns the first k of the unit whose
+// sum equals the output's max tv (tv NaN: whose sum is NaN), or kBestNone.
+// The common case -- the unit does not hold the max -- costs eight adds, a
+// three-instruction max tree and one compare.
+constexpr int kBestNone = 0x7fffffff;
+
+__device__ __forceinline__ int unit_first_hit(float tv, int k, int K, const float4& a0,
+                                              const float4& a1, const float4& b0,
+                                              const float4& b1) {
+  const float s[8] = {a0.x + b0.x, a0.y + b0.y, a0.z + b0.z, a0.w + b0.w,
+                      a1.x + b1.x, a1.y + b1.y, a1.z + b1.z, a1.w + b1.w};
+  float mx = tp_max3_nan(s[0], s[1], s[2]);
+  mx = tp_max3_nan(mx, s[3], s[4]);
+  mx = tp_max3_nan(mx, s[5], s[6]);
+  mx = tp_max_nan(mx, s[7]);
+  const bool tnan = tv != tv;
+  int best = kBestNone;
+  if (tnan ? (mx != mx) : (mx == tv)) {
+#pragma unroll
+    for (int e = 7; e >= 0; --e) {
+      const bool hit = (k + e < K) && (tnan ? (s[e] != s[e]) : (s[e] == tv));
+      if (hit) best = k + e;
+    }
+  }
+  return best;
 }
 
-// atomic post-increment of a 16-bit shared counter (through its aligned word)
-__device__ __forceinline__ uint32_t atomicAdd_u16(uint16_t* p) {
-  uint32_t* w = (uint32_t*)((uintptr_t)p & ~(uintptr_t)3);
-  const uint32_t sh = ((uintptr_t)p & 2) ? 16u : 0u;
-  const uint32_t old = atomicAdd(w, 1u << sh);
-  return (old >> sh) & 0xffffu;
+// x and w quads of the unit at xr / wr (its first k is k); k >= K reads as
+// x = -inf, w = 0, so that it can never hold the max
+__device__ __forceinline__ void load_unit(const float* xr, const float* wr, int k, int K,
+                                          float4& a0, float4& a1, float4& b0, float4& b1) {
+  if (k + 8 <= K) {
+    a0 = __ldg(reinterpret_cast<const float4*>(xr));
+    a1 = __ldg(reinterpret_cast<const float4*>(xr + 4));
+    b0 = __ldg(reinterpret_cast<const float4*>(wr));
+    b1 = __ldg(reinterpret_cast<const float4*>(wr + 4));
+  } else {
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    float xv[8], wv[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const bool in = k + e < K;
+      xv[e] = in ? __ldg(xr + e) : NEG_INF;
+      wv[e] = in ? __ldg(wr + e) : 0.0f;
+    }
+    a0 = make_float4(xv[0], xv[1], xv[2], xv[3]);
+    a1 = make_float4(xv[4], xv[5], xv[6], xv[7]);
+    b0 = make_float4(wv[0], wv[1], wv[2], wv[3]);
+    b1 = make_float4(wv[4], wv[5], wv[6], wv[7]);
+  }
 }
 
-// shared-memory address of element (row, k) of a 128 x 32 fp32 tile stored
-// with the 128-byte TMA swizzle (16-byte chunk c of row r sits at c ^ (r & 7))
-__device__ __forceinline__ uint32_t swz(uint32_t base, int row, int k) {
-  return base + (uint32_t)row * 128u + ((((uint32_t)k >> 2) ^ ((uint32_t)row & 7u)) << 4) +
-         ((uint32_t)k & 3u) * 4u;
+// final value (bias, scale) and argmax of output (m, n), to y/argmax and to
+// every extra destination
+__device__ __forceinline__ void store_output(const TmaParams& p, int64_t m, int64_t n, float tv,
+                                             int32_t k) {
+  p.am[m * p.lda + n] = k;
+  float v = tv;
+  if (p.bias) v = v + p.bias[n];
+  if (p.scale != 1.0f) v = v * p.scale;
+  p.y[m * p.ldy + n] = v;
+  for (int d = 0; d < p.ndst; ++d) {
+    p.ydst[d][m * p.ldy + p.col0 + n] = v;
+    p.adst[d][m * p.lda + p.col0 + n] = k;
+  }
 }
 
 template <class C, bool kArgmax>
-__global__ void __launch_bounds__(C::THREADS, 1)
+__global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
     maxplus_tma_kernel(const __grid_constant__ CUtensorMap xmap,
                        const __grid_constant__ CUtensorMap wmap, const TmaParams p) {
   constexpr int TM = C::TM, TN = C::TN, TX = C::TX, TY = C::TY, CT = C::CT;
@@ -178,62 +231,60 @@ __global__ void __launch_bounds__(C::THREADS, 1)
   // 1024-byte alignment for the 128-byte swizzle pattern
   unsigned char* smem =
       (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  constexpr int STAGES = stages<kArgmax>();
   unsigned char* stage_base = smem;                                  // STAGES x (x tile, w tile)
   float4* snap = (float4*)(smem + STAGES * STAGE_BYTES);             // [OUTS/4][CT]
   uint16_t* cid = (uint16_t*)(smem + STAGES * STAGE_BYTES + SNAP_BYTES);  // [OUTS][CT]
-  uint16_t* offs = (uint16_t*)(smem + STAGES * STAGE_BYTES + SNAP_BYTES + CIDX_BYTES);
-  uint64_t* bars =
-      (uint64_t*)(smem + STAGES * STAGE_BYTES + SNAP_BYTES + CIDX_BYTES + OFFS_BYTES);
+  uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES +
+                               (kArgmax ? SNAP_BYTES + CIDX_BYTES : 0));
   uint64_t* full = bars;                 // [STAGES]
   uint64_t* empty = bars + STAGES;       // [STAGES]
-  uint64_t* cbar = bars + 2 * STAGES;    // compute-thread barrier
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // k-tile passes per output tile: the main pass, plus the argmax pass
-  constexpr int PASSES = kArgmax ? 2 : 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       tp_mbar_init(&full[s], 1);
       tp_mbar_init(&empty[s], C::CW);
     }
-    tp_mbar_init(cbar, CT);
     tp_fence_mbar_init();
   }
   __syncthreads();
 
-  if (warp == C::PRODUCER_WARP) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      tp_prefetch_tensormap(&xmap);
-      tp_prefetch_tensormap(&wmap);
-      uint32_t it = 0;
-      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-        int mt, nt;
-        tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
-        for (int pass = 0; pass < PASSES; ++pass) {
-          // main pass in k order; the argmax pass chunk by chunk from the last
-          // chunk back (its k-tiles were read most recently: likelier L2 hits)
-          const int nchunks = (p.k_tiles + C::KT_PER_CHUNK - 1) / C::KT_PER_CHUNK;
-          for (int i = 0; i < p.k_tiles; ++i, ++it) {
-            int kt = i;
-            if (pass == 1) {
-              const int c = nchunks - 1 - i / C::KT_PER_CHUNK;   // valid: chunks are full
-              kt = c * C::KT_PER_CHUNK + i % C::KT_PER_CHUNK;    // except the last one,
-              if (nchunks * C::KT_PER_CHUNK != p.k_tiles) {       // which comes first
-                const int last = p.k_tiles - (nchunks - 1) * C::KT_PER_CHUNK;  // its size
-                if (i < last) {
-                  kt = (nchunks - 1) * C::KT_PER_CHUNK + i;
-                } else {
-                  const int j = i - last;
-                  kt = (nchunks - 2 - j / C::KT_PER_CHUNK) * C::KT_PER_CHUNK + j % C::KT_PER_CHUNK;
-                }
-              }
-            }
-            const uint32_t s = it % STAGES;
-            const uint32_t ph = (it / STAGES) & 1u;
-            if (!tp_mbar_wait(&empty[s], ph ^ 1u, p.err)) return;
+  // k-tile j of this CTA (tiles blockIdx.x, +gridDim.x, ...; k-tiles in order)
+  // goes to stage j % STAGES once the stage's previous k-tile is released
+  const uint32_t my_tiles = (uint32_t)((p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) /
+                                       (int)gridDim.x);
+  const uint32_t total_kt = my_tiles * (uint32_t)p.k_tiles;
+  auto produce = [&](uint32_t j) -> bool {
+    const int tile = (int)blockIdx.x + (int)(j / (uint32_t)p.k_tiles) * (int)gridDim.x;
+    const int kt = (int)(j % (uint32_t)p.k_tiles);
+    int mt, nt;
+    tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+    const uint32_t s = j % STAGES;
+    const uint32_t ph = (j / STAGES) & 1u;
+    if (!tp_mbar_wait(&empty[s], ph ^ 1u, p.err)) return false;
+    unsigned char* dst = stage_base + s * STAGE_BYTES;
+    tp_mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+    tp_tma_load_2d(dst, &xmap, kt * BK, mt * BM, &full[s]);
+    tp_tma_load_2d(dst + TILE_BYTES, &wmap, kt * BK, nt * BN, &full[s]);
+    return true;
+  };
+
+  if constexpr (!kArgmax) {
+    if (warp == C::PRODUCER_WARP) {
+      // ---------------------------------------------------------- producer
+      if (lane == 0) {
+        tp_prefetch_tensormap(&xmap);
+        tp_prefetch_tensormap(&wmap);
+        uint32_t j = 0;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+          int mt, nt;
+          tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+          for (int kt = 0; kt < p.k_tiles; ++kt, ++j) {
+            const uint32_t s = j % STAGES;
+            if (!tp_mbar_wait(&empty[s], ((j / STAGES) & 1u) ^ 1u, p.err)) return;
             unsigned char* dst = stage_base + s * STAGE_BYTES;
             tp_mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
             tp_tma_load_2d(dst, &xmap, kt * BK, mt * BM, &full[s]);
@@ -241,8 +292,17 @@ __global__ void __launch_bounds__(C::THREADS, 1)
           }
         }
       }
+      return;
     }
-    return;
+  } else {
+    // thread 0 fills all but one stage now, then one stage per k-tile: at
+    // k-tile j it refills the stage of k-tile j-1 with k-tile j+STAGES-1
+    if (threadIdx.x == 0) {
+      tp_prefetch_tensormap(&xmap);
+      tp_prefetch_tensormap(&wmap);
+      for (uint32_t j = 0; j < STAGES - 1 && j < total_kt; ++j)
+        if (!produce(j)) return;
+    }
   }
 
   // -------------------------------------------------------------- compute
@@ -250,12 +310,74 @@ __global__ void __launch_bounds__(C::THREADS, 1)
   const int tx = t % TX;
   const int ty = t / TX;
   const uint32_t stage_addr = tp_smem_addr(stage_base);
-  const uint32_t snap_addr = tp_smem_addr(snap);
   const uint32_t xsw = (uint32_t)(ty & 7);
   const uint32_t wsw = (uint32_t)(tx & 7);
   const float NEG_INF = -__int_as_float(0x7f800000);
+
+  // Deferred argmax search of the previous tile (see the file comment).  The
+  // thread's outputs are searched in 8-k units; a unit's four 16-byte loads
+  // are issued at one k-tile of the current tile and tested at the next.
+  constexpr int UPO = C::CHUNK / 8;            // units per output
+  constexpr int UNITS = C::OUTS * UPO;         // units per thread per tile
+  const int Kc = (int)p.K;
+  const int Mc = (int)p.M, Nc = (int)p.N;
+  int s_u = UNITS + 1;          // next unit to issue (unit s_u-1 in flight); UNITS+1: idle
+  int s_m0 = 0, s_n0 = 0;       // origin of the tile being searched
+  float s_tv = 0.0f, s_ntv = 0.0f;   // max of the current / next output
+  int s_kc = 0, s_nkc = 0;           // first k of their chunks
+  int s_best = kBestNone;
+  const float* s_xp = nullptr;  // next unit's x / w (null: the output is outside M x N)
+  const float* s_wp = nullptr;
+  float4 qa0 = make_float4(0.f, 0.f, 0.f, 0.f), qa1 = qa0, qb0 = qa0, qb1 = qa0;
+  const int steps = kArgmax ? (UNITS + p.k_tiles - 1) / p.k_tiles : 0;
+
+  // the raw max and chunk this thread stored for output o of the searched tile
+  auto prefetch = [&](int o) {
+    const int m = s_m0 + ty + TY * (o / TN), n = s_n0 + tx + TX * (o % TN);
+    if (o < C::OUTS && m < Mc && n < Nc) {
+      s_ntv = p.y[(int64_t)m * p.ldy + n];
+      s_nkc = p.am[(int64_t)m * p.lda + n] * C::CHUNK;
+    }
+  };
+  // test the unit in flight, then issue the next one
+  auto step = [&]() {
+    if (s_u >= 1 && s_u <= UNITS) {
+      const int pu = s_u - 1;
+      if (s_xp != nullptr) {
+        if (s_best == kBestNone)
+          s_best = unit_first_hit(s_tv, s_kc + 8 * (pu % UPO), Kc, qa0, qa1, qb0, qb1);
+        if (pu % UPO == UPO - 1) {
+          const int o = pu / UPO;
+          store_output(p, s_m0 + ty + TY * (o / TN), s_n0 + tx + TX * (o % TN), s_tv,
+                       s_best != kBestNone ? s_best : s_kc);
+        }
+      }
+    }
+    if (s_u < UNITS) {
+      if (s_u % UPO == 0) {
+        const int o = s_u / UPO;
+        const int m = s_m0 + ty + TY * (o / TN), n = s_n0 + tx + TX * (o % TN);
+        s_tv = s_ntv;
+        s_kc = s_nkc;
+        s_best = kBestNone;
+        if (m < Mc && n < Nc) {
+          s_xp = p.x + (int64_t)m * p.ldx + s_kc;
+          s_wp = p.w + (int64_t)n * p.ldw + s_kc;
+        } else {
+          s_xp = s_wp = nullptr;
+        }
+        prefetch(o + 1);
+      }
+      if (s_xp != nullptr) {
+        load_unit(s_xp, s_wp, s_kc + 8 * (s_u % UPO), Kc, qa0, qa1, qb0, qb1);
+        s_xp += 8;
+        s_wp += 8;
+      }
+    }
+    if (s_u <= UNITS) ++s_u;
+  };
+
   uint32_t it = 0;
-  uint32_t cphase = 0;
   for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
     int mt, nt;
     tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
@@ -273,11 +395,15 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       for (int o = 0; o < C::OUTS; ++o) cid[o * CT + t] = 0;
     }
 
-    // ---- main pass: values (+ chunk tracking)
+    // ---- main pass: values (+ chunk tracking, + the previous tile's search)
     for (int kt = 0; kt < p.k_tiles; ++kt, ++it) {
       const uint32_t s = it % STAGES;
       const uint32_t ph = (it / STAGES) & 1u;
+      if (kArgmax && threadIdx.x == 0 && it + STAGES - 1 < total_kt)
+        if (!produce(it + STAGES - 1)) return;
       if (!tp_mbar_wait(&full[s], ph, p.err)) return;
+      if (kArgmax)
+        for (int r = 0; r < steps; ++r) step();
       const uint32_t xbase = stage_addr + s * STAGE_BYTES;
       const uint32_t wbase = xbase + TILE_BYTES;
       const int64_t k0 = (int64_t)kt * BK;
@@ -331,7 +457,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       }
     }
 
-    if (!kArgmax) {
+    if constexpr (!kArgmax) {
       // ---- value-only epilogue
 #pragma unroll
       for (int i = 0; i < TM; ++i) {
@@ -348,173 +474,56 @@ __global__ void __launch_bounds__(C::THREADS, 1)
           for (int d = 0; d < p.ndst; ++d) p.ydst[d][m * p.ldy + p.col0 + n] = v;
         }
       }
-      continue;
+    } else {
+    // ---- argmax: finish the previous tile's search (its last unit is in
+    // flight), then hand this tile's raw maxima and chunks to the search
+    while (s_u <= UNITS) step();
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+      const int64_t m = m0 + ty + TY * i;
+      if (m >= p.M) continue;
+#pragma unroll
+      for (int j = 0; j < TN; ++j) {
+        const int64_t n = n0 + tx + TX * j;
+        if (n >= p.N) continue;
+        p.y[m * p.ldy + n] = acc[i][j];
+        p.am[m * p.lda + n] = (int32_t)cid[(i * TN + j) * CT + t];
+      }
     }
+    s_m0 = (int)m0;
+    s_n0 = (int)n0;
+    s_u = 0;
+    prefetch(0);
+    }
+  }
 
-    // ---- argmax pass.  The snapshot holds each output's final max and cid its
-    // last-change chunk.  First bucket the tile's outputs by chunk (counting
-    // sort in shared memory; the list overwrites cid), then stream the tile's
-    // k-tiles through the ring again; each chunk's outputs are shared evenly
-    // by the CTA's 4-lane groups, which search 8 k per lane and k-tile with
-    // 16-byte shared loads and write the argmax and the final value.
-    const int nchunks = (p.k_tiles + C::KT_PER_CHUNK - 1) / C::KT_PER_CHUNK;
-    for (int c = t; c <= nchunks; c += CT) offs[c] = 0;
-    if (!compute_sync(cbar, cphase, p.err)) return;
-#pragma unroll 4
-    for (int o = 0; o < C::OUTS; ++o) {                   // count per chunk (in offs[c+1])
-      const bool valid = (m0 + ty + TY * (o / TN) < p.M) && (n0 + tx + TX * (o % TN) < p.N);
-      if (valid) atomicAdd_u16(&offs[cid[o * CT + t] + 1]);
+  if (s_u == 0) {
+    // ---- drain: the CTA's last tile (the tile loop always ends with a
+    // hand-off, so nothing of it has been searched yet).  Each output's units
+    // are tested four at a time.
+    for (int o = 0; o < C::OUTS; ++o) {
+      const int m = s_m0 + ty + TY * (o / TN), n = s_n0 + tx + TX * (o % TN);
+      if (m >= Mc || n >= Nc) continue;
+      const float tv = p.y[(int64_t)m * p.ldy + n];
+      const int kc = p.am[(int64_t)m * p.lda + n] * C::CHUNK;
+      const float* xr = p.x + (int64_t)m * p.ldx + kc;
+      const float* wr = p.w + (int64_t)n * p.ldw + kc;
+      int best = kBestNone;
+      for (int j0 = 0; j0 < UPO && best == kBestNone; j0 += 4) {
+        float4 dx[4][2], dw[4][2];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (j0 + u < UPO)
+            load_unit(xr + 8 * (j0 + u), wr + 8 * (j0 + u), kc + 8 * (j0 + u), Kc, dx[u][0],
+                      dx[u][1], dw[u][0], dw[u][1]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (j0 + u < UPO && best == kBestNone)
+            best = unit_first_hit(tv, kc + 8 * (j0 + u), Kc, dx[u][0], dx[u][1], dw[u][0],
+                                  dw[u][1]);
+      }
+      store_output(p, m, n, tv, best != kBestNone ? best : kc);
     }
-    if (!compute_sync(cbar, cphase, p.err)) return;
-    if (warp == 0) {                              // prefix sum: offs[c] = start of chunk c
-      uint32_t carry = 0;
-      for (int base = 0; base <= nchunks; base += 32) {
-        const int c = base + lane;
-        uint32_t v = c <= nchunks ? offs[c] : 0u;
-#pragma unroll
-        for (int d = 1; d < 32; d <<= 1) {
-          const uint32_t up = __shfl_up_sync(0xffffffffu, v, d);
-          if (lane >= d) v += up;
-        }
-        if (c <= nchunks) offs[c] = (uint16_t)(v + carry);
-        carry += __shfl_sync(0xffffffffu, v, 31);
-      }
-    }
-    {
-      // my outputs' chunk ids, two per register (0xFFFF: not an output); read
-      // before the barrier, because the list below overwrites cid
-      uint32_t cr[C::OUTS / 2];
-#pragma unroll
-      for (int q = 0; q < C::OUTS / 2; ++q) {
-        uint32_t v[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int o = 2 * q + h;
-          const bool valid = (m0 + ty + TY * (o / TN) < p.M) && (n0 + tx + TX * (o % TN) < p.N);
-          v[h] = valid ? (uint32_t)cid[o * CT + t] : 0xFFFFu;
-        }
-        cr[q] = v[0] | (v[1] << 16);
-      }
-      if (!compute_sync(cbar, cphase, p.err)) return;
-      // scatter: the counter of each chunk walks from its start to its end, so
-      // afterwards offs[c] is the end of chunk c (= start of chunk c+1)
-#pragma unroll
-      for (int q = 0; q < C::OUTS / 2; ++q) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t c = h ? (cr[q] >> 16) : (cr[q] & 0xffffu);
-          if (c != 0xFFFFu) {
-            const uint32_t pos = atomicAdd_u16(&offs[c]);
-            cid[pos] = (uint16_t)((2 * q + h) * CT + t);   // list entry: output slot
-          }
-        }
-      }
-    }
-    if (!compute_sync(cbar, cphase, p.err)) return;
-
-    // 4 lanes per output: lane gl covers k = 8*gl .. 8*gl+7 of each k-tile.
-    // The stages of a chunk are held only for the shared loads and compares:
-    // the items' metadata is fetched before the chunk's wait, and the group
-    // reductions and global stores happen after the stages are released.
-    const int g = lane >> 2, gl = lane & 3;
-    const int group = warp * 8 + g;                  // 0 .. 8*CW-1
-    constexpr int NGROUPS = 8 * C::CW;
-    constexpr int R = 1;                             // rounds prepared per chunk
-    for (int c = nchunks - 1; c >= 0; --c) {
-      const int kt0 = c * C::KT_PER_CHUNK;
-      const int nkt = min(C::KT_PER_CHUNK, p.k_tiles - kt0);
-      const int kbase = kt0 * BK, kmax = (int)p.K;
-      const int lo = c > 0 ? offs[c - 1] : 0, hi = offs[c];
-      for (int base0 = lo; base0 < hi; base0 += R * NGROUPS) {   // warp-uniform
-        bool active[R];
-        int mr[R], nr[R];
-        float tv[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const int item = base0 + r * NGROUPS + group;
-          active[r] = item < hi;
-          const int slot = active[r] ? cid[item] : 0;
-          const int o = slot / CT, tl = slot % CT;
-          mr[r] = tl / TX + TY * (o / TN);
-          nr[r] = tl % TX + TX * (o % TN);
-          tv[r] = lds32(snap_addr + ((uint32_t)((o >> 2) * CT + tl) * 4u + (o & 3)) * 4u);
-        }
-        const bool last_batch = base0 + R * NGROUPS >= hi;
-        if (base0 == lo) {
-          for (int u = 0; u < nkt; ++u) {
-            const uint32_t s = (it + u) % STAGES;
-            if (!tp_mbar_wait(&full[s], ((it + u) / STAGES) & 1u, p.err)) return;
-          }
-        }
-        int best[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          best[r] = 1 << 30;
-          const bool tnan = tv[r] != tv[r];
-#pragma unroll
-          for (int u = 0; u < C::KT_PER_CHUNK; ++u) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              if (u < nkt) {
-                const uint32_t xb = stage_addr + ((it + u) % STAGES) * STAGE_BYTES;
-                const uint32_t q = (uint32_t)(2 * gl + h);       // 16-byte chunk of the row
-                uint64_t xv0, xv1, wv0, wv1;
-                lds128(xb + (uint32_t)mr[r] * 128u + ((q ^ ((uint32_t)mr[r] & 7u)) << 4), xv0, xv1);
-                lds128(xb + TILE_BYTES + (uint32_t)nr[r] * 128u +
-                           ((q ^ ((uint32_t)nr[r] & 7u)) << 4),
-                       wv0, wv1);
-                const float sum[4] = {
-                    __uint_as_float((uint32_t)xv0) + __uint_as_float((uint32_t)wv0),
-                    __uint_as_float((uint32_t)(xv0 >> 32)) + __uint_as_float((uint32_t)(wv0 >> 32)),
-                    __uint_as_float((uint32_t)xv1) + __uint_as_float((uint32_t)wv1),
-                    __uint_as_float((uint32_t)(xv1 >> 32)) + __uint_as_float((uint32_t)(wv1 >> 32))};
-                const int kl = u * BK + 4 * (int)q;               // chunk-local k of sum[0]
-#pragma unroll
-                for (int e = 3; e >= 0; --e) {
-                  const bool hit = (kbase + kl + e < kmax) &&
-                                   (tnan ? (sum[e] != sum[e]) : (sum[e] == tv[r]));
-                  if (hit) best[r] = min(best[r], kl + e);
-                }
-              }
-            }
-          }
-        }
-        if (last_batch) {                             // release the chunk's stages
-          __syncwarp();
-          if (lane == 0)
-            for (int u = 0; u < nkt; ++u) tp_mbar_arrive(&empty[(it + u) % STAGES]);
-        }
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          int b = min(best[r], __shfl_xor_sync(0xffffffffu, best[r], 1));
-          b = min(b, __shfl_xor_sync(0xffffffffu, b, 2));
-          if (active[r] && gl == 0) {
-            const int64_t m = m0 + mr[r], n = n0 + nr[r];
-            const int32_t k = b < (1 << 30) ? kbase + b : kbase;
-            p.am[m * p.lda + n] = k;
-            float v = tv[r];
-            if (p.bias) v = v + p.bias[n];
-            if (p.scale != 1.0f) v = v * p.scale;
-            p.y[m * p.ldy + n] = v;
-            for (int d = 0; d < p.ndst; ++d) {
-              p.ydst[d][m * p.ldy + p.col0 + n] = v;
-              p.adst[d][m * p.lda + p.col0 + n] = k;
-            }
-          }
-        }
-      }
-      if (lo == hi) {                                 // an empty chunk still holds stages
-        for (int u = 0; u < nkt; ++u) {
-          const uint32_t s = (it + u) % STAGES;
-          if (!tp_mbar_wait(&full[s], ((it + u) / STAGES) & 1u, p.err)) return;
-        }
-        __syncwarp();
-        if (lane == 0)
-          for (int u = 0; u < nkt; ++u) tp_mbar_arrive(&empty[(it + u) % STAGES]);
-      }
-      it += nkt;
-    }
-    if (!compute_sync(cbar, cphase, p.err)) return;   // the list (in cid) is read until here
   }
 }
 
@@ -535,11 +544,13 @@ template <class C, bool kArgmax>
 int launch_cfg(const CUtensorMap& xmap, const CUtensorMap& wmap, const TmaParams& tp_,
                cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(maxplus_tma_kernel<C, kArgmax>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       smem_bytes<kArgmax>());
   if (e != cudaSuccess) return (int)e;
   int grid = num_sms();
   if (grid > tp_.num_tiles) grid = tp_.num_tiles;
-  maxplus_tma_kernel<C, kArgmax><<<grid, C::THREADS, SMEM_BYTES, stream>>>(xmap, wmap, tp_);
+  maxplus_tma_kernel<C, kArgmax>
+      <<<grid, C::template threads<kArgmax>(), smem_bytes<kArgmax>(), stream>>>(xmap, wmap, tp_);
   return launch_status();
 }
 
@@ -550,7 +561,6 @@ bool maxplus_tma_eligible(const StridedMaxPlus& p) {
   if (p.B1 * p.B2 != 1) return false;
   if (p.sx_k != 1 || p.sw_k != 1 || p.sy_n != 1) return false;
   if (p.am && p.sa_n != 1) return false;
-  if (p.am && ceil_div(p.K, DefaultCfg::CHUNK) > MAX_ARGMAX_CHUNKS) return false;
   if (p.M < BM || p.N < BN || p.K < 2 * BK || p.K > DefaultCfg::MAX_K) return false;
   if ((p.sx_m % 4) != 0 || (p.sw_n % 4) != 0) return false;
   if (!aligned16(p.x) || !aligned16(p.w)) return false;
@@ -575,6 +585,10 @@ int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
   tp_.M = p.M;
   tp_.N = p.N;
   tp_.K = p.K;
+  tp_.x = (const float*)p.x;
+  tp_.ldx = p.sx_m;
+  tp_.w = (const float*)p.w;
+  tp_.ldw = p.sw_n;
   tp_.bias = p.bias;
   tp_.y = p.y;
   tp_.ldy = p.sy_m;
