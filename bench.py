@@ -14,6 +14,9 @@ weak scaling): forward (read b, x; write h: 12 B/elem) plus argmax-path
 backward recomputing the winners (read g, h, b, x; write gu: 20 B/elem);
 metric GB/s of those algorithmic bytes.
 
+``--workload linear``: config 1, the tropical linear x [1024,256] (x) W [256,256]
+forward with int32 argmax and the argmax backward; Gop/s of forward ops.
+
 ``--workload dtn``: config 2, the drop-in DTNAttention(256, 8) block
 (tropical Q/K projections with the STE backward, tropical score, Maslov
 softmax) forward + backward at B=128, L=64 per rank; metric tokens/s.
@@ -55,7 +58,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["gemm", "scan", "dtn"], default="gemm")
+    p.add_argument("--workload", choices=["gemm", "scan", "dtn", "linear"], default="gemm")
     p.add_argument("--size", type=int, default=8192, help="M = N = K of the GEMM workload")
     p.add_argument("--dtype", choices=["f32", "bf16"], default="f32",
                    help="GEMM operand storage (bf16 is widened exactly; arithmetic is fp32)")
@@ -586,6 +589,138 @@ def dtn_workload(args, world, rank):
     }
 
 
+def linear_workload(args, world, rank):
+    """Config 1: tropical linear x [1024,256] (x) W [256,256] forward with int32 argmax
+    plus the argmax backward (upstream g ~ N(0,1)); per rank (weak scaling)."""
+    from mk_iii_technologies_tsrn_b200 import ops, _lib
+
+    _lib.load().tp_set_pointer_checks(0)
+    M, K, N = 1024, 256, 256
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(rank)
+    hx = torch.randn(M, K, generator=gen).pin_memory()
+    hw = torch.randn(N, K, generator=gen)
+    hg = torch.randn(M, N, generator=gen).pin_memory()
+    x = hx.to(dev).requires_grad_(True)
+    w = hw.to(dev).requires_grad_(True)
+    gy = hg.to(dev)
+
+    def step(xi=x, gi=gy):
+        y = ops.MaxPlusLinearFunction.apply(xi, w, None, "argmax", 1.0)
+        gx, gw = torch.autograd.grad(y, (xi, w), gi)
+        return y, gx, gw
+
+    # parity on this workload before timing: values and the gradient scatter
+    y, gx, gw = step()
+    ry, ri, rgx, rgw = oracle_linear(hx, hw, hg)
+    if not torch.equal(y.detach().cpu(), ry):
+        raise RuntimeError("config-1 forward differs from the reference expression")
+    if (gx.cpu() - rgx).abs().max() > 1e-4 or (gw.cpu() - rgw).abs().max() > 1e-3:
+        raise RuntimeError("config-1 backward differs from the reference autograd")
+    steps = max(args.steps, 50)
+    for _ in range(max(args.warmup, 10)):
+        step()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    ms = time_steps(step, steps, world)
+    clk = clocks.stop()
+    ops_step = 2.0 * M * N * K
+    value = ops_step * world / (ms / steps / 1e3) / 1e9
+    # dominant kernel: the forward with argmax, timed alone
+    xd = x.detach()
+    wd = w.detach()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ops.maxplus(xd, wd)
+    e0.record()
+    for _ in range(50):
+        ops.maxplus(xd, wd)
+    e1.record()
+    torch.cuda.synchronize()
+    kms = e0.elapsed_time(e1) / 50
+    probe = []
+    for form in range(5):
+        ops.probe_addmax(form, 148 * 8, 50)
+        pms, terms = ops.probe_addmax(form, 148 * 8, 400)
+        probe.append(2.0 * terms / (pms / 1e3) / 1e12)
+    peak = max(probe)
+    achieved = ops_step / (kms / 1e3) / 1e12
+    # end to end: x and g from pinned host, y and gx back
+    dx = torch.empty_like(xd)
+    dg = torch.empty_like(gy)
+    hy = torch.empty(M, N).pin_memory()
+    hgx = torch.empty(M, K).pin_memory()
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        dg.copy_(hg, non_blocking=True)
+        xi = dx.requires_grad_(True)
+        y, gx, _ = step(xi, dg)
+        hy.copy_(y.detach(), non_blocking=True)
+        hgx.copy_(gx, non_blocking=True)
+        dx.requires_grad_(False)
+
+    for _ in range(5):
+        e2e_step()
+    e2e_ms = time_steps(e2e_step, steps, world)
+    try:
+        per_step = count_library_kernels(step)
+    except Exception:   # profiler unavailable: leave the count out rather than guess
+        per_step = None
+    return {
+        "metric": "tropical linear fwd+argmax+bwd Gop/s (2*M*N*K forward ops per step)",
+        "value": value, "unit": "Gop/s", "n_gpus": world, "steps": steps,
+        "warmup": max(args.warmup, 10), "ms_per_step": ms / steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: x, W, g ~ N(0,1) (seeded)",
+        "config": {"workload": "tropical linear M=1024 K=256 N=256 fwd + int32 argmax + "
+                               "argmax backward (eval mode), no bias",
+                   "parallelism": f"replicated x{world} (weak)" if world > 1 else "single GPU",
+                   "l2": "inputs 2 MiB, resident in L2 (the problem is smaller than L2)"},
+        "e2e": {"value": ops_step * world / (e2e_ms / steps / 1e3) / 1e9, "unit": "Gop/s",
+                "h2d_bytes_per_step": (hx.numel() + hg.numel()) * 4,
+                "d2h_bytes_per_step": (hy.numel() + hgx.numel()) * 4},
+        "gpu_launches": per_step * steps if per_step is not None else None,
+        "roofline": {"bound": "cuda-core", "achieved": achieved, "peak": peak, "unit": "Top/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "kernel": "max-plus forward with argmax (M=1024, N=K=256): 16 tiles, "
+                               "too small to fill 148 SMs",
+                     "kernel_ms": kms,
+                     "peak_source": "in-repo add+max probe, best form, this run; of measured"},
+        "clocks": clk,
+    }
+
+
+def oracle_linear(hx, hw, hg):
+    from oracle.torch_ref import tropical_linear_fwd_bwd_torch
+
+    y, idx, gx, gw = tropical_linear_fwd_bwd_torch(hx, hw, hg)
+    return y, idx, gx, gw
+
+
+def cpu_linear_rate(target_s: float = 10.0):
+    from oracle.torch_ref import tropical_linear_fwd_bwd_torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(1024, 256, generator=gen)
+    w = torch.randn(256, 256, generator=gen)
+    g = torch.randn(1024, 256, generator=gen)
+    t0 = time.perf_counter()
+    tropical_linear_fwd_bwd_torch(x, w, g)
+    dt = time.perf_counter() - t0
+    reps = int(max(1, min(50, target_s / max(dt, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        tropical_linear_fwd_bwd_torch(x, w, g)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": 2.0 * 1024 * 256 * 256 / dt / 1e9, "unit": "Gop/s", "cores": threads,
+            "kind": "port",
+            "sample": f"the whole config-1 step (reference eval TropicalLinear expression "
+                      f"fwd + autograd bwd, oracle/torch_ref.py), {reps} reps, "
+                      f"{dt * 1e3:.1f} ms each"}
+
+
 def cpu_dtn_rate(target_s: float = 10.0):
     from oracle.torch_ref import DTNAttentionRef
 
@@ -613,7 +748,12 @@ def cpu_dtn_rate(target_s: float = 10.0):
 def reference_arm(args, world, rank):
     if rank != 0:
         return None
-    if args.workload == "dtn":
+    if args.workload == "linear":
+        cb = cpu_linear_rate(target_s=max(3.0, 2.0 * args.steps))
+        metric = "tropical linear fwd+argmax+bwd Gop/s (2*M*N*K forward ops per step)"
+        cfg = {"workload": "tropical linear M=1024 K=256 N=256 fwd + argmax + argmax backward "
+                           "(torch CPU)"}
+    elif args.workload == "dtn":
         cb = cpu_dtn_rate(target_s=max(3.0, 2.0 * args.steps))
         metric = "DTN tropical attention block tokens/s (fwd+bwd, train mode)"
         cfg = {"workload": "DTNAttention d_model=256 heads=8 L=64 fwd+bwd (torch CPU)"}
@@ -645,6 +785,8 @@ def main():
             res = gemm_workload(args, world, rank)
         elif args.workload == "dtn":
             res = dtn_workload(args, world, rank)
+        elif args.workload == "linear":
+            res = linear_workload(args, world, rank)
         else:
             res = scan_workload(args, world, rank)
         if res is not None and args.impl == "ours" and rank == 0 and world == 1 \
@@ -653,6 +795,8 @@ def main():
                 res["cpu_baseline"] = cpu_gemm_rate(args.size)
             elif args.workload == "dtn":
                 res["cpu_baseline"] = cpu_dtn_rate()
+            elif args.workload == "linear":
+                res["cpu_baseline"] = cpu_linear_rate()
             else:
                 res["cpu_baseline"] = cpu_scan_rate(16, 4096, 1024)
         if rank == 0 and res is not None:

@@ -164,7 +164,8 @@ TP_API int tp_maxplus_bwd_argmax_strided(int64_t B1, int64_t B2, int64_t M, int6
                                   float* gbias, float scale, void* stream);
 
 /* Workspace bytes needed by tp_maxplus_bwd_smooth for `batch` (M, N, K)
- * problems: three [M][N] stat planes per batch, plus per-slice partial sums
+ * problems: six [M][N] stat planes per batch (three, and the same three
+ * transposed for the input-gradient pass), plus per-slice partial sums
  * when the gradient outputs are too small to fill the GPU and the reduced
  * index is cut into slices (a function of the shapes only). */
 TP_API int64_t tp_maxplus_bwd_smooth_workspace_bytes(int64_t batch, int64_t M, int64_t N,

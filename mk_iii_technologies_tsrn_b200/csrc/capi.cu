@@ -264,9 +264,11 @@ int tp_maxplus_bwd_smooth(int mode, float tau, int dtype, int64_t batch, int64_t
   if (M * K > 0) TP_CHECK_PTR(gx);
   if (N * K > 0) TP_CHECK_OPT_PTR(gw);
   TP_CHECK_OPT_PTR(gbias);
+  const bool async_stage = dtype == TP_DTYPE_F32 && M % 4 == 0 && N % 4 == 0 && K % 4 == 0 &&
+                           aligned16(x) && aligned16(w);
   SmoothArgs p{mode, tau, dtype, batch, M, N, K, x, w, gy, gx, gw, gbias, (float*)workspace,
-               tp::smooth_splits(batch, M, N, K), tp::smooth_splits(batch, N, M, K),
-               (float*)workspace + 3 * batch * M * N};
+               async_stage, tp::smooth_splits(batch, M, N, K), tp::smooth_splits(batch, N, M, K),
+               (float*)workspace + 6 * batch * M * N};
   return launch_maxplus_bwd_smooth(p, as_stream(stream));
 }
 

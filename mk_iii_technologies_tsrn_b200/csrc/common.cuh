@@ -158,6 +158,22 @@ __device__ __forceinline__ bool tp_mbar_wait(uint64_t* bar, uint32_t parity, int
   return true;
 }
 
+// Asynchronous 16-byte global -> shared copy (L2 only); bytes past
+// src_bytes (0 or 16) are zero-filled and not read.
+__device__ __forceinline__ void tp_cp_async16(void* smem_dst, const void* gsrc, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tp_smem_addr(smem_dst)),
+               "l"(gsrc), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void tp_cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// wait until at most `N` of this thread's committed copy groups are pending
+template <int N>
+__device__ __forceinline__ void tp_cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // 2-D tiled TMA load (no multicast) into shared memory, completing on `bar`.
 __device__ __forceinline__ void tp_tma_load_2d(void* smem_dst, const CUtensorMap* map,
                                                int32_t c0, int32_t c1, uint64_t* bar) {

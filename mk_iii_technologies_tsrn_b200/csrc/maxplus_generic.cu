@@ -466,6 +466,13 @@ __global__ void __launch_bounds__(G_THREADS, 3) smooth_stats_kernel(SmoothArgs p
       wsb[m * p.N + n] = ref;
       wsb[MN + m * p.N + n] = A;
       wsb[2 * MN + m * p.N + n] = Bp;
+      if (p.async_stage) {
+        // transposed planes [N][M] for the input-gradient kernel
+        float* wt = p.ws + 3 * p.batch * MN + bz * 3 * MN;
+        wt[n * p.M + m] = ref;
+        wt[MN + n * p.M + m] = A;
+        wt[2 * MN + n * p.M + m] = Bp;
+      }
     }
   }
 }
@@ -566,6 +573,130 @@ __global__ void __launch_bounds__(G_THREADS, 3) smooth_grad_kernel(SmoothArgs p)
         }
       }
     }
+  }
+  float* out = S > 1 ? p.part + ((int64_t)blockIdx.z) * R * p.K
+                     : (kOut == 0 ? p.gx + bz * p.M * p.K : p.gw + bz * p.N * p.K);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = r0 + 4 * ty + i;
+    if (r >= R) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t k = k0 + 4 * tx + j;
+      const float v = j & 1 ? acc[i][j >> 1].y : acc[i][j >> 1].x;
+      if (k < p.K) out[r * p.K + k] = v;
+    }
+  }
+}
+
+// gx (kOut == 0) or gw (kOut == 1) for fp32 operands with M, N, K multiples of
+// 4: the same arithmetic as smooth_grad_kernel, but each QS-row slab of the
+// other operand and of the stats (read from planes laid out [q][r], r
+// contiguous) is copied with 16-byte cp.async into one of two shared buffers
+// while the previous slab is being consumed.  The other operand is staged
+// unscaled and scaled inside the first packed fma.
+template <int kOut>
+__global__ void __launch_bounds__(G_THREADS, 3) smooth_grad_async_kernel(SmoothArgs p) {
+  constexpr int QS = 16;
+  __shared__ __align__(16) float os[2][QS][GB_N];       // other operand (raw): [q][k]
+  __shared__ __align__(16) float st[2][3][QS][GB_M];    // stats: [plane][q][r]
+  const int tx = threadIdx.x % 16;
+  const int ty = threadIdx.x / 16;
+  const int64_t r0 = (int64_t)blockIdx.y * GB_M;
+  const int64_t k0 = (int64_t)blockIdx.x * GB_N;
+  const int64_t S = kOut == 0 ? p.splits_x : p.splits_w;
+  const int64_t bz = blockIdx.z / S;
+  const int64_t split = blockIdx.z % S;
+  const int64_t MN = p.M * p.N;
+  const float* xb = static_cast<const float*>(p.x) + bz * p.M * p.K;
+  const float* wb = static_cast<const float*>(p.w) + bz * p.N * p.K;
+  const float* mine = kOut == 0 ? xb : wb;
+  const float* other = kOut == 0 ? wb : xb;
+  const int64_t R = kOut == 0 ? p.M : p.N;
+  const int64_t Q = kOut == 0 ? p.N : p.M;
+  // planes [q][r]: gW reads the [M][N] planes, gx the transposed [N][M] ones
+  const float* planes = (kOut == 0 ? p.ws + 3 * p.batch * MN : p.ws) + bz * 3 * MN;
+  const float L = kLog2e / p.tau;
+  const int64_t qchunk = ceil_div(ceil_div(Q, S), (int64_t)QS) * QS;
+  const int64_t qbeg = split * qchunk;
+  const int64_t qend = (qbeg + qchunk < Q) ? qbeg + qchunk : Q;
+
+  float2 own[4][2], acc[4][2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = r0 + 4 * ty + i;
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t k = k0 + 4 * tx + j;
+      v[j] = (r < R && k < p.K) ? __ldg(mine + r * p.K + k) * L : 0.0f;
+    }
+    own[i][0] = make_float2(v[0], v[1]);
+    own[i][1] = make_float2(v[2], v[3]);
+    acc[i][0] = make_float2(0.0f, 0.0f);
+    acc[i][1] = make_float2(0.0f, 0.0f);
+  }
+
+  // slab q0 -> buffer b: QS x 64 operand values (one quad per thread) and
+  // 3 x QS x 64 stats (three quads per thread); out-of-range quads zero-filled
+  auto issue = [&](int b, int64_t q0) {
+    {
+      const int qq = threadIdx.x / 16, kv = threadIdx.x % 16;
+      const int64_t q = q0 + qq, k = k0 + 4 * kv;
+      const bool ok = q < qend && k < p.K;
+      tp_cp_async16(&os[b][qq][4 * kv], ok ? other + q * p.K + k : other, ok ? 16 : 0);
+    }
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const int e = threadIdx.x + c * G_THREADS;
+      const int pl = e / (QS * 16), rem = e % (QS * 16);
+      const int qq = rem / 16, rv = rem % 16;
+      const int64_t q = q0 + qq, r = r0 + 4 * rv;
+      const bool ok = q < qend && r < R;
+      tp_cp_async16(&st[b][pl][qq][4 * rv], ok ? planes + pl * MN + q * R + r : planes,
+                    ok ? 16 : 0);
+    }
+    tp_cp_async_commit();
+  };
+
+  const float2 Lp = make_float2(L, L);
+  int b = 0;
+  if (qbeg < qend) issue(0, qbeg);
+  for (int64_t q0 = qbeg; q0 < qend; q0 += QS, b ^= 1) {
+    if (q0 + QS < qend) {
+      issue(b ^ 1, q0 + QS);
+      tp_cp_async_wait<1>();
+    } else {
+      tp_cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int qmax = (int)((qend - q0) < QS ? (qend - q0) : QS);
+#pragma unroll 2
+    for (int qq = 0; qq < qmax; ++qq) {
+      const float4 o4 = *reinterpret_cast<const float4*>(&os[b][qq][4 * tx]);
+      const float2 ob[2] = {make_float2(o4.x, o4.y), make_float2(o4.z, o4.w)};
+      const float4 rf = *reinterpret_cast<const float4*>(&st[b][0][qq][4 * ty]);
+      const float4 aa = *reinterpret_cast<const float4*>(&st[b][1][qq][4 * ty]);
+      const float4 bb = *reinterpret_cast<const float4*>(&st[b][2][qq][4 * ty]);
+      const float rfv[4] = {rf.x, rf.y, rf.z, rf.w};
+      const float av[4] = {aa.x, aa.y, aa.z, aa.w};
+      const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 nref = make_float2(-rfv[i], -rfv[i]);
+        const float2 A = make_float2(av[i], av[i]);
+        const float2 Bp = make_float2(bv[i], bv[i]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float2 t = tp_add2(tp_fma2(Lp, ob[h], own[i][h]), nref);
+          t.x = tp_max_nan(t.x, kClampL);
+          t.y = tp_max_nan(t.y, kClampL);
+          const float2 e = make_float2(tp_ex2(t.x), tp_ex2(t.y));
+          acc[i][h] = tp_fma2(e, tp_fma2(Bp, t, A), acc[i][h]);
+        }
+      }
+    }
+    __syncthreads();   // buffer b is refilled by the next iteration's issue
   }
   float* out = S > 1 ? p.part + ((int64_t)blockIdx.z) * R * p.K
                      : (kOut == 0 ? p.gx + bz * p.M * p.K : p.gw + bz * p.N * p.K);
@@ -700,7 +831,7 @@ int64_t smooth_workspace_floats(int64_t batch, int64_t M, int64_t N, int64_t K) 
   int64_t part = 0;
   if (sx > 1) part = batch * sx * M * K;
   if (sw > 1 && batch * sw * N * K > part) part = batch * sw * N * K;
-  return 3 * batch * M * N + part;
+  return 6 * batch * M * N + part;
 }
 
 int launch_maxplus_bwd_smooth(const SmoothArgs& p, cudaStream_t stream) {
@@ -731,7 +862,9 @@ int launch_maxplus_bwd_smooth(const SmoothArgs& p, cudaStream_t stream) {
     dim3 gx((unsigned)ceil_div(p.K, GB_N), (unsigned)ceil_div(p.M, GB_M), (unsigned)(nb * sx));
     dim3 gw((unsigned)ceil_div(p.K, GB_N), (unsigned)ceil_div(p.N, GB_M), (unsigned)(nb * sw));
     if (gx.y > 65535u || gw.y > 65535u) return TP_ERR_TOO_LARGE;
-    if (p.dtype == TP_DTYPE_F32)
+    if (p.async_stage)
+      smooth_grad_async_kernel<0><<<gx, G_THREADS, 0, stream>>>(p);
+    else if (p.dtype == TP_DTYPE_F32)
       smooth_grad_kernel<float, 0><<<gx, G_THREADS, 0, stream>>>(p);
     else
       smooth_grad_kernel<uint16_t, 0><<<gx, G_THREADS, 0, stream>>>(p);
@@ -741,7 +874,9 @@ int launch_maxplus_bwd_smooth(const SmoothArgs& p, cudaStream_t stream) {
     s = launch_status();
     if (s != TP_OK) return s;
     if (p.gw) {
-      if (p.dtype == TP_DTYPE_F32)
+      if (p.async_stage)
+        smooth_grad_async_kernel<1><<<gw, G_THREADS, 0, stream>>>(p);
+      else if (p.dtype == TP_DTYPE_F32)
         smooth_grad_kernel<float, 1><<<gw, G_THREADS, 0, stream>>>(p);
       else
         smooth_grad_kernel<uint16_t, 1><<<gw, G_THREADS, 0, stream>>>(p);

@@ -49,7 +49,9 @@ struct SmoothArgs {
   float* gx;
   float* gw;
   float* gbias;
-  float* ws;  // per batch 3 planes of [M][N]: reference max, A, B
+  float* ws;  // per batch 3 planes of [M][N]: reference max, A, B; then, after all
+              // batches, the same planes transposed ([N][M]) when `async_stage`
+  bool async_stage;  // fp32, M, N, K multiples of 4: grad kernels stage with cp.async
   // Splits of the reduced index for gx (over n) and gw (over m); > 1 only when
   // the output tiles alone cannot fill the GPU.  Partial sums then go to
   // `part` ([batch][splits][rows][K], after the stat planes in the workspace)

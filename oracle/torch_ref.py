@@ -82,3 +82,13 @@ class DTNAttentionRef(torch.nn.Module):
         attn = torch.softmax(scores / tau, dim=-1)
         out = torch.matmul(attn, V).transpose(1, 2).contiguous().view(B, L, D)
         return self.o(out), attn
+
+
+def tropical_linear_fwd_bwd_torch(x: torch.Tensor, w: torch.Tensor, g: torch.Tensor):
+    """Eval-mode TropicalLinear forward and backward (tropformer.py:131,141 and the
+    autograd of ``.max(dim=-1).values``): returns (y, argmax, grad_x, grad_w)."""
+    x = x.detach().requires_grad_(True)
+    w = w.detach().requires_grad_(True)
+    mx = (w.unsqueeze(0) + x.unsqueeze(1)).max(dim=-1)
+    gx, gw = torch.autograd.grad(mx.values, (x, w), g)
+    return mx.values.detach(), mx.indices, gx, gw

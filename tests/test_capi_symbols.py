@@ -82,10 +82,11 @@ def test_null_pointer_rejected_without_pointer_checks():
 def test_workspace_size():
     from mk_iii_technologies_tsrn_b200 import _lib
     lib = _lib.load()
-    assert lib.tp_maxplus_bwd_smooth_workspace_bytes(2, 3, 5, 7) == 2 * 3 * 3 * 5 * 4
+    # six [M][N] stat planes per batch (three, and the same three transposed)
+    assert lib.tp_maxplus_bwd_smooth_workspace_bytes(2, 3, 5, 7) == 2 * 6 * 3 * 5 * 4
     assert lib.tp_maxplus_bwd_smooth_workspace_bytes(-1, 3, 5, 7) == 0
     # a projection-shaped problem (M=8192 rows, N=K=256): the 16 weight-gradient
     # tiles are cut into 32 slices of 256 rows, partials [32][256][256]
-    stats = 3 * 8192 * 256
+    stats = 6 * 8192 * 256
     assert lib.tp_maxplus_bwd_smooth_workspace_bytes(1, 8192, 256, 256) == \
         (stats + 32 * 256 * 256) * 4
