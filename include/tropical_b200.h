@@ -189,6 +189,13 @@ TP_API int tp_maxplus_bwd_smooth(int mode, float tau, int dtype,
                                  float* gx, float* gw, float* gbias,
                                  void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Kernel choice for a forward with argmax: problems with M*N*K below this many
+ * terms (default 2^30) run the per-term generic kernel, larger contiguous fp32
+ * ones the TMA kernel, whose deferred argmax search has a fixed cost of about
+ * 0.17 ms per launch.  Both give identical results.  Returns the previous
+ * value; process-wide.  (Tuning; no reference counterpart.) */
+TP_API int64_t tp_set_argmax_tma_min_terms(int64_t terms);
+
 /* ======================================================================== *
  *  Tropical (max-plus) diagonal SSM scan  (research/tsrn_dml.py:917-980)
  *

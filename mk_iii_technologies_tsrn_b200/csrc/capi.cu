@@ -364,6 +364,8 @@ void maxplus_matmul_cuda(const float* A, const float* B, float* C, int M, int K,
   set_last_error(s);
 }
 
+int64_t tp_set_argmax_tma_min_terms(int64_t terms) { return tp::set_argmax_tma_min_terms(terms); }
+
 int tp_last_error(void) { return last_error(); }
 
 int tp_device_error(int reset) {

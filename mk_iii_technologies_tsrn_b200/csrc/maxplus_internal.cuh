@@ -82,6 +82,9 @@ int launch_column_sum(const float* g, int64_t B1, int64_t B2, int64_t M, int64_t
 // maxplus_tma.cu: large contiguous fp32 GEMM.  Returns TP_ERR_UNSUPPORTED
 // when the problem does not meet its layout rules (caller falls back).
 bool maxplus_tma_eligible(const StridedMaxPlus& p);
+// smallest M*N*K for which a forward with argmax takes the TMA kernel
+int64_t argmax_tma_min_terms();
+int64_t set_argmax_tma_min_terms(int64_t terms);
 int launch_maxplus_fwd_tma(const StridedMaxPlus& p, cudaStream_t stream);
 // Same, additionally storing every output into ndst (<= 8) further buffers
 // at column offset col0 (same row strides as y / argmax).

@@ -35,6 +35,8 @@
 //
 // Every mbarrier wait is bounded (common.cuh); a timeout records a device
 // error and the kernel returns.
+#include <atomic>
+
 #include "maxplus_internal.cuh"
 
 namespace tp {
@@ -556,12 +558,27 @@ int launch_cfg(const CUtensorMap& xmap, const CUtensorMap& wmap, const TmaParams
 
 }  // namespace
 
+namespace {
+std::atomic<int64_t> g_argmax_tma_min_terms{(int64_t)1 << 30};
+}  // namespace
+
+int64_t argmax_tma_min_terms() { return g_argmax_tma_min_terms.load(std::memory_order_relaxed); }
+
+int64_t set_argmax_tma_min_terms(int64_t terms) {
+  return g_argmax_tma_min_terms.exchange(terms < 0 ? 0 : terms);
+}
+
 bool maxplus_tma_eligible(const StridedMaxPlus& p) {
   if (p.dtype != TP_DTYPE_F32) return false;
   if (p.B1 * p.B2 != 1) return false;
   if (p.sx_k != 1 || p.sw_k != 1 || p.sy_n != 1) return false;
   if (p.am && p.sa_n != 1) return false;
   if (p.M < BM || p.N < BN || p.K < 2 * BK || p.K > DefaultCfg::MAX_K) return false;
+  // With argmax, each CTA searches its last tile after its main loop; below
+  // about 2^30 terms that fixed cost (~0.17 ms) outweighs the faster main loop
+  // and the per-term generic kernel is quicker (measured: 1024x256x256 0.05 vs
+  // 0.22 ms, 8192x256x256 0.19 vs 0.22 ms; 1024^3 0.38 vs 0.36 ms).
+  if (p.am && p.M * p.N * p.K < argmax_tma_min_terms()) return false;
   if ((p.sx_m % 4) != 0 || (p.sw_n % 4) != 0) return false;
   if (!aligned16(p.x) || !aligned16(p.w)) return false;
   if (p.M > (int64_t)INT32_MAX || p.N > (int64_t)INT32_MAX) return false;

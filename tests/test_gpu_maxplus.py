@@ -14,6 +14,23 @@ def _ops():
     return ops
 
 
+@pytest.fixture(autouse=True, params=["auto", "tma"])
+def argmax_path(request):
+    """Every test runs with the library's default kernel choice and again with the
+    TMA kernel forced for every eligible forward with argmax (its deferred
+    argmax search is otherwise used only above 2^30 terms)."""
+    from mk_iii_technologies_tsrn_b200 import _lib
+    lib = _lib.load()
+    if request.param == "auto":
+        yield request.param
+        return
+    old = lib.tp_set_argmax_tma_min_terms(0)
+    try:
+        yield request.param
+    finally:
+        lib.tp_set_argmax_tma_min_terms(old)
+
+
 def _run(x, w, bias=None, argmax=True, dev="cuda:0", dtype=torch.float32):
     ops = _ops()
     xt = torch.tensor(x, device=dev).to(dtype)
@@ -207,3 +224,23 @@ def test_bf16_widening_exact(cuda):
     assert torch.equal(out.view(torch.int32), src.float().view(torch.int32))
     odd = src[1:]                      # unaligned start: scalar path
     assert torch.equal(ops.widen_bf16(odd).view(torch.int32), odd.float().view(torch.int32))
+
+
+def test_forward_large_sampled(cuda):
+    # above the default TMA threshold (1100*1030*1000 > 2^30 terms), with M, N, K
+    # tails, integer ties, NaN, +inf, an all -inf row and a bias; rows sampled
+    # for the oracle
+    rng = np.random.default_rng(31)
+    M, N, K = 1100, 1030, 1000
+    x = rng.integers(-3, 4, (M, K)).astype(np.float32)
+    w = rng.standard_normal((N, K)).astype(np.float32)
+    w[:, ::7] = np.round(w[:, ::7])
+    x[rng.random((M, K)) < 0.0003] = np.nan
+    x[rng.random((M, K)) < 0.0005] = np.inf
+    x[5, :] = -np.inf
+    bias = rng.standard_normal(N).astype(np.float32)
+    y, am = _run(x, w, bias)
+    rows = np.concatenate([[0, 5, M - 1], rng.choice(M, 61, replace=False)])
+    ry, ri = oracle.maxplus_fwd(x[rows], w, bias)
+    np.testing.assert_array_equal(y[rows], ry)
+    np.testing.assert_array_equal(am[rows], ri)
