@@ -165,6 +165,12 @@ __device__ __forceinline__ void tp_cp_async16(void* smem_dst, const void* gsrc, 
                "l"(gsrc), "r"(src_bytes)
                : "memory");
 }
+// 4-byte variant (through L1); src_bytes 0 zero-fills without reading
+__device__ __forceinline__ void tp_cp_async4(void* smem_dst, const void* gsrc, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(tp_smem_addr(smem_dst)),
+               "l"(gsrc), "r"(src_bytes)
+               : "memory");
+}
 __device__ __forceinline__ void tp_cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }

@@ -477,6 +477,153 @@ __global__ void __launch_bounds__(G_THREADS, 3) smooth_stats_kernel(SmoothArgs p
   }
 }
 
+// Stats pass for fp32 operands: the same results as smooth_stats_kernel, with
+// the [16 k x 64 rows] slabs of x and w copied by 4-byte cp.async into one of
+// two shared buffers while the other is consumed.  Slabs hold raw values (the
+// scale L enters as fma(a + b, L, -refL)); the K tail is cut by the loop bound.
+__global__ void __launch_bounds__(G_THREADS, 3) smooth_stats_async_kernel(SmoothArgs p) {
+  __shared__ __align__(16) float xs[2][GB_K][GB_M + 4];
+  __shared__ __align__(16) float ws[2][GB_K][GB_N + 4];
+  const int tx = threadIdx.x % 16;
+  const int ty = threadIdx.x / 16;
+  const int64_t m0 = (int64_t)blockIdx.y * GB_M;
+  const int64_t n0 = (int64_t)blockIdx.x * GB_N;
+  const int64_t bz = blockIdx.z;
+  const float* xg = static_cast<const float*>(p.x) + bz * p.M * p.K;
+  const float* wg = static_cast<const float*>(p.w) + bz * p.N * p.K;
+  const float* gyb = p.gy + bz * p.M * p.N;
+  float* wsb = p.ws + bz * 3 * p.M * p.N;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  const float L = kLog2e / p.tau;
+  const int nslab = (int)ceil_div(p.K, (int64_t)GB_K);
+
+  // slab `sl` -> buffer b: element (row rr, k kk) of each operand, kk fastest
+  auto issue = [&](int b, int sl) {
+    const int64_t k0 = (int64_t)sl * GB_K;
+#pragma unroll
+    for (int r = 0; r < (GB_M * GB_K) / G_THREADS; ++r) {
+      const int e = threadIdx.x + r * G_THREADS;
+      const int rr = e / GB_K, kk = e % GB_K;
+      const int64_t k = k0 + kk, mr = m0 + rr, nr = n0 + rr;
+      const bool okx = k < p.K && mr < p.M, okw = k < p.K && nr < p.N;
+      tp_cp_async4(&xs[b][kk][rr], okx ? xg + mr * p.K + k : xg, okx ? 4 : 0);
+      tp_cp_async4(&ws[b][kk][rr], okw ? wg + nr * p.K + k : wg, okw ? 4 : 0);
+    }
+    tp_cp_async_commit();
+  };
+  // run `body(buffer, k-count)` over all slabs with the next slab in flight
+  auto sweep = [&](auto&& body) {
+    if (nslab > 0) issue(0, 0);
+    for (int sl = 0; sl < nslab; ++sl) {
+      const int b = sl & 1;
+      if (sl + 1 < nslab) {
+        issue(b ^ 1, sl + 1);
+        tp_cp_async_wait<1>();
+      } else {
+        tp_cp_async_wait<0>();
+      }
+      __syncthreads();
+      const int64_t krem = p.K - (int64_t)sl * GB_K;
+      body(b, krem < GB_K ? (int)krem : GB_K);
+      __syncthreads();
+    }
+  };
+
+  // pass 0: raw max of x + w
+  float mx[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) mx[i][j] = NEG_INF;
+  sweep([&](int b, int kn) {
+    for (int kk = 0; kk < kn; ++kk) {
+      const float4 a4 = lds_f4(&xs[b][kk][4 * ty]);
+      const float4 b4 = lds_f4(&ws[b][kk][4 * tx]);
+      const float a[4] = {a4.x, a4.y, a4.z, a4.w};
+      const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) mx[i][j] = tp_max_nan(mx[i][j], a[i] + bv[j]);
+    }
+  });
+
+  // pass 1: Z and S1 relative to refL = L * max
+  float2 nref[4][2], Z[4][2], S1[4][2];
+  uint32_t finite = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const bool f0 = isfinite(mx[i][2 * h]), f1 = isfinite(mx[i][2 * h + 1]);
+      finite |= (f0 ? 1u : 0u) << (4 * i + 2 * h);
+      finite |= (f1 ? 1u : 0u) << (4 * i + 2 * h + 1);
+      nref[i][h] = make_float2(f0 ? -(mx[i][2 * h] * L) : 0.0f,
+                               f1 ? -(mx[i][2 * h + 1] * L) : 0.0f);
+      Z[i][h] = make_float2(0.0f, 0.0f);
+      S1[i][h] = make_float2(0.0f, 0.0f);
+    }
+  const float2 Lp = make_float2(L, L);
+  sweep([&](int b, int kn) {
+#pragma unroll 4
+    for (int kk = 0; kk < kn; ++kk) {
+      const float4 a4 = lds_f4(&xs[b][kk][4 * ty]);
+      const float4 b4 = lds_f4(&ws[b][kk][4 * tx]);
+      const float a[4] = {a4.x, a4.y, a4.z, a4.w};
+      const float2 bp[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 ap = make_float2(a[i], a[i]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float2 t = tp_fma2(tp_add2(ap, bp[h]), Lp, nref[i][h]);
+          t.x = tp_max_nan(t.x, kClampL);
+          t.y = tp_max_nan(t.y, kClampL);
+          const float2 e = make_float2(tp_ex2(t.x), tp_ex2(t.y));
+          Z[i][h] = tp_add2(Z[i][h], e);
+          S1[i][h] = tp_fma2(e, t, S1[i][h]);
+        }
+      }
+    }
+  });
+
+  const int64_t MN = p.M * p.N;
+  const float inv_log2e = 1.0f / kLog2e;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t m = m0 + 4 * ty + i;
+    if (m >= p.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t n = n0 + 4 * tx + j;
+      if (n >= p.N) continue;
+      const float z = j & 1 ? Z[i][j >> 1].y : Z[i][j >> 1].x;
+      const float s1 = j & 1 ? S1[i][j >> 1].y : S1[i][j >> 1].x;
+      const float g = gyb[m * p.N + n];
+      float A = 0.0f, Bp = 0.0f, ref = 0.0f;
+      if (((finite >> (4 * i + j)) & 1u) && z > 0.0f) {
+        ref = -(j & 1 ? nref[i][j >> 1].y : nref[i][j >> 1].x);
+        const float invZ = 1.0f / z;
+        if (p.mode == TP_BWD_STE) {
+          Bp = g * invZ * inv_log2e;
+          A = g * invZ - Bp * s1 * invZ;
+        } else {
+          A = g * invZ;
+        }
+      }
+      wsb[m * p.N + n] = ref;
+      wsb[MN + m * p.N + n] = A;
+      wsb[2 * MN + m * p.N + n] = Bp;
+      if (p.async_stage) {
+        float* wt = p.ws + 3 * p.batch * MN + bz * 3 * MN;
+        wt[n * p.M + m] = ref;
+        wt[MN + n * p.M + m] = A;
+        wt[2 * MN + n * p.M + m] = Bp;
+      }
+    }
+  }
+}
+
 // gx[m,k] (kOut == 0) or gw[n,k] (kOut == 1).  Tile over (r, k) with r = m or
 // n; loop over this block's slice of the other index q (n or m) in slabs of
 // QS.  The three stat planes are staged interleaved ({refL, A, Bp} per (q, r))
@@ -850,7 +997,9 @@ int launch_maxplus_bwd_smooth(const SmoothArgs& p, cudaStream_t stream) {
   const unsigned nb = (unsigned)p.batch;
   dim3 g1((unsigned)ceil_div(p.N, GB_N), (unsigned)ceil_div(p.M, GB_M), nb);
   if (g1.y > 65535u) return TP_ERR_TOO_LARGE;
-  if (p.dtype == TP_DTYPE_F32)
+  if (p.async_stage)
+    smooth_stats_async_kernel<<<g1, G_THREADS, 0, stream>>>(p);
+  else if (p.dtype == TP_DTYPE_F32)
     smooth_stats_kernel<float><<<g1, G_THREADS, 0, stream>>>(p);
   else
     smooth_stats_kernel<uint16_t><<<g1, G_THREADS, 0, stream>>>(p);
