@@ -55,6 +55,11 @@ extern "C" {
 /* ---- enums ------------------------------------------------------------- */
 #define TP_DTYPE_F32 0   /* operands stored as IEEE fp32                       */
 #define TP_DTYPE_BF16 1  /* operands stored as bf16; arithmetic is exact fp32  */
+#define TP_DTYPE_BF16_ARITH 2  /* bf16 storage AND bf16 arithmetic: every sum
+                                  x + w rounded to bf16 (ties to even) as torch
+                                  does on bf16 tensors; exact max; the max is
+                                  returned in fp32, bias/scale applied in fp32.
+                                  Forward only (tp_maxplus_fwd[_strided]). */
 
 #define TP_BWD_STE 1     /* d/ds of sum(softmax(s/tau)*s): TropicalLinear train mode */
 #define TP_BWD_LSE 2     /* softmax(s/tau): gradient of tau*logsumexp(s/tau) (Maslov) */
@@ -270,8 +275,10 @@ TP_API int tp_convert_bf16_to_f32(int64_t n, const void* src, float* dst, void* 
  *  max-plus term rate.  form 0: FADD + 2-input FMNMX per term;
  *  form 1: packed add.f32x2 + 3-input max per two terms; form 2: form 1 with
  *  NaN-propagating max; form 3: two scalar adds + 3-input NaN max per two
- *  terms; form 4: forms 2 and 3 alternating.  Each of `threads` threads runs `iters` iterations
- *  of 64 terms; the caller times the launch.  sink receives one float per
+ *  terms; form 4: forms 2 and 3 alternating; form 5: packed add.bf16x2 +
+ *  max.bf16x2 per two terms (bf16 arithmetic); form 6: form 5 with the
+ *  NaN-propagating max.  Each of `threads` threads runs `iters` iterations
+ *  of 128 terms; the caller times the launch.  sink receives one float per
  *  thread (keeps the work live).
  * ======================================================================== */
 TP_API int tp_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters,

@@ -81,7 +81,9 @@ using namespace tp;
 static inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 static int validate_strided(const StridedMaxPlus& p) {
-  TP_RETURN_IF(p.dtype != TP_DTYPE_F32 && p.dtype != TP_DTYPE_BF16, TP_ERR_UNSUPPORTED);
+  TP_RETURN_IF(p.dtype != TP_DTYPE_F32 && p.dtype != TP_DTYPE_BF16 &&
+                   p.dtype != TP_DTYPE_BF16_ARITH,
+               TP_ERR_UNSUPPORTED);
   TP_RETURN_IF(p.B1 < 0 || p.B2 < 0 || p.M < 0 || p.N < 0 || p.K < 0, TP_ERR_INVALID_ARG);
   TP_RETURN_IF(p.K > (int64_t)INT32_MAX, TP_ERR_TOO_LARGE);  // int32 argmax
   TP_RETURN_IF(!(p.tau > 0.0f), TP_ERR_INVALID_ARG);
@@ -200,6 +202,7 @@ int tp_maxplus_lse_fwd_strided(int dtype, float tau, int64_t B1, int64_t B2, int
   StridedMaxPlus p{dtype, B1, B2,  M,    N,    K,     x,     sx_b1, sx_b2, sx_m,    sx_k,
                    w,     sw_b1, sw_b2, sw_n, sw_k, bias,  y,     sy_b1, sy_b2, sy_m,  sy_n,
                    nullptr, 0,   0,     0,    0,    scale, tau};
+  TP_RETURN_IF(dtype == TP_DTYPE_BF16_ARITH, TP_ERR_UNSUPPORTED);
   int s = validate_strided(p);
   if (s != TP_OK) return s;
   if (B1 * B2 * M * N == 0) return TP_OK;
@@ -329,7 +332,7 @@ int tp_convert_bf16_to_f32(int64_t n, const void* src, float* dst, void* stream)
 
 int tp_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters, float* sink,
                     void* stream) {
-  TP_RETURN_IF(form < 0 || form > 4 || blocks <= 0 || blocks > 65535 || iters < 0,
+  TP_RETURN_IF(form < 0 || form > 6 || blocks <= 0 || blocks > 65535 || iters < 0,
                TP_ERR_INVALID_ARG);
   TP_CHECK_PTR(sink);
   return launch_probe_addmax(form, blocks, threads, iters, sink, as_stream(stream));

@@ -61,7 +61,9 @@ __device__ __forceinline__ void load_slab(float (*dst)[GB_M + 4], const T* base,
 // ---------------------------------------------------------------------------
 // forward (hard max, optional argmax)
 // ---------------------------------------------------------------------------
-template <typename T, bool kArgmax>
+// kBf16Sum: every sum is rounded to bf16 (ties to even) before the max, the
+// arithmetic torch applies to bf16 tensors (TP_DTYPE_BF16_ARITH).
+template <typename T, bool kArgmax, bool kBf16Sum = false>
 __global__ void __launch_bounds__(G_THREADS)
     maxplus_fwd_generic_kernel(StridedMaxPlus p) {
   __shared__ float xs[GB_K][GB_M + 4];
@@ -108,6 +110,7 @@ __global__ void __launch_bounds__(G_THREADS)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             float s = a[i] + b[j];
+            if (kBf16Sum) s = __bfloat162float(__float2bfloat16_rn(s));
             if (kArgmax) {
               bool upd = (s > acc[i][j]) | ((s != s) & (acc[i][j] == acc[i][j]));
               acc[i][j] = upd ? s : acc[i][j];
@@ -898,11 +901,16 @@ int launch_maxplus_fwd_generic(const StridedMaxPlus& p, cudaStream_t stream) {
       maxplus_fwd_generic_kernel<float, true><<<grid, G_THREADS, 0, stream>>>(p);
     else
       maxplus_fwd_generic_kernel<float, false><<<grid, G_THREADS, 0, stream>>>(p);
-  } else {
+  } else if (p.dtype == TP_DTYPE_BF16) {
     if (am)
       maxplus_fwd_generic_kernel<uint16_t, true><<<grid, G_THREADS, 0, stream>>>(p);
     else
       maxplus_fwd_generic_kernel<uint16_t, false><<<grid, G_THREADS, 0, stream>>>(p);
+  } else {
+    if (am)
+      maxplus_fwd_generic_kernel<uint16_t, true, true><<<grid, G_THREADS, 0, stream>>>(p);
+    else
+      maxplus_fwd_generic_kernel<uint16_t, false, true><<<grid, G_THREADS, 0, stream>>>(p);
   }
   return launch_status();
 }

@@ -529,6 +529,406 @@ __global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
   }
 }
 
+// ===========================================================================
+// Packed bf16x2 kernel (TP_DTYPE_BF16_ARITH): the reference expression on bf16
+// tensors, where every sum x + w is rounded to bf16.  Same CTA structure as the
+// fp32 kernel; a k-tile is 128 x 64 bf16 (128-byte rows).  Each accumulator
+// register holds two bf16 lanes: the running max over the even and over the
+// odd k of one output.  Per two terms: one add.rn.bf16x2 (both sums rounded to
+// bf16, ties to even -- the rounding torch applies) and one max.NaN.bf16x2.
+// Chunk tracking compares the max of the two lanes (16-bit snapshot); the
+// deferred argmax search tests 32-k units (packed adds and a max tree) and
+// compares in fp32 (bf16 values widen exactly).
+// ===========================================================================
+constexpr int BK16 = 64;                         // bf16 per TMA row (128 bytes)
+constexpr int CHUNK16 = 128;                     // argmax chunk: two k-tiles
+constexpr int KT_PER_CHUNK16 = CHUNK16 / BK16;
+constexpr int SNAP16_BYTES = BM * BN * 2;        // 16-bit combined maxima
+constexpr uint32_t BF2_NEG_INF = 0xff80ff80u;
+constexpr int64_t MAX_K16 = (int64_t)CHUNK16 * 65535;
+
+template <bool kArgmax>
+constexpr int smem_bytes16() {
+  return stages<kArgmax>() * STAGE_BYTES + (kArgmax ? SNAP16_BYTES + CIDX_BYTES : 0) + 128 + 1024;
+}
+
+__device__ __forceinline__ uint32_t bf2_add(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf2_max(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+// max.NaN of the two lanes, as a bf16 bit pattern
+__device__ __forceinline__ uint32_t bf2_lanes_max(uint32_t a) {
+  uint16_t r;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %1;\n\tmax.NaN.bf16 %0, lo, hi;\n\t}"
+      : "=h"(r)
+      : "r"(a));
+  return (uint32_t)r;
+}
+__device__ __forceinline__ float bf_bits_to_f32(uint32_t b16) { return __uint_as_float(b16 << 16); }
+
+__device__ __forceinline__ uint4 lds128u4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+// lanes of a bf16x2 word at k (lo) and k+1 (hi): those at or past K become -inf
+__device__ __forceinline__ uint32_t bf2_mask(uint32_t v, int64_t k, int64_t K) {
+  if (k >= K) v = (v & 0xffff0000u) | 0xff80u;
+  if (k + 1 >= K) v = (v & 0x0000ffffu) | 0xff800000u;
+  return v;
+}
+
+// 32 bf16 terms of one output: x and w row chunks (8 words each) at k
+struct Unit16 {
+  uint4 a[4], b[4];
+};
+
+__device__ __forceinline__ void load_unit16(const uint16_t* xr, const uint16_t* wr, int k, int K,
+                                            Unit16& u) {
+  if (k + 32 <= K) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      u.a[c] = __ldg(reinterpret_cast<const uint4*>(xr) + c);
+      u.b[c] = __ldg(reinterpret_cast<const uint4*>(wr) + c);
+    }
+  } else {
+    uint32_t aw[16], bw[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int k0 = k + 2 * e;
+      const uint32_t xl = k0 < K ? __ldg(xr + 2 * e) : 0xff80u;
+      const uint32_t xh = k0 + 1 < K ? __ldg(xr + 2 * e + 1) : 0xff80u;
+      const uint32_t wl = k0 < K ? __ldg(wr + 2 * e) : 0u;
+      const uint32_t wh = k0 + 1 < K ? __ldg(wr + 2 * e + 1) : 0u;
+      aw[e] = xl | (xh << 16);
+      bw[e] = wl | (wh << 16);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      u.a[c] = make_uint4(aw[4 * c], aw[4 * c + 1], aw[4 * c + 2], aw[4 * c + 3]);
+      u.b[c] = make_uint4(bw[4 * c], bw[4 * c + 1], bw[4 * c + 2], bw[4 * c + 3]);
+    }
+  }
+}
+
+// first k of the unit whose bf16 sum equals tv (NaN: is NaN), or kBestNone
+__device__ __forceinline__ int unit_first_hit16(float tv, int k, int K, const Unit16& u) {
+  uint32_t s[16];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    s[4 * c + 0] = bf2_add(u.a[c].x, u.b[c].x);
+    s[4 * c + 1] = bf2_add(u.a[c].y, u.b[c].y);
+    s[4 * c + 2] = bf2_add(u.a[c].z, u.b[c].z);
+    s[4 * c + 3] = bf2_add(u.a[c].w, u.b[c].w);
+  }
+  uint32_t m = s[0];
+#pragma unroll
+  for (int e = 1; e < 16; ++e) m = bf2_max(m, s[e]);
+  const float mx = bf_bits_to_f32(bf2_lanes_max(m));
+  const bool tnan = tv != tv;
+  int best = kBestNone;
+  if (tnan ? (mx != mx) : (mx == tv)) {
+#pragma unroll
+    for (int e = 31; e >= 0; --e) {
+      const uint32_t w = s[e >> 1];
+      const float se = bf_bits_to_f32((e & 1) ? (w >> 16) : (w & 0xffffu));
+      const bool hit = (k + e < K) && (tnan ? (se != se) : (se == tv));
+      if (hit) best = k + e;
+    }
+  }
+  return best;
+}
+
+template <class C, bool kArgmax>
+__global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
+    maxplus_tma_bf16_kernel(const __grid_constant__ CUtensorMap xmap,
+                            const __grid_constant__ CUtensorMap wmap, const TmaParams p) {
+  constexpr int TM = C::TM, TN = C::TN, TX = C::TX, TY = C::TY, CT = C::CT;
+  constexpr int OUTS = TM * TN;
+  static_assert(OUTS % 8 == 0, "16-bit snapshots are moved eight at a time");
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem =
+      (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  constexpr int STAGES = stages<kArgmax>();
+  unsigned char* stage_base = smem;
+  uint4* snap = (uint4*)(smem + STAGES * STAGE_BYTES);                      // [OUTS/8][CT]
+  uint16_t* cid = (uint16_t*)(smem + STAGES * STAGE_BYTES + SNAP16_BYTES);  // [OUTS][CT]
+  uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES +
+                               (kArgmax ? SNAP16_BYTES + CIDX_BYTES : 0));
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tp_mbar_init(&full[s], 1);
+      tp_mbar_init(&empty[s], C::CW);
+    }
+    tp_fence_mbar_init();
+  }
+  __syncthreads();
+
+  const uint32_t my_tiles = (uint32_t)((p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) /
+                                       (int)gridDim.x);
+  const uint32_t total_kt = my_tiles * (uint32_t)p.k_tiles;
+  auto produce = [&](uint32_t j) -> bool {
+    const int tile = (int)blockIdx.x + (int)(j / (uint32_t)p.k_tiles) * (int)gridDim.x;
+    const int kt = (int)(j % (uint32_t)p.k_tiles);
+    int mt, nt;
+    tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+    const uint32_t s = j % STAGES;
+    const uint32_t ph = (j / STAGES) & 1u;
+    if (!tp_mbar_wait(&empty[s], ph ^ 1u, p.err)) return false;
+    unsigned char* dst = stage_base + s * STAGE_BYTES;
+    tp_mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+    tp_tma_load_2d(dst, &xmap, kt * BK16, mt * BM, &full[s]);
+    tp_tma_load_2d(dst + TILE_BYTES, &wmap, kt * BK16, nt * BN, &full[s]);
+    return true;
+  };
+
+  if constexpr (!kArgmax) {
+    if (warp == C::PRODUCER_WARP) {
+      if (lane == 0) {
+        tp_prefetch_tensormap(&xmap);
+        tp_prefetch_tensormap(&wmap);
+        for (uint32_t j = 0; j < total_kt; ++j)
+          if (!produce(j)) return;
+      }
+      return;
+    }
+  } else {
+    if (threadIdx.x == 0) {
+      tp_prefetch_tensormap(&xmap);
+      tp_prefetch_tensormap(&wmap);
+      for (uint32_t j = 0; j < STAGES - 1 && j < total_kt; ++j)
+        if (!produce(j)) return;
+    }
+  }
+
+  // -------------------------------------------------------------- compute
+  const int t = threadIdx.x;
+  const int tx = t % TX;
+  const int ty = t / TX;
+  const uint32_t stage_addr = tp_smem_addr(stage_base);
+  const uint32_t xsw = (uint32_t)(ty & 7);
+  const uint32_t wsw = (uint32_t)(tx & 7);
+  const uint16_t* xg = reinterpret_cast<const uint16_t*>(p.x);
+  const uint16_t* wg = reinterpret_cast<const uint16_t*>(p.w);
+
+  // deferred argmax search (as in the fp32 kernel), 32-k units
+  constexpr int UPO = CHUNK16 / 32;
+  constexpr int UNITS = OUTS * UPO;
+  const int Kc = (int)p.K;
+  const int Mc = (int)p.M, Nc = (int)p.N;
+  int s_u = UNITS + 1;
+  int s_m0 = 0, s_n0 = 0;
+  float s_tv = 0.0f, s_ntv = 0.0f;
+  int s_kc = 0, s_nkc = 0;
+  int s_best = kBestNone;
+  const uint16_t* s_xp = nullptr;
+  const uint16_t* s_wp = nullptr;
+  Unit16 su;
+  const int steps = kArgmax ? (UNITS + p.k_tiles - 1) / p.k_tiles : 0;
+
+  auto prefetch = [&](int o) {
+    const int m = s_m0 + ty + TY * (o / TN), n = s_n0 + tx + TX * (o % TN);
+    if (o < OUTS && m < Mc && n < Nc) {
+      s_ntv = p.y[(int64_t)m * p.ldy + n];
+      s_nkc = p.am[(int64_t)m * p.lda + n] * CHUNK16;
+    }
+  };
+  auto step = [&]() {
+    if (s_u >= 1 && s_u <= UNITS) {
+      const int pu = s_u - 1;
+      if (s_xp != nullptr) {
+        if (s_best == kBestNone) s_best = unit_first_hit16(s_tv, s_kc + 32 * (pu % UPO), Kc, su);
+        if (pu % UPO == UPO - 1) {
+          const int o = pu / UPO;
+          store_output(p, s_m0 + ty + TY * (o / TN), s_n0 + tx + TX * (o % TN), s_tv,
+                       s_best != kBestNone ? s_best : s_kc);
+        }
+      }
+    }
+    if (s_u < UNITS) {
+      if (s_u % UPO == 0) {
+        const int o = s_u / UPO;
+        const int m = s_m0 + ty + TY * (o / TN), n = s_n0 + tx + TX * (o % TN);
+        s_tv = s_ntv;
+        s_kc = s_nkc;
+        s_best = kBestNone;
+        if (m < Mc && n < Nc) {
+          s_xp = xg + (int64_t)m * p.ldx + s_kc;
+          s_wp = wg + (int64_t)n * p.ldw + s_kc;
+        } else {
+          s_xp = s_wp = nullptr;
+        }
+        prefetch(o + 1);
+      }
+      if (s_xp != nullptr) {
+        load_unit16(s_xp, s_wp, s_kc + 32 * (s_u % UPO), Kc, su);
+        s_xp += 32;
+        s_wp += 32;
+      }
+    }
+    if (s_u <= UNITS) ++s_u;
+  };
+
+  uint32_t it = 0;
+  for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    int mt, nt;
+    tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+    const int64_t m0 = (int64_t)mt * BM, n0 = (int64_t)nt * BN;
+    uint32_t acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+      for (int j = 0; j < TN; ++j) acc[i][j] = BF2_NEG_INF;
+    if (kArgmax) {
+#pragma unroll
+      for (int q = 0; q < OUTS / 8; ++q)
+        snap[q * CT + t] = make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+#pragma unroll
+      for (int o = 0; o < OUTS; ++o) cid[o * CT + t] = 0;
+    }
+
+    for (int kt = 0; kt < p.k_tiles; ++kt, ++it) {
+      const uint32_t s = it % STAGES;
+      const uint32_t ph = (it / STAGES) & 1u;
+      if (kArgmax && threadIdx.x == 0 && it + STAGES - 1 < total_kt)
+        if (!produce(it + STAGES - 1)) return;
+      if (!tp_mbar_wait(&full[s], ph, p.err)) return;
+      if (kArgmax)
+        for (int r = 0; r < steps; ++r) step();
+      const uint32_t xbase = stage_addr + s * STAGE_BYTES;
+      const uint32_t wbase = xbase + TILE_BYTES;
+      const int64_t k0 = (int64_t)kt * BK16;
+      const bool tail = k0 + BK16 > p.K;
+#pragma unroll 4
+      for (int q = 0; q < 8; ++q) {
+        uint32_t xw[TM][4];
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+          const uint4 v =
+              lds128u4(xbase + (uint32_t)(ty + TY * i) * 128u + (((uint32_t)q ^ xsw) << 4));
+          xw[i][0] = v.x;
+          xw[i][1] = v.y;
+          xw[i][2] = v.z;
+          xw[i][3] = v.w;
+        }
+        if (tail) {
+          const int64_t kq = k0 + 8 * q;
+#pragma unroll
+          for (int i = 0; i < TM; ++i)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) xw[i][c] = bf2_mask(xw[i][c], kq + 2 * c, p.K);
+        }
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+          const uint4 wv =
+              lds128u4(wbase + (uint32_t)(tx + TX * j) * 128u + (((uint32_t)q ^ wsw) << 4));
+#pragma unroll
+          for (int i = 0; i < TM; ++i) {
+            acc[i][j] = bf2_max(acc[i][j], bf2_add(xw[i][0], wv.x));
+            acc[i][j] = bf2_max(acc[i][j], bf2_add(xw[i][1], wv.y));
+            acc[i][j] = bf2_max(acc[i][j], bf2_add(xw[i][2], wv.z));
+            acc[i][j] = bf2_max(acc[i][j], bf2_add(xw[i][3], wv.w));
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) tp_mbar_arrive(&empty[s]);
+
+      if (kArgmax && (((kt + 1) % KT_PER_CHUNK16) == 0 || kt == p.k_tiles - 1)) {
+        const uint16_t chunk = (uint16_t)(kt / KT_PER_CHUNK16);
+#pragma unroll
+        for (int q = 0; q < OUTS / 8; ++q) {
+          const uint4 sv = snap[q * CT + t];
+          const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+          uint32_t nw[4];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const int o0 = 8 * q + 2 * h, o1 = o0 + 1;
+            const uint32_t m0v = bf2_lanes_max(acc[o0 / TN][o0 % TN]);
+            const uint32_t m1v = bf2_lanes_max(acc[o1 / TN][o1 % TN]);
+            if (m0v != (sw[h] & 0xffffu)) cid[o0 * CT + t] = chunk;
+            if (m1v != (sw[h] >> 16)) cid[o1 * CT + t] = chunk;
+            nw[h] = m0v | (m1v << 16);
+          }
+          snap[q * CT + t] = make_uint4(nw[0], nw[1], nw[2], nw[3]);
+        }
+      }
+    }
+
+    if constexpr (!kArgmax) {
+#pragma unroll
+      for (int i = 0; i < TM; ++i) {
+        const int64_t m = m0 + ty + TY * i;
+        if (m >= p.M) continue;
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+          const int64_t n = n0 + tx + TX * j;
+          if (n >= p.N) continue;
+          float v = bf_bits_to_f32(bf2_lanes_max(acc[i][j]));
+          if (p.bias) v = v + p.bias[n];
+          if (p.scale != 1.0f) v = v * p.scale;
+          p.y[m * p.ldy + n] = v;
+          for (int d = 0; d < p.ndst; ++d) p.ydst[d][m * p.ldy + p.col0 + n] = v;
+        }
+      }
+    } else {
+      while (s_u <= UNITS) step();
+#pragma unroll
+      for (int i = 0; i < TM; ++i) {
+        const int64_t m = m0 + ty + TY * i;
+        if (m >= p.M) continue;
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+          const int64_t n = n0 + tx + TX * j;
+          if (n >= p.N) continue;
+          p.y[m * p.ldy + n] = bf_bits_to_f32(bf2_lanes_max(acc[i][j]));
+          p.am[m * p.lda + n] = (int32_t)cid[(i * TN + j) * CT + t];
+        }
+      }
+      s_m0 = (int)m0;
+      s_n0 = (int)n0;
+      s_u = 0;
+      prefetch(0);
+    }
+  }
+
+  if (s_u == 0) {
+    // drain: the CTA's last tile, two units in flight at a time
+    for (int o = 0; o < OUTS; ++o) {
+      const int m = s_m0 + ty + TY * (o / TN), n = s_n0 + tx + TX * (o % TN);
+      if (m >= Mc || n >= Nc) continue;
+      const float tv = p.y[(int64_t)m * p.ldy + n];
+      const int kc = p.am[(int64_t)m * p.lda + n] * CHUNK16;
+      const uint16_t* xr = xg + (int64_t)m * p.ldx + kc;
+      const uint16_t* wr = wg + (int64_t)n * p.ldw + kc;
+      int best = kBestNone;
+      for (int j0 = 0; j0 < UPO && best == kBestNone; j0 += 2) {
+        Unit16 d0, d1;
+        load_unit16(xr + 32 * j0, wr + 32 * j0, kc + 32 * j0, Kc, d0);
+        if (j0 + 1 < UPO) load_unit16(xr + 32 * (j0 + 1), wr + 32 * (j0 + 1), kc + 32 * (j0 + 1), Kc, d1);
+        best = unit_first_hit16(tv, kc + 32 * j0, Kc, d0);
+        if (best == kBestNone && j0 + 1 < UPO)
+          best = unit_first_hit16(tv, kc + 32 * (j0 + 1), Kc, d1);
+      }
+      store_output(p, m, n, tv, best != kBestNone ? best : kc);
+    }
+  }
+}
+
 bool make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t K, int64_t ld) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return false;
@@ -540,6 +940,33 @@ bool make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t K, int6
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+bool make_map16(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int64_t ld) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {BK16, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <class C, bool kArgmax>
+int launch_cfg16(const CUtensorMap& xmap, const CUtensorMap& wmap, const TmaParams& tp_,
+                 cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(maxplus_tma_bf16_kernel<C, kArgmax>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       smem_bytes16<kArgmax>());
+  if (e != cudaSuccess) return (int)e;
+  int grid = num_sms();
+  if (grid > tp_.num_tiles) grid = tp_.num_tiles;
+  maxplus_tma_bf16_kernel<C, kArgmax>
+      <<<grid, C::template threads<kArgmax>(), smem_bytes16<kArgmax>(), stream>>>(xmap, wmap, tp_);
+  return launch_status();
 }
 
 template <class C, bool kArgmax>
@@ -569,6 +996,19 @@ int64_t set_argmax_tma_min_terms(int64_t terms) {
 }
 
 bool maxplus_tma_eligible(const StridedMaxPlus& p) {
+  if (p.dtype == TP_DTYPE_BF16_ARITH) {
+    // packed bf16x2 kernel: 16-byte aligned bf16 rows
+    if (p.B1 * p.B2 != 1) return false;
+    if (p.sx_k != 1 || p.sw_k != 1 || p.sy_n != 1) return false;
+    if (p.am && p.sa_n != 1) return false;
+    if (p.M < BM || p.N < BN || p.K < 2 * BK16 || p.K > MAX_K16) return false;
+    if (p.am && p.M * p.N * p.K < argmax_tma_min_terms()) return false;
+    if ((p.sx_m % 8) != 0 || (p.sw_n % 8) != 0) return false;
+    if (!aligned16(p.x) || !aligned16(p.w)) return false;
+    if (p.M > (int64_t)INT32_MAX || p.N > (int64_t)INT32_MAX) return false;
+    const int64_t tiles = ceil_div(p.M, BM) * ceil_div(p.N, BN);
+    return tiles >= 16 && tiles < (int64_t)INT32_MAX;
+  }
   if (p.dtype != TP_DTYPE_F32) return false;
   if (p.B1 * p.B2 != 1) return false;
   if (p.sx_k != 1 || p.sw_k != 1 || p.sy_n != 1) return false;
@@ -595,9 +1035,15 @@ int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
                                  cudaStream_t stream) {
   if (!maxplus_tma_eligible(p)) return TP_ERR_UNSUPPORTED;
   if (ndst < 0 || ndst > MAX_DESTS) return TP_ERR_TOO_LARGE;
+  const bool bf16 = p.dtype == TP_DTYPE_BF16_ARITH;
   CUtensorMap xmap, wmap;
-  if (!make_map(&xmap, (const float*)p.x, p.M, p.K, p.sx_m)) return TP_ERR_UNSUPPORTED;
-  if (!make_map(&wmap, (const float*)p.w, p.N, p.K, p.sw_n)) return TP_ERR_UNSUPPORTED;
+  if (bf16) {
+    if (!make_map16(&xmap, p.x, p.M, p.K, p.sx_m)) return TP_ERR_UNSUPPORTED;
+    if (!make_map16(&wmap, p.w, p.N, p.K, p.sw_n)) return TP_ERR_UNSUPPORTED;
+  } else {
+    if (!make_map(&xmap, (const float*)p.x, p.M, p.K, p.sx_m)) return TP_ERR_UNSUPPORTED;
+    if (!make_map(&wmap, (const float*)p.w, p.N, p.K, p.sw_n)) return TP_ERR_UNSUPPORTED;
+  }
   TmaParams tp_;
   tp_.M = p.M;
   tp_.N = p.N;
@@ -614,7 +1060,7 @@ int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
   tp_.scale = p.scale;
   tp_.m_tiles = (int)ceil_div(p.M, BM);
   tp_.n_tiles = (int)ceil_div(p.N, BN);
-  tp_.k_tiles = (int)ceil_div(p.K, BK);
+  tp_.k_tiles = (int)ceil_div(p.K, bf16 ? BK16 : BK);
   tp_.num_tiles = tp_.m_tiles * tp_.n_tiles;
   tp_.err = device_error_ptr();
   tp_.ndst = ndst;
@@ -622,6 +1068,10 @@ int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
   for (int d = 0; d < MAX_DESTS; ++d) {
     tp_.ydst[d] = d < ndst ? ydst[d] : nullptr;
     tp_.adst[d] = (d < ndst && adst) ? adst[d] : nullptr;
+  }
+  if (bf16) {
+    if (p.am) return launch_cfg16<DefaultCfg, true>(xmap, wmap, tp_, stream);
+    return launch_cfg16<DefaultCfg, false>(xmap, wmap, tp_, stream);
   }
   if (p.am) return launch_cfg<DefaultCfg, true>(xmap, wmap, tp_, stream);
   return launch_cfg<DefaultCfg, false>(xmap, wmap, tp_, stream);

@@ -13,6 +13,9 @@
 //   form 2: add.rn.f32x2 + 3-input max.NaN.f32
 //   form 3: two add.rn.f32 + 3-input max.NaN.f32 per two terms (3 instructions)
 //   form 4: forms 2 and 3 alternating over the outputs
+//   form 5: add.rn.bf16x2 + 2-input max.bf16x2 per two terms (packed bf16
+//           arithmetic; there is no 3-input packed max)
+//   form 6: add.rn.bf16x2 + max.NaN.bf16x2
 #include "maxplus_internal.cuh"
 
 namespace tp {
@@ -95,6 +98,49 @@ __global__ void __launch_bounds__(256) probe_kernel(int64_t iters, float* sink) 
   sink[t] = r;
 }
 
+// bf16x2 forms: each register holds two bf16 lanes; per pair of terms one
+// packed add and one packed max into a two-lane accumulator
+template <bool kNaN>
+__global__ void __launch_bounds__(256) probe_bf16_kernel(int64_t iters, float* sink) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  uint32_t xa[8], wb[8], acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float f0 = (float)(t % 97) * 0.01f + (float)i;
+    const float f1 = (float)(t % 89) * 0.02f - (float)i;
+    xa[i] = (__float_as_uint(f1) & 0xffff0000u) | (__float_as_uint(f0) >> 16);
+    wb[i] = (__float_as_uint(f0 * 0.5f) & 0xffff0000u) | (__float_as_uint(f1 * 0.25f) >> 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0xff80ff80u;   // two -inf lanes
+  const uint32_t step = (__float_as_uint(1.0e-2f) & 0xffff0000u) | (__float_as_uint(-1.0e-2f) >> 16);
+  for (int64_t it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) asm volatile("add.rn.bf16x2 %0, %0, %1;" : "+r"(xa[i]) : "r"(step));
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (kNaN)
+          asm volatile("{\n\t.reg .b32 s;\n\tadd.rn.bf16x2 s, %1, %2;\n\t"
+                       "max.NaN.bf16x2 %0, %0, s;\n\t}"
+                       : "+r"(acc[i][j]) : "r"(xa[i]), "r"(wb[j]));
+        else
+          asm volatile("{\n\t.reg .b32 s;\n\tadd.rn.bf16x2 s, %1, %2;\n\t"
+                       "max.bf16x2 %0, %0, s;\n\t}"
+                       : "+r"(acc[i][j]) : "r"(xa[i]), "r"(wb[j]));
+      }
+  }
+  float r = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r += __uint_as_float(acc[i][j] << 16) + __uint_as_float(acc[i][j] & 0xffff0000u);
+  sink[t] = r;
+}
+
 }  // namespace
 
 int launch_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters, float* sink,
@@ -108,8 +154,12 @@ int launch_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters
     probe_kernel<2><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
   else if (form == 3)
     probe_kernel<3><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
-  else
+  else if (form == 4)
     probe_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
+  else if (form == 5)
+    probe_bf16_kernel<false><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
+  else
+    probe_bf16_kernel<true><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
   return launch_status();
 }
 

@@ -25,7 +25,7 @@ from typing import Optional, Tuple
 import torch
 
 from . import _lib
-from ._lib import TP_BWD_LSE, TP_BWD_STE, TP_DTYPE_BF16, TP_DTYPE_F32
+from ._lib import TP_BWD_LSE, TP_BWD_STE, TP_DTYPE_BF16, TP_DTYPE_BF16_ARITH, TP_DTYPE_F32
 
 MODES = ("argmax", "ste", "lse")
 
@@ -107,18 +107,29 @@ def _widen_pays(x: torch.Tensor, w: torch.Tensor) -> bool:
 def maxplus_strided(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
                     *, argmax: bool = True, scale: float = 1.0,
                     out: Optional[torch.Tensor] = None,
-                    out_argmax: Optional[torch.Tensor] = None):
+                    out_argmax: Optional[torch.Tensor] = None, arith: str = "f32"):
     """Batched max-plus product on strided views.
 
     ``x``: [..., M, K], ``w``: [..., N, K] (same 0-2 leading batch dims, any
     strides); returns ``y`` [..., M, N] fp32 and ``argmax`` [..., M, N] int32
     (or None).  ``y = (max_k(x + w) [+ bias]) * scale``.
+
+    ``arith``: "f32" adds in fp32 (bf16 operands are widened exactly);
+    "bf16" (bf16 operands only) rounds every sum to bf16 as torch does on bf16
+    tensors -- the reference expression evaluated in bf16 -- and runs the
+    packed bf16x2 kernel on large problems.
     """
     dev = _require_cuda(x, w, bias)
     if x.dtype != w.dtype:
         raise TypeError(f"x and w must share a dtype, got {x.dtype} and {w.dtype}")
+    if arith not in ("f32", "bf16"):
+        raise ValueError(f"arith must be 'f32' or 'bf16', got {arith!r}")
     code = _dtype_code(x)
-    if code == TP_DTYPE_BF16 and _widen_pays(x, w):
+    if arith == "bf16":
+        if code != TP_DTYPE_BF16:
+            raise TypeError("arith='bf16' needs bf16 operands")
+        code = TP_DTYPE_BF16_ARITH
+    elif code == TP_DTYPE_BF16 and _widen_pays(x, w):
         # large bf16 problems: widen exactly to fp32 scratch, run the fp32 TMA kernel
         x, w = widen_bf16(x), widen_bf16(w)
         code = TP_DTYPE_F32
@@ -160,11 +171,11 @@ def maxplus_strided(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tenso
 
 
 def maxplus(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
-            *, argmax: bool = True):
+            *, argmax: bool = True, arith: str = "f32"):
     """``y[m,n] = max_k(x[m,k] + w[n,k]) (+ bias[n])`` and the lowest argmax k (int32)."""
     if x.dim() != 2 or w.dim() != 2:
         raise ValueError("maxplus takes x [M,K] and w [N,K]")
-    return maxplus_strided(x, w, bias, argmax=argmax)
+    return maxplus_strided(x, w, bias, argmax=argmax, arith=arith)
 
 
 def tropical_scores(Q: torch.Tensor, K: torch.Tensor, scale: float = 1.0, *, argmax: bool = True):

@@ -16,6 +16,8 @@ reference's hand-computed known-answer test (``cuda/test_kernel.py:117-136``).
 """
 from .maxplus import (  # noqa: F401
     maxplus_fwd,
+    maxplus_fwd_bf16,
+    round_bf16,
     maxplus_bwd_argmax,
     maxplus_bwd_smooth,
     maxplus_lse_fwd,

@@ -54,6 +54,44 @@ def maxplus_fwd(x: np.ndarray, w: np.ndarray, bias: np.ndarray | None = None,
     return y, idx
 
 
+def round_bf16(a: np.ndarray) -> np.ndarray:
+    """Round float32 values to the nearest bfloat16 (ties to even), returned as
+    float32; NaN stays NaN, overflow goes to +-inf."""
+    a = np.asarray(a, dtype=np.float32)
+    bits = a.view(np.uint32).astype(np.uint64)
+    rounded = ((bits + 0x7FFF + ((bits >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    out = rounded.view(np.float32)
+    return np.where(np.isnan(a), np.float32(np.nan), out).astype(np.float32)
+
+
+def maxplus_fwd_bf16(x: np.ndarray, w: np.ndarray, bias: np.ndarray | None = None,
+                     scale: float = 1.0):
+    """The reference expression on bf16 tensors (tropformer.py:131,141 with bf16
+    weight and input): every sum w[n,k] + x[m,k] rounded to bf16, exact max,
+    lowest-index argmax.  The max is returned as float32; bias and scale are
+    then applied in float32 (the library's output convention)."""
+    x = round_bf16(x)
+    w = round_bf16(w)
+    M, K = x.shape
+    N = w.shape[0]
+    y = np.empty((M, N), dtype=np.float32)
+    idx = np.zeros((M, N), dtype=np.int64)
+    if K == 0:
+        y.fill(-np.inf)
+    else:
+        step = _rows_per_chunk(N, K)
+        with np.errstate(invalid="ignore", over="ignore"):
+            for m0 in range(0, M, step):
+                s = round_bf16(w[None, :, :] + x[m0:m0 + step, None, :])
+                y[m0:m0 + step] = s.max(axis=-1)
+                idx[m0:m0 + step] = s.argmax(axis=-1)
+    if bias is not None:
+        y = (y + np.asarray(bias, dtype=np.float32)[None, :]).astype(np.float32)
+    if scale != 1.0:
+        y = (y * np.float32(scale)).astype(np.float32)
+    return y, idx
+
+
 def maxplus_bwd_argmax(idx: np.ndarray, gy: np.ndarray, K: int, scale: float = 1.0):
     """(gx [M,K], gw [N,K], gbias [N]) routing gy*scale to the argmax term (float64 sums)."""
     M, N = gy.shape

@@ -139,6 +139,32 @@ def gen_linear(trop):
     _save("linear_nan", x=_np(x), W=_np(W), max=_np(mx.values), idx=_np(mx.indices))
 
 
+def gen_bf16(trop):
+    # eval-mode TropicalLinear on bf16 weight and input (tropformer.py:131,141):
+    # the reference's own bf16 arithmetic (each sum rounded to bf16).  No bias,
+    # so the module output is the bf16 max itself.
+    for name, seed, kind in (("linear_bf16_gauss", 10, "gauss"), ("linear_bf16_ties", 11, "ties")):
+        gen = torch.Generator().manual_seed(seed)
+        if kind == "gauss":
+            x = torch.randn(40, 72, generator=gen) * 3.0
+            w = torch.randn(24, 72, generator=gen) * 3.0
+            x[2, 5] = float("nan")
+            w[3, :] = float("-inf")
+        else:
+            x = torch.randint(-4, 5, (33, 50), generator=gen).float() * 0.25
+            w = torch.randint(-4, 5, (21, 50), generator=gen).float() * 0.25
+        layer = trop.TropicalLinear(x.shape[1], w.shape[0], bias=False)
+        with torch.no_grad():
+            layer.weight.copy_(w)
+        layer = layer.bfloat16().eval()
+        xb = x.bfloat16()
+        with torch.no_grad():
+            y = layer(xb)
+            idx = (layer.weight.unsqueeze(0) + xb.unsqueeze(1)).max(dim=-1).indices
+        _save(name, x=_np(xb.float()), W=_np(layer.weight.float()), max=_np(y.float()),
+              idx=_np(idx))
+
+
 def gen_scores(trop, dtn):
     # DTNAttention tropical score (deep_tropical_net.py:148-150): hard and smooth
     gen = torch.Generator().manual_seed(4)
@@ -230,6 +256,7 @@ def main():
     research = _load("research_tsrn_dml", "research/tsrn_dml.py")
     gen_kat(trop)
     gen_linear(trop)
+    gen_bf16(trop)
     gen_scores(trop, dtn)
     gen_tsrn(research)
 

@@ -244,3 +244,67 @@ def test_forward_large_sampled(cuda):
     ry, ri = oracle.maxplus_fwd(x[rows], w, bias)
     np.testing.assert_array_equal(y[rows], ry)
     np.testing.assert_array_equal(am[rows], ri)
+
+
+# ----------------------------------------------------------------- bf16 arithmetic
+def _run_bf16_arith(x, w, bias=None, argmax=True):
+    ops = _ops()
+    xt = torch.tensor(x, device="cuda").bfloat16()
+    wt = torch.tensor(w, device="cuda").bfloat16()
+    bt = torch.tensor(bias, device="cuda") if bias is not None else None
+    y, am = ops.maxplus(xt, wt, bt, argmax=argmax, arith="bf16")
+    torch.cuda.synchronize()
+    return y.cpu().numpy(), (am.cpu().numpy() if am is not None else None)
+
+
+@pytest.mark.parametrize("name", ["linear_bf16_gauss", "linear_bf16_ties"])
+def test_bf16_arith_golden(cuda, name):
+    # the reference TropicalLinear on bf16 tensors: bit-exact max and index
+    g = load_golden(name)
+    y, am = _run_bf16_arith(g["x"], g["W"])
+    np.testing.assert_array_equal(y, g["max"])
+    np.testing.assert_array_equal(am, g["idx"])
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 256, 256), (300, 200, 136), (512, 384, 1000),
+                                   (256, 130, 4100), (33, 20, 50)])
+def test_bf16_arith_shapes(cuda, M, N, K):
+    rng = np.random.default_rng(M + N + K)
+    x = (rng.standard_normal((M, K)) * 3).astype(np.float32)
+    w = (rng.standard_normal((N, K)) * 3).astype(np.float32)
+    x[rng.random((M, K)) < 0.0005] = np.nan
+    w[rng.random((N, K)) < 0.05] = -np.inf
+    x[min(3, M - 1), :] = -np.inf
+    y, am = _run_bf16_arith(x, w)
+    ry, ri = oracle.maxplus_fwd_bf16(x, w)
+    np.testing.assert_array_equal(y, ry)
+    np.testing.assert_array_equal(am, ri)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 256, 320), (40, 30, 70)])
+def test_bf16_arith_ties_bias_value_only(cuda, M, N, K):
+    rng = np.random.default_rng(7)
+    x = (rng.integers(-4, 5, (M, K)) * 0.25).astype(np.float32)
+    w = (rng.integers(-4, 5, (N, K)) * 0.25).astype(np.float32)
+    bias = rng.standard_normal(N).astype(np.float32)
+    y, am = _run_bf16_arith(x, w, bias)
+    ry, ri = oracle.maxplus_fwd_bf16(x, w, bias)
+    np.testing.assert_array_equal(y, ry)
+    np.testing.assert_array_equal(am, ri)
+    y2, _ = _run_bf16_arith(x, w, bias, argmax=False)
+    np.testing.assert_array_equal(y2, ry)
+
+
+def test_bf16_arith_large_sampled(cuda):
+    # above the default TMA threshold: the packed bf16x2 kernel with its argmax search
+    rng = np.random.default_rng(41)
+    M, N, K = 1100, 1030, 1000
+    x = (rng.standard_normal((M, K)) * 2).astype(np.float32)
+    w = (rng.standard_normal((N, K)) * 2).astype(np.float32)
+    x[rng.random((M, K)) < 0.0003] = np.nan
+    bias = rng.standard_normal(N).astype(np.float32)
+    y, am = _run_bf16_arith(x, w, bias)
+    rows = np.concatenate([[0, M - 1], rng.choice(M, 62, replace=False)])
+    ry, ri = oracle.maxplus_fwd_bf16(x[rows], w, bias)
+    np.testing.assert_array_equal(y[rows], ry)
+    np.testing.assert_array_equal(am[rows], ri)

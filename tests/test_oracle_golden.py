@@ -150,3 +150,26 @@ def test_win_mask_packing():
     for t in range(70):
         bit = (words[:, t // 32, :] >> (t % 32)) & 1
         np.testing.assert_array_equal(bit.astype(bool), win[:, t, :])
+
+
+@pytest.mark.parametrize("name", ["linear_bf16_gauss", "linear_bf16_ties"])
+def test_bf16_arith_forward(name):
+    # the reference TropicalLinear evaluated on bf16 tensors: sums rounded to bf16
+    g = load_golden(name)
+    y, idx = oracle.maxplus_fwd_bf16(g["x"], g["W"])
+    np.testing.assert_array_equal(y, g["max"])
+    np.testing.assert_array_equal(idx, g["idx"])
+    # and it differs from fp32 arithmetic on the same inputs (the mode matters)
+    if name == "linear_bf16_gauss":
+        assert not np.array_equal(oracle.maxplus_fwd(g["x"], g["W"])[0], g["max"])
+
+
+def test_round_bf16_rule():
+    vals = np.array([1.0, 1.00390625, 1.005859375, 1.0078125, -2.0, np.inf, -np.inf,
+                     3.4e38, 1e-40], dtype=np.float32)
+    r = oracle.round_bf16(vals)
+    # 1 + 2^-8 is halfway between 1 and 1 + 2^-7: ties to even -> 1
+    assert r[1] == 1.0
+    assert r[2] == np.float32(1.0078125)      # above halfway rounds up
+    assert np.isinf(r[7])                     # beyond the largest bf16 -> inf
+    assert np.isnan(oracle.round_bf16(np.array([np.nan], np.float32)))[0]
