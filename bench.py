@@ -22,7 +22,8 @@ forward with int32 argmax and the argmax backward; Gop/s of forward ops.
 softmax) forward + backward at B=128, L=64 per rank; metric tokens/s.
 
 ``--dtype bf16`` stores the GEMM operands in bf16 (widened exactly on the GPU;
-the arithmetic stays fp32).
+the arithmetic stays fp32); with ``--arith bf16`` every sum is rounded to bf16
+as the reference does on bf16 tensors (packed bf16x2 kernel).
 
 ``--impl reference`` times the reference's own CPU implementation (its PyTorch
 expression, restated in ``oracle/torch_ref.py``) on the host cores for the same
@@ -61,7 +62,11 @@ def parse_args():
     p.add_argument("--workload", choices=["gemm", "scan", "dtn", "linear"], default="gemm")
     p.add_argument("--size", type=int, default=8192, help="M = N = K of the GEMM workload")
     p.add_argument("--dtype", choices=["f32", "bf16"], default="f32",
-                   help="GEMM operand storage (bf16 is widened exactly; arithmetic is fp32)")
+                   help="GEMM operand storage")
+    p.add_argument("--arith", choices=["f32", "bf16"], default="f32",
+                   help="bf16 operands: fp32 arithmetic (exact widening) or bf16 arithmetic "
+                        "(sums rounded to bf16, as the reference on bf16 tensors; packed "
+                        "bf16x2 kernel)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                    help="N>1 GEMM: fused peer-store epilogue (p2p) or NCCL all-gather")
@@ -188,8 +193,9 @@ def time_steps(step, steps, world):
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def cpu_gemm_rate(size: int, target_s: float = 12.0):
-    """Reference expression (oracle/torch_ref.py) on a row sample of the size^3 problem."""
+def cpu_gemm_rate(size: int, target_s: float = 12.0, bf16: bool = False):
+    """Reference expression (oracle/torch_ref.py) on a row sample of the size^3 problem
+    (on bf16 tensors when ``bf16``: the reference's own bf16 arithmetic)."""
     from oracle.torch_ref import maxplus_fwd_torch
 
     threads = os.cpu_count() or 1
@@ -197,6 +203,8 @@ def cpu_gemm_rate(size: int, target_s: float = 12.0):
     g = torch.Generator().manual_seed(1)
     w = torch.randn(size, size, generator=g)
     x = torch.randn(64, size, generator=g)
+    if bf16:
+        w, x = w.bfloat16(), x.bfloat16()
     # calibrate on 1 row, then size the sample for ~target_s seconds
     t0 = time.perf_counter()
     maxplus_fwd_torch(x[:1], w)
@@ -209,7 +217,7 @@ def cpu_gemm_rate(size: int, target_s: float = 12.0):
     return {"value": ops / dt / 1e9, "unit": "Gop/s", "cores": threads, "kind": "port",
             "sample": f"{rows} of {size} rows of x against all of W ({size}x{size}) "
                       f"through the reference expression W[None]+x[:,None] -> max(-1) "
-                      f"(values + indices), {dt:.1f} s"}
+                      f"(values + indices){' on bf16 tensors' if bf16 else ''}, {dt:.1f} s"}
 
 
 def cpu_scan_rate(B, T, C, target_s: float = 12.0):
@@ -258,6 +266,11 @@ def gemm_workload(args, world, rank):
     del W_full_rows
     if args.dtype == "bf16":
         x, W = x.to(torch.bfloat16), W.to(torch.bfloat16)
+    bf16_arith = args.dtype == "bf16" and args.arith == "bf16"
+    if args.arith == "bf16" and args.dtype != "bf16":
+        raise SystemExit("--arith bf16 needs --dtype bf16")
+    if bf16_arith and world > 1:
+        raise SystemExit("--arith bf16 is a single-GPU workload here")
     y = torch.empty(M, Nr, device=dev)
     am = torch.empty(M, Nr, device=dev, dtype=torch.int32)
     sharded = None
@@ -273,7 +286,7 @@ def gemm_workload(args, world, rank):
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
         if sharded is None:
-            ops.maxplus_strided(x, W, out=y, out_argmax=am)
+            ops.maxplus_strided(x, W, out=y, out_argmax=am, arith=args.arith)
         elif args.dtype == "bf16":
             sharded(ops.widen_bf16(x), ops.widen_bf16(W))
         else:
@@ -290,7 +303,8 @@ def gemm_workload(args, world, rank):
         import oracle
         import numpy as np
         rows = slice(0, 2)
-        ry, ri = oracle.maxplus_fwd(x[rows].float().cpu().numpy(), W[:256].float().cpu().numpy())
+        ref_fn = oracle.maxplus_fwd_bf16 if bf16_arith else oracle.maxplus_fwd
+        ry, ri = ref_fn(x[rows].float().cpu().numpy(), W[:256].float().cpu().numpy())
         if sharded is None:
             yc, ac = y[rows, :256], am[rows, :256]
         else:
@@ -325,7 +339,7 @@ def gemm_workload(args, world, rank):
         dx.copy_(hx, non_blocking=True)
         dW.copy_(hW, non_blocking=True)
         if sharded is None:
-            ys, ams = ops.maxplus_strided(dx, dW, out=y, out_argmax=am)
+            ys, ams = ops.maxplus_strided(dx, dW, out=y, out_argmax=am, arith=args.arith)
         else:
             if args.dtype == "bf16":
                 yf, af = sharded(ops.widen_bf16(dx), ops.widen_bf16(dW))
@@ -350,29 +364,35 @@ def gemm_workload(args, world, rank):
     # context, the nominal issue limit of the packed form is 128 terms per
     # clock per SM; measured forms reach about half of it.
     probe = {}
-    for form in range(5):
+    for form in range(7):
         ops.probe_addmax(form, 148 * 8, 50)                      # warm
         pms, terms = ops.probe_addmax(form, 148 * 8, 400)
         probe[form] = 2.0 * terms / (pms / 1e3) / 1e12           # Top/s (2 ops per term)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     mhz = (clk or {}).get("sm_mhz") or measured_peaks().get("sm_max_mhz", 1965.0)
     issue_limit = 256.0 * sms * mhz * 1e6 / 1e12
-    peak = max(probe.values())
+    # the peak of the arithmetic the kernel runs: fp32 forms 0-4, bf16x2 forms 5-6
+    peak = max(probe[f] for f in ((5, 6) if bf16_arith else range(5)))
     per_gpu_ops = 2.0 * M * Nr * K
     achieved = per_gpu_ops / (kms / 1e3) / 1e12
     roofline = {"bound": "cuda-core", "achieved": achieved, "peak": peak, "unit": "Top/s",
                 "frac": achieved / peak,
                 "traffic": profiled_traffic(f"maxplus_tma_gemm{S}") if world == 1 else None,
-                "peak_source": "in-repo register-only add+max probe (tp_probe_addmax), best of "
-                               "5 instruction forms, measured in this run; of measured",
+                "peak_source": "in-repo register-only add+max probe (tp_probe_addmax), best "
+                               "instruction form of the kernel's arithmetic (" +
+                               ("bf16x2" if bf16_arith else "fp32") +
+                               "), measured in this run; of measured",
                 "probe_top_s": {"fadd_fmnmx": probe[0], "fadd2_fmnmx3": probe[1],
                                 "fadd2_fmnmx3_nan": probe[2], "2fadd_fmnmx3_nan": probe[3],
-                                "mixed": probe[4]},
+                                "mixed": probe[4], "bf16x2_add_max": probe[5],
+                                "bf16x2_add_max_nan": probe[6]},
                 "nominal_issue_limit_top_s": issue_limit,
                 "kernel_ms": kms}
     res = {
         "metric": "max-plus GEMM Gop/s (fp32, with int32 argmax)" if args.dtype == "f32" else
-                  "max-plus GEMM Gop/s (bf16 operands, fp32 arithmetic, with int32 argmax)",
+                  ("max-plus GEMM Gop/s (bf16 operands, bf16 arithmetic, with int32 argmax)"
+                   if bf16_arith else
+                   "max-plus GEMM Gop/s (bf16 operands, fp32 arithmetic, with int32 argmax)"),
         "value": value,
         "unit": "Gop/s",
         "n_gpus": world,
@@ -382,10 +402,12 @@ def gemm_workload(args, world, rank):
         "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
-        "dtype": "f32",
+        "dtype": "bf16" if bf16_arith else "f32",
         "data": "synthetic: x, W ~ N(0,1) (seeded), 5% of W = -inf",
-        "config": {"workload": f"maxplus_gemm M=N=K={S} {args.dtype} operands + int32 argmax",
+        "config": {"workload": f"maxplus_gemm M=N=K={S} {args.dtype} operands + int32 argmax"
+                               + (", bf16 arithmetic" if bf16_arith else ""),
                    "operand_storage": args.dtype,
+                   "arithmetic": "bf16" if bf16_arith else "f32",
                    "M": M, "N": N, "K": K,
                    "parallelism": (f"column-shard x{world}, " + (
                        "all-gather fused into the GEMM epilogue (peer stores into "
@@ -394,7 +416,9 @@ def gemm_workload(args, world, rank):
                    "l2": "inputs (2 x 256 MiB) larger than L2"},
         "e2e": {"value": e2e_value, "unit": "Gop/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps,   # one max-plus kernel per step (plus 2 barrier kernels at N>1)
+        # one max-plus kernel per step (+2 exact widening kernels for bf16 operands with
+        # fp32 arithmetic; +2 barrier kernels at N>1)
+        "gpu_launches": args.steps * (3 if (args.dtype == "bf16" and not bf16_arith) else 1),
         "roofline": roofline,
         "clocks": clk,
     }
@@ -757,6 +781,11 @@ def reference_arm(args, world, rank):
         cb = cpu_dtn_rate(target_s=max(3.0, 2.0 * args.steps))
         metric = "DTN tropical attention block tokens/s (fwd+bwd, train mode)"
         cfg = {"workload": "DTNAttention d_model=256 heads=8 L=64 fwd+bwd (torch CPU)"}
+    elif args.workload == "gemm" and args.dtype == "bf16" and args.arith == "bf16":
+        cb = cpu_gemm_rate(args.size, target_s=max(3.0, 2.0 * args.steps), bf16=True)
+        metric = "max-plus GEMM Gop/s (bf16 operands, bf16 arithmetic, with int32 argmax)"
+        cfg = {"workload": f"maxplus_gemm M=N=K={args.size} bf16 tensors + int64 argmax "
+                           f"(torch CPU)", "M": args.size, "N": args.size, "K": args.size}
     elif args.workload == "gemm":
         cb = cpu_gemm_rate(args.size, target_s=max(3.0, 2.0 * args.steps))
         metric = "max-plus GEMM Gop/s (fp32, with int32 argmax)"
@@ -792,7 +821,8 @@ def main():
         if res is not None and args.impl == "ours" and rank == 0 and world == 1 \
                 and not args.no_cpu_baseline:
             if args.workload == "gemm":
-                res["cpu_baseline"] = cpu_gemm_rate(args.size)
+                res["cpu_baseline"] = cpu_gemm_rate(
+                    args.size, bf16=(args.dtype == "bf16" and args.arith == "bf16"))
             elif args.workload == "dtn":
                 res["cpu_baseline"] = cpu_dtn_rate()
             elif args.workload == "linear":
