@@ -17,11 +17,21 @@ import oracle
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("M,N,K,Ns,col0", [(512, 1024, 192, 512, 256),   # fused TMA epilogue
-                                           (96, 300, 50, 100, 150)])     # generic + copies
-def test_sharded_entry_two_local_destinations(cuda, M, N, K, Ns, col0):
+@pytest.mark.parametrize("M,N,K,Ns,col0,force_tma", [
+    (512, 1024, 192, 512, 256, True),    # fused TMA epilogue (deferred argmax search)
+    (512, 1024, 192, 512, 256, False),   # below the TMA threshold: generic + copies
+    (96, 300, 50, 100, 150, False)])     # generic + copies
+def test_sharded_entry_two_local_destinations(cuda, M, N, K, Ns, col0, force_tma):
     from mk_iii_technologies_tsrn_b200 import _lib
     lib = _lib.load()
+    old = lib.tp_set_argmax_tma_min_terms(0 if force_tma else 1 << 30)
+    try:
+        _two_local_destinations(lib, cuda, M, N, K, Ns, col0)
+    finally:
+        lib.tp_set_argmax_tma_min_terms(old)
+
+
+def _two_local_destinations(lib, cuda, M, N, K, Ns, col0):
     g = torch.Generator(device=cuda).manual_seed(0)
     x = torch.randn(M, K, device=cuda, generator=g)
     w = torch.randn(Ns, K, device=cuda, generator=g)
@@ -50,12 +60,15 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _two_rank_worker(rank, world, port, mode, q):
+def _two_rank_worker(rank, world, port, mode, force_tma, q):
     try:
         import sys
         sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
         import torch.distributed as dist
         from mk_iii_technologies_tsrn_b200.dist import ShardedMaxPlus
+        from mk_iii_technologies_tsrn_b200 import _lib
+        if force_tma:      # this small case would otherwise take the generic kernel
+            _lib.load().tp_set_argmax_tma_min_terms(0)
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -82,15 +95,16 @@ def _two_rank_worker(rank, world, port, mode, q):
         q.put((rank, repr(e)))
 
 
-@pytest.mark.parametrize("mode", ["p2p", "nccl"])
-def test_two_rank_sharded_gemm(cuda, mode):
+@pytest.mark.parametrize("mode,force_tma", [("p2p", True), ("p2p", False), ("nccl", True)])
+def test_two_rank_sharded_gemm(cuda, mode, force_tma):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_two_rank_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_two_rank_worker, args=(r, 2, port, mode, force_tma, q))
+             for r in range(2)]
     for p in procs:
         p.start()
     out = dict(q.get(timeout=300) for _ in range(2))
