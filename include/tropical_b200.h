@@ -202,6 +202,31 @@ TP_API int tp_maxplus_bwd_smooth(int mode, float tau, int dtype,
 TP_API int64_t tp_set_argmax_tma_min_terms(int64_t terms);
 
 /* ======================================================================== *
+ *  Fused TSRN tropical top-k attention, forward (inference)
+ *  Replaces research/tsrn_dml.py:462-548 (TropicalAttention.forward) from the
+ *  scores on: the tropical score (:438-460, log-sum-exp over channels), the
+ *  ALiBi bias (:509-514), the causal mask (:516-518), the top-k threshold
+ *  (:520-521), the softmax and the product with V (:522-524).  Q/K/V come
+ *  after the projections, QK-norm and RoPE.
+ *    S[i,j] = log sum_c exp(Q[i,c] + K[j,c]) - slope[h] * |i - (j - Tc)|
+ *             (-inf when causal and j - Tc > i)
+ *    thr_i  = top_k-th largest of S[i,:] (ties counted, as torch.topk)
+ *    out[i] = sum over {j : S[i,j] >= thr_i} of softmax(S[i,:])_j * V[j]
+ *  Q [B,H,T,dh], K and V [B,H,Tkv,dh] contiguous fp32; keys j < Tc are the
+ *  cross-window cached keys (positions j - Tc < 0), Tkv = Tc + T when they
+ *  are used.  alibi_slopes [H].  dh <= 128, top_k <= 64, Tkv <= 6144.  The
+ *  scores match the reference's fp32 log-sum-exp within 1e-5; rows whose
+ *  top_k-th and next scores lie within that distance may select differently.
+ *  workspace: tp_tsrn_attention_workspace_bytes(...) bytes, 16-byte aligned.
+ * ======================================================================== */
+TP_API int64_t tp_tsrn_attention_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t Tkv,
+                                                 int64_t dh);
+TP_API int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc,
+                                 int64_t dh, const float* Q, const float* K, const float* V,
+                                 const float* alibi_slopes, int top_k, int causal, float* out,
+                                 void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ======================================================================== *
  *  Tropical (max-plus) diagonal SSM scan  (research/tsrn_dml.py:917-980)
  *
  *    u[b,t,c] = bb[b,t,c] + xx[b,t,c]     (xx may be NULL: u = bb)

@@ -367,6 +367,34 @@ void maxplus_matmul_cuda(const float* A, const float* B, float* C, int M, int K,
   set_last_error(s);
 }
 
+int64_t tp_tsrn_attention_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t Tkv,
+                                          int64_t dh) {
+  if (B < 0 || H < 0 || T < 0 || Tkv < 0 || dh < 0) return 0;
+  return tp::tsrn_attention_workspace_floats(B, H, T, Tkv, dh) * (int64_t)sizeof(float);
+}
+
+int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc, int64_t dh,
+                          const float* Q, const float* K, const float* V,
+                          const float* alibi_slopes, int top_k, int causal, float* out,
+                          void* workspace, int64_t workspace_bytes, void* stream) {
+  TP_RETURN_IF(B < 0 || H < 0 || T < 0 || Tkv < 0 || Tc < 0 || dh < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(Tc > Tkv, TP_ERR_INVALID_ARG);
+  if (B * H * T == 0) return TP_OK;
+  TP_RETURN_IF(Tkv == 0 || dh == 0 || top_k < 1, TP_ERR_INVALID_ARG);
+  TP_CHECK_PTR(Q);
+  TP_CHECK_PTR(K);
+  TP_CHECK_PTR(V);
+  TP_CHECK_PTR(alibi_slopes);
+  TP_CHECK_PTR(out);
+  TP_RETURN_IF(workspace == nullptr ||
+                   workspace_bytes < tp_tsrn_attention_workspace_bytes(B, H, T, Tkv, dh),
+               TP_ERR_WORKSPACE);
+  TP_RETURN_IF(!aligned16(workspace), TP_ERR_MISALIGNED);
+  TP_CHECK_PTR(workspace);
+  return tp::launch_tsrn_attention_fwd(B, H, T, Tkv, Tc, dh, Q, K, V, alibi_slopes, top_k,
+                                       causal, out, (float*)workspace, as_stream(stream));
+}
+
 int64_t tp_set_argmax_tma_min_terms(int64_t terms) { return tp::set_argmax_tma_min_terms(terms); }
 
 int tp_last_error(void) { return last_error(); }

@@ -118,4 +118,11 @@ int launch_scan_bwd(const ScanArgs& p, cudaStream_t stream);
 int launch_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters, float* sink,
                         cudaStream_t stream);
 
+// tsrn_attention.cu: fused TSRN tropical top-k attention forward
+int64_t tsrn_attention_workspace_floats(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t dh);
+int launch_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc, int64_t dh,
+                              const float* Q, const float* K, const float* V,
+                              const float* slopes, int top_k, int causal, float* out,
+                              float* ws, cudaStream_t stream);
+
 }  // namespace tp

@@ -496,3 +496,33 @@ def probe_addmax(form: int, blocks: int, iters: int, device=None) -> Tuple[float
         end.synchronize()
     _lib.check(st, "tp_probe_addmax")
     return start.elapsed_time(end), blocks * 256 * iters * 128
+
+
+# --------------------------------------------------------------------------- TSRN attention
+def tsrn_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, slopes: torch.Tensor,
+                   top_k: int, causal: bool = True, Tc: int = 0) -> torch.Tensor:
+    """Fused TSRN tropical top-k attention forward (research/tsrn_dml.py:462-548 after RoPE):
+    log-sum-exp scores, ALiBi, causal mask, top-k threshold, softmax and @V in one pass.
+
+    ``Q`` [B,H,T,dh], ``K``/``V`` [B,H,Tkv,dh] fp32 (made contiguous), ``slopes`` [H];
+    the first ``Tc`` keys are cross-window cached keys.  Forward only (inference)."""
+    dev = _require_cuda(Q, K, V, slopes)
+    if Q.dim() != 4 or K.shape != V.shape or K.shape[:2] != Q.shape[:2] or \
+            K.shape[-1] != Q.shape[-1]:
+        raise ValueError(f"shapes {tuple(Q.shape)}, {tuple(K.shape)}, {tuple(V.shape)}")
+    Q, K, V = (_f32(t).contiguous() for t in (Q, K, V))
+    slopes = _f32(slopes).contiguous()
+    B, H, T, dh = Q.shape
+    Tkv = K.shape[2]
+    if slopes.shape != (H,):
+        raise ValueError("slopes must be [H]")
+    lib = _lib.load()
+    ws_bytes = int(lib.tp_tsrn_attention_workspace_bytes(B, H, T, Tkv, dh))
+    ws = torch.empty(max(ws_bytes // 4, 4), device=dev, dtype=torch.float32)
+    out = torch.empty_like(Q)
+    with torch.cuda.device(dev):
+        st = lib.tp_tsrn_attention_fwd(B, H, T, Tkv, int(Tc), dh, _ptr(Q), _ptr(K), _ptr(V),
+                                       _ptr(slopes), int(top_k), 1 if causal else 0, _ptr(out),
+                                       _ptr(ws), ws.numel() * 4, _stream(dev))
+    _lib.check(st, "tp_tsrn_attention_fwd")
+    return out

@@ -18,6 +18,7 @@ from .maxplus import (  # noqa: F401
     maxplus_fwd,
     maxplus_fwd_bf16,
     round_bf16,
+    tsrn_attention_fwd,
     maxplus_bwd_argmax,
     maxplus_bwd_smooth,
     maxplus_lse_fwd,

@@ -148,3 +148,34 @@ def maxplus_lse_fwd(x: np.ndarray, w: np.ndarray, tau: float = 1.0):
         mx = s.max(axis=-1, keepdims=True)
         y[m0:m0 + step] = tau * (mx[..., 0] + np.log(np.exp(s - mx).sum(axis=-1)))
     return y
+
+
+def tsrn_attention_fwd(Q, K, V, slopes, top_k: int, causal: bool = True, Tc: int = 0):
+    """TropicalAttention after RoPE (research/tsrn_dml.py:438-460 score, :505-526
+    ALiBi, causal mask, top-k threshold, softmax, @V) in float64.
+
+    Q [B,H,T,dh], K/V [B,H,Tkv,dh], slopes [H].  Returns (out [B,H,T,dh], the
+    masked scores before the top-k step [B,H,T,Tkv])."""
+    Q = np.asarray(Q, np.float64)
+    K = np.asarray(K, np.float64)
+    V = np.asarray(V, np.float64)
+    slopes = np.asarray(slopes, np.float64)
+    B, H, T, dh = Q.shape
+    Tkv = K.shape[2]
+    raw = Q[:, :, :, None, :] + K[:, :, None, :, :]
+    m = raw.max(axis=-1, keepdims=True)
+    S = (m + np.log(np.exp(raw - m).sum(axis=-1, keepdims=True)))[..., 0]
+    q_pos = np.arange(T)
+    k_pos = np.arange(-Tc, Tkv - Tc)
+    dist = np.abs(q_pos[:, None] - k_pos[None, :])
+    S = S - slopes[None, :, None, None] * dist[None, None]
+    if causal:
+        S = np.where((k_pos[None, :] > q_pos[:, None])[None, None], -np.inf, S)
+    k = min(top_k, Tkv)
+    thr = -np.sort(-S, axis=-1)[..., k - 1:k]
+    Sm = np.where(S < thr, -np.inf, S)
+    mx = Sm.max(axis=-1, keepdims=True)
+    with np.errstate(invalid="ignore"):
+        w = np.exp(Sm - mx)
+        w = w / w.sum(axis=-1, keepdims=True)
+    return w @ V, S

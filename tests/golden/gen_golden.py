@@ -248,6 +248,36 @@ def gen_tsrn(research):
           H=_np(Hs), A_c=_np(A_c), **state, **grads)
 
 
+def gen_tsrn_attention(research):
+    # research TropicalAttention (research/tsrn_dml.py:355-548), eval, causal,
+    # fast path: the module output, the Wo input (the attention context) and
+    # the rotated Q/K/V computed by the module's own sub-modules
+    torch.manual_seed(8)
+    d, heads, top_k, B, T = 32, 4, 6, 2, 40
+    attn = research.TropicalAttention(d, top_k=top_k, n_heads=heads)
+    with torch.no_grad():
+        attn.q_norm.weight.uniform_(0.5, 1.5)
+        attn.k_norm.bias.uniform_(-0.2, 0.2)
+    attn.eval()
+    x = torch.randn(B, T, d)
+    with torch.no_grad():
+        out = attn(x).clone()
+        # the attention context (Wo's input): the same forward with Wo = identity
+        wo = attn.Wo.weight.detach().clone()
+        attn.Wo.weight.copy_(torch.eye(d))
+        ctx = attn(x).clone()
+        attn.Wo.weight.copy_(wo)
+        dh = d // heads
+        Q = attn.q_norm(attn.Wq(x).view(B, T, heads, dh).permute(0, 2, 1, 3))
+        K = attn.k_norm(attn.Wk(x).view(B, T, heads, dh).permute(0, 2, 1, 3))
+        V = attn.Wv(x).view(B, T, heads, dh).permute(0, 2, 1, 3)
+        Q, K = attn.rope(Q, K)
+    ctx = ctx.view(B, T, heads, dh).permute(0, 2, 1, 3)
+    state = {f"p_{k}": _np(v) for k, v in attn.state_dict().items()}
+    _save("tsrn_attention", x=_np(x), out=_np(out), Q=_np(Q), K=_np(K), V=_np(V),
+          ctx=_np(ctx), slopes=_np(attn.alibi_slopes), top_k=np.int64(top_k), **state)
+
+
 def main():
     sys.path.insert(0, REF)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
@@ -259,6 +289,7 @@ def main():
     gen_bf16(trop)
     gen_scores(trop, dtn)
     gen_tsrn(research)
+    gen_tsrn_attention(research)
 
 
 if __name__ == "__main__":

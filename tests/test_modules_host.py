@@ -1,6 +1,7 @@
 """Host-side checks of the drop-in modules (no GPU): names, parameters and
 state-dict layout match the reference's (from the golden fixtures), and CPU
 inputs are refused rather than silently computed on the CPU."""
+import numpy as np
 import pytest
 import torch
 
@@ -56,3 +57,15 @@ def test_cpu_inputs_are_refused():
 def test_is_cuda_kernel_available_without_gpu():
     from mk_iii_technologies_tsrn_b200.maxplus_binding import is_cuda_kernel_available
     assert is_cuda_kernel_available() == torch.cuda.is_available()
+
+
+def test_tsrn_attention_state_dict_matches_reference():
+    # same parameter and buffer names as research TropicalAttention
+    from conftest import load_golden
+    from mk_iii_technologies_tsrn_b200.tsrn_attention import TropicalAttention
+    g = load_golden("tsrn_attention")
+    ref_keys = sorted(k[2:] for k in g.keys() if k.startswith("p_"))
+    m = TropicalAttention(32, top_k=6, n_heads=4)
+    assert sorted(m.state_dict().keys()) == ref_keys
+    m.load_state_dict({k: torch.tensor(g["p_" + k]) for k in ref_keys})
+    np.testing.assert_allclose(m.alibi_slopes.numpy(), g["slopes"])
