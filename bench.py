@@ -17,6 +17,9 @@ metric GB/s of those algorithmic bytes.
 ``--workload linear``: config 1, the tropical linear x [1024,256] (x) W [256,256]
 forward with int32 argmax and the argmax backward; Gop/s of forward ops.
 
+``--workload tsrn_attn``: the TSRN tropical top-k attention of config 5 (B=64, H=8,
+T=1024, d_h=80, top_k=16, causal) through the fused kernel; tokens/s.
+
 ``--workload dtn``: config 2, the drop-in DTNAttention(256, 8) block
 (tropical Q/K projections with the STE backward, tropical score, Maslov
 softmax) forward + backward at B=128, L=64 per rank; metric tokens/s.
@@ -59,7 +62,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["gemm", "scan", "dtn", "linear"], default="gemm")
+    p.add_argument("--workload", choices=["gemm", "scan", "dtn", "linear", "tsrn_attn"],
+                   default="gemm")
     p.add_argument("--size", type=int, default=8192, help="M = N = K of the GEMM workload")
     p.add_argument("--dtype", choices=["f32", "bf16"], default="f32",
                    help="GEMM operand storage")
@@ -714,6 +718,122 @@ def linear_workload(args, world, rank):
     }
 
 
+TSRN_ATT = dict(B=64, H=8, T=1024, dh=80, top_k=16)   # TSRN block at scale 1 (config 5)
+
+
+def tsrn_attn_workload(args, world, rank):
+    """The TSRN tropical top-k attention of config 5 at scale 1 (B=64 per rank, H=8,
+    T=1024, d_h=80, top_k=16, causal): the fused kernel from Q/K/V (after QK-norm and
+    RoPE) to the attention context."""
+    from mk_iii_technologies_tsrn_b200 import ops, _lib
+
+    _lib.load().tp_set_pointer_checks(0)
+    B, H, T, dh, k = (TSRN_ATT[n] for n in ("B", "H", "T", "dh", "top_k"))
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(10 + rank)
+    # LayerNorm'd, rotated Q and K have unit-variance entries; V as projected
+    hQ = torch.randn(B, H, T, dh, generator=gen).pin_memory()
+    hK = torch.randn(B, H, T, dh, generator=gen).pin_memory()
+    hV = torch.randn(B, H, T, dh, generator=gen).pin_memory()
+    Q, K, V = hQ.to(dev), hK.to(dev), hV.to(dev)
+    slopes = (2.0 ** (-8.0 / H * (torch.arange(H, dtype=torch.float32) + 1))).to(dev)
+    # parity on a slice of this workload before timing (oracle on CPU, fp64)
+    if rank == 0:
+        import numpy as np
+        import oracle
+        out = ops.tsrn_attention(Q[:1, :2, :256].contiguous(), K[:1, :2, :256].contiguous(),
+                                 V[:1, :2, :256].contiguous(), slopes[:2], k, True)
+        ref, S = oracle.tsrn_attention_fwd(hQ[:1, :2, :256].numpy(), hK[:1, :2, :256].numpy(),
+                                           hV[:1, :2, :256].numpy(), slopes[:2].cpu().numpy(),
+                                           k, True)
+        srt = -np.sort(-S, axis=-1)
+        with np.errstate(invalid="ignore"):          # -inf - -inf in fully masked rows
+            gap = np.abs(srt[..., k - 1] - srt[..., k])
+        ok = ~(np.isfinite(gap) & (gap < 1e-4))     # rows whose top-k cut is not a near-tie
+        if not np.allclose(out.cpu().numpy()[ok], ref[ok], rtol=1e-4, atol=2e-5):
+            raise RuntimeError("fused TSRN attention differs from the oracle")
+
+    def step():
+        return ops.tsrn_attention(Q, K, V, slopes, k, True)
+
+    for _ in range(args.warmup):
+        step()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    ms = time_steps(step, args.steps, world)
+    clk = clocks.stop()
+    tokens = B * T * world
+    value = tokens / (ms / args.steps / 1e3)
+    # roofline: the score dot products (causal: sum over rows of (i+1) keys, dh FMAs
+    # each) against the measured fp32 FMA rate
+    fmas = B * H * dh * T * (T + 1) / 2
+    ops.probe_addmax(7, 148 * 8, 50)
+    pms, terms = ops.probe_addmax(7, 148 * 8, 400)
+    peak = 2.0 * terms / (pms / 1e3) / 1e12
+    achieved = 2.0 * fmas / (ms / args.steps / 1e3) / 1e12
+    hout = torch.empty(B, H, T, dh).pin_memory()
+    dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
+
+    def e2e_step():
+        dQ.copy_(hQ, non_blocking=True)
+        dK.copy_(hK, non_blocking=True)
+        dV.copy_(hV, non_blocking=True)
+        hout.copy_(ops.tsrn_attention(dQ, dK, dV, slopes, k, True), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_steps = max(3, min(args.steps, 5))
+    e2e_ms = time_steps(e2e_step, e2e_steps, world)
+    try:
+        per_step = count_library_kernels(step)
+    except Exception:   # profiler unavailable: leave the count out rather than guess
+        per_step = None
+    return {
+        "metric": "TSRN tropical top-k attention tokens/s (fused fwd, inference)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: Q, K, V ~ N(0,1) (seeded; the statistics of LayerNorm'd, rotated "
+                "Q/K), ALiBi slopes 2^(-8(h+1)/H)",
+        "config": {"workload": f"TSRN TropicalAttention B={B} H={H} T={T} d_h={dh} "
+                               f"top_k={k} causal (config 5, scale 1)",
+                   "parallelism": f"batch x{world} (weak)" if world > 1 else "single GPU",
+                   "l2": "Q/K/V 3 x 168 MiB, larger than L2"},
+        "e2e": {"value": tokens / (e2e_ms / e2e_steps / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": 3 * hQ.numel() * 4, "d2h_bytes_per_step": hout.numel() * 4},
+        "gpu_launches": per_step * args.steps if per_step is not None else None,
+        "roofline": {"bound": "cuda-core fp32 FMA (score dot products) + selection",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "kernel": "att_fwd_kernel (score dots, causal) incl. its top-k selection",
+                     "peak_source": "in-repo register-only FFMA probe (tp_probe_addmax form 7), "
+                                    "this run; of measured"},
+        "clocks": clk,
+    }
+
+
+def cpu_tsrn_attn_rate(target_s: float = 10.0):
+    from oracle.torch_ref import tsrn_attention_torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    H, T, dh, k = TSRN_ATT["H"], TSRN_ATT["T"], TSRN_ATT["dh"], TSRN_ATT["top_k"]
+    gen = torch.Generator().manual_seed(10)
+    Q, K, V = (torch.randn(1, H, T, dh, generator=gen) for _ in range(3))
+    slopes = 2.0 ** (-8.0 / H * (torch.arange(H, dtype=torch.float32) + 1))
+    t0 = time.perf_counter()
+    tsrn_attention_torch(Q, K, V, slopes, k)
+    dt = time.perf_counter() - t0
+    reps = int(max(1, min(5, target_s / max(dt, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        tsrn_attention_torch(Q, K, V, slopes, k)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": T / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"one sequence (B=1 of 64, H={H}, T={T}, d_h={dh}) through the reference "
+                      f"attention expressions (oracle/torch_ref.py), {reps} reps, {dt:.2f} s each"}
+
+
 def oracle_linear(hx, hw, hg):
     from oracle.torch_ref import tropical_linear_fwd_bwd_torch
 
@@ -772,7 +892,12 @@ def cpu_dtn_rate(target_s: float = 10.0):
 def reference_arm(args, world, rank):
     if rank != 0:
         return None
-    if args.workload == "linear":
+    if args.workload == "tsrn_attn":
+        cb = cpu_tsrn_attn_rate(target_s=max(3.0, 2.0 * args.steps))
+        metric = "TSRN tropical top-k attention tokens/s (fused fwd, inference)"
+        cfg = {"workload": "TSRN TropicalAttention H=8 T=1024 d_h=80 top_k=16 causal "
+                           "(torch CPU)"}
+    elif args.workload == "linear":
         cb = cpu_linear_rate(target_s=max(3.0, 2.0 * args.steps))
         metric = "tropical linear fwd+argmax+bwd Gop/s (2*M*N*K forward ops per step)"
         cfg = {"workload": "tropical linear M=1024 K=256 N=256 fwd + argmax + argmax backward "
@@ -816,6 +941,8 @@ def main():
             res = dtn_workload(args, world, rank)
         elif args.workload == "linear":
             res = linear_workload(args, world, rank)
+        elif args.workload == "tsrn_attn":
+            res = tsrn_attn_workload(args, world, rank)
         else:
             res = scan_workload(args, world, rank)
         if res is not None and args.impl == "ours" and rank == 0 and world == 1 \
@@ -827,6 +954,8 @@ def main():
                 res["cpu_baseline"] = cpu_dtn_rate()
             elif args.workload == "linear":
                 res["cpu_baseline"] = cpu_linear_rate()
+            elif args.workload == "tsrn_attn":
+                res["cpu_baseline"] = cpu_tsrn_attn_rate()
             else:
                 res["cpu_baseline"] = cpu_scan_rate(16, 4096, 1024)
         if rank == 0 and res is not None:

@@ -302,8 +302,9 @@ TP_API int tp_convert_bf16_to_f32(int64_t n, const void* src, float* dst, void* 
  *  NaN-propagating max; form 3: two scalar adds + 3-input NaN max per two
  *  terms; form 4: forms 2 and 3 alternating; form 5: packed add.bf16x2 +
  *  max.bf16x2 per two terms (bf16 arithmetic); form 6: form 5 with the
- *  NaN-propagating max.  Each of `threads` threads runs `iters` iterations
- *  of 128 terms; the caller times the launch.  sink receives one float per
+ *  NaN-propagating max; form 7: fp32 fma (a term is one FMA, 2 flops: the
+ *  CUDA-core peak of dot products).  Each of `threads` threads runs `iters`
+ *  iterations of 128 terms; the caller times the launch.  sink receives one float per
  *  thread (keeps the work live).
  * ======================================================================== */
 TP_API int tp_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters,

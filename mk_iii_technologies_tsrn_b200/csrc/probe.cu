@@ -16,6 +16,8 @@
 //   form 5: add.rn.bf16x2 + 2-input max.bf16x2 per two terms (packed bf16
 //           arithmetic; there is no 3-input packed max)
 //   form 6: add.rn.bf16x2 + max.NaN.bf16x2
+//   form 7: fp32 fused multiply-add (two per accumulator and iteration; one
+//           "term" = one FMA = 2 flops), the CUDA-core roofline of dot products
 #include "maxplus_internal.cuh"
 
 namespace tp {
@@ -141,6 +143,37 @@ __global__ void __launch_bounds__(256) probe_bf16_kernel(int64_t iters, float* s
   sink[t] = r;
 }
 
+__global__ void __launch_bounds__(256) probe_ffma_kernel(int64_t iters, float* sink) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  float a[8], b[8], acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    a[i] = (float)(t % 97) * 1e-3f + (float)i * 1e-2f;
+    b[i] = 1.0f - (float)(t % 89) * 1e-4f - (float)i * 1e-3f;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+  for (int64_t it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) asm volatile("add.rn.f32 %0, %0, 0f3A83126F;" : "+f"(a[i]));
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        asm volatile("fma.rn.f32 %0, %1, %2, %0;" : "+f"(acc[i][j]) : "f"(a[i]), "f"(b[j]));
+        asm volatile("fma.rn.f32 %0, %1, %2, %0;" : "+f"(acc[i][j]) : "f"(b[j]), "f"(a[i]));
+      }
+  }
+  float r = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r += acc[i][j];
+  sink[t] = r;
+}
+
 }  // namespace
 
 int launch_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters, float* sink,
@@ -158,8 +191,10 @@ int launch_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters
     probe_kernel<4><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
   else if (form == 5)
     probe_bf16_kernel<false><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
-  else
+  else if (form == 6)
     probe_bf16_kernel<true><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
+  else
+    probe_ffma_kernel<<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
   return launch_status();
 }
 

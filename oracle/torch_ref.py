@@ -92,3 +92,27 @@ def tropical_linear_fwd_bwd_torch(x: torch.Tensor, w: torch.Tensor, g: torch.Ten
     mx = (w.unsqueeze(0) + x.unsqueeze(1)).max(dim=-1)
     gx, gw = torch.autograd.grad(mx.values, (x, w), g)
     return mx.values.detach(), mx.indices, gx, gw
+
+
+def tsrn_attention_torch(Q, K, V, slopes, top_k: int, causal: bool = True, q_chunk: int = 64):
+    """TropicalAttention after RoPE on the reference's own torch expressions
+    (research/tsrn_dml.py:384-436 _attend_chunk: logsumexp score per query chunk,
+    ALiBi, causal mask, top-k threshold, softmax, @V), fp32.  CPU timing only."""
+    B, H, T, dh = Q.shape
+    Tkv = K.shape[2]
+    out = []
+    for qi in range(0, T, q_chunk):
+        q_end = min(qi + q_chunk, T)
+        Qq = Q[:, :, qi:q_end]
+        scores = torch.logsumexp(Qq.unsqueeze(3) + K.unsqueeze(2), dim=-1)
+        q_pos = torch.arange(qi, q_end)
+        k_pos = torch.arange(0, Tkv)
+        dist = (q_pos.unsqueeze(1) - k_pos.unsqueeze(0)).abs()
+        scores = scores - slopes.view(-1, 1, 1) * dist.unsqueeze(0)
+        if causal:
+            scores = scores.masked_fill((k_pos.unsqueeze(0) > q_pos.unsqueeze(1))[None, None],
+                                        float("-inf"))
+        thr = scores.topk(min(top_k, Tkv), dim=-1).values[..., -1:]
+        scores = scores.masked_fill(scores < thr, float("-inf"))
+        out.append(torch.softmax(scores, dim=-1) @ V)
+    return torch.cat(out, dim=2)
