@@ -72,6 +72,8 @@ def parse_args():
                         "(sums rounded to bf16, as the reference on bf16 tensors; packed "
                         "bf16x2 kernel)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--att-batch", type=int, default=64,
+                   help="sequences per rank of the tsrn_attn workload (64 = config 5)")
     p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                    help="N>1 GEMM: fused peer-store epilogue (p2p) or NCCL all-gather")
     return p.parse_args()
@@ -729,6 +731,7 @@ def tsrn_attn_workload(args, world, rank):
 
     _lib.load().tp_set_pointer_checks(0)
     B, H, T, dh, k = (TSRN_ATT[n] for n in ("B", "H", "T", "dh", "top_k"))
+    B = args.att_batch
     dev = torch.device("cuda")
     gen = torch.Generator().manual_seed(10 + rank)
     # LayerNorm'd, rotated Q and K have unit-variance entries; V as projected
