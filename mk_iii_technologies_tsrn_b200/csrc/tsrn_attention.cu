@@ -21,11 +21,13 @@
 // Main kernel: one CTA per R (16, or 8 when shared memory is short) query
 // rows of one (b, h).  Key tiles of 64
 // feature columns are double-buffered with cp.async; the CTA keeps its R x Tkv
-// score block in shared memory.  Then each warp takes R/8 rows: the k-th
-// largest score is found by rounds of (max below the previous value, count of
-// equal values) over the row in shared memory, the kept scores' softmax
-// weights are formed, and the weighted V rows are gathered (the kept entries
-// are broadcast one at a time; lanes split the dh channels).
+// score block in shared memory.  Then each warp takes R/8 rows: each lane
+// keeps its 4 largest scores and the warp pops the overall largest top_k times
+// (the last popped value is the k-th largest, ties counted); a row where one
+// lane held more than 4 of the top_k falls back to exact rounds (count the
+// current value, find the next smaller one).  The kept scores' softmax
+// weights are formed and the weighted V rows gathered (the kept entries are
+// broadcast one at a time; lanes split the dh channels).
 #include "maxplus_internal.cuh"
 
 namespace tp {
@@ -244,17 +246,63 @@ __global__ void __launch_bounds__(ATT_THREADS) att_fwd_kernel(AttArgs p) {
       float v[PL];
 #pragma unroll
       for (int u = 0; u < PL; ++u) v[u] = sval(lane + 32 * (int64_t)u);
-      // rounds: count the current value, find the next smaller one; the
+      // Fast selection: each lane keeps its 4 largest scores (sorted, NaN
+      // dropped); the warp pops the overall largest top_k times, one instance
+      // per pop, so the last popped value is the top_k-th largest counting
+      // ties.  If a lane runs out of candidates before the last pop (it held
+      // more than 4 of the top_k), the row falls back to the exact rounds below.
+      constexpr int NC = 4;
+      float cand[NC];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) cand[c] = NEG_INF;
+#pragma unroll
+      for (int u = 0; u < PL; ++u) {
+        float x = v[u];
+        if (x == x) {
+#pragma unroll
+          for (int c = 0; c < NC; ++c) {
+            const float hi = fmaxf(cand[c], x);
+            x = fminf(cand[c], x);
+            cand[c] = hi;
+          }
+        }
+      }
+      int popped = 0;
+      bool exhausted = false;
+      for (int round = 0; round < kk; ++round) {
+        float wm = cand[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+        if (round == 0) rowmax = wm;
+        thr = wm;
+        if (wm == NEG_INF) break;                 // everything left is -inf
+        const unsigned hold = __ballot_sync(0xffffffffu, cand[0] == wm);
+        const int win = __ffs(hold) - 1;
+        if (lane == win) {
+#pragma unroll
+          for (int c = 0; c < NC - 1; ++c) cand[c] = cand[c + 1];
+          cand[NC - 1] = NEG_INF;
+          ++popped;
+        }
+        // a lane that gave up all its candidates may hold more: exact path
+        if (round + 1 < kk && __any_sync(0xffffffffu, popped == NC)) {
+          exhausted = true;
+          break;
+        }
+      }
+      // exact rounds: count the current value, find the next smaller one; the
       // threshold is the value at which the running count reaches top_k
       float cur = NEG_INF;
-#pragma unroll
-      for (int u = 0; u < PL; ++u) cur = fmaxf(cur, v[u]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) cur = fmaxf(cur, __shfl_xor_sync(0xffffffffu, cur, o));
-      rowmax = cur;
-      thr = cur;
       int need = kk;
-      for (int round = 0; round < kk; ++round) {
+      if (exhausted) {
+#pragma unroll
+        for (int u = 0; u < PL; ++u) cur = fmaxf(cur, v[u]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) cur = fmaxf(cur, __shfl_xor_sync(0xffffffffu, cur, o));
+        rowmax = cur;
+        thr = cur;
+      }
+      for (int round = 0; exhausted && round < kk; ++round) {
         int cnt = 0;
         float nxt = NEG_INF;
         bool below = false;

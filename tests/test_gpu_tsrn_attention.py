@@ -81,3 +81,24 @@ def test_training_path_matches_fused(cuda):
     with torch.no_grad():
         y_eval = m(x)
     torch.testing.assert_close(y_train.detach(), y_eval, rtol=1e-4, atol=2e-5)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_fused_attention_one_lane_holds_the_top_k(cuda, causal):
+    # keys j = 0, 32, 64, ... (all owned by one lane of the selection warp) score
+    # highest, so that lane holds more than its 4 candidates: the exact path runs;
+    # integer-valued inputs also produce exact score ties
+    from mk_iii_technologies_tsrn_b200 import ops
+    B, H, T, dh, top_k = 1, 2, 256, 16, 8
+    rng = np.random.default_rng(12)
+    Q = rng.integers(-2, 3, (B, H, T, dh)).astype(np.float32)
+    K = rng.integers(-2, 3, (B, H, T, dh)).astype(np.float32)
+    K[:, :, ::32, :] += 6.0
+    V = rng.standard_normal((B, H, T, dh)).astype(np.float32)
+    slopes = np.zeros(H, np.float32)
+    out = ops.tsrn_attention(*(torch.tensor(a, device=cuda) for a in (Q, K, V, slopes)),
+                             top_k=top_k, causal=causal).cpu().numpy()
+    ref, S = oracle.tsrn_attention_fwd(Q, K, V, slopes, top_k, causal)
+    ok = ~_ambiguous_rows(S, top_k, gap=1e-5)
+    assert ok.mean() > 0.5
+    np.testing.assert_allclose(out[ok], ref[ok], rtol=1e-4, atol=2e-5)
