@@ -194,6 +194,17 @@ TP_API int tp_maxplus_bwd_smooth(int mode, float tau, int dtype,
                                  float* gx, float* gw, float* gbias,
                                  void* workspace, int64_t workspace_bytes, void* stream);
 
+/* The same, given the forward's maxima ref_max[b][m][n] = max_k (x + w) (before
+ * bias; NULL: computed here).  Saves the stats pass's own max sweep over K
+ * (a TropicalLinear forward has these values: the STE forward is the hard
+ * max).  Any finite ref_max close to the max gives the same gradients within
+ * the stated tolerance; a non-finite entry gives that output zero weight. */
+TP_API int tp_maxplus_bwd_smooth_ref(int mode, float tau, int dtype,
+                                     int64_t batch, int64_t M, int64_t N, int64_t K,
+                                     const void* x, const void* w, const float* gy,
+                                     const float* ref_max, float* gx, float* gw, float* gbias,
+                                     void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Kernel choice for a forward with argmax: problems with M*N*K below this many
  * terms (default 2^30) run the per-term generic kernel, larger contiguous fp32
  * ones the TMA kernel, whose deferred argmax search has a fixed cost of about

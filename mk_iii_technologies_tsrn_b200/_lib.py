@@ -69,6 +69,11 @@ SIGNATURES: dict[str, tuple] = {
         [_c_int, _c_f, _c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
          _c_p, _c_i64, _c_p],
     ),
+    "tp_maxplus_bwd_smooth_ref": (
+        _c_int,
+        [_c_int, _c_f, _c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
+         _c_p, _c_p, _c_i64, _c_p],
+    ),
     "tp_scan_fwd": (
         _c_int,
         [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p],

@@ -242,10 +242,10 @@ int64_t tp_maxplus_bwd_smooth_workspace_bytes(int64_t batch, int64_t M, int64_t 
   return tp::smooth_workspace_floats(batch, M, N, K) * (int64_t)sizeof(float);
 }
 
-int tp_maxplus_bwd_smooth(int mode, float tau, int dtype, int64_t batch, int64_t M, int64_t N,
-                          int64_t K, const void* x, const void* w, const float* gy, float* gx,
-                          float* gw, float* gbias, void* workspace, int64_t workspace_bytes,
-                          void* stream) {
+int tp_maxplus_bwd_smooth_ref(int mode, float tau, int dtype, int64_t batch, int64_t M,
+                              int64_t N, int64_t K, const void* x, const void* w, const float* gy,
+                              const float* ref_max, float* gx, float* gw, float* gbias,
+                              void* workspace, int64_t workspace_bytes, void* stream) {
   TP_RETURN_IF(mode != TP_BWD_STE && mode != TP_BWD_LSE, TP_ERR_INVALID_ARG);
   TP_RETURN_IF(!(tau > 0.0f), TP_ERR_INVALID_ARG);
   TP_RETURN_IF(dtype != TP_DTYPE_F32 && dtype != TP_DTYPE_BF16, TP_ERR_UNSUPPORTED);
@@ -267,12 +267,21 @@ int tp_maxplus_bwd_smooth(int mode, float tau, int dtype, int64_t batch, int64_t
   if (M * K > 0) TP_CHECK_PTR(gx);
   if (N * K > 0) TP_CHECK_OPT_PTR(gw);
   TP_CHECK_OPT_PTR(gbias);
+  TP_CHECK_OPT_PTR(ref_max);
   const bool async_stage = dtype == TP_DTYPE_F32 && M % 4 == 0 && N % 4 == 0 && K % 4 == 0 &&
                            aligned16(x) && aligned16(w);
   SmoothArgs p{mode, tau, dtype, batch, M, N, K, x, w, gy, gx, gw, gbias, (float*)workspace,
                async_stage, tp::smooth_splits(batch, M, N, K), tp::smooth_splits(batch, N, M, K),
-               (float*)workspace + 6 * batch * M * N};
+               (float*)workspace + 6 * batch * M * N, ref_max};
   return launch_maxplus_bwd_smooth(p, as_stream(stream));
+}
+
+int tp_maxplus_bwd_smooth(int mode, float tau, int dtype, int64_t batch, int64_t M, int64_t N,
+                          int64_t K, const void* x, const void* w, const float* gy, float* gx,
+                          float* gw, float* gbias, void* workspace, int64_t workspace_bytes,
+                          void* stream) {
+  return tp_maxplus_bwd_smooth_ref(mode, tau, dtype, batch, M, N, K, x, w, gy, nullptr, gx, gw,
+                                   gbias, workspace, workspace_bytes, stream);
 }
 
 int tp_scan_fwd(int64_t B, int64_t T, int64_t C, const float* bb, const float* xx, const float* a,

@@ -375,13 +375,25 @@ __global__ void __launch_bounds__(G_THREADS, 3) smooth_stats_kernel(SmoothArgs p
   const float NEG_INF = -__int_as_float(0x7f800000);
   const float L = kLog2e / p.tau;
 
-  // pass 0: refL = max_k (xL + wL)
+  // pass 0: refL = max_k (xL + wL) (or L times the forward's max, when given)
   float mx[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) mx[i][j] = NEG_INF;
-  for (int64_t k0 = 0; k0 < p.K; k0 += GB_K) {
+  if (p.ref) {
+    const float* rb = p.ref + bz * p.M * p.N;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t m = m0 + 4 * ty + i;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t n = n0 + 4 * tx + j;
+        if (m < p.M && n < p.N) mx[i][j] = rb[m * p.N + n] * L;
+      }
+    }
+  }
+  for (int64_t k0 = 0; !p.ref && k0 < p.K; k0 += GB_K) {
     __syncthreads();
     load_slab_scaled<T>(xs, xg, p.M, p.K, m0, k0, NEG_INF, L);
     load_slab_scaled<T>(ws, wg, p.N, p.K, n0, k0, 0.0f, L);
@@ -532,13 +544,24 @@ __global__ void __launch_bounds__(G_THREADS, 3) smooth_stats_async_kernel(Smooth
     }
   };
 
-  // pass 0: raw max of x + w
+  // pass 0: raw max of x + w (or the forward's, when given)
   float mx[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) mx[i][j] = NEG_INF;
-  sweep([&](int b, int kn) {
+  if (p.ref) {
+    const float* rb = p.ref + bz * p.M * p.N;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t m = m0 + 4 * ty + i;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t n = n0 + 4 * tx + j;
+        if (m < p.M && n < p.N) mx[i][j] = rb[m * p.N + n];
+      }
+    }
+  } else sweep([&](int b, int kn) {
     for (int kk = 0; kk < kn; ++kk) {
       const float4 a4 = lds_f4(&xs[b][kk][4 * ty]);
       const float4 b4 = lds_f4(&ws[b][kk][4 * tx]);

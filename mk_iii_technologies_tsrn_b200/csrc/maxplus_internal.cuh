@@ -58,6 +58,9 @@ struct SmoothArgs {
   // and are added in split order.
   int64_t splits_x, splits_w;
   float* part;
+  // optional [batch][M][N] maxima max_k(x + w) from the forward: the stats
+  // pass then skips its own max pass
+  const float* ref;
 };
 
 // Number of slices the smooth backward cuts the reduced index Q into for an

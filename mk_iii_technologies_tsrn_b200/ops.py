@@ -248,7 +248,7 @@ def maxplus_backward_argmax(am: torch.Tensor, gy: torch.Tensor, K: int, *,
 
 def maxplus_backward_smooth(mode: str, tau: float, x: torch.Tensor, w: torch.Tensor,
                             gy: torch.Tensor, *, need_gw: bool = True,
-                            need_gbias: bool = False):
+                            need_gbias: bool = False, ref_max: Optional[torch.Tensor] = None):
     """STE (``tropformer.py:133-139``) or LSE/Maslov (``tropformer.py:95-97``) backward.
 
     ``x`` [B?, M, K], ``w`` [B?, N, K], ``gy`` [B?, M, N] (contiguous copies are made
@@ -268,6 +268,10 @@ def maxplus_backward_smooth(mode: str, tau: float, x: torch.Tensor, w: torch.Ten
     N = w.shape[1]
     if w.shape != (B, N, K) or gy.shape != (B, M, N):
         raise ValueError("shape mismatch in smooth backward")
+    if ref_max is not None:
+        ref_max = _f32(ref_max).contiguous()
+        if ref_max.numel() != B * M * N:
+            raise ValueError("ref_max must hold the [.., M, N] forward maxima")
     lib = _lib.load()
     ws_bytes = int(lib.tp_maxplus_bwd_smooth_workspace_bytes(B, M, N, K))
     ws = torch.empty(max(ws_bytes // 4, 4), device=dev, dtype=torch.float32)
@@ -275,11 +279,11 @@ def maxplus_backward_smooth(mode: str, tau: float, x: torch.Tensor, w: torch.Ten
     gw = torch.empty((B, N, K), device=dev, dtype=torch.float32) if need_gw else None
     gb = torch.empty((N,), device=dev, dtype=torch.float32) if need_gbias else None
     with torch.cuda.device(dev):
-        st = lib.tp_maxplus_bwd_smooth(
+        st = lib.tp_maxplus_bwd_smooth_ref(
             TP_BWD_STE if mode == "ste" else TP_BWD_LSE, float(tau), code, B, M, N, K,
-            _ptr(x), _ptr(w), _ptr(gy), _ptr(gx), _ptr(gw), _ptr(gb),
+            _ptr(x), _ptr(w), _ptr(gy), _ptr(ref_max), _ptr(gx), _ptr(gw), _ptr(gb),
             _ptr(ws), ws.numel() * 4, _stream(dev))
-    _lib.check(st, "tp_maxplus_bwd_smooth")
+    _lib.check(st, "tp_maxplus_bwd_smooth_ref")
     if squeeze:
         gx = gx[0]
         gw = gw[0] if gw is not None else None
@@ -359,14 +363,17 @@ class MaxPlusLinearFunction(torch.autograd.Function):
     def forward(ctx, x, weight, bias, mode: str, tau: float):
         if mode not in MODES:
             raise ValueError(f"mode must be one of {MODES}")
-        y, am = maxplus(x, weight, bias, argmax=(mode == "argmax"))
         ctx.mode, ctx.tau, ctx.K = mode, float(tau), x.shape[1]
         ctx.has_bias = bias is not None
         if mode == "argmax":
+            y, am = maxplus(x, weight, bias, argmax=True)
             ctx.save_for_backward(am)
-        else:
-            ctx.save_for_backward(x, weight)
-        return y
+            return y
+        # smooth modes: keep the hard max (before bias): the backward's stats
+        # pass starts from it instead of sweeping K for it again
+        y0, _ = maxplus(x, weight, None, argmax=False)
+        ctx.save_for_backward(x, weight, y0)
+        return y0 + bias if bias is not None else y0.clone()
 
     @staticmethod
     def backward(ctx, gy):
@@ -377,9 +384,10 @@ class MaxPlusLinearFunction(torch.autograd.Function):
             gx, gw, gb = maxplus_backward_argmax(am, gy, ctx.K, need_gw=need_w,
                                                  need_gbias=need_b and ctx.needs_input_grad[2])
         else:
-            x, w = ctx.saved_tensors
+            x, w, y0 = ctx.saved_tensors
             gx, gw, gb = maxplus_backward_smooth(ctx.mode, ctx.tau, x, w, gy, need_gw=need_w,
-                                                 need_gbias=need_b and ctx.needs_input_grad[2])
+                                                 need_gbias=need_b and ctx.needs_input_grad[2],
+                                                 ref_max=y0)
         return (gx if need_x else None), gw, gb, None, None
 
 

@@ -128,3 +128,19 @@ def test_smooth_split_reduction(cuda, batch, M, N, K):
         assert _rel_err(gx[b].cpu().numpy(), rgx) < 1e-5
         assert _rel_err(gw[b].cpu().numpy(), rgw) < 1e-5
     np.testing.assert_allclose(gb.cpu().numpy(), g.sum(axis=(0, 1)), rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("M,N,K", [(512, 256, 256), (96, 72, 40)])
+def test_smooth_backward_with_forward_max(cuda, dtype, M, N, K):
+    # the stats pass seeded with the forward's maxima gives the same gradients
+    ops = _fn()
+    rng = np.random.default_rng(8)
+    x = torch.tensor(rng.standard_normal((M, K)).astype(np.float32), device=cuda).to(dtype)
+    w = torch.tensor(rng.standard_normal((N, K)).astype(np.float32), device=cuda).to(dtype)
+    g = torch.tensor(rng.standard_normal((M, N)).astype(np.float32), device=cuda)
+    y0, _ = ops.maxplus(x.float(), w.float(), argmax=False)
+    a = ops.maxplus_backward_smooth("ste", 0.7, x, w, g)
+    b = ops.maxplus_backward_smooth("ste", 0.7, x, w, g, ref_max=y0)
+    for u, v in zip(a[:2], b[:2]):
+        assert _rel_err(v.cpu().numpy(), u.cpu().numpy()) < 1e-5
