@@ -97,6 +97,24 @@ TP_API int tp_maxplus_fwd(int dtype, int64_t M, int64_t N, int64_t K,
                    int32_t* argmax, int64_t ld_argmax,
                    void* stream);
 
+/* Tropical linear followed by its Legendre-Fenchel dual activation, fused
+ * into the forward epilogue (inference: values only, no argmax).
+ * Replaces trop_up + lf_act of TropicalHybridFFN / DTNHybridFFN
+ * (tropformer.py:447, deep_tropical_net.py:206; LFDualActivation,
+ * tropformer.py:224-289):  v = max_k(x + w) + bias, then
+ *   act_mode 0 (primal):  max_p (v*slopes[p] + piece_bias[p])
+ *   act_mode 1 (dual):    max_p (v*x_grid[p] - f(x_grid[p])), f the primal
+ *   act_mode 2 (blend):   gate[n]*primal + (1 - gate[n])*dual, gate = sigmoid(blend_gate)
+ * Products and sums are rounded separately, as the reference evaluates them,
+ * so the result is bit-exact with it (given the same gate values).
+ * pieces <= 16; slopes, piece_bias, x_grid, gate are device arrays. */
+TP_API int tp_maxplus_fwd_lfdual(int dtype, int64_t M, int64_t N, int64_t K,
+                                 const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                 const float* bias, float* y, int64_t ldy,
+                                 int act_mode, int pieces, const float* slopes,
+                                 const float* piece_bias, const float* x_grid,
+                                 const float* gate, void* stream);
+
 /* Fully strided, two-level batched form of tp_maxplus_fwd.  Batch index
  * (b1, b2) in [0,B1) x [0,B2) offsets every operand by b1*s_b1 + b2*s_b2;
  * element (m,k) of x is x[m*sx_m + k*sx_k], element (n,k) of w is

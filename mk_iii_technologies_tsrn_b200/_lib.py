@@ -40,6 +40,11 @@ SIGNATURES: dict[str, tuple] = {
          _c_p, _c_i64, _c_i64, _c_i64, _c_i64,
          _c_f, _c_p],
     ),
+    "tp_maxplus_fwd_lfdual": (
+        _c_int,
+        [_c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_i64,
+         _c_int, _c_int, _c_p, _c_p, _c_p, _c_p, _c_p],
+    ),
     "tp_maxplus_fwd_sharded": (
         _c_int,
         [_c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_p, _c_p, _c_int, _c_i64,

@@ -151,6 +151,39 @@ int tp_maxplus_fwd(int dtype, int64_t M, int64_t N, int64_t K, const void* x, in
                                 0, ldy, 1, argmax, 0, 0, ld_argmax, 1, 1.0f, stream);
 }
 
+int tp_maxplus_fwd_lfdual(int dtype, int64_t M, int64_t N, int64_t K, const void* x,
+                          int64_t ldx, const void* w, int64_t ldw, const float* bias, float* y,
+                          int64_t ldy, int act_mode, int pieces, const float* slopes,
+                          const float* piece_bias, const float* x_grid, const float* gate,
+                          void* stream) {
+  TP_RETURN_IF(M < 0 || N < 0 || K < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF((M > 0 && K > 0 && ldx < K) || (N > 0 && K > 0 && ldw < K) || (M > 0 && ldy < N),
+               TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(act_mode < 0 || act_mode > 2, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(pieces < 1 || pieces > LF_MAX_PIECES, TP_ERR_INVALID_ARG);
+  StridedMaxPlus p{dtype, 1, 1, M, N, K, x, 0, 0, ldx, 1, w, 0, 0, ldw, 1, bias, y, 0, 0, ldy, 1,
+                   nullptr, 0, 0, 0, 0, 1.0f, 1.0f};
+  p.act = LfAct{act_mode, pieces, slopes, piece_bias, x_grid, gate};
+  int s = validate_strided(p);
+  if (s != TP_OK) return s;
+  if (M * N == 0) return TP_OK;
+  TP_CHECK_PTR(y);
+  TP_CHECK_OPT_PTR(bias);
+  TP_CHECK_PTR(slopes);
+  TP_CHECK_PTR(piece_bias);
+  TP_CHECK_PTR(x_grid);
+  if (act_mode == 2) TP_CHECK_PTR(gate);
+  if (K > 0) {
+    TP_CHECK_PTR(x);
+    TP_CHECK_PTR(w);
+  }
+  if (maxplus_tma_eligible(p)) {
+    s = launch_maxplus_fwd_tma(p, as_stream(stream));
+    if (s != TP_ERR_UNSUPPORTED) return s;
+  }
+  return launch_maxplus_fwd_generic(p, as_stream(stream));
+}
+
 int tp_maxplus_fwd_sharded(int64_t M, int64_t N_shard, int64_t K, const float* x, int64_t ldx,
                            const float* w_shard, int64_t ldw, const float* bias_shard,
                            float* const* y_dst, int32_t* const* argmax_dst, int n_dst,

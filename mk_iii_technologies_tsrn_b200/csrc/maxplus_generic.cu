@@ -68,6 +68,11 @@ __global__ void __launch_bounds__(G_THREADS)
     maxplus_fwd_generic_kernel(StridedMaxPlus p) {
   __shared__ float xs[GB_K][GB_M + 4];
   __shared__ float ws[GB_K][GB_N + 4];
+  __shared__ float lf_sm[64];
+  if (!kArgmax && p.act.mode >= 0) {
+    lf_stage(p.act, lf_sm);
+    __syncthreads();
+  }
   const int tx = threadIdx.x % 16;
   const int ty = threadIdx.x / 16;
   const int64_t m0 = (int64_t)blockIdx.y * GB_M;
@@ -135,6 +140,7 @@ __global__ void __launch_bounds__(G_THREADS)
         float v = acc[i][j];
         if (p.bias) v = v + p.bias[n];
         if (p.scale != 1.0f) v = v * p.scale;
+        if (!kArgmax && p.act.mode >= 0) v = lf_apply(p.act, lf_sm, n, v);
         yb[m * p.sy_m + n * p.sy_n] = v;
         if (kArgmax) ab[m * p.sa_m + n * p.sa_n] = idx[i][j];
       }

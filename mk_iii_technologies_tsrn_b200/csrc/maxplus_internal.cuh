@@ -7,6 +7,66 @@
 namespace tp {
 
 // One strided, two-level batched max-plus problem (see tp_maxplus_fwd_strided).
+// Legendre-Fenchel dual activation applied in a forward epilogue
+// (tropformer.py:224-289, LFDualActivation), value only.  mode: -1 none,
+// 0 primal f(v) = max_k(v*s_k + b_k), 1 dual f*(v) = max_j(v*x_j - f(x_j)),
+// 2 blend g_n*f(v) + (1-g_n)*f*(v) with g = sigmoid(blend_gate) given per
+// output column.  Products and sums are separately rounded, as the reference
+// evaluates them (no fused multiply-add).
+constexpr int LF_MAX_PIECES = 16;
+struct LfAct {
+  int mode;
+  int pieces;
+  const float* s;       // [pieces] slopes
+  const float* b;       // [pieces] biases
+  const float* xg;      // [pieces] x grid
+  const float* gate;    // [N] sigmoid(blend_gate) (blend only)
+};
+
+// params staged in shared memory: sm[0..P) s, [16..) b, [32..) x_grid, [48..) f(x_j)
+__device__ __forceinline__ void lf_stage(const LfAct& a, float* sm) {
+  const int t = threadIdx.x;
+  if (t < a.pieces) {
+    sm[t] = a.s[t];
+    sm[16 + t] = a.b[t];
+    sm[32 + t] = a.xg[t];
+    const float x = a.xg[t];
+    float f = -__int_as_float(0x7f800000);
+    bool nan = false;
+    for (int k = 0; k < a.pieces; ++k) {
+      const float piece = __fadd_rn(__fmul_rn(x, a.s[k]), a.b[k]);
+      nan |= piece != piece;
+      f = fmaxf(f, piece);
+    }
+    sm[48 + t] = nan ? __int_as_float(0x7fc00000) : f;
+  }
+}
+
+__device__ __forceinline__ float lf_apply(const LfAct& a, const float* sm, int64_t n, float v) {
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  float p = NEG_INF, d = NEG_INF;
+  bool pnan = false, dnan = false;
+  if (a.mode != 1) {
+    for (int k = 0; k < a.pieces; ++k) {
+      const float piece = __fadd_rn(__fmul_rn(v, sm[k]), sm[16 + k]);
+      pnan |= piece != piece;
+      p = fmaxf(p, piece);
+    }
+    if (pnan) p = __int_as_float(0x7fc00000);
+    if (a.mode == 0) return p;
+  }
+  for (int j = 0; j < a.pieces; ++j) {
+    const float piece = __fsub_rn(__fmul_rn(v, sm[32 + j]), sm[48 + j]);
+    dnan |= piece != piece;
+    d = fmaxf(d, piece);
+  }
+  if (dnan) d = __int_as_float(0x7fc00000);
+  if (a.mode == 1) return d;
+  const float g = a.gate[n];
+  const float omg = __fsub_rn(1.0f, g);
+  return __fadd_rn(__fmul_rn(g, p), __fmul_rn(omg, d));
+}
+
 struct StridedMaxPlus {
   int dtype;
   int64_t B1, B2, M, N, K;
@@ -21,6 +81,7 @@ struct StridedMaxPlus {
   int64_t sa_b1, sa_b2, sa_m, sa_n;
   float scale;
   float tau;
+  LfAct act{-1, 0, nullptr, nullptr, nullptr, nullptr};   // forward epilogue (value only)
 };
 
 struct ScatterArgs {

@@ -122,6 +122,7 @@ struct TmaParams {
   int64_t col0;
   int m_tiles, n_tiles, k_tiles, num_tiles;
   int* err;
+  LfAct act;   // value-only epilogue activation (mode -1: none)
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mt, int& nt) {
@@ -244,6 +245,8 @@ __global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  __shared__ float lf_sm[64];
+  if (!kArgmax && p.act.mode >= 0) lf_stage(p.act, lf_sm);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -472,6 +475,7 @@ __global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
           float v = acc[i][j];
           if (p.bias) v = v + p.bias[n];
           if (p.scale != 1.0f) v = v * p.scale;
+          if (p.act.mode >= 0) v = lf_apply(p.act, lf_sm, n, v);
           p.y[m * p.ldy + n] = v;
           for (int d = 0; d < p.ndst; ++d) p.ydst[d][m * p.ldy + p.col0 + n] = v;
         }
@@ -996,6 +1000,7 @@ int64_t set_argmax_tma_min_terms(int64_t terms) {
 }
 
 bool maxplus_tma_eligible(const StridedMaxPlus& p) {
+  if (p.act.mode >= 0 && (p.am || p.dtype != TP_DTYPE_F32)) return false;
   if (p.dtype == TP_DTYPE_BF16_ARITH) {
     // packed bf16x2 kernel: 16-byte aligned bf16 rows
     if (p.B1 * p.B2 != 1) return false;
@@ -1065,6 +1070,7 @@ int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
   tp_.err = device_error_ptr();
   tp_.ndst = ndst;
   tp_.col0 = col0;
+  tp_.act = p.act;
   for (int d = 0; d < MAX_DESTS; ++d) {
     tp_.ydst[d] = d < ndst ? ydst[d] : nullptr;
     tp_.adst[d] = (d < ndst && adst) ? adst[d] : nullptr;

@@ -13,7 +13,7 @@ import torch
 import torch.nn as nn
 
 from . import tropical
-from .tropical import MaslovTemperature, TropicalLinear
+from .tropical import LFDualActivation, MaslovTemperature, TropicalLinear, tropical_up_lf
 
 
 class DTNAttention(nn.Module):
@@ -53,3 +53,30 @@ class DTNAttention(nn.Module):
         attn = self.attn_dropout(self.maslov(scores))
         out = torch.matmul(attn, V).transpose(1, 2).contiguous().view(B, L, D)
         return self.out_proj(out), attn
+
+
+class DTNHybridFFN(nn.Module):
+    """Tropical-biased hybrid FFN (deep_tropical_net.py:172-211): tropical branch
+    TropicalLinear -> LFDualActivation -> dropout, classical Linear -> GELU,
+    g * trop + (1 - g) * classical with g = sigmoid(gate_proj(x)) (bias +2)."""
+
+    def __init__(self, d_model: int, ffn_dim: int, dropout: float = 0.1, lf_pieces: int = 8,
+                 lf_mode: str = "blend"):
+        super().__init__()
+        self.trop_up = TropicalLinear(d_model, ffn_dim)
+        self.lf_act = LFDualActivation(ffn_dim, num_pieces=lf_pieces, mode=lf_mode)
+        self.trop_drop = nn.Dropout(dropout)
+        self.class_up = nn.Linear(d_model, ffn_dim)
+        self.gelu = nn.GELU()
+        self.gate_proj = nn.Linear(d_model, ffn_dim)
+        nn.init.zeros_(self.gate_proj.weight)
+        nn.init.constant_(self.gate_proj.bias, +2.0)
+        self.down_proj = nn.Linear(ffn_dim, d_model)
+        self.dropout = nn.Dropout(dropout)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        trop = self.trop_drop(tropical_up_lf(self.trop_up, self.lf_act, x))
+        classical = self.gelu(self.class_up(x))
+        g = torch.sigmoid(self.gate_proj(x))
+        fused = g * trop + (1.0 - g) * classical
+        return self.dropout(self.down_proj(fused))

@@ -178,6 +178,43 @@ def maxplus(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = Non
     return maxplus_strided(x, w, bias, argmax=argmax, arith=arith)
 
 
+LF_MODES = {"primal": 0, "dual": 1, "blend": 2}
+
+
+def maxplus_lfdual(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
+                   mode: str, slopes: torch.Tensor, piece_bias: torch.Tensor,
+                   x_grid: torch.Tensor, gate: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``lf_act(max_k(x + w) + bias)`` in one kernel (inference): the tropical
+    up-projection and LFDualActivation of TropicalHybridFFN (tropformer.py:447).
+
+    ``gate`` = sigmoid(blend_gate) [N] for mode "blend"."""
+    dev = _require_cuda(x, w, bias, slopes, piece_bias, x_grid, gate)
+    if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1]:
+        raise ValueError("maxplus_lfdual takes x [M,K] and w [N,K]")
+    if mode not in LF_MODES:
+        raise ValueError(f"mode must be one of {tuple(LF_MODES)}")
+    x, w = _f32(x).contiguous(), _f32(w).contiguous()
+    M, K = x.shape
+    N = w.shape[0]
+    sl, pb, xg = (_f32(t).contiguous() for t in (slopes, piece_bias, x_grid))
+    if not (sl.numel() == pb.numel() == xg.numel()):
+        raise ValueError("slopes, biases and x_grid must have the same length")
+    if bias is not None:
+        bias = _f32(bias).contiguous()
+    if mode == "blend":
+        if gate is None or gate.numel() != N:
+            raise ValueError("blend mode needs gate [N]")
+        gate = _f32(gate).contiguous()
+    y = torch.empty((M, N), device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        st = _lib.load().tp_maxplus_fwd_lfdual(
+            TP_DTYPE_F32, M, N, K, _ptr(x), x.stride(0), _ptr(w), w.stride(0), _ptr(bias),
+            _ptr(y), N, LF_MODES[mode], sl.numel(), _ptr(sl), _ptr(pb), _ptr(xg),
+            _ptr(gate if mode == "blend" else None), _stream(dev))
+    _lib.check(st, "tp_maxplus_fwd_lfdual")
+    return y
+
+
 def tropical_scores(Q: torch.Tensor, K: torch.Tensor, scale: float = 1.0, *, argmax: bool = True):
     """``S[..., i, j] = max_f(Q[..., i, f] + K[..., j, f]) * scale`` (+ int32 argmax f)."""
     return maxplus_strided(Q, K, None, argmax=argmax, scale=scale)

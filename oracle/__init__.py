@@ -19,6 +19,7 @@ from .maxplus import (  # noqa: F401
     maxplus_fwd_bf16,
     round_bf16,
     tsrn_attention_fwd,
+    lfdual_act,
     maxplus_bwd_argmax,
     maxplus_bwd_smooth,
     maxplus_lse_fwd,

@@ -179,3 +179,22 @@ def tsrn_attention_fwd(Q, K, V, slopes, top_k: int, causal: bool = True, Tc: int
         w = np.exp(Sm - mx)
         w = w / w.sum(axis=-1, keepdims=True)
     return w @ V, S
+
+
+def lfdual_act(y, mode: str, slopes, biases, x_grid, blend_gate=None):
+    """LFDualActivation (tropformer.py:224-289) in float32, each product and sum
+    rounded separately as torch evaluates the reference expressions."""
+    y = np.asarray(y, np.float32)
+    s = np.asarray(slopes, np.float32)
+    b = np.asarray(biases, np.float32)
+    xg = np.asarray(x_grid, np.float32)
+    with np.errstate(invalid="ignore", over="ignore"):
+        primal = (y[..., None] * s + b).max(axis=-1)
+        f_at_grid = (xg[:, None] * s + b).max(axis=-1)
+        dual = (y[..., None] * xg - f_at_grid).max(axis=-1)
+    if mode == "primal":
+        return primal
+    if mode == "dual":
+        return dual
+    g = (1.0 / (1.0 + np.exp(-np.asarray(blend_gate, np.float64)))).astype(np.float32)
+    return (g * primal + (np.float32(1.0) - g) * dual).astype(np.float32)

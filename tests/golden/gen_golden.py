@@ -248,6 +248,53 @@ def gen_tsrn(research):
           H=_np(Hs), A_c=_np(A_c), **state, **grads)
 
 
+def gen_lfdual(trop, dtn):
+    # TropicalLinear (eval, with bias) followed by LFDualActivation in each mode
+    # (tropformer.py:224-289), and the two hybrid FFNs (tropformer.py:407-456,
+    # deep_tropical_net.py:172-211) in eval mode with non-default parameters
+    torch.manual_seed(9)
+    d, ffn, M = 24, 40, 30
+    x = torch.randn(M, d)
+    out = {"x": _np(x)}
+    lin = trop.TropicalLinear(d, ffn)
+    with torch.no_grad():
+        lin.weight.normal_(0.0, 0.7)
+        lin.bias.normal_(0.0, 0.5)
+    lin.eval()
+    out["W"], out["b"] = _np(lin.weight), _np(lin.bias)
+    with torch.no_grad():
+        y = lin(x)
+    for mode in ("primal", "dual", "blend"):
+        act = trop.LFDualActivation(ffn, num_pieces=8, mode=mode)
+        with torch.no_grad():
+            act.slopes.add_(torch.randn(8) * 0.3)
+            act.biases.normal_(0.0, 0.4)
+            act.x_grid.add_(torch.randn(8) * 0.2)
+            if mode == "blend":
+                act.blend_gate.normal_(0.0, 1.0)
+            out[f"{mode}_out"] = _np(act(y))
+        out[f"{mode}_slopes"] = _np(act.slopes)
+        out[f"{mode}_biases"] = _np(act.biases)
+        out[f"{mode}_x_grid"] = _np(act.x_grid)
+        if mode == "blend":
+            out["blend_gate"] = _np(act.blend_gate)
+    _save("lfdual", **out)
+    for name, cls in (("ffn_tropformer", trop.TropicalHybridFFN),
+                      ("ffn_dtn", dtn.DTNHybridFFN)):
+        torch.manual_seed(10)
+        ffn_mod = cls(d, ffn)
+        with torch.no_grad():
+            for pname, prm in ffn_mod.named_parameters():
+                if "lf_act" in pname or "gate_proj" in pname:
+                    prm.add_(torch.randn_like(prm) * 0.3)
+        ffn_mod.eval()
+        xx = torch.randn(2, 7, d)
+        with torch.no_grad():
+            yy = ffn_mod(xx)
+        state = {f"p_{k}": _np(v) for k, v in ffn_mod.state_dict().items()}
+        _save(name, x=_np(xx), out=_np(yy), **state)
+
+
 def gen_tsrn_attention(research):
     # research TropicalAttention (research/tsrn_dml.py:355-548), eval, causal,
     # fast path: the module output, the Wo input (the attention context) and
@@ -287,6 +334,7 @@ def main():
     gen_kat(trop)
     gen_linear(trop)
     gen_bf16(trop)
+    gen_lfdual(trop, dtn)
     gen_scores(trop, dtn)
     gen_tsrn(research)
     gen_tsrn_attention(research)

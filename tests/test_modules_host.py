@@ -69,3 +69,15 @@ def test_tsrn_attention_state_dict_matches_reference():
     assert sorted(m.state_dict().keys()) == ref_keys
     m.load_state_dict({k: torch.tensor(g["p_" + k]) for k in ref_keys})
     np.testing.assert_allclose(m.alibi_slopes.numpy(), g["slopes"])
+
+
+@pytest.mark.parametrize("name,cls", [("ffn_tropformer", "TropicalHybridFFN"),
+                                      ("ffn_dtn", "DTNHybridFFN")])
+def test_hybrid_ffn_state_dict_matches_reference(name, cls):
+    from conftest import load_golden
+    from mk_iii_technologies_tsrn_b200 import dtn, tropical
+    g = load_golden(name)
+    mod = (tropical.TropicalHybridFFN if cls == "TropicalHybridFFN" else dtn.DTNHybridFFN)(24, 40)
+    ref_keys = sorted(k[2:] for k in g.keys() if k.startswith("p_"))
+    assert sorted(mod.state_dict().keys()) == ref_keys
+    mod.load_state_dict({k: torch.tensor(g["p_" + k]) for k in ref_keys})

@@ -196,3 +196,15 @@ def test_tsrn_attention_oracle_pinned():
     assert amb.mean() < 0.05
     ok = ~amb
     np.testing.assert_allclose(out[ok], g["ctx"][ok], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("mode", ["primal", "dual", "blend"])
+def test_lfdual_oracle_pinned(mode):
+    g = load_golden("lfdual")
+    y, _ = oracle.maxplus_fwd(g["x"], g["W"], g["b"])
+    out = oracle.lfdual_act(y, mode, g[f"{mode}_slopes"], g[f"{mode}_biases"],
+                            g[f"{mode}_x_grid"], g.get("blend_gate"))
+    if mode == "blend":      # sigmoid: numpy vs torch may differ in the last place
+        np.testing.assert_allclose(out, g[f"{mode}_out"], rtol=1e-6, atol=1e-6)
+    else:
+        np.testing.assert_array_equal(out, g[f"{mode}_out"])
