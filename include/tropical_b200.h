@@ -256,6 +256,37 @@ TP_API int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, i
                                  void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ======================================================================== *
+ *  Echo-state reservoir recurrences, forward (inference), whole sequence in
+ *  one launch.  h_{-1} = 0; for t = 0..T-1, H[:, t] = h_t.
+ *
+ *  tp_esn_gru_fwd replaces the per-timestep loop of the GRU-gated
+ *  EchoStateReservoir.forward (research/tsrn_dml.py:808-843, loop :834-840):
+ *    z = sigmoid(h Wzh^T + Uz_t);  r = sigmoid(h Wrh^T + Ur_t)
+ *    h~ = tanh((r * h) Ws^T + U_t);  h = (1 - z) * h + z * h~
+ *  with U = W_in(x), Uz = U Wz_u^T + b_z, Ur = U Wr_u^T + b_r.
+ *
+ *  tp_esn_leaky_fwd replaces the loop of the leaky EchoStateReservoir.forward
+ *  (tsrn_gpu.py:466-487):  h = (1 - lk) * h + lk * tanh(h Ws^T + U_t),
+ *  U = W_in(x); `leak` points to the device scalar lk = sigmoid(leak).
+ *
+ *  U, Uz, Ur, H: [B, T, dr] contiguous fp32.  Weights [dr, dr] with row
+ *  stride ld >= dr (Wzh / Wrh may be the first dr columns of W_z / W_r
+ *  weights in place: ld = 2 dr); Ws = the spectrally scaled W_res.  Each
+ *  group of batch rows runs on one thread-block cluster (no grid barrier, no
+ *  waits beyond hardware cluster barriers).  Weights that do not fit in
+ *  shared memory are read from L2, which needs dr and ld multiples of 4 and
+ *  16-byte aligned weights (else TP_ERR_UNSUPPORTED).  Matches the reference
+ *  within the fp32 rounding of the dot products (summation order) and of
+ *  sigmoid / tanh (1e-5 on h).
+ * ======================================================================== */
+TP_API int tp_esn_gru_fwd(int64_t B, int64_t T, int64_t dr, const float* U, const float* Uz,
+                          const float* Ur, const float* Wzh, int64_t ld_wzh, const float* Wrh,
+                          int64_t ld_wrh, const float* Ws, int64_t ld_ws, float* H,
+                          void* stream);
+TP_API int tp_esn_leaky_fwd(int64_t B, int64_t T, int64_t dr, const float* U, const float* Ws,
+                            int64_t ld_ws, const float* leak, float* H, void* stream);
+
+/* ======================================================================== *
  *  Tropical (max-plus) diagonal SSM scan  (research/tsrn_dml.py:917-980)
  *
  *    u[b,t,c] = bb[b,t,c] + xx[b,t,c]     (xx may be NULL: u = bb)

@@ -100,6 +100,13 @@ SIGNATURES: dict[str, tuple] = {
         None, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_f, _c_int, _c_int, _c_int]),
     "maxplus_matmul_cuda": (None, [_c_p, _c_p, _c_p, _c_int, _c_int, _c_int]),
     "tp_set_argmax_tma_min_terms": (_c_i64, [_c_i64]),
+    "tp_esn_gru_fwd": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p,
+         _c_p],
+    ),
+    "tp_esn_leaky_fwd": (
+        _c_int, [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_p]),
     "tp_tsrn_attention_workspace_bytes": (_c_i64, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64]),
     "tp_tsrn_attention_fwd": (
         _c_int,

@@ -437,6 +437,39 @@ int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t 
                                        causal, out, (float*)workspace, as_stream(stream));
 }
 
+int tp_esn_gru_fwd(int64_t B, int64_t T, int64_t dr, const float* U, const float* Uz,
+                   const float* Ur, const float* Wzh, int64_t ld_wzh, const float* Wrh,
+                   int64_t ld_wrh, const float* Ws, int64_t ld_ws, float* H, void* stream) {
+  TP_RETURN_IF(B < 0 || T < 0 || dr < 0, TP_ERR_INVALID_ARG);
+  if (B * T * dr == 0) return TP_OK;
+  TP_RETURN_IF(ld_wzh < dr || ld_wrh < dr || ld_ws < dr, TP_ERR_INVALID_ARG);
+  TP_CHECK_PTR(U);
+  TP_CHECK_PTR(Uz);
+  TP_CHECK_PTR(Ur);
+  TP_CHECK_PTR(Wzh);
+  TP_CHECK_PTR(Wrh);
+  TP_CHECK_PTR(Ws);
+  TP_CHECK_PTR(H);
+  const float* W[3] = {Wzh, Wrh, Ws};
+  const int64_t ld[3] = {ld_wzh, ld_wrh, ld_ws};
+  return tp::launch_esn_fwd(true, B, T, dr, U, Uz, Ur, W, ld, nullptr, H, as_stream(stream));
+}
+
+int tp_esn_leaky_fwd(int64_t B, int64_t T, int64_t dr, const float* U, const float* Ws,
+                     int64_t ld_ws, const float* leak, float* H, void* stream) {
+  TP_RETURN_IF(B < 0 || T < 0 || dr < 0, TP_ERR_INVALID_ARG);
+  if (B * T * dr == 0) return TP_OK;
+  TP_RETURN_IF(ld_ws < dr, TP_ERR_INVALID_ARG);
+  TP_CHECK_PTR(U);
+  TP_CHECK_PTR(Ws);
+  TP_CHECK_PTR(leak);
+  TP_CHECK_PTR(H);
+  const float* W[3] = {Ws, nullptr, nullptr};
+  const int64_t ld[3] = {ld_ws, 0, 0};
+  return tp::launch_esn_fwd(false, B, T, dr, U, nullptr, nullptr, W, ld, leak, H,
+                            as_stream(stream));
+}
+
 int64_t tp_set_argmax_tma_min_terms(int64_t terms) { return tp::set_argmax_tma_min_terms(terms); }
 
 int tp_last_error(void) { return last_error(); }

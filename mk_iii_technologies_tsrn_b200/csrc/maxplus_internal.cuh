@@ -189,4 +189,10 @@ int launch_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int6
                               const float* slopes, int top_k, int causal, float* out,
                               float* ws, cudaStream_t stream);
 
+// esn.cu: echo-state reservoir recurrences (GRU-gated when gru, else leaky);
+// W[0..2] = Wzh, Wrh, Ws for GRU, W[0] = Ws for leaky
+int launch_esn_fwd(bool gru, int64_t B, int64_t T, int64_t dr, const float* U, const float* Uz,
+                   const float* Ur, const float* const W[3], const int64_t ld[3],
+                   const float* leak, float* H, cudaStream_t stream);
+
 }  // namespace tp

@@ -571,3 +571,52 @@ def tsrn_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, slopes: to
                                        _ptr(ws), ws.numel() * 4, _stream(dev))
     _lib.check(st, "tp_tsrn_attention_fwd")
     return out
+
+
+# --------------------------------------------------------------------------- reservoir
+def _rows(w: torch.Tensor, dr: int) -> Tuple[torch.Tensor, int]:
+    """fp32 [dr, dr] weight view with unit column stride; returns (tensor, row stride)."""
+    w = _f32(w)
+    if w.shape != (dr, dr):
+        raise ValueError(f"reservoir weight of shape {tuple(w.shape)}, expected ({dr}, {dr})")
+    if w.stride(1) != 1 or w.stride(0) < dr:
+        w = w.contiguous()
+    return w, w.stride(0)
+
+
+def esn_gru_fwd(U: torch.Tensor, Uz: torch.Tensor, Ur: torch.Tensor, Wzh: torch.Tensor,
+                Wrh: torch.Tensor, Ws: torch.Tensor) -> torch.Tensor:
+    """GRU-gated echo-state recurrence over all T steps in one launch
+    (research/tsrn_dml.py:834-840); returns H [B, T, dr].  Forward only.
+    Wzh / Wrh may be the column slices ``W_z.weight[:, :dr]`` in place."""
+    dev = _require_cuda(U, Uz, Ur, Wzh, Wrh, Ws)
+    U, Uz, Ur = (_f32(t).contiguous() for t in (U, Uz, Ur))
+    B, T, dr = U.shape
+    if Uz.shape != U.shape or Ur.shape != U.shape:
+        raise ValueError("esn_gru_fwd: U, Uz and Ur must have the same shape")
+    (Wzh, lz), (Wrh, lr), (Ws, ls) = (_rows(w, dr) for w in (Wzh, Wrh, Ws))
+    H = torch.empty_like(U)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = lib.tp_esn_gru_fwd(B, T, dr, _ptr(U), _ptr(Uz), _ptr(Ur), _ptr(Wzh), lz,
+                                _ptr(Wrh), lr, _ptr(Ws), ls, _ptr(H), _stream(dev))
+    _lib.check(st, "tp_esn_gru_fwd")
+    return H
+
+
+def esn_leaky_fwd(U: torch.Tensor, Ws: torch.Tensor, lk: torch.Tensor) -> torch.Tensor:
+    """Leaky echo-state recurrence h = (1 - lk) h + lk tanh(h Ws^T + U_t) over
+    all T steps in one launch (tsrn_gpu.py:480-484); ``lk`` is the device
+    scalar sigmoid(leak).  Returns H [B, T, dr].  Forward only."""
+    dev = _require_cuda(U, Ws, lk)
+    U = _f32(U).contiguous()
+    B, T, dr = U.shape
+    Ws, ls = _rows(Ws, dr)
+    lk = _f32(lk).reshape(1).contiguous()
+    H = torch.empty_like(U)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = lib.tp_esn_leaky_fwd(B, T, dr, _ptr(U), _ptr(Ws), ls, _ptr(lk), _ptr(H),
+                                  _stream(dev))
+    _lib.check(st, "tp_esn_leaky_fwd")
+    return H

@@ -20,6 +20,8 @@ from .maxplus import (  # noqa: F401
     round_bf16,
     tsrn_attention_fwd,
     lfdual_act,
+    esn_gru_fwd,
+    esn_leaky_fwd,
     maxplus_bwd_argmax,
     maxplus_bwd_smooth,
     maxplus_lse_fwd,

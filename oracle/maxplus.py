@@ -198,3 +198,36 @@ def lfdual_act(y, mode: str, slopes, biases, x_grid, blend_gate=None):
         return dual
     g = (1.0 / (1.0 + np.exp(-np.asarray(blend_gate, np.float64)))).astype(np.float32)
     return (g * primal + (np.float32(1.0) - g) * dual).astype(np.float32)
+
+
+def esn_gru_fwd(U, Uz, Ur, Wzh, Wrh, Ws):
+    """GRU-gated echo-state recurrence (research/tsrn_dml.py:834-840) in float64,
+    h_{-1} = 0; returns H [B, T, dr]."""
+    U, Uz, Ur = (np.asarray(a, np.float64) for a in (U, Uz, Ur))
+    Wzh, Wrh, Ws = (np.asarray(a, np.float64) for a in (Wzh, Wrh, Ws))
+    B, T, dr = U.shape
+    h = np.zeros((B, dr))
+    H = np.empty((B, T, dr))
+    sig = lambda v: 1.0 / (1.0 + np.exp(-v))
+    for t in range(T):
+        z = sig(h @ Wzh.T + Uz[:, t])
+        r = sig(h @ Wrh.T + Ur[:, t])
+        ht = np.tanh((r * h) @ Ws.T + U[:, t])
+        h = (1 - z) * h + z * ht
+        H[:, t] = h
+    return H
+
+
+def esn_leaky_fwd(U, Ws, lk):
+    """Leaky echo-state recurrence h = (1 - lk) h + lk tanh(h Ws^T + U_t)
+    (tsrn_gpu.py:480-484) in float64, h_{-1} = 0; returns H [B, T, dr]."""
+    U = np.asarray(U, np.float64)
+    Ws = np.asarray(Ws, np.float64)
+    lk = float(np.asarray(lk).reshape(()))
+    B, T, dr = U.shape
+    h = np.zeros((B, dr))
+    H = np.empty((B, T, dr))
+    for t in range(T):
+        h = (1 - lk) * h + lk * np.tanh(h @ Ws.T + U[:, t])
+        H[:, t] = h
+    return H

@@ -295,6 +295,62 @@ def gen_lfdual(trop, dtn):
         _save(name, x=_np(xx), out=_np(yy), **state)
 
 
+def gen_esn(research):
+    # research EchoStateReservoir (research/tsrn_dml.py:736-843), eval: d_model =
+    # d_reservoir and readout = identity, so the output is the state sequence H.
+    # _cached_v is set before the forward so the power iteration draws no
+    # random numbers; the recurrence inputs are computed by the module's own parts.
+    import copy
+    torch.manual_seed(11)
+    d = 24
+    esn = research.EchoStateReservoir(d, d)
+    with torch.no_grad():
+        esn.W_z.weight.normal_(0.0, 0.15)
+        esn.W_r.weight.normal_(0.0, 0.15)
+        esn.log_rho.fill_(0.4)
+        esn.readout.weight.copy_(torch.eye(d))
+        esn._cached_v.copy_(torch.randn(d))
+    esn.eval()
+    x = torch.randn(2, 30, d)
+    # copies: the forward updates _cached_v in place
+    state = {f"p_{k}": _np(v).copy() for k, v in esn.state_dict().items()}
+    with torch.no_grad():
+        probe = copy.deepcopy(esn)
+        rho_target = torch.sigmoid(probe.log_rho) * 1.5
+        rho_current = probe._power_iter_spectral_radius(probe.W_res)
+        W_scaled = probe.W_res * (rho_target / rho_current.clamp(min=1e-6))
+        U = probe.W_in(x)
+        Uz = U @ probe.W_z.weight[:, d:].T + probe.W_z.bias
+        Ur = U @ probe.W_r.weight[:, d:].T + probe.W_r.bias
+        H = esn(x)
+    _save("esn", x=_np(x), H=_np(H), U=_np(U), Uz=_np(Uz), Ur=_np(Ur),
+          Wzh=_np(esn.W_z.weight[:, :d]), Wrh=_np(esn.W_r.weight[:, :d]), Ws=_np(W_scaled),
+          **state)
+
+
+def gen_esn_leaky(tsrn_gpu):
+    # leaky EchoStateReservoir of tsrn_gpu.py (:435-487), eval; d_model =
+    # d_reservoir, readout = identity, so the output is the state sequence H.
+    torch.manual_seed(12)
+    d = 24
+    esn = tsrn_gpu.EchoStateReservoir(d, d)
+    with torch.no_grad():
+        esn.log_rho.fill_(0.4)
+        esn.leak.fill_(-0.6)
+        esn.readout.weight.copy_(torch.eye(d))
+    esn.eval()
+    x = torch.randn(2, 30, d)
+    state = {f"p_{k}": _np(v).copy() for k, v in esn.state_dict().items()}
+    with torch.no_grad():
+        rho = torch.sigmoid(esn.log_rho) * 1.5
+        eigs = torch.linalg.eigvals(esn.W_res).abs()
+        W_scaled = esn.W_res * (rho / (eigs.max().real.clamp(min=1e-6)))
+        lk = torch.sigmoid(esn.leak)
+        U = esn.W_in(x)
+        H = esn(x)
+    _save("esn_leaky", x=_np(x), H=_np(H), U=_np(U), Ws=_np(W_scaled), lk=_np(lk), **state)
+
+
 def gen_tsrn_attention(research):
     # research TropicalAttention (research/tsrn_dml.py:355-548), eval, causal,
     # fast path: the module output, the Wo input (the attention context) and
@@ -331,6 +387,7 @@ def main():
     trop = _load("tropformer", "tropformer.py")
     dtn = _load("deep_tropical_net", "deep_tropical_net.py")
     research = _load("research_tsrn_dml", "research/tsrn_dml.py")
+    tsrn_gpu = _load("tsrn_gpu", "tsrn_gpu.py")
     gen_kat(trop)
     gen_linear(trop)
     gen_bf16(trop)
@@ -338,6 +395,8 @@ def main():
     gen_scores(trop, dtn)
     gen_tsrn(research)
     gen_tsrn_attention(research)
+    gen_esn(research)
+    gen_esn_leaky(tsrn_gpu)
 
 
 if __name__ == "__main__":

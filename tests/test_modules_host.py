@@ -81,3 +81,39 @@ def test_hybrid_ffn_state_dict_matches_reference(name, cls):
     ref_keys = sorted(k[2:] for k in g.keys() if k.startswith("p_"))
     assert sorted(mod.state_dict().keys()) == ref_keys
     mod.load_state_dict({k: torch.tensor(g["p_" + k]) for k in ref_keys})
+
+
+def test_reservoir_state_dict_matches_reference():
+    from mk_iii_technologies_tsrn_b200.reservoir import EchoStateReservoir
+    ref = _golden_state("esn")
+    d = ref["W_in.weight"].shape[1]
+    mod = EchoStateReservoir(d, d)
+    ours = mod.state_dict()
+    assert set(ours) == set(ref)
+    for k, v in ref.items():
+        assert tuple(ours[k].shape) == v.shape, k
+    mod.load_state_dict({k: torch.tensor(v) for k, v in ref.items()})
+
+
+def test_reservoir_cpu_training_path_matches_golden():
+    # on CPU with autograd the module runs the reference loop; it reproduces the
+    # reference module's output for the same state
+    from mk_iii_technologies_tsrn_b200.reservoir import EchoStateReservoir
+    g = load_golden("esn")
+    d = g["x"].shape[-1]
+    mod = EchoStateReservoir(d, d)
+    mod.load_state_dict({k: torch.tensor(v) for k, v in _golden_state("esn").items()})
+    y = mod(torch.tensor(g["x"]))
+    np.testing.assert_allclose(y.detach().numpy(), g["H"], rtol=0, atol=1e-5)
+
+
+def test_leaky_reservoir_matches_reference_on_cpu():
+    from mk_iii_technologies_tsrn_b200.reservoir import LeakyEchoStateReservoir
+    g = load_golden("esn_leaky")
+    ref = _golden_state("esn_leaky")
+    d = g["x"].shape[-1]
+    mod = LeakyEchoStateReservoir(d, d)
+    assert set(mod.state_dict()) == set(ref)
+    mod.load_state_dict({k: torch.tensor(v) for k, v in ref.items()})
+    y = mod(torch.tensor(g["x"]))
+    np.testing.assert_allclose(y.detach().numpy(), g["H"], rtol=0, atol=1e-5)

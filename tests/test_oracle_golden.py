@@ -208,3 +208,15 @@ def test_lfdual_oracle_pinned(mode):
         np.testing.assert_allclose(out, g[f"{mode}_out"], rtol=1e-6, atol=1e-6)
     else:
         np.testing.assert_array_equal(out, g[f"{mode}_out"])
+
+
+def test_esn_oracle_pinned():
+    g = load_golden("esn")
+    H = oracle.esn_gru_fwd(g["U"], g["Uz"], g["Ur"], g["Wzh"], g["Wrh"], g["Ws"])
+    np.testing.assert_allclose(H, g["H"], rtol=0, atol=1e-6)
+
+
+def test_esn_leaky_oracle_pinned():
+    g = load_golden("esn_leaky")
+    H = oracle.esn_leaky_fwd(g["U"], g["Ws"], g["lk"])
+    np.testing.assert_allclose(H, g["H"], rtol=0, atol=1e-6)
