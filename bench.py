@@ -20,6 +20,12 @@ forward with int32 argmax and the argmax backward; Gop/s of forward ops.
 ``--workload tsrn_attn``: the TSRN tropical top-k attention of config 5 (B=64, H=8,
 T=1024, d_h=80, top_k=16, causal) through the fused kernel; tokens/s.
 
+``--workload esn``: the echo-state reservoir recurrence of the TSRN scale-1 block
+of config 5 (tsrn_gpu.py: leaky, d_reservoir = d_model = 640; B=64, T=1024 per
+rank) in one fused launch from U = W_in(x) to the state sequence H; ``--esn-mode
+gru`` runs the GRU-gated reservoir of research/tsrn_dml.py (d_reservoir =
+d_model / 2 = 320).  Metric tokens/s.
+
 ``--workload dtn``: config 2, the drop-in DTNAttention(256, 8) block
 (tropical Q/K projections with the STE backward, tropical score, Maslov
 softmax) forward + backward at B=128, L=64 per rank; metric tokens/s.
@@ -62,7 +68,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["gemm", "scan", "dtn", "linear", "tsrn_attn"],
+    p.add_argument("--workload",
+                   choices=["gemm", "scan", "dtn", "linear", "tsrn_attn", "esn"],
                    default="gemm")
     p.add_argument("--size", type=int, default=8192, help="M = N = K of the GEMM workload")
     p.add_argument("--dtype", choices=["f32", "bf16"], default="f32",
@@ -74,6 +81,9 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--att-batch", type=int, default=64,
                    help="sequences per rank of the tsrn_attn workload (64 = config 5)")
+    p.add_argument("--esn-mode", choices=["leaky", "gru"], default="leaky",
+                   help="esn workload: leaky reservoir (tsrn_gpu.py, dr 640) or GRU-gated "
+                        "(research/tsrn_dml.py, dr 320)")
     p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                    help="N>1 GEMM: fused peer-store epilogue (p2p) or NCCL all-gather")
     return p.parse_args()
@@ -815,6 +825,135 @@ def tsrn_attn_workload(args, world, rank):
     }
 
 
+ESN = dict(B=64, T=1024, dr_leaky=640, dr_gru=320)   # TSRN scale-1 reservoir (config 5)
+
+
+def esn_inputs(mode, B, T, gen):
+    """Reservoir inputs with the reference modules' statistics: U = W_in(LayerNorm(x))
+    (default nn.Linear init: entries of variance 1/3), W_res sparse N(0,1) at 10% density
+    scaled to spectral radius sigmoid(0) * 1.5 = 0.75, leak sigmoid(0.3); GRU gates from
+    zero-initialised weights plus N(0, 0.1^2) (a trained-from-init state) and the
+    reference's biases 0.85 / 2.0."""
+    dr = ESN["dr_leaky"] if mode == "leaky" else ESN["dr_gru"]
+    U = torch.randn(B, T, dr, generator=gen) / math.sqrt(3.0)
+    W = torch.randn(dr, dr, generator=gen) * (torch.rand(dr, dr, generator=gen) > 0.9).float()
+    Ws = W * (0.75 / torch.linalg.eigvals(W).abs().max().real)
+    if mode == "leaky":
+        return dr, (U, Ws, torch.sigmoid(torch.tensor(0.3)))
+    Wz_u, Wr_u, Wzh, Wrh = (0.1 * torch.randn(dr, dr, generator=gen) / math.sqrt(dr)
+                            for _ in range(4))
+    Uz = U @ Wz_u.T + 0.85
+    Ur = U @ Wr_u.T + 2.0
+    return dr, (U, Uz, Ur, Wzh, Wrh, Ws)
+
+
+def esn_workload(args, world, rank):
+    """The reservoir recurrence of config 5's scale-1 block, B=64 sequences per rank of
+    T=1024 steps, fused (one launch per call) from the input projections to H."""
+    from mk_iii_technologies_tsrn_b200 import ops, _lib
+
+    _lib.load().tp_set_pointer_checks(0)
+    mode, B, T = args.esn_mode, ESN["B"], ESN["T"]
+    dev = torch.device("cuda")
+    gen = torch.Generator().manual_seed(20 + rank)
+    dr, host = esn_inputs(mode, B, T, gen)
+    hU = host[0].pin_memory()
+    dev_in = [t.to(dev) for t in host]
+    fn = ops.esn_leaky_fwd if mode == "leaky" else ops.esn_gru_fwd
+    # parity on a slice of this workload before timing (oracle on CPU, fp64)
+    if rank == 0:
+        import numpy as np
+        import oracle
+        Bs, Ts = 2, 64
+        sl = [t[:Bs, :Ts].contiguous() if t.dim() == 3 else t for t in dev_in]
+        out = fn(*sl).cpu().numpy()
+        hs = [t.cpu().numpy() for t in sl]
+        ref = oracle.esn_leaky_fwd(*hs) if mode == "leaky" else oracle.esn_gru_fwd(*hs)
+        if not np.allclose(out, ref, rtol=0, atol=2e-5):
+            raise RuntimeError("fused reservoir recurrence differs from the oracle")
+
+    def step():
+        return fn(*dev_in)
+
+    for _ in range(args.warmup):
+        step()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    ms = time_steps(step, args.steps, world)
+    clk = clocks.stop()
+    tokens = B * T * world
+    value = tokens / (ms / args.steps / 1e3)
+    gates = 1 if mode == "leaky" else 3
+    ops.probe_addmax(7, 148 * 8, 50)
+    pms, terms = ops.probe_addmax(7, 148 * 8, 400)
+    peak = 2.0 * terms / (pms / 1e3) / 1e12
+    achieved = 2.0 * gates * B * T * dr * dr / (ms / args.steps / 1e3) / 1e12
+    hH = torch.empty(B, T, dr).pin_memory()
+    dU = torch.empty_like(dev_in[0])
+    rest = dev_in[1:]
+
+    def e2e_step():
+        dU.copy_(hU, non_blocking=True)
+        hH.copy_(fn(dU, *rest), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_steps = max(3, min(args.steps, 5))
+    e2e_ms = time_steps(e2e_step, e2e_steps, world)
+    try:
+        per_step = count_library_kernels(step)
+    except Exception:   # profiler unavailable: leave the count out rather than guess
+        per_step = None
+    name = ("leaky EchoStateReservoir (tsrn_gpu.py)" if mode == "leaky"
+            else "GRU-gated EchoStateReservoir (research/tsrn_dml.py)")
+    return {
+        "metric": f"echo-state reservoir tokens/s ({mode}, fused recurrence, inference)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded): U with the statistics of W_in(LayerNorm(x)), sparse "
+                "W_res scaled to spectral radius 0.75" + ("" if mode == "leaky" else
+                                                          ", GRU gate inputs"),
+        "config": {"workload": f"{name} d_reservoir={dr} B={B} T={T} (config 5 scale-1 "
+                               f"reservoir)",
+                   "parallelism": f"batch x{world} (weak)" if world > 1 else "single GPU",
+                   "l2": f"U and H {B * T * dr * 4 / 2**20:.0f} MiB each, larger than L2"},
+        "e2e": {"value": tokens / (e2e_ms / e2e_steps / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": hU.numel() * 4, "d2h_bytes_per_step": hH.numel() * 4},
+        "gpu_launches": per_step * args.steps if per_step is not None else None,
+        "roofline": {"bound": "cuda-core fp32 FMA (recurrent mat-vec products); the "
+                              "recurrence is latency-bound per step",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "kernel": "esn_kernel",
+                     "peak_source": "in-repo register-only FFMA probe (tp_probe_addmax form 7), "
+                                    "this run; of measured"},
+        "clocks": clk,
+    }
+
+
+def cpu_esn_rate(mode, target_s: float = 10.0):
+    from oracle.torch_ref import esn_gru_torch, esn_leaky_torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    B, T = ESN["B"], ESN["T"]
+    gen = torch.Generator().manual_seed(20)
+    dr, host = esn_inputs(mode, B, T, gen)
+    fn = esn_leaky_torch if mode == "leaky" else esn_gru_torch
+    t0 = time.perf_counter()
+    fn(*host)
+    dt = time.perf_counter() - t0
+    reps = int(max(1, min(20, target_s / max(dt, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        fn(*host)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": B * T / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"B={B}, T={T}: one step of the workload (d_reservoir={dr}) through the "
+                      f"reference {mode} loop (oracle/torch_ref.py), {reps} reps, {dt:.2f} s each"}
+
+
 def cpu_tsrn_attn_rate(target_s: float = 10.0):
     from oracle.torch_ref import tsrn_attention_torch
 
@@ -895,7 +1034,13 @@ def cpu_dtn_rate(target_s: float = 10.0):
 def reference_arm(args, world, rank):
     if rank != 0:
         return None
-    if args.workload == "tsrn_attn":
+    if args.workload == "esn":
+        cb = cpu_esn_rate(args.esn_mode, target_s=max(3.0, 2.0 * args.steps))
+        metric = f"echo-state reservoir tokens/s ({args.esn_mode}, fused recurrence, inference)"
+        dr = ESN["dr_leaky"] if args.esn_mode == "leaky" else ESN["dr_gru"]
+        cfg = {"workload": f"{args.esn_mode} EchoStateReservoir d_reservoir={dr} "
+                           f"B={ESN['B']} T={ESN['T']} (torch CPU)"}
+    elif args.workload == "tsrn_attn":
         cb = cpu_tsrn_attn_rate(target_s=max(3.0, 2.0 * args.steps))
         metric = "TSRN tropical top-k attention tokens/s (fused fwd, inference)"
         cfg = {"workload": "TSRN TropicalAttention H=8 T=1024 d_h=80 top_k=16 causal "
@@ -946,6 +1091,8 @@ def main():
             res = linear_workload(args, world, rank)
         elif args.workload == "tsrn_attn":
             res = tsrn_attn_workload(args, world, rank)
+        elif args.workload == "esn":
+            res = esn_workload(args, world, rank)
         else:
             res = scan_workload(args, world, rank)
         if res is not None and args.impl == "ours" and rank == 0 and world == 1 \
@@ -959,6 +1106,8 @@ def main():
                 res["cpu_baseline"] = cpu_linear_rate()
             elif args.workload == "tsrn_attn":
                 res["cpu_baseline"] = cpu_tsrn_attn_rate()
+            elif args.workload == "esn":
+                res["cpu_baseline"] = cpu_esn_rate(args.esn_mode)
             else:
                 res["cpu_baseline"] = cpu_scan_rate(16, 4096, 1024)
         if rank == 0 and res is not None:

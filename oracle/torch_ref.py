@@ -116,3 +116,31 @@ def tsrn_attention_torch(Q, K, V, slopes, top_k: int, causal: bool = True, q_chu
         scores = scores.masked_fill(scores < thr, float("-inf"))
         out.append(torch.softmax(scores, dim=-1) @ V)
     return torch.cat(out, dim=2)
+
+
+def esn_leaky_torch(U, Ws, lk):
+    """The leaky reservoir loop of tsrn_gpu.py:479-487 on precomputed inputs U = W_in(x):
+    h = (1 - lk) h + lk tanh(h Ws^T + U_t), h_{-1} = 0; returns H [B, T, dr]."""
+    B, T, dr = U.shape
+    h = torch.zeros(B, dr, dtype=U.dtype)
+    outs = []
+    Wt = Ws.T
+    for t in range(T):
+        h = (1 - lk) * h + lk * torch.tanh(h @ Wt + U[:, t, :])
+        outs.append(h)
+    return torch.stack(outs, dim=1)
+
+
+def esn_gru_torch(U, Uz, Ur, Wzh, Wrh, Ws):
+    """The GRU-gated reservoir loop of research/tsrn_dml.py:832-842 on precomputed
+    inputs; returns H [B, T, dr]."""
+    B, T, dr = U.shape
+    h = torch.zeros(B, dr, dtype=U.dtype)
+    outs = []
+    for t in range(T):
+        z = torch.sigmoid(h @ Wzh.T + Uz[:, t, :])
+        r = torch.sigmoid(h @ Wrh.T + Ur[:, t, :])
+        h_tilde = torch.tanh((r * h) @ Ws.T + U[:, t, :])
+        h = (1 - z) * h + z * h_tilde
+        outs.append(h)
+    return torch.stack(outs, dim=1)
