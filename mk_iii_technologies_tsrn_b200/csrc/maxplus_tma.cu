@@ -14,8 +14,8 @@
 //   TMA loads       128x32 fp32 x/w tiles (128-byte swizzle, no multicast)
 //                   into a full/empty mbarrier ring.  The value-only kernel
 //                   has a producer warp and 4 stages; the argmax kernel lets
-//                   its thread 0 issue the loads (16 warps: 128 registers per
-//                   thread) and uses 3 stages (more L1 for the search below).
+//                   its thread 0 issue the loads, uses 3 stages (more L1 for
+//                   the search below) and adds a search warpgroup.
 //
 // Exact argmax without per-term index tracking.  The running max only grows,
 // so the lowest k attaining the final max lies in the LAST CHUNK-wide k-range
@@ -23,15 +23,17 @@
 // threads compare their accumulators with a snapshot kept in shared memory
 // (bitwise, so NaN counts once) and record the chunk index (16-bit, shared
 // memory).  At the end of a tile each thread stores its outputs' raw maxima
-// in y and their chunk indices in argmax; while the CTA computes its NEXT
-// tile, each thread searches its previous tile's outputs, 8 k at a time: the
-// x and w quads of a unit are loaded (through L1/L2) at one k-tile and tested
-// at the next, so the loads hide behind the tile's arithmetic.  The first k
+// in y and their chunk indices in argmax.  While the compute warps run the
+// CTA's NEXT tile, a dedicated search warpgroup (one thread per tile column)
+// walks the previous tile's outputs 8 k at a time, the next unit's x and w
+// quads loaded (through L1/L2) while the current one is tested: the first k
 // of the chunk whose sum equals the output's max (or is NaN when the max is
 // NaN) is its argmax; then the final y (bias, scale) and the argmax are
-// stored.  The CTA's last tile is searched after its main loop.  The result
-// equals torch.max(dim=-1) on the reference's broadcast tensor, bit for bit,
-// in values and indices.
+// stored.  Two mbarrier pairs hand tiles over (compute -> search: raw maxima
+// stored; search -> compute: tile searched, so that a barrier phase is never
+// overtaken).  The compute warps search the CTA's last tile themselves after
+// their main loop.  The result equals torch.max(dim=-1) on the reference's
+// broadcast tensor, bit for bit, in values and indices.
 //
 // Every mbarrier wait is bounded (common.cuh); a timeout records a device
 // error and the kernel returns.
@@ -83,10 +85,18 @@ struct Cfg {
   static constexpr int CW = CT / 32;       // compute warps
   static constexpr int PRODUCER_WARP = CW;           // value-only kernel: a TMA warp
   static constexpr int THREADS = 32 * (CW + 1);
-  // The argmax kernel has no producer warp (its thread 0 issues the TMA loads):
-  // 16 warps leave 128 registers per thread, room for the search's loads.
+  // The bf16x2 argmax kernel has no producer warp (its thread 0 issues the TMA
+  // loads): 16 warps leave 128 registers per thread, room for the search's loads.
   template <bool kArgmax>
   static constexpr int threads() { return kArgmax ? CT : THREADS; }
+  // The fp32 argmax kernel adds a search warpgroup (thread 0 still issues the
+  // loads): 20 warps at 96 registers each.  (Moving 32 registers per thread
+  // from the search warpgroup to the compute warps with setmaxnreg gained
+  // 0.7% at K = 8192 but lost 5% at K = 4096, where the slower search falls
+  // behind the shorter tiles.)
+  static constexpr int SEARCH_THREADS = 128;
+  template <bool kArgmax>
+  static constexpr int threads32() { return kArgmax ? CT + SEARCH_THREADS : THREADS; }
   static constexpr int OUTS = TM * TN;     // outputs per compute thread
   static constexpr int KT_PER_CHUNK = CHUNK / BK;
   static constexpr int64_t MAX_K = (int64_t)CHUNK * 65535;  // 16-bit chunk index
@@ -226,7 +236,7 @@ __device__ __forceinline__ void store_output(const TmaParams& p, int64_t m, int6
 }
 
 template <class C, bool kArgmax>
-__global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
+__global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
     maxplus_tma_kernel(const __grid_constant__ CUtensorMap xmap,
                        const __grid_constant__ CUtensorMap wmap, const TmaParams p) {
   constexpr int TM = C::TM, TN = C::TN, TX = C::TX, TY = C::TY, CT = C::CT;
@@ -242,6 +252,9 @@ __global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
                                (kArgmax ? SNAP_BYTES + CIDX_BYTES : 0));
   uint64_t* full = bars;                 // [STAGES]
   uint64_t* empty = bars + STAGES;       // [STAGES]
+  uint64_t* tile_ready = bars + 2 * STAGES;        // [2] argmax: raw maxima stored
+  uint64_t* search_done = bars + 2 * STAGES + 2;   // [2] argmax: tile searched
+  constexpr int SEARCH_WARPS = C::SEARCH_THREADS / 32;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -252,6 +265,12 @@ __global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
     for (int s = 0; s < STAGES; ++s) {
       tp_mbar_init(&full[s], 1);
       tp_mbar_init(&empty[s], C::CW);
+    }
+    if (kArgmax) {
+      for (int b = 0; b < 2; ++b) {
+        tp_mbar_init(&tile_ready[b], C::CW);
+        tp_mbar_init(&search_done[b], SEARCH_WARPS);
+      }
     }
     tp_fence_mbar_init();
   }
@@ -310,6 +329,68 @@ __global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
     }
   }
 
+  constexpr int UPO = C::CHUNK / 8;            // 8-k search units per output
+  const int Kc = (int)p.K;
+  const int Mc = (int)p.M, Nc = (int)p.N;
+
+  if constexpr (kArgmax) {
+    if (threadIdx.x >= CT) {
+      // ---------------------------------------------------- search warpgroup
+      // Tiles 0 .. my_tiles-2 of this CTA, each once its raw maxima and
+      // chunks are stored; thread sid walks column sid of the tile row by
+      // row (a warp covers 32 adjacent columns: coalesced y / argmax loads).
+      const int sid = (int)threadIdx.x - CT;
+      uint32_t lt = 0;
+      for (int tile = blockIdx.x; lt + 1 < my_tiles; tile += gridDim.x, ++lt) {
+        const bool ok = tp_mbar_wait(&tile_ready[lt & 1], (lt >> 1) & 1u, p.err);
+        if (!__all_sync(0xffffffffu, ok)) return;
+        int mt, nt;
+        tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+        const int n = nt * BN + sid;
+        const int m0 = mt * BM;
+        const int rows = n < Nc ? min(BM, Mc - m0) : 0;
+        const float* wrow = p.w + (int64_t)n * p.ldw;
+        float tv = 0.0f;
+        int kc = 0;
+        if (rows > 0) {
+          tv = p.y[(int64_t)m0 * p.ldy + n];
+          kc = p.am[(int64_t)m0 * p.lda + n] * C::CHUNK;
+        }
+        for (int r = 0; r < rows; ++r) {
+          const int m = m0 + r;
+          float ntv = 0.0f;
+          int nkc = 0;
+          if (r + 1 < rows) {
+            ntv = p.y[(int64_t)(m + 1) * p.ldy + n];
+            nkc = p.am[(int64_t)(m + 1) * p.lda + n] * C::CHUNK;
+          }
+          const float* xr = p.x + (int64_t)m * p.ldx + kc;
+          const float* wr = wrow + kc;
+          float4 a0, a1, b0, b1;
+          load_unit(xr, wr, kc, Kc, a0, a1, b0, b1);
+          int best = kBestNone;
+          for (int u = 0; u < UPO; ++u) {
+            float4 c0 = a0, c1 = a1, d0 = b0, d1 = b1;
+            if (u + 1 < UPO)
+              load_unit(xr + 8 * (u + 1), wr + 8 * (u + 1), kc + 8 * (u + 1), Kc, c0, c1, d0, d1);
+            best = unit_first_hit(tv, kc + 8 * u, Kc, a0, a1, b0, b1);
+            if (best != kBestNone) break;
+            a0 = c0;
+            a1 = c1;
+            b0 = d0;
+            b1 = d1;
+          }
+          store_output(p, m, n, tv, best != kBestNone ? best : kc);
+          tv = ntv;
+          kc = nkc;
+        }
+        __syncwarp();
+        if (lane == 0) tp_mbar_arrive(&search_done[lt & 1]);
+      }
+      return;
+    }
+  }
+
   // -------------------------------------------------------------- compute
   const int t = threadIdx.x;  // 0..CT-1
   const int tx = t % TX;
@@ -319,71 +400,10 @@ __global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
   const uint32_t wsw = (uint32_t)(tx & 7);
   const float NEG_INF = -__int_as_float(0x7f800000);
 
-  // Deferred argmax search of the previous tile (see the file comment).  The
-  // thread's outputs are searched in 8-k units; a unit's four 16-byte loads
-  // are issued at one k-tile of the current tile and tested at the next.
-  constexpr int UPO = C::CHUNK / 8;            // units per output
-  constexpr int UNITS = C::OUTS * UPO;         // units per thread per tile
-  const int Kc = (int)p.K;
-  const int Mc = (int)p.M, Nc = (int)p.N;
-  int s_u = UNITS + 1;          // next unit to issue (unit s_u-1 in flight); UNITS+1: idle
-  int s_m0 = 0, s_n0 = 0;       // origin of the tile being searched
-  float s_tv = 0.0f, s_ntv = 0.0f;   // max of the current / next output
-  int s_kc = 0, s_nkc = 0;           // first k of their chunks
-  int s_best = kBestNone;
-  const float* s_xp = nullptr;  // next unit's x / w (null: the output is outside M x N)
-  const float* s_wp = nullptr;
-  float4 qa0 = make_float4(0.f, 0.f, 0.f, 0.f), qa1 = qa0, qb0 = qa0, qb1 = qa0;
-  const int steps = kArgmax ? (UNITS + p.k_tiles - 1) / p.k_tiles : 0;
-
-  // the raw max and chunk this thread stored for output o of the searched tile
-  auto prefetch = [&](int o) {
-    const int m = s_m0 + ty + TY * (o / TN), n = s_n0 + tx + TX * (o % TN);
-    if (o < C::OUTS && m < Mc && n < Nc) {
-      s_ntv = p.y[(int64_t)m * p.ldy + n];
-      s_nkc = p.am[(int64_t)m * p.lda + n] * C::CHUNK;
-    }
-  };
-  // test the unit in flight, then issue the next one
-  auto step = [&]() {
-    if (s_u >= 1 && s_u <= UNITS) {
-      const int pu = s_u - 1;
-      if (s_xp != nullptr) {
-        if (s_best == kBestNone)
-          s_best = unit_first_hit(s_tv, s_kc + 8 * (pu % UPO), Kc, qa0, qa1, qb0, qb1);
-        if (pu % UPO == UPO - 1) {
-          const int o = pu / UPO;
-          store_output(p, s_m0 + ty + TY * (o / TN), s_n0 + tx + TX * (o % TN), s_tv,
-                       s_best != kBestNone ? s_best : s_kc);
-        }
-      }
-    }
-    if (s_u < UNITS) {
-      if (s_u % UPO == 0) {
-        const int o = s_u / UPO;
-        const int m = s_m0 + ty + TY * (o / TN), n = s_n0 + tx + TX * (o % TN);
-        s_tv = s_ntv;
-        s_kc = s_nkc;
-        s_best = kBestNone;
-        if (m < Mc && n < Nc) {
-          s_xp = p.x + (int64_t)m * p.ldx + s_kc;
-          s_wp = p.w + (int64_t)n * p.ldw + s_kc;
-        } else {
-          s_xp = s_wp = nullptr;
-        }
-        prefetch(o + 1);
-      }
-      if (s_xp != nullptr) {
-        load_unit(s_xp, s_wp, s_kc + 8 * (s_u % UPO), Kc, qa0, qa1, qb0, qb1);
-        s_xp += 8;
-        s_wp += 8;
-      }
-    }
-    if (s_u <= UNITS) ++s_u;
-  };
-
   uint32_t it = 0;
-  for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+  uint32_t lt = 0;              // this CTA's tile count so far
+  int64_t last_m0 = 0, last_n0 = 0;
+  for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
     int mt, nt;
     tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
     const int64_t m0 = (int64_t)mt * BM, n0 = (int64_t)nt * BN;
@@ -400,15 +420,13 @@ __global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
       for (int o = 0; o < C::OUTS; ++o) cid[o * CT + t] = 0;
     }
 
-    // ---- main pass: values (+ chunk tracking, + the previous tile's search)
+    // ---- main pass: values (+ chunk tracking)
     for (int kt = 0; kt < p.k_tiles; ++kt, ++it) {
       const uint32_t s = it % STAGES;
       const uint32_t ph = (it / STAGES) & 1u;
       if (kArgmax && threadIdx.x == 0 && it + STAGES - 1 < total_kt)
         if (!produce(it + STAGES - 1)) return;
       if (!tp_mbar_wait(&full[s], ph, p.err)) return;
-      if (kArgmax)
-        for (int r = 0; r < steps; ++r) step();
       const uint32_t xbase = stage_addr + s * STAGE_BYTES;
       const uint32_t wbase = xbase + TILE_BYTES;
       const int64_t k0 = (int64_t)kt * BK;
@@ -481,34 +499,39 @@ __global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
         }
       }
     } else {
-    // ---- argmax: finish the previous tile's search (its last unit is in
-    // flight), then hand this tile's raw maxima and chunks to the search
-    while (s_u <= UNITS) step();
+      // ---- argmax: store this tile's raw maxima and chunks, then hand the
+      // tile to the search warpgroup (all but the CTA's last tile)
 #pragma unroll
-    for (int i = 0; i < TM; ++i) {
-      const int64_t m = m0 + ty + TY * i;
-      if (m >= p.M) continue;
+      for (int i = 0; i < TM; ++i) {
+        const int64_t m = m0 + ty + TY * i;
+        if (m >= p.M) continue;
 #pragma unroll
-      for (int j = 0; j < TN; ++j) {
-        const int64_t n = n0 + tx + TX * j;
-        if (n >= p.N) continue;
-        p.y[m * p.ldy + n] = acc[i][j];
-        p.am[m * p.lda + n] = (int32_t)cid[(i * TN + j) * CT + t];
+        for (int j = 0; j < TN; ++j) {
+          const int64_t n = n0 + tx + TX * j;
+          if (n >= p.N) continue;
+          p.y[m * p.ldy + n] = acc[i][j];
+          p.am[m * p.lda + n] = (int32_t)cid[(i * TN + j) * CT + t];
+        }
       }
-    }
-    s_m0 = (int)m0;
-    s_n0 = (int)n0;
-    s_u = 0;
-    prefetch(0);
+      last_m0 = m0;
+      last_n0 = n0;
+      if (lt + 1 < my_tiles) {
+        __syncwarp();
+        bool ok = true;
+        // the search of tile lt-2 has ended before this barrier's next phase
+        if (lane == 0 && lt >= 2)
+          ok = tp_mbar_wait(&search_done[lt & 1], ((lt - 2) >> 1) & 1u, p.err);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+        if (lane == 0) tp_mbar_arrive(&tile_ready[lt & 1]);
+      }
     }
   }
 
-  if (s_u == 0) {
-    // ---- drain: the CTA's last tile (the tile loop always ends with a
-    // hand-off, so nothing of it has been searched yet).  Each output's units
-    // are tested four at a time.
+  if (kArgmax && my_tiles > 0) {
+    // ---- the CTA's last tile, searched by the compute warps after their
+    // main loop; each output's units are tested four at a time
     for (int o = 0; o < C::OUTS; ++o) {
-      const int m = s_m0 + ty + TY * (o / TN), n = s_n0 + tx + TX * (o % TN);
+      const int m = (int)last_m0 + ty + TY * (o / TN), n = (int)last_n0 + tx + TX * (o % TN);
       if (m >= Mc || n >= Nc) continue;
       const float tv = p.y[(int64_t)m * p.ldy + n];
       const int kc = p.am[(int64_t)m * p.lda + n] * C::CHUNK;
@@ -778,7 +801,8 @@ __global__ void __launch_bounds__(C::template threads<kArgmax>(), 1)
         }
         prefetch(o + 1);
       }
-      if (s_xp != nullptr) {
+      // once a unit held the output's max, its remaining units are not loaded
+      if (s_xp != nullptr && s_best == kBestNone) {
         load_unit16(s_xp, s_wp, s_kc + 32 * (s_u % UPO), Kc, su);
         s_xp += 32;
         s_wp += 32;
@@ -983,7 +1007,7 @@ int launch_cfg(const CUtensorMap& xmap, const CUtensorMap& wmap, const TmaParams
   int grid = num_sms();
   if (grid > tp_.num_tiles) grid = tp_.num_tiles;
   maxplus_tma_kernel<C, kArgmax>
-      <<<grid, C::template threads<kArgmax>(), smem_bytes<kArgmax>(), stream>>>(xmap, wmap, tp_);
+      <<<grid, C::template threads32<kArgmax>(), smem_bytes<kArgmax>(), stream>>>(xmap, wmap, tp_);
   return launch_status();
 }
 
