@@ -20,11 +20,11 @@ forward with int32 argmax and the argmax backward; Gop/s of forward ops.
 ``--workload tsrn_attn``: the TSRN tropical top-k attention of config 5 (B=64, H=8,
 T=1024, d_h=80, top_k=16, causal) through the fused kernel; tokens/s.
 
-``--workload esn``: the echo-state reservoir recurrence of the TSRN scale-1 block
-of config 5 (tsrn_gpu.py: leaky, d_reservoir = d_model = 640; B=64, T=1024 per
-rank) in one fused launch from U = W_in(x) to the state sequence H; ``--esn-mode
-gru`` runs the GRU-gated reservoir of research/tsrn_dml.py (d_reservoir =
-d_model / 2 = 320).  Metric tokens/s.
+``--workload esn``: the echo-state reservoir recurrence of config 5's first
+TSRN block (research/tsrn_dml.py:1073: GRU-gated, d_reservoir = d_model / 2 =
+320; B=64, T=1024 per rank) in one fused launch from the input projections to
+the state sequence H; ``--esn-mode leaky`` runs the leaky reservoir of
+tsrn_gpu.py (d_reservoir = d_model = 640) instead.  Metric tokens/s.
 
 ``--workload dtn``: config 2, the drop-in DTNAttention(256, 8) block
 (tropical Q/K projections with the STE backward, tropical score, Maslov
@@ -81,9 +81,9 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--att-batch", type=int, default=64,
                    help="sequences per rank of the tsrn_attn workload (64 = config 5)")
-    p.add_argument("--esn-mode", choices=["leaky", "gru"], default="leaky",
-                   help="esn workload: leaky reservoir (tsrn_gpu.py, dr 640) or GRU-gated "
-                        "(research/tsrn_dml.py, dr 320)")
+    p.add_argument("--esn-mode", choices=["gru", "leaky"], default="gru",
+                   help="esn workload: GRU-gated reservoir of config 5 (research/tsrn_dml.py, "
+                        "d_reservoir 320) or the leaky one of tsrn_gpu.py (d_reservoir 640)")
     p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                    help="N>1 GEMM: fused peer-store epilogue (p2p) or NCCL all-gather")
     return p.parse_args()
@@ -825,7 +825,9 @@ def tsrn_attn_workload(args, world, rank):
     }
 
 
-ESN = dict(B=64, T=1024, dr_leaky=640, dr_gru=320)   # TSRN scale-1 reservoir (config 5)
+# config 5 reservoir: research/tsrn_dml.py:1073, d_reservoir = d_model // 2 (GRU);
+# tsrn_gpu.py:615 builds the leaky one with d_reservoir = d_model
+ESN = dict(B=64, T=1024, dr_leaky=640, dr_gru=320)
 
 
 def esn_inputs(mode, B, T, gen):
@@ -848,8 +850,9 @@ def esn_inputs(mode, B, T, gen):
 
 
 def esn_workload(args, world, rank):
-    """The reservoir recurrence of config 5's scale-1 block, B=64 sequences per rank of
-    T=1024 steps, fused (one launch per call) from the input projections to H."""
+    """The reservoir recurrence of config 5's first block (GRU, d_reservoir 320; or the
+    leaky tsrn_gpu.py one), B=64 sequences per rank of T=1024 steps, fused (one launch
+    per call) from the input projections to H."""
     from mk_iii_technologies_tsrn_b200 import ops, _lib
 
     _lib.load().tp_set_pointer_checks(0)
@@ -914,8 +917,8 @@ def esn_workload(args, world, rank):
         "data": "synthetic (seeded): U with the statistics of W_in(LayerNorm(x)), sparse "
                 "W_res scaled to spectral radius 0.75" + ("" if mode == "leaky" else
                                                           ", GRU gate inputs"),
-        "config": {"workload": f"{name} d_reservoir={dr} B={B} T={T} (config 5 scale-1 "
-                               f"reservoir)",
+        "config": {"workload": f"{name} d_reservoir={dr} B={B} T={T}" +
+                               (" (config 5 first-block reservoir)" if mode == "gru" else ""),
                    "parallelism": f"batch x{world} (weak)" if world > 1 else "single GPU",
                    "l2": f"U and H {B * T * dr * 4 / 2**20:.0f} MiB each, larger than L2"},
         "e2e": {"value": tokens / (e2e_ms / e2e_steps / 1e3), "unit": "tokens/s",

@@ -351,6 +351,51 @@ def gen_esn_leaky(tsrn_gpu):
     _save("esn_leaky", x=_np(x), H=_np(H), U=_np(U), Ws=_np(W_scaled), lk=_np(lk), **state)
 
 
+def gen_real_weights(trop, research):
+    # Trained weights shipped with the reference: TropFormer's first hybrid FFN
+    # block (tropformer_best.pt, all parameters) and the TSRN-gist attention
+    # projections (checkpoints/tsrn_gist_best.pt: Wq/Wk/Wv/Wo; that checkpoint
+    # predates the QK-norm, which keeps its initial identity affine).  Inputs
+    # seeded; outputs from the reference modules in eval mode.
+    ck = torch.load(os.path.join(REF, "tropformer_best.pt"), map_location="cpu",
+                    weights_only=False)
+    pre = "blocks.0.ffn."
+    sub = {k[len(pre):]: v for k, v in ck.items() if k.startswith(pre)}
+    torch.manual_seed(13)
+    ffn = trop.TropicalHybridFFN(128, 256)
+    ffn.load_state_dict(sub, strict=True)
+    ffn.eval()
+    x = torch.randn(4, 17, 128)
+    with torch.no_grad():
+        out = ffn(x)
+    _save("real_ffn_tropformer", x=_np(x), out=_np(out),
+          **{f"p_{k}": _np(v).copy() for k, v in ffn.state_dict().items()})
+
+    gk = torch.load(os.path.join(REF, "checkpoints", "tsrn_gist_best.pt"), map_location="cpu",
+                    weights_only=False)
+    pre = "s1_blocks.0.attn."
+    sub = {k[len(pre):]: v for k, v in gk["model_state_dict"].items() if k.startswith(pre)}
+    cfg = gk["config"]
+    torch.manual_seed(14)
+    d, heads, top_k = cfg["d_model"], cfg["n_heads"], cfg["top_k"]
+    attn = research.TropicalAttention(d, top_k=top_k, n_heads=heads)
+    missing, unexpected = attn.load_state_dict(sub, strict=False)
+    assert not unexpected and {"Wq.weight", "Wk.weight", "Wv.weight", "Wo.weight"} & set(sub)
+    attn.eval()
+    B, T = 2, cfg["context_len"]
+    x = torch.randn(B, T, d)
+    with torch.no_grad():
+        out = attn(x)
+        dh = d // heads
+        Q = attn.q_norm(attn.Wq(x).view(B, T, heads, dh).permute(0, 2, 1, 3))
+        K = attn.k_norm(attn.Wk(x).view(B, T, heads, dh).permute(0, 2, 1, 3))
+        V = attn.Wv(x).view(B, T, heads, dh).permute(0, 2, 1, 3)
+        Q, K = attn.rope(Q, K)
+    _save("real_attention_gist", x=_np(x), out=_np(out), Q=_np(Q), K=_np(K), V=_np(V),
+          slopes=_np(attn.alibi_slopes), top_k=np.int64(top_k), n_heads=np.int64(heads),
+          **{f"p_{k}": _np(v).copy() for k, v in attn.state_dict().items()})
+
+
 def gen_tsrn_attention(research):
     # research TropicalAttention (research/tsrn_dml.py:355-548), eval, causal,
     # fast path: the module output, the Wo input (the attention context) and
@@ -397,6 +442,7 @@ def main():
     gen_tsrn_attention(research)
     gen_esn(research)
     gen_esn_leaky(tsrn_gpu)
+    gen_real_weights(trop, research)
 
 
 if __name__ == "__main__":

@@ -62,3 +62,15 @@ def test_hybrid_ffn_matches_reference(cuda, name):
     np.testing.assert_allclose(y, g["out"], rtol=1e-5, atol=1e-5)
     y2 = mod(x).detach().cpu().numpy()          # graph-building path (module forward)
     np.testing.assert_allclose(y2, g["out"], rtol=1e-5, atol=1e-5)
+
+
+def test_hybrid_ffn_real_weights(cuda):
+    # TropFormer's trained first FFN block (tropformer_best.pt), reference output
+    from mk_iii_technologies_tsrn_b200 import tropical
+    g = load_golden("real_ffn_tropformer")
+    mod = tropical.TropicalHybridFFN(128, 256)
+    mod.load_state_dict({k[2:]: torch.tensor(v) for k, v in g.items() if k.startswith("p_")})
+    mod = mod.to(cuda).eval()
+    with torch.no_grad():
+        y = mod(torch.tensor(g["x"], device=cuda)).cpu().numpy()
+    np.testing.assert_allclose(y, g["out"], rtol=1e-5, atol=1e-5)

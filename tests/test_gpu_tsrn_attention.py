@@ -102,3 +102,19 @@ def test_fused_attention_one_lane_holds_the_top_k(cuda, causal):
     ok = ~_ambiguous_rows(S, top_k, gap=1e-5)
     assert ok.mean() > 0.5
     np.testing.assert_allclose(out[ok], ref[ok], rtol=1e-4, atol=2e-5)
+
+
+def test_module_real_weights(cuda):
+    # the TSRN-gist checkpoint's trained attention projections (Wq/Wk/Wv/Wo)
+    from mk_iii_technologies_tsrn_b200.tsrn_attention import TropicalAttention
+    g = load_golden("real_attention_gist")
+    top_k, heads = int(g["top_k"]), int(g["n_heads"])
+    m = TropicalAttention(g["x"].shape[-1], top_k=top_k, n_heads=heads)
+    m.load_state_dict({k[2:]: torch.tensor(v) for k, v in g.items() if k.startswith("p_")})
+    m = m.to(cuda).eval()
+    with torch.no_grad():
+        out = m(torch.tensor(g["x"], device=cuda)).cpu().numpy()
+    _, S = oracle.tsrn_attention_fwd(g["Q"], g["K"], g["V"], g["slopes"], top_k)
+    rows_ok = (~_ambiguous_rows(S, top_k)).all(axis=1)
+    assert rows_ok.mean() > 0.9
+    np.testing.assert_allclose(out[rows_ok], g["out"][rows_ok], rtol=1e-4, atol=2e-5)

@@ -117,3 +117,17 @@ def test_leaky_reservoir_matches_reference_on_cpu():
     mod.load_state_dict({k: torch.tensor(v) for k, v in ref.items()})
     y = mod(torch.tensor(g["x"]))
     np.testing.assert_allclose(y.detach().numpy(), g["H"], rtol=0, atol=1e-5)
+
+
+def test_real_weight_state_dicts_load():
+    # the reference's trained checkpoints (via the fixtures) load into the drop-ins
+    from mk_iii_technologies_tsrn_b200.tropical import TropicalHybridFFN
+    from mk_iii_technologies_tsrn_b200.tsrn_attention import TropicalAttention
+    ffn = _golden_state("real_ffn_tropformer")
+    mod = TropicalHybridFFN(128, 256)
+    assert set(mod.state_dict()) == set(ffn)
+    mod.load_state_dict({k: torch.tensor(v) for k, v in ffn.items()})
+    att = _golden_state("real_attention_gist")
+    m = TropicalAttention(128, top_k=8, n_heads=2)
+    assert set(m.state_dict()) == set(att)
+    m.load_state_dict({k: torch.tensor(v) for k, v in att.items()})
