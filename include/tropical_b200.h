@@ -230,6 +230,17 @@ TP_API int tp_maxplus_bwd_smooth_ref(int mode, float tau, int dtype,
  * value; process-wide.  (Tuning; no reference counterpart.) */
 TP_API int64_t tp_set_argmax_tma_min_terms(int64_t terms);
 
+/* Schedule of the large fp32 forward (TMA kernel): 0 = each CTA takes whole
+ * 128x128 tiles; 1 (default) = stream-K when the tile count leaves the last
+ * wave partly idle (with argmax: at least 5% of the run): whole-tile waves up
+ * to the last full one, then that wave's and the remaining tiles' 64-k chunks
+ * split evenly over the CTAs; a tile shared by two CTAs is merged exactly
+ * (values and argmax identical to the whole-tile schedule), using a
+ * stream-ordered workspace from a library-owned pool; 2 = stream-K whenever
+ * there are at least as many tiles as CTAs.  Returns the previous mode; process-wide.  (Tuning; no reference
+ * counterpart.) */
+TP_API int tp_set_stream_k(int mode);
+
 /* ======================================================================== *
  *  Fused TSRN tropical top-k attention, forward (inference)
  *  Replaces research/tsrn_dml.py:462-548 (TropicalAttention.forward) from the

@@ -472,6 +472,8 @@ int tp_esn_leaky_fwd(int64_t B, int64_t T, int64_t dr, const float* U, const flo
 
 int64_t tp_set_argmax_tma_min_terms(int64_t terms) { return tp::set_argmax_tma_min_terms(terms); }
 
+int tp_set_stream_k(int mode) { return tp::set_stream_k(mode); }
+
 int tp_last_error(void) { return last_error(); }
 
 int tp_device_error(int reset) {

@@ -149,6 +149,7 @@ bool maxplus_tma_eligible(const StridedMaxPlus& p);
 // smallest M*N*K for which a forward with argmax takes the TMA kernel
 int64_t argmax_tma_min_terms();
 int64_t set_argmax_tma_min_terms(int64_t terms);
+int set_stream_k(int mode);
 int launch_maxplus_fwd_tma(const StridedMaxPlus& p, cudaStream_t stream);
 // Same, additionally storing every output into ndst (<= 8) further buffers
 // at column offset col0 (same row strides as y / argmax).

@@ -37,7 +37,9 @@
 //
 // Every mbarrier wait is bounded (common.cuh); a timeout records a device
 // error and the kernel returns.
+#include <algorithm>
 #include <atomic>
+#include <mutex>
 
 #include "maxplus_internal.cuh"
 
@@ -133,6 +135,22 @@ struct TmaParams {
   int m_tiles, n_tiles, k_tiles, num_tiles;
   int* err;
   LfAct act;   // value-only epilogue activation (mode -1: none)
+  // Stream-K schedule (fp32 kernel; sk = 0: each CTA takes whole tiles
+  // blockIdx.x, +gridDim.x, ...).  With sk, the first sk_dp waves stay whole
+  // tiles (CTA c: tiles c, c+grid, ...; a wave of neighbouring tiles shares
+  // the x/W panels in L2) and the remaining tiles' 64-k chunks form one
+  // sequence of sk_units = tiles * sk_cpt units split evenly over the CTAs
+  // (at least one tile's chunks each), so a tile may be shared by two CTAs:
+  // the later one computes its tail chunks first and leaves partial maxima
+  // (and last-change chunks) in slot cta-1; the earlier one computes the head
+  // chunks last, merges and finishes the tile.
+  int sk;
+  int sk_cpt;
+  int sk_dp;
+  int64_t sk_units;
+  float* sk_max;       // [grid][OUTS * CT] partial maxima, thread-major
+  int32_t* sk_cid;     // [grid][OUTS * CT] their last-change chunks (argmax)
+  unsigned* sk_flag;   // [grid] 1 once slot c holds the tail of CTA c's last tile
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mt, int& nt) {
@@ -254,11 +272,20 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
   uint64_t* empty = bars + STAGES;       // [STAGES]
   uint64_t* tile_ready = bars + 2 * STAGES;        // [2] argmax: raw maxima stored
   uint64_t* search_done = bars + 2 * STAGES + 2;   // [2] argmax: tile searched
+  uint64_t* cbar = bars + 2 * STAGES + 4;          // compute threads only (stream-K)
   constexpr int SEARCH_WARPS = C::SEARCH_THREADS / 32;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   __shared__ float lf_sm[64];
+  __shared__ int sk_ok;
+  // This CTA's schedule: whole tiles blockIdx.x, +gridDim.x, ... (all of
+  // them, or the first sch_dp under stream-K) then, under stream-K, the
+  // contiguous range [sch_g0, sch_g1) of the global k-tile order (tile
+  // major), cut at chunk boundaries.  Kept in shared memory: it is read
+  // between segments, not in the main loop.
+  __shared__ long long sch_g0, sch_g1;
+  __shared__ unsigned sch_nseg, sch_total_kt, sch_dp;
   if (!kArgmax && p.act.mode >= 0) lf_stage(p.act, lf_sm);
 
   if (threadIdx.x == 0) {
@@ -272,18 +299,66 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
         tp_mbar_init(&search_done[b], SEARCH_WARPS);
       }
     }
+    tp_mbar_init(cbar, CT);
     tp_fence_mbar_init();
+    const int cta = (int)blockIdx.x, G = (int)gridDim.x;
+    if (p.sk) {
+      const int64_t first = (int64_t)p.sk_dp * G;       // first stream-K tile
+      auto g_of = [&](int64_t u) -> int64_t {
+        return (first + u / p.sk_cpt) * p.k_tiles +
+               min((u % p.sk_cpt) * (int64_t)C::KT_PER_CHUNK, (int64_t)p.k_tiles);
+      };
+      const int64_t g0 = g_of(p.sk_units * cta / G), g1 = g_of(p.sk_units * (cta + 1) / G);
+      sch_g0 = g0;
+      sch_g1 = g1;
+      sch_dp = (unsigned)p.sk_dp;
+      sch_nseg = (unsigned)p.sk_dp +
+                 (g1 > g0 ? (unsigned)((g1 - 1) / p.k_tiles - g0 / p.k_tiles + 1) : 0u);
+      sch_total_kt = (unsigned)p.sk_dp * (unsigned)p.k_tiles + (unsigned)(g1 - g0);
+    } else {
+      const unsigned my_tiles = (unsigned)((p.num_tiles - cta + G - 1) / G);
+      sch_g0 = sch_g1 = 0;
+      sch_dp = my_tiles;
+      sch_nseg = my_tiles;
+      sch_total_kt = my_tiles * (unsigned)p.k_tiles;
+    }
   }
   __syncthreads();
 
-  // k-tile j of this CTA (tiles blockIdx.x, +gridDim.x, ...; k-tiles in order)
-  // goes to stage j % STAGES once the stage's previous k-tile is released
-  const uint32_t my_tiles = (uint32_t)((p.num_tiles - (int)blockIdx.x + (int)gridDim.x - 1) /
-                                       (int)gridDim.x);
-  const uint32_t total_kt = my_tiles * (uint32_t)p.k_tiles;
+  // Segment i of the schedule is tile `tile`, k-tiles [kb, ke); k-tile j of
+  // the CTA goes to stage j % STAGES once the stage's previous k-tile is
+  // released.
+  const int cta = (int)blockIdx.x, G = (int)gridDim.x;
+  // (the schedule sizes sch_nseg / sch_total_kt are read from shared memory
+  // where used, so that they do not occupy registers across the main loop)
+  auto seg = [&](uint32_t i, int& tile, int& kb, int& ke) {
+    const uint32_t dp = sch_dp;
+    if (i >= dp) {
+      const int64_t g0 = sch_g0, g1 = sch_g1;
+      tile = (int)(g0 / p.k_tiles) + (int)(i - dp);
+      const int64_t base = (int64_t)tile * p.k_tiles;
+      kb = (int)max(g0 - base, (int64_t)0);
+      ke = (int)min(g1 - base, (int64_t)p.k_tiles);
+    } else {
+      tile = cta + (int)i * G;
+      kb = 0;
+      ke = p.k_tiles;
+    }
+  };
+  // segments the search warpgroup takes: finished here (not a stream-K tail
+  // piece) and not the CTA's last segment (the compute warps search that one)
+  auto searched = [&](uint32_t i, int kb) { return !(p.sk && kb > 0) && i + 1 < sch_nseg; };
   auto produce = [&](uint32_t j) -> bool {
-    const int tile = (int)blockIdx.x + (int)(j / (uint32_t)p.k_tiles) * (int)gridDim.x;
-    const int kt = (int)(j % (uint32_t)p.k_tiles);
+    int tile, kt;
+    const uint32_t dp_kt = sch_dp * (uint32_t)p.k_tiles;
+    if (j >= dp_kt) {
+      const int64_t g = sch_g0 + (j - dp_kt);
+      tile = (int)(g / p.k_tiles);
+      kt = (int)(g % p.k_tiles);
+    } else {
+      tile = cta + (int)(j / (uint32_t)p.k_tiles) * G;
+      kt = (int)(j % (uint32_t)p.k_tiles);
+    }
     int mt, nt;
     tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
     const uint32_t s = j % STAGES;
@@ -302,19 +377,8 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
       if (lane == 0) {
         tp_prefetch_tensormap(&xmap);
         tp_prefetch_tensormap(&wmap);
-        uint32_t j = 0;
-        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-          int mt, nt;
-          tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
-          for (int kt = 0; kt < p.k_tiles; ++kt, ++j) {
-            const uint32_t s = j % STAGES;
-            if (!tp_mbar_wait(&empty[s], ((j / STAGES) & 1u) ^ 1u, p.err)) return;
-            unsigned char* dst = stage_base + s * STAGE_BYTES;
-            tp_mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-            tp_tma_load_2d(dst, &xmap, kt * BK, mt * BM, &full[s]);
-            tp_tma_load_2d(dst + TILE_BYTES, &wmap, kt * BK, nt * BN, &full[s]);
-          }
-        }
+        for (uint32_t j = 0; j < sch_total_kt; ++j)
+          if (!produce(j)) return;
       }
       return;
     }
@@ -324,7 +388,7 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
     if (threadIdx.x == 0) {
       tp_prefetch_tensormap(&xmap);
       tp_prefetch_tensormap(&wmap);
-      for (uint32_t j = 0; j < STAGES - 1 && j < total_kt; ++j)
+      for (uint32_t j = 0; j < STAGES - 1 && j < sch_total_kt; ++j)
         if (!produce(j)) return;
     }
   }
@@ -336,13 +400,16 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
   if constexpr (kArgmax) {
     if (threadIdx.x >= CT) {
       // ---------------------------------------------------- search warpgroup
-      // Tiles 0 .. my_tiles-2 of this CTA, each once its raw maxima and
+      // This CTA's finished tiles but the last, each once its raw maxima and
       // chunks are stored; thread sid walks column sid of the tile row by
       // row (a warp covers 32 adjacent columns: coalesced y / argmax loads).
       const int sid = (int)threadIdx.x - CT;
-      uint32_t lt = 0;
-      for (int tile = blockIdx.x; lt + 1 < my_tiles; tile += gridDim.x, ++lt) {
-        const bool ok = tp_mbar_wait(&tile_ready[lt & 1], (lt >> 1) & 1u, p.err);
+      uint32_t h = 0;               // tiles taken so far
+      for (uint32_t i = 0; i < sch_nseg; ++i) {
+        int tile, kb, ke;
+        seg(i, tile, kb, ke);
+        if (!searched(i, kb)) continue;
+        const bool ok = tp_mbar_wait(&tile_ready[h & 1], (h >> 1) & 1u, p.err);
         if (!__all_sync(0xffffffffu, ok)) return;
         int mt, nt;
         tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
@@ -385,7 +452,8 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
           kc = nkc;
         }
         __syncwarp();
-        if (lane == 0) tp_mbar_arrive(&search_done[lt & 1]);
+        if (lane == 0) tp_mbar_arrive(&search_done[h & 1]);
+        ++h;
       }
       return;
     }
@@ -401,12 +469,17 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
   const float NEG_INF = -__int_as_float(0x7f800000);
 
   uint32_t it = 0;
-  uint32_t lt = 0;              // this CTA's tile count so far
-  int64_t last_m0 = 0, last_n0 = 0;
-  for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
-    int mt, nt;
-    tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
-    const int64_t m0 = (int64_t)mt * BM, n0 = (int64_t)nt * BN;
+  uint32_t h = 0;               // tiles handed to the search warpgroup so far
+  // barrier of the compute threads (producer / search warps take no part),
+  // waits bounded like every other
+  uint32_t cphase = 0;
+  auto compute_sync = [&]() -> bool {
+    tp_mbar_arrive(cbar);
+    const bool ok = tp_mbar_wait(cbar, cphase, p.err);
+    cphase ^= 1u;
+    return ok;
+  };
+  for (uint32_t si = 0; si < sch_nseg; ++si) {
     float acc[TM][TN];
 #pragma unroll
     for (int i = 0; i < TM; ++i)
@@ -421,10 +494,15 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
     }
 
     // ---- main pass: values (+ chunk tracking)
-    for (int kt = 0; kt < p.k_tiles; ++kt, ++it) {
+    int kb0, ke0;
+    {
+      int tile0;
+      seg(si, tile0, kb0, ke0);
+    }
+    for (int kt = kb0; kt < ke0; ++kt, ++it) {
       const uint32_t s = it % STAGES;
       const uint32_t ph = (it / STAGES) & 1u;
-      if (kArgmax && threadIdx.x == 0 && it + STAGES - 1 < total_kt)
+      if (kArgmax && threadIdx.x == 0 && it + STAGES - 1 < sch_total_kt)
         if (!produce(it + STAGES - 1)) return;
       if (!tp_mbar_wait(&full[s], ph, p.err)) return;
       const uint32_t xbase = stage_addr + s * STAGE_BYTES;
@@ -480,6 +558,67 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
       }
     }
 
+    // this segment again (tile origin, k range), after the main loop
+    int tile, kb, ke, mt, nt;
+    seg(si, tile, kb, ke);
+    tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+    const int64_t m0 = (int64_t)mt * BM, n0 = (int64_t)nt * BN;
+    if (p.sk && kb > 0) {
+      // ---- stream-K tail piece: partial maxima (+ chunks) to slot cta-1,
+      // then release the flag for the CTA that finishes this tile
+      float* wm = p.sk_max + (int64_t)(cta - 1) * C::OUTS * CT;
+#pragma unroll
+      for (int o = 0; o < C::OUTS; ++o) wm[o * CT + t] = acc[o / TN][o % TN];
+      if (kArgmax) {
+        int32_t* wc = p.sk_cid + (int64_t)(cta - 1) * C::OUTS * CT;
+#pragma unroll
+        for (int o = 0; o < C::OUTS; ++o) wc[o * CT + t] = (int32_t)cid[o * CT + t];
+      }
+      if (!compute_sync()) return;
+      if (t == 0) {
+        __threadfence();
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p.sk_flag + cta - 1), "r"(1u)
+                     : "memory");
+      }
+      continue;
+    }
+    if (p.sk && ke < p.k_tiles) {
+      // ---- stream-K head piece (the CTA's last segment): wait for the tail's
+      // partials, then merge.  The tail wins only with a strictly larger max
+      // (or a NaN where the head has none): ties keep the head's lower k.
+      if (t == 0) {
+        const uint64_t t0 = tp_globaltimer();
+        uint32_t polls = 0;
+        int ok = 1;
+        while (true) {
+          unsigned f;
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(f) : "l"(p.sk_flag + cta)
+                       : "memory");
+          if (f == 1u) break;
+          if (((++polls) & 63u) == 0u && tp_globaltimer() - t0 > TP_WAIT_BUDGET_NS) {
+            tp_record_device_error(p.err, TP_DEVERR_FLAG_TIMEOUT);
+            ok = 0;
+            break;
+          }
+        }
+        sk_ok = ok;
+      }
+      if (!compute_sync() || !sk_ok) return;
+      const float* wm = p.sk_max + (int64_t)cta * C::OUTS * CT;
+      const int32_t* wc = p.sk_cid + (int64_t)cta * C::OUTS * CT;
+#pragma unroll
+      for (int o = 0; o < C::OUTS; ++o) {
+        float& a = acc[o / TN][o % TN];
+        const float tv = __ldcg(wm + o * CT + t);
+        if constexpr (!kArgmax) {
+          a = tp_max_nan(a, tv);
+        } else if (a == a && (tv != tv || tv > a)) {
+          a = tv;
+          cid[o * CT + t] = (uint16_t)__ldcg(wc + o * CT + t);
+        }
+      }
+    }
+
     if constexpr (!kArgmax) {
       // ---- value-only epilogue
 #pragma unroll
@@ -500,7 +639,7 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
       }
     } else {
       // ---- argmax: store this tile's raw maxima and chunks, then hand the
-      // tile to the search warpgroup (all but the CTA's last tile)
+      // tile to the search warpgroup (all but the CTA's last segment)
 #pragma unroll
       for (int i = 0; i < TM; ++i) {
         const int64_t m = m0 + ty + TY * i;
@@ -513,23 +652,29 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
           p.am[m * p.lda + n] = (int32_t)cid[(i * TN + j) * CT + t];
         }
       }
-      last_m0 = m0;
-      last_n0 = n0;
-      if (lt + 1 < my_tiles) {
+      if (searched(si, kb)) {
         __syncwarp();
         bool ok = true;
-        // the search of tile lt-2 has ended before this barrier's next phase
-        if (lane == 0 && lt >= 2)
-          ok = tp_mbar_wait(&search_done[lt & 1], ((lt - 2) >> 1) & 1u, p.err);
+        // the search of the tile handed two before has ended before this
+        // barrier's next phase
+        if (lane == 0 && h >= 2)
+          ok = tp_mbar_wait(&search_done[h & 1], ((h - 2) >> 1) & 1u, p.err);
         if (!__shfl_sync(0xffffffffu, ok, 0)) return;
-        if (lane == 0) tp_mbar_arrive(&tile_ready[lt & 1]);
+        if (lane == 0) tp_mbar_arrive(&tile_ready[h & 1]);
+        ++h;
       }
     }
   }
 
-  if (kArgmax && my_tiles > 0) {
+  // (a stream-K range spans at least one tile's chunks, so its last segment
+  // is never a tail piece: it is finished here)
+  if (kArgmax && sch_nseg > 0) {
     // ---- the CTA's last tile, searched by the compute warps after their
     // main loop; each output's units are tested four at a time
+    int tile, kb, ke, mt, nt;
+    seg(sch_nseg - 1, tile, kb, ke);
+    tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
+    const int64_t last_m0 = (int64_t)mt * BM, last_n0 = (int64_t)nt * BN;
     for (int o = 0; o < C::OUTS; ++o) {
       const int m = (int)last_m0 + ty + TY * (o / TN), n = (int)last_n0 + tx + TX * (o % TN);
       if (m >= Mc || n >= Nc) continue;
@@ -1015,7 +1160,36 @@ int launch_cfg(const CUtensorMap& xmap, const CUtensorMap& wmap, const TmaParams
 
 namespace {
 std::atomic<int64_t> g_argmax_tma_min_terms{(int64_t)1 << 30};
+std::atomic<int> g_stream_k{1};   // 0 off, 1 when it removes a partial last wave, 2 always
+
+// Stream-ordered workspace for the stream-K partials: a library-owned pool per
+// device that keeps its memory (allocation after the first is cheap), so that
+// every caller of the forward gets the schedule without passing a buffer.
+std::mutex g_sk_pool_mu;
+cudaMemPool_t g_sk_pool[64] = {};
+
+cudaMemPool_t sk_pool(int dev) {
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_sk_pool_mu);
+  if (g_sk_pool[dev] == nullptr) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return nullptr;
+    }
+    uint64_t keep = UINT64_MAX;
+    (void)cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    g_sk_pool[dev] = pool;
+  }
+  return g_sk_pool[dev];
+}
 }  // namespace
+
+int set_stream_k(int mode) { return g_stream_k.exchange(mode < 0 ? 0 : (mode > 2 ? 2 : mode)); }
 
 int64_t argmax_tma_min_terms() { return g_argmax_tma_min_terms.load(std::memory_order_relaxed); }
 
@@ -1099,12 +1273,69 @@ int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
     tp_.ydst[d] = d < ndst ? ydst[d] : nullptr;
     tp_.adst[d] = (d < ndst && adst) ? adst[d] : nullptr;
   }
+  tp_.sk = 0;
+  tp_.sk_cpt = 0;
+  tp_.sk_dp = 0;
+  tp_.sk_units = 0;
+  tp_.sk_max = nullptr;
+  tp_.sk_cid = nullptr;
+  tp_.sk_flag = nullptr;
   if (bf16) {
     if (p.am) return launch_cfg16<DefaultCfg, true>(xmap, wmap, tp_, stream);
     return launch_cfg16<DefaultCfg, false>(xmap, wmap, tp_, stream);
   }
-  if (p.am) return launch_cfg<DefaultCfg, true>(xmap, wmap, tp_, stream);
-  return launch_cfg<DefaultCfg, false>(xmap, wmap, tp_, stream);
+  // Stream-K when the tiles leave the last wave partly idle (every CTA must
+  // cover at least one tile's chunks), unless the stream is being captured
+  // (the workspace is allocated on the stream).  With argmax only when that
+  // idle share is at least 5% of the run: below it the split tiles cost about
+  // what they save (measured: 8192 x 1024 x 8192, 3.46 waves, 5.62 -> 5.27 ms;
+  // 8192 x 2048 x 8192, 6.92 waves, 9.72 -> 9.97 ms; value-only gains in both).
+  const int grid = std::min(num_sms(), tp_.num_tiles);
+  const int mode = g_stream_k.load(std::memory_order_relaxed);
+  const int waves = (int)ceil_div(tp_.num_tiles, grid);
+  const double idle = (double)(waves * grid - tp_.num_tiles) / ((double)waves * grid);
+  bool sk = mode != 0 && tp_.num_tiles >= grid && grid > 1 &&
+            (mode == 2 || (tp_.num_tiles % grid != 0 && (!p.am || idle >= 0.05)));
+  void* ws = nullptr;
+  if (sk) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    int dev = 0;
+    cudaMemPool_t pool = nullptr;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone ||
+        cudaGetDevice(&dev) != cudaSuccess || (pool = sk_pool(dev)) == nullptr) {
+      (void)cudaGetLastError();
+      sk = false;
+    } else {
+      const size_t slot = (size_t)DefaultCfg::OUTS * DefaultCfg::CT;
+      const size_t bytes = (size_t)grid * slot * (p.am ? 8 : 4) + (size_t)grid * 4 + 256;
+      if (cudaMallocFromPoolAsync(&ws, bytes, pool, stream) != cudaSuccess) {
+        (void)cudaGetLastError();
+        sk = false;
+      } else {
+        // whole-tile waves for all but the last full wave; stream-K over that
+        // wave and the remainder (at least one tile's chunks per CTA)
+        tp_.sk = 1;
+        tp_.sk_cpt = (int)ceil_div(tp_.k_tiles, DefaultCfg::KT_PER_CHUNK);
+        tp_.sk_dp = std::max(0, tp_.num_tiles / grid - 1);
+        tp_.sk_units = (int64_t)(tp_.num_tiles - tp_.sk_dp * grid) * tp_.sk_cpt;
+        tp_.sk_max = (float*)ws;
+        tp_.sk_cid = p.am ? (int32_t*)(tp_.sk_max + (size_t)grid * slot) : nullptr;
+        tp_.sk_flag = (unsigned*)((char*)ws + (size_t)grid * slot * (p.am ? 8 : 4));
+        const cudaError_t e = cudaMemsetAsync(tp_.sk_flag, 0, (size_t)grid * 4, stream);
+        if (e != cudaSuccess) {
+          (void)cudaFreeAsync(ws, stream);
+          return (int)e;
+        }
+      }
+    }
+  }
+  const int st = p.am ? launch_cfg<DefaultCfg, true>(xmap, wmap, tp_, stream)
+                      : launch_cfg<DefaultCfg, false>(xmap, wmap, tp_, stream);
+  if (ws != nullptr) {
+    const cudaError_t e = cudaFreeAsync(ws, stream);
+    if (st == TP_OK && e != cudaSuccess) return (int)e;
+  }
+  return st;
 }
 
 }  // namespace tp
