@@ -14,9 +14,11 @@
 // of the weights in shared memory (read from L2 when they do not fit).  Each
 // CTA holds the group's full state h (and r*h) in shared memory; the owner of
 // a column broadcasts its new values to every CTA of the cluster with
-// distributed-shared-memory stores, and a hardware cluster barrier ends each
-// half-step.  The next step's U/Uz/Ur slices are fetched with cp.async while
-// the current step computes.  Eight adjacent lanes own one column: each takes
+// distributed-shared-memory stores.  The next step's U/Uz/Ur slices are fetched with cp.async while
+// the current step computes.  New values travel as st.async stores that
+// complete on the receiving CTA's mbarrier (armed with the exchange's byte
+// count), so a CTA waits only for its own incoming data -- no cluster-wide
+// barrier per step.  Eight adjacent lanes own one column: each takes
 // every eighth 16-byte granule of k for all batch rows of the group (one
 // weight load serves every row), and a shuffle reduction leaves row r's sum
 // on lane r.
@@ -44,6 +46,7 @@ struct EsnParams {
   int64_t ld[3];
   const float* leak;  // leaky: device scalar lk
   float* H;
+  int* err;           // device error word (bounded waits)
   int ncl;            // columns per CTA
   int off_h, off_pre; // shared-memory offsets in floats
 };
@@ -71,11 +74,18 @@ __device__ __forceinline__ void esn_cluster_sync() {
   esn_cluster_arrive();
   esn_cluster_wait();
 }
-__device__ __forceinline__ void esn_st_cluster(const float* local, uint32_t rank, float v) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(tp_smem_addr(local)),
+// v to CTA `rank`'s copy of *local, completing 4 bytes on that CTA's copy of
+// *mbar (its receive barrier for this exchange)
+__device__ __forceinline__ void esn_st_async(const float* local, const uint64_t* mbar,
+                                             uint32_t rank, float v) {
+  uint32_t ra, rm;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(tp_smem_addr(local)),
                "r"(rank));
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rm) : "r"(tp_smem_addr(mbar)),
+               "r"(rank));
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(ra),
+               "f"(v), "r"(rm)
+               : "memory");
 }
 __device__ __forceinline__ float esn_sigmoid(float v) { return 1.0f / (1.0f + expf(-v)); }
 
@@ -186,14 +196,40 @@ __global__ void __launch_bounds__(ESN_MAX_NT, 1) esn_kernel(EsnParams p) {
   float hprev = 0.0f, zv = 0.0f;
   const float lk = kGru ? 0.0f : *p.leak;
 
+  // Receive barriers, one phase per exchange: each expects the bytes of every
+  // valid (row, column) of the group (all CTAs send to all, this one
+  // included).  Leaky: mb[b] for the h buffer b (step t writes buffer
+  // (t+1)&1).  GRU: mb[0] for r*h, mb[1] for h (single buffers: a sender's
+  // next write needs values this CTA sends only after its reads).  A barrier
+  // is re-armed (arrive + expect) by thread 0 right after its phase is
+  // waited for.
+  __shared__ __align__(8) uint64_t mb[2];
+  const uint32_t xbytes = (uint32_t)(min(RB, p.B - b0) * dr * (int)sizeof(float));
+  if (tid == 0) {
+    tp_mbar_init(&mb[0], 1);
+    tp_mbar_init(&mb[1], 1);
+    tp_fence_mbar_init();
+    tp_mbar_arrive_expect_tx(&mb[0], xbytes);
+    tp_mbar_arrive_expect_tx(&mb[1], xbytes);
+  }
+  // waits are bounded; after a timeout (recorded) the kernel runs on without
+  // waiting, so that no CTA leaves while others may still write into it
+  bool failed = false;
+  auto recv = [&](int b, uint32_t parity) {
+    if (!failed && !tp_mbar_wait(&mb[b], parity, p.err)) failed = true;
+    if (tid == 0) tp_mbar_arrive_expect_tx(&mb[b], xbytes);
+  };
+
   prefetch(0);
   prefetch(1);
   tp_cp_async_wait<1>();
-  esn_cluster_sync();  // every CTA of the cluster is running; weights, state, step 0 staged
+  esn_cluster_sync();  // every CTA of the cluster is running; barriers, weights, state, step 0
 
   for (int t = 0; t < p.T; ++t) {
     prefetch(t + 2);
     const float* pin = pre + (t % 3) * P * items;
+    if (kGru && t >= 1) recv(1, (uint32_t)(t - 1) & 1u);           // h_{t-1}
+    if (!kGru && t >= 1) recv(t & 1, (uint32_t)((t - 1) >> 1) & 1u);  // h_{t-1}
     if (kGru) {
       // half-step A: z, r and r * h_{t-1} for column c0 + cl
       float2 az[RB], ar[RB];
@@ -221,10 +257,11 @@ __global__ void __launch_bounds__(ESN_MAX_NT, 1) esn_kernel(EsnParams p) {
       const float r = esn_sigmoid(sr + pin[2 * items + pidx]);
       zv = z;
       const float rh = r * hprev;
+      __syncthreads();  // every thread has seen the last phase before any send
       if (col_ok && row_ok)
         for (uint32_t rk = part; rk < csize; rk += PARTS)
-          esn_st_cluster(rhs + row * dr4 + c0 + cl, rk, rh);
-      esn_cluster_sync();
+          esn_st_async(rhs + row * dr4 + c0 + cl, &mb[0], rk, rh);
+      recv(0, (uint32_t)t & 1u);                                      // r*h_{t-1}
     }
     // GRU half-step B / leaky step: h~ and h_t for column c0 + cl
     const float* src = kGru ? rhs : hs + (t & 1) * RB * dr4;
@@ -246,15 +283,27 @@ __global__ void __launch_bounds__(ESN_MAX_NT, 1) esn_kernel(EsnParams p) {
     const float z = kGru ? zv : lk;
     const float h = __fadd_rn(__fmul_rn(1.0f - z, hprev), __fmul_rn(z, ht));
     hprev = h;
-    if (col_ok && row_ok)
-      for (uint32_t rk = part; rk < csize; rk += PARTS)
-        esn_st_cluster(dst + row * dr4 + c0 + cl, rk, h);
-    // the next step's inputs landed (the newest group may still be in flight)
+    // the next step's inputs landed (the newest group may still be in
+    // flight); the barrier publishes them to every thread, frees this step's
+    // input slot, and orders every thread's view of the last phase before the
+    // sends below
     tp_cp_async_wait<1>();
-    esn_cluster_arrive();
-    if (col_ok && row_ok && part == 0) p.H[((int64_t)(b0 + row) * p.T + t) * dr + c0 + cl] = h;
-    esn_cluster_wait();
+    __syncthreads();
+    if (col_ok && row_ok) {
+      for (uint32_t rk = part; rk < csize; rk += PARTS)
+        esn_st_async(dst + row * dr4 + c0 + cl, &mb[kGru ? 1 : (t + 1) & 1], rk, h);
+      if (part == 0) p.H[((int64_t)(b0 + row) * p.T + t) * dr + c0 + cl] = h;
+    }
   }
+  // the last exchange has fully arrived here, and (cluster barrier) everywhere
+  // else, before any CTA leaves
+  if (p.T >= 1) {
+    if (kGru)
+      recv(1, (uint32_t)(p.T - 1) & 1u);
+    else
+      recv(p.T & 1, (uint32_t)((p.T - 1) >> 1) & 1u);
+  }
+  esn_cluster_sync();
 }
 
 struct EsnPlan {
@@ -345,6 +394,7 @@ int esn_plan(bool gru, int B, int dr, bool global_ok, int cs_cap, EsnPlan* pl) {
   if (e != cudaSuccess) return (int)e;
   e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (e != cudaSuccess) return (int)e;
+  smem_max -= 1024;   // the kernel's static shared memory (receive barriers)
   const int sms = num_sms();
   // candidate (CS, RB) -> filled plan, or false when it cannot run
   auto make = [&](int CS, int RB, EsnPlan* out, int* maxc) -> int {
@@ -474,6 +524,7 @@ int launch_esn_fwd(bool gru, int64_t B, int64_t T, int64_t dr, const float* U, c
   }
   p.leak = leak;
   p.H = H;
+  p.err = device_error_ptr();
   p.ncl = pl.ncl;
   p.off_h = pl.smemW ? G * pl.ncl * p.dr4 : 0;
   p.off_pre = p.off_h + 2 * pl.RB * p.dr4;
