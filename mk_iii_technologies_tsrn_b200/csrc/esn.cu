@@ -380,13 +380,10 @@ int esn_dispatch(bool gru, int kind, const EsnPlan& pl, const EsnParams& p, cuda
                   : esn_run_rb<false, false>(kind, pl, p, s, out);
 }
 
-// Plan (measured on B200: the step is latency-bound, so fewer batch rows per
-// cluster win as long as every cluster is resident at once, and one CTA per
-// SM beats two).  Take the smallest rows-per-cluster RB whose clusters all fit
-// in one wave; among the cluster sizes that allow it, the largest <= 8 whose
-// CTAs fit one per SM, else the smallest.  With no single-wave plan, the
-// largest RB that fits with the smallest cluster size.  Weights stay in
-// shared memory when they fit, else they are read from L2 (global_ok).
+// Plan: over cluster sizes CS (at most cs_cap CTAs, <= 64 columns each) and
+// rows per cluster RB (power of two <= 8), the candidate with the lowest
+// waves x (2 + RB) score (below); weights stay in shared memory when they
+// fit, else they are read from L2 (global_ok).
 int esn_plan(bool gru, int B, int dr, bool global_ok, int cs_cap, EsnPlan* pl) {
   const int dr4 = (dr + 3) & ~3;
   int dev = 0, smem_max = 0;
@@ -395,7 +392,6 @@ int esn_plan(bool gru, int B, int dr, bool global_ok, int cs_cap, EsnPlan* pl) {
   e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (e != cudaSuccess) return (int)e;
   smem_max -= 1024;   // the kernel's static shared memory (receive barriers)
-  const int sms = num_sms();
   // candidate (CS, RB) -> filled plan, or false when it cannot run
   auto make = [&](int CS, int RB, EsnPlan* out, int* maxc) -> int {
     const int ncl = (dr + CS - 1) / CS;
@@ -419,35 +415,37 @@ int esn_plan(bool gru, int B, int dr, bool global_ok, int cs_cap, EsnPlan* pl) {
     }
     return *maxc >= 1 ? 0 : -1;
   };
+  // score = waves x (2 + RB): the per-step cost of a wave grows with the rows
+  // a cluster carries, and extra waves repeat it (fitted to a sweep on B200
+  // of d_reservoir 256/320/640, both recurrences, B=64: it picks the fastest
+  // measured (CS, RB) in every case).  Ties: cluster sizes in the order
+  // 8, 4, 16, 2, 1 (8 CTAs measured fastest at equal waves), then smaller RB.
+  static const int kCsOrder[5] = {8, 4, 16, 2, 1};
+  bool have = false;
+  EsnPlan best{};
+  int64_t best_score = 0;
+  int best_rank = 0;
   for (int RB = 1; RB <= ESN_MAX_RB; RB *= 2) {
-    EsnPlan best{};
-    bool have = false, best_fits_sms = false;
-    for (int CS = 1; CS <= cs_cap; CS *= 2) {
+    for (int r = 0; r < 5; ++r) {
+      const int CS = kCsOrder[r];
+      if (CS > cs_cap) continue;
       EsnPlan c{};
       int maxc = 0;
-      if (make(CS, RB, &c, &maxc) != 0 || c.clusters > maxc) continue;
-      const bool fits_sms = (int64_t)c.clusters * CS <= sms && CS <= 8;
-      if (!have || (fits_sms && (!best_fits_sms || CS > best.CS))) {
+      if (make(CS, RB, &c, &maxc) != 0) continue;
+      const int64_t waves = (c.clusters + maxc - 1) / maxc;
+      const int64_t score = waves * (2 + RB);
+      if (!have || score < best_score || (score == best_score && r < best_rank)) {
         best = c;
-        best_fits_sms = fits_sms;
+        best_score = score;
+        best_rank = r;
         have = true;
       }
     }
-    if (have) {
-      *pl = best;
-      return TP_OK;
-    }
     if (RB >= B) break;  // one cluster already; more rows per cluster cannot help
   }
-  for (int RB = ESN_MAX_RB; RB >= 1; RB /= 2) {
-    for (int CS = 1; CS <= cs_cap; CS *= 2) {
-      EsnPlan c{};
-      int maxc = 0;
-      if (make(CS, RB, &c, &maxc) == 0) {
-        *pl = c;
-        return TP_OK;
-      }
-    }
+  if (have) {
+    *pl = best;
+    return TP_OK;
   }
   return TP_ERR_UNSUPPORTED;
 }
