@@ -204,7 +204,9 @@ __global__ void __launch_bounds__(ATT_THREADS) att_fwd_kernel(AttArgs p) {
         } else {
           const float d = acc[r][q];
           if (d >= 1e-30f) {
-            s = logf(d) + qmx[i] + kmx[j];
+            // fast log: absolute error ~1e-7 here, far inside the scores'
+            // 1e-5 tolerance (one per score: the epilogue bounds this kernel)
+            s = __logf(d) + qmx[i] + kmx[j];
           } else {
             // exact max-shifted log-sum-exp from the raw rows (rare)
             const float* qr = p.Q + (slice * p.T + i) * dh;
