@@ -396,6 +396,69 @@ def gen_real_weights(trop, research):
           **{f"p_{k}": _np(v).copy() for k, v in attn.state_dict().items()})
 
 
+def gen_dropin(dropin):
+    # tropformer_dropin.py modules in eval mode (dropout 0): the hybrid
+    # attention (self and cross, masks, KV-cache decoding), an encoder-decoder
+    # transformer, a causal LM; and training-mode gradients of an encoder layer
+    torch.manual_seed(15)
+    d, heads = 32, 4
+
+    def liven(mod):   # gates away from their initial constants, so both score kinds count
+        with torch.no_grad():
+            for name, prm in mod.named_parameters():
+                if "score_gate" in name or "gate_proj" in name or "lf_act" in name:
+                    prm.add_(torch.randn_like(prm) * 0.5)
+        return mod
+
+    out = {}
+    sa = liven(dropin.TropicalMultiHeadAttention(d, heads, dropout=0.0)).eval()
+    ca = liven(dropin.TropicalMultiHeadAttention(d, heads, dropout=0.0,
+                                                 is_cross_attention=True)).eval()
+    x = torch.randn(2, 7, d)
+    mem = torch.randn(2, 5, d)
+    mask = dropin.make_causal_mask(7, torch.device("cpu"))
+    pad = torch.zeros(2, 7, dtype=torch.bool)
+    pad[1, 5:] = True
+    with torch.no_grad():
+        out["sa_out"] = _np(sa(x, x, x, attn_mask=mask, key_padding_mask=pad)[0])
+        out["ca_out"] = _np(ca(x, mem, mem)[0])
+        cache = dropin.TropicalKVCache()
+        out["kv_out1"] = _np(sa(x[:, :4], x[:, :4], x[:, :4], cache=cache)[0])
+        out["kv_out2"] = _np(sa(x[:, 4:5], x[:, 4:5], x[:, 4:5], cache=cache)[0])
+    out.update({f"psa_{k}": _np(v).copy() for k, v in sa.state_dict().items()})
+    out.update({f"pca_{k}": _np(v).copy() for k, v in ca.state_dict().items()})
+    _save("dropin_attention", x=_np(x), mem=_np(mem), pad=pad.numpy(), **out)
+
+    torch.manual_seed(16)
+    tr = liven(dropin.TropicalTransformer(d_model=d, nhead=heads, num_encoder_layers=2,
+                                          num_decoder_layers=2, dim_feedforward=64,
+                                          dropout=0.0)).eval()
+    src, tgt = torch.randn(2, 6, d), torch.randn(2, 5, d)
+    with torch.no_grad():
+        y = tr(src, tgt, tgt_mask=dropin.make_causal_mask(5, torch.device("cpu")))
+    _save("dropin_transformer", src=_np(src), tgt=_np(tgt), out=_np(y),
+          **{f"p_{k}": _np(v).copy() for k, v in tr.state_dict().items()})
+
+    torch.manual_seed(17)
+    lm = liven(dropin.TropicalDecoderModel(50, d_model=d, nhead=heads, num_layers=2,
+                                           dim_feedforward=64, dropout=0.0,
+                                           max_seq_len=16)).eval()
+    ids = torch.randint(0, 50, (2, 9))
+    with torch.no_grad():
+        logits = lm(ids)
+    _save("dropin_lm", ids=ids.numpy(), logits=_np(logits),
+          **{f"p_{k}": _np(v).copy() for k, v in lm.state_dict().items()})
+
+    torch.manual_seed(18)
+    enc = liven(dropin.TropicalEncoderLayer(d, heads, dim_feedforward=64, dropout=0.0))
+    enc.train()
+    xe = torch.randn(2, 6, d)
+    state = {f"p_{k}": _np(v).copy() for k, v in enc.state_dict().items()}
+    enc(xe).square().sum().backward()
+    grads = {f"g_{k}": _np(p.grad) for k, p in enc.named_parameters()}
+    _save("dropin_encoder_grad", x=_np(xe), **state, **grads)
+
+
 def gen_tsrn_attention(research):
     # research TropicalAttention (research/tsrn_dml.py:355-548), eval, causal,
     # fast path: the module output, the Wo input (the attention context) and
@@ -433,6 +496,7 @@ def main():
     dtn = _load("deep_tropical_net", "deep_tropical_net.py")
     research = _load("research_tsrn_dml", "research/tsrn_dml.py")
     tsrn_gpu = _load("tsrn_gpu", "tsrn_gpu.py")
+    dropin = _load("tropformer_dropin", "tropformer_dropin.py")
     gen_kat(trop)
     gen_linear(trop)
     gen_bf16(trop)
@@ -443,6 +507,7 @@ def main():
     gen_esn(research)
     gen_esn_leaky(tsrn_gpu)
     gen_real_weights(trop, research)
+    gen_dropin(dropin)
 
 
 if __name__ == "__main__":

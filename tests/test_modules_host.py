@@ -131,3 +131,30 @@ def test_real_weight_state_dicts_load():
     m = TropicalAttention(128, top_k=8, n_heads=2)
     assert set(m.state_dict()) == set(att)
     m.load_state_dict({k: torch.tensor(v) for k, v in att.items()})
+
+
+@pytest.mark.parametrize("name,build", [
+    ("dropin_transformer", lambda d: d.TropicalTransformer(
+        d_model=32, nhead=4, num_encoder_layers=2, num_decoder_layers=2,
+        dim_feedforward=64, dropout=0.0)),
+    ("dropin_lm", lambda d: d.TropicalDecoderModel(
+        50, d_model=32, nhead=4, num_layers=2, dim_feedforward=64, dropout=0.0, max_seq_len=16)),
+    ("dropin_encoder_grad", lambda d: d.TropicalEncoderLayer(32, 4, dim_feedforward=64,
+                                                            dropout=0.0)),
+])
+def test_dropin_state_dicts_match_reference(name, build):
+    from mk_iii_technologies_tsrn_b200 import dropin
+    ref = _golden_state(name)
+    mod = build(dropin)
+    assert set(mod.state_dict()) == set(ref)
+    mod.load_state_dict({k: torch.tensor(v) for k, v in ref.items()})
+
+
+def test_dropin_kv_cache_appends():
+    from mk_iii_technologies_tsrn_b200.dropin import TropicalKVCache
+    c = TropicalKVCache()
+    k1, v1 = c.update(torch.zeros(1, 2, 3, 4), torch.ones(1, 2, 3, 4))
+    k2, v2 = c.update(torch.zeros(1, 2, 1, 4), torch.ones(1, 2, 1, 4))
+    assert k2.shape == (1, 2, 4, 4) and v2.shape == (1, 2, 4, 4)
+    c.reset()
+    assert c.k is None and c.v is None
