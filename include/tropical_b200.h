@@ -231,8 +231,9 @@ TP_API int tp_maxplus_bwd_smooth_ref(int mode, float tau, int dtype,
 TP_API int64_t tp_set_argmax_tma_min_terms(int64_t terms);
 
 /* Schedule of the large fp32 forward (TMA kernel): 0 = each CTA takes whole
- * 128x128 tiles; 1 (default) = stream-K when the tile count leaves the last
- * wave partly idle (with argmax: at least 5% of the run): whole-tile waves up
+ * 128x128 tiles; 1 (default) = stream-K when K >= 4096 and the tile count
+ * leaves the last wave partly idle (with argmax: at least 5% of the run):
+ * whole-tile waves up
  * to the last full one, then that wave's and the remaining tiles' 64-k chunks
  * split evenly over the CTAs; a tile shared by two CTAs is merged exactly
  * (values and argmax identical to the whole-tile schedule), using a

@@ -1285,17 +1285,20 @@ int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
     return launch_cfg16<DefaultCfg, false>(xmap, wmap, tp_, stream);
   }
   // Stream-K when the tiles leave the last wave partly idle (every CTA must
-  // cover at least one tile's chunks), unless the stream is being captured
-  // (the workspace is allocated on the stream).  With argmax only when that
-  // idle share is at least 5% of the run: below it the split tiles cost about
-  // what they save (measured: 8192 x 1024 x 8192, 3.46 waves, 5.62 -> 5.27 ms;
-  // 8192 x 2048 x 8192, 6.92 waves, 9.72 -> 9.97 ms; value-only gains in both).
+  // cover at least one tile's chunks) and K is long (K >= 4096: shorter tiles
+  // do not repay the split -- 2048^3 with argmax measured 1.07 ms whole-tile
+  // vs 1.17 ms split), unless the stream is being captured (the workspace is
+  // allocated on the stream).  With argmax only when the idle share is at
+  // least 5% of the run: below it the split tiles cost about what they save
+  // (measured: 8192 x 1024 x 8192, 3.46 waves, 5.62 -> 5.27 ms; 8192 x 2048 x
+  // 8192, 6.92 waves, 9.72 -> 9.97 ms; value-only gains in both).
   const int grid = std::min(num_sms(), tp_.num_tiles);
   const int mode = g_stream_k.load(std::memory_order_relaxed);
   const int waves = (int)ceil_div(tp_.num_tiles, grid);
   const double idle = (double)(waves * grid - tp_.num_tiles) / ((double)waves * grid);
   bool sk = mode != 0 && tp_.num_tiles >= grid && grid > 1 &&
-            (mode == 2 || (tp_.num_tiles % grid != 0 && (!p.am || idle >= 0.05)));
+            (mode == 2 || (tp_.num_tiles % grid != 0 && p.K >= 4096 &&
+                           (!p.am || idle >= 0.05)));
   void* ws = nullptr;
   if (sk) {
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
