@@ -17,17 +17,22 @@ import oracle
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("M,N,K,Ns,col0,force_tma", [
-    (512, 1024, 192, 512, 256, True),    # fused TMA epilogue (deferred argmax search)
-    (512, 1024, 192, 512, 256, False),   # below the TMA threshold: generic + copies
-    (96, 300, 50, 100, 150, False)])     # generic + copies
-def test_sharded_entry_two_local_destinations(cuda, M, N, K, Ns, col0, force_tma):
+@pytest.mark.parametrize("M,N,K,Ns,col0,force_tma,stream_k", [
+    (512, 1024, 192, 512, 256, True, 1),    # fused TMA epilogue (deferred argmax search)
+    (512, 1024, 192, 512, 256, False, 1),   # below the TMA threshold: generic + copies
+    (96, 300, 50, 100, 150, False, 1),      # generic + copies
+    # 160 tiles: the stream-K schedule (forced) with the destination stores of
+    # the split tiles' merges, as an 8-rank shard of a large GEMM takes it
+    (2048, 2560, 256, 1280, 640, True, 2)])
+def test_sharded_entry_two_local_destinations(cuda, M, N, K, Ns, col0, force_tma, stream_k):
     from mk_iii_technologies_tsrn_b200 import _lib
     lib = _lib.load()
     old = lib.tp_set_argmax_tma_min_terms(0 if force_tma else 1 << 30)
+    old_sk = lib.tp_set_stream_k(stream_k)
     try:
         _two_local_destinations(lib, cuda, M, N, K, Ns, col0)
     finally:
+        lib.tp_set_stream_k(old_sk)
         lib.tp_set_argmax_tma_min_terms(old)
 
 
