@@ -178,6 +178,71 @@ def maxplus(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = Non
     return maxplus_strided(x, w, bias, argmax=argmax, arith=arith)
 
 
+def maxplus_host(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                 *, argmax: bool = True, out: Optional[torch.Tensor] = None,
+                 out_argmax: Optional[torch.Tensor] = None, blocks: int = 4):
+    """``maxplus`` on host-resident operands, results back in host memory, with the
+    PCIe transfers overlapped with the computation.
+
+    ``x`` [M,K], ``w`` [N,K] (and ``bias`` [N]) are CPU fp32 tensors, best pinned.
+    W goes to the current CUDA device first; x follows in ``blocks`` row blocks on
+    one copy stream while earlier blocks compute on the caller's current stream,
+    and each block's y (and argmax) returns on a second copy stream.  Returns
+    pinned host tensors (or fills ``out`` / ``out_argmax``); like any non-blocking
+    copy they are complete once the current stream has been synchronised.  The
+    results equal ``maxplus`` on device copies of the operands."""
+    if x.is_cuda or w.is_cuda or (bias is not None and bias.is_cuda):
+        raise ValueError("maxplus_host takes host tensors; use maxplus for device tensors")
+    if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1]:
+        raise ValueError("maxplus_host takes x [M,K] and w [N,K]")
+    _lib.load()  # no CPU computation: fails loudly without the CUDA library
+    dev = torch.device("cuda", torch.cuda.current_device())
+    M, K = x.shape
+    N = w.shape[0]
+    y = out if out is not None else torch.empty(M, N, pin_memory=True)
+    am = None
+    if argmax:
+        am = out_argmax if out_argmax is not None else torch.empty(M, N, dtype=torch.int32,
+                                                                   pin_memory=True)
+    main = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    # device buffers belong to the caller's stream, which waits for both copy
+    # streams before returning: the caching allocator reuses them only afterwards
+    dx = torch.empty(M, K, device=dev)
+    dw = torch.empty(N, K, device=dev)
+    dy = torch.empty(M, N, device=dev)
+    da = torch.empty(M, N, device=dev, dtype=torch.int32) if argmax else None
+    db = torch.empty(N, device=dev) if bias is not None else None
+    s_in.wait_stream(main)
+    s_out.wait_stream(main)
+    step = max(128, -(-(-(-M // max(1, blocks))) // 128) * 128)
+    ranges = [(a, min(M, a + step)) for a in range(0, M, step)]
+    ev_x = []
+    with torch.cuda.stream(s_in):
+        dw.copy_(_f32(w), non_blocking=True)
+        if db is not None:
+            db.copy_(_f32(bias), non_blocking=True)
+        for a, b in ranges:
+            dx[a:b].copy_(_f32(x[a:b]), non_blocking=True)
+            e = torch.cuda.Event()
+            e.record(s_in)
+            ev_x.append(e)
+    for (a, b), e in zip(ranges, ev_x):
+        main.wait_event(e)          # W, bias and this block of x are on the device
+        maxplus_strided(dx[a:b], dw, db, argmax=argmax, out=dy[a:b],
+                        out_argmax=da[a:b] if argmax else None)
+        done = torch.cuda.Event()
+        done.record(main)
+        s_out.wait_event(done)
+        with torch.cuda.stream(s_out):
+            y[a:b].copy_(dy[a:b], non_blocking=True)
+            if argmax:
+                am[a:b].copy_(da[a:b], non_blocking=True)
+    main.wait_stream(s_out)
+    main.wait_stream(s_in)
+    return y, am
+
+
 LF_MODES = {"primal": 0, "dual": 1, "blend": 2}
 
 
