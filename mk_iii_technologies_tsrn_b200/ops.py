@@ -185,12 +185,21 @@ def maxplus_host(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] 
     PCIe transfers overlapped with the computation.
 
     ``x`` [M,K], ``w`` [N,K] (and ``bias`` [N]) are CPU fp32 tensors, best pinned.
-    W goes to the current CUDA device first; x follows in ``blocks`` row blocks on
-    one copy stream while earlier blocks compute on the caller's current stream,
-    and each block's y (and argmax) returns on a second copy stream.  Returns
-    pinned host tensors (or fills ``out`` / ``out_argmax``); like any non-blocking
-    copy they are complete once the current stream has been synchronised.  The
-    results equal ``maxplus`` on device copies of the operands."""
+    Copies to the current CUDA device run on one stream, computation on the
+    caller's current stream, results return on a second stream:
+
+    * W travels in ``blocks`` row blocks (output columns), the first of them
+      ahead of the first row block of x, so the first row block computes as one
+      product per W block, each starting as soon as its block has landed;
+    * x travels in ``blocks`` row blocks (the last one halved, so that less is
+      left to return after the last product); each later block computes
+      against all of W once it has landed;
+    * each row block's y (and argmax) returns as soon as it is complete.
+
+    Returns pinned host tensors (or fills ``out`` / ``out_argmax``); like any
+    non-blocking copy they are complete once the current stream has been
+    synchronised.  The results equal ``maxplus`` on device copies of the
+    operands bit for bit."""
     if x.is_cuda or w.is_cuda or (bias is not None and bias.is_cuda):
         raise ValueError("maxplus_host takes host tensors; use maxplus for device tensors")
     if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1]:
@@ -199,6 +208,7 @@ def maxplus_host(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] 
     dev = torch.device("cuda", torch.cuda.current_device())
     M, K = x.shape
     N = w.shape[0]
+    blocks = max(1, int(blocks))
     y = out if out is not None else torch.empty(M, N, pin_memory=True)
     am = None
     if argmax:
@@ -215,22 +225,51 @@ def maxplus_host(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] 
     db = torch.empty(N, device=dev) if bias is not None else None
     s_in.wait_stream(main)
     s_out.wait_stream(main)
-    step = max(128, -(-(-(-M // max(1, blocks))) // 128) * 128)
-    ranges = [(a, min(M, a + step)) for a in range(0, M, step)]
-    ev_x = []
+
+    def spans(n, parts):
+        step = max(128, -(-(-(-n // parts)) // 128) * 128)
+        return [(a, min(n, a + step)) for a in range(0, n, step)]
+
+    rows = spans(M, blocks)
+    last_a, last_b = rows[-1]
+    if last_b - last_a >= 256:               # halve the last row block
+        mid = last_a + (((last_b - last_a) // 2 + 127) // 128) * 128
+        rows[-1:] = [(last_a, mid), (mid, last_b)]
+    cols = spans(N, blocks)
+
+    ev_w, ev_x = [], []
     with torch.cuda.stream(s_in):
-        dw.copy_(_f32(w), non_blocking=True)
-        if db is not None:
-            db.copy_(_f32(bias), non_blocking=True)
-        for a, b in ranges:
+        for j, (c0, c1) in enumerate(cols):
+            dw[c0:c1].copy_(_f32(w[c0:c1]), non_blocking=True)
+            if db is not None:
+                db[c0:c1].copy_(_f32(bias[c0:c1]), non_blocking=True)
+            e = torch.cuda.Event()
+            e.record(s_in)
+            ev_w.append(e)
+            if j == 0:
+                a, b = rows[0]
+                dx[a:b].copy_(_f32(x[a:b]), non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(s_in)
+                ev_x.append(e)
+        for a, b in rows[1:]:
             dx[a:b].copy_(_f32(x[a:b]), non_blocking=True)
             e = torch.cuda.Event()
             e.record(s_in)
             ev_x.append(e)
-    for (a, b), e in zip(ranges, ev_x):
-        main.wait_event(e)          # W, bias and this block of x are on the device
-        maxplus_strided(dx[a:b], dw, db, argmax=argmax, out=dy[a:b],
-                        out_argmax=da[a:b] if argmax else None)
+
+    for i, ((a, b), e) in enumerate(zip(rows, ev_x)):
+        main.wait_event(e)
+        if i == 0 and len(cols) > 1:
+            for (c0, c1), ew in zip(cols, ev_w):
+                main.wait_event(ew)
+                maxplus_strided(dx[a:b], dw[c0:c1], db[c0:c1] if db is not None else None,
+                                argmax=argmax, out=dy[a:b, c0:c1],
+                                out_argmax=da[a:b, c0:c1] if argmax else None)
+        else:
+            main.wait_event(ev_w[-1])   # all of W (in stream order before this x block)
+            maxplus_strided(dx[a:b], dw, db, argmax=argmax, out=dy[a:b],
+                            out_argmax=da[a:b] if argmax else None)
         done = torch.cuda.Event()
         done.record(main)
         s_out.wait_event(done)
