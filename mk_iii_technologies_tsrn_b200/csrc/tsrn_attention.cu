@@ -242,6 +242,34 @@ __global__ void __launch_bounds__(ATT_THREADS) att_fwd_kernel(AttArgs p) {
 #pragma unroll
     for (int u = 0; u < ATT_MAX_DH / 32; ++u) oacc[u] = 0.0f;
     const float* Vs = p.V + slice * Tkv * dh;
+    // out += sum over the kept keys j = jbase + (bits of mask) of weight * V[j]:
+    // four kept keys at a time, their V rows loaded before any is accumulated
+    // (same order of accumulation as one key at a time)
+    auto gather = [&](unsigned mask, float wl, int64_t jbase) {
+      while (mask) {
+        int src[4];
+        float wv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          src[e] = mask ? __ffs(mask) - 1 : -1;
+          if (mask) mask &= mask - 1;
+          wv[e] = __shfl_sync(0xffffffffu, wl, src[e] < 0 ? 0 : src[e]);
+        }
+        float val[4][ATT_MAX_DH / 32];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+#pragma unroll
+          for (int q = 0; q < ATT_MAX_DH / 32; ++q) {
+            const int c = lane + 32 * q;
+            val[e][q] = (src[e] >= 0 && c < dh) ? __ldg(Vs + (jbase + src[e]) * dh + c) : 0.0f;
+          }
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (src[e] >= 0)
+#pragma unroll
+            for (int q = 0; q < ATT_MAX_DH / 32; ++q) oacc[q] = fmaf(wv[e], val[e][q], oacc[q]);
+      }
+    };
     if constexpr (PL > 0) {
       // the row in registers (slots past Tkv read -inf: with at least top_k
       // real keys, extra -inf entries never change the threshold)
@@ -338,19 +366,9 @@ __global__ void __launch_bounds__(ATT_THREADS) att_fwd_kernel(AttArgs p) {
       for (int u = 0; u < PL; ++u) {
         const int64_t jl = lane + 32 * (int64_t)u;
         const bool kept = jl < Tkv && !(v[u] < thr) && v[u] != NEG_INF;
-        unsigned mask = __ballot_sync(0xffffffffu, kept);
+        const unsigned mask = __ballot_sync(0xffffffffu, kept);
         const float wl = kept ? expf(v[u] - rowmax) * invz : 0.0f;
-        while (mask) {
-          const int src = __ffs(mask) - 1;
-          mask &= mask - 1;
-          const float wv = __shfl_sync(0xffffffffu, wl, src);
-          const int64_t j = 32 * (int64_t)u + src;
-#pragma unroll
-          for (int q = 0; q < ATT_MAX_DH / 32; ++q) {
-            const int c = lane + 32 * q;
-            if (c < dh) oacc[q] = fmaf(wv, __ldg(Vs + j * dh + c), oacc[q]);
-          }
-        }
+        gather(mask, wl, 32 * (int64_t)u);
       }
     } else {
     // threshold: top_k-th largest value, ties counted (torch.topk(k)[..., -1])
@@ -398,19 +416,9 @@ __global__ void __launch_bounds__(ATT_THREADS) att_fwd_kernel(AttArgs p) {
       const int64_t jl = jb + lane;
       const float v = jl < Tkv ? sval(jl) : NEG_INF;
       const bool kept = jl < Tkv && !(v < thr) && v != NEG_INF;
-      unsigned mask = __ballot_sync(0xffffffffu, kept);
+      const unsigned mask = __ballot_sync(0xffffffffu, kept);
       const float wl = kept ? expf(v - rowmax) * invz : 0.0f;
-      while (mask) {
-        const int src = __ffs(mask) - 1;
-        mask &= mask - 1;
-        const float wv = __shfl_sync(0xffffffffu, wl, src);
-        const int64_t j = jb + src;
-#pragma unroll
-        for (int q = 0; q < ATT_MAX_DH / 32; ++q) {
-          const int c = lane + 32 * q;
-          if (c < dh) oacc[q] = fmaf(wv, __ldg(Vs + j * dh + c), oacc[q]);
-        }
-      }
+      gather(mask, wl, jb);
     }
     }
     float* orow = p.out + (slice * p.T + i) * dh;
