@@ -355,20 +355,80 @@ __global__ void __launch_bounds__(ATT_THREADS) att_fwd_kernel(AttArgs p) {
         need -= cnt;
         cur = nxt;
       }
-      float z = 0.0f;
-#pragma unroll
-      for (int u = 0; u < PL; ++u)
-        if (!(v[u] < thr) && v[u] != NEG_INF) z += expf(v[u] - rowmax);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-      const float invz = 1.0f / z;
+      // kept keys (ascending j): count them; when at most ATT_MAX_TOPK, list
+      // them (index, score) in this row's own score slots -- the row is in
+      // registers, so the slots are free -- and form the softmax and the V
+      // gather over the list only
+      int nk = 0;
 #pragma unroll
       for (int u = 0; u < PL; ++u) {
         const int64_t jl = lane + 32 * (int64_t)u;
-        const bool kept = jl < Tkv && !(v[u] < thr) && v[u] != NEG_INF;
-        const unsigned mask = __ballot_sync(0xffffffffu, kept);
-        const float wl = kept ? expf(v[u] - rowmax) * invz : 0.0f;
-        gather(mask, wl, 32 * (int64_t)u);
+        nk += __popc(__ballot_sync(0xffffffffu,
+                                   jl < Tkv && !(v[u] < thr) && v[u] != NEG_INF));
+      }
+      if (nk <= ATT_MAX_TOPK && tkv_pad >= 2 * ATT_MAX_TOPK) {
+        float* slot = S + rr * tkv_pad;          // this warp's row
+        int* kidx = reinterpret_cast<int*>(slot);
+        float* kval = slot + ATT_MAX_TOPK;
+        __syncwarp();
+        int base = 0;
+#pragma unroll
+        for (int u = 0; u < PL; ++u) {
+          const int64_t jl = lane + 32 * (int64_t)u;
+          const bool kept = jl < Tkv && !(v[u] < thr) && v[u] != NEG_INF;
+          const unsigned mask = __ballot_sync(0xffffffffu, kept);
+          if (kept) {
+            const int pos = base + __popc(mask & ((1u << lane) - 1u));
+            kidx[pos] = (int)jl;
+            kval[pos] = v[u];
+          }
+          base += __popc(mask);
+        }
+        __syncwarp();
+        float z = 0.0f;
+        for (int e = lane; e < nk; e += 32) z += expf(kval[e] - rowmax);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+        const float invz = 1.0f / z;
+        for (int e0 = 0; e0 < nk; e0 += 4) {
+          int jj[4];
+          float wv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const bool ok = e0 + e < nk;
+            jj[e] = ok ? kidx[e0 + e] : -1;
+            wv[e] = ok ? expf(kval[e0 + e] - rowmax) * invz : 0.0f;
+          }
+          float val[4][ATT_MAX_DH / 32];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+#pragma unroll
+            for (int q = 0; q < ATT_MAX_DH / 32; ++q) {
+              const int c = lane + 32 * q;
+              val[e][q] = (jj[e] >= 0 && c < dh) ? __ldg(Vs + (int64_t)jj[e] * dh + c) : 0.0f;
+            }
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (jj[e] >= 0)
+#pragma unroll
+              for (int q = 0; q < ATT_MAX_DH / 32; ++q) oacc[q] = fmaf(wv[e], val[e][q], oacc[q]);
+        }
+      } else {
+        float z = 0.0f;
+#pragma unroll
+        for (int u = 0; u < PL; ++u)
+          if (!(v[u] < thr) && v[u] != NEG_INF) z += expf(v[u] - rowmax);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+        const float invz = 1.0f / z;
+#pragma unroll
+        for (int u = 0; u < PL; ++u) {
+          const int64_t jl = lane + 32 * (int64_t)u;
+          const bool kept = jl < Tkv && !(v[u] < thr) && v[u] != NEG_INF;
+          const unsigned mask = __ballot_sync(0xffffffffu, kept);
+          const float wl = kept ? expf(v[u] - rowmax) * invz : 0.0f;
+          gather(mask, wl, 32 * (int64_t)u);
+        }
       }
     } else {
     // threshold: top_k-th largest value, ties counted (torch.topk(k)[..., -1])
