@@ -299,6 +299,41 @@ TP_API int tp_esn_leaky_fwd(int64_t B, int64_t T, int64_t dr, const float* U, co
                             int64_t ld_ws, const float* leak, float* H, void* stream);
 
 /* ======================================================================== *
+ *  Maslov softmax of attention scores, optionally gated (one warp per row).
+ *
+ *  tp_maslov_softmax_fwd replaces MaslovTemperature.forward
+ *  (tropformer.py:206-212) and, with C != NULL, the score blend before it in
+ *  DTNAttention.forward (deep_tropical_net.py:152-160):
+ *    s = C ? g*T + (1-g)*C : T;   s = -1e9 where mask != 0;
+ *    P = softmax(s / tau[h]) over the last dimension.
+ *  T, C, P: [B, H, Lq, Lk] contiguous fp32 (T = the tropical scores, C = the
+ *  classical ones); g: the gate sigmoid(score_gate(x)) read at
+ *  g[b*gsb + i*gsi + h*gsh] (NULL iff C is NULL); mask: bytes, nonzero where
+ *  the module's mask == 0, at mask[b*msb + h*msh + i*msi + j*msj] (strides
+ *  may be 0 to broadcast), or NULL; tau: [H] device temperatures.  The blend
+ *  and the division round like the PyTorch expression; the softmax differs
+ *  from PyTorch's only in exp rounding and summation order.
+ *
+ *  tp_maslov_softmax_bwd is the autograd backward of that chain, given P and
+ *  dP = dL/dP: dz = P*(dP - sum_j P*dP), ds = dz / tau (0 where masked),
+ *  dT = g*ds (ds without C), dC = (1-g)*ds, dg[b,i,h] (strides of g) =
+ *  sum_j ds*T - sum_j ds*C, dtau_rows[row] = sum_j dz*s (row = (b*H+h)*Lq+i);
+ *  the caller forms dL/dtau[h] = -(sum of h's dtau_rows) / tau[h]^2.  Any
+ *  output may be NULL.
+ * ======================================================================== */
+TP_API int tp_maslov_softmax_fwd(int64_t B, int64_t H, int64_t Lq, int64_t Lk, const float* T,
+                                 const float* C, const float* g, int64_t gsb, int64_t gsi,
+                                 int64_t gsh, const unsigned char* mask, int64_t msb,
+                                 int64_t msh, int64_t msi, int64_t msj, const float* tau,
+                                 float* P, void* stream);
+TP_API int tp_maslov_softmax_bwd(int64_t B, int64_t H, int64_t Lq, int64_t Lk, const float* T,
+                                 const float* C, const float* g, int64_t gsb, int64_t gsi,
+                                 int64_t gsh, const unsigned char* mask, int64_t msb,
+                                 int64_t msh, int64_t msi, int64_t msj, const float* tau,
+                                 const float* P, const float* dP, float* dT, float* dC,
+                                 float* dg, float* dtau_rows, void* stream);
+
+/* ======================================================================== *
  *  Tropical (max-plus) diagonal SSM scan  (research/tsrn_dml.py:917-980)
  *
  *    u[b,t,c] = bb[b,t,c] + xx[b,t,c]     (xx may be NULL: u = bb)

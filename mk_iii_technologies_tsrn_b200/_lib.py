@@ -114,6 +114,16 @@ SIGNATURES: dict[str, tuple] = {
         [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_int, _c_int,
          _c_p, _c_p, _c_i64, _c_p],
     ),
+    "tp_maslov_softmax_fwd": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64,
+         _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p],
+    ),
+    "tp_maslov_softmax_bwd": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64,
+         _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p],
+    ),
     "tp_last_error": (_c_int, []),
     "tp_device_error": (_c_int, [_c_int]),
 }

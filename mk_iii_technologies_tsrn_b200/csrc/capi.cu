@@ -470,6 +470,87 @@ int tp_esn_leaky_fwd(int64_t B, int64_t T, int64_t dr, const float* U, const flo
                             as_stream(stream));
 }
 
+namespace {
+
+// shared argument checks of the two Maslov softmax entries (T and C are
+// not read when Lk == 0)
+int maslov_args(int64_t B, int64_t H, int64_t Lq, int64_t Lk, const float* T, const float* C,
+                const float* g, int64_t gsb, int64_t gsi, int64_t gsh,
+                const unsigned char* mask, int64_t msb, int64_t msh, int64_t msi, int64_t msj,
+                const float* tau, tp::MaslovArgs& a) {
+  TP_RETURN_IF(B < 0 || H < 0 || Lq < 0 || Lk < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(Lk > 0 && (C == nullptr) != (g == nullptr), TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(gsb < 0 || gsi < 0 || gsh < 0 || msb < 0 || msh < 0 || msi < 0 || msj < 0,
+               TP_ERR_INVALID_ARG);
+  a = tp::MaslovArgs{};
+  a.rows = B * H * Lq;
+  a.H = H;
+  a.Lq = Lq;
+  a.Lk = Lk;
+  a.T = T;
+  a.C = C;
+  a.g = g;
+  a.gsb = gsb;
+  a.gsi = gsi;
+  a.gsh = gsh;
+  a.mask = mask;
+  a.msb = msb;
+  a.msh = msh;
+  a.msi = msi;
+  a.msj = msj;
+  a.tau = tau;
+  if (a.rows == 0) return TP_OK;
+  TP_CHECK_PTR(tau);
+  if (g) TP_CHECK_PTR(g);
+  if (Lk > 0) {
+    TP_CHECK_PTR(T);
+    if (C) TP_CHECK_PTR(C);
+    if (mask) TP_CHECK_PTR(mask);
+  }
+  return TP_OK;
+}
+
+}  // namespace
+
+int tp_maslov_softmax_fwd(int64_t B, int64_t H, int64_t Lq, int64_t Lk, const float* T,
+                          const float* C, const float* g, int64_t gsb, int64_t gsi, int64_t gsh,
+                          const unsigned char* mask, int64_t msb, int64_t msh, int64_t msi,
+                          int64_t msj, const float* tau, float* P, void* stream) {
+  tp::MaslovArgs a;
+  int st = maslov_args(B, H, Lq, Lk, T, C, g, gsb, gsi, gsh, mask, msb, msh, msi, msj, tau, a);
+  if (st != TP_OK || a.rows == 0 || Lk == 0) return st;
+  TP_CHECK_PTR(P);
+  a.P = P;
+  return tp::launch_maslov(a, false, as_stream(stream));
+}
+
+int tp_maslov_softmax_bwd(int64_t B, int64_t H, int64_t Lq, int64_t Lk, const float* T,
+                          const float* C, const float* g, int64_t gsb, int64_t gsi, int64_t gsh,
+                          const unsigned char* mask, int64_t msb, int64_t msh, int64_t msi,
+                          int64_t msj, const float* tau, const float* P, const float* dP,
+                          float* dT, float* dC, float* dg, float* dtau_rows, void* stream) {
+  tp::MaslovArgs a;
+  int st = maslov_args(B, H, Lq, Lk, T, C, g, gsb, gsi, gsh, mask, msb, msh, msi, msj, tau, a);
+  if (st != TP_OK || a.rows == 0) return st;
+  if (Lk > 0) {
+    TP_CHECK_PTR(P);
+    TP_CHECK_PTR(dP);
+    if (dT) TP_CHECK_PTR(dT);
+    if (dC) TP_CHECK_PTR(dC);
+  } else if (dg == nullptr && dtau_rows == nullptr) {
+    return TP_OK;              // empty rows and no per-row output
+  }
+  if (dg) TP_CHECK_PTR(dg);
+  if (dtau_rows) TP_CHECK_PTR(dtau_rows);
+  a.P = const_cast<float*>(P);
+  a.dP = dP;
+  a.dT = dT;
+  a.dC = dC;
+  a.dg = g ? dg : nullptr;
+  a.dtau_rows = dtau_rows;
+  return tp::launch_maslov(a, true, as_stream(stream));
+}
+
 int64_t tp_set_argmax_tma_min_terms(int64_t terms) { return tp::set_argmax_tma_min_terms(terms); }
 
 int tp_set_stream_k(int mode) { return tp::set_stream_k(mode); }

@@ -196,4 +196,25 @@ int launch_esn_fwd(bool gru, int64_t B, int64_t T, int64_t dr, const float* U, c
                    const float* Ur, const float* const W[3], const int64_t ld[3],
                    const float* leak, float* H, cudaStream_t stream);
 
+// maslov.cu: (gated) Maslov softmax of attention scores.  Scores T, C, P, dP,
+// dT, dC: [rows = B*H*Lq, Lk] contiguous; g / dg at b*gsb + i*gsi + h*gsh;
+// mask bytes (nonzero = masked) at b*msb + h*msh + i*msi + j*msj.
+struct MaslovArgs {
+  int64_t rows, H, Lq, Lk;
+  const float* T;
+  const float* C;
+  const float* g;
+  int64_t gsb, gsi, gsh;
+  const unsigned char* mask;
+  int64_t msb, msh, msi, msj;
+  const float* tau;
+  float* P;            // forward: output; backward: input
+  const float* dP;
+  float* dT;
+  float* dC;
+  float* dg;
+  float* dtau_rows;
+};
+int launch_maslov(const MaslovArgs& a, bool backward, cudaStream_t stream);
+
 }  // namespace tp

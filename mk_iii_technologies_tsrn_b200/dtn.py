@@ -5,14 +5,15 @@ Same constructor, sub-module names and state-dict keys as the reference
 classical; ``maslov``; ``attn_dropout``), so a reference checkpoint loads
 unchanged.  The tropical Q/K projections run the max-plus GEMM kernels and
 the tropical score runs the batched max-plus kernel on strided head views;
-the classical parts stay in PyTorch.
+the gate blend, mask and Maslov softmax run as one kernel (forward and
+backward); the classical linears and products stay in PyTorch.
 """
 from __future__ import annotations
 
 import torch
 import torch.nn as nn
 
-from . import tropical
+from . import ops, tropical
 from .tropical import LFDualActivation, MaslovTemperature, TropicalLinear, tropical_up_lf
 
 
@@ -46,11 +47,11 @@ class DTNAttention(nn.Module):
         V = self._split_heads(self.v_proj(x))
         class_scores = torch.matmul(Q, K.transpose(-2, -1)) * self._scale
         trop_scores = tropical.tropical_score(Q, K, self._scale)
-        g = torch.sigmoid(self.score_gate(x)).permute(0, 2, 1).unsqueeze(-1)
-        scores = g * trop_scores + (1.0 - g) * class_scores
-        if mask is not None:
-            scores = scores.masked_fill(mask == 0, -1e9)
-        attn = self.attn_dropout(self.maslov(scores))
+        g = torch.sigmoid(self.score_gate(x))                     # [B, L, H]
+        # gate blend, mask and Maslov softmax in one kernel (:152-160)
+        attn = ops.maslov_softmax(trop_scores, self.maslov.temperatures,
+                                  classical=class_scores, gate=g, mask=mask)
+        attn = self.attn_dropout(attn)
         out = torch.matmul(attn, V).transpose(1, 2).contiguous().view(B, L, D)
         return self.out_proj(out), attn
 

@@ -724,3 +724,103 @@ def esn_leaky_fwd(U: torch.Tensor, Ws: torch.Tensor, lk: torch.Tensor) -> torch.
                                   _stream(dev))
     _lib.check(st, "tp_esn_leaky_fwd")
     return H
+
+
+def _maslov_inputs(T, C, g, tau, mask):
+    """Contiguous fp32 scores, gate [B, Lq, H] and temperatures [H]; the mask
+    as bytes (True where the module's ``mask == 0``) broadcast to [B, H, Lq, Lk]."""
+    dev = _require_cuda(T, C, g, tau)
+    if T.dim() != 4:
+        raise ValueError("scores must be [B, H, Lq, Lk]")
+    B, H, Lq, Lk = T.shape
+    T = _f32(T).contiguous()
+    if (C is None) != (g is None):
+        raise ValueError("the classical scores and the gate come together")
+    if C is not None:
+        if C.shape != T.shape:
+            raise ValueError(f"classical scores {tuple(C.shape)} != {tuple(T.shape)}")
+        if g.shape != (B, Lq, H):
+            raise ValueError(f"gate must be [B, Lq, H] = {(B, Lq, H)}, got {tuple(g.shape)}")
+        C, g = _f32(C).contiguous(), _f32(g).contiguous()
+    if tau.shape != (H,):
+        raise ValueError(f"tau must be [H] = ({H},), got {tuple(tau.shape)}")
+    tau = _f32(tau).detach().contiguous()
+    m, ms = None, (0, 0, 0, 0)
+    if mask is not None:
+        if mask.device != dev:
+            raise RuntimeError(f"mask on {mask.device}, scores on {dev}")
+        m = torch.broadcast_to(mask == 0, (B, H, Lq, Lk))
+        ms = tuple(m.stride())
+    return dev, (B, H, Lq, Lk), T, C, g, tau, m, ms
+
+
+def _gate_strides(g):
+    return (0, 0, 0) if g is None else tuple(g.stride())
+
+
+def maslov_softmax_fwd(T, C, g, tau, mask=None) -> torch.Tensor:
+    """softmax((g*T + (1-g)*C masked to -1e9 where mask == 0) / tau_h) over the
+    last dim (without C and g: softmax(T / tau_h)) -- DTNAttention's score blend
+    and MaslovTemperature (deep_tropical_net.py:152-160, tropformer.py:206-212)."""
+    dev, (B, H, Lq, Lk), T, C, g, tau, m, ms = _maslov_inputs(T, C, g, tau, mask)
+    P = torch.empty_like(T)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        st = lib.tp_maslov_softmax_fwd(B, H, Lq, Lk, _ptr(T), _ptr(C), _ptr(g), *_gate_strides(g),
+                                       _ptr(m), *ms, _ptr(tau), _ptr(P), _stream(dev))
+    _lib.check(st, "tp_maslov_softmax_fwd")
+    return P
+
+
+class MaslovSoftmaxFunction(torch.autograd.Function):
+    """Autograd of the (gated) Maslov softmax: gradients for the tropical and
+    classical scores, the gate and the temperatures, as PyTorch's autograd of
+    the module expression forms them (deep_tropical_net.py:152-160)."""
+
+    @staticmethod
+    def forward(ctx, T, C, g, tau, mask):
+        dev, shape, Tc, Cc, gc, tc, m, ms = _maslov_inputs(T, C, g, tau, mask)
+        P = torch.empty_like(Tc)
+        lib = _lib.load()
+        with torch.cuda.device(dev):
+            st = lib.tp_maslov_softmax_fwd(*shape, _ptr(Tc), _ptr(Cc), _ptr(gc),
+                                           *_gate_strides(gc), _ptr(m), *ms, _ptr(tc), _ptr(P),
+                                           _stream(dev))
+        _lib.check(st, "tp_maslov_softmax_fwd")
+        ctx.save_for_backward(Tc, Cc, gc, tc, P)
+        ctx.mask = (m, ms)
+        ctx.shape = shape
+        return P
+
+    @staticmethod
+    def backward(ctx, dP):
+        T, C, g, tau, P = ctx.saved_tensors
+        m, ms = ctx.mask
+        B, H, Lq, Lk = ctx.shape
+        need_T, need_C, need_g, need_tau = ctx.needs_input_grad[:4]
+        dev = T.device
+        dP = _f32(dP).contiguous()
+        dT = torch.empty_like(T) if need_T else None
+        dC = torch.empty_like(T) if (need_C and C is not None) else None
+        dg = torch.empty_like(g) if (need_g and g is not None) else None
+        rows = torch.empty(B * H * Lq, device=dev) if need_tau else None
+        lib = _lib.load()
+        with torch.cuda.device(dev):
+            st = lib.tp_maslov_softmax_bwd(B, H, Lq, Lk, _ptr(T), _ptr(C), _ptr(g),
+                                           *_gate_strides(g), _ptr(m), *ms, _ptr(tau), _ptr(P),
+                                           _ptr(dP), _ptr(dT), _ptr(dC), _ptr(dg), _ptr(rows),
+                                           _stream(dev))
+        _lib.check(st, "tp_maslov_softmax_bwd")
+        dtau = None
+        if need_tau:
+            dtau = -rows.view(B, H, Lq).sum(dim=(0, 2)) / (tau * tau)
+        return dT, dC, dg, dtau, None
+
+
+def maslov_softmax(scores: torch.Tensor, tau: torch.Tensor, *,
+                   classical: Optional[torch.Tensor] = None, gate: Optional[torch.Tensor] = None,
+                   mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Differentiable ``softmax(s / tau_h)`` with ``s = gate*scores +
+    (1-gate)*classical`` (or ``scores``), set to -1e9 where ``mask == 0``;
+    ``scores``/``classical`` [B, H, Lq, Lk], ``gate`` [B, Lq, H], ``tau`` [H]."""
+    return MaslovSoftmaxFunction.apply(scores, classical, gate, tau, mask)

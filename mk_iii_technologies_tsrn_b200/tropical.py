@@ -24,7 +24,6 @@ import math
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from . import ops
 from .ops import MaxPlusLinearFunction, TropicalScoreFunction
@@ -87,8 +86,9 @@ class MaslovTemperature(nn.Module):
         return self.log_temps.exp().clamp(min=0.02, max=10.0)
 
     def forward(self, scores: torch.Tensor) -> torch.Tensor:
-        tau = self.temperatures.view(1, -1, 1, 1)
-        return F.softmax(scores / tau, dim=-1)
+        """``scores`` [B, H, Lq, Lk] -> softmax over keys at temperature tau_h
+        (one fused kernel, forward and backward)."""
+        return ops.maslov_softmax(scores, self.temperatures)
 
     def extra_repr(self) -> str:
         t = self.temperatures.detach()
