@@ -410,7 +410,9 @@ TP_API int tp_convert_bf16_to_f32(int64_t n, const void* src, float* dst, void* 
  *  terms; form 4: forms 2 and 3 alternating; form 5: packed add.bf16x2 +
  *  max.bf16x2 per two terms (bf16 arithmetic); form 6: form 5 with the
  *  NaN-propagating max; form 7: fp32 fma (a term is one FMA, 2 flops: the
- *  CUDA-core peak of dot products).  Each of `threads` threads runs `iters`
+ *  CUDA-core peak of dot products); form 8: the smooth backward's per-term
+ *  shape with one ex2.approx per term (a term is one exponential: the SFU
+ *  peak of the STE / LSE passes).  Each of `threads` threads runs `iters`
  *  iterations of 128 terms; the caller times the launch.  sink receives one float per
  *  thread (keeps the work live).
  * ======================================================================== */

@@ -18,6 +18,10 @@
 //   form 6: add.rn.bf16x2 + max.NaN.bf16x2
 //   form 7: fp32 fused multiply-add (two per accumulator and iteration; one
 //           "term" = one FMA = 2 flops), the CUDA-core roofline of dot products
+//   form 8: the smooth (STE / LSE) backward's per-term shape: packed adds
+//           forming s - max, a clamp, ex2.approx per term, a packed add into
+//           the partition sum and a packed FMA into the first moment (one
+//           "term" = one exponential): the SFU-bound roofline of those passes
 #include "maxplus_internal.cuh"
 
 namespace tp {
@@ -174,6 +178,47 @@ __global__ void __launch_bounds__(256) probe_ffma_kernel(int64_t iters, float* s
   sink[t] = r;
 }
 
+__global__ void __launch_bounds__(256) probe_smooth_kernel(int64_t iters, float* sink) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  float2 a[4], n[4], b[8], Z[4][8], S1[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    a[i] = make_float2(-1.0f - (float)(t % 97) * 1e-3f, -1.5f + (float)i * 1e-2f);
+    n[i] = make_float2(-2.0f + (float)i * 1e-3f, -2.5f);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) b[j] = make_float2(-(float)(t % 89) * 1e-3f, -0.25f * (float)j);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) Z[i][j] = S1[i][j] = make_float2(0.0f, 0.0f);
+  const float2 step = make_float2(1.0e-7f, -1.0e-7f);
+  for (int64_t it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {            // two k steps of 4 x 8 x 2 terms
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = tp_add2(a[i], step);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float2 s = tp_add2(tp_add2(a[i], b[j]), n[i]);
+          s.x = tp_max_nan(s.x, -256.0f);
+          s.y = tp_max_nan(s.y, -256.0f);
+          const float2 e = make_float2(tp_ex2(s.x), tp_ex2(s.y));
+          Z[i][j] = tp_add2(Z[i][j], e);
+          S1[i][j] = tp_fma2(e, s, S1[i][j]);
+        }
+    }
+  }
+  float r = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r += Z[i][j].x + Z[i][j].y + S1[i][j].x + S1[i][j].y;
+  sink[t] = r;
+}
+
 }  // namespace
 
 int launch_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters, float* sink,
@@ -193,8 +238,12 @@ int launch_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters
     probe_bf16_kernel<false><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
   else if (form == 6)
     probe_bf16_kernel<true><<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
-  else
+  else if (form == 7)
     probe_ffma_kernel<<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
+  else if (form == 8)
+    probe_smooth_kernel<<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
+  else
+    return TP_ERR_INVALID_ARG;
   return launch_status();
 }
 
