@@ -572,10 +572,10 @@ def dtn_workload(args, world, rank):
     clk = clocks.stop()
     tokens = B * L * world
     value = tokens / (ms / args.steps / 1e3)
-    # dominant kernels (about half of the step): the STE backward of a tropical
-    # projection (M=8192, N=K=256): its stats pass and the two gradient passes
-    # each evaluate one exponential per (m, n, k) term -> 3*M*N*K per call,
-    # against the SFU-bound probe of the same per-term instruction form
+    # dominant kernels (about 40% of the step): the STE backward of a tropical
+    # projection (M=8192, N=K=256): its stats pass and the one-pass gx + gW
+    # kernel each evaluate one exponential per (m, n, k) term -> 2*M*N*K per
+    # call, against the SFU-bound probe of the same per-term instruction form
     xf = x.detach().reshape(-1, D)
     wq = attn.q_proj.weight.detach()
     y0, _ = ops.maxplus(xf, wq, argmax=False)
@@ -589,7 +589,7 @@ def dtn_workload(args, world, rank):
     s1.record()
     torch.cuda.synchronize()
     kms = s0.elapsed_time(s1) / 20
-    achieved = 3.0 * xf.shape[0] * D * D / (kms / 1e3) / 1e12
+    achieved = 2.0 * xf.shape[0] * D * D / (kms / 1e3) / 1e12
     ops.probe_addmax(8, 148 * 8, 50)
     pms, terms = ops.probe_addmax(8, 148 * 8, 400)
     peak = terms / (pms / 1e3) / 1e12
@@ -629,8 +629,8 @@ def dtn_workload(args, world, rank):
         "gpu_launches": per_step * args.steps if per_step is not None else None,
         "roofline": {"bound": "sfu (ex2)", "achieved": achieved, "peak": peak,
                      "unit": "T exp/s", "frac": achieved / peak, "traffic": None,
-                     "kernel": "STE backward of the Q projection (M=8192, N=K=256): stats + "
-                               "gx + gW passes, 3*M*N*K exponentials per call",
+                     "kernel": "STE backward of the Q projection (M=8192, N=K=256): stats "
+                               "pass + one-pass gx/gW kernel, 2*M*N*K exponentials per call",
                      "kernel_ms": kms,
                      "peak_source": "in-repo SFU probe of the same per-term form "
                                     "(tp_probe_addmax form 8), this run; of measured"},

@@ -242,6 +242,13 @@ TP_API int64_t tp_set_argmax_tma_min_terms(int64_t terms);
  * counterpart.) */
 TP_API int tp_set_stream_k(int mode);
 
+/* Smooth (STE / LSE) backward: 1 (default) lets shapes that allow it form gx
+ * and gW in one pass (one exponential per term instead of one per gradient;
+ * fp32, M, N, K multiples of 4, gx tiles filling the GPU, gW partials of at
+ * most 64 MiB), 0 keeps one pass per gradient.  Both are deterministic and
+ * agree to fp32 summation order.  Returns the previous setting. */
+TP_API int tp_set_smooth_fused(int enable);
+
 /* ======================================================================== *
  *  Fused TSRN tropical top-k attention, forward (inference)
  *  Replaces research/tsrn_dml.py:462-548 (TropicalAttention.forward) from the

@@ -101,6 +101,7 @@ SIGNATURES: dict[str, tuple] = {
     "maxplus_matmul_cuda": (None, [_c_p, _c_p, _c_p, _c_int, _c_int, _c_int]),
     "tp_set_argmax_tma_min_terms": (_c_i64, [_c_i64]),
     "tp_set_stream_k": (_c_int, [_c_int]),
+    "tp_set_smooth_fused": (_c_int, [_c_int]),
     "tp_esn_gru_fwd": (
         _c_int,
         [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p,

@@ -16,6 +16,7 @@ namespace tp {
 
 namespace {
 std::atomic<int> g_pointer_checks{1};
+std::atomic<int> g_smooth_fused{1};
 thread_local int g_last_error = TP_OK;
 }  // namespace
 
@@ -305,7 +306,9 @@ int tp_maxplus_bwd_smooth_ref(int mode, float tau, int dtype, int64_t batch, int
                            aligned16(x) && aligned16(w);
   SmoothArgs p{mode, tau, dtype, batch, M, N, K, x, w, gy, gx, gw, gbias, (float*)workspace,
                async_stage, tp::smooth_splits(batch, M, N, K), tp::smooth_splits(batch, N, M, K),
-               (float*)workspace + 6 * batch * M * N, ref_max};
+               (float*)workspace + 6 * batch * M * N, ref_max, false};
+  p.fused_gw = async_stage && gw != nullptr && tp::smooth_fused_ok(batch, M, N, K) &&
+               g_smooth_fused.load(std::memory_order_relaxed) != 0;
   return launch_maxplus_bwd_smooth(p, as_stream(stream));
 }
 
@@ -554,6 +557,8 @@ int tp_maslov_softmax_bwd(int64_t B, int64_t H, int64_t Lq, int64_t Lk, const fl
 int64_t tp_set_argmax_tma_min_terms(int64_t terms) { return tp::set_argmax_tma_min_terms(terms); }
 
 int tp_set_stream_k(int mode) { return tp::set_stream_k(mode); }
+
+int tp_set_smooth_fused(int enable) { return g_smooth_fused.exchange(enable ? 1 : 0); }
 
 int tp_last_error(void) { return last_error(); }
 

@@ -52,13 +52,24 @@ __device__ __forceinline__ float tp_max3_nan(float a, float b, float c) {
   return r;
 }
 
-// Packed fp32 pairs (sm_100a add/fma .f32x2): each half is an ordinary
-// round-to-nearest fp32 add / fused multiply-add, two per instruction.
+// Packed fp32 pairs (sm_100a add/mul/fma .f32x2): each half is an ordinary
+// round-to-nearest fp32 add / multiply / fused multiply-add, two per
+// instruction.
 __device__ __forceinline__ float2 tp_add2(float2 a, float2 b) {
   float2 r;
   asm("{\n\t.reg .b64 pa, pb, pr;\n\t"
       "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
       "add.rn.f32x2 pr, pa, pb;\n\tmov.b64 {%0, %1}, pr;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+__device__ __forceinline__ float2 tp_mul2(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 pa, pb, pr;\n\t"
+      "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+      "mul.rn.f32x2 pr, pa, pb;\n\tmov.b64 {%0, %1}, pr;\n\t}"
       : "=f"(r.x), "=f"(r.y)
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return r;

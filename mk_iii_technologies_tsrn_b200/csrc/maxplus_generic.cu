@@ -892,6 +892,158 @@ __global__ void __launch_bounds__(G_THREADS, 3) smooth_grad_async_kernel(SmoothA
   }
 }
 
+// Both STE / LSE gradients in one pass over (m, n, k): the gx pass above
+// (a block owns 64 rows of x and 64 k, walks all n, sums dS over n in
+// registers) that also sums the same dS over its 64 rows into this block's
+// partial gW[n][k] -- one exponential per term instead of one per term in each
+// of two passes.  Threads map so that each warp holds 4 row groups (ty) of 8
+// k-quads (tx): the row sum is a two-step xor shuffle within the warp, then
+// four warp groups meet in shared memory.  Partials go to part[b][mt][N][K]
+// (mt = the block's row tile) and are added in tile order afterwards
+// (deterministic).  Needs fp32, M, N, K multiples of 4, one split (the gx
+// tiles fill the GPU).
+__global__ void __launch_bounds__(G_THREADS, 3) smooth_grad_fused_kernel(SmoothArgs p) {
+  constexpr int QS = 16;
+  __shared__ __align__(16) float os[2][QS][GB_N];       // w rows (raw): [n][k]
+  __shared__ __align__(16) float st[2][3][QS][GB_M];    // stats: [plane][n][m]
+  __shared__ __align__(16) float gws[4][QS][GB_N];      // gW partial per warp group
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tx = (lane & 7) + 8 * (warp & 1);           // k quad: k0 + 4 tx
+  const int ty = (lane >> 3) + 4 * (warp >> 1);         // row quad: r0 + 4 ty
+  const int wg = warp >> 1;
+  const int64_t r0 = (int64_t)blockIdx.y * GB_M;
+  const int64_t k0 = (int64_t)blockIdx.x * GB_N;
+  const int64_t bz = blockIdx.z;
+  const int64_t MN = p.M * p.N;
+  const float* xb = static_cast<const float*>(p.x) + bz * p.M * p.K;
+  const float* wb = static_cast<const float*>(p.w) + bz * p.N * p.K;
+  const float* planes = p.ws + 3 * p.batch * MN + bz * 3 * MN;   // [n][m] planes
+  const float L = kLog2e / p.tau;
+  const bool rows_ok = r0 + 4 * ty < p.M;                // M % 4 == 0: all four or none
+  const int64_t mt = gridDim.y;
+  float* gpart = p.part + (bz * mt + blockIdx.y) * p.N * p.K;
+
+  float2 own[4][2], acc[4][2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = r0 + 4 * ty + i;
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t k = k0 + 4 * tx + j;
+      v[j] = (r < p.M && k < p.K) ? __ldg(xb + r * p.K + k) * L : 0.0f;
+    }
+    own[i][0] = make_float2(v[0], v[1]);
+    own[i][1] = make_float2(v[2], v[3]);
+    acc[i][0] = make_float2(0.0f, 0.0f);
+    acc[i][1] = make_float2(0.0f, 0.0f);
+  }
+
+  auto issue = [&](int b, int64_t q0) {
+    {
+      const int qq = threadIdx.x / 16, kv = threadIdx.x % 16;
+      const int64_t q = q0 + qq, k = k0 + 4 * kv;
+      const bool ok = q < p.N && k < p.K;
+      tp_cp_async16(&os[b][qq][4 * kv], ok ? wb + q * p.K + k : wb, ok ? 16 : 0);
+    }
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const int e = threadIdx.x + c * G_THREADS;
+      const int pl = e / (QS * 16), rem = e % (QS * 16);
+      const int qq = rem / 16, rv = rem % 16;
+      const int64_t q = q0 + qq, r = r0 + 4 * rv;
+      const bool ok = q < p.N && r < p.M;
+      tp_cp_async16(&st[b][pl][qq][4 * rv], ok ? planes + pl * MN + q * p.M + r : planes,
+                    ok ? 16 : 0);
+    }
+    tp_cp_async_commit();
+  };
+
+  const float2 Lp = make_float2(L, L);
+  const float2 zero2 = make_float2(0.0f, 0.0f);
+  int b = 0;
+  issue(0, 0);
+  for (int64_t q0 = 0; q0 < p.N; q0 += QS, b ^= 1) {
+    if (q0 + QS < p.N) {
+      issue(b ^ 1, q0 + QS);
+      tp_cp_async_wait<1>();
+    } else {
+      tp_cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int qmax = (int)((p.N - q0) < QS ? (p.N - q0) : QS);
+#pragma unroll 2
+    for (int qq = 0; qq < qmax; ++qq) {
+      const float4 o4 = *reinterpret_cast<const float4*>(&os[b][qq][4 * tx]);
+      const float2 ob[2] = {make_float2(o4.x, o4.y), make_float2(o4.z, o4.w)};
+      const float4 rf = *reinterpret_cast<const float4*>(&st[b][0][qq][4 * ty]);
+      const float4 aa = *reinterpret_cast<const float4*>(&st[b][1][qq][4 * ty]);
+      const float4 bb = *reinterpret_cast<const float4*>(&st[b][2][qq][4 * ty]);
+      const float rfv[4] = {rf.x, rf.y, rf.z, rf.w};
+      const float av[4] = {aa.x, aa.y, aa.z, aa.w};
+      const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
+      float2 gs[2] = {zero2, zero2};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 nref = make_float2(-rfv[i], -rfv[i]);
+        const float2 A = make_float2(av[i], av[i]);
+        const float2 Bp = make_float2(bv[i], bv[i]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float2 t = tp_add2(tp_fma2(Lp, ob[h], own[i][h]), nref);
+          t.x = tp_max_nan(t.x, kClampL);
+          t.y = tp_max_nan(t.y, kClampL);
+          const float2 e = make_float2(tp_ex2(t.x), tp_ex2(t.y));
+          const float2 d = tp_mul2(e, tp_fma2(Bp, t, A));
+          acc[i][h] = tp_add2(acc[i][h], d);
+          gs[h] = tp_add2(gs[h], d);
+        }
+      }
+      // sum over the warp's four row groups, then one store per k quad
+      float g4[4] = {rows_ok ? gs[0].x : 0.0f, rows_ok ? gs[0].y : 0.0f,
+                     rows_ok ? gs[1].x : 0.0f, rows_ok ? gs[1].y : 0.0f};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        g4[j] += __shfl_xor_sync(0xffffffffu, g4[j], 8);
+        g4[j] += __shfl_xor_sync(0xffffffffu, g4[j], 16);
+      }
+      if (lane < 8)
+        *reinterpret_cast<float4*>(&gws[wg][qq][4 * tx]) = make_float4(g4[0], g4[1], g4[2], g4[3]);
+    }
+    __syncthreads();
+    // gW partial of this chunk: add the four warp groups, store k quads
+    {
+      const int qq = threadIdx.x / 16, kv = threadIdx.x % 16;
+      const int64_t q = q0 + qq, k = k0 + 4 * kv;
+      if (qq < qmax && k < p.K) {
+        float4 sum = *reinterpret_cast<const float4*>(&gws[0][qq][4 * kv]);
+#pragma unroll
+        for (int g = 1; g < 4; ++g) {
+          const float4 v = *reinterpret_cast<const float4*>(&gws[g][qq][4 * kv]);
+          sum.x += v.x;
+          sum.y += v.y;
+          sum.z += v.z;
+          sum.w += v.w;
+        }
+        *reinterpret_cast<float4*>(gpart + q * p.K + k) = sum;
+      }
+    }
+    __syncthreads();   // buffer b and gws are rewritten by the next iteration
+  }
+  float* out = p.gx + bz * p.M * p.K;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = r0 + 4 * ty + i;
+    if (r >= p.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t k = k0 + 4 * tx + j;
+      const float v = j & 1 ? acc[i][j >> 1].y : acc[i][j >> 1].x;
+      if (k < p.K) out[r * p.K + k] = v;
+    }
+  }
+}
+
 // out[b][i] = sum_s part[b][s][i], s in increasing order (deterministic).
 __global__ void split_sum_kernel(const float* __restrict__ part, int64_t batch, int64_t S,
                                  int64_t n, float* __restrict__ out) {
@@ -1010,11 +1162,26 @@ int64_t smooth_splits(int64_t batch, int64_t rows, int64_t Q, int64_t K) {
   return s < 1 ? 1 : s;
 }
 
+// The one-pass gradient kernel: fp32 staging shapes, gx tiles that fill the
+// GPU without splits, and gW partials ([batch][ceil(M/64)][N][K]) of at most
+// 16M floats (64 MiB; their write and read cost far less than the pass saved).
+bool smooth_fused_ok(int64_t batch, int64_t M, int64_t N, int64_t K) {
+  if (batch <= 0 || M <= 0 || N <= 0 || K <= 0) return false;
+  if (M % 4 || N % 4 || K % 4) return false;
+  if (smooth_splits(batch, M, N, K) != 1) return false;
+  const int64_t mt = ceil_div(M, (int64_t)GB_M);
+  return mt <= 65535 && batch * mt * N * K <= ((int64_t)1 << 24);
+}
+
 int64_t smooth_workspace_floats(int64_t batch, int64_t M, int64_t N, int64_t K) {
   const int64_t sx = smooth_splits(batch, M, N, K), sw = smooth_splits(batch, N, M, K);
   int64_t part = 0;
   if (sx > 1) part = batch * sx * M * K;
   if (sw > 1 && batch * sw * N * K > part) part = batch * sw * N * K;
+  if (smooth_fused_ok(batch, M, N, K)) {
+    const int64_t f = batch * ceil_div(M, (int64_t)GB_M) * N * K;
+    if (f > part) part = f;
+  }
   return 6 * batch * M * N + part;
 }
 
@@ -1048,6 +1215,15 @@ int launch_maxplus_bwd_smooth(const SmoothArgs& p, cudaStream_t stream) {
     dim3 gx((unsigned)ceil_div(p.K, GB_N), (unsigned)ceil_div(p.M, GB_M), (unsigned)(nb * sx));
     dim3 gw((unsigned)ceil_div(p.K, GB_N), (unsigned)ceil_div(p.N, GB_M), (unsigned)(nb * sw));
     if (gx.y > 65535u || gw.y > 65535u) return TP_ERR_TOO_LARGE;
+    if (p.fused_gw && p.gw && p.async_stage && sx == 1) {
+      // one pass for both gradients, then the row tiles' gW partials added
+      dim3 gf((unsigned)ceil_div(p.K, GB_N), (unsigned)ceil_div(p.M, GB_M), nb);
+      smooth_grad_fused_kernel<<<gf, G_THREADS, 0, stream>>>(p);
+      split_sum_kernel<<<flat_grid(p.batch * p.N * p.K, 256), 256, 0, stream>>>(
+          p.part, p.batch, (int64_t)gf.y, p.N * p.K, p.gw);
+      s = launch_status();
+      if (s != TP_OK) return s;
+    } else {
     if (p.async_stage)
       smooth_grad_async_kernel<0><<<gx, G_THREADS, 0, stream>>>(p);
     else if (p.dtype == TP_DTYPE_F32)
@@ -1071,6 +1247,7 @@ int launch_maxplus_bwd_smooth(const SmoothArgs& p, cudaStream_t stream) {
             p.part, p.batch, sw, p.N * p.K, p.gw);
       s = launch_status();
       if (s != TP_OK) return s;
+    }
     }
   }
   if (p.gbias)

@@ -122,6 +122,9 @@ struct SmoothArgs {
   // optional [batch][M][N] maxima max_k(x + w) from the forward: the stats
   // pass then skips its own max pass
   const float* ref;
+  // both gradients in one pass (smooth_fused_ok shapes, gw requested): the
+  // per-row-tile gW partials go to `part` ([batch][ceil(M/64)][N][K])
+  bool fused_gw;
 };
 
 // Number of slices the smooth backward cuts the reduced index Q into for an
@@ -130,6 +133,7 @@ struct SmoothArgs {
 int64_t smooth_splits(int64_t batch, int64_t rows, int64_t Q, int64_t K);
 // Workspace floats of the smooth backward (stat planes + split partials).
 int64_t smooth_workspace_floats(int64_t batch, int64_t M, int64_t N, int64_t K);
+bool smooth_fused_ok(int64_t batch, int64_t M, int64_t N, int64_t K);
 
 // maxplus_generic.cu
 int launch_maxplus_fwd_generic(const StridedMaxPlus& p, cudaStream_t stream);

@@ -85,8 +85,13 @@ def test_workspace_size():
     # six [M][N] stat planes per batch (three, and the same three transposed)
     assert lib.tp_maxplus_bwd_smooth_workspace_bytes(2, 3, 5, 7) == 2 * 6 * 3 * 5 * 4
     assert lib.tp_maxplus_bwd_smooth_workspace_bytes(-1, 3, 5, 7) == 0
-    # a projection-shaped problem (M=8192 rows, N=K=256): the 16 weight-gradient
-    # tiles are cut into 32 slices of 256 rows, partials [32][256][256]
+    # a projection-shaped problem (M=8192 rows, N=K=256): both gradients in one
+    # pass, the weight gradient's partials per 64-row tile [128][256][256]
+    # (larger than the two-pass split's [32][256][256])
     stats = 6 * 8192 * 256
     assert lib.tp_maxplus_bwd_smooth_workspace_bytes(1, 8192, 256, 256) == \
-        (stats + 32 * 256 * 256) * 4
+        (stats + 128 * 256 * 256) * 4
+    # the input gradient's 2 tiles cut into 16 slices of n: two passes, partials
+    # [16][64][128]
+    assert lib.tp_maxplus_bwd_smooth_workspace_bytes(1, 64, 4096, 128) == \
+        (6 * 64 * 4096 + 16 * 64 * 128) * 4

@@ -144,3 +144,60 @@ def test_smooth_backward_with_forward_max(cuda, dtype, M, N, K):
     b = ops.maxplus_backward_smooth("ste", 0.7, x, w, g, ref_max=y0)
     for u, v in zip(a[:2], b[:2]):
         assert _rel_err(v.cpu().numpy(), u.cpu().numpy()) < 1e-5
+
+
+def _smooth_both_paths(ops, lib, *args, **kw):
+    old = lib.tp_set_smooth_fused(1)
+    try:
+        fused = ops.maxplus_backward_smooth(*args, **kw)
+        lib.tp_set_smooth_fused(0)
+        split = ops.maxplus_backward_smooth(*args, **kw)
+    finally:
+        lib.tp_set_smooth_fused(old)
+    return fused, split
+
+
+@pytest.mark.parametrize("mode,tau", [("ste", 0.5), ("lse", 1.0)])
+@pytest.mark.parametrize("batch,M,N,K", [(1, 4096, 36, 320), (2, 4100, 20, 324)])
+def test_smooth_fused_gradients_vs_oracle(cuda, mode, tau, batch, M, N, K):
+    # shapes whose gx tiles fill the GPU: gx and gW come from one pass (row-tile
+    # gW partials added in tile order); tails in every dimension in the second
+    from mk_iii_technologies_tsrn_b200 import _lib
+    ops, lib = _fn(), _lib.load()
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((batch, M, K)).astype(np.float32)
+    w = rng.standard_normal((batch, N, K)).astype(np.float32)
+    g = rng.standard_normal((batch, M, N)).astype(np.float32)
+    xt, wt, gt = (torch.tensor(a, device=cuda) for a in (x, w, g))
+    (gx, gw, _), (sx, sw, _) = _smooth_both_paths(ops, lib, mode, tau, xt, wt, gt)
+    again = ops.maxplus_backward_smooth(mode, tau, xt, wt, gt)
+    assert torch.equal(gx, again[0]) and torch.equal(gw, again[1])     # deterministic
+    for b in range(batch):
+        rgx, rgw, _ = oracle.maxplus_bwd_smooth(mode, tau, x[b], w[b], g[b])
+        assert _rel_err(gx[b].cpu().numpy(), rgx) < 1e-5
+        assert _rel_err(gw[b].cpu().numpy(), rgw) < 1e-5
+    assert _rel_err(gx.cpu().numpy(), sx.cpu().numpy()) < 1e-5
+    assert _rel_err(gw.cpu().numpy(), sw.cpu().numpy()) < 1e-5
+
+
+def test_smooth_fused_projection_shape(cuda):
+    # the DTN projection (M=8192, N=K=256, forward maxima given): the one-pass
+    # kernel runs, agrees with the two-pass one, and its gx rows with the oracle
+    from torch.profiler import ProfilerActivity, profile
+    from mk_iii_technologies_tsrn_b200 import _lib
+    ops, lib = _fn(), _lib.load()
+    gen = torch.Generator(device=cuda).manual_seed(5)
+    x = torch.randn(8192, 256, device=cuda, generator=gen)
+    w = torch.randn(256, 256, device=cuda, generator=gen) * 0.02
+    g = torch.randn(8192, 256, device=cuda, generator=gen)
+    y0, _ = ops.maxplus(x, w, argmax=False)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        ops.maxplus_backward_smooth("ste", 1.0, x, w, g, ref_max=y0)
+        torch.cuda.synchronize()
+    assert any("smooth_grad_fused_kernel" in e.name for e in prof.events())
+    (gx, gw, _), (sx, sw, _) = _smooth_both_paths(ops, lib, "ste", 1.0, x, w, g, ref_max=y0)
+    assert _rel_err(gx.cpu().numpy(), sx.cpu().numpy()) < 1e-5
+    assert _rel_err(gw.cpu().numpy(), sw.cpu().numpy()) < 1e-5
+    rgx, _, _ = oracle.maxplus_bwd_smooth("ste", 1.0, x[:64].cpu().numpy(), w.cpu().numpy(),
+                                          g[:64].cpu().numpy())
+    assert _rel_err(gx[:64].cpu().numpy(), rgx) < 1e-5
