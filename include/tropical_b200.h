@@ -231,15 +231,17 @@ TP_API int tp_maxplus_bwd_smooth_ref(int mode, float tau, int dtype,
 TP_API int64_t tp_set_argmax_tma_min_terms(int64_t terms);
 
 /* Schedule of the large fp32 forward (TMA kernel): 0 = each CTA takes whole
- * 128x128 tiles; 1 (default) = stream-K when K >= 4096 and the tile count
- * leaves the last wave partly idle (with argmax: at least 5% of the run):
- * whole-tile waves up
- * to the last full one, then that wave's and the remaining tiles' 64-k chunks
- * split evenly over the CTAs; a tile shared by two CTAs is merged exactly
- * (values and argmax identical to the whole-tile schedule), using a
- * stream-ordered workspace from a library-owned pool; 2 = stream-K whenever
- * there are at least as many tiles as CTAs.  Returns the previous mode; process-wide.  (Tuning; no reference
- * counterpart.) */
+ * 128x128 tiles; 1 (default) = when K >= 4096 and the tile count leaves the
+ * last wave partly idle (with argmax: at least 5% of the run), whole-tile
+ * waves up to the last full one, then the remaining tiles either split
+ * evenly by 64-k chunks over the CTAs or (argmax kernel, when a cost model
+ * of the three options picks it) cut into two k-aligned halves, or left as
+ * whole tiles; 2 = the even split whenever there are at least as many tiles
+ * as CTAs; 3 = the k-aligned pieces (2 or 4 per tile, argmax kernel) whenever
+ * K allows them, else as 2.  Tiles shared by CTAs are merged exactly (values
+ * and argmax identical to the whole-tile schedule), using a stream-ordered
+ * workspace from a library-owned pool.  Returns the previous mode;
+ * process-wide.  (Tuning; no reference counterpart.) */
 TP_API int tp_set_stream_k(int mode);
 
 /* Smooth (STE / LSE) backward: 1 (default) lets shapes that allow it form gx

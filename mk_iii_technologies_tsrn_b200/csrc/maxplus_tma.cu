@@ -144,13 +144,22 @@ struct TmaParams {
   // the later one computes its tail chunks first and leaves partial maxima
   // (and last-change chunks) in slot cta-1; the earlier one computes the head
   // chunks last, merges and finishes the tile.
+  // sk = 2 (k-aligned split): the sk_rem remaining tiles are cut into sk_split
+  // pieces of k_tiles / sk_split k-tiles (whole 64-k chunks); piece q (of
+  // sk_split * sk_rem) is piece q / sk_rem of remaining tile q % sk_rem and
+  // goes to CTA q % grid, so that the CTAs walk the same k range at the same
+  // time (L2 sharing as in whole-tile waves).  Pieces below the last leave
+  // their partials in slot (tile - first) * (sk_split - 1) + piece; the last
+  // piece comes in a later round, waits for them and merges in k order.
   int sk;
   int sk_cpt;
   int sk_dp;
   int64_t sk_units;
-  float* sk_max;       // [grid][OUTS * CT] partial maxima, thread-major
-  int32_t* sk_cid;     // [grid][OUTS * CT] their last-change chunks (argmax)
-  unsigned* sk_flag;   // [grid] 1 once slot c holds the tail of CTA c's last tile
+  int sk_split;
+  int sk_rem;
+  float* sk_max;       // [slots][OUTS * CT] partial maxima, thread-major
+  int32_t* sk_cid;     // [slots][OUTS * CT] their last-change chunks (argmax)
+  unsigned* sk_flag;   // [slots] 1 once the slot holds its partials
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mt, int& nt) {
@@ -302,7 +311,15 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
     tp_mbar_init(cbar, CT);
     tp_fence_mbar_init();
     const int cta = (int)blockIdx.x, G = (int)gridDim.x;
-    if (p.sk) {
+    if (kArgmax && p.sk == 2) {
+      const int64_t total = (int64_t)p.sk_split * p.sk_rem;
+      const unsigned np = cta < total ? (unsigned)((total - cta + G - 1) / G) : 0u;
+      sch_g0 = sch_g1 = 0;
+      sch_dp = (unsigned)p.sk_dp;
+      sch_nseg = (unsigned)p.sk_dp + np;
+      sch_total_kt = (unsigned)p.sk_dp * (unsigned)p.k_tiles +
+                     np * (unsigned)(p.k_tiles / p.sk_split);
+    } else if (p.sk) {
       const int64_t first = (int64_t)p.sk_dp * G;       // first stream-K tile
       auto g_of = [&](int64_t u) -> int64_t {
         return (first + u / p.sk_cpt) * p.k_tiles +
@@ -333,7 +350,13 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
   // where used, so that they do not occupy registers across the main loop)
   auto seg = [&](uint32_t i, int& tile, int& kb, int& ke) {
     const uint32_t dp = sch_dp;
-    if (i >= dp) {
+    if (kArgmax && i >= dp && p.sk == 2) {
+      const int64_t q = (int64_t)cta + (int64_t)(i - dp) * G;
+      const int L = p.k_tiles / p.sk_split;
+      tile = (int)((int64_t)dp * G + q % p.sk_rem);
+      kb = (int)(q / p.sk_rem) * L;
+      ke = kb + L;
+    } else if (i >= dp) {
       const int64_t g0 = sch_g0, g1 = sch_g1;
       tile = (int)(g0 / p.k_tiles) + (int)(i - dp);
       const int64_t base = (int64_t)tile * p.k_tiles;
@@ -346,12 +369,21 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
     }
   };
   // segments the search warpgroup takes: finished here (not a stream-K tail
-  // piece) and not the CTA's last segment (the compute warps search that one)
-  auto searched = [&](uint32_t i, int kb) { return !(p.sk && kb > 0) && i + 1 < sch_nseg; };
+  // piece, not a split piece below the last) and not the CTA's last segment
+  // (the compute warps search that one)
+  auto searched = [&](uint32_t i, int kb, int ke) {
+    const bool finished = (kArgmax && p.sk == 2) ? ke == p.k_tiles : !(p.sk && kb > 0);
+    return finished && i + 1 < sch_nseg;
+  };
   auto produce = [&](uint32_t j) -> bool {
     int tile, kt;
     const uint32_t dp_kt = sch_dp * (uint32_t)p.k_tiles;
-    if (j >= dp_kt) {
+    if (kArgmax && j >= dp_kt && p.sk == 2) {
+      const uint32_t L = (uint32_t)(p.k_tiles / p.sk_split);
+      const int64_t q = (int64_t)cta + (int64_t)((j - dp_kt) / L) * G;
+      tile = (int)((int64_t)sch_dp * G + q % p.sk_rem);
+      kt = (int)((q / p.sk_rem) * L + (j - dp_kt) % L);
+    } else if (j >= dp_kt) {
       const int64_t g = sch_g0 + (j - dp_kt);
       tile = (int)(g / p.k_tiles);
       kt = (int)(g % p.k_tiles);
@@ -408,7 +440,7 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
       for (uint32_t i = 0; i < sch_nseg; ++i) {
         int tile, kb, ke;
         seg(i, tile, kb, ke);
-        if (!searched(i, kb)) continue;
+        if (!searched(i, kb, ke)) continue;
         const bool ok = tp_mbar_wait(&tile_ready[h & 1], (h >> 1) & 1u, p.err);
         if (!__all_sync(0xffffffffu, ok)) return;
         int mt, nt;
@@ -563,7 +595,83 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
     seg(si, tile, kb, ke);
     tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
     const int64_t m0 = (int64_t)mt * BM, n0 = (int64_t)nt * BN;
-    if (p.sk && kb > 0) {
+    if (kArgmax && p.sk == 2 && ke < p.k_tiles) {
+      // ---- k-aligned split, a piece below the last: partial maxima (+ chunks)
+      // to its slot, then release the slot's flag
+      const int64_t slot = (int64_t)(tile - (int)sch_dp * G) * (p.sk_split - 1) +
+                           kb / (p.k_tiles / p.sk_split);
+      float* wm = p.sk_max + slot * C::OUTS * CT;
+#pragma unroll
+      for (int o = 0; o < C::OUTS; ++o) wm[o * CT + t] = acc[o / TN][o % TN];
+      if (kArgmax) {
+        int32_t* wc = p.sk_cid + slot * C::OUTS * CT;
+#pragma unroll
+        for (int o = 0; o < C::OUTS; ++o) wc[o * CT + t] = (int32_t)cid[o * CT + t];
+      }
+      if (!compute_sync()) return;
+      if (t == 0) {
+        __threadfence();
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p.sk_flag + slot), "r"(1u)
+                     : "memory");
+      }
+      continue;
+    }
+    if (kArgmax && p.sk == 2 && kb > 0) {
+      // ---- k-aligned split, the last piece (pieces below ran in earlier
+      // rounds): wait for their flags, then fold the partials in k order and
+      // this piece last -- a higher piece wins only with a strictly larger max
+      // (or a NaN where the lower has none), so ties keep the lowest k.
+      const int64_t slot0 = (int64_t)(tile - (int)sch_dp * G) * (p.sk_split - 1);
+      if (t == 0) {
+        const uint64_t t0 = tp_globaltimer();
+        uint32_t polls = 0;
+        int ok = 1;
+        for (int sp = 0; ok && sp < p.sk_split - 1; ++sp) {
+          while (true) {
+            unsigned f;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];"
+                         : "=r"(f)
+                         : "l"(p.sk_flag + slot0 + sp)
+                         : "memory");
+            if (f == 1u) break;
+            if (((++polls) & 63u) == 0u && tp_globaltimer() - t0 > TP_WAIT_BUDGET_NS) {
+              tp_record_device_error(p.err, TP_DEVERR_FLAG_TIMEOUT);
+              ok = 0;
+              break;
+            }
+          }
+        }
+        sk_ok = ok;
+      }
+      if (!compute_sync() || !sk_ok) return;
+      const float* wm = p.sk_max + slot0 * C::OUTS * CT;
+      const int32_t* wc = kArgmax ? p.sk_cid + slot0 * C::OUTS * CT : nullptr;
+#pragma unroll
+      for (int o = 0; o < C::OUTS; ++o) {
+        float v = __ldcg(wm + o * CT + t);
+        int32_t c = kArgmax ? __ldcg(wc + o * CT + t) : 0;
+        for (int sp = 1; sp < p.sk_split - 1; ++sp) {
+          const int64_t off = (int64_t)sp * C::OUTS * CT + o * CT + t;
+          const float h = __ldcg(wm + off);
+          if constexpr (!kArgmax) {
+            v = tp_max_nan(v, h);
+          } else if (v == v && (h != h || h > v)) {
+            v = h;
+            c = __ldcg(wc + off);
+          }
+        }
+        float& a = acc[o / TN][o % TN];
+        if constexpr (!kArgmax) {
+          a = tp_max_nan(v, a);
+        } else if (v == v && (a != a || a > v)) {
+          // this piece's own maximum stands
+        } else {
+          a = v;
+          cid[o * CT + t] = (uint16_t)c;
+        }
+      }
+    }
+    if (p.sk == 1 && kb > 0) {
       // ---- stream-K tail piece: partial maxima (+ chunks) to slot cta-1,
       // then release the flag for the CTA that finishes this tile
       float* wm = p.sk_max + (int64_t)(cta - 1) * C::OUTS * CT;
@@ -582,7 +690,7 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
       }
       continue;
     }
-    if (p.sk && ke < p.k_tiles) {
+    if (p.sk == 1 && ke < p.k_tiles) {
       // ---- stream-K head piece (the CTA's last segment): wait for the tail's
       // partials, then merge.  The tail wins only with a strictly larger max
       // (or a NaN where the head has none): ties keep the head's lower k.
@@ -652,7 +760,7 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
           p.am[m * p.lda + n] = (int32_t)cid[(i * TN + j) * CT + t];
         }
       }
-      if (searched(si, kb)) {
+      if (searched(si, kb, ke)) {
         __syncwarp();
         bool ok = true;
         // the search of the tile handed two before has ended before this
@@ -1160,7 +1268,9 @@ int launch_cfg(const CUtensorMap& xmap, const CUtensorMap& wmap, const TmaParams
 
 namespace {
 std::atomic<int64_t> g_argmax_tma_min_terms{(int64_t)1 << 30};
-std::atomic<int> g_stream_k{1};   // 0 off, 1 when it removes a partial last wave, 2 always
+// 0 off, 1 when it removes a partial last wave, 2 always (even split of
+// chunks), 3 always (k-aligned split of tiles when K allows it)
+std::atomic<int> g_stream_k{1};
 
 // Stream-ordered workspace for the stream-K partials: a library-owned pool per
 // device that keeps its memory (allocation after the first is cheap), so that
@@ -1189,7 +1299,7 @@ cudaMemPool_t sk_pool(int dev) {
 }
 }  // namespace
 
-int set_stream_k(int mode) { return g_stream_k.exchange(mode < 0 ? 0 : (mode > 2 ? 2 : mode)); }
+int set_stream_k(int mode) { return g_stream_k.exchange(mode < 0 ? 0 : (mode > 3 ? 3 : mode)); }
 
 int64_t argmax_tma_min_terms() { return g_argmax_tma_min_terms.load(std::memory_order_relaxed); }
 
@@ -1277,6 +1387,8 @@ int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
   tp_.sk_cpt = 0;
   tp_.sk_dp = 0;
   tp_.sk_units = 0;
+  tp_.sk_split = 0;
+  tp_.sk_rem = 0;
   tp_.sk_max = nullptr;
   tp_.sk_cid = nullptr;
   tp_.sk_flag = nullptr;
@@ -1297,8 +1409,40 @@ int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
   const int waves = (int)ceil_div(tp_.num_tiles, grid);
   const double idle = (double)(waves * grid - tp_.num_tiles) / ((double)waves * grid);
   bool sk = mode != 0 && tp_.num_tiles >= grid && grid > 1 &&
-            (mode == 2 || (tp_.num_tiles % grid != 0 && p.K >= 4096 &&
+            (mode >= 2 || (tp_.num_tiles % grid != 0 && p.K >= 4096 &&
                            (!p.am || idle >= 0.05)));
+  // The remainder after the whole-tile waves (rem tiles, grid <= rem < 2 grid)
+  // as whole tiles (2 rounds), an even split of its chunks (rem / grid
+  // tile-times), or tiles cut into S k-aligned pieces of whole 64-k chunks
+  // (ceil(S rem / grid) / S).  Forced mode 3 takes the S in {2, 4} with the
+  // fewest rounds.  Auto mode, argmax kernel: the cheapest of the three with
+  // S = 2, each split charged its measured overhead in tile-times at
+  // K = 8192 (even split 0.34: 8192 x 1024 x 8192 took 5.28 ms for an ideal
+  // 4.81; halves 0.10: 5.11 ms for 4.97; quarters were dearer still,
+  // 2048^2 x 8192 2.95 ms against 2.89 ms whole); value-only: the even split
+  // (no measurable overhead).
+  const int sk_dp = std::max(0, tp_.num_tiles / grid - 1);
+  const int rem = tp_.num_tiles - sk_dp * grid;
+  int split = 0;
+  if (sk && p.am && mode == 3) {
+    double best = 1e30;
+    for (int S = 2; S <= 4; S *= 2) {
+      if (tp_.k_tiles % (S * DefaultCfg::KT_PER_CHUNK) != 0) continue;
+      const double cost = (double)ceil_div((int64_t)S * rem, (int64_t)grid) / S;
+      if (cost < best - 1e-9) {
+        best = cost;
+        split = S;
+      }
+    }
+  } else if (sk && p.am && mode == 1) {
+    const double whole = (double)ceil_div(rem, grid);
+    const double even = (double)rem / grid + 0.34;
+    const double halves = tp_.k_tiles % (2 * DefaultCfg::KT_PER_CHUNK) == 0
+                              ? (double)ceil_div((int64_t)2 * rem, (int64_t)grid) / 2 + 0.10
+                              : 1e30;
+    if (whole <= even && whole <= halves) sk = false;
+    else if (halves < even) split = 2;
+  }
   void* ws = nullptr;
   if (sk) {
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
@@ -1310,21 +1454,24 @@ int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
       sk = false;
     } else {
       const size_t slot = (size_t)DefaultCfg::OUTS * DefaultCfg::CT;
-      const size_t bytes = (size_t)grid * slot * (p.am ? 8 : 4) + (size_t)grid * 4 + 256;
+      const size_t nslots = split ? (size_t)(split - 1) * rem : (size_t)grid;
+      const size_t bytes = nslots * slot * (p.am ? 8 : 4) + nslots * 4 + 256;
       if (cudaMallocFromPoolAsync(&ws, bytes, pool, stream) != cudaSuccess) {
         (void)cudaGetLastError();
         sk = false;
       } else {
         // whole-tile waves for all but the last full wave; stream-K over that
         // wave and the remainder (at least one tile's chunks per CTA)
-        tp_.sk = 1;
+        tp_.sk = split ? 2 : 1;
         tp_.sk_cpt = (int)ceil_div(tp_.k_tiles, DefaultCfg::KT_PER_CHUNK);
-        tp_.sk_dp = std::max(0, tp_.num_tiles / grid - 1);
-        tp_.sk_units = (int64_t)(tp_.num_tiles - tp_.sk_dp * grid) * tp_.sk_cpt;
+        tp_.sk_dp = sk_dp;
+        tp_.sk_units = (int64_t)rem * tp_.sk_cpt;
+        tp_.sk_split = split;
+        tp_.sk_rem = rem;
         tp_.sk_max = (float*)ws;
-        tp_.sk_cid = p.am ? (int32_t*)(tp_.sk_max + (size_t)grid * slot) : nullptr;
-        tp_.sk_flag = (unsigned*)((char*)ws + (size_t)grid * slot * (p.am ? 8 : 4));
-        const cudaError_t e = cudaMemsetAsync(tp_.sk_flag, 0, (size_t)grid * 4, stream);
+        tp_.sk_cid = p.am ? (int32_t*)(tp_.sk_max + nslots * slot) : nullptr;
+        tp_.sk_flag = (unsigned*)((char*)ws + nslots * slot * (p.am ? 8 : 4));
+        const cudaError_t e = cudaMemsetAsync(tp_.sk_flag, 0, nslots * 4, stream);
         if (e != cudaSuccess) {
           (void)cudaFreeAsync(ws, stream);
           return (int)e;

@@ -23,7 +23,8 @@ pytestmark = pytest.mark.gpu
     (96, 300, 50, 100, 150, False, 1),      # generic + copies
     # 160 tiles: the stream-K schedule (forced) with the destination stores of
     # the split tiles' merges, as an 8-rank shard of a large GEMM takes it
-    (2048, 2560, 256, 1280, 640, True, 2)])
+    (2048, 2560, 256, 1280, 640, True, 2),
+    (2048, 2560, 256, 1280, 640, True, 3)])   # the same, tiles cut into 4 k-aligned pieces
 def test_sharded_entry_two_local_destinations(cuda, M, N, K, Ns, col0, force_tma, stream_k):
     from mk_iii_technologies_tsrn_b200 import _lib
     lib = _lib.load()

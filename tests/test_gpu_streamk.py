@@ -1,7 +1,9 @@
-"""Stream-K schedule of the large fp32 forward (TMA kernel): tiles shared by
-two CTAs are merged exactly, so values and argmax equal the whole-tile
-schedule bit for bit (and the oracle on sampled rows).  Shapes have at least
-as many 128x128 tiles as SMs; K values give odd k-tile counts and K tails."""
+"""Stream-K schedules of the large fp32 forward (TMA kernel): tiles shared by
+CTAs (an even split of chunks, mode 2; or tiles cut into 2 or 4 k-aligned
+pieces, mode 3, the argmax kernel's choice in auto mode) are merged exactly, so
+values and argmax equal the whole-tile schedule bit for bit (and the oracle on
+sampled rows).  Shapes have at least as many 128x128 tiles as SMs; K values
+give odd k-tile counts and K tails."""
 import numpy as np
 import pytest
 import torch
@@ -56,22 +58,27 @@ def _fwd(lib, mode, x, w, bias=None, argmax=True):
     (1280, 2048, 520, "special"),
     (2048, 2560, 300, "normal"),     # 320 tiles: one whole-tile wave, then stream-K over 172
     (2560, 2048, 160, "int"),        # the same with exact ties, 5 k-tiles
+    # k-aligned pieces (mode 3): 16 / 32 k-tiles -> 4 pieces of 160 tiles,
+    # 12 k-tiles -> 2 pieces of the 172 remaining tiles, K tail in the last piece
+    (2048, 1280, 512, "normal"),
+    (1280, 2048, 1024, "special"),
+    (2560, 2048, 384, "int"),
+    (2048, 1280, 1000, "normal"),
 ])
 def test_stream_k_equals_whole_tiles(lib, cuda, M, N, K, kind):
     x, w = _inputs(M, N, K, kind, seed=M + N + K)
     xt, wt = torch.tensor(x, device=cuda), torch.tensor(w, device=cuda)
     y0, a0 = _fwd(lib, 0, xt, wt)
-    y2, a2 = _fwd(lib, 2, xt, wt)
-    y1, a1 = _fwd(lib, 1, xt, wt)
-    np.testing.assert_array_equal(y2.view(np.uint32), y0.view(np.uint32))
-    np.testing.assert_array_equal(a2, a0)
-    np.testing.assert_array_equal(y1.view(np.uint32), y0.view(np.uint32))
-    np.testing.assert_array_equal(a1, a0)
+    for mode in (2, 3, 1):
+        ym, am = _fwd(lib, mode, xt, wt)
+        np.testing.assert_array_equal(ym.view(np.uint32), y0.view(np.uint32), err_msg=str(mode))
+        np.testing.assert_array_equal(am, a0, err_msg=str(mode))
+    y3, a3 = _fwd(lib, 3, xt, wt)
     rows = [0, 5, 9, 100, M // 2, M - 1]
     ry, ri = oracle.maxplus_fwd(x[rows], w)
     # against the oracle: NaN is NaN whatever its payload (the GPU's is canonical)
-    np.testing.assert_array_equal(y2[rows], ry)
-    np.testing.assert_array_equal(a2[rows], ri)
+    np.testing.assert_array_equal(y3[rows], ry)
+    np.testing.assert_array_equal(a3[rows], ri)
 
 
 def test_stream_k_value_only_bias_scale(lib, cuda):
@@ -120,7 +127,7 @@ def test_stream_k_shard_shape(lib, cuda):
     w[torch.rand(N, K, device=cuda, generator=g) < 0.05] = float("-inf")
     from mk_iii_technologies_tsrn_b200 import ops
     res = {}
-    for mode in (0, 2):
+    for mode in (0, 2, 3):
         lib.tp_set_stream_k(mode)
         y, am = ops.maxplus(x, w)
         torch.cuda.synchronize()
@@ -131,9 +138,11 @@ def test_stream_k_shard_shape(lib, cuda):
         e1.record()
         torch.cuda.synchronize()
         res[mode] = (y, am, e0.elapsed_time(e1) / 3)
-    assert torch.equal(res[0][0].view(torch.int32), res[2][0].view(torch.int32))
-    assert torch.equal(res[0][1], res[2][1])
-    print(f"\n8192x1024x8192: whole tiles {res[0][2]:.2f} ms, stream-K {res[2][2]:.2f} ms")
+    for mode in (2, 3):
+        assert torch.equal(res[0][0].view(torch.int32), res[mode][0].view(torch.int32))
+        assert torch.equal(res[0][1], res[mode][1])
+    print(f"\n8192x1024x8192: whole tiles {res[0][2]:.2f} ms, even split {res[2][2]:.2f} ms, "
+          f"k-aligned pieces {res[3][2]:.2f} ms")
     ry, ri = oracle.maxplus_fwd(x[:2].cpu().numpy(), w[:300].cpu().numpy())
     np.testing.assert_array_equal(res[2][0][:2, :300].cpu().numpy(), ry)
     np.testing.assert_array_equal(res[2][1][:2, :300].cpu().numpy(), ri)
