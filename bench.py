@@ -79,6 +79,8 @@ def parse_args():
                         "(sums rounded to bf16, as the reference on bf16 tensors; packed "
                         "bf16x2 kernel)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-graph", action="store_true",
+                   help="dtn workload: run the step eagerly instead of replaying a CUDA graph")
     p.add_argument("--att-batch", type=int, default=64,
                    help="sequences per rank of the tsrn_attn workload (64 = config 5)")
     p.add_argument("--esn-mode", choices=["gru", "leaky"], default="gru",
@@ -560,9 +562,31 @@ def dtn_workload(args, world, rank):
     x = torch.randn(B, L, D, device=dev, generator=gen, requires_grad=True)
     g = torch.randn(B, L, D, device=dev, generator=gen)
 
-    def step():
+    def eager_step():
         out, _ = attn(x)
         out.backward(g)
+
+    step = eager_step
+    graph = None
+    if not args.no_graph:
+        # the whole forward + backward captured once and replayed each step:
+        # the same kernels without the per-launch host cost of the Python /
+        # autograd loop (gradients are rewritten by every replay, as after a
+        # zero_grad(set_to_none=True))
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                attn.zero_grad(set_to_none=True)
+                x.grad = None
+                eager_step()
+        torch.cuda.current_stream().wait_stream(side)
+        attn.zero_grad(set_to_none=True)
+        x.grad = None
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            eager_step()
+        step = graph.replay
 
     for _ in range(args.warmup):
         step()
@@ -607,11 +631,20 @@ def dtn_workload(args, world, rank):
         xi.grad = None
         dx.requires_grad_(False)
 
+    if graph is not None:
+        # the captured step reads the static input x and leaves x.grad: the
+        # step's activations arrive in x, its input gradient leaves from x.grad
+        def e2e_step():
+            with torch.no_grad():
+                x.copy_(hx, non_blocking=True)
+            graph.replay()
+            hgx.copy_(x.grad, non_blocking=True)
+
     for _ in range(2):
         e2e_step()
     e2e_ms = time_steps(e2e_step, 3, world)
-    try:
-        per_step = count_library_kernels(step)
+    try:   # counted on an eager step: the graph replays the same kernels
+        per_step = count_library_kernels(eager_step)
     except Exception:   # profiler unavailable: leave the count out rather than guess
         per_step = None
     return {
@@ -623,6 +656,7 @@ def dtn_workload(args, world, rank):
                 "tau_h ~ U(0.1,1) (seeded)",
         "config": {"workload": "DTNAttention d_model=256 heads=8 B=128 L=64 fwd+bwd (STE)",
                    "parallelism": f"batch-replicated x{world} (weak)" if world > 1 else "single GPU",
+                   "launch": "CUDA graph of the whole step" if graph is not None else "eager",
                    "l2": "activations 8 MiB (fit L2); the tropical kernels are compute-bound"},
         "e2e": {"value": tokens / (e2e_ms / 3 / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hgx.numel() * 4},
