@@ -871,13 +871,9 @@ def tsrn_attn_workload(args, world, rank):
     peak = 2.0 * terms / (pms / 1e3) / 1e12
     achieved = 2.0 * fmas / (ms / args.steps / 1e3) / 1e12
     hout = torch.empty(B, H, T, dh).pin_memory()
-    dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
 
-    def e2e_step():
-        dQ.copy_(hQ, non_blocking=True)
-        dK.copy_(hK, non_blocking=True)
-        dV.copy_(hV, non_blocking=True)
-        hout.copy_(ops.tsrn_attention(dQ, dK, dV, slopes, k, True), non_blocking=True)
+    def e2e_step():   # the host entry: sequence groups' copies overlap the computation
+        ops.tsrn_attention_host(hQ, hK, hV, slopes, k, True, out=hout)
 
     for _ in range(2):
         e2e_step()

@@ -648,6 +648,28 @@ def probe_addmax(form: int, blocks: int, iters: int, device=None) -> Tuple[float
 
 
 # --------------------------------------------------------------------------- TSRN attention
+def _tsrn_attention_into(Q, K, V, slopes, top_k: int, causal: bool, Tc: int,
+                         out: torch.Tensor, dev: torch.device) -> None:
+    B, H, T, dh = Q.shape
+    Tkv = K.shape[2]
+    lib = _lib.load()
+    ws_bytes = int(lib.tp_tsrn_attention_workspace_bytes(B, H, T, Tkv, dh))
+    ws = torch.empty(max(ws_bytes // 4, 4), device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        st = lib.tp_tsrn_attention_fwd(B, H, T, Tkv, int(Tc), dh, _ptr(Q), _ptr(K), _ptr(V),
+                                       _ptr(slopes), int(top_k), 1 if causal else 0, _ptr(out),
+                                       _ptr(ws), ws.numel() * 4, _stream(dev))
+    _lib.check(st, "tp_tsrn_attention_fwd")
+
+
+def _attention_shapes(Q, K, V, slopes):
+    if Q.dim() != 4 or K.shape != V.shape or K.shape[:2] != Q.shape[:2] or \
+            K.shape[-1] != Q.shape[-1]:
+        raise ValueError(f"shapes {tuple(Q.shape)}, {tuple(K.shape)}, {tuple(V.shape)}")
+    if slopes.shape != (Q.shape[1],):
+        raise ValueError("slopes must be [H]")
+
+
 def tsrn_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, slopes: torch.Tensor,
                    top_k: int, causal: bool = True, Tc: int = 0) -> torch.Tensor:
     """Fused TSRN tropical top-k attention forward (research/tsrn_dml.py:462-548 after RoPE):
@@ -656,25 +678,61 @@ def tsrn_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, slopes: to
     ``Q`` [B,H,T,dh], ``K``/``V`` [B,H,Tkv,dh] fp32 (made contiguous), ``slopes`` [H];
     the first ``Tc`` keys are cross-window cached keys.  Forward only (inference)."""
     dev = _require_cuda(Q, K, V, slopes)
-    if Q.dim() != 4 or K.shape != V.shape or K.shape[:2] != Q.shape[:2] or \
-            K.shape[-1] != Q.shape[-1]:
-        raise ValueError(f"shapes {tuple(Q.shape)}, {tuple(K.shape)}, {tuple(V.shape)}")
+    _attention_shapes(Q, K, V, slopes)
     Q, K, V = (_f32(t).contiguous() for t in (Q, K, V))
     slopes = _f32(slopes).contiguous()
-    B, H, T, dh = Q.shape
-    Tkv = K.shape[2]
-    if slopes.shape != (H,):
-        raise ValueError("slopes must be [H]")
-    lib = _lib.load()
-    ws_bytes = int(lib.tp_tsrn_attention_workspace_bytes(B, H, T, Tkv, dh))
-    ws = torch.empty(max(ws_bytes // 4, 4), device=dev, dtype=torch.float32)
     out = torch.empty_like(Q)
-    with torch.cuda.device(dev):
-        st = lib.tp_tsrn_attention_fwd(B, H, T, Tkv, int(Tc), dh, _ptr(Q), _ptr(K), _ptr(V),
-                                       _ptr(slopes), int(top_k), 1 if causal else 0, _ptr(out),
-                                       _ptr(ws), ws.numel() * 4, _stream(dev))
-    _lib.check(st, "tp_tsrn_attention_fwd")
+    _tsrn_attention_into(Q, K, V, slopes, top_k, causal, Tc, out, dev)
     return out
+
+
+def tsrn_attention_host(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
+                        slopes: torch.Tensor, top_k: int, causal: bool = True, Tc: int = 0, *,
+                        out: Optional[torch.Tensor] = None, chunks: int = 16) -> torch.Tensor:
+    """``tsrn_attention`` on host-resident Q, K, V (CPU fp32, best pinned), result
+    in host memory, the PCIe transfers overlapped with the computation: the
+    batch runs in ``chunks`` groups of sequences; group i+1's inputs travel on
+    one copy stream while group i computes on the caller's current stream and
+    group i-1's output returns on a second copy stream.
+
+    Returns a pinned host tensor (or fills ``out``); like any non-blocking copy
+    it is complete once the current stream has been synchronised.  Equals
+    ``tsrn_attention`` on device copies of the inputs bit for bit."""
+    if Q.is_cuda or K.is_cuda or V.is_cuda:
+        raise ValueError("tsrn_attention_host takes host Q, K, V; use tsrn_attention on device")
+    _attention_shapes(Q, K, V, slopes)
+    _lib.load()  # no CPU computation: fails loudly without the CUDA library
+    dev = torch.device("cuda", torch.cuda.current_device())
+    B = Q.shape[0]
+    host_out = out if out is not None else torch.empty(Q.shape, pin_memory=True)
+    main = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    dQ, dK, dV = (torch.empty(t.shape, device=dev) for t in (Q, K, V))
+    dO = torch.empty(Q.shape, device=dev)
+    sl = _f32(slopes).to(dev).contiguous()
+    s_in.wait_stream(main)
+    s_out.wait_stream(main)
+    step = max(1, -(-B // max(1, int(chunks))))
+    groups = [(a, min(B, a + step)) for a in range(0, B, step)]
+    landed = []
+    with torch.cuda.stream(s_in):
+        for a, b in groups:
+            for d, h in ((dQ, Q), (dK, K), (dV, V)):
+                d[a:b].copy_(_f32(h[a:b]), non_blocking=True)
+            e = torch.cuda.Event()
+            e.record(s_in)
+            landed.append(e)
+    for (a, b), e in zip(groups, landed):
+        main.wait_event(e)
+        _tsrn_attention_into(dQ[a:b], dK[a:b], dV[a:b], sl, top_k, causal, Tc, dO[a:b], dev)
+        done = torch.cuda.Event()
+        done.record(main)
+        s_out.wait_event(done)
+        with torch.cuda.stream(s_out):
+            host_out[a:b].copy_(dO[a:b], non_blocking=True)
+    main.wait_stream(s_out)
+    main.wait_stream(s_in)
+    return host_out
 
 
 # --------------------------------------------------------------------------- reservoir

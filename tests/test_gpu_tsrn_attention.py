@@ -118,3 +118,19 @@ def test_module_real_weights(cuda):
     rows_ok = (~_ambiguous_rows(S, top_k)).all(axis=1)
     assert rows_ok.mean() > 0.9
     np.testing.assert_allclose(out[rows_ok], g["out"][rows_ok], rtol=1e-4, atol=2e-5)
+
+
+@pytest.mark.parametrize("chunks", [1, 2, 3, 16])
+def test_host_entry_equals_device_entry(cuda, chunks):
+    # the host-pipelined entry (sequence groups' copies overlapping the
+    # computation) gives the device entry's output bit for bit
+    from mk_iii_technologies_tsrn_b200 import ops
+    Q, K, V, slopes = _case(5, 3, 70, 6, 24, seed=9)
+    hQ, hK, hV = (torch.tensor(a).pin_memory() for a in (Q, K, V))
+    got = ops.tsrn_attention_host(hQ, hK, hV, torch.tensor(slopes), 6, True, 6, chunks=chunks)
+    torch.cuda.synchronize()
+    ref = ops.tsrn_attention(*(torch.tensor(a, device=cuda) for a in (Q, K, V, slopes)), 6, True, 6)
+    assert not got.is_cuda
+    assert torch.equal(got, ref.cpu())
+    with pytest.raises(ValueError):
+        ops.tsrn_attention_host(hQ.cuda(), hK, hV, torch.tensor(slopes), 6)
