@@ -220,14 +220,15 @@ def cpu_gemm_rate(size: int, target_s: float = 12.0, bf16: bool = False):
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(1)
     w = torch.randn(size, size, generator=g)
-    x = torch.randn(64, size, generator=g)
+    x = torch.randn(1024, size, generator=g)
     if bf16:
         w, x = w.bfloat16(), x.bfloat16()
-    # calibrate on 1 row, then size the sample for ~target_s seconds
-    t0 = time.perf_counter()
+    # warm up on 1 row, calibrate on 4, then size the sample for ~target_s seconds
     maxplus_fwd_torch(x[:1], w)
-    dt1 = time.perf_counter() - t0
-    rows = int(max(1, min(64, target_s / max(dt1, 1e-6))))
+    t0 = time.perf_counter()
+    maxplus_fwd_torch(x[:4], w)
+    dt1 = (time.perf_counter() - t0) / 4
+    rows = int(max(1, min(1024, target_s / max(dt1, 1e-6))))
     t0 = time.perf_counter()
     maxplus_fwd_torch(x[:rows], w)
     dt = time.perf_counter() - t0
