@@ -975,12 +975,13 @@ def esn_workload(args, world, rank):
     peak = 2.0 * terms / (pms / 1e3) / 1e12
     achieved = 2.0 * gates * B * T * dr * dr / (ms / args.steps / 1e3) / 1e12
     hH = torch.empty(B, T, dr).pin_memory()
-    dU = torch.empty_like(dev_in[0])
-    rest = dev_in[1:]
 
-    def e2e_step():
-        dU.copy_(hU, non_blocking=True)
-        hH.copy_(fn(dU, *rest), non_blocking=True)
+    def e2e_step():   # the host entry: time windows' copies overlap the recurrence
+        if mode == "leaky":
+            ops.esn_fwd_host(hU, dev_in[1], lk=dev_in[2].reshape(1).to(dev), out=hH)
+        else:   # Uz, Ur derive from U on the device in the module: read in place
+            ops.esn_fwd_host(hU, dev_in[5], Uz=dev_in[1], Ur=dev_in[2], Wzh=dev_in[3],
+                             Wrh=dev_in[4], out=hH)
 
     for _ in range(2):
         e2e_step()

@@ -307,6 +307,29 @@ TP_API int tp_esn_gru_fwd(int64_t B, int64_t T, int64_t dr, const float* U, cons
 TP_API int tp_esn_leaky_fwd(int64_t B, int64_t T, int64_t dr, const float* U, const float* Ws,
                             int64_t ld_ws, const float* leak, float* H, void* stream);
 
+/* Segments of a longer sequence: T steps starting from state h0 ([B] rows of
+ * ld_h0 >= dr floats; NULL: zeros), with U, Uz, Ur and H rows t_stride >= T
+ * steps apart (a time window [t0, t0 + T) of [B, t_stride, dr] tensors is the
+ * base pointer + t0 * dr).  Running [0, T) in consecutive segments, each
+ * starting from the previous segment's last state H[:, t0 - 1], equals one
+ * call over [0, T) bit for bit. */
+TP_API int tp_esn_gru_fwd_seg(int64_t B, int64_t T, int64_t t_stride, int64_t dr,
+                              const float* U, const float* Uz, const float* Ur,
+                              const float* Wzh, int64_t ld_wzh, const float* Wrh,
+                              int64_t ld_wrh, const float* Ws, int64_t ld_ws, const float* h0,
+                              int64_t ld_h0, float* H, void* stream);
+TP_API int tp_esn_leaky_fwd_seg(int64_t B, int64_t T, int64_t t_stride, int64_t dr,
+                                const float* U, const float* Ws, int64_t ld_ws,
+                                const float* leak, const float* h0, int64_t ld_h0, float* H,
+                                void* stream);
+
+/* Copy `rows` rows of width_bytes from src (row pitch src_pitch bytes) to dst
+ * (pitch dst_pitch), host or device memory on either side (pinned host memory
+ * for an asynchronous copy), on `stream`: the strided time windows the
+ * segmented reservoir entries read.  (Utility; no reference counterpart.) */
+TP_API int tp_memcpy2d_async(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                             int64_t width_bytes, int64_t rows, void* stream);
+
 /* ======================================================================== *
  *  Maslov softmax of attention scores, optionally gated (one warp per row).
  *

@@ -109,6 +109,15 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "tp_esn_leaky_fwd": (
         _c_int, [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_p]),
+    "tp_esn_gru_fwd_seg": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p,
+         _c_i64, _c_p, _c_i64, _c_p, _c_p],
+    ),
+    "tp_esn_leaky_fwd_seg": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_p]),
+    "tp_memcpy2d_async": (_c_int, [_c_p, _c_i64, _c_p, _c_i64, _c_i64, _c_i64, _c_p]),
     "tp_tsrn_attention_workspace_bytes": (_c_i64, [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64]),
     "tp_tsrn_attention_fwd": (
         _c_int,

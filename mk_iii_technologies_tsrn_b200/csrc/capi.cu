@@ -473,6 +473,57 @@ int tp_esn_leaky_fwd(int64_t B, int64_t T, int64_t dr, const float* U, const flo
                             as_stream(stream));
 }
 
+int tp_esn_gru_fwd_seg(int64_t B, int64_t T, int64_t t_stride, int64_t dr, const float* U,
+                       const float* Uz, const float* Ur, const float* Wzh, int64_t ld_wzh,
+                       const float* Wrh, int64_t ld_wrh, const float* Ws, int64_t ld_ws,
+                       const float* h0, int64_t ld_h0, float* H, void* stream) {
+  TP_RETURN_IF(B < 0 || T < 0 || dr < 0, TP_ERR_INVALID_ARG);
+  if (B * T * dr == 0) return TP_OK;
+  TP_RETURN_IF(t_stride < T || ld_wzh < dr || ld_wrh < dr || ld_ws < dr, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(h0 != nullptr && ld_h0 < dr, TP_ERR_INVALID_ARG);
+  TP_CHECK_PTR(U);
+  TP_CHECK_PTR(Uz);
+  TP_CHECK_PTR(Ur);
+  TP_CHECK_PTR(Wzh);
+  TP_CHECK_PTR(Wrh);
+  TP_CHECK_PTR(Ws);
+  TP_CHECK_OPT_PTR(h0);
+  TP_CHECK_PTR(H);
+  const float* W[3] = {Wzh, Wrh, Ws};
+  const int64_t ld[3] = {ld_wzh, ld_wrh, ld_ws};
+  return tp::launch_esn_fwd(true, B, T, dr, U, Uz, Ur, W, ld, nullptr, H, as_stream(stream),
+                            t_stride, h0, ld_h0);
+}
+
+int tp_esn_leaky_fwd_seg(int64_t B, int64_t T, int64_t t_stride, int64_t dr, const float* U,
+                         const float* Ws, int64_t ld_ws, const float* leak, const float* h0,
+                         int64_t ld_h0, float* H, void* stream) {
+  TP_RETURN_IF(B < 0 || T < 0 || dr < 0, TP_ERR_INVALID_ARG);
+  if (B * T * dr == 0) return TP_OK;
+  TP_RETURN_IF(t_stride < T || ld_ws < dr, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(h0 != nullptr && ld_h0 < dr, TP_ERR_INVALID_ARG);
+  TP_CHECK_PTR(U);
+  TP_CHECK_PTR(Ws);
+  TP_CHECK_PTR(leak);
+  TP_CHECK_OPT_PTR(h0);
+  TP_CHECK_PTR(H);
+  const float* W[3] = {Ws, nullptr, nullptr};
+  const int64_t ld[3] = {ld_ws, 0, 0};
+  return tp::launch_esn_fwd(false, B, T, dr, U, nullptr, nullptr, W, ld, leak, H,
+                            as_stream(stream), t_stride, h0, ld_h0);
+}
+
+int tp_memcpy2d_async(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch,
+                      int64_t width_bytes, int64_t rows, void* stream) {
+  TP_RETURN_IF(width_bytes < 0 || rows < 0 || dst_pitch < width_bytes || src_pitch < width_bytes,
+               TP_ERR_INVALID_ARG);
+  if (width_bytes == 0 || rows == 0) return TP_OK;
+  TP_RETURN_IF(dst == nullptr || src == nullptr, TP_ERR_NULL_POINTER);
+  return cuda_status(cudaMemcpy2DAsync(dst, (size_t)dst_pitch, src, (size_t)src_pitch,
+                                       (size_t)width_bytes, (size_t)rows, cudaMemcpyDefault,
+                                       as_stream(stream)));
+}
+
 namespace {
 
 // shared argument checks of the two Maslov softmax entries (T and C are

@@ -39,6 +39,9 @@ constexpr int ESN_MAX_RB = 8;      // batch rows per cluster
 
 struct EsnParams {
   int B, T, dr, dr4;
+  int64_t ts;         // steps between consecutive batch rows of U, Uz, Ur, H (>= T)
+  const float* h0;    // initial state [B][ld_h0] (NULL: zeros)
+  int64_t ld_h0;
   const float* U;
   const float* Uz;
   const float* Ur;
@@ -167,7 +170,16 @@ __global__ void __launch_bounds__(ESN_MAX_NT, 1) esn_kernel(EsnParams p) {
         wsm[(g * ncl + c) * dr4 + k] = v;
       }
   }
-  for (int e = tid; e < 2 * RB * dr4; e += nt) hs[e] = 0.0f;
+  // state buffers: h_{-1} = h0 (or 0) in the buffer step 0 reads (GRU: h;
+  // leaky: buffer 0), zeros elsewhere
+  for (int e = tid; e < 2 * RB * dr4; e += nt) {
+    float v = 0.0f;
+    if (p.h0 && e < RB * dr4) {
+      const int r = e / dr4, k = e - r * dr4;
+      if (k < dr && b0 + r < p.B) v = p.h0[(int64_t)(b0 + r) * p.ld_h0 + k];
+    }
+    hs[e] = v;
+  }
 
   // stage step t's inputs into ring slot t % 3 (one commit group per call,
   // empty past the end so that the group count stays uniform)
@@ -179,7 +191,7 @@ __global__ void __launch_bounds__(ESN_MAX_NT, 1) esn_kernel(EsnParams p) {
       const int b = b0 + bl, cg = c0 + c;
       const float* src = pi == 0 ? p.U : (pi == 1 ? p.Uz : p.Ur);
       const bool ok = b < p.B && cg < dr;
-      tp_cp_async4(dst + e, ok ? src + ((int64_t)b * p.T + t) * dr + cg : src, ok ? 4 : 0);
+      tp_cp_async4(dst + e, ok ? src + ((int64_t)b * p.ts + t) * dr + cg : src, ok ? 4 : 0);
     }
     tp_cp_async_commit();
   };
@@ -194,6 +206,7 @@ __global__ void __launch_bounds__(ESN_MAX_NT, 1) esn_kernel(EsnParams p) {
   const float4* w_r = kGru ? wrow(1) : w_s;
   const int pidx = row * ncl + min(cl, ncl - 1);
   float hprev = 0.0f, zv = 0.0f;
+  if (p.h0 && col_ok && row_ok) hprev = p.h0[(int64_t)(b0 + row) * p.ld_h0 + c0 + cl];
   const float lk = kGru ? 0.0f : *p.leak;
 
   // Receive barriers, one phase per exchange: each expects the bytes of every
@@ -292,7 +305,7 @@ __global__ void __launch_bounds__(ESN_MAX_NT, 1) esn_kernel(EsnParams p) {
     if (col_ok && row_ok) {
       for (uint32_t rk = part; rk < csize; rk += PARTS)
         esn_st_async(dst + row * dr4 + c0 + cl, &mb[kGru ? 1 : (t + 1) & 1], rk, h);
-      if (part == 0) p.H[((int64_t)(b0 + row) * p.T + t) * dr + c0 + cl] = h;
+      if (part == 0) p.H[((int64_t)(b0 + row) * p.ts + t) * dr + c0 + cl] = h;
     }
   }
   // the last exchange has fully arrived here, and (cluster barrier) everywhere
@@ -497,9 +510,11 @@ bool esn_vec_ok(const float* w, int64_t ld, int dr) {
 
 int launch_esn_fwd(bool gru, int64_t B, int64_t T, int64_t dr, const float* U, const float* Uz,
                    const float* Ur, const float* const W[3], const int64_t ld[3],
-                   const float* leak, float* H, cudaStream_t stream) {
+                   const float* leak, float* H, cudaStream_t stream, int64_t ts,
+                   const float* h0, int64_t ld_h0) {
   if (B * T * dr == 0) return TP_OK;
   if (B > INT32_MAX / 2 || T > INT32_MAX / 2) return TP_ERR_TOO_LARGE;
+  if (ts < T) ts = T;
   if (dr > 16 * ESN_MAX_NCL) return TP_ERR_UNSUPPORTED;
   const int G = gru ? 3 : 1;
   bool global_ok = true;
@@ -511,6 +526,9 @@ int launch_esn_fwd(bool gru, int64_t B, int64_t T, int64_t dr, const float* U, c
   EsnParams p{};
   p.B = (int)B;
   p.T = (int)T;
+  p.ts = ts;
+  p.h0 = h0;
+  p.ld_h0 = ld_h0;
   p.dr = (int)dr;
   p.dr4 = ((int)dr + 3) & ~3;
   p.U = U;

@@ -198,7 +198,8 @@ int launch_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int6
 // W[0..2] = Wzh, Wrh, Ws for GRU, W[0] = Ws for leaky
 int launch_esn_fwd(bool gru, int64_t B, int64_t T, int64_t dr, const float* U, const float* Uz,
                    const float* Ur, const float* const W[3], const int64_t ld[3],
-                   const float* leak, float* H, cudaStream_t stream);
+                   const float* leak, float* H, cudaStream_t stream, int64_t ts = 0,
+                   const float* h0 = nullptr, int64_t ld_h0 = 0);
 
 // maslov.cu: (gated) Maslov softmax of attention scores.  Scores T, C, P, dP,
 // dT, dC: [rows = B*H*Lq, Lk] contiguous; g / dg at b*gsb + i*gsi + h*gsh;

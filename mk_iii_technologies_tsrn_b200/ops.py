@@ -746,42 +746,145 @@ def _rows(w: torch.Tensor, dr: int) -> Tuple[torch.Tensor, int]:
     return w, w.stride(0)
 
 
+def _h0(h0: Optional[torch.Tensor], B: int, dr: int):
+    if h0 is None:
+        return None, 0
+    if h0.shape != (B, dr):
+        raise ValueError(f"h0 must be [B, dr] = {(B, dr)}, got {tuple(h0.shape)}")
+    h0 = _f32(h0)
+    if h0.stride(1) != 1:
+        h0 = h0.contiguous()
+    return h0, h0.stride(0)
+
+
+def _esn_call(gru: bool, U, Uz, Ur, W, lk, h0, H, T: int, t_stride: int, dev) -> None:
+    """One segmented launch: T steps of the [B, t_stride, dr] tensors U (Uz, Ur)
+    and H starting at their base pointers (views), from state h0."""
+    B, dr = U.shape[0], U.shape[2]
+    lib = _lib.load()
+    h0, ldh = _h0(h0, B, dr)
+    with torch.cuda.device(dev):
+        if gru:
+            (Wzh, lz), (Wrh, lr), (Ws, ls) = W
+            st = lib.tp_esn_gru_fwd_seg(B, T, t_stride, dr, _ptr(U), _ptr(Uz), _ptr(Ur),
+                                        _ptr(Wzh), lz, _ptr(Wrh), lr, _ptr(Ws), ls, _ptr(h0),
+                                        ldh, _ptr(H), _stream(dev))
+        else:
+            (Ws, ls), = W
+            st = lib.tp_esn_leaky_fwd_seg(B, T, t_stride, dr, _ptr(U), _ptr(Ws), ls, _ptr(lk),
+                                          _ptr(h0), ldh, _ptr(H), _stream(dev))
+    _lib.check(st, "tp_esn_gru_fwd_seg" if gru else "tp_esn_leaky_fwd_seg")
+
+
 def esn_gru_fwd(U: torch.Tensor, Uz: torch.Tensor, Ur: torch.Tensor, Wzh: torch.Tensor,
-                Wrh: torch.Tensor, Ws: torch.Tensor) -> torch.Tensor:
+                Wrh: torch.Tensor, Ws: torch.Tensor,
+                h0: Optional[torch.Tensor] = None) -> torch.Tensor:
     """GRU-gated echo-state recurrence over all T steps in one launch
     (research/tsrn_dml.py:834-840); returns H [B, T, dr].  Forward only.
-    Wzh / Wrh may be the column slices ``W_z.weight[:, :dr]`` in place."""
-    dev = _require_cuda(U, Uz, Ur, Wzh, Wrh, Ws)
+    Wzh / Wrh may be the column slices ``W_z.weight[:, :dr]`` in place.
+    ``h0`` [B, dr] continues a sequence from that state (default zeros, as the
+    reference module starts)."""
+    dev = _require_cuda(U, Uz, Ur, Wzh, Wrh, Ws, h0)
     U, Uz, Ur = (_f32(t).contiguous() for t in (U, Uz, Ur))
     B, T, dr = U.shape
     if Uz.shape != U.shape or Ur.shape != U.shape:
         raise ValueError("esn_gru_fwd: U, Uz and Ur must have the same shape")
-    (Wzh, lz), (Wrh, lr), (Ws, ls) = (_rows(w, dr) for w in (Wzh, Wrh, Ws))
+    W = [_rows(w, dr) for w in (Wzh, Wrh, Ws)]
     H = torch.empty_like(U)
-    lib = _lib.load()
-    with torch.cuda.device(dev):
-        st = lib.tp_esn_gru_fwd(B, T, dr, _ptr(U), _ptr(Uz), _ptr(Ur), _ptr(Wzh), lz,
-                                _ptr(Wrh), lr, _ptr(Ws), ls, _ptr(H), _stream(dev))
-    _lib.check(st, "tp_esn_gru_fwd")
+    _esn_call(True, U, Uz, Ur, W, None, h0, H, T, T, dev)
     return H
 
 
-def esn_leaky_fwd(U: torch.Tensor, Ws: torch.Tensor, lk: torch.Tensor) -> torch.Tensor:
+def esn_leaky_fwd(U: torch.Tensor, Ws: torch.Tensor, lk: torch.Tensor,
+                  h0: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Leaky echo-state recurrence h = (1 - lk) h + lk tanh(h Ws^T + U_t) over
     all T steps in one launch (tsrn_gpu.py:480-484); ``lk`` is the device
-    scalar sigmoid(leak).  Returns H [B, T, dr].  Forward only."""
-    dev = _require_cuda(U, Ws, lk)
+    scalar sigmoid(leak).  Returns H [B, T, dr].  Forward only.  ``h0`` [B, dr]
+    continues a sequence from that state (default zeros)."""
+    dev = _require_cuda(U, Ws, lk, h0)
     U = _f32(U).contiguous()
     B, T, dr = U.shape
-    Ws, ls = _rows(Ws, dr)
     lk = _f32(lk).reshape(1).contiguous()
     H = torch.empty_like(U)
-    lib = _lib.load()
-    with torch.cuda.device(dev):
-        st = lib.tp_esn_leaky_fwd(B, T, dr, _ptr(U), _ptr(Ws), ls, _ptr(lk), _ptr(H),
-                                  _stream(dev))
-    _lib.check(st, "tp_esn_leaky_fwd")
+    _esn_call(False, U, None, None, [_rows(Ws, dr)], lk, h0, H, T, T, dev)
     return H
+
+
+def _copy_rows(dst: torch.Tensor, src: torch.Tensor, stream) -> None:
+    """dst[b] <- src[b] for every row b of two [B, ...] views whose rows are
+    contiguous runs (time windows of [B, T, dr] tensors): one 2-D copy."""
+    B = src.shape[0]
+    width = src[0].numel() * src.element_size()
+    st = _lib.load().tp_memcpy2d_async(_ptr(dst), dst.stride(0) * dst.element_size(), _ptr(src),
+                                       src.stride(0) * src.element_size(), width, B,
+                                       ctypes.c_void_p(stream.cuda_stream))
+    _lib.check(st, "tp_memcpy2d_async")
+
+
+def esn_fwd_host(U: torch.Tensor, Ws: torch.Tensor, *, Uz: Optional[torch.Tensor] = None,
+                 Ur: Optional[torch.Tensor] = None, Wzh: Optional[torch.Tensor] = None,
+                 Wrh: Optional[torch.Tensor] = None, lk: Optional[torch.Tensor] = None,
+                 out: Optional[torch.Tensor] = None, segments: int = 4) -> torch.Tensor:
+    """Reservoir recurrence on host-resident inputs (CPU fp32 [B, T, dr], best
+    pinned), H returned in host memory, PCIe transfers overlapped with the
+    recurrence: the sequence runs in ``segments`` time windows, each continuing
+    from the previous window's last state on the device; window i+1's inputs
+    travel on one copy stream while window i runs on the caller's current
+    stream and window i-1's states return on a second copy stream.  GRU-gated
+    (tsrn_dml.py) when ``Uz``, ``Ur``, ``Wzh``, ``Wrh`` are given, else leaky
+    (tsrn_gpu.py) with the device scalar ``lk``.  Weights are device tensors;
+    ``Uz`` / ``Ur`` may be device tensors too (computed on the device from U,
+    as the module does), which are then read in place.
+
+    Returns a pinned host tensor (or fills ``out``); complete once the current
+    stream has been synchronised.  Equals ``esn_gru_fwd`` / ``esn_leaky_fwd``
+    on device copies bit for bit."""
+    gru = Uz is not None
+    if U.is_cuda:
+        raise ValueError("esn_fwd_host takes host U; use esn_*_fwd on device")
+    if gru and (Ur is None or Wzh is None or Wrh is None):
+        raise ValueError("the GRU recurrence needs Uz, Ur, Wzh and Wrh")
+    if not gru and lk is None:
+        raise ValueError("the leaky recurrence needs lk")
+    dev = _require_cuda(Ws, Wzh, Wrh, lk)
+    ins = [U] + ([Uz, Ur] if gru else [])
+    B, T, dr = U.shape
+    for t in ins:
+        if t.shape != (B, T, dr) or t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError("U (Uz, Ur) must be contiguous fp32 [B, T, dr] tensors")
+        if t.is_cuda and t.device != dev:
+            raise RuntimeError(f"{t.device} input with weights on {dev}")
+    W = [_rows(w, dr) for w in ((Wzh, Wrh, Ws) if gru else (Ws,))]
+    lkd = _f32(lk).reshape(1).contiguous() if lk is not None else None
+    host_H = out if out is not None else torch.empty((B, T, dr), pin_memory=True)
+    main = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    dev_in = [t if t.is_cuda else torch.empty((B, T, dr), device=dev) for t in ins]
+    dH = torch.empty((B, T, dr), device=dev)
+    s_in.wait_stream(main)
+    s_out.wait_stream(main)
+    step = max(1, -(-T // max(1, int(segments))))
+    wins = [(a, min(T, a + step)) for a in range(0, T, step)]
+    landed = []
+    for a, b in wins:
+        for d, h in zip(dev_in, ins):
+            if not h.is_cuda:
+                _copy_rows(d[:, a:b], h[:, a:b], s_in)
+        e = torch.cuda.Event()
+        e.record(s_in)
+        landed.append(e)
+    for (a, b), e in zip(wins, landed):
+        main.wait_event(e)
+        h0 = dH[:, a - 1] if a > 0 else None
+        _esn_call(gru, dev_in[0][:, a:], dev_in[1][:, a:] if gru else None,
+                  dev_in[2][:, a:] if gru else None, W, lkd, h0, dH[:, a:], b - a, T, dev)
+        done = torch.cuda.Event()
+        done.record(main)
+        s_out.wait_event(done)
+        _copy_rows(host_H[:, a:b], dH[:, a:b], s_out)
+    main.wait_stream(s_out)
+    main.wait_stream(s_in)
+    return host_H
 
 
 def _maslov_inputs(T, C, g, tau, mask):

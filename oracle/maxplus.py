@@ -200,13 +200,13 @@ def lfdual_act(y, mode: str, slopes, biases, x_grid, blend_gate=None):
     return (g * primal + (np.float32(1.0) - g) * dual).astype(np.float32)
 
 
-def esn_gru_fwd(U, Uz, Ur, Wzh, Wrh, Ws):
+def esn_gru_fwd(U, Uz, Ur, Wzh, Wrh, Ws, h0=None):
     """GRU-gated echo-state recurrence (research/tsrn_dml.py:834-840) in float64,
-    h_{-1} = 0; returns H [B, T, dr]."""
+    h_{-1} = h0 (the reference: 0); returns H [B, T, dr]."""
     U, Uz, Ur = (np.asarray(a, np.float64) for a in (U, Uz, Ur))
     Wzh, Wrh, Ws = (np.asarray(a, np.float64) for a in (Wzh, Wrh, Ws))
     B, T, dr = U.shape
-    h = np.zeros((B, dr))
+    h = np.zeros((B, dr)) if h0 is None else np.asarray(h0, np.float64).copy()
     H = np.empty((B, T, dr))
     sig = lambda v: 1.0 / (1.0 + np.exp(-v))
     for t in range(T):
@@ -218,14 +218,15 @@ def esn_gru_fwd(U, Uz, Ur, Wzh, Wrh, Ws):
     return H
 
 
-def esn_leaky_fwd(U, Ws, lk):
+def esn_leaky_fwd(U, Ws, lk, h0=None):
     """Leaky echo-state recurrence h = (1 - lk) h + lk tanh(h Ws^T + U_t)
-    (tsrn_gpu.py:480-484) in float64, h_{-1} = 0; returns H [B, T, dr]."""
+    (tsrn_gpu.py:480-484) in float64, h_{-1} = h0 (the reference: 0); returns
+    H [B, T, dr]."""
     U = np.asarray(U, np.float64)
     Ws = np.asarray(Ws, np.float64)
     lk = float(np.asarray(lk).reshape(()))
     B, T, dr = U.shape
-    h = np.zeros((B, dr))
+    h = np.zeros((B, dr)) if h0 is None else np.asarray(h0, np.float64).copy()
     H = np.empty((B, T, dr))
     for t in range(T):
         h = (1 - lk) * h + lk * np.tanh(h @ Ws.T + U[:, t])

@@ -133,3 +133,57 @@ def test_esn_rejects_cpu_inputs():
     w = torch.zeros(4, 4)
     with pytest.raises((RuntimeError, ValueError)):
         ops.esn_gru_fwd(z, z, z, w, w, w)
+
+
+@pytest.mark.parametrize("gru", [True, False])
+@pytest.mark.parametrize("B,T,dr", [(9, 40, 96), (64, 30, 320)])
+def test_esn_segments_continue_bit_for_bit(cuda, gru, B, T, dr):
+    # a sequence run as consecutive segments, each from the previous segment's
+    # last state (h0), equals one launch over the whole sequence bit for bit;
+    # h0 against the oracle
+    from mk_iii_technologies_tsrn_b200 import ops
+    rng = np.random.default_rng(B + T + dr)
+    U, Uz, Ur, Wzh, Wrh, Ws = (torch.tensor(a, device=cuda) for a in _inputs(rng, B, T, dr))
+    lk = torch.tensor([0.3], device=cuda)
+
+    def run(sl, h0=None):
+        if gru:
+            return ops.esn_gru_fwd(U[:, sl], Uz[:, sl], Ur[:, sl], Wzh, Wrh, Ws, h0=h0)
+        return ops.esn_leaky_fwd(U[:, sl], Ws, lk, h0=h0)
+
+    whole = run(slice(0, T))
+    parts, h0 = [], None
+    for a, b in ((0, 7), (7, 8), (8, 25), (25, T)):
+        parts.append(run(slice(a, b), h0))
+        h0 = parts[-1][:, -1]
+    assert torch.equal(torch.cat(parts, dim=1), whole)
+    h0 = torch.tensor(rng.uniform(-0.9, 0.9, (B, dr)).astype(np.float32), device=cuda)
+    got = run(slice(0, T), h0).cpu().numpy()
+    if gru:
+        ref = oracle.esn_gru_fwd(*(t.cpu().numpy() for t in (U, Uz, Ur, Wzh, Wrh, Ws)),
+                                 h0=h0.cpu().numpy())
+    else:
+        ref = oracle.esn_leaky_fwd(U.cpu().numpy(), Ws.cpu().numpy(), 0.3, h0=h0.cpu().numpy())
+    np.testing.assert_allclose(got, ref, rtol=0, atol=TOL)
+
+
+@pytest.mark.parametrize("gru", [True, False])
+@pytest.mark.parametrize("segments", [1, 3, 4])
+def test_esn_host_entry_equals_device(cuda, gru, segments):
+    # host-resident inputs, time windows' copies overlapping the recurrence
+    from mk_iii_technologies_tsrn_b200 import ops
+    rng = np.random.default_rng(21)
+    U, Uz, Ur, Wzh, Wrh, Ws = _inputs(rng, 17, 50, 72)
+    hU, hUz, hUr = (torch.tensor(a).pin_memory() for a in (U, Uz, Ur))
+    dW = [torch.tensor(a, device=cuda) for a in (Wzh, Wrh, Ws)]
+    lk = torch.tensor([0.25], device=cuda)
+    if gru:
+        got = ops.esn_fwd_host(hU, dW[2], Uz=hUz, Ur=hUr, Wzh=dW[0], Wrh=dW[1],
+                               segments=segments)
+        ref = ops.esn_gru_fwd(hU.to(cuda), hUz.to(cuda), hUr.to(cuda), *dW)
+    else:
+        got = ops.esn_fwd_host(hU, dW[2], lk=lk, segments=segments)
+        ref = ops.esn_leaky_fwd(hU.to(cuda), dW[2], lk)
+    torch.cuda.synchronize()
+    assert not got.is_cuda
+    assert torch.equal(got, ref.cpu())
