@@ -86,6 +86,12 @@ def parse_args():
     p.add_argument("--esn-mode", choices=["gru", "leaky"], default="gru",
                    help="esn workload: GRU-gated reservoir of config 5 (research/tsrn_dml.py, "
                         "d_reservoir 320) or the leaky one of tsrn_gpu.py (d_reservoir 640)")
+    p.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                   help="batch workloads (scan, dtn, linear, tsrn_attn, esn, tsrn_block): "
+                        "'strong' splits the configuration's batch over the ranks, 'weak' "
+                        "gives every rank the whole batch")
+    p.add_argument("--no-secondary", action="store_true",
+                   help="default GEMM line only: skip the other workloads' sub-lines")
     p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                    help="N>1 GEMM: fused peer-store epilogue (p2p) or NCCL all-gather")
     return p.parse_args()
@@ -194,6 +200,25 @@ def profiled_traffic(key):
     return None
 
 
+def local_batch(total: int, world: int, args) -> int:
+    """Rows of a batch workload this rank runs: the whole batch (weak scaling) or
+    its 1/world share (strong scaling: the configuration's batch split over the
+    ranks, no exchange between them)."""
+    if args.scaling == "weak" or world == 1:
+        return total
+    if total % world:
+        raise SystemExit(f"batch {total} does not split over {world} ranks")
+    return total // world
+
+
+def parallelism(total: int, local: int, world: int, what: str = "batch") -> str:
+    if world == 1:
+        return "single GPU"
+    if local == total:
+        return f"{what} replicated x{world} (weak: {total} per rank)"
+    return f"{what}-sharded x{world} (strong: {local} of {total} per rank, no exchange)"
+
+
 def time_steps(step, steps, world):
     """Device time of `steps` calls of step() between barrier+sync fences (max over ranks)."""
     stream = torch.cuda.current_stream()
@@ -206,6 +231,10 @@ def time_steps(step, steps, world):
         step()
     end.record(stream)
     torch.cuda.synchronize()
+    # a bounded device-side wait that ran out means a kernel returned early:
+    # the step's results (and its timing) are not valid -- raise
+    from mk_iii_technologies_tsrn_b200 import ops
+    ops.check_device_error()
     barrier(world)
     return max_over_ranks(start.elapsed_time(end), world)
 
@@ -282,6 +311,12 @@ def gemm_workload(args, world, rank):
     gm = torch.Generator(device=dev).manual_seed(2)
     W_full_rows[torch.rand(N, K, device=dev, generator=gm) < 0.05] = float("-inf")
     W = W_full_rows[rank * Nr:(rank + 1) * Nr].contiguous()
+    # columns the self-check compares: the first and last 64 of EVERY rank's
+    # column range (at N>1 the other ranks' columns arrive over NVLink or NCCL)
+    ce = min(64, Nr)
+    chk_cols = torch.cat([torch.arange(r * Nr, r * Nr + ce) for r in range(world)] +
+                         [torch.arange((r + 1) * Nr - ce, (r + 1) * Nr) for r in range(world)])
+    W_chk = W_full_rows[chk_cols.to(dev)].cpu()
     del W_full_rows
     if args.dtype == "bf16":
         x, W = x.to(torch.bfloat16), W.to(torch.bfloat16)
@@ -317,23 +352,39 @@ def gemm_workload(args, world, rank):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    # quick self-check on a few rows (oracle on CPU is too slow for the full size)
-    if rank == 0:
-        import oracle
-        import numpy as np
-        rows = slice(0, 2)
-        ref_fn = oracle.maxplus_fwd_bf16 if bf16_arith else oracle.maxplus_fwd
-        ry, ri = ref_fn(x[rows].float().cpu().numpy(), W[:256].float().cpu().numpy())
-        if sharded is None:
-            yc, ac = y[rows, :256], am[rows, :256]
-        else:
-            yo, ao = sharded(x.float(), W.float())
-            torch.cuda.synchronize()
-            yc, ac = yo[rows, :256], ao[rows, :256]
-        assert np.array_equal(yc.cpu().numpy(), ry)
-        assert np.array_equal(ac.cpu().numpy(), ri)
-    elif sharded is not None:
-        sharded(x.float(), W.float())   # every rank takes the same collective steps
+    # bit-exact self-check against the oracle (oracle.maxplus_fwd: the
+    # reference expression tropformer.py:131,141) on sampled rows x the columns
+    # above.  Every rank checks its own full result, so at N>1 the columns that
+    # the other ranks wrote are compared too; the verdict is reduced over the
+    # ranks (MIN) and any mismatch ends the run with a non-zero exit code.
+    import oracle
+    import numpy as np
+    chk_rows = torch.tensor([0, 1, M // 2 + 3, M - 1])
+    if sharded is None:
+        yo, ao = y, am
+    else:
+        yo, ao = sharded(x.float(), W.float())   # every rank takes the same collective steps
+    torch.cuda.synchronize()
+    ref_fn = oracle.maxplus_fwd_bf16 if bf16_arith else oracle.maxplus_fwd
+    wref = W_chk.to(x.dtype).float() if args.dtype == "bf16" else W_chk
+    ry, ri = ref_fn(x[chk_rows.to(dev)].float().cpu().numpy(), wref.numpy())
+    cc = chk_cols.to(dev)
+    got_y = yo[chk_rows.to(dev)][:, cc].cpu().numpy()
+    got_i = ao[chk_rows.to(dev)][:, cc].cpu().numpy()
+    ok = bool(np.array_equal(got_y, ry) and np.array_equal(got_i, ri))
+    flag = torch.tensor([1 if ok else 0], device=dev, dtype=torch.int32)
+    if world > 1:
+        torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN)
+    if not ok:
+        bad = np.argwhere((got_y != ry) | (got_i != ri))[:4]
+        print(f"rank {rank}: max-plus self-check MISMATCH at (row, column) "
+              f"{[(int(chk_rows[a]), int(chk_cols[b])) for a, b in bad]}", file=sys.stderr,
+              flush=True)
+    if int(flag.item()) != 1:
+        raise SystemExit("max-plus self-check failed against the oracle")
+    check_desc = (f"bit-exact vs oracle on {len(chk_rows)} rows x {len(chk_cols)} columns "
+                  f"(first/last {ce} of each of the {world} rank column ranges), "
+                  f"all ranks (MIN-reduced)")
 
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
@@ -437,7 +488,8 @@ def gemm_workload(args, world, rank):
                        "all-gather fused into the GEMM epilogue (peer stores into "
                        "symmetric memory over NVLink)" if args.exchange == "p2p" else
                        "NCCL all-gather of y/argmax")) if world > 1 else "single GPU",
-                   "l2": "inputs (2 x 256 MiB) larger than L2"},
+                   "l2": "inputs (2 x 256 MiB) larger than L2",
+                   "self_check": check_desc},
         "e2e": {"value": e2e_value, "unit": "Gop/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         # one max-plus kernel per step (+2 exact widening kernels for bf16 operands with
@@ -453,7 +505,7 @@ def scan_workload(args, world, rank):
     from mk_iii_technologies_tsrn_b200 import ops, _lib
 
     _lib.load().tp_set_pointer_checks(0)
-    B, T, C = 16, 4096, 1024
+    B, T, C = local_batch(16, world, args), 4096, 1024
     dev = torch.device("cuda")
     gen = torch.Generator(device=dev).manual_seed(100 + rank)
     a = -torch.rand(C, device=dev, generator=gen)
@@ -513,11 +565,13 @@ def scan_workload(args, world, rank):
         "metric": "tropical scan GB/s (fwd 12 B/elem + argmax-path bwd 20 B/elem)",
         "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: a=-U(0,1), b~N(0,0.1), x~N(0,1), g~N(0,1), h0=-inf (seeded)",
-        "config": {"workload": "tropical_ssm_scan B=16 T=4096 C=1024 per GPU, fwd+bwd",
-                   "parallelism": f"batch-replicated x{world} (weak)",
-                   "l2": "inputs (3 x 256 MiB) larger than L2"},
+        "config": {"workload": f"tropical_ssm_scan B={B * world} T={T} C={C}, fwd+bwd",
+                   "parallelism": parallelism(16, B, world),
+                   "l2": f"inputs (3 x {B * T * C * 4 >> 20} MiB)" + (
+                       " larger than L2" if 3 * B * T * C * 4 > 126 << 20 else
+                       " fit L2 together; each step rewrites h and gu")},
         "e2e": {"value": e2e_value, "unit": "GB/s",
                 "h2d_bytes_per_step": 3 * elems * 4, "d2h_bytes_per_step": 2 * elems * 4},
         "gpu_launches": 3 * args.steps,
@@ -550,7 +604,7 @@ def dtn_workload(args, world, rank):
     from mk_iii_technologies_tsrn_b200.dtn import DTNAttention
 
     _lib.load().tp_set_pointer_checks(0)
-    B, L, D, H = 128, 64, 256, 8
+    B, L, D, H = local_batch(128, world, args), 64, 256, 8
     dev = torch.device("cuda")
     torch.manual_seed(1 + rank)
     attn = DTNAttention(D, H, dropout=0.0).to(dev)
@@ -598,7 +652,7 @@ def dtn_workload(args, world, rank):
     tokens = B * L * world
     value = tokens / (ms / args.steps / 1e3)
     # dominant kernels (about 40% of the step): the STE backward of a tropical
-    # projection (M=8192, N=K=256): its stats pass and the one-pass gx + gW
+    # projection (M=B*64, N=K=256): its stats pass and the one-pass gx + gW
     # kernel each evaluate one exponential per (m, n, k) term -> 2*M*N*K per
     # call, against the SFU-bound probe of the same per-term instruction form
     xf = x.detach().reshape(-1, D)
@@ -652,11 +706,12 @@ def dtn_workload(args, world, rank):
         "metric": "DTN tropical attention block tokens/s (fwd+bwd, train mode)",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: x ~ N(0,1), upstream grad ~ N(0,1), Q/K weights N(0,0.02), "
                 "tau_h ~ U(0.1,1) (seeded)",
-        "config": {"workload": "DTNAttention d_model=256 heads=8 B=128 L=64 fwd+bwd (STE)",
-                   "parallelism": f"batch-replicated x{world} (weak)" if world > 1 else "single GPU",
+        "config": {"workload": f"DTNAttention d_model=256 heads=8 B={B * world} L=64 fwd+bwd "
+                               "(STE)",
+                   "parallelism": parallelism(128, B, world),
                    "launch": "CUDA graph of the whole step" if graph is not None else "eager",
                    "l2": "activations 8 MiB (fit L2); the tropical kernels are compute-bound"},
         "e2e": {"value": tokens / (e2e_ms / 3 / 1e3), "unit": "tokens/s",
@@ -664,7 +719,7 @@ def dtn_workload(args, world, rank):
         "gpu_launches": per_step * args.steps if per_step is not None else None,
         "roofline": {"bound": "sfu (ex2)", "achieved": achieved, "peak": peak,
                      "unit": "T exp/s", "frac": achieved / peak, "traffic": None,
-                     "kernel": "STE backward of the Q projection (M=8192, N=K=256): stats "
+                     "kernel": f"STE backward of the Q projection (M={B * L}, N=K=256): stats "
                                "pass + one-pass gx/gW kernel, 2*M*N*K exponentials per call",
                      "kernel_ms": kms,
                      "peak_source": "in-repo SFU probe of the same per-term form "
@@ -679,7 +734,7 @@ def linear_workload(args, world, rank):
     from mk_iii_technologies_tsrn_b200 import ops, _lib
 
     _lib.load().tp_set_pointer_checks(0)
-    M, K, N = 1024, 256, 256
+    M, K, N = local_batch(1024, world, args), 256, 256
     dev = torch.device("cuda")
     gen = torch.Generator().manual_seed(rank)
     hx = torch.randn(M, K, generator=gen).pin_memory()
@@ -796,11 +851,11 @@ def linear_workload(args, world, rank):
         "metric": "tropical linear fwd+argmax+bwd Gop/s (2*M*N*K forward ops per step)",
         "value": value, "unit": "Gop/s", "n_gpus": world, "steps": steps,
         "warmup": max(args.warmup, 10), "ms_per_step": ms / steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: x, W, g ~ N(0,1) (seeded)",
-        "config": {"workload": "tropical linear M=1024 K=256 N=256 fwd + int32 argmax + "
-                               "argmax backward (eval mode), no bias",
-                   "parallelism": f"replicated x{world} (weak)" if world > 1 else "single GPU",
+        "config": {"workload": f"tropical linear M={M * world} K=256 N=256 fwd + int32 argmax "
+                               "+ argmax backward (eval mode), no bias",
+                   "parallelism": parallelism(1024, M, world, "rows"),
                    "launch": "CUDA graph of the whole step" if graph is not None else "eager",
                    "l2": "inputs 2 MiB, resident in L2 (the problem is smaller than L2)"},
         "e2e": {"value": ops_step * world / (e2e_ms / steps / 1e3) / 1e9, "unit": "Gop/s",
@@ -809,8 +864,8 @@ def linear_workload(args, world, rank):
         "gpu_launches": per_step * steps if per_step is not None else None,
         "roofline": {"bound": "cuda-core", "achieved": achieved, "peak": peak, "unit": "Top/s",
                      "frac": achieved / peak, "traffic": None,
-                     "kernel": "max-plus forward with argmax (M=1024, N=K=256): 16 tiles, "
-                               "too small to fill 148 SMs",
+                     "kernel": f"max-plus forward with argmax (M={M}, N=K=256): too few "
+                               "tiles to fill 148 SMs",
                      "kernel_ms": kms,
                      "peak_source": "in-repo add+max probe, best form, this run; of measured"},
         "clocks": clk,
@@ -828,7 +883,7 @@ def tsrn_attn_workload(args, world, rank):
 
     _lib.load().tp_set_pointer_checks(0)
     B, H, T, dh, k = (TSRN_ATT[n] for n in ("B", "H", "T", "dh", "top_k"))
-    B = args.att_batch
+    B = local_batch(args.att_batch, world, args)
     dev = torch.device("cuda")
     gen = torch.Generator().manual_seed(10 + rank)
     # LayerNorm'd, rotated Q and K have unit-variance entries; V as projected
@@ -888,13 +943,13 @@ def tsrn_attn_workload(args, world, rank):
         "metric": "TSRN tropical top-k attention tokens/s (fused fwd, inference)",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: Q, K, V ~ N(0,1) (seeded; the statistics of LayerNorm'd, rotated "
                 "Q/K), ALiBi slopes 2^(-8(h+1)/H)",
-        "config": {"workload": f"TSRN TropicalAttention B={B} H={H} T={T} d_h={dh} "
+        "config": {"workload": f"TSRN TropicalAttention B={B * world} H={H} T={T} d_h={dh} "
                                f"top_k={k} causal (config 5, scale 1)",
-                   "parallelism": f"batch x{world} (weak)" if world > 1 else "single GPU",
-                   "l2": "Q/K/V 3 x 168 MiB, larger than L2"},
+                   "parallelism": parallelism(args.att_batch, B, world),
+                   "l2": f"Q/K/V 3 x {B * H * T * dh * 4 >> 20} MiB"},
         "e2e": {"value": tokens / (e2e_ms / e2e_steps / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": 3 * hQ.numel() * 4, "d2h_bytes_per_step": hout.numel() * 4},
         "gpu_launches": per_step * args.steps if per_step is not None else None,
@@ -939,7 +994,7 @@ def esn_workload(args, world, rank):
     from mk_iii_technologies_tsrn_b200 import ops, _lib
 
     _lib.load().tp_set_pointer_checks(0)
-    mode, B, T = args.esn_mode, ESN["B"], ESN["T"]
+    mode, B, T = args.esn_mode, local_batch(ESN["B"], world, args), ESN["T"]
     dev = torch.device("cuda")
     gen = torch.Generator().manual_seed(20 + rank)
     dr, host = esn_inputs(mode, B, T, gen)
@@ -997,14 +1052,14 @@ def esn_workload(args, world, rank):
         "metric": f"echo-state reservoir tokens/s ({mode}, fused recurrence, inference)",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded): U with the statistics of W_in(LayerNorm(x)), sparse "
                 "W_res scaled to spectral radius 0.75" + ("" if mode == "leaky" else
                                                           ", GRU gate inputs"),
-        "config": {"workload": f"{name} d_reservoir={dr} B={B} T={T}" +
+        "config": {"workload": f"{name} d_reservoir={dr} B={B * world} T={T}" +
                                (" (config 5 first-block reservoir)" if mode == "gru" else ""),
-                   "parallelism": f"batch x{world} (weak)" if world > 1 else "single GPU",
-                   "l2": f"U and H {B * T * dr * 4 / 2**20:.0f} MiB each, larger than L2"},
+                   "parallelism": parallelism(ESN["B"], B, world),
+                   "l2": f"U and H {B * T * dr * 4 / 2**20:.0f} MiB each"},
         "e2e": {"value": tokens / (e2e_ms / e2e_steps / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": hU.numel() * 4, "d2h_bytes_per_step": hH.numel() * 4},
         "gpu_launches": per_step * args.steps if per_step is not None else None,
@@ -1164,6 +1219,42 @@ def reference_arm(args, world, rank):
                     "d2h_bytes_per_step": 0}}
 
 
+SECONDARY_KEYS = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "scaling",
+                  "config", "e2e", "roofline", "clocks", "gpu_launches", "cpu_baseline")
+
+
+def secondary_workloads(args, world, rank):
+    """The other configurations of the hot path, measured in the same run as the
+    GEMM headline: each workload with its own warm-up, device-timed steps (max
+    over ranks), clocks, roofline, end-to-end and (one GPU) CPU baseline on a
+    shorter sample.  Batch workloads are split over the ranks (strong scaling)."""
+    import copy
+    out = []
+    plan = [("scan", scan_workload, lambda: cpu_scan_rate(16, 4096, 1024, target_s=5.0)),
+            ("dtn", dtn_workload, lambda: cpu_dtn_rate(target_s=5.0)),
+            ("tsrn_attn", tsrn_attn_workload, lambda: cpu_tsrn_attn_rate(target_s=5.0)),
+            ("esn", esn_workload, lambda: cpu_esn_rate("gru", target_s=5.0)),
+            ("linear", linear_workload, lambda: cpu_linear_rate(target_s=3.0))]
+    for name, fn, cpu in plan:
+        sub = copy.copy(args)
+        sub.workload = name
+        sub.steps = max(3, min(args.steps, 10))
+        sub.warmup = max(3, min(args.warmup, 5))
+        sub.scaling = "strong"
+        sub.esn_mode = "gru"
+        torch.cuda.empty_cache()
+        r = fn(sub, world, rank)
+        torch.cuda.synchronize()
+        if rank == 0 and r is not None:
+            if world == 1 and not args.no_cpu_baseline:
+                r["cpu_baseline"] = cpu()
+            entry = {"workload": name}
+            entry.update({k: r[k] for k in SECONDARY_KEYS if k in r})
+            out.append(entry)
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     args = parse_args()
     world, rank, local = dist_setup()
@@ -1197,6 +1288,11 @@ def main():
                 res["cpu_baseline"] = cpu_esn_rate(args.esn_mode)
             else:
                 res["cpu_baseline"] = cpu_scan_rate(16, 4096, 1024)
+        if args.impl == "ours" and args.workload == "gemm" and not args.no_secondary \
+                and args.dtype == "f32" and args.size == 8192:
+            sec = secondary_workloads(args, world, rank)
+            if res is not None:
+                res["secondary"] = sec
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
     finally:

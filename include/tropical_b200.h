@@ -8,7 +8,11 @@
  *  - Sizes are int64_t element counts; strides are in ELEMENTS (not bytes).
  *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
  *    Every launch is asynchronous on that stream; no entry point synchronises
- *    the device or allocates device memory.
+ *    the device.  No entry point allocates device memory, with one exception:
+ *    the large fp32 forward's stream-K schedule (tp_set_stream_k) draws a
+ *    stream-ordered workspace of up to ~27 MB from a library-owned memory
+ *    pool that keeps its memory between calls; tp_set_stream_k(0) turns that
+ *    off (results are identical either way).
  *  - Every function returns int: 0 (TP_OK) on success, a negative TP_ERR_*
  *    value when host-side validation rejects the arguments (nothing is
  *    launched), or a positive cudaError_t value if a CUDA call failed.
@@ -240,8 +244,15 @@ TP_API int64_t tp_set_argmax_tma_min_terms(int64_t terms);
  * as CTAs; 3 = the k-aligned pieces (2 or 4 per tile, argmax kernel) whenever
  * K allows them, else as 2.  Tiles shared by CTAs are merged exactly (values
  * and argmax identical to the whole-tile schedule), using a stream-ordered
- * workspace from a library-owned pool.  Returns the previous mode;
- * process-wide.  (Tuning; no reference counterpart.) */
+ * workspace from a library-owned pool (skipped under stream capture).
+ * Co-residency: in the even split (mode 2, and mode 1 when it picks it) the
+ * CTA holding a tile's head chunks waits for the LATER CTA that computes its
+ * tail, so every CTA of the persistent grid (one per SM) must be resident at
+ * once -- true on a whole GPU, not under an SM partition (MPS thread
+ * percentage, green contexts).  There use mode 0 or 3 (k-aligned pieces wait
+ * only on pieces of earlier rounds).  A wait that cannot complete ends after
+ * the wait budget with TP_DEVERR_FLAG_TIMEOUT in tp_device_error().  Returns
+ * the previous mode; process-wide.  (Tuning; no reference counterpart.) */
 TP_API int tp_set_stream_k(int mode);
 
 /* Smooth (STE / LSE) backward: 1 (default) lets shapes that allow it form gx
@@ -412,8 +423,10 @@ TP_API int tp_scan_bwd(int64_t B, int64_t T, int64_t C,
  * Same arguments, results and validation as tp_scan_bwd, without the
  * workspace: the [B, C] partial sums behind ga live in one fixed array of this
  * library's device memory (1 MiB per GPU that loads the library, held until
- * the process exits).  Limit: when ga is requested, B*C <= 262144, else the
- * call returns TP_ERR_TOO_LARGE and launches nothing.  No allocation or free
+ * the process exits).  Limit: when ga is requested and T > 0, B*C <= 262144,
+ * else the call returns TP_ERR_TOO_LARGE (after the argument checks of
+ * tp_scan_bwd) and launches nothing.  The array's address is cached per
+ * device: do not call after cudaDeviceReset in the same process.  No allocation or free
  * happens in this call.  The first call on a device looks up that device's
  * array address (cudaGetSymbolAddress) -- make that first call outside any
  * stream capture.  Every entry of the array that a call reads it has written
@@ -471,11 +484,40 @@ TP_API void maxplus_matmul_cuda(const float* A, const float* B, float* C, int M,
 /* Status of the last reference-compatible call on this host thread. */
 TP_API int tp_last_error(void);
 
+/* ---- device-side failures ------------------------------------------------
+ * Every wait inside a kernel (TMA pipeline mbarriers, the reservoir's cluster
+ * exchange, the stream-K merge flags) is bounded by a budget of %globaltimer
+ * time.  A wait that runs out records a code in the device error word of its
+ * GPU and the kernel returns early (its outputs are then incomplete), so the
+ * context stays usable.  The word keeps the FIRST code recorded. */
+#define TP_DEVERR_BARRIER_TIMEOUT 1   /* an mbarrier wait ran out of budget  */
+#define TP_DEVERR_FLAG_TIMEOUT 2      /* a flag wait ran out of budget       */
+
 /* Device-side error word of the current device: 0 when no kernel reported a
- * problem, 1 when a bounded barrier wait ran out of time, 2 when a bounded
- * flag wait did.  Synchronises with the device (it reads device memory).
- * reset != 0 clears the word afterwards.  Returns -cudaError_t on failure. */
+ * problem, else a TP_DEVERR_* code.  Synchronises with the device (it reads
+ * device memory).  reset != 0 clears the word afterwards.  Returns
+ * -cudaError_t on failure.  The word's address is cached per device for the
+ * life of the process: do not call the library after cudaDeviceReset in the
+ * same process. */
 TP_API int tp_device_error(int reset);
+
+/* Budget of every bounded device-side wait on the current device, in ns of
+ * %globaltimer (default 2e9 = 2 s; accepted range [1e3, 6e10]).  Stores the
+ * previous budget in *previous when it is not NULL.  Synchronous (a copy to
+ * device memory): not during stream capture.  (No reference counterpart.) */
+#define TP_WAIT_BUDGET_MIN_NS 1000LL
+#define TP_WAIT_BUDGET_MAX_NS 60000000000LL
+TP_API int tp_set_wait_budget_ns(int64_t ns, int64_t* previous);
+
+/* Failure-path self-test: launches one single-warp kernel whose bounded wait
+ * can never complete -- kind 0: an mbarrier phase that receives one of its
+ * two arrivals; kind 1: the flag word at `flag` (device memory, caller keeps
+ * it 0), polled with the same acquire-load wait the stream-K merges use.
+ * After the wait budget the kernel records TP_DEVERR_BARRIER_TIMEOUT (kind 0)
+ * or TP_DEVERR_FLAG_TIMEOUT (kind 1) and returns; nothing faults or hangs.
+ * For tests of the error path (set a short budget first).  (No reference
+ * counterpart.) */
+TP_API int tp_selftest_bounded_wait(int kind, const unsigned* flag, void* stream);
 
 #ifdef __cplusplus
 }

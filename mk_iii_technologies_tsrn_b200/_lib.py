@@ -136,6 +136,8 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "tp_last_error": (_c_int, []),
     "tp_device_error": (_c_int, [_c_int]),
+    "tp_set_wait_budget_ns": (_c_int, [_c_i64, ctypes.POINTER(_c_i64)]),
+    "tp_selftest_bounded_wait": (_c_int, [_c_int, _c_p, _c_p]),
 }
 
 # status codes (include/tropical_b200.h)
@@ -145,6 +147,8 @@ TP_DTYPE_BF16 = 1
 TP_DTYPE_BF16_ARITH = 2
 TP_BWD_STE = 1
 TP_BWD_LSE = 2
+TP_DEVERR_BARRIER_TIMEOUT = 1
+TP_DEVERR_FLAG_TIMEOUT = 2
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

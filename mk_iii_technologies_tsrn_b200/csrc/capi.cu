@@ -10,7 +10,9 @@
 
 #include "maxplus_internal.cuh"
 
-__device__ int g_tp_device_error = 0;
+// One per GPU that loads the library: the device error word and the budget
+// of every bounded wait (TpDeviceStatus, common.cuh).
+__device__ TpDeviceStatus g_tp_status = {0, 0, TP_WAIT_BUDGET_NS};
 
 namespace tp {
 
@@ -59,8 +61,10 @@ int* device_error_ptr() {
   std::lock_guard<std::mutex> lock(mu);
   if (ptrs[dev] == nullptr) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_tp_device_error) == cudaSuccess) ptrs[dev] = (int*)p;
-    else cudaGetLastError();
+    if (cudaGetSymbolAddress(&p, g_tp_status) == cudaSuccess)
+      ptrs[dev] = &static_cast<TpDeviceStatus*>(p)->error;
+    else
+      cudaGetLastError();
   }
   return ptrs[dev];
 }
@@ -70,6 +74,50 @@ int num_sms() {
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   return n > 0 ? n : 148;
+}
+
+int check_scan_bwd_pointers(int64_t T, const float* gh, const float* bb, const float* xx,
+                            const float* a, const float* h0, const float* h,
+                            const uint32_t* win_mask, const float* gu, const float* ga,
+                            const float* gh0) {
+  TP_CHECK_PTR(a);
+  TP_CHECK_OPT_PTR(h0);
+  TP_CHECK_OPT_PTR(ga);
+  TP_CHECK_OPT_PTR(gh0);
+  if (T > 0) {
+    TP_CHECK_PTR(gh);
+    TP_CHECK_PTR(gu);
+    if (win_mask) {
+      TP_CHECK_PTR(win_mask);
+    } else {
+      TP_CHECK_PTR(bb);
+      TP_CHECK_OPT_PTR(xx);
+      TP_CHECK_PTR(h);
+    }
+  }
+  return TP_OK;
+}
+
+// One warp; lane 0 runs a bounded wait that nothing can satisfy (see
+// tp_selftest_bounded_wait).  The mbarrier expects two arrivals and gets one.
+__global__ void selftest_wait_kernel(int kind, const unsigned* flag, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  if (kind == 0) {
+    tp_mbar_init(&bar, 2);
+    tp_fence_mbar_init();
+    tp_mbar_arrive(&bar);
+    (void)tp_mbar_wait(&bar, 0u, err);
+  } else {
+    (void)tp_flag_wait(flag, err);
+  }
+}
+
+int launch_selftest_wait(int kind, const unsigned* flag, cudaStream_t stream) {
+  int* err = device_error_ptr();
+  if (err == nullptr) return TP_ERR_UNSUPPORTED;
+  selftest_wait_kernel<<<1, 32, 0, stream>>>(kind, flag, err);
+  return launch_status();
 }
 
 static void set_last_error(int s) { g_last_error = s; }
@@ -343,22 +391,9 @@ int tp_scan_bwd(int64_t B, int64_t T, int64_t C, const float* gh, const float* b
   TP_RETURN_IF(B < 0 || T < 0 || C < 0, TP_ERR_INVALID_ARG);
   if (B * C == 0) return TP_OK;
   TP_RETURN_IF(ga != nullptr && workspace == nullptr, TP_ERR_WORKSPACE);
-  TP_CHECK_PTR(a);
-  TP_CHECK_OPT_PTR(h0);
-  TP_CHECK_OPT_PTR(ga);
-  TP_CHECK_OPT_PTR(gh0);
+  const int s = tp::check_scan_bwd_pointers(T, gh, bb, xx, a, h0, h, win_mask, gu, ga, gh0);
+  if (s != TP_OK) return s;
   TP_CHECK_OPT_PTR(workspace);
-  if (T > 0) {
-    TP_CHECK_PTR(gh);
-    TP_CHECK_PTR(gu);
-    if (win_mask) {
-      TP_CHECK_PTR(win_mask);
-    } else {
-      TP_CHECK_PTR(bb);
-      TP_CHECK_OPT_PTR(xx);
-      TP_CHECK_PTR(h);
-    }
-  }
   ScanArgs p{};
   p.B = B; p.T = T; p.C = C;
   p.gh = gh; p.bb = bb; p.xx = win_mask ? nullptr : xx; p.a = a; p.h_init = h_init; p.h0 = h0;
@@ -615,14 +650,39 @@ int tp_last_error(void) { return last_error(); }
 
 int tp_device_error(int reset) {
   int v = 0;
-  cudaError_t e = cudaMemcpyFromSymbol(&v, g_tp_device_error, sizeof(int));
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_tp_status, sizeof(int), offsetof(TpDeviceStatus, error));
   if (e != cudaSuccess) return -(int)e;
   if (reset) {
     const int zero = 0;
-    e = cudaMemcpyToSymbol(g_tp_device_error, &zero, sizeof(int));
+    e = cudaMemcpyToSymbol(g_tp_status, &zero, sizeof(int), offsetof(TpDeviceStatus, error));
     if (e != cudaSuccess) return -(int)e;
   }
   return v;
+}
+
+int tp_set_wait_budget_ns(int64_t ns, int64_t* previous) {
+  TP_RETURN_IF(ns < TP_WAIT_BUDGET_MIN_NS || ns > TP_WAIT_BUDGET_MAX_NS, TP_ERR_INVALID_ARG);
+  unsigned long long old = 0;
+  const size_t off = offsetof(TpDeviceStatus, wait_budget_ns);
+  cudaError_t e = cudaMemcpyFromSymbol(&old, g_tp_status, sizeof(old), off);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_status(e);
+  }
+  const unsigned long long v = (unsigned long long)ns;
+  e = cudaMemcpyToSymbol(g_tp_status, &v, sizeof(v), off);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_status(e);
+  }
+  if (previous) *previous = (int64_t)old;
+  return TP_OK;
+}
+
+int tp_selftest_bounded_wait(int kind, const unsigned* flag, void* stream) {
+  TP_RETURN_IF(kind != 0 && kind != 1, TP_ERR_INVALID_ARG);
+  if (kind == 1) TP_CHECK_PTR(flag);
+  return tp::launch_selftest_wait(kind, flag, as_stream(stream));
 }
 
 }  // extern "C"

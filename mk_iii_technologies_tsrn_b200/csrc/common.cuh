@@ -18,12 +18,19 @@
 #include "tropical_b200.h"
 
 // ---------------------------------------------------------------------------
-// device error word (module-scope device memory, not a per-call allocation)
+// device status block (module-scope device memory, not a per-call allocation)
 // ---------------------------------------------------------------------------
-#define TP_DEVERR_BARRIER_TIMEOUT 1   // an mbarrier wait exceeded its budget
-#define TP_DEVERR_FLAG_TIMEOUT 2      // a flag wait exceeded its budget
+// Kernels that wait receive `int* err`, the address of `error` below; the
+// budget of every bounded wait is read from the same block, so the host can
+// change it at run time (tp_set_wait_budget_ns).  Error codes
+// TP_DEVERR_BARRIER_TIMEOUT / TP_DEVERR_FLAG_TIMEOUT are in tropical_b200.h.
+struct TpDeviceStatus {
+  int error;                          // 0, or the first TP_DEVERR_* recorded
+  int reserved;
+  unsigned long long wait_budget_ns;  // %globaltimer budget of one bounded wait
+};
 
-// Bounded-wait budget: 2 seconds of %globaltimer (ns).
+// Default bounded-wait budget: 2 seconds of %globaltimer (ns).
 #define TP_WAIT_BUDGET_NS 2000000000ull
 
 __device__ __forceinline__ uint64_t tp_globaltimer() {
@@ -34,6 +41,14 @@ __device__ __forceinline__ uint64_t tp_globaltimer() {
 
 __device__ __forceinline__ void tp_record_device_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
+}
+
+// The wait budget of the status block that `err` belongs to (read when a wait
+// first fails to complete, so the fast path never touches it).
+__device__ __forceinline__ uint64_t tp_wait_budget(const int* err) {
+  if (err == nullptr) return TP_WAIT_BUDGET_NS;
+  const TpDeviceStatus* st = reinterpret_cast<const TpDeviceStatus*>(err);
+  return *reinterpret_cast<const volatile unsigned long long*>(&st->wait_budget_ns);
 }
 
 // ---------------------------------------------------------------------------
@@ -157,16 +172,38 @@ __device__ __forceinline__ bool tp_mbar_try_wait(uint64_t* bar, uint32_t parity)
 __device__ __forceinline__ bool tp_mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (tp_mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = tp_globaltimer();
+  const uint64_t budget = tp_wait_budget(err);
   uint32_t polls = 0;
   while (!tp_mbar_try_wait(bar, parity)) {
     if (((++polls) & 255u) == 0u) {
-      if (tp_globaltimer() - t0 > TP_WAIT_BUDGET_NS) {
+      if (tp_globaltimer() - t0 > budget) {
         tp_record_device_error(err, TP_DEVERR_BARRIER_TIMEOUT);
         return false;
       }
     }
   }
   return true;
+}
+
+// Wait until the global flag word reads 1 (acquire load, GPU scope: the
+// writer releases it after storing the data it guards).  Returns false (and
+// records TP_DEVERR_FLAG_TIMEOUT) if the budget runs out.
+__device__ __forceinline__ bool tp_flag_wait(const unsigned* flag, int* err) {
+  uint64_t t0 = 0, budget = 0;
+  uint32_t polls = 0;
+  while (true) {
+    unsigned f;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(f) : "l"(flag) : "memory");
+    if (f == 1u) return true;
+    if (polls == 0) {
+      t0 = tp_globaltimer();
+      budget = tp_wait_budget(err);
+    }
+    if (((++polls) & 63u) == 0u && tp_globaltimer() - t0 > budget) {
+      tp_record_device_error(err, TP_DEVERR_FLAG_TIMEOUT);
+      return false;
+    }
+  }
 }
 
 // Asynchronous 16-byte global -> shared copy (L2 only); bytes past

@@ -182,6 +182,13 @@ struct ScanArgs {
 };
 int launch_scan_fwd(const ScanArgs& p, cudaStream_t stream);
 int launch_scan_bwd(const ScanArgs& p, cudaStream_t stream);
+// capi.cu: the pointer checks of tp_scan_bwd (shared with its allocation-free form)
+int check_scan_bwd_pointers(int64_t T, const float* gh, const float* bb, const float* xx,
+                            const float* a, const float* h0, const float* h,
+                            const uint32_t* win_mask, const float* gu, const float* ga,
+                            const float* gh0);
+// capi.cu: failure-path self-test (tp_selftest_bounded_wait)
+int launch_selftest_wait(int kind, const unsigned* flag, cudaStream_t stream);
 
 // probe.cu
 int launch_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters, float* sink,

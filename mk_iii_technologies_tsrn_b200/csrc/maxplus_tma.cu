@@ -623,24 +623,9 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
       // (or a NaN where the lower has none), so ties keep the lowest k.
       const int64_t slot0 = (int64_t)(tile - (int)sch_dp * G) * (p.sk_split - 1);
       if (t == 0) {
-        const uint64_t t0 = tp_globaltimer();
-        uint32_t polls = 0;
         int ok = 1;
-        for (int sp = 0; ok && sp < p.sk_split - 1; ++sp) {
-          while (true) {
-            unsigned f;
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];"
-                         : "=r"(f)
-                         : "l"(p.sk_flag + slot0 + sp)
-                         : "memory");
-            if (f == 1u) break;
-            if (((++polls) & 63u) == 0u && tp_globaltimer() - t0 > TP_WAIT_BUDGET_NS) {
-              tp_record_device_error(p.err, TP_DEVERR_FLAG_TIMEOUT);
-              ok = 0;
-              break;
-            }
-          }
-        }
+        for (int sp = 0; ok && sp < p.sk_split - 1; ++sp)
+          ok = tp_flag_wait(p.sk_flag + slot0 + sp, p.err) ? 1 : 0;
         sk_ok = ok;
       }
       if (!compute_sync() || !sk_ok) return;
@@ -694,23 +679,7 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
       // ---- stream-K head piece (the CTA's last segment): wait for the tail's
       // partials, then merge.  The tail wins only with a strictly larger max
       // (or a NaN where the head has none): ties keep the head's lower k.
-      if (t == 0) {
-        const uint64_t t0 = tp_globaltimer();
-        uint32_t polls = 0;
-        int ok = 1;
-        while (true) {
-          unsigned f;
-          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(f) : "l"(p.sk_flag + cta)
-                       : "memory");
-          if (f == 1u) break;
-          if (((++polls) & 63u) == 0u && tp_globaltimer() - t0 > TP_WAIT_BUDGET_NS) {
-            tp_record_device_error(p.err, TP_DEVERR_FLAG_TIMEOUT);
-            ok = 0;
-            break;
-          }
-        }
-        sk_ok = ok;
-      }
+      if (t == 0) sk_ok = tp_flag_wait(p.sk_flag + cta, p.err) ? 1 : 0;
       if (!compute_sync() || !sk_ok) return;
       const float* wm = p.sk_max + (int64_t)cta * C::OUTS * CT;
       const int32_t* wc = p.sk_cid + (int64_t)cta * C::OUTS * CT;

@@ -384,13 +384,19 @@ int scan_scratch_address(float** out) {
   static float* addr[64] = {nullptr};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return (int)e;
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return tp::cuda_status(e);
+  }
   if (dev < 0 || dev >= 64) return TP_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lock(mu);
   if (addr[dev] == nullptr) {
     void* ptr = nullptr;
     e = cudaGetSymbolAddress(&ptr, g_scan_ga_scratch);
-    if (e != cudaSuccess) return (int)e;
+    if (e != cudaSuccess) {
+      cudaGetLastError();  // do not leave the error for an unrelated later call
+      return tp::cuda_status(e);
+    }
     addr[dev] = static_cast<float*>(ptr);
   }
   *out = addr[dev];
@@ -406,7 +412,13 @@ extern "C" int tp_scan_bwd_noalloc(int64_t B, int64_t T, int64_t C, const float*
                                    void* stream) {
   float* ws = nullptr;
   if (ga != nullptr && B > 0 && C > 0) {
-    if (B > kScanNoAllocMaxLanes / C) return TP_ERR_TOO_LARGE;
+    // tp_scan_bwd's own argument checks come first, so a call that is wrong in
+    // several ways reports what tp_scan_bwd would
+    if (T < 0) return TP_ERR_INVALID_ARG;
+    const int chk = tp::check_scan_bwd_pointers(T, gh, bb, xx, a, h0, h, win_mask, gu, ga, gh0);
+    if (chk != TP_OK) return chk;
+    // with T == 0 the backward only zeroes ga and gh0: the array is not used
+    if (T > 0 && B > kScanNoAllocMaxLanes / C) return TP_ERR_TOO_LARGE;
     const int s = scan_scratch_address(&ws);
     if (s != TP_OK) return s;
   }

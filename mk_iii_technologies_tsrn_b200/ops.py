@@ -50,6 +50,54 @@ def _require_cuda(*tensors: Optional[torch.Tensor]) -> torch.device:
     return dev
 
 
+class DeviceWaitTimeout(RuntimeError):
+    """A bounded wait inside a kernel ran out of its budget: that kernel returned
+    early and its outputs (and those of later kernels that read them) are
+    incomplete."""
+
+    def __init__(self, code: int, device):
+        what = {_lib.TP_DEVERR_BARRIER_TIMEOUT: "an mbarrier wait (TMA pipeline or cluster "
+                                                "exchange)",
+                _lib.TP_DEVERR_FLAG_TIMEOUT: "a flag wait (stream-K partials)"}.get(
+                    code, f"device error code {code}")
+        super().__init__(f"{what} on {device} ran out of its wait budget; the kernel "
+                         "returned early and its results are incomplete")
+        self.code = code
+
+
+def check_device_error(device=None, reset: bool = True) -> None:
+    """Raise :class:`DeviceWaitTimeout` if a kernel on ``device`` (default: the
+    current CUDA device) recorded a timed-out wait since the last reset.
+
+    Synchronises with the device.  The library's kernels never hang: a wait that
+    cannot complete ends after the budget (:func:`set_wait_budget`) and leaves a
+    code here, which this call turns into an exception (and clears, unless
+    ``reset`` is False)."""
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None \
+        else torch.device(device)
+    with torch.cuda.device(dev):
+        code = lib.tp_device_error(1 if reset else 0)
+    if code < 0:
+        raise _lib.TropicalLibraryError("tp_device_error", -code, f"CUDA error {-code}")
+    if code:
+        raise DeviceWaitTimeout(code, dev)
+
+
+def set_wait_budget(seconds: float, device=None) -> float:
+    """Set the budget of every bounded device-side wait on ``device`` (default
+    2 s) and return the previous one, in seconds.  Synchronous; not during
+    stream capture."""
+    lib = _lib.load()
+    prev = ctypes.c_int64(0)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None \
+        else torch.device(device)
+    with torch.cuda.device(dev):
+        st = lib.tp_set_wait_budget_ns(int(round(seconds * 1e9)), ctypes.byref(prev))
+    _lib.check(st, "tp_set_wait_budget_ns")
+    return prev.value / 1e9
+
+
 def _ptr(t: Optional[torch.Tensor]):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
@@ -176,6 +224,26 @@ def maxplus(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = Non
     if x.dim() != 2 or w.dim() != 2:
         raise ValueError("maxplus takes x [M,K] and w [N,K]")
     return maxplus_strided(x, w, bias, argmax=argmax, arith=arith)
+
+
+def maxplus_matmul(A: torch.Tensor, B: torch.Tensor, *, argmax: bool = False):
+    """Max-plus matrix product ``C[i,j] = max_k(A[i,k] + B[k,j])`` with B stored
+    [K, N] -- the layout of ``_tropical_matmul`` (benchmarks/synthetic_scheduling.py:35-38)
+    and of ``maxplus_matmul_kernel`` (cuda/maxplus_gemm.cu:269-290).
+
+    Returns C [M, N] fp32 (and the lowest maximising k as int32 when ``argmax``).
+    Large products copy B once into the [N, K] layout (N*K elements against
+    M*N*K terms) and run the TMA kernel; small ones read B in place through the
+    strided kernel.  Values are identical either way."""
+    if A.dim() != 2 or B.dim() != 2 or A.shape[1] != B.shape[0]:
+        raise ValueError(f"maxplus_matmul takes A [M,K] and B [K,N], got {tuple(A.shape)} "
+                         f"and {tuple(B.shape)}")
+    Bt = B.t()                                     # [N, K] view, k stride N
+    if _widen_pays(A, Bt) and A.dtype == torch.float32:
+        Bt = Bt.contiguous()
+        A = A.contiguous()
+    y, am = maxplus_strided(A, Bt, argmax=argmax)
+    return (y, am) if argmax else y
 
 
 def maxplus_host(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,

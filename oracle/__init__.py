@@ -17,6 +17,8 @@ reference's hand-computed known-answer test (``cuda/test_kernel.py:117-136``).
 from .maxplus import (  # noqa: F401
     maxplus_fwd,
     maxplus_fwd_bf16,
+    maxplus_matmul,
+    tropical_power_chain,
     round_bf16,
     tsrn_attention_fwd,
     lfdual_act,

@@ -54,6 +54,24 @@ def maxplus_fwd(x: np.ndarray, w: np.ndarray, bias: np.ndarray | None = None,
     return y, idx
 
 
+def maxplus_matmul(A: np.ndarray, B: np.ndarray):
+    """C[i,j] = max_k(A[i,k] + B[k,j]) with B stored [K, N], and the lowest
+    maximising k -- ``_tropical_matmul`` (benchmarks/synthetic_scheduling.py:35-38:
+    ``(A[:, :, None] + B[None, :, :]).max(axis=1)``).  Each term is one float32
+    add (commutative), so this is maxplus_fwd with w = B transposed."""
+    return maxplus_fwd(np.asarray(A, np.float32), np.ascontiguousarray(np.asarray(B, np.float32).T))
+
+
+def tropical_power_chain(A: np.ndarray, steps: int):
+    """A^(steps+1) by repeated right-multiplication ``Ak = Ak (x) A`` -- the loop of
+    ``_tropical_eigenvalue`` (benchmarks/synthetic_scheduling.py:41-55) -- and the
+    eigenvalue estimate max_i Ak[i,i] / (steps + 1) that it returns."""
+    Ak = np.asarray(A, np.float32).copy()
+    for _ in range(steps):
+        Ak, _ = maxplus_matmul(Ak, A)
+    return Ak, float(np.diag(Ak).max() / (steps + 1))
+
+
 def round_bf16(a: np.ndarray) -> np.ndarray:
     """Round float32 values to the nearest bfloat16 (ties to even), returned as
     float32; NaN stays NaN, overflow goes to +-inf."""

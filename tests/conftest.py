@@ -27,11 +27,17 @@ def golden():
 
 @pytest.fixture
 def cuda():
+    """cuda:0 with the library loaded; after the test, no kernel may have left a
+    timed-out wait in the device error word (a wait that ran out means some
+    kernel returned early, so the test's results cannot be trusted)."""
     import torch
 
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
-    from mk_iii_technologies_tsrn_b200 import _lib
+    from mk_iii_technologies_tsrn_b200 import _lib, ops
 
     _lib.load()  # fails loudly if the library is missing
-    return torch.device("cuda:0")
+    dev = torch.device("cuda:0")
+    ops.check_device_error(dev)   # start clean
+    yield dev
+    ops.check_device_error(dev)

@@ -95,3 +95,30 @@ def test_workspace_size():
     # [16][64][128]
     assert lib.tp_maxplus_bwd_smooth_workspace_bytes(1, 64, 4096, 128) == \
         (6 * 64 * 4096 + 16 * 64 * 128) * 4
+
+
+def test_failure_entry_points_validate_on_the_host():
+    from mk_iii_technologies_tsrn_b200 import _lib
+    lib = _lib.load()
+    prev = ctypes.c_int64(0)
+    # out-of-range budgets and self-test kinds are rejected before any CUDA call
+    assert lib.tp_set_wait_budget_ns(0, ctypes.byref(prev)) == -1
+    assert lib.tp_set_wait_budget_ns(-5, None) == -1
+    assert lib.tp_set_wait_budget_ns(10 ** 11, None) == -1
+    assert lib.tp_selftest_bounded_wait(2, None, None) == -1
+    assert lib.tp_selftest_bounded_wait(1, None, None) == -2   # kind 1 needs its flag word
+
+
+def test_noalloc_checks_arguments_before_its_limit():
+    from mk_iii_technologies_tsrn_b200 import _lib
+    lib = _lib.load()
+    big_c = 262144 // 2 + 32          # B*C over the array's limit at B = 2
+    # NULL required pointers (here `a`) are reported as tp_scan_bwd reports
+    # them, although ga is requested and B*C is over the limit; the checks stop
+    # at the NULL before touching the (fake, never dereferenced) ga address
+    fake_ga = ctypes.c_void_p(4096)
+    assert lib.tp_scan_bwd_noalloc(2, 4, big_c, None, None, None, None, 0.0, None, None, None,
+                                   None, fake_ga, None, None) == -2
+    # negative sizes
+    assert lib.tp_scan_bwd_noalloc(2, -1, 4, None, None, None, None, 0.0, None, None, None,
+                                   None, None, None, None) == -1

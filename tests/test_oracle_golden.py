@@ -18,6 +18,37 @@ def test_kat_2x2():
     np.testing.assert_array_equal(idx, g["idx"])
 
 
+def test_kat_2x2_matmul_oracle():
+    # the same KAT through the A (x) B restatement (B stored [K, N])
+    g = load_golden("kat_2x2")
+    y, idx = oracle.maxplus_matmul(g["A"], g["B"])
+    np.testing.assert_array_equal(y, g["expected"])
+    np.testing.assert_array_equal(idx, g["idx"])
+    # the eigenvalue iteration on the KAT matrix, against a direct loop
+    Ak, lam = oracle.tropical_power_chain(g["A"], 3)
+    direct = g["A"].astype(np.float32)
+    for _ in range(3):
+        direct = (direct[:, :, None] + g["A"][None, :, :]).max(axis=1)
+    np.testing.assert_array_equal(Ak, direct)
+    assert lam == float(np.diag(direct).max() / 4)
+
+
+def test_bf16_checkers_agree():
+    # the large-size bf16 checker (the reference expression run by torch on
+    # bf16 tensors, oracle.torch_ref) agrees with the numpy restatement, which
+    # the reference fixtures pin
+    import torch
+    from oracle.torch_ref import maxplus_fwd_torch
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((24, 700)) * 3).astype(np.float32)
+    w = (rng.standard_normal((300, 700)) * 3).astype(np.float32)
+    w[rng.random(w.shape) < 0.05] = -np.inf
+    ry, ri = oracle.maxplus_fwd_bf16(x, w)
+    tv, ti = maxplus_fwd_torch(torch.tensor(x).bfloat16(), torch.tensor(w).bfloat16())
+    np.testing.assert_array_equal(tv.float().numpy(), ry)
+    np.testing.assert_array_equal(ti.numpy(), ri)
+
+
 @pytest.mark.parametrize("name", ["linear_seed42", "linear_gauss", "linear_ties",
                                   "linear_neginf", "linear_nan"])
 def test_forward_bit_exact(name):

@@ -53,9 +53,10 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda, use_mask):
     from mk_iii_technologies_tsrn_b200 import _lib, ops
     lib = _lib.load()
     stream = ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
-    # two calls in a row with different shapes: the second must not see the
-    # first call's leftovers in the shared array
-    for seed, (B, T, C) in enumerate([(6, 300, 96), (3, 129, 40)]):
+    # calls in a row with different shapes: each must not see the previous
+    # call's leftovers in the shared array.  C % 4 == 0 runs the TMA backward
+    # kernel, C = 33 the plain-load kernel; both write the array.
+    for seed, (B, T, C) in enumerate([(6, 300, 96), (3, 129, 40), (5, 77, 33)]):
         a, b, x, gh, h0 = _inputs(B, T, C, seed, cuda)
         h, mask = ops.scan_forward(b, x, a, 0.0, h0, need_mask=True)
         kw = (None, None, None, mask) if use_mask else (b, x, h, None)
