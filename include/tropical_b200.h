@@ -413,6 +413,39 @@ TP_API int tp_scan_bwd(int64_t B, int64_t T, int64_t C,
                 float* gu, float* ga, float* gh0,
                 float* workspace, void* stream);
 
+/* ---- chunk-parallel scan --------------------------------------------------
+ * The same recurrence for shapes whose B * C lanes cannot fill the GPU (the
+ * kernels above run one warp per 32 channels of a batch row: B=2, C=1024 is
+ * 64 warps): time is cut into chunks of `chunk` steps (a multiple of 32; 0 =
+ * the library's choice, tp_scan_chunk_length) that run in parallel.  The
+ * forward computes each chunk from -inf, then every chunk's exact starting
+ * state (the carry through a chunk is `chunk` rounded adds of a, combined
+ * with the chunk's own result by a max; rounding is monotone, so the two
+ * separate exactly), then reruns every chunk from it: h and win_mask are
+ * BIT-EXACT with tp_scan_fwd.  The backward likewise finds the exact
+ * gradient entering every chunk, so gu and gh0 are bit-exact with
+ * tp_scan_bwd; ga sums per-chunk partials (ascending batch, descending
+ * chunk), which agrees with tp_scan_bwd's single running sum to rounding.
+ * Caller-owned workspace of tp_scan_chunked_workspace_bytes(B, T, C, chunk)
+ * bytes, 256-byte aligned (TP_ERR_WORKSPACE / TP_ERR_MISALIGNED otherwise).
+ * Reference: research/tsrn_dml.py:961-972 evaluates the scan in parallel over
+ * T through a closed form (t*A + cummax), whose rounding differs from the
+ * recurrence; this mode is parallel over T without that difference. */
+TP_API int64_t tp_scan_chunked_workspace_bytes(int64_t B, int64_t T, int64_t C, int chunk);
+TP_API int tp_scan_chunk_length(int64_t B, int64_t T, int64_t C);
+TP_API int tp_scan_fwd_chunked(int64_t B, int64_t T, int64_t C,
+                               const float* bb, const float* xx, const float* a,
+                               float h_init, const float* h0,
+                               float* h, uint32_t* win_mask, int chunk,
+                               void* workspace, int64_t workspace_bytes, void* stream);
+TP_API int tp_scan_bwd_chunked(int64_t B, int64_t T, int64_t C,
+                               const float* gh,
+                               const float* bb, const float* xx, const float* a,
+                               float h_init, const float* h0, const float* h,
+                               const uint32_t* win_mask,
+                               float* gu, float* ga, float* gh0, int chunk,
+                               void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Allocation-free form of tp_scan_bwd, for callers that cannot allocate
  * device memory themselves: a thin FFI binding that only forwards pointers of
  * buffers some other runtime already owns, or a process whose device memory

@@ -93,6 +93,18 @@ SIGNATURES: dict[str, tuple] = {
         [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
          _c_p],
     ),
+    "tp_scan_chunked_workspace_bytes": (_c_i64, [_c_i64, _c_i64, _c_i64, _c_int]),
+    "tp_scan_chunk_length": (_c_int, [_c_i64, _c_i64, _c_i64]),
+    "tp_scan_fwd_chunked": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_f, _c_p, _c_p, _c_p, _c_int, _c_p, _c_i64,
+         _c_p],
+    ),
+    "tp_scan_bwd_chunked": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
+         _c_int, _c_p, _c_i64, _c_p],
+    ),
     "tp_convert_bf16_to_f32": (_c_int, [_c_i64, _c_p, _c_p, _c_p]),
     "tp_probe_addmax": (_c_int, [_c_int, _c_i64, _c_i64, _c_i64, _c_p, _c_p]),
     "maxplus_forward_cuda": (None, [_c_p, _c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_bool]),

@@ -402,6 +402,56 @@ int tp_scan_bwd(int64_t B, int64_t T, int64_t C, const float* gh, const float* b
   return launch_scan_bwd(p, as_stream(stream));
 }
 
+int64_t tp_scan_chunked_workspace_bytes(int64_t B, int64_t T, int64_t C, int chunk) {
+  if (B < 0 || T < 0 || C < 0 || chunk < 0 || chunk % 32 != 0) return -1;
+  return tp::scan_chunked_workspace_bytes(B, T, C, chunk);
+}
+
+int tp_scan_chunk_length(int64_t B, int64_t T, int64_t C) {
+  TP_RETURN_IF(B < 0 || T < 0 || C < 0, TP_ERR_INVALID_ARG);
+  return tp::scan_chunk_pick(B, T, C);
+}
+
+int tp_scan_fwd_chunked(int64_t B, int64_t T, int64_t C, const float* bb, const float* xx,
+                        const float* a, float h_init, const float* h0, float* h,
+                        uint32_t* win_mask, int chunk, void* workspace, int64_t workspace_bytes,
+                        void* stream) {
+  TP_RETURN_IF(B < 0 || T < 0 || C < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(chunk < 0 || chunk % 32 != 0, TP_ERR_INVALID_ARG);
+  if (B * T * C == 0) return TP_OK;
+  TP_RETURN_IF(C > (int64_t)INT32_MAX || ceil_div(T, 32) > (int64_t)INT32_MAX, TP_ERR_TOO_LARGE);
+  TP_CHECK_PTR(bb);
+  TP_CHECK_OPT_PTR(xx);
+  TP_CHECK_PTR(a);
+  TP_CHECK_OPT_PTR(h0);
+  TP_CHECK_PTR(h);
+  TP_CHECK_OPT_PTR(win_mask);
+  TP_CHECK_PTR(workspace);
+  ScanArgs p{};
+  p.B = B; p.T = T; p.C = C;
+  p.bb = bb; p.xx = xx; p.a = a; p.h_init = h_init; p.h0 = h0; p.h = h; p.win = win_mask;
+  return launch_scan_fwd_chunked(p, chunk, workspace, workspace_bytes, as_stream(stream));
+}
+
+int tp_scan_bwd_chunked(int64_t B, int64_t T, int64_t C, const float* gh, const float* bb,
+                        const float* xx, const float* a, float h_init, const float* h0,
+                        const float* h, const uint32_t* win_mask, float* gu, float* ga,
+                        float* gh0, int chunk, void* workspace, int64_t workspace_bytes,
+                        void* stream) {
+  TP_RETURN_IF(B < 0 || T < 0 || C < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(chunk < 0 || chunk % 32 != 0, TP_ERR_INVALID_ARG);
+  if (B * C == 0) return TP_OK;
+  TP_RETURN_IF(C > (int64_t)INT32_MAX || ceil_div(T, 32) > (int64_t)INT32_MAX, TP_ERR_TOO_LARGE);
+  const int s = tp::check_scan_bwd_pointers(T, gh, bb, xx, a, h0, h, win_mask, gu, ga, gh0);
+  if (s != TP_OK) return s;
+  if (T > 0) TP_CHECK_PTR(workspace);
+  ScanArgs p{};
+  p.B = B; p.T = T; p.C = C;
+  p.gh = gh; p.bb = bb; p.xx = win_mask ? nullptr : xx; p.a = a; p.h_init = h_init; p.h0 = h0;
+  p.h = const_cast<float*>(h); p.win_in = win_mask; p.gu = gu; p.ga = ga; p.gh0 = gh0;
+  return launch_scan_bwd_chunked(p, chunk, workspace, workspace_bytes, as_stream(stream));
+}
+
 int tp_convert_bf16_to_f32(int64_t n, const void* src, float* dst, void* stream) {
   TP_RETURN_IF(n < 0, TP_ERR_INVALID_ARG);
   if (n == 0) return TP_OK;

@@ -182,6 +182,13 @@ struct ScanArgs {
 };
 int launch_scan_fwd(const ScanArgs& p, cudaStream_t stream);
 int launch_scan_bwd(const ScanArgs& p, cudaStream_t stream);
+// scan_chunked.cu: chunk-parallel scan (workspace from the caller)
+int scan_chunk_pick(int64_t B, int64_t T, int64_t C);
+int64_t scan_chunked_workspace_bytes(int64_t B, int64_t T, int64_t C, int chunk);
+int launch_scan_fwd_chunked(const ScanArgs& p, int chunk, void* ws, int64_t ws_bytes,
+                            cudaStream_t stream);
+int launch_scan_bwd_chunked(const ScanArgs& p, int chunk, void* ws, int64_t ws_bytes,
+                            cudaStream_t stream);
 // capi.cu: the pointer checks of tp_scan_bwd (shared with its allocation-free form)
 int check_scan_bwd_pointers(int64_t T, const float* gh, const float* bb, const float* xx,
                             const float* a, const float* h0, const float* h,

@@ -1,0 +1,594 @@
+// scan_chunked.cu -- chunk-parallel evaluation of the tropical SSM scan
+// (research/tsrn_dml.py:917-980, TropicalSSM) for shapes whose (batch x
+// channel) lanes cannot fill the GPU: the sequential kernels of scan.cu run
+// one warp per 32 channels of a batch row, so B=2, C=1024 (config 3's batch
+// split over 8 GPUs) gives 64 warps for 148 SMs.  Here time is cut into
+// chunks of L steps (a multiple of 32) and each (batch, chunk, 4 channels)
+// is one thread, so the lanes multiply by T / L.
+//
+// Forward, bit-exact with the sequential recurrence h_t = (u_t >= a + h_{t-1})
+// ? u_t : fl(a + h_{t-1}):
+//   1. beta: every chunk runs the recurrence from h = -inf (its own inputs
+//      only) and keeps its last state beta_j.
+//   2. carry: one thread per (b, c) walks the chunks in order.  The state
+//      after chunk j from any start h is max(chain_L(h), beta_j), where
+//      chain_L is L rounded additions of a (rounding is monotone, so
+//      fl(a + max(p, q)) = max(fl(a+p), fl(a+q)) and the carry and the
+//      chunk's own winners separate).  Which side wins decides the bits: a
+//      carry that never loses gives chain_L(h) exactly, a carry that loses
+//      once gives beta_j exactly (from the step it loses, the run equals the
+//      chunk's own run).  A rounding-error bound on chain_L settles most
+//      chunks without the L dependent adds; an exact tie at zero (where +0
+//      and -0 differ) replays the chunk.  The walk writes each chunk's
+//      exact starting state.
+//   3. output: every chunk reruns the recurrence from its exact starting
+//      state and writes h and the win-mask words -- the same bits as the
+//      sequential kernel.
+// Backward (G_t = g_t + carry_{t+1}; gu_t = win ? G : 0; carry_t = win ? 0 : G):
+//   A. summary: every chunk runs its reverse walk from carry 0 and keeps the
+//      carry leaving its first step, and whether any input won in it.  A
+//      chunk with a winner sends the same carry whatever enters it.
+//   B. carry: one thread per (b, c) walks the chunks backwards; a chunk with
+//      no winner passes the entering carry through its L rounded adds of g
+//      (in order, exact).  gh0 is the carry leaving chunk 0.
+//   C. output: every chunk reruns its reverse walk from its exact entering
+//      carry and writes gu -- bit-exact -- and its partial sum of the lost
+//      gradients; ga sums the partials (ascending batch, descending chunk),
+//      an order that differs from one sequential sum over T: ga agrees with
+//      the sequential kernel to rounding, gu and gh0 bit for bit.
+//
+// Memory: pass 1 reads b, x once and pass 3 reads them again; between the
+// two they stay in L2 when B*T*C is small (the case this mode exists for:
+// 2 x 32 MiB at B=2).  Loads are 128-bit across 4 channels (C % 4 == 0 and
+// 16-byte aligned tensors; otherwise one channel per thread).
+#include <math.h>
+
+#include "maxplus_internal.cuh"
+
+namespace tp {
+
+namespace {
+
+constexpr int kRowBlock = 8;     // rows whose loads are issued together
+
+struct ChunkArgs {
+  int64_t B, T, C;
+  int L, nch, nw;                 // chunk length, chunks, mask words per row
+  const float* bb;
+  const float* xx;                // may be null (u = bb)
+  const float* a;
+  float h_init;
+  const float* h0;                // [B, C] or null
+  // forward
+  float* h;
+  uint32_t* win;                  // [B, nw, C] or null
+  // backward
+  const float* gh;
+  const float* hin;               // forward states (recompute path)
+  const uint32_t* win_in;         // or the forward's mask
+  float* gu;
+  float* ga;
+  float* gh0;
+  // workspace planes, [B][nch][C] each
+  float* beta;
+  float* hs;
+  float* cout;
+  float* cin;
+  float* gap;
+  uint8_t* tflag;
+};
+
+template <int V>
+__device__ __forceinline__ void ldv(float (&d)[V], const float* p) {
+  if constexpr (V == 4) {
+    const float4 t = __ldg(reinterpret_cast<const float4*>(p));
+    d[0] = t.x; d[1] = t.y; d[2] = t.z; d[3] = t.w;
+  } else {
+    d[0] = __ldg(p);
+  }
+}
+
+// last use of an input: evict-first loads
+template <int V>
+__device__ __forceinline__ void ldv_last(float (&d)[V], const float* p) {
+  if constexpr (V == 4) {
+    const float4 t = __ldcs(reinterpret_cast<const float4*>(p));
+    d[0] = t.x; d[1] = t.y; d[2] = t.z; d[3] = t.w;
+  } else {
+    d[0] = __ldcs(p);
+  }
+}
+
+template <int V>
+__device__ __forceinline__ void stv(float* p, const float (&s)[V]) {
+  if constexpr (V == 4) {
+    *reinterpret_cast<float4*>(p) = make_float4(s[0], s[1], s[2], s[3]);
+  } else {
+    p[0] = s[0];
+  }
+}
+
+template <int V>
+__device__ __forceinline__ void stv_stream(float* p, const float (&s)[V]) {
+  if constexpr (V == 4) {
+    __stcs(reinterpret_cast<float4*>(p), make_float4(s[0], s[1], s[2], s[3]));
+  } else {
+    __stcs(p, s[0]);
+  }
+}
+
+template <int V>
+__device__ __forceinline__ void stw(uint32_t* p, const uint32_t (&s)[V]) {
+  if constexpr (V == 4) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(s[0], s[1], s[2], s[3]);
+  } else {
+    p[0] = s[0];
+  }
+}
+
+template <int V>
+__device__ __forceinline__ void ldw(uint32_t (&d)[V], const uint32_t* p) {
+  if constexpr (V == 4) {
+    const uint4 t = __ldg(reinterpret_cast<const uint4*>(p));
+    d[0] = t.x; d[1] = t.y; d[2] = t.z; d[3] = t.w;
+  } else {
+    d[0] = __ldg(p);
+  }
+}
+
+// one step of the recurrence, exactly as scan.cu evaluates it
+__device__ __forceinline__ bool fwd_step(float& h, float a, float u) {
+  const float d = a + h;
+  const bool win = u >= d;
+  h = win ? u : d;
+  return win;
+}
+
+// thread -> (b, chunk j, first channel c) of the chunk-parallel passes
+struct Slot {
+  int64_t b, c;
+  int j, rows;
+  int64_t t0;
+};
+
+template <int V>
+__device__ __forceinline__ bool slot_of(const ChunkArgs& p, Slot& s) {
+  const int64_t nq = p.C / V;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= p.B * p.nch * nq) return false;
+  const int64_t q = idx % nq;
+  const int64_t r = idx / nq;
+  s.j = (int)(r % p.nch);
+  s.b = r / p.nch;
+  s.c = q * V;
+  s.t0 = (int64_t)s.j * p.L;
+  s.rows = (int)((p.T - s.t0) < p.L ? (p.T - s.t0) : p.L);
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// forward pass 1 (kOut = false: chunk state from -inf into beta) and pass 3
+// (kOut = true: from the exact starting state, writing h and the mask)
+// ---------------------------------------------------------------------------
+template <int V, bool kHasX, bool kOut, bool kMask>
+__global__ void __launch_bounds__(256) chunk_fwd_kernel(const ChunkArgs p) {
+  Slot s;
+  if (!slot_of<V>(p, s)) return;
+  const int64_t o = (s.b * p.nch + s.j) * p.C + s.c;
+  float a[V], h[V];
+  ldv<V>(a, p.a + s.c);
+  if (kOut) {
+    ldv<V>(h, p.hs + o);
+  } else {
+#pragma unroll
+    for (int v = 0; v < V; ++v) h[v] = -INFINITY;
+  }
+  const int64_t base = (s.b * p.T + s.t0) * p.C + s.c;
+  const float* pb = p.bb + base;
+  const float* px = kHasX ? p.xx + base : nullptr;
+  float* ph = kOut ? p.h + base : nullptr;
+  uint32_t bits[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) bits[v] = 0u;
+  int t = 0;
+  for (; t + kRowBlock <= s.rows; t += kRowBlock) {
+    float u[kRowBlock][V];
+#pragma unroll
+    for (int k = 0; k < kRowBlock; ++k) {
+      const int64_t off = (int64_t)(t + k) * p.C;
+      if (kOut) ldv_last<V>(u[k], pb + off); else ldv<V>(u[k], pb + off);
+      if (kHasX) {
+        float xv[V];
+        if (kOut) ldv_last<V>(xv, px + off); else ldv<V>(xv, px + off);
+#pragma unroll
+        for (int v = 0; v < V; ++v) u[k][v] = u[k][v] + xv[v];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kRowBlock; ++k) {
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const bool w = fwd_step(h[v], a[v], u[k][v]);
+        if (kMask) bits[v] |= (uint32_t)w << ((t + k) & 31);
+      }
+      if (kOut) stv_stream<V>(ph + (int64_t)(t + k) * p.C, h);
+    }
+    if (kMask && ((t + kRowBlock) & 31) == 0) {
+      stw<V>(p.win + (s.b * p.nw + (s.t0 + t) / 32) * p.C + s.c, bits);
+#pragma unroll
+      for (int v = 0; v < V; ++v) bits[v] = 0u;
+    }
+  }
+  for (; t < s.rows; ++t) {
+    const int64_t off = (int64_t)t * p.C;
+    float u[V];
+    if (kOut) ldv_last<V>(u, pb + off); else ldv<V>(u, pb + off);
+    if (kHasX) {
+      float xv[V];
+      if (kOut) ldv_last<V>(xv, px + off); else ldv<V>(xv, px + off);
+#pragma unroll
+      for (int v = 0; v < V; ++v) u[v] = u[v] + xv[v];
+    }
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const bool w = fwd_step(h[v], a[v], u[v]);
+      if (kMask) bits[v] |= (uint32_t)w << (t & 31);
+    }
+    if (kOut) stv_stream<V>(ph + off, h);
+  }
+  if (kMask && (s.rows & 31) != 0)   // the last, partial word of the sequence
+    stw<V>(p.win + (s.b * p.nw + (s.t0 + s.rows - 1) / 32) * p.C + s.c, bits);
+  if (!kOut) stv<V>(p.beta + o, h);
+}
+
+// state after a chunk of `rows` steps entered with h, given the chunk's own
+// state from -inf (beta); exact (see the file comment).
+__device__ float chunk_compose(float h, float beta, float a, int rows, const ChunkArgs& p,
+                               int64_t b, int64_t c, int64_t t0) {
+  if (beta != beta) return beta;          // NaN inside the chunk whatever enters
+  if (h != h) return h;                   // a NaN state stays NaN
+  if (h == -INFINITY) return beta;
+  if (isfinite(a) && isfinite(h) && !(beta == INFINITY)) {
+    // chain_L(h) <= h + L a + L 2^-22 (|h| + L |a|) + L 2^-126 (each rounded
+    // add errs by at most 2^-24 of its result or 2^-150 absolute)
+    const double hd = h, ad = a, Ld = rows;
+    const double ub = hd + Ld * ad + Ld * 0x1p-22 * (fabs(hd) + Ld * fabs(ad)) + Ld * 0x1p-126;
+    if (ub < (double)beta) return beta;
+  }
+  float ch = h;
+  for (int k = 0; k < rows; ++k) ch = a + ch;
+  if (ch != ch) return ch;
+  if (ch > beta) return ch;
+  if (ch < beta) return beta;
+  if (ch != 0.0f) return beta;            // equal nonzero values have equal bits
+  // a tie at zero: replay the chunk from h
+  float hh = h;
+  const int64_t base = (b * p.T + t0) * p.C + c;
+  for (int t = 0; t < rows; ++t) {
+    float u = p.bb[base + (int64_t)t * p.C];
+    if (p.xx) u = u + p.xx[base + (int64_t)t * p.C];
+    fwd_step(hh, a, u);
+  }
+  return hh;
+}
+
+// forward pass 2: the exact starting state of every chunk
+__global__ void __launch_bounds__(128) chunk_fwd_carry_kernel(const ChunkArgs p) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= p.B * p.C) return;
+  const int64_t b = e / p.C, c = e % p.C;
+  const float a = p.a[c];
+  float h = p.h0 ? p.h0[b * p.C + c] : p.h_init;
+  const float* __restrict__ beta = p.beta + b * p.nch * p.C + c;
+  float* __restrict__ hs = p.hs + b * p.nch * p.C + c;
+  constexpr int PF = 4;
+  float nb[PF];
+#pragma unroll
+  for (int k = 0; k < PF; ++k) nb[k] = k < p.nch ? __ldcg(beta + (int64_t)k * p.C) : 0.0f;
+  for (int j = 0; j < p.nch; j += PF) {
+    float cur[PF];
+#pragma unroll
+    for (int k = 0; k < PF; ++k) {
+      cur[k] = nb[k];
+      nb[k] = (j + PF + k) < p.nch ? __ldcg(beta + (int64_t)(j + PF + k) * p.C) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < PF; ++k) {
+      const int jj = j + k;
+      if (jj >= p.nch) break;
+      hs[(int64_t)jj * p.C] = h;
+      const int64_t t0 = (int64_t)jj * p.L;
+      const int rows = (int)((p.T - t0) < p.L ? (p.T - t0) : p.L);
+      h = chunk_compose(h, cur[k], a, rows, p, b, c, t0);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// backward: pass A (kOut = false: carry leaving the chunk from carry 0, and
+// whether an input won in it) and pass C (kOut = true: from the exact
+// entering carry, writing gu and the chunk's partial ga)
+// ---------------------------------------------------------------------------
+template <int V, bool kMask, bool kHasX, bool kOut>
+__global__ void __launch_bounds__(256) chunk_bwd_kernel(const ChunkArgs p) {
+  Slot s;
+  if (!slot_of<V>(p, s)) return;
+  const int64_t o = (s.b * p.nch + s.j) * p.C + s.c;
+  float a[V], hm1[V], carry[V], part[V];
+  bool any[V];
+  ldv<V>(a, p.a + s.c);
+  if (p.h0) {
+    ldv<V>(hm1, p.h0 + s.b * p.C + s.c);
+  } else {
+#pragma unroll
+    for (int v = 0; v < V; ++v) hm1[v] = p.h_init;
+  }
+  if (kOut) {
+    ldv<V>(carry, p.cin + o);
+  } else {
+#pragma unroll
+    for (int v = 0; v < V; ++v) carry[v] = 0.0f;
+  }
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    part[v] = 0.0f;
+    any[v] = false;
+  }
+  const int64_t base = (s.b * p.T + s.t0) * p.C + s.c;
+  uint32_t word[V];
+  int cur_w = -1;
+  auto step_row = [&](int t, const float (&g)[V], const float (&u)[V], const float (&hp)[V]) {
+    if (kMask) {
+      const int w = (int)((s.t0 + t) / 32);
+      if (w != cur_w) {
+        ldw<V>(word, p.win_in + (s.b * p.nw + w) * p.C + s.c);
+        cur_w = w;
+      }
+    }
+    float out[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      bool win;
+      if (kMask) win = (word[v] >> ((s.t0 + t) & 31)) & 1u;
+      else win = u[v] >= a[v] + hp[v];
+      const float G = g[v] + carry[v];
+      out[v] = win ? G : 0.0f;
+      const float lost = win ? 0.0f : G;
+      part[v] += lost;
+      carry[v] = lost;
+      any[v] |= win;
+    }
+    if (kOut) stv_stream<V>(p.gu + base + (int64_t)t * p.C, out);
+  };
+  int t = s.rows - 1;
+  for (; t + 1 >= kRowBlock; t -= kRowBlock) {
+    float g[kRowBlock][V], u[kRowBlock][V], hp[kRowBlock][V];
+#pragma unroll
+    for (int k = 0; k < kRowBlock; ++k) {
+      const int tt = t - k;
+      const int64_t off = base + (int64_t)tt * p.C;
+      ldv<V>(g[k], p.gh + off);
+      if (!kMask) {
+        ldv<V>(u[k], p.bb + off);
+        if (kHasX) {
+          float xv[V];
+          ldv<V>(xv, p.xx + off);
+#pragma unroll
+          for (int v = 0; v < V; ++v) u[k][v] = u[k][v] + xv[v];
+        }
+        if (s.t0 + tt == 0) {
+#pragma unroll
+          for (int v = 0; v < V; ++v) hp[k][v] = hm1[v];
+        } else {
+          ldv<V>(hp[k], p.hin + off - p.C);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kRowBlock; ++k) step_row(t - k, g[k], u[k], hp[k]);
+  }
+  for (; t >= 0; --t) {
+    float g[V], u[V], hp[V];
+    const int64_t off = base + (int64_t)t * p.C;
+    ldv<V>(g, p.gh + off);
+    if (!kMask) {
+      ldv<V>(u, p.bb + off);
+      if (kHasX) {
+        float xv[V];
+        ldv<V>(xv, p.xx + off);
+#pragma unroll
+        for (int v = 0; v < V; ++v) u[v] = u[v] + xv[v];
+      }
+      if (s.t0 + t == 0) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) hp[v] = hm1[v];
+      } else {
+        ldv<V>(hp, p.hin + off - p.C);
+      }
+    }
+    step_row(t, g, u, hp);
+  }
+  if (kOut) {
+    stv<V>(p.gap + o, part);
+  } else {
+    stv<V>(p.cout + o, carry);
+#pragma unroll
+    for (int v = 0; v < V; ++v) p.tflag[o + v] = any[v] ? 0 : 1;
+  }
+}
+
+// backward pass B: the exact carry entering every chunk (from the end)
+__global__ void __launch_bounds__(128) chunk_bwd_carry_kernel(const ChunkArgs p) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= p.B * p.C) return;
+  const int64_t b = e / p.C, c = e % p.C;
+  float carry = 0.0f;
+  for (int j = p.nch - 1; j >= 0; --j) {
+    const int64_t o = (b * p.nch + j) * p.C + c;
+    p.cin[o] = carry;
+    if (p.tflag[o]) {
+      // no input won in this chunk: every step passes G = g + carry on
+      const int64_t t0 = (int64_t)j * p.L;
+      const int rows = (int)((p.T - t0) < p.L ? (p.T - t0) : p.L);
+      const float* g = p.gh + (b * p.T + t0) * p.C + c;
+      for (int t = rows - 1; t >= 0; --t) carry = __ldg(g + (int64_t)t * p.C) + carry;
+    } else {
+      carry = __ldcg(p.cout + o);
+    }
+  }
+  if (p.gh0) p.gh0[b * p.C + c] = carry;
+}
+
+// ga[c] = sum over b (ascending) of the chunk partials summed in descending
+// chunk order
+__global__ void chunk_ga_reduce_kernel(const ChunkArgs p) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= p.C) return;
+  float total = 0.0f;
+  for (int64_t b = 0; b < p.B; ++b) {
+    float sb = 0.0f;
+    for (int j = p.nch - 1; j >= 0; --j) sb += p.gap[(b * p.nch + j) * p.C + c];
+    total += sb;
+  }
+  p.ga[c] = total;
+}
+
+int64_t align256(int64_t n) { return (n + 255) & ~(int64_t)255; }
+
+unsigned blocks_for(int64_t threads, int per_block) {
+  return (unsigned)ceil_div(threads, per_block);
+}
+
+}  // namespace
+
+int scan_chunk_pick(int64_t B, int64_t T, int64_t C) {
+  // the longest chunk (32 * 2^k steps) that still gives the passes at least 16
+  // warps of threads per SM
+  const int64_t quads = B * ((C % 4 == 0) ? C / 4 : C);
+  const int64_t want = (int64_t)num_sms() * 512;
+  int L = 32;
+  while (L < 4096 && L * 2 <= T && quads * ceil_div(T, (int64_t)L * 2) >= want) L *= 2;
+  return L;
+}
+
+int64_t scan_chunked_workspace_bytes(int64_t B, int64_t T, int64_t C, int chunk) {
+  if (B <= 0 || T <= 0 || C <= 0) return 0;
+  const int L = chunk > 0 ? chunk : scan_chunk_pick(B, T, C);
+  const int64_t plane = B * ceil_div(T, L) * C;
+  return 3 * align256(plane * 4) + align256(plane);
+}
+
+static int prepare(ChunkArgs& p, int chunk, void* ws, int64_t ws_bytes) {
+  p.L = chunk > 0 ? chunk : scan_chunk_pick(p.B, p.T, p.C);
+  if (p.L % 32 != 0 || p.L <= 0) return TP_ERR_INVALID_ARG;
+  p.nch = (int)ceil_div(p.T, p.L);
+  p.nw = (int)ceil_div(p.T, 32);
+  const int64_t plane = p.B * (int64_t)p.nch * p.C;
+  if (ws == nullptr || ws_bytes < scan_chunked_workspace_bytes(p.B, p.T, p.C, p.L))
+    return TP_ERR_WORKSPACE;
+  if (((uintptr_t)ws & 255u) != 0) return TP_ERR_MISALIGNED;
+  char* w = static_cast<char*>(ws);
+  float* f0 = reinterpret_cast<float*>(w);
+  float* f1 = reinterpret_cast<float*>(w + align256(plane * 4));
+  float* f2 = reinterpret_cast<float*>(w + 2 * align256(plane * 4));
+  uint8_t* u0 = reinterpret_cast<uint8_t*>(w + 3 * align256(plane * 4));
+  // forward: beta, hs; backward: cout, cin, gap, tflag
+  p.beta = f0;
+  p.hs = f1;
+  p.cout = f0;
+  p.cin = f1;
+  p.gap = f2;
+  p.tflag = u0;
+  return TP_OK;
+}
+
+static bool vec4_ok(const ChunkArgs& p, const void* const* ptrs, int n) {
+  if (p.C % 4 != 0) return false;
+  for (int i = 0; i < n; ++i)
+    if (ptrs[i] && !aligned16(ptrs[i])) return false;
+  return true;
+}
+
+int launch_scan_fwd_chunked(const ScanArgs& q, int chunk, void* ws, int64_t ws_bytes,
+                            cudaStream_t stream) {
+  if (q.B == 0 || q.C == 0 || q.T == 0) return TP_OK;
+  ChunkArgs p{};
+  p.B = q.B; p.T = q.T; p.C = q.C;
+  p.bb = q.bb; p.xx = q.xx; p.a = q.a; p.h_init = q.h_init; p.h0 = q.h0;
+  p.h = q.h; p.win = q.win;
+  int s = prepare(p, chunk, ws, ws_bytes);
+  if (s != TP_OK) return s;
+  const void* ptrs[6] = {p.bb, p.xx, p.a, p.h0, p.h, p.win};
+  const bool v4 = vec4_ok(p, ptrs, 6);
+  const int V = v4 ? 4 : 1;
+  const int64_t slots = p.B * p.nch * (p.C / V);
+  const unsigned g1 = blocks_for(slots, 256);
+  const unsigned g2 = blocks_for(p.B * p.C, 128);
+#define TP_FWD1(VV, HX) chunk_fwd_kernel<VV, HX, false, false><<<g1, 256, 0, stream>>>(p)
+#define TP_FWD3(VV, HX, MK) chunk_fwd_kernel<VV, HX, true, MK><<<g1, 256, 0, stream>>>(p)
+  if (v4) {
+    if (p.xx) TP_FWD1(4, true); else TP_FWD1(4, false);
+  } else {
+    if (p.xx) TP_FWD1(1, true); else TP_FWD1(1, false);
+  }
+  if ((s = launch_status()) != TP_OK) return s;
+  chunk_fwd_carry_kernel<<<g2, 128, 0, stream>>>(p);
+  if ((s = launch_status()) != TP_OK) return s;
+  const bool mk = p.win != nullptr;
+  if (v4) {
+    if (p.xx) { if (mk) TP_FWD3(4, true, true); else TP_FWD3(4, true, false); }
+    else      { if (mk) TP_FWD3(4, false, true); else TP_FWD3(4, false, false); }
+  } else {
+    if (p.xx) { if (mk) TP_FWD3(1, true, true); else TP_FWD3(1, true, false); }
+    else      { if (mk) TP_FWD3(1, false, true); else TP_FWD3(1, false, false); }
+  }
+#undef TP_FWD1
+#undef TP_FWD3
+  (void)V;
+  return launch_status();
+}
+
+int launch_scan_bwd_chunked(const ScanArgs& q, int chunk, void* ws, int64_t ws_bytes,
+                            cudaStream_t stream) {
+  if (q.B == 0 || q.C == 0) return TP_OK;
+  if (q.T == 0) {
+    int s = TP_OK;
+    if (q.gh0) s = cuda_status(cudaMemsetAsync(q.gh0, 0, q.B * q.C * 4, stream));
+    if (s == TP_OK && q.ga) s = cuda_status(cudaMemsetAsync(q.ga, 0, q.C * 4, stream));
+    return s;
+  }
+  ChunkArgs p{};
+  p.B = q.B; p.T = q.T; p.C = q.C;
+  p.bb = q.bb; p.xx = q.xx; p.a = q.a; p.h_init = q.h_init; p.h0 = q.h0;
+  p.gh = q.gh; p.hin = q.h; p.win_in = q.win_in; p.gu = q.gu; p.ga = q.ga; p.gh0 = q.gh0;
+  int s = prepare(p, chunk, ws, ws_bytes);
+  if (s != TP_OK) return s;
+  const bool mk = p.win_in != nullptr;
+  const void* ptrs[8] = {p.gh, p.a, p.h0, p.gu, mk ? nullptr : p.bb, mk ? nullptr : p.xx,
+                         mk ? nullptr : p.hin, p.win_in};
+  const bool v4 = vec4_ok(p, ptrs, 8);
+  const int64_t slots = p.B * p.nch * (p.C / (v4 ? 4 : 1));
+  const unsigned g1 = blocks_for(slots, 256);
+  const unsigned g2 = blocks_for(p.B * p.C, 128);
+  const bool hx = !mk && p.xx != nullptr;
+#define TP_BWD(VV, OUT)                                                              \
+  do {                                                                               \
+    if (mk) chunk_bwd_kernel<VV, true, false, OUT><<<g1, 256, 0, stream>>>(p);       \
+    else if (hx) chunk_bwd_kernel<VV, false, true, OUT><<<g1, 256, 0, stream>>>(p);  \
+    else chunk_bwd_kernel<VV, false, false, OUT><<<g1, 256, 0, stream>>>(p);         \
+  } while (0)
+  if (v4) TP_BWD(4, false); else TP_BWD(1, false);
+  if ((s = launch_status()) != TP_OK) return s;
+  chunk_bwd_carry_kernel<<<g2, 128, 0, stream>>>(p);
+  if ((s = launch_status()) != TP_OK) return s;
+  if (v4) TP_BWD(4, true); else TP_BWD(1, true);
+#undef TP_BWD
+  if ((s = launch_status()) != TP_OK) return s;
+  if (p.ga) {
+    chunk_ga_reduce_kernel<<<blocks_for(p.C, 128), 128, 0, stream>>>(p);
+    return launch_status();
+  }
+  return TP_OK;
+}
+
+}  // namespace tp

@@ -500,12 +500,38 @@ def maxplus_backward_smooth(mode: str, tau: float, x: torch.Tensor, w: torch.Ten
 
 
 # --------------------------------------------------------------------------- scan
+SCAN_MODES = ("auto", "sequential", "chunked")
+
+
+def scan_mode(B: int, T: int, C: int, mode: str = "auto") -> str:
+    """The scan evaluation for a shape: "sequential" (one warp per 32 channels
+    of a batch row walks all of T) or "chunked" (time cut into chunks that run
+    in parallel; same forward bits, see tp_scan_fwd_chunked).  "auto" chunks
+    when the batch-row lanes give fewer than two warps per SM and T is long."""
+    if mode not in SCAN_MODES:
+        raise ValueError(f"scan mode must be one of {SCAN_MODES}, got {mode!r}")
+    if mode != "auto":
+        return mode
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return "chunked" if (B * -(-C // 32) < 2 * sms and T >= 1024) else "sequential"
+
+
+def _scan_workspace(B: int, T: int, C: int, dev, chunk: int = 0) -> torch.Tensor:
+    n = _lib.load().tp_scan_chunked_workspace_bytes(B, T, C, chunk)
+    if n < 0:
+        raise ValueError(f"bad scan chunk length {chunk}")
+    return torch.empty(max(n, 256), device=dev, dtype=torch.uint8)
+
+
 def scan_forward(b: torch.Tensor, x: Optional[torch.Tensor], a: torch.Tensor,
                  h_init: float = float("-inf"), h0: Optional[torch.Tensor] = None,
-                 *, need_mask: bool = False):
+                 *, need_mask: bool = False, mode: str = "auto", chunk: int = 0):
     """``h[:, t] = max(a + h[:, t-1], b[:, t] (+ x[:, t]))`` over [B, T, C] contiguous fp32.
 
-    Returns (h, win_mask | None); win_mask is [B, ceil(T/32), C] int32 bit words."""
+    Returns (h, win_mask | None); win_mask is [B, ceil(T/32), C] int32 bit words.
+    ``mode`` picks the evaluation (:func:`scan_mode`); both give the same bits.
+    ``chunk`` (chunked mode): steps per chunk, a multiple of 32 (0: the
+    library's choice)."""
     dev = _require_cuda(b, x, a, h0)
     b = _f32(b).contiguous()
     x = _f32(x).contiguous() if x is not None else None
@@ -524,6 +550,13 @@ def scan_forward(b: torch.Tensor, x: Optional[torch.Tensor], a: torch.Tensor,
     mask = (torch.empty((B, (T + 31) // 32, C), device=dev, dtype=torch.int32)
             if need_mask else None)
     with torch.cuda.device(dev):
+        if scan_mode(B, T, C, mode) == "chunked":
+            ws = _scan_workspace(B, T, C, dev, chunk)
+            st = _lib.load().tp_scan_fwd_chunked(
+                B, T, C, _ptr(b), _ptr(x), _ptr(a), float(h_init), _ptr(h0), _ptr(h),
+                _ptr(mask), int(chunk), _ptr(ws), ws.numel(), _stream(dev))
+            _lib.check(st, "tp_scan_fwd_chunked")
+            return h, mask
         st = _lib.load().tp_scan_fwd(B, T, C, _ptr(b), _ptr(x), _ptr(a), float(h_init),
                                      _ptr(h0), _ptr(h), _ptr(mask), _stream(dev))
     _lib.check(st, "tp_scan_fwd")
@@ -534,10 +567,12 @@ def scan_backward(gh: torch.Tensor, a: torch.Tensor, h_init: float = float("-inf
                   h0: Optional[torch.Tensor] = None, *, mask: Optional[torch.Tensor] = None,
                   b: Optional[torch.Tensor] = None, x: Optional[torch.Tensor] = None,
                   h: Optional[torch.Tensor] = None, need_ga: bool = True,
-                  need_gh0: bool = False):
+                  need_gh0: bool = False, mode: str = "auto", chunk: int = 0):
     """Argmax-path backward of :func:`scan_forward`: returns (gu, ga | None, gh0 | None).
 
-    Winners come from ``mask`` when given, else are recomputed from (b, x, h)."""
+    Winners come from ``mask`` when given, else are recomputed from (b, x, h).
+    ``mode``/``chunk`` as in :func:`scan_forward`; in chunked mode gu and gh0
+    are the same bits and ga agrees to rounding (its sum runs per chunk)."""
     dev = _require_cuda(gh, a, h0, mask, b, x, h)
     gh = _f32(gh).contiguous()
     B, T, C = gh.shape
@@ -547,6 +582,19 @@ def scan_backward(gh: torch.Tensor, a: torch.Tensor, h_init: float = float("-inf
     gu = torch.empty_like(gh)
     ga = torch.empty((C,), device=dev, dtype=torch.float32) if need_ga else None
     gh0 = torch.empty((B, C), device=dev, dtype=torch.float32) if need_gh0 else None
+    if scan_mode(B, T, C, mode) == "chunked":
+        ws = _scan_workspace(B, T, C, dev, chunk)
+        with torch.cuda.device(dev):
+            st = _lib.load().tp_scan_bwd_chunked(
+                B, T, C, _ptr(gh),
+                _ptr(b.contiguous() if b is not None else None),
+                _ptr(x.contiguous() if x is not None else None),
+                _ptr(a), float(h_init), _ptr(h0.contiguous() if h0 is not None else None),
+                _ptr(h.contiguous() if h is not None else None),
+                _ptr(mask), _ptr(gu), _ptr(ga), _ptr(gh0), int(chunk), _ptr(ws), ws.numel(),
+                _stream(dev))
+        _lib.check(st, "tp_scan_bwd_chunked")
+        return gu, ga, gh0
     ws = torch.empty((B, C), device=dev, dtype=torch.float32) if need_ga else None
     with torch.cuda.device(dev):
         st = _lib.load().tp_scan_bwd(

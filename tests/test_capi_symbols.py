@@ -122,3 +122,20 @@ def test_noalloc_checks_arguments_before_its_limit():
     # negative sizes
     assert lib.tp_scan_bwd_noalloc(2, -1, 4, None, None, None, None, 0.0, None, None, None,
                                    None, None, None, None) == -1
+
+
+def test_chunked_scan_validates_on_the_host():
+    from mk_iii_technologies_tsrn_b200 import _lib
+    lib = _lib.load()
+    assert lib.tp_scan_chunked_workspace_bytes(2, 256, 64, 33) == -1
+    assert lib.tp_scan_chunked_workspace_bytes(2, 256, 64, 64) > 0
+    assert lib.tp_scan_chunked_workspace_bytes(0, 256, 64, 0) == 0
+    # chunk lengths must be multiples of 32; negative sizes; NULL inputs
+    assert lib.tp_scan_fwd_chunked(2, 64, 8, None, None, None, 0.0, None, None, None, 48,
+                                   None, 0, None) == -1
+    assert lib.tp_scan_fwd_chunked(-1, 64, 8, None, None, None, 0.0, None, None, None, 32,
+                                   None, 0, None) == -1
+    assert lib.tp_scan_fwd_chunked(2, 64, 8, None, None, None, 0.0, None, None, None, 32,
+                                   None, 0, None) == -2
+    assert lib.tp_scan_bwd_chunked(2, 64, 8, None, None, None, None, 0.0, None, None, None,
+                                   None, None, None, 32, None, 0, None) == -2
