@@ -26,6 +26,16 @@ TSRN block (research/tsrn_dml.py:1073: GRU-gated, d_reservoir = d_model / 2 =
 the state sequence H; ``--esn-mode leaky`` runs the leaky reservoir of
 tsrn_gpu.py (d_reservoir = d_model = 640) instead.  Metric tokens/s.
 
+``--workload tsrn_block``: config 5's hot path, the tropical branches of the first
+TSRN block (research/tsrn_dml.py:1096-1106: fused top-k attention, GRU reservoir,
+tropical SSM, with their LayerNorms and projections) on B=64 sequences of
+T=1024 tokens, d=640; tokens/s and each branch's share of the step.
+
+Batch workloads (scan, dtn, linear, tsrn_attn, esn, tsrn_block) split the
+configuration's batch over the ranks by default (``--scaling strong``); the
+default GEMM line also carries a ``secondary`` list with each of them measured
+in the same run.
+
 ``--workload dtn``: config 2, the drop-in DTNAttention(256, 8) block
 (tropical Q/K projections with the STE backward, tropical score, Maslov
 softmax) forward + backward at B=128, L=64 per rank; metric tokens/s.
@@ -69,7 +79,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload",
-                   choices=["gemm", "scan", "dtn", "linear", "tsrn_attn", "esn"],
+                   choices=["gemm", "scan", "dtn", "linear", "tsrn_attn", "esn", "tsrn_block"],
                    default="gemm")
     p.add_argument("--size", type=int, default=8192, help="M = N = K of the GEMM workload")
     p.add_argument("--dtype", choices=["f32", "bf16"], default="f32",
@@ -1074,6 +1084,184 @@ def esn_workload(args, world, rank):
     }
 
 
+TSRN_BLOCK = dict(B=64, T=1024, d=640, H=8, top_k=16)   # config 5, scale-1 block 0
+
+
+def _tsrn_block_module(dev, seed):
+    """TSRNTropicalPath at config 5's block-0 shape, reference initialisation, with
+    the zero-initialised output projections (reservoir readout, SSM C_proj and
+    gates) drawn small so that every branch changes the residual stream."""
+    from mk_iii_technologies_tsrn_b200.tsrn_block import TSRNTropicalPath
+    torch.manual_seed(seed)
+    d, H, k = TSRN_BLOCK["d"], TSRN_BLOCK["H"], TSRN_BLOCK["top_k"]
+    m = TSRNTropicalPath(d, k, H)
+    with torch.no_grad():
+        m.reservoir.readout.weight.normal_(0.0, 0.02)
+        m.reservoir.W_z.weight.normal_(0.0, 0.02)
+        m.reservoir.W_r.weight.normal_(0.0, 0.02)
+        m.tropical_ssm.C_proj.weight.normal_(0.0, 0.02)
+        m.tropical_ssm.gate_B.weight.normal_(0.0, 0.02)
+        m.tropical_ssm.gate_out.weight.normal_(0.0, 0.02)
+    return m.to(dev).eval()
+
+
+def tsrn_block_workload(args, world, rank):
+    """Config 5's hot path: the tropical branches of the first TSRN block
+    (research/tsrn_dml.py:1096-1106, scale 1: d=640, 8 heads, top_k=16) -- fused
+    top-k attention, GRU echo-state reservoir (d_r=320), tropical SSM scan
+    (h_init=0) with their LayerNorms and projections -- inference on B=64 sequences
+    of T=1024 tokens (split over the ranks)."""
+    from mk_iii_technologies_tsrn_b200 import ops, _lib
+
+    _lib.load().tp_set_pointer_checks(0)
+    B = local_batch(TSRN_BLOCK["B"], world, args)
+    T, d, H, k = TSRN_BLOCK["T"], TSRN_BLOCK["d"], TSRN_BLOCK["H"], TSRN_BLOCK["top_k"]
+    dev = torch.device("cuda")
+    m = _tsrn_block_module(dev, 30)
+    gen = torch.Generator().manual_seed(40 + rank)
+    hx = torch.randn(B, T, d, generator=gen).pin_memory()
+    x = hx.to(dev)
+    names = ("attn", "reservoir", "tropical_ssm")
+    branch_ms = {n: [] for n in names}
+
+    def step(record=False):
+        ev = None
+        if record:
+            ev = {n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for n in names}
+        with torch.no_grad():
+            y = m(x, events=ev)
+        if record:
+            for n in names:
+                branch_ms[n].append(ev[n])
+        return y
+
+    # parity on a slice before timing: the CPU port of the reference block
+    if rank == 0:
+        from oracle.torch_ref import tsrn_block_torch
+        sd = {kk: v.detach().cpu() for kk, v in m.state_dict().items()}
+        xs = hx[:1, :128].clone()
+        with torch.no_grad():
+            got = m(xs.to(dev)).cpu()
+        ref = tsrn_block_torch(xs, sd, H, k)
+        err = (got - ref).abs().max().item()
+        if not err < 2e-3:
+            raise RuntimeError(f"TSRN block tropical path differs from the reference port ({err})")
+    for _ in range(args.warmup):
+        step()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    ms = time_steps(lambda: step(True), args.steps, world)
+    clk = clocks.stop()
+    tokens = B * T * world
+    value = tokens / (ms / args.steps / 1e3)
+    share = {n: max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in branch_ms[n]),
+                               world) for n in names}
+    step_ms = ms / args.steps
+    # the two recurrent / selection kernels timed alone on this step's inputs
+    with torch.no_grad():
+        xa = m.ln_attn(x)
+        Q, K, V = m.attn.project(xa)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ops.tsrn_attention(Q, K, V, m.attn.alibi_slopes, k, True)
+        e0.record()
+        for _ in range(3):
+            ops.tsrn_attention(Q, K, V, m.attn.alibi_slopes, k, True)
+        e1.record()
+        torch.cuda.synchronize()
+        att_ms = e0.elapsed_time(e1) / 3
+        esn_in = m.reservoir.recurrence_inputs(m.ln_res(x))
+        ops.esn_gru_fwd(*esn_in)
+        e0.record()
+        for _ in range(3):
+            ops.esn_gru_fwd(*esn_in)
+        e1.record()
+        torch.cuda.synchronize()
+        esn_ms = e0.elapsed_time(e1) / 3
+        del Q, K, V, esn_in, xa
+    ops.probe_addmax(7, 148 * 8, 50)
+    pms, terms = ops.probe_addmax(7, 148 * 8, 400)
+    peak = 2.0 * terms / (pms / 1e3) / 1e12
+    dr = d // 2
+    att_flops = 2.0 * B * H * (d // H) * T * (T + 1) / 2
+    esn_flops = 2.0 * 3 * B * T * dr * dr
+    if att_ms >= esn_ms:
+        dom = {"kernel": "att_fwd_kernel (fused top-k LSE attention; score dot products, causal)",
+               "achieved": att_flops / (att_ms / 1e3) / 1e12, "kernel_ms": att_ms}
+    else:
+        dom = {"kernel": "esn_kernel (GRU reservoir recurrence; latency-bound per step)",
+               "achieved": esn_flops / (esn_ms / 1e3) / 1e12, "kernel_ms": esn_ms}
+    hy = torch.empty(B, T, d).pin_memory()
+    dx = torch.empty_like(x)
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        with torch.no_grad():
+            y = m(dx)
+        hy.copy_(y, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_steps = max(3, min(args.steps, 5))
+    e2e_ms = time_steps(e2e_step, e2e_steps, world)
+    try:
+        per_step = count_library_kernels(step)
+    except Exception:   # profiler unavailable: leave the count out rather than guess
+        per_step = None
+    return {
+        "metric": "TSRN block tropical path tokens/s (attention + reservoir + SSM, inference)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: x ~ N(0,1) residual stream (seeded), reference initialisation "
+                "(zero-initialised output projections drawn N(0,0.02))",
+        "config": {"workload": f"TSRN block-0 tropical branches B={B * world} T={T} d={d} "
+                               f"H={H} top_k={k} d_reservoir={dr} (config 5, scale 1)",
+                   "parallelism": parallelism(TSRN_BLOCK["B"], B, world),
+                   "branch_ms": share,
+                   "branch_share": {n: share[n] / step_ms for n in names},
+                   "hot_kernel_ms": {"tsrn_attention": att_ms, "esn_gru": esn_ms},
+                   "not_included": "sheaf diffusion, Clifford FFN, p-adic memory and the "
+                                   "embedding / head of the 50.19M-parameter model "
+                                   "(non-tropical)",
+                   "l2": f"residual stream {B * T * d * 4 >> 20} MiB"},
+        "e2e": {"value": tokens / (e2e_ms / e2e_steps / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4},
+        "gpu_launches": per_step * args.steps if per_step is not None else None,
+        "roofline": {"bound": "cuda-core fp32 FMA (dominant kernel)", "achieved": dom["achieved"],
+                     "peak": peak, "unit": "TFLOP/s", "frac": dom["achieved"] / peak,
+                     "traffic": None, "kernel": dom["kernel"], "kernel_ms": dom["kernel_ms"],
+                     "peak_source": "in-repo register-only FFMA probe (tp_probe_addmax form 7), "
+                                    "this run; of measured"},
+        "clocks": clk,
+    }
+
+
+def cpu_tsrn_block_rate(target_s: float = 10.0):
+    """The reference block's tropical branches on CPU torch (oracle/torch_ref.py, pinned
+    to the reference module) on one sequence of T=1024 tokens."""
+    from oracle.torch_ref import tsrn_block_torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    m = _tsrn_block_module(torch.device("cpu"), 30)
+    sd = {k: v.detach() for k, v in m.state_dict().items()}
+    T, d, H, k = TSRN_BLOCK["T"], TSRN_BLOCK["d"], TSRN_BLOCK["H"], TSRN_BLOCK["top_k"]
+    x = torch.randn(1, T, d, generator=torch.Generator().manual_seed(40))
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        tsrn_block_torch(x, sd, H, k)
+        dt = time.perf_counter() - t0
+        reps = int(max(1, min(10, target_s / max(dt, 1e-6))))
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            tsrn_block_torch(x, sd, H, k)
+        dt = (time.perf_counter() - t0) / reps
+    return {"value": T / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"1 of {TSRN_BLOCK['B']} sequences (T={T}) through the reference "
+                      f"block's tropical branches on CPU torch, {reps} reps, {dt:.2f} s each"}
+
+
 def cpu_esn_rate(mode, target_s: float = 10.0):
     from oracle.torch_ref import esn_gru_torch, esn_leaky_torch
 
@@ -1182,6 +1370,11 @@ def reference_arm(args, world, rank):
         dr = ESN["dr_leaky"] if args.esn_mode == "leaky" else ESN["dr_gru"]
         cfg = {"workload": f"{args.esn_mode} EchoStateReservoir d_reservoir={dr} "
                            f"B={ESN['B']} T={ESN['T']} (torch CPU)"}
+    elif args.workload == "tsrn_block":
+        cb = cpu_tsrn_block_rate(target_s=max(3.0, 2.0 * args.steps))
+        metric = "TSRN block tropical path tokens/s (attention + reservoir + SSM, inference)"
+        cfg = {"workload": "TSRN block-0 tropical branches d=640 H=8 top_k=16 d_reservoir=320 "
+                           "T=1024 (torch CPU)"}
     elif args.workload == "tsrn_attn":
         cb = cpu_tsrn_attn_rate(target_s=max(3.0, 2.0 * args.steps))
         metric = "TSRN tropical top-k attention tokens/s (fused fwd, inference)"
@@ -1234,6 +1427,7 @@ def secondary_workloads(args, world, rank):
             ("dtn", dtn_workload, lambda: cpu_dtn_rate(target_s=5.0)),
             ("tsrn_attn", tsrn_attn_workload, lambda: cpu_tsrn_attn_rate(target_s=5.0)),
             ("esn", esn_workload, lambda: cpu_esn_rate("gru", target_s=5.0)),
+            ("tsrn_block", tsrn_block_workload, lambda: cpu_tsrn_block_rate(target_s=5.0)),
             ("linear", linear_workload, lambda: cpu_linear_rate(target_s=3.0))]
     for name, fn, cpu in plan:
         sub = copy.copy(args)
@@ -1271,6 +1465,8 @@ def main():
             res = tsrn_attn_workload(args, world, rank)
         elif args.workload == "esn":
             res = esn_workload(args, world, rank)
+        elif args.workload == "tsrn_block":
+            res = tsrn_block_workload(args, world, rank)
         else:
             res = scan_workload(args, world, rank)
         if res is not None and args.impl == "ours" and rank == 0 and world == 1 \
@@ -1286,6 +1482,8 @@ def main():
                 res["cpu_baseline"] = cpu_tsrn_attn_rate()
             elif args.workload == "esn":
                 res["cpu_baseline"] = cpu_esn_rate(args.esn_mode)
+            elif args.workload == "tsrn_block":
+                res["cpu_baseline"] = cpu_tsrn_block_rate()
             else:
                 res["cpu_baseline"] = cpu_scan_rate(16, 4096, 1024)
         if args.impl == "ours" and args.workload == "gemm" and not args.no_secondary \

@@ -263,6 +263,26 @@ TP_API int tp_set_stream_k(int mode);
 TP_API int tp_set_smooth_fused(int enable);
 
 /* ======================================================================== *
+ *  TSRN attention prologue (research/tsrn_dml.py:472-500: q_norm / k_norm,
+ *  rope, and the view/permute to heads) in one pass.  qkv: [B*T, ld] rows, the
+ *  Q, K, V projections of token (b, t) at columns [0, H*dh), [koff, koff+H*dh),
+ *  [voff, voff+H*dh).  Per head: LayerNorm over dh channels (biased variance,
+ *  eps) with q_gamma/q_beta (Q) or k_gamma/k_beta (K), then the rotary
+ *  embedding of position pos0 + t: channel c < dh/2 paired with c + dh/2,
+ *  out_c = x_c cos - x_{c+dh/2} sin, out_{c+dh/2} = x_{c+dh/2} cos + x_c sin,
+ *  cos/sin from tables [npos, dh/2] (row p = position p).  Outputs Q, K, V are
+ *  [B, H, T, dh] contiguous (the layout tp_tsrn_attention_fwd reads).  dh even,
+ *  at most 128.  (Replaces the reference's PyTorch chain; no C counterpart.)
+ * ======================================================================== */
+TP_API int tp_tsrn_attention_prologue(int64_t B, int64_t T, int64_t H, int64_t dh,
+                                      const float* qkv, int64_t ld, int64_t koff, int64_t voff,
+                                      const float* q_gamma, const float* q_beta,
+                                      const float* k_gamma, const float* k_beta, float eps,
+                                      const float* cos_table, const float* sin_table,
+                                      int64_t npos, int64_t pos0, float* Q, float* K, float* V,
+                                      void* stream);
+
+/* ======================================================================== *
  *  Fused TSRN tropical top-k attention, forward (inference)
  *  Replaces research/tsrn_dml.py:462-548 (TropicalAttention.forward) from the
  *  scores on: the tropical score (:438-460, log-sum-exp over channels), the

@@ -497,6 +497,34 @@ void maxplus_matmul_cuda(const float* A, const float* B, float* C, int M, int K,
   set_last_error(s);
 }
 
+int tp_tsrn_attention_prologue(int64_t B, int64_t T, int64_t H, int64_t dh, const float* qkv,
+                               int64_t ld, int64_t koff, int64_t voff, const float* q_gamma,
+                               const float* q_beta, const float* k_gamma, const float* k_beta,
+                               float eps, const float* cos_table, const float* sin_table,
+                               int64_t npos, int64_t pos0, float* Q, float* K, float* V,
+                               void* stream) {
+  TP_RETURN_IF(B < 0 || T < 0 || H < 0 || dh <= 0 || npos < 0 || pos0 < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(dh % 2 != 0 || dh > 128, TP_ERR_UNSUPPORTED);
+  TP_RETURN_IF(koff < 0 || voff < 0 || ld < 0, TP_ERR_INVALID_ARG);
+  if (B * T * H == 0) return TP_OK;
+  TP_RETURN_IF(ld < H * dh || koff + H * dh > ld || voff + H * dh > ld, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(pos0 + T > npos, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(!(eps >= 0.0f), TP_ERR_INVALID_ARG);
+  TP_CHECK_PTR(qkv);
+  TP_CHECK_PTR(q_gamma);
+  TP_CHECK_PTR(q_beta);
+  TP_CHECK_PTR(k_gamma);
+  TP_CHECK_PTR(k_beta);
+  TP_CHECK_PTR(cos_table);
+  TP_CHECK_PTR(sin_table);
+  TP_CHECK_PTR(Q);
+  TP_CHECK_PTR(K);
+  TP_CHECK_PTR(V);
+  return tp::launch_tsrn_prologue(B, T, H, dh, qkv, ld, koff, voff, q_gamma, q_beta, k_gamma,
+                                  k_beta, eps, cos_table, sin_table, pos0, Q, K, V,
+                                  as_stream(stream));
+}
+
 int64_t tp_tsrn_attention_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t Tkv,
                                           int64_t dh) {
   if (B < 0 || H < 0 || T < 0 || Tkv < 0 || dh < 0) return 0;

@@ -208,6 +208,13 @@ int launch_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int6
                               const float* slopes, int top_k, int causal, float* out,
                               float* ws, cudaStream_t stream);
 
+// tsrn_prologue.cu: QK LayerNorm + rotary embedding + head-major layout of Q/K/V
+int launch_tsrn_prologue(int64_t B, int64_t T, int64_t H, int64_t dh, const float* qkv, int64_t ld,
+                         int64_t koff, int64_t voff, const float* qg, const float* qb,
+                         const float* kg, const float* kb, float eps, const float* cosb,
+                         const float* sinb, int64_t pos0, float* Q, float* K, float* V,
+                         cudaStream_t stream);
+
 // esn.cu: echo-state reservoir recurrences (GRU-gated when gru, else leaky);
 // W[0..2] = Wzh, Wrh, Ws for GRU, W[0] = Ws for leaky
 int launch_esn_fwd(bool gru, int64_t B, int64_t T, int64_t dr, const float* U, const float* Uz,

@@ -802,6 +802,43 @@ def tsrn_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, slopes: to
     return out
 
 
+def tsrn_attention_prologue(qkv: torch.Tensor, B: int, T: int, H: int, dh: int,
+                            q_norm: torch.nn.LayerNorm, k_norm: torch.nn.LayerNorm,
+                            cos: torch.Tensor, sin: torch.Tensor, pos0: int = 0):
+    """Q, K, V [B, H, T, dh] from the stacked projections ``qkv`` [B*T, 3*H*dh]
+    (Q | K | V columns): per-head LayerNorm (``q_norm`` / ``k_norm``) and the
+    rotary embedding of positions pos0..pos0+T-1 (tables ``cos``/``sin``
+    [positions, dh/2]) on Q and K, head-major layout for all three -- the
+    prologue of research/tsrn_dml.py:472-477 in one kernel (inference)."""
+    dev = _require_cuda(qkv, cos, sin)
+    qkv = _f32(qkv)
+    d = H * dh
+    if qkv.dim() != 2 or qkv.shape[0] != B * T or qkv.shape[1] < 3 * d or qkv.stride(1) != 1:
+        raise ValueError(f"qkv must be [B*T, >= 3*H*dh] with unit column stride, "
+                         f"got {tuple(qkv.shape)}")
+    if cos.shape != sin.shape or cos.dim() != 2 or cos.shape[1] * 2 != dh:
+        raise ValueError("cos / sin tables must be [positions, dh/2]")
+
+    def affine(ln):
+        if ln.weight is None:
+            return torch.ones(dh, device=dev), torch.zeros(dh, device=dev)
+        return _f32(ln.weight.detach()).contiguous(), _f32(ln.bias.detach()).contiguous()
+
+    qg, qb = affine(q_norm)
+    kg, kb = affine(k_norm)
+    if q_norm.eps != k_norm.eps:
+        raise ValueError("q_norm and k_norm must share eps")
+    cos, sin = _f32(cos).contiguous(), _f32(sin).contiguous()
+    Q, K, V = (torch.empty(B, H, T, dh, device=dev) for _ in range(3))
+    with torch.cuda.device(dev):
+        st = _lib.load().tp_tsrn_attention_prologue(
+            B, T, H, dh, _ptr(qkv), qkv.stride(0), d, 2 * d, _ptr(qg), _ptr(qb), _ptr(kg),
+            _ptr(kb), float(q_norm.eps), _ptr(cos), _ptr(sin), cos.shape[0], int(pos0),
+            _ptr(Q), _ptr(K), _ptr(V), _stream(dev))
+    _lib.check(st, "tp_tsrn_attention_prologue")
+    return Q, K, V
+
+
 def tsrn_attention_host(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
                         slopes: torch.Tensor, top_k: int, causal: bool = True, Tc: int = 0, *,
                         out: Optional[torch.Tensor] = None, chunks: int = 16) -> torch.Tensor:

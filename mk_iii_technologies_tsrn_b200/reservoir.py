@@ -1,133 +1,210 @@
-"""Echo-state reservoir drop-ins for TSRN.
+"""Echo-state reservoir drop-ins for TSRN on the B200 recurrence kernels.
 
 ``EchoStateReservoir`` replaces the GRU-gated reservoir of
 research/tsrn_dml.py:736-843; ``LeakyEchoStateReservoir`` replaces the leaky
 ``EchoStateReservoir`` of tsrn_gpu.py:435-487 (import it under that name).
-Each has the reference's constructor (including its random initialisation
-order), parameters and buffers, so a reference state dict loads unchanged.
-The spectral scaling and the input projections are the reference's own
-expressions; in inference (no autograd graph, CUDA tensors) the T-step
-recurrence runs as one launch (``ops.esn_gru_fwd`` / ``ops.esn_leaky_fwd``)
-instead of T iterations of small GEMMs.  With autograd the reference loop
-runs, so training is unchanged.
+Both keep the reference's constructor, parameter and buffer names (so a
+reference state dict loads unchanged) and its spectral scaling of the
+recurrent matrix.  The recurrence over T steps runs as one launch
+(``ops.esn_gru_fwd`` / ``ops.esn_leaky_fwd``) in inference and in training;
+for training, :class:`GRUReservoirFunction` / :class:`LeakyReservoirFunction`
+add a backward through time: every step's gates are recomputed at once from the
+saved states (batched GEMMs), a single reverse-time loop carries the state
+gradient, and the weight gradients are batched GEMMs over all steps.  CUDA
+tensors only (no CPU fallback).
 """
 from __future__ import annotations
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from . import ops
 
 
+def _scaled_sparse_gaussian(n: int, sparsity: float, radius: float) -> torch.Tensor:
+    """An n x n N(0,1) matrix keeping each entry with probability 1 - sparsity, scaled
+    to spectral radius ``radius`` (the reference draws the entries, then the mask)."""
+    W = torch.randn(n, n)
+    W = W * (torch.rand(n, n) > sparsity).float()
+    with torch.no_grad():
+        rho = torch.linalg.eigvals(W).abs().max().real.item()
+    return W * (radius / rho) if rho > 0 else W
+
+
+def _previous_states(H: torch.Tensor, h0=None) -> torch.Tensor:
+    """h_{t-1} for every step t of H [B, T, dr] (h_{-1} = 0)."""
+    first = torch.zeros_like(H[:, :1]) if h0 is None else h0.unsqueeze(1)
+    return torch.cat((first, H[:, :-1]), dim=1)
+
+
+class GRUReservoirFunction(torch.autograd.Function):
+    """H [B, T, dr] of the GRU-gated recurrence (h_{-1} = 0)
+    z = sig(h Wzh^T + Uz_t), r = sig(h Wrh^T + Ur_t),
+    h~ = tanh((r * h) Ws^T + U_t), h <- (1 - z) h + z h~."""
+
+    @staticmethod
+    def forward(ctx, U, Uz, Ur, Wzh, Wrh, Ws):
+        H = ops.esn_gru_fwd(U, Uz, Ur, Wzh, Wrh, Ws)
+        ctx.save_for_backward(U, Uz, Ur, Wzh, Wrh, Ws, H)
+        return H
+
+    @staticmethod
+    def backward(ctx, dH):
+        U, Uz, Ur, Wzh, Wrh, Ws, H = ctx.saved_tensors
+        B, T, dr = H.shape
+        Hp = _previous_states(H)
+        z = torch.sigmoid(Hp @ Wzh.T + Uz)
+        r = torch.sigmoid(Hp @ Wrh.T + Ur)
+        m = r * Hp
+        hc = torch.tanh(m @ Ws.T + U)
+        # per-step factors, all steps at once
+        fa = z * (1.0 - hc * hc)              # d h / d a_h  (a_h = m Ws^T + U)
+        fz = (hc - Hp) * z * (1.0 - z)        # d h / d a_z
+        fr = Hp * r * (1.0 - r)               # d m / d a_r
+        keep = 1.0 - z
+        Wzr = torch.cat((Wzh, Wrh), dim=0)    # [2 dr, dr]
+        dA = torch.empty(B, T, 3, dr, device=H.device, dtype=H.dtype)   # a_h, a_z, a_r
+        dH = dH.contiguous()
+        g = torch.zeros(B, dr, device=H.device, dtype=H.dtype)
+        for t in range(T - 1, -1, -1):
+            dh = dH[:, t] + g
+            dah = dh * fa[:, t]
+            dm = dah @ Ws
+            dar = dm * fr[:, t]
+            daz = dh * fz[:, t]
+            dzr = torch.stack((daz, dar), dim=1)                 # [B, 2, dr]
+            g = dh * keep[:, t] + dm * r[:, t] + dzr.reshape(B, 2 * dr) @ Wzr
+            dA[:, t, 0] = dah
+            dA[:, t, 1:] = dzr
+        dAh, dAz, dAr = dA.unbind(2)
+        flat = lambda t: t.reshape(B * T, dr)   # noqa: E731
+        dWs = flat(dAh).T @ flat(m)
+        dWzh = flat(dAz).T @ flat(Hp)
+        dWrh = flat(dAr).T @ flat(Hp)
+        return dAh, dAz, dAr, dWzh, dWrh, dWs
+
+
+class LeakyReservoirFunction(torch.autograd.Function):
+    """H [B, T, dr] of h <- (1 - lk) h + lk tanh(h Ws^T + U_t) (h_{-1} = 0), lk a
+    one-element tensor."""
+
+    @staticmethod
+    def forward(ctx, U, Ws, lk):
+        H = ops.esn_leaky_fwd(U, Ws, lk)
+        ctx.save_for_backward(U, Ws, lk, H)
+        return H
+
+    @staticmethod
+    def backward(ctx, dH):
+        U, Ws, lk, H = ctx.saved_tensors
+        B, T, dr = H.shape
+        Hp = _previous_states(H)
+        s = torch.tanh(Hp @ Ws.T + U)
+        fa = lk * (1.0 - s * s)
+        dA = torch.empty_like(H)
+        dHs = torch.empty_like(H)
+        dH = dH.contiguous()
+        g = torch.zeros(B, dr, device=H.device, dtype=H.dtype)
+        for t in range(T - 1, -1, -1):
+            dh = dH[:, t] + g
+            da = dh * fa[:, t]
+            g = dh * (1.0 - lk) + da @ Ws
+            dA[:, t] = da
+            dHs[:, t] = dh
+        flat = lambda t: t.reshape(B * T, dr)   # noqa: E731
+        dWs = flat(dA).T @ flat(Hp)
+        dlk = (dHs * (s - Hp)).sum().reshape(lk.shape)
+        return dA, dWs, dlk
+
+
+def _needs_graph(x: torch.Tensor, module: nn.Module) -> bool:
+    return torch.is_grad_enabled() and (x.requires_grad or any(
+        p.requires_grad for p in module.parameters()))
+
+
 class EchoStateReservoir(nn.Module):
+    """GRU-gated echo-state reservoir (research/tsrn_dml.py:736-843).  Submodules are
+    created in the reference's order, so a seeded construction draws the same
+    initial weights."""
+
     def __init__(self, d_model: int, d_reservoir: int = None, sparsity: float = 0.9):
         super().__init__()
         dr = d_reservoir or d_model
         self.dr = dr
         self.W_in = nn.Linear(d_model, dr, bias=False)
-        W_res = torch.randn(dr, dr)
-        mask = torch.rand(dr, dr) > sparsity
-        W_res = W_res * mask.float()
-        with torch.no_grad():
-            rho = torch.linalg.eigvals(W_res).abs().max().item()
-            if rho > 0:
-                W_res = W_res * (0.95 / rho)
-        self.W_res = nn.Parameter(W_res)
+        self.W_res = nn.Parameter(_scaled_sparse_gaussian(dr, sparsity, 0.95))
         self.log_rho = nn.Parameter(torch.tensor(0.0))
         self.readout = nn.Linear(dr, d_model, bias=False)
         nn.init.zeros_(self.readout.weight)
         self.W_z = nn.Linear(2 * dr, dr)
         self.W_r = nn.Linear(2 * dr, dr)
-        nn.init.zeros_(self.W_z.weight)
-        nn.init.constant_(self.W_z.bias, 0.85)
-        nn.init.zeros_(self.W_r.weight)
-        nn.init.constant_(self.W_r.bias, 2.0)
+        for gate, bias in ((self.W_z, 0.85), (self.W_r, 2.0)):
+            nn.init.zeros_(gate.weight)
+            nn.init.constant_(gate.bias, bias)
         self.register_buffer("_cached_v", torch.zeros(dr))
 
-    def _power_iter_spectral_radius(self, W: torch.Tensor, n_iter: int = 3) -> torch.Tensor:
-        W_det = W.detach()
-        with torch.no_grad():
-            if torch.all(self._cached_v == 0):
-                self._cached_v.copy_(torch.randn(W_det.shape[0], device=W_det.device,
-                                                 dtype=W_det.dtype))
-            v = self._cached_v.clone().unsqueeze(-1)
-            for _ in range(n_iter):
-                v = W_det @ v
-                v_norm = v.norm()
-                if v_norm > 0:
-                    v = v / v_norm
-            self._cached_v.copy_(v.squeeze(-1))
-            return (W_det @ v).norm()
+    @torch.no_grad()
+    def _radius_estimate(self, iters: int = 3) -> torch.Tensor:
+        """Spectral radius of W_res by ``iters`` normalised power iterations started
+        from the persistent vector ``_cached_v`` (drawn once if still zero), which is
+        advanced in place -- research/tsrn_dml.py:783-806."""
+        W = self.W_res.detach()
+        if not bool(self._cached_v.any()):
+            self._cached_v.copy_(torch.randn(self.dr, device=W.device, dtype=W.dtype))
+        v = self._cached_v.clone().unsqueeze(-1)
+        for _ in range(iters):
+            v = W @ v
+            n = v.norm()
+            v = torch.where(n > 0, v / n, v)     # no host round trip per iteration
+        self._cached_v.copy_(v.squeeze(-1))
+        return (W @ v).norm()
+
+    def _scaled_recurrent(self) -> torch.Tensor:
+        target = torch.sigmoid(self.log_rho) * 1.5
+        return self.W_res * (target / self._radius_estimate().clamp(min=1e-6))
+
+    def recurrence_inputs(self, x: torch.Tensor):
+        """(U, Uz, Ur, Wzh, Wrh, Ws) of ``ops.esn_gru_fwd`` for x [B, T, d_model]."""
+        dr = self.dr
+        Ws = self._scaled_recurrent()
+        U = self.W_in(x)
+        Wzh, Wzu = self.W_z.weight.split(dr, dim=1)
+        Wrh, Wru = self.W_r.weight.split(dr, dim=1)
+        return U, F.linear(U, Wzu, self.W_z.bias), F.linear(U, Wru, self.W_r.bias), Wzh, Wrh, Ws
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        B, T, d = x.shape
-        dr = self.dr
-        rho_target = torch.sigmoid(self.log_rho) * 1.5
-        rho_current = self._power_iter_spectral_radius(self.W_res)
-        scale = rho_target / rho_current.clamp(min=1e-6)
-        W_scaled = self.W_res * scale
-        U = self.W_in(x)
-        W_z_h = self.W_z.weight[:, :dr]
-        W_z_u = self.W_z.weight[:, dr:]
-        W_r_h = self.W_r.weight[:, :dr]
-        W_r_u = self.W_r.weight[:, dr:]
-        U_for_z = U @ W_z_u.T + self.W_z.bias
-        U_for_r = U @ W_r_u.T + self.W_r.bias
-        needs_graph = torch.is_grad_enabled() and any(
-            t.requires_grad for t in (x, *self.parameters()))
-        if not needs_graph and x.is_cuda:
-            H = ops.esn_gru_fwd(U, U_for_z, U_for_r, W_z_h, W_r_h, W_scaled.detach())
-            return self.readout(H)
-        # the reference loop (autograd through time)
-        h = torch.zeros(B, dr, device=x.device, dtype=x.dtype)
-        outs = []
-        for t in range(T):
-            u_t = U[:, t, :]
-            z = torch.sigmoid(h @ W_z_h.T + U_for_z[:, t, :])
-            r = torch.sigmoid(h @ W_r_h.T + U_for_r[:, t, :])
-            h_tilde = torch.tanh((r * h) @ W_scaled.T + u_t)
-            h = (1 - z) * h + z * h_tilde
-            outs.append(h)
-        return self.readout(torch.stack(outs, dim=1))
+        U, Uz, Ur, Wzh, Wrh, Ws = self.recurrence_inputs(x)
+        if _needs_graph(x, self):
+            H = GRUReservoirFunction.apply(U, Uz, Ur, Wzh, Wrh, Ws)
+        else:
+            H = ops.esn_gru_fwd(U, Uz, Ur, Wzh, Wrh, Ws.detach())
+        return self.readout(H)
 
 
 class LeakyEchoStateReservoir(nn.Module):
     """Leaky echo-state reservoir (tsrn_gpu.py:435-487):
-    h_t = (1 - lk) h_{t-1} + lk tanh(h_{t-1} W_scaled^T + W_in x_t), lk = sigmoid(leak)."""
+    h_t = (1 - lk) h_{t-1} + lk tanh(h_{t-1} W_scaled^T + W_in x_t), lk = sigmoid(leak),
+    W_scaled = W_res * sigmoid(log_rho) * 1.5 / (largest |eigenvalue| of W_res)."""
 
     def __init__(self, d_model: int, d_reservoir: int = None, sparsity: float = 0.9):
         super().__init__()
         dr = d_reservoir or d_model
         self.dr = dr
         self.W_in = nn.Linear(d_model, dr, bias=False)
-        W_res = torch.randn(dr, dr)
-        mask = torch.rand(dr, dr) > sparsity
-        W_res = W_res * mask.float()
-        with torch.no_grad():
-            rho = torch.linalg.eigvals(W_res).abs().max().real
-            if rho > 0:
-                W_res = W_res * (0.95 / rho.item())
-        self.W_res = nn.Parameter(W_res)
+        self.W_res = nn.Parameter(_scaled_sparse_gaussian(dr, sparsity, 0.95))
         self.log_rho = nn.Parameter(torch.tensor(0.0))
         self.readout = nn.Linear(dr, d_model, bias=False)
         nn.init.zeros_(self.readout.weight)
         self.leak = nn.Parameter(torch.tensor(0.3))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        B, T, d = x.shape
-        rho = torch.sigmoid(self.log_rho) * 1.5
-        eigs = torch.linalg.eigvals(self.W_res).abs()
-        W_scaled = self.W_res * (rho / (eigs.max().real.clamp(min=1e-6)))
+        radius = torch.linalg.eigvals(self.W_res).abs().max().real.clamp(min=1e-6)
+        Ws = self.W_res * (torch.sigmoid(self.log_rho) * 1.5 / radius)
         lk = torch.sigmoid(self.leak)
-        needs_graph = torch.is_grad_enabled() and any(
-            t.requires_grad for t in (x, *self.parameters()))
-        if not needs_graph and x.is_cuda:
-            H = ops.esn_leaky_fwd(self.W_in(x), W_scaled, lk)
-            return self.readout(H)
-        h = torch.zeros(B, self.dr, device=x.device, dtype=x.dtype)
-        outs = []
-        for t in range(T):
-            u = self.W_in(x[:, t, :])
-            h = (1 - lk) * h + lk * torch.tanh(h @ W_scaled.T + u)
-            outs.append(h)
-        return self.readout(torch.stack(outs, dim=1))
+        U = self.W_in(x)
+        if _needs_graph(x, self):
+            H = LeakyReservoirFunction.apply(U, Ws, lk.reshape(1))
+        else:
+            H = ops.esn_leaky_fwd(U, Ws.detach(), lk.detach())
+        return self.readout(H)

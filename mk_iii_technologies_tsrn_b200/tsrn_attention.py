@@ -1,98 +1,164 @@
-"""``TropicalAttention`` drop-in for TSRN (research/tsrn_dml.py:355-548).
+"""``TropicalAttention`` drop-in for TSRN (research/tsrn_dml.py:355-548) on the B200 kernels.
 
-Same constructor, sub-module and buffer names as the reference (``Wq``, ``Wk``,
-``Wv``, ``Wo``, ``q_norm``, ``k_norm``, ``rope``, ``alibi_slopes``,
-``cross_window_mem``), so a reference state dict loads unchanged.  The Q/K/V
-projections, QK-norm and RoPE stay in PyTorch; in inference (eval mode or no
-grad) the tropical score, ALiBi, causal mask, top-k threshold, softmax and
-@V run as one fused kernel (``ops.tsrn_attention``).  With gradients enabled
-in training the score runs on the LSE kernel (``ops.LSEScoreFunction``) and
-the rest in PyTorch, so autograd sees the reference's expression.
+The module keeps the reference's constructor and its parameter / buffer names
+(``Wq``, ``Wk``, ``Wv``, ``Wo``, ``q_norm``, ``k_norm``, ``rope.inv_freq``,
+``alibi_slopes``, ``cross_window_mem.cached_k`` / ``cached_v``), so a reference
+state dict loads unchanged.  The computation is this library's:
+
+* one GEMM projects Q, K and V together (the three weights stacked);
+* one kernel (``tp_tsrn_attention_prologue``) applies the per-head QK
+  LayerNorm and the rotary embedding and lays Q/K/V out head-major;
+* one kernel (``tp_tsrn_attention_fwd``) computes the log-sum-exp tropical
+  score, ALiBi, the causal mask, the top-k threshold, the softmax and @V
+  without materialising the T x T scores;
+* in training, :class:`TopKAttentionFunction` keeps that forward and supplies
+  an analytic backward (scores recomputed by the LSE kernel, softmax and top-k
+  mask differentiated in closed form, Q/K gradients by the LSE backward
+  kernel); with attention dropout the forward runs densely so that the
+  dropped weights are the ones differentiated.
 """
 from __future__ import annotations
 
-from typing import Optional, Tuple
+from typing import Dict, Optional, Tuple
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from . import ops
 
 
-class RotaryPositionEmbedding(nn.Module):
-    """RoPE with base 500000 (research/tsrn_dml.py:284-319)."""
+def alibi_slopes(n_heads: int) -> torch.Tensor:
+    """Slope of head h (0-based): 2^(-8 (h + 1) / H) (research/tsrn_dml.py:329-334)."""
+    e = torch.arange(1, n_heads + 1, dtype=torch.float64) * (-8.0 / n_heads)
+    return torch.pow(2.0, e).float()
+
+
+class RotaryTable(nn.Module):
+    """Rotary position embedding of research/tsrn_dml.py:284-319: base 500000,
+    channel c paired with c + dh/2 and rotated by pos * inv_freq[c].
+
+    Holds the reference's persistent buffer ``inv_freq``.  The cos / sin tables
+    ([positions, dh/2]) are computed on the host, as the reference builds its
+    cache at construction, and kept per device outside the state dict."""
 
     def __init__(self, dim: int, max_seq_len: int = 4096, base: float = 500000.0):
         super().__init__()
-        inv_freq = 1.0 / (base ** (torch.arange(0, dim, 2).float() / dim))
-        self.register_buffer("inv_freq", inv_freq)
-        self._build_cache(max_seq_len)
+        self.register_buffer("inv_freq",
+                             1.0 / (base ** (torch.arange(0, dim, 2).float() / dim)))
+        self.max_seq_len = max_seq_len
+        self._tables: Dict[tuple, Tuple[torch.Tensor, torch.Tensor]] = {}
 
-    def _build_cache(self, seq_len: int):
-        t = torch.arange(seq_len, dtype=self.inv_freq.dtype, device=self.inv_freq.device)
-        freqs = torch.einsum("i,j->ij", t, self.inv_freq)
-        emb = torch.cat([freqs, freqs], dim=-1)
-        self.register_buffer("cos_cached", emb.cos(), persistent=False)
-        self.register_buffer("sin_cached", emb.sin(), persistent=False)
+    def tables(self, n: int, device) -> Tuple[torch.Tensor, torch.Tensor]:
+        n = max(n, self.max_seq_len)
+        inv = self.inv_freq.detach()
+        key = (str(device), n, inv.data_ptr(), inv._version)
+        hit = self._tables.get(key)
+        if hit is None:
+            angle = torch.outer(torch.arange(n, dtype=torch.float32), inv.float().cpu())
+            hit = (angle.cos().to(device), angle.sin().to(device))
+            self._tables = {key: hit}
+        return hit
 
     @staticmethod
-    def _rotate_half(x: torch.Tensor) -> torch.Tensor:
-        x1, x2 = x[..., :x.shape[-1] // 2], x[..., x.shape[-1] // 2:]
-        return torch.cat([-x2, x1], dim=-1)
-
-    def forward(self, q: torch.Tensor, k: torch.Tensor, offset: int = 0):
-        T = q.shape[2]
-        if offset + T > self.cos_cached.shape[0]:
-            self._build_cache(offset + T)
-        cos = self.cos_cached[offset:offset + T].unsqueeze(0).unsqueeze(0)
-        sin = self.sin_cached[offset:offset + T].unsqueeze(0).unsqueeze(0)
-        return q * cos + self._rotate_half(q) * sin, k * cos + self._rotate_half(k) * sin
+    def rotate(t: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        """Differentiable rotation of t [..., T, dh] by tables [T, dh/2]."""
+        lo, hi = t.chunk(2, dim=-1)
+        return torch.cat((lo * cos - hi * sin, hi * cos + lo * sin), dim=-1)
 
 
-def build_alibi_slopes(n_heads: int) -> torch.Tensor:
-    """Per-head ALiBi slopes 2^(-8 (h+1) / H) (research/tsrn_dml.py:329-334)."""
-    ratio = 2.0 ** (-8.0 / n_heads)
-    return torch.tensor([ratio ** (h + 1) for h in range(n_heads)])
-
-
-class PersistentCrossWindowMemory(nn.Module):
-    """Opt-in K/V cache of the previous window (research/tsrn_dml.py:994-1047)."""
+class CrossWindowCache(nn.Module):
+    """Opt-in K/V of the previous window for autoregressive generation in eval
+    mode (research/tsrn_dml.py:994-1047): after a call the last
+    ``max_cached_len`` positions of sequence 0's rotated K and V are kept and
+    prepended, broadcast over the batch, to the next call's keys."""
 
     def __init__(self, d_model: int, n_heads: int, max_cached_len: int = 256):
         super().__init__()
-        self.H = n_heads
-        self.dh = d_model // n_heads
         self.max_cached_len = max_cached_len
         self.register_buffer("cached_k", torch.zeros(0))
         self.register_buffer("cached_v", torch.zeros(0))
-        self._has_cache = False
         self.enabled = False
+        self._filled = False          # set by store(), not by loading a state dict
 
-    def cache_kv(self, k: torch.Tensor, v: torch.Tensor):
-        with torch.no_grad():
-            T = k.shape[2]
-            start = max(0, T - self.max_cached_len)
-            self.cached_k = k[0, :, start:, :].detach().clone()
-            self.cached_v = v[0, :, start:, :].detach().clone()
-            self._has_cache = True
+    def has(self) -> bool:
+        return self._filled and self.cached_k.numel() > 0
 
-    def get_cached_kv(self, B: int) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor]]:
-        if not self._has_cache or self.cached_k.numel() == 0:
-            return None, None
-        return (self.cached_k.unsqueeze(0).expand(B, -1, -1, -1),
-                self.cached_v.unsqueeze(0).expand(B, -1, -1, -1))
+    def store(self, K: torch.Tensor, V: torch.Tensor) -> None:
+        keep = slice(max(0, K.shape[2] - self.max_cached_len), None)
+        self.cached_k = K[0, :, keep].detach().clone()
+        self.cached_v = V[0, :, keep].detach().clone()
+        self._filled = True
 
-    def reset(self):
+    def prepend(self, K: torch.Tensor, V: torch.Tensor):
+        B = K.shape[0]
+        ck = self.cached_k.unsqueeze(0).expand(B, -1, -1, -1)
+        cv = self.cached_v.unsqueeze(0).expand(B, -1, -1, -1)
+        return torch.cat((ck, K), dim=2), torch.cat((cv, V), dim=2), ck.shape[2]
+
+    def reset(self) -> None:
         self.cached_k = torch.zeros(0, device=self.cached_k.device)
         self.cached_v = torch.zeros(0, device=self.cached_v.device)
-        self._has_cache = False
+        self._filled = False
+
+
+def _masked_scores(Q, K, slopes, top_k: int, causal: bool, Tc: int) -> torch.Tensor:
+    """Dense scores with ALiBi, the causal mask and the top-k cut (-inf outside),
+    the score itself from the LSE kernel."""
+    T, Tkv = Q.shape[2], K.shape[2]
+    S = ops.lse_scores(Q, K)
+    qp = torch.arange(T, device=S.device)
+    kp = torch.arange(-Tc, Tkv - Tc, device=S.device)
+    S = S - slopes.view(-1, 1, 1) * (qp[:, None] - kp[None, :]).abs()
+    if causal:
+        S = S.masked_fill(kp[None, :] > qp[:, None], float("-inf"))
+    cut = S.topk(min(top_k, Tkv), dim=-1).values[..., -1:]
+    return S.masked_fill(S < cut, float("-inf"))
+
+
+class TopKAttentionFunction(torch.autograd.Function):
+    """Tropical top-k attention core: Q, K, V [B, H, T(kv), dh] (rotated) ->
+    context [B, H, T, dh].  The top-k cut is not differentiated (the reference
+    detaches its threshold).  ``drop_p`` > 0 draws an attention-dropout mask
+    (scaled by 1 / (1 - p)) over the kept weights."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, slopes, top_k: int, causal: bool, Tc: int, drop_p: float):
+        ctx.args = (top_k, causal, Tc, drop_p)
+        if drop_p > 0.0:
+            P = torch.softmax(_masked_scores(Q, K, slopes, top_k, causal, Tc), dim=-1)
+            keep = (torch.rand_like(P) >= drop_p).to(P.dtype) / (1.0 - drop_p)
+            ctx.save_for_backward(Q, K, V, slopes, keep)
+            return (P * keep) @ V
+        ctx.save_for_backward(Q, K, V, slopes, None)
+        return ops.tsrn_attention(Q, K, V, slopes, top_k, causal, Tc)
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V, slopes, keep = ctx.saved_tensors
+        top_k, causal, Tc, _ = ctx.args
+        P = torch.softmax(_masked_scores(Q, K, slopes, top_k, causal, Tc), dim=-1)
+        Pd = P * keep if keep is not None else P
+        dV = Pd.transpose(-1, -2) @ dO
+        dP = dO @ V.transpose(-1, -2)
+        if keep is not None:
+            dP = dP * keep
+        # softmax backward: dS = P (dP - sum_j P dP); -inf entries have P = 0
+        dS = P * (dP - (P * dP).sum(dim=-1, keepdim=True))
+        lead = Q.shape[:-2]
+        gQ, gK, _ = ops.maxplus_backward_smooth(
+            "lse", 1.0, Q.reshape(-1, *Q.shape[-2:]), K.reshape(-1, *K.shape[-2:]),
+            dS.reshape(-1, *dS.shape[-2:]))
+        return (gQ.reshape(*lead, *Q.shape[-2:]), gK.reshape(*lead, *K.shape[-2:]), dV,
+                None, None, None, None, None)
 
 
 class TropicalAttention(nn.Module):
     def __init__(self, d_model: int, top_k: int = 8, n_heads: int = 4,
                  dropout: float = 0.0, max_seq_len: int = 4096):
         super().__init__()
-        assert d_model % n_heads == 0
+        if d_model % n_heads:
+            raise ValueError(f"d_model {d_model} is not a multiple of n_heads {n_heads}")
         self.H = n_heads
         self.dh = d_model // n_heads
         self.top_k = top_k
@@ -100,57 +166,53 @@ class TropicalAttention(nn.Module):
         self.Wk = nn.Linear(d_model, d_model, bias=False)
         self.Wv = nn.Linear(d_model, d_model, bias=False)
         self.Wo = nn.Linear(d_model, d_model, bias=False)
+        for w in (self.Wq, self.Wk, self.Wv):
+            nn.init.xavier_uniform_(w.weight, gain=0.5)
         self.drop = nn.Dropout(dropout)
-        nn.init.xavier_uniform_(self.Wq.weight, gain=0.5)
-        nn.init.xavier_uniform_(self.Wk.weight, gain=0.5)
-        nn.init.xavier_uniform_(self.Wv.weight, gain=0.5)
-        self.q_norm = nn.LayerNorm(self.dh, elementwise_affine=True)
-        self.k_norm = nn.LayerNorm(self.dh, elementwise_affine=True)
-        self.rope = RotaryPositionEmbedding(self.dh, max_seq_len=max_seq_len)
-        self.register_buffer("alibi_slopes", build_alibi_slopes(n_heads))
-        self.cross_window_mem = PersistentCrossWindowMemory(d_model, n_heads, max_cached_len=256)
+        self.q_norm = nn.LayerNorm(self.dh)
+        self.k_norm = nn.LayerNorm(self.dh)
+        self.rope = RotaryTable(self.dh, max_seq_len=max_seq_len)
+        self.register_buffer("alibi_slopes", alibi_slopes(n_heads))
+        self.cross_window_mem = CrossWindowCache(d_model, n_heads, max_cached_len=256)
 
-    def _unfused(self, Q, K, V, causal: bool, T_c: int, k: int):
-        # the reference expression (research/tsrn_dml.py:505-526) on the LSE kernel
-        T, T_kv = Q.shape[2], K.shape[2]
-        scores = ops.LSEScoreFunction.apply(Q.contiguous(), K.contiguous(), 1.0)
-        q_pos = torch.arange(T, device=scores.device)
-        k_pos = torch.arange(-T_c, T_kv - T_c, device=scores.device)
-        dist = (q_pos.unsqueeze(1) - k_pos.unsqueeze(0)).abs()
-        alibi = -self.alibi_slopes.to(scores.device).view(-1, 1, 1) * dist.unsqueeze(0)
-        scores = scores + alibi.unsqueeze(0)
-        if causal:
-            mask = k_pos.unsqueeze(0) > q_pos.unsqueeze(1)
-            scores = scores.masked_fill(mask.unsqueeze(0).unsqueeze(0), float("-inf"))
-        topk_v, _ = scores.topk(min(k, T_kv), dim=-1)
-        thr = topk_v[:, :, :, -1:].detach()
-        scores = scores.masked_fill(scores < thr, float("-inf"))
-        w = self.drop(torch.softmax(scores, dim=-1))
-        return w @ V
+    def _qkv_weight(self) -> torch.Tensor:
+        return torch.cat((self.Wq.weight, self.Wk.weight, self.Wv.weight), dim=0)
+
+    def project(self, x: torch.Tensor):
+        """Rotated, normalised Q, K and V [B, H, T, dh] of x [B, T, d] (inference:
+        one stacked GEMM and the fused prologue kernel)."""
+        B, T, d = x.shape
+        qkv = F.linear(x, self._qkv_weight()).reshape(B * T, 3 * d)
+        cos, sin = self.rope.tables(T, x.device)
+        return ops.tsrn_attention_prologue(qkv, B, T, self.H, self.dh, self.q_norm, self.k_norm,
+                                           cos, sin)
+
+    def _project_differentiable(self, x: torch.Tensor):
+        B, T, d = x.shape
+        q, k, v = F.linear(x, self._qkv_weight()).view(B, T, 3, self.H, self.dh).unbind(2)
+        cos, sin = self.rope.tables(T, x.device)
+        cos, sin = cos[:T], sin[:T]
+        heads = lambda t: t.permute(0, 2, 1, 3)   # noqa: E731
+        Q = RotaryTable.rotate(self.q_norm(heads(q)), cos, sin)
+        K = RotaryTable.rotate(self.k_norm(heads(k)), cos, sin)
+        return Q, K, heads(v)
 
     def forward(self, x: torch.Tensor, causal: bool = True) -> torch.Tensor:
         B, T, d = x.shape
-        H, dh = self.H, self.dh
         k = min(self.top_k, T)
-        Q = self.Wq(x).view(B, T, H, dh).permute(0, 2, 1, 3)
-        K = self.Wk(x).view(B, T, H, dh).permute(0, 2, 1, 3)
-        V = self.Wv(x).view(B, T, H, dh).permute(0, 2, 1, 3)
-        Q = self.q_norm(Q)
-        K = self.k_norm(K)
-        Q, K = self.rope(Q, K)
-        K_orig, V_orig = K, V
-        T_c = 0
-        if not self.training and self.cross_window_mem.enabled:
-            ck, cv = self.cross_window_mem.get_cached_kv(B)
-            if ck is not None:
-                K = torch.cat([ck, K], dim=2)
-                V = torch.cat([cv, V], dim=2)
-                T_c = ck.shape[2]
-        if self.training and torch.is_grad_enabled():
-            ctx = self._unfused(Q, K, V, causal, T_c, k)
+        grad = torch.is_grad_enabled() and (x.requires_grad or any(
+            p.requires_grad for p in self.parameters()))
+        Q, K, V = self._project_differentiable(x) if grad else self.project(x)
+        use_cache = not self.training and self.cross_window_mem.enabled
+        Kn, Vn, Tc = K, V, 0
+        if use_cache and self.cross_window_mem.has():
+            K, V, Tc = self.cross_window_mem.prepend(K, V)
+        slopes = self.alibi_slopes.to(device=x.device, dtype=torch.float32)
+        if grad:
+            p = self.drop.p if self.training else 0.0
+            ctx = TopKAttentionFunction.apply(Q, K, V, slopes, k, causal, Tc, p)
         else:
-            ctx = ops.tsrn_attention(Q, K, V, self.alibi_slopes, k, causal, T_c)
-        ctx = ctx.permute(0, 2, 1, 3).contiguous().reshape(B, T, d)
-        if not self.training and self.cross_window_mem.enabled:
-            self.cross_window_mem.cache_kv(K_orig, V_orig)
-        return self.Wo(ctx)
+            ctx = ops.tsrn_attention(Q, K.contiguous(), V.contiguous(), slopes, k, causal, Tc)
+        if use_cache:
+            self.cross_window_mem.store(Kn, Vn)
+        return self.Wo(ctx.transpose(1, 2).reshape(B, T, d))

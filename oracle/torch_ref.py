@@ -144,3 +144,69 @@ def esn_gru_torch(U, Uz, Ur, Wzh, Wrh, Ws):
         h = (1 - z) * h + z * h_tilde
         outs.append(h)
     return torch.stack(outs, dim=1)
+
+
+def _rope_torch(q, k, inv_freq):
+    """Rotary embedding of research/tsrn_dml.py:284-319 (half-split rotation)."""
+    T = q.shape[2]
+    freqs = torch.outer(torch.arange(T, dtype=inv_freq.dtype), inv_freq)
+    emb = torch.cat([freqs, freqs], dim=-1)
+    cos, sin = emb.cos(), emb.sin()
+
+    def rot(t):
+        h = t.shape[-1] // 2
+        return torch.cat([-t[..., h:], t[..., :h]], dim=-1)
+
+    return q * cos + rot(q) * sin, k * cos + rot(k) * sin
+
+
+def tsrn_block_torch(x, sd, heads: int, top_k: int):
+    """The tropical branches of TSRNBlock.forward (research/tsrn_dml.py:1096-1106) in
+    the block's order -- attention (:472-540 with the _attend_chunk core of
+    tsrn_attention_torch), GRU reservoir (:808-843), TropicalSSM (:951-980 with the
+    closed-form scan) -- on CPU torch from a state dict ``sd`` with the block's key
+    names.  CPU timing only."""
+    import torch.nn.functional as F
+
+    def ln(t, p, n=None):
+        return F.layer_norm(t, (n or t.shape[-1],), sd[p + ".weight"], sd[p + ".bias"])
+
+    B, T, d = x.shape
+    dh = d // heads
+    # attention branch
+    h = ln(x, "ln_attn")
+    def heads_of(w):
+        return (h @ sd[w].T).view(B, T, heads, dh).permute(0, 2, 1, 3)
+    Q = ln(heads_of("attn.Wq.weight"), "attn.q_norm")
+    K = ln(heads_of("attn.Wk.weight"), "attn.k_norm")
+    V = heads_of("attn.Wv.weight")
+    Q, K = _rope_torch(Q, K, sd["attn.rope.inv_freq"])
+    ctx = tsrn_attention_torch(Q, K, V, sd["attn.alibi_slopes"], min(top_k, T))
+    x = x + ctx.permute(0, 2, 1, 3).reshape(B, T, d) @ sd["attn.Wo.weight"].T
+    # reservoir branch: spectral scale from 3 power iterations started at the
+    # module's cached vector (research/tsrn_dml.py:783-806, :812-814)
+    h = ln(x, "ln_res")
+    Wres = sd["reservoir.W_res"]
+    dr = Wres.shape[0]
+    v = sd["reservoir._cached_v"].clone().unsqueeze(-1)
+    for _ in range(3):
+        v = Wres @ v
+        nv = v.norm()
+        if nv > 0:
+            v = v / nv
+    rho = torch.sigmoid(sd["reservoir.log_rho"]) * 1.5
+    Ws = Wres * (rho / (Wres @ v).norm().clamp(min=1e-6))
+    U = h @ sd["reservoir.W_in.weight"].T
+    Wz, Wr = sd["reservoir.W_z.weight"], sd["reservoir.W_r.weight"]
+    Uz = U @ Wz[:, dr:].T + sd["reservoir.W_z.bias"]
+    Ur = U @ Wr[:, dr:].T + sd["reservoir.W_r.bias"]
+    Hres = esn_gru_torch(U, Uz, Ur, Wz[:, :dr], Wr[:, :dr], Ws)
+    x = x + Hres @ sd["reservoir.readout.weight"].T
+    # tropical SSM branch
+    h = ln(x, "ln_ssm")
+    u = torch.sigmoid(h @ sd["tropical_ssm.gate_B.weight"].T + sd["tropical_ssm.gate_B.bias"]) \
+        * (h @ sd["tropical_ssm.B_proj.weight"].T)
+    Hs = scan_closed_form_torch(u, sd["tropical_ssm.A"].clamp(max=0))
+    out = torch.sigmoid(h @ sd["tropical_ssm.gate_out.weight"].T
+                        + sd["tropical_ssm.gate_out.bias"]) * (Hs @ sd["tropical_ssm.C_proj.weight"].T)
+    return x + torch.sigmoid(sd["tropical_ssm.mix"]) * out

@@ -3,7 +3,7 @@
 Run in a container that has the reference checkout (default
 /root/reference, override with TSRN_REFERENCE):
 
-    python tests/golden/gen_golden.py
+    python tests/golden/gen_golden.py [generator ...]
 
 Writes ``tests/golden/*.npz``.  Each fixture stores its inputs and the outputs
 of the reference expression, so the tests (and the oracle pin) need nothing
@@ -489,7 +489,74 @@ def gen_tsrn_attention(research):
           ctx=_np(ctx), slopes=_np(attn.alibi_slopes), top_k=np.int64(top_k), **state)
 
 
+def gen_tsrn_block(research):
+    # the tropical branches of research TSRNBlock (research/tsrn_dml.py:1050-1110),
+    # eval: x + attn(ln_attn(x)), then + reservoir(ln_res(.)), then
+    # + tropical_ssm(ln_ssm(.)) -- the block's order without the sheaf, FFN and
+    # p-adic branches between them -- each by the block's own sub-modules.
+    # Inputs are redrawn until no attention row has a near-tie at its top-k cut.
+    import copy
+    d, heads, top_k, B, T = 48, 4, 4, 2, 36
+    for seed in range(12, 40):
+        torch.manual_seed(seed)
+        blk = research.TSRNBlock(d, top_k=top_k, n_heads=heads, sheaf_window=4, mem_depth=3,
+                                 use_reservoir=True, use_padic_attn=False, use_memory=False,
+                                 use_tropical_ssm=True, dropout=0.0)
+        with torch.no_grad():
+            for ln in (blk.ln_attn, blk.ln_res, blk.ln_ssm):
+                ln.weight.uniform_(0.6, 1.4)
+                ln.bias.uniform_(-0.2, 0.2)
+            blk.attn.Wo.weight.normal_(0.0, 0.2)
+            r = blk.reservoir
+            r.W_z.weight.normal_(0.0, 0.15)
+            r.W_r.weight.normal_(0.0, 0.15)
+            r.log_rho.fill_(0.4)
+            r.readout.weight.normal_(0.0, 0.3)
+            r._cached_v.copy_(torch.randn(r.dr if hasattr(r, "dr") else r.W_res.shape[0]))
+            m = blk.tropical_ssm
+            m.C_proj.weight.normal_(0.0, 0.3)
+            m.A.copy_(torch.linspace(-0.3, 0.05, m.A.numel()))
+            m.gate_B.weight.normal_(0.0, 0.2)
+            m.gate_out.weight.normal_(0.0, 0.2)
+        blk.eval()
+        x = torch.randn(B, T, d)
+        state = {f"p_{k}": _np(v).copy() for k, v in blk.state_dict().items()}
+        with torch.no_grad():
+            probe = copy.deepcopy(blk)
+            xa = probe.ln_attn(x)
+            Bq, H, dh = B, heads, d // heads
+            Q = probe.attn.q_norm(probe.attn.Wq(xa).view(Bq, T, H, dh).permute(0, 2, 1, 3))
+            K = probe.attn.k_norm(probe.attn.Wk(xa).view(Bq, T, H, dh).permute(0, 2, 1, 3))
+            Q, K = probe.attn.rope(Q, K)
+            S = torch.logsumexp(Q.double().unsqueeze(3) + K.double().unsqueeze(2), dim=-1)
+            pos = torch.arange(T)
+            S = S - probe.attn.alibi_slopes.double().view(-1, 1, 1) * \
+                (pos[:, None] - pos[None, :]).abs()
+            S = S.masked_fill((pos[None, :] > pos[:, None])[None, None], float("-inf"))
+            srt = S.sort(dim=-1, descending=True).values
+            kk = min(top_k, T)
+            gap = (srt[..., kk - 1] - srt[..., kk]).abs()
+            if torch.nan_to_num(gap, nan=1.0, posinf=1.0).min() < 2e-4:
+                continue
+            y1 = x + blk.attn(blk.ln_attn(x))
+            y2 = y1 + blk.reservoir(blk.ln_res(y1))
+            y3 = y2 + blk.tropical_ssm(blk.ln_ssm(y2))
+        _save("tsrn_block", x=_np(x), y_attn=_np(y1), y_res=_np(y2), y=_np(y3),
+              d=np.int64(d), heads=np.int64(heads), top_k=np.int64(top_k), seed=np.int64(seed),
+              **state)
+        return
+    raise RuntimeError("no seed without a top-k near-tie")
+
+
+GENERATORS = ("kat", "linear", "bf16", "lfdual", "scores", "tsrn", "tsrn_attention", "esn",
+              "esn_leaky", "real_weights", "dropin", "tsrn_block")
+
+
 def main():
+    only = set(sys.argv[1:])
+    if only - set(GENERATORS):
+        raise SystemExit(f"unknown generators {sorted(only - set(GENERATORS))}; "
+                         f"choose from {GENERATORS}")
     sys.path.insert(0, REF)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     trop = _load("tropformer", "tropformer.py")
@@ -497,17 +564,17 @@ def main():
     research = _load("research_tsrn_dml", "research/tsrn_dml.py")
     tsrn_gpu = _load("tsrn_gpu", "tsrn_gpu.py")
     dropin = _load("tropformer_dropin", "tropformer_dropin.py")
-    gen_kat(trop)
-    gen_linear(trop)
-    gen_bf16(trop)
-    gen_lfdual(trop, dtn)
-    gen_scores(trop, dtn)
-    gen_tsrn(research)
-    gen_tsrn_attention(research)
-    gen_esn(research)
-    gen_esn_leaky(tsrn_gpu)
-    gen_real_weights(trop, research)
-    gen_dropin(dropin)
+    jobs = {"kat": lambda: gen_kat(trop), "linear": lambda: gen_linear(trop),
+            "bf16": lambda: gen_bf16(trop), "lfdual": lambda: gen_lfdual(trop, dtn),
+            "scores": lambda: gen_scores(trop, dtn), "tsrn": lambda: gen_tsrn(research),
+            "tsrn_attention": lambda: gen_tsrn_attention(research),
+            "esn": lambda: gen_esn(research), "esn_leaky": lambda: gen_esn_leaky(tsrn_gpu),
+            "real_weights": lambda: gen_real_weights(trop, research),
+            "dropin": lambda: gen_dropin(dropin),
+            "tsrn_block": lambda: gen_tsrn_block(research)}
+    for name in GENERATORS:          # every fixture unless some are named
+        if not only or name in only:
+            jobs[name]()
 
 
 if __name__ == "__main__":

@@ -1,0 +1,159 @@
+"""Training paths of the TSRN drop-ins: forward on the fused kernels, backward
+by this library's analytic gradients (GRUReservoirFunction,
+LeakyReservoirFunction, TopKAttentionFunction) -- against float64 autograd of
+the reference's own expressions on the CPU (oracle/torch_ref.py: the loops of
+research/tsrn_dml.py:832-842 and tsrn_gpu.py:479-484, the attention core of
+research/tsrn_dml.py:384-436) and against the reference modules' outputs
+(golden fixtures)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from oracle.torch_ref import esn_gru_torch, esn_leaky_torch, tsrn_attention_torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(got, ref, rtol=2e-4, atol=2e-5):
+    got = got.detach().double().cpu()
+    ref = ref.detach().double()
+    scale = ref.abs().max().item() + 1e-30
+    assert torch.allclose(got, ref, rtol=rtol, atol=atol * max(1.0, scale)), \
+        float((got - ref).abs().max() / scale)
+
+
+def test_gru_reservoir_training_matches_autograd(cuda):
+    from mk_iii_technologies_tsrn_b200.reservoir import EchoStateReservoir
+    g = load_golden("esn")
+    d = g["x"].shape[-1]
+    state = {k[2:]: torch.tensor(v) for k, v in g.items() if k.startswith("p_")}
+    mod = EchoStateReservoir(d, d).to(cuda).train()
+    mod.load_state_dict(state)
+    x = torch.tensor(g["x"], device=cuda, requires_grad=True)
+    y = mod(x)
+    np.testing.assert_allclose(y.detach().cpu().numpy(), g["H"], rtol=0, atol=2e-5)
+    gout = torch.randn(y.shape, generator=torch.Generator().manual_seed(1))
+    (y * gout.to(cuda)).sum().backward()
+    # float64 reference: the module's expressions with autograd through the loop
+    ref = {k: v.double().clone().requires_grad_(v.is_floating_point()) for k, v in state.items()
+           if k != "_cached_v"}
+    v = state["_cached_v"].double().unsqueeze(-1)
+    with torch.no_grad():
+        W = ref["W_res"].detach()
+        for _ in range(3):
+            v = W @ v
+            v = v / v.norm()
+        radius = (W @ v).norm()
+    Ws = ref["W_res"] * (torch.sigmoid(ref["log_rho"]) * 1.5 / radius)
+    xd = torch.tensor(g["x"]).double().requires_grad_(True)
+    U = xd @ ref["W_in.weight"].T
+    Wz, Wr = ref["W_z.weight"], ref["W_r.weight"]
+    Uz = U @ Wz[:, d:].T + ref["W_z.bias"]
+    Ur = U @ Wr[:, d:].T + ref["W_r.bias"]
+    H = esn_gru_torch(U, Uz, Ur, Wz[:, :d], Wr[:, :d], Ws)
+    yr = H @ ref["readout.weight"].T
+    (yr * gout.double()).sum().backward()
+    _close(x.grad, xd.grad)
+    params = dict(mod.named_parameters())
+    for name in ("W_res", "log_rho", "W_in.weight", "W_z.weight", "W_z.bias", "W_r.weight",
+                 "W_r.bias", "readout.weight"):
+        _close(params[name].grad, ref[name].grad)
+
+
+def test_leaky_reservoir_training_matches_autograd(cuda):
+    from mk_iii_technologies_tsrn_b200.reservoir import LeakyEchoStateReservoir
+    g = load_golden("esn_leaky")
+    d = g["x"].shape[-1]
+    state = {k[2:]: torch.tensor(v) for k, v in g.items() if k.startswith("p_")}
+    mod = LeakyEchoStateReservoir(d, d).to(cuda).train()
+    mod.load_state_dict(state)
+    with torch.no_grad():
+        mod.readout.weight.copy_(torch.randn(d, d, generator=torch.Generator().manual_seed(4)))
+    x = torch.tensor(g["x"], device=cuda, requires_grad=True)
+    y = mod(x)
+    gout = torch.randn(y.shape, generator=torch.Generator().manual_seed(2))
+    (y * gout.to(cuda)).sum().backward()
+    ref = {k: v.double().clone().requires_grad_(True) for k, v in state.items()}
+    ref["readout.weight"] = mod.readout.weight.detach().double().cpu().requires_grad_(True)
+    xd = torch.tensor(g["x"]).double().requires_grad_(True)
+    radius = torch.linalg.eigvals(ref["W_res"]).abs().max().real
+    Ws = ref["W_res"] * (torch.sigmoid(ref["log_rho"]) * 1.5 / radius)
+    lk = torch.sigmoid(ref["leak"])
+    H = esn_leaky_torch(xd @ ref["W_in.weight"].T, Ws, lk)
+    ((H @ ref["readout.weight"].T) * gout.double()).sum().backward()
+    _close(x.grad, xd.grad)
+    params = dict(mod.named_parameters())
+    for name in ("W_res", "log_rho", "leak", "W_in.weight", "readout.weight"):
+        _close(params[name].grad, ref[name].grad)
+
+
+def _unambiguous_case(B, H, T, dh, top_k):
+    # inputs whose float64 scores have no near-tie at the top-k cut in any row
+    for seed in range(50):
+        gen = torch.Generator().manual_seed(seed)
+        Q, K, V = (torch.randn(B, H, T, dh, generator=gen) for _ in range(3))
+        slopes = 2.0 ** (-8.0 * torch.arange(1, H + 1, dtype=torch.float64) / H)
+        S = torch.logsumexp(Q.double().unsqueeze(3) + K.double().unsqueeze(2), dim=-1)
+        pos = torch.arange(T)
+        S = S - slopes.view(-1, 1, 1) * (pos[:, None] - pos[None, :]).abs()
+        S = S.masked_fill(pos[None, :] > pos[:, None], float("-inf"))
+        srt = S.sort(dim=-1, descending=True).values
+        gap = (srt[..., top_k - 1] - srt[..., top_k]).abs()
+        if torch.nan_to_num(gap, nan=1.0, posinf=1.0).min() > 1e-3:
+            return Q, K, V, slopes.float()
+    raise RuntimeError("no unambiguous case")
+
+
+@pytest.mark.parametrize("drop", [0.0, 1e-12])
+def test_attention_core_gradients_match_autograd(cuda, drop):
+    # drop > 0 runs the dense dropout path (with p = 1e-12 it keeps every weight)
+    from mk_iii_technologies_tsrn_b200.tsrn_attention import TopKAttentionFunction
+    B, H, T, dh, k = 2, 3, 40, 16, 5
+    Q, K, V, slopes = _unambiguous_case(B, H, T, dh, k)
+    q, kk, v = (t.to(cuda).requires_grad_(True) for t in (Q, K, V))
+    out = TopKAttentionFunction.apply(q, kk, v, slopes.to(cuda), k, True, 0, drop)
+    gout = torch.randn(out.shape, generator=torch.Generator().manual_seed(9))
+    (out * gout.to(cuda)).sum().backward()
+    qd, kd, vd = (t.double().requires_grad_(True) for t in (Q, K, V))
+    ref = tsrn_attention_torch(qd, kd, vd, slopes.double(), k, True)
+    (ref * gout.double()).sum().backward()
+    _close(out, ref, rtol=1e-4, atol=2e-5)
+    _close(q.grad, qd.grad)
+    _close(kk.grad, kd.grad)
+    _close(v.grad, vd.grad)
+
+
+def test_attention_module_training_step(cuda):
+    # the module in train mode (no dropout): output equals the inference path,
+    # gradients reach every parameter
+    from mk_iii_technologies_tsrn_b200.tsrn_attention import TropicalAttention
+    torch.manual_seed(3)
+    m = TropicalAttention(64, top_k=8, n_heads=4).to(cuda)
+    x = torch.randn(2, 48, 64, device=cuda, requires_grad=True)
+    m.train()
+    y_train = m(x)
+    y_train.sum().backward()
+    assert x.grad is not None and torch.isfinite(x.grad).all()
+    for n, p in m.named_parameters():
+        assert p.grad is not None and torch.isfinite(p.grad).all(), n
+    m.eval()
+    with torch.no_grad():
+        y_eval = m(x)
+    torch.testing.assert_close(y_train.detach(), y_eval, rtol=1e-4, atol=2e-5)
+
+
+def test_attention_prologue_matches_torch(cuda):
+    # the fused QK-norm + RoPE + layout kernel against the same chain in PyTorch
+    from mk_iii_technologies_tsrn_b200.tsrn_attention import TropicalAttention
+    torch.manual_seed(5)
+    for d, H in ((64, 4), (640, 8), (96, 2)):
+        m = TropicalAttention(d, top_k=4, n_heads=H).to(cuda).eval()
+        with torch.no_grad():
+            m.q_norm.weight.uniform_(0.5, 1.5)
+            m.k_norm.bias.uniform_(-0.3, 0.3)
+            x = torch.randn(3, 37, d, device=cuda)
+            got = m.project(x)
+            ref = m._project_differentiable(x)
+        for a, b in zip(got, ref):
+            torch.testing.assert_close(a, b.contiguous(), rtol=2e-6, atol=2e-6)

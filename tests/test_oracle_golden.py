@@ -251,3 +251,14 @@ def test_esn_leaky_oracle_pinned():
     g = load_golden("esn_leaky")
     H = oracle.esn_leaky_fwd(g["U"], g["Ws"], g["lk"])
     np.testing.assert_allclose(H, g["H"], rtol=0, atol=1e-6)
+
+
+def test_tsrn_block_cpu_port_pinned():
+    # the CPU port timed as the config-5 block baseline reproduces the reference
+    # TSRNBlock's tropical branches (fixture from the reference module)
+    import torch
+    from oracle.torch_ref import tsrn_block_torch
+    g = load_golden("tsrn_block")
+    sd = {k[2:]: torch.tensor(v) for k, v in g.items() if k.startswith("p_")}
+    y = tsrn_block_torch(torch.tensor(g["x"]), sd, int(g["heads"]), int(g["top_k"]))
+    np.testing.assert_allclose(y.numpy(), g["y"], rtol=1e-6, atol=1e-6)
