@@ -414,12 +414,23 @@ def gemm_workload(args, world, rank):
     ham = torch.empty(M, Nr, dtype=torch.int32).pin_memory()
     dx = torch.empty_like(x)
     dW = torch.empty_like(W)
+    host_sharded = sharded is not None and args.dtype == "f32"
+    if host_sharded:
+        # each rank's host holds its row block of x and its W shard
+        hx = x[rank * (M // world):(rank + 1) * (M // world)].cpu().pin_memory()
 
     def e2e_step():
         if sharded is None and args.dtype == "f32":
             # the host-to-host entry point: x in row blocks, overlapped with the
             # computation and with the results' return
             ops.maxplus_host(hx, hW, out=hy, out_argmax=ham)
+            return
+        if host_sharded:
+            # the rank's row block of x and its W shard over PCIe, x all-gathered
+            # over NVLink while the own block computes, the rank's columns of y
+            # and argmax back to its host
+            from mk_iii_technologies_tsrn_b200.dist import maxplus_host_sharded
+            maxplus_host_sharded(hx, hW, out=hy, out_argmax=ham)
             return
         dx.copy_(hx, non_blocking=True)
         dW.copy_(hW, non_blocking=True)
@@ -501,7 +512,15 @@ def gemm_workload(args, world, rank):
                    "l2": "inputs (2 x 256 MiB) larger than L2",
                    "self_check": check_desc},
         "e2e": {"value": e2e_value, "unit": "Gop/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+                "d2h_bytes_per_step": d2h,
+                "path": ("ops.maxplus_host (x row blocks over PCIe overlapped with the "
+                         "products and the results' return)") if sharded is None and
+                        args.dtype == "f32" else
+                        ("dist.maxplus_host_sharded: per rank its 1/P row block of x and its "
+                         "W shard over PCIe, x all-gathered over NVLink (NCCL, in place) "
+                         "while the own block computes, the rank's columns of y/argmax "
+                         "back to its host (column-sharded result)") if host_sharded else
+                        "device copies + the device entry"},
         # one max-plus kernel per step (+2 exact widening kernels for bf16 operands with
         # fp32 arithmetic; +2 barrier kernels at N>1)
         "gpu_launches": args.steps * (3 if (args.dtype == "bf16" and not bf16_arith) else 1),
@@ -1102,6 +1121,7 @@ def _tsrn_block_module(dev, seed):
         m.tropical_ssm.C_proj.weight.normal_(0.0, 0.02)
         m.tropical_ssm.gate_B.weight.normal_(0.0, 0.02)
         m.tropical_ssm.gate_out.weight.normal_(0.0, 0.02)
+        m.reservoir._cached_v.normal_()    # the power iteration's start, seeded here
     return m.to(dev).eval()
 
 

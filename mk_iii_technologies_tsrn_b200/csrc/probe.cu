@@ -162,13 +162,19 @@ __global__ void __launch_bounds__(256) probe_ffma_kernel(int64_t iters, float* s
   for (int64_t it = 0; it < iters; ++it) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) asm volatile("add.rn.f32 %0, %0, 0f3A83126F;" : "+f"(a[i]));
+    // two sweeps over the 64 accumulators: consecutive FMAs are independent
+    // (volatile asm keeps program order, so a dependent pair issued back to
+    // back would wait out the FMA latency every time)
 #pragma unroll
     for (int j = 0; j < 8; ++j)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < 8; ++i)
         asm volatile("fma.rn.f32 %0, %1, %2, %0;" : "+f"(acc[i][j]) : "f"(a[i]), "f"(b[j]));
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
         asm volatile("fma.rn.f32 %0, %1, %2, %0;" : "+f"(acc[i][j]) : "f"(b[j]), "f"(a[i]));
-      }
   }
   float r = 0.0f;
 #pragma unroll

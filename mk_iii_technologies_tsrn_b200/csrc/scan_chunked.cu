@@ -248,12 +248,17 @@ __device__ float chunk_compose(float h, float beta, float a, int rows, const Chu
   if (beta != beta) return beta;          // NaN inside the chunk whatever enters
   if (h != h) return h;                   // a NaN state stays NaN
   if (h == -INFINITY) return beta;
-  if (isfinite(a) && isfinite(h) && !(beta == INFINITY)) {
-    // chain_L(h) <= h + L a + L 2^-22 (|h| + L |a|) + L 2^-126 (each rounded
-    // add errs by at most 2^-24 of its result or 2^-150 absolute)
-    const double hd = h, ad = a, Ld = rows;
-    const double ub = hd + Ld * ad + Ld * 0x1p-22 * (fabs(hd) + Ld * fabs(ad)) + Ld * 0x1p-126;
-    if (ub < (double)beta) return beta;
+  if (isfinite(a) && isfinite(h)) {
+    // chain_L(h) <= h + L a + L 2^-24 max_k |f_k| (+ 2^-150 per add below the
+    // normal range), and every |f_k| <= |h| + L |a| up to the same errors.  The
+    // margin L 2^-20 (|h| + L |a|) + L 2^-126 exceeds that bound together
+    // with the rounding of these few fp32 operations (each at most 2^-24 of
+    // |h| + L |a| + margin), so ub < beta proves the chain loses; an
+    // overflow makes ub infinite and merely skips the shortcut.
+    const float Lf = (float)rows;
+    const float mag = fabsf(h) + Lf * fabsf(a);
+    const float ub = fmaf(Lf, a, h) + Lf * 0x1p-20f * mag + Lf * 0x1p-126f;
+    if (ub < beta) return beta;
   }
   float ch = h;
   for (int k = 0; k < rows; ++k) ch = a + ch;
@@ -417,23 +422,57 @@ __global__ void __launch_bounds__(256) chunk_bwd_kernel(const ChunkArgs p) {
   }
 }
 
-// backward pass B: the exact carry entering every chunk (from the end)
+// backward pass B: the exact carry entering every chunk (from the end).  The
+// per-chunk words (winner flag, carry out) do not depend on the carry and are
+// prefetched a few chunks ahead; a chunk without a winner passes the carry
+// through its own gradients in order, loaded 32 rows at a time.
 __global__ void __launch_bounds__(128) chunk_bwd_carry_kernel(const ChunkArgs p) {
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= p.B * p.C) return;
   const int64_t b = e / p.C, c = e % p.C;
+  const int64_t base = b * p.nch * p.C + c;
+  constexpr int PF = 4;
+  uint8_t ntf[PF];
+  float nco[PF];
+#pragma unroll
+  for (int k = 0; k < PF; ++k) {
+    const int j = p.nch - 1 - k;
+    ntf[k] = j >= 0 ? __ldcg(p.tflag + base + (int64_t)j * p.C) : (uint8_t)0;
+    nco[k] = j >= 0 ? __ldcg(p.cout + base + (int64_t)j * p.C) : 0.0f;
+  }
   float carry = 0.0f;
-  for (int j = p.nch - 1; j >= 0; --j) {
-    const int64_t o = (b * p.nch + j) * p.C + c;
-    p.cin[o] = carry;
-    if (p.tflag[o]) {
+  for (int j0 = p.nch - 1; j0 >= 0; j0 -= PF) {
+    uint8_t tf[PF];
+    float co[PF];
+#pragma unroll
+    for (int k = 0; k < PF; ++k) {
+      tf[k] = ntf[k];
+      co[k] = nco[k];
+      const int j = j0 - PF - k;
+      ntf[k] = j >= 0 ? __ldcg(p.tflag + base + (int64_t)j * p.C) : (uint8_t)0;
+      nco[k] = j >= 0 ? __ldcg(p.cout + base + (int64_t)j * p.C) : 0.0f;
+    }
+#pragma unroll 1
+    for (int k = 0; k < PF; ++k) {
+      const int j = j0 - k;
+      if (j < 0) break;
+      p.cin[base + (int64_t)j * p.C] = carry;
+      if (!tf[k]) {
+        carry = co[k];
+        continue;
+      }
       // no input won in this chunk: every step passes G = g + carry on
       const int64_t t0 = (int64_t)j * p.L;
       const int rows = (int)((p.T - t0) < p.L ? (p.T - t0) : p.L);
       const float* g = p.gh + (b * p.T + t0) * p.C + c;
-      for (int t = rows - 1; t >= 0; --t) carry = __ldg(g + (int64_t)t * p.C) + carry;
-    } else {
-      carry = __ldcg(p.cout + o);
+      for (int t = rows - 1; t >= 0; t -= 32) {
+        float gv[32];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) gv[q] = (t - q >= 0) ? __ldg(g + (int64_t)(t - q) * p.C) : 0.0f;
+#pragma unroll
+        for (int q = 0; q < 32; ++q)
+          if (t - q >= 0) carry = gv[q] + carry;
+      }
     }
   }
   if (p.gh0) p.gh0[b * p.C + c] = carry;
@@ -462,10 +501,10 @@ unsigned blocks_for(int64_t threads, int per_block) {
 }  // namespace
 
 int scan_chunk_pick(int64_t B, int64_t T, int64_t C) {
-  // the longest chunk (32 * 2^k steps) that still gives the passes at least 16
-  // warps of threads per SM
+  // the longest chunk (32 * 2^k steps) that still gives the passes at least 4
+  // warps of threads per SM (longer chunks shorten the per-lane carry walks)
   const int64_t quads = B * ((C % 4 == 0) ? C / 4 : C);
-  const int64_t want = (int64_t)num_sms() * 512;
+  const int64_t want = (int64_t)num_sms() * 128;
   int L = 32;
   while (L < 4096 && L * 2 <= T && quads * ceil_div(T, (int64_t)L * 2) >= want) L *= 2;
   return L;

@@ -141,3 +141,77 @@ class ShardedMaxPlus:
         # every rank's stores into my buffers are complete after this
         self.y_h.barrier(channel=1, timeout_ms=BARRIER_TIMEOUT_MS)
         return self.y, self.am
+
+
+def maxplus_host_sharded(x_rows: torch.Tensor, w_shard: torch.Tensor, *, group=None,
+                         argmax: bool = True, out: Optional[torch.Tensor] = None,
+                         out_argmax: Optional[torch.Tensor] = None):
+    """Column-sharded max-plus GEMM from host memory to host memory.
+
+    Rank r holds, in (pinned) host memory, its block of rows of x
+    (``x_rows`` [M/P, K], rows r*M/P ... of the full x) and its block of rows of
+    W (``w_shard`` [N/P, K]).  Each rank uploads only those two over PCIe; the
+    full x is assembled on every GPU by an in-place NCCL all-gather over NVLink
+    while the rank's own row block is already being multiplied; the other row
+    blocks follow once the gather lands.  Returns this rank's columns of y (and
+    argmax) for ALL M rows in pinned host memory ([M, N/P]): the result is
+    column-sharded across the ranks' hosts, the union being y = max_k(x + W).
+    Every rank of ``group`` must call this with equal shapes.  Results equal
+    :func:`~.ops.maxplus` of the full operands bit for bit."""
+    if x_rows.is_cuda or w_shard.is_cuda:
+        raise ValueError("maxplus_host_sharded takes host tensors")
+    group = group or dist.group.WORLD
+    P, r = dist.get_world_size(group), dist.get_rank(group)
+    Mr, K = x_rows.shape
+    Ns = w_shard.shape[0]
+    if w_shard.shape[1] != K:
+        raise ValueError("x and W shards differ in K")
+    _lib.load()          # no CPU computation: fails loudly without the CUDA library
+    dev = torch.device("cuda", torch.cuda.current_device())
+    M = Mr * P
+    y_host = out if out is not None else torch.empty(M, Ns, pin_memory=True)
+    a_host = None
+    if argmax:
+        a_host = out_argmax if out_argmax is not None else torch.empty(
+            M, Ns, dtype=torch.int32, pin_memory=True)
+    main = torch.cuda.current_stream(dev)
+    s_in, s_comm, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+    for s in (s_in, s_comm, s_out):
+        s.wait_stream(main)
+    x_full = torch.empty(M, K, device=dev)
+    w_dev = torch.empty(Ns, K, device=dev)
+    y = torch.empty(M, Ns, device=dev)
+    am = torch.empty(M, Ns, device=dev, dtype=torch.int32) if argmax else None
+    own = slice(r * Mr, (r + 1) * Mr)
+    with torch.cuda.stream(s_in):
+        x_full[own].copy_(x_rows, non_blocking=True)
+        w_dev.copy_(w_shard, non_blocking=True)
+    landed = torch.cuda.Event()
+    landed.record(s_in)
+    s_comm.wait_event(landed)
+    with torch.cuda.stream(s_comm):
+        # in place: rank r's input is its own slot of the output
+        dist.all_gather_into_tensor(x_full, x_full[own], group=group)
+    gathered = torch.cuda.Event()
+    gathered.record(s_comm)
+
+    def product(rows: slice):
+        maxplus_strided(x_full[rows], w_dev, argmax=argmax, out=y[rows],
+                        out_argmax=am[rows] if argmax else None)
+        done = torch.cuda.Event()
+        done.record(main)
+        s_out.wait_event(done)
+        with torch.cuda.stream(s_out):
+            y_host[rows].copy_(y[rows], non_blocking=True)
+            if argmax:
+                a_host[rows].copy_(am[rows], non_blocking=True)
+
+    main.wait_event(landed)
+    product(own)
+    main.wait_event(gathered)
+    for rows in (slice(0, r * Mr), slice((r + 1) * Mr, M)):
+        if rows.stop > rows.start:
+            product(rows)
+    for s in (s_in, s_comm, s_out):
+        main.wait_stream(s)
+    return y_host, a_host

@@ -117,3 +117,52 @@ def test_two_rank_sharded_gemm(cuda, mode, force_tma):
     for p in procs:
         p.join(timeout=60)
     assert out == {0: True, 1: True}, out
+
+
+def _two_rank_host_worker(rank, world, port, q):
+    try:
+        import sys
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        import torch.distributed as dist
+        from mk_iii_technologies_tsrn_b200.dist import maxplus_host_sharded
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+        M, N, K = 768, 1024, 288
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(M, K, generator=g)
+        w = torch.randn(N, K, generator=g)
+        w[torch.rand(N, K, generator=g) < 0.05] = float("-inf")
+        Mr, Ns = M // world, N // world
+        ok = True
+        for rep in range(2):                   # two calls in a row
+            y, am = maxplus_host_sharded(x[rank * Mr:(rank + 1) * Mr].pin_memory(),
+                                         w[rank * Ns:(rank + 1) * Ns].pin_memory())
+            torch.cuda.synchronize()
+            ry, ri = oracle.maxplus_fwd(x.numpy(), w[rank * Ns:(rank + 1) * Ns].numpy())
+            ok &= bool(np.array_equal(y.numpy(), ry)) and bool(np.array_equal(am.numpy(), ri))
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, ok))
+    except Exception as e:  # pragma: no cover
+        q.put((rank, repr(e)))
+
+
+def test_two_rank_host_sharded_gemm(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_two_rank_host_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert out == {0: True, 1: True}, out
