@@ -510,7 +510,8 @@ TP_API int tp_convert_bf16_to_f32(int64_t n, const void* src, float* dst, void* 
  *  NaN-propagating max; form 7: fp32 fma (a term is one FMA, 2 flops: the
  *  CUDA-core peak of dot products); form 8: the smooth backward's per-term
  *  shape with one ex2.approx per term (a term is one exponential: the SFU
- *  peak of the STE / LSE passes).  Each of `threads` threads runs `iters`
+ *  peak of the STE / LSE passes); form 9: packed fp32 FMA pairs
+ *  (fma.rn.f32x2, a term is one FMA).  Each of `threads` threads runs `iters`
  *  iterations of 128 terms; the caller times the launch.  sink receives one float per
  *  thread (keeps the work live).
  * ======================================================================== */

@@ -462,7 +462,7 @@ int tp_convert_bf16_to_f32(int64_t n, const void* src, float* dst, void* stream)
 
 int tp_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters, float* sink,
                     void* stream) {
-  TP_RETURN_IF(form < 0 || form > 8 || blocks <= 0 || blocks > 65535 || iters < 0,
+  TP_RETURN_IF(form < 0 || form > 9 || blocks <= 0 || blocks > 65535 || iters < 0,
                TP_ERR_INVALID_ARG);
   TP_CHECK_PTR(sink);
   return launch_probe_addmax(form, blocks, threads, iters, sink, as_stream(stream));

@@ -53,6 +53,9 @@ namespace {
 #ifndef TP_TMA_TN
 #define TP_TMA_TN 8
 #endif
+#ifndef TP_TMA_SEARCH
+#define TP_TMA_SEARCH 128
+#endif
 #ifndef TP_TMA_CHUNK
 #define TP_TMA_CHUNK 64
 #endif
@@ -96,7 +99,7 @@ struct Cfg {
   // from the search warpgroup to the compute warps with setmaxnreg gained
   // 0.7% at K = 8192 but lost 5% at K = 4096, where the slower search falls
   // behind the shorter tiles.)
-  static constexpr int SEARCH_THREADS = 128;
+  static constexpr int SEARCH_THREADS = TP_TMA_SEARCH;   // a divisor of BN, multiple of 32
   template <bool kArgmax>
   static constexpr int threads32() { return kArgmax ? CT + SEARCH_THREADS : THREADS; }
   static constexpr int OUTS = TM * TN;     // outputs per compute thread
@@ -445,8 +448,11 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
         if (!__all_sync(0xffffffffu, ok)) return;
         int mt, nt;
         tile_coords(tile, p.m_tiles, p.n_tiles, mt, nt);
-        const int n = nt * BN + sid;
         const int m0 = mt * BM;
+        // SEARCH_THREADS may be below BN: thread sid walks columns sid,
+        // sid + SEARCH_THREADS, ... of the tile
+        for (int col = sid; col < BN; col += C::SEARCH_THREADS) {
+        const int n = nt * BN + col;
         const int rows = n < Nc ? min(BM, Mc - m0) : 0;
         const float* wrow = p.w + (int64_t)n * p.ldw;
         float tv = 0.0f;
@@ -482,6 +488,7 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
           store_output(p, m, n, tv, best != kBestNone ? best : kc);
           tv = ntv;
           kc = nkc;
+        }
         }
         __syncwarp();
         if (lane == 0) tp_mbar_arrive(&search_done[h & 1]);

@@ -18,6 +18,7 @@
 //   form 6: add.rn.bf16x2 + max.NaN.bf16x2
 //   form 7: fp32 fused multiply-add (two per accumulator and iteration; one
 //           "term" = one FMA = 2 flops), the CUDA-core roofline of dot products
+//   form 9: packed fp32 FMA pairs (fma.rn.f32x2; a term is one FMA)
 //   form 8: the smooth (STE / LSE) backward's per-term shape: packed adds
 //           forming s - max, a clamp, ex2.approx per term, a packed add into
 //           the partition sum and a packed FMA into the first moment (one
@@ -147,6 +148,42 @@ __global__ void __launch_bounds__(256) probe_bf16_kernel(int64_t iters, float* s
   sink[t] = r;
 }
 
+// packed fp32 FMA pairs (fma.rn.f32x2): 32 accumulator pairs, two sweeps of
+// independent instructions per iteration; a "term" is one FMA (2 flops)
+__global__ void __launch_bounds__(256) probe_ffma2_kernel(int64_t iters, float* sink) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  float2 a[4], b[8], acc[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    a[i] = make_float2((float)(t % 97) * 1e-3f + (float)i * 1e-2f,
+                       (float)(t % 83) * 1e-3f + (float)i * 2e-2f);
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    b[j] = make_float2(1.0f - (float)(t % 89) * 1e-4f - (float)j * 1e-3f,
+                       1.0f - (float)(t % 79) * 1e-4f - (float)j * 2e-3f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = make_float2(0.0f, 0.0f);
+  const float2 step = make_float2(1e-3f, 1e-3f);
+  for (int64_t it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = tp_add2(a[i], step);
+#pragma unroll
+    for (int sweep = 0; sweep < 2; ++sweep)
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i][j] = tp_fma2(a[i], b[j], acc[i][j]);
+  }
+  float r = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r += acc[i][j].x + acc[i][j].y;
+  sink[t] = r;
+}
+
 __global__ void __launch_bounds__(256) probe_ffma_kernel(int64_t iters, float* sink) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   float a[8], b[8], acc[8][8];
@@ -248,6 +285,8 @@ int launch_probe_addmax(int form, int64_t blocks, int64_t threads, int64_t iters
     probe_ffma_kernel<<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
   else if (form == 8)
     probe_smooth_kernel<<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
+  else if (form == 9)
+    probe_ffma2_kernel<<<(unsigned)blocks, 256, 0, stream>>>(iters, sink);
   else
     return TP_ERR_INVALID_ARG;
   return launch_status();

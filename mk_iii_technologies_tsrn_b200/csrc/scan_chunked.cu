@@ -50,6 +50,7 @@ namespace tp {
 namespace {
 
 constexpr int kRowBlock = 8;     // rows whose loads are issued together
+constexpr int kPassThreads = 128;   // threads per block of the chunk-parallel passes
 
 struct ChunkArgs {
   int64_t B, T, C;
@@ -171,7 +172,7 @@ __device__ __forceinline__ bool slot_of(const ChunkArgs& p, Slot& s) {
 // (kOut = true: from the exact starting state, writing h and the mask)
 // ---------------------------------------------------------------------------
 template <int V, bool kHasX, bool kOut, bool kMask>
-__global__ void __launch_bounds__(256) chunk_fwd_kernel(const ChunkArgs p) {
+__global__ void __launch_bounds__(kPassThreads) chunk_fwd_kernel(const ChunkArgs p) {
   Slot s;
   if (!slot_of<V>(p, s)) return;
   const int64_t o = (s.b * p.nch + s.j) * p.C + s.c;
@@ -277,7 +278,11 @@ __device__ float chunk_compose(float h, float beta, float a, int rows, const Chu
   return hh;
 }
 
-// forward pass 2: the exact starting state of every chunk
+// forward pass 2: the exact starting state of every chunk.  The chunk states
+// beta do not depend on the walk: they are read 16 at a time (all loads in
+// flight together) ahead of the dependent composes.
+constexpr int kWalkGroup = 16;
+
 __global__ void __launch_bounds__(128) chunk_fwd_carry_kernel(const ChunkArgs p) {
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= p.B * p.C) return;
@@ -286,20 +291,14 @@ __global__ void __launch_bounds__(128) chunk_fwd_carry_kernel(const ChunkArgs p)
   float h = p.h0 ? p.h0[b * p.C + c] : p.h_init;
   const float* __restrict__ beta = p.beta + b * p.nch * p.C + c;
   float* __restrict__ hs = p.hs + b * p.nch * p.C + c;
-  constexpr int PF = 4;
-  float nb[PF];
+  for (int j0 = 0; j0 < p.nch; j0 += kWalkGroup) {
+    float cur[kWalkGroup];
 #pragma unroll
-  for (int k = 0; k < PF; ++k) nb[k] = k < p.nch ? __ldcg(beta + (int64_t)k * p.C) : 0.0f;
-  for (int j = 0; j < p.nch; j += PF) {
-    float cur[PF];
-#pragma unroll
-    for (int k = 0; k < PF; ++k) {
-      cur[k] = nb[k];
-      nb[k] = (j + PF + k) < p.nch ? __ldcg(beta + (int64_t)(j + PF + k) * p.C) : 0.0f;
-    }
-#pragma unroll
-    for (int k = 0; k < PF; ++k) {
-      const int jj = j + k;
+    for (int k = 0; k < kWalkGroup; ++k)
+      cur[k] = __ldcg(beta + (int64_t)min(j0 + k, p.nch - 1) * p.C);
+#pragma unroll 1
+    for (int k = 0; k < kWalkGroup; ++k) {
+      const int jj = j0 + k;
       if (jj >= p.nch) break;
       hs[(int64_t)jj * p.C] = h;
       const int64_t t0 = (int64_t)jj * p.L;
@@ -315,7 +314,7 @@ __global__ void __launch_bounds__(128) chunk_fwd_carry_kernel(const ChunkArgs p)
 // entering carry, writing gu and the chunk's partial ga)
 // ---------------------------------------------------------------------------
 template <int V, bool kMask, bool kHasX, bool kOut>
-__global__ void __launch_bounds__(256) chunk_bwd_kernel(const ChunkArgs p) {
+__global__ void __launch_bounds__(kPassThreads) chunk_bwd_kernel(const ChunkArgs p) {
   Slot s;
   if (!slot_of<V>(p, s)) return;
   const int64_t o = (s.b * p.nch + s.j) * p.C + s.c;
@@ -422,58 +421,82 @@ __global__ void __launch_bounds__(256) chunk_bwd_kernel(const ChunkArgs p) {
   }
 }
 
-// backward pass B: the exact carry entering every chunk (from the end).  The
-// per-chunk words (winner flag, carry out) do not depend on the carry and are
-// prefetched a few chunks ahead; a chunk without a winner passes the carry
-// through its own gradients in order, loaded 32 rows at a time.
+// backward pass B: the exact carry entering every chunk (from the end).  A
+// run of consecutive chunks without a winner passes the carry through all of
+// their gradients in order: one chain over the run's rows, loaded kRowBatch
+// rows at a time (all loads issued before the adds, row indices clamped so
+// that no load is predicated), the entering carry of each chunk of the run
+// recorded as the chain crosses its boundary.  The per-chunk words (winner
+// flags, carries out) do not depend on the walk and are read 16 at a time.
+constexpr int kRowBatch = 64;
+
 __global__ void __launch_bounds__(128) chunk_bwd_carry_kernel(const ChunkArgs p) {
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= p.B * p.C) return;
   const int64_t b = e / p.C, c = e % p.C;
   const int64_t base = b * p.nch * p.C + c;
-  constexpr int PF = 4;
-  uint8_t ntf[PF];
-  float nco[PF];
-#pragma unroll
-  for (int k = 0; k < PF; ++k) {
-    const int j = p.nch - 1 - k;
-    ntf[k] = j >= 0 ? __ldcg(p.tflag + base + (int64_t)j * p.C) : (uint8_t)0;
-    nco[k] = j >= 0 ? __ldcg(p.cout + base + (int64_t)j * p.C) : 0.0f;
-  }
+  const float* g = p.gh + b * p.T * p.C + c;
   float carry = 0.0f;
-  for (int j0 = p.nch - 1; j0 >= 0; j0 -= PF) {
-    uint8_t tf[PF];
-    float co[PF];
+  int j = p.nch - 1;
+  while (j >= 0) {
+    // the next group of chunk words, read together
+    uint8_t tf[kWalkGroup];
+    float co[kWalkGroup];
 #pragma unroll
-    for (int k = 0; k < PF; ++k) {
-      tf[k] = ntf[k];
-      co[k] = nco[k];
-      const int j = j0 - PF - k;
-      ntf[k] = j >= 0 ? __ldcg(p.tflag + base + (int64_t)j * p.C) : (uint8_t)0;
-      nco[k] = j >= 0 ? __ldcg(p.cout + base + (int64_t)j * p.C) : 0.0f;
+    for (int k = 0; k < kWalkGroup; ++k) {
+      const int64_t o = base + (int64_t)max(j - k, 0) * p.C;
+      tf[k] = __ldcg(p.tflag + o);
+      co[k] = __ldcg(p.cout + o);
     }
-#pragma unroll 1
-    for (int k = 0; k < PF; ++k) {
-      const int j = j0 - k;
-      if (j < 0) break;
-      p.cin[base + (int64_t)j * p.C] = carry;
+    int k = 0;
+    while (k < kWalkGroup && j - k >= 0) {
+      const int jj = j - k;
       if (!tf[k]) {
+        p.cin[base + (int64_t)jj * p.C] = carry;
         carry = co[k];
+        ++k;
         continue;
       }
-      // no input won in this chunk: every step passes G = g + carry on
-      const int64_t t0 = (int64_t)j * p.L;
-      const int rows = (int)((p.T - t0) < p.L ? (p.T - t0) : p.L);
-      const float* g = p.gh + (b * p.T + t0) * p.C + c;
-      for (int t = rows - 1; t >= 0; t -= 32) {
-        float gv[32];
+      // a run of chunks without a winner: jj down to jlo (may leave the group)
+      int jlo = jj;
+      int kk = k;
+      while (jlo - 1 >= 0) {
+        const bool next = (kk + 1 < kWalkGroup) ? (tf[kk + 1] != 0)
+                                                 : (__ldcg(p.tflag + base +
+                                                           (int64_t)(jlo - 1) * p.C) != 0);
+        if (!next) break;
+        --jlo;
+        ++kk;
+      }
+      p.cin[base + (int64_t)jj * p.C] = carry;
+      const int64_t t_hi = min(p.T, (int64_t)(jj + 1) * p.L) - 1;
+      const int64_t t_lo = (int64_t)jlo * p.L;
+      for (int64_t t = t_hi; t >= t_lo; t -= kRowBatch) {
+        float gv[kRowBatch];
 #pragma unroll
-        for (int q = 0; q < 32; ++q) gv[q] = (t - q >= 0) ? __ldg(g + (int64_t)(t - q) * p.C) : 0.0f;
+        for (int q = 0; q < kRowBatch; ++q)
+          gv[q] = __ldg(g + max(t - q, t_lo) * p.C);
 #pragma unroll
-        for (int q = 0; q < 32; ++q)
-          if (t - q >= 0) carry = gv[q] + carry;
+        for (int q = 0; q < kRowBatch; ++q) {
+          const int64_t tq = t - q;
+          if (tq >= t_lo) {
+            carry = gv[q] + carry;
+            // leaving the first row of a chunk of the run: the carry enters
+            // the chunk below
+            if (tq % p.L == 0 && tq > t_lo) p.cin[base + (tq / p.L - 1) * p.C] = carry;
+          }
+        }
+      }
+      // continue after the run
+      const int consumed = jj - jlo + 1;
+      k += consumed;
+      if (k >= kWalkGroup) {          // the run left this group: restart below it
+        j = jlo - 1;
+        k = -1;
+        break;
       }
     }
+    if (k >= 0) j -= k;
   }
   if (p.gh0) p.gh0[b * p.C + c] = carry;
 }
@@ -485,8 +508,16 @@ __global__ void chunk_ga_reduce_kernel(const ChunkArgs p) {
   if (c >= p.C) return;
   float total = 0.0f;
   for (int64_t b = 0; b < p.B; ++b) {
+    const float* gp = p.gap + b * p.nch * p.C + c;
     float sb = 0.0f;
-    for (int j = p.nch - 1; j >= 0; --j) sb += p.gap[(b * p.nch + j) * p.C + c];
+    for (int j0 = p.nch - 1; j0 >= 0; j0 -= kWalkGroup) {
+      float v[kWalkGroup];
+#pragma unroll
+      for (int k = 0; k < kWalkGroup; ++k) v[k] = __ldcg(gp + (int64_t)max(j0 - k, 0) * p.C);
+#pragma unroll
+      for (int k = 0; k < kWalkGroup; ++k)
+        if (j0 - k >= 0) sb += v[k];
+    }
     total += sb;
   }
   p.ga[c] = total;
@@ -501,10 +532,10 @@ unsigned blocks_for(int64_t threads, int per_block) {
 }  // namespace
 
 int scan_chunk_pick(int64_t B, int64_t T, int64_t C) {
-  // the longest chunk (32 * 2^k steps) that still gives the passes at least 4
+  // the longest chunk (32 * 2^k steps) that still gives the passes at least 16
   // warps of threads per SM (longer chunks shorten the per-lane carry walks)
   const int64_t quads = B * ((C % 4 == 0) ? C / 4 : C);
-  const int64_t want = (int64_t)num_sms() * 128;
+  const int64_t want = (int64_t)num_sms() * 512;
   int L = 32;
   while (L < 4096 && L * 2 <= T && quads * ceil_div(T, (int64_t)L * 2) >= want) L *= 2;
   return L;
@@ -561,10 +592,10 @@ int launch_scan_fwd_chunked(const ScanArgs& q, int chunk, void* ws, int64_t ws_b
   const bool v4 = vec4_ok(p, ptrs, 6);
   const int V = v4 ? 4 : 1;
   const int64_t slots = p.B * p.nch * (p.C / V);
-  const unsigned g1 = blocks_for(slots, 256);
+  const unsigned g1 = blocks_for(slots, kPassThreads);
   const unsigned g2 = blocks_for(p.B * p.C, 128);
-#define TP_FWD1(VV, HX) chunk_fwd_kernel<VV, HX, false, false><<<g1, 256, 0, stream>>>(p)
-#define TP_FWD3(VV, HX, MK) chunk_fwd_kernel<VV, HX, true, MK><<<g1, 256, 0, stream>>>(p)
+#define TP_FWD1(VV, HX) chunk_fwd_kernel<VV, HX, false, false><<<g1, kPassThreads, 0, stream>>>(p)
+#define TP_FWD3(VV, HX, MK) chunk_fwd_kernel<VV, HX, true, MK><<<g1, kPassThreads, 0, stream>>>(p)
   if (v4) {
     if (p.xx) TP_FWD1(4, true); else TP_FWD1(4, false);
   } else {
@@ -607,14 +638,14 @@ int launch_scan_bwd_chunked(const ScanArgs& q, int chunk, void* ws, int64_t ws_b
                          mk ? nullptr : p.hin, p.win_in};
   const bool v4 = vec4_ok(p, ptrs, 8);
   const int64_t slots = p.B * p.nch * (p.C / (v4 ? 4 : 1));
-  const unsigned g1 = blocks_for(slots, 256);
+  const unsigned g1 = blocks_for(slots, kPassThreads);
   const unsigned g2 = blocks_for(p.B * p.C, 128);
   const bool hx = !mk && p.xx != nullptr;
 #define TP_BWD(VV, OUT)                                                              \
   do {                                                                               \
-    if (mk) chunk_bwd_kernel<VV, true, false, OUT><<<g1, 256, 0, stream>>>(p);       \
-    else if (hx) chunk_bwd_kernel<VV, false, true, OUT><<<g1, 256, 0, stream>>>(p);  \
-    else chunk_bwd_kernel<VV, false, false, OUT><<<g1, 256, 0, stream>>>(p);         \
+    if (mk) chunk_bwd_kernel<VV, true, false, OUT><<<g1, kPassThreads, 0, stream>>>(p);       \
+    else if (hx) chunk_bwd_kernel<VV, false, true, OUT><<<g1, kPassThreads, 0, stream>>>(p);  \
+    else chunk_bwd_kernel<VV, false, false, OUT><<<g1, kPassThreads, 0, stream>>>(p);         \
   } while (0)
   if (v4) TP_BWD(4, false); else TP_BWD(1, false);
   if ((s = launch_status()) != TP_OK) return s;
