@@ -591,15 +591,16 @@ def scan_workload(args, world, rank):
 
     for _ in range(args.warmup):
         step()
+    steps = steps_for(step, args.steps, world)
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
-    ms = time_steps(lambda: step(True), args.steps, world)
+    ms = time_steps(lambda: step(True), steps, world)
     clk = clocks.stop()
     f_ms = max_over_ranks(statistics.mean(p.elapsed_time(q) for p, q in fwd_ms), world)
     b_ms = max_over_ranks(statistics.mean(p.elapsed_time(q) for p, q in bwd_ms), world)
     elems = B * T * C
     bytes_step = 32.0 * elems * world
-    value = bytes_step / (ms / args.steps / 1e3) / 1e9
+    value = bytes_step / (ms / steps / 1e3) / 1e9
     peak = measured_peaks().get("hbm_gbs", 6650.0)
     ach_f = 12.0 * elems / (f_ms / 1e3) / 1e9
     ach_b = 20.0 * elems / (b_ms / 1e3) / 1e9
@@ -624,8 +625,8 @@ def scan_workload(args, world, rank):
     e2e_value = bytes_step / (e2e_ms / 3 / 1e3) / 1e9
     return {
         "metric": "tropical scan GB/s (fwd 12 B/elem + argmax-path bwd 20 B/elem)",
-        "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "value": value, "unit": "GB/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True,
         "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: a=-U(0,1), b~N(0,0.1), x~N(0,1), g~N(0,1), h0=-inf (seeded)",
         "config": {"workload": f"tropical_ssm_scan B={B * world} T={T} C={C}, fwd+bwd",
@@ -635,7 +636,7 @@ def scan_workload(args, world, rank):
                        " fit L2 together; each step rewrites h and gu")},
         "e2e": {"value": e2e_value, "unit": "GB/s",
                 "h2d_bytes_per_step": 3 * elems * 4, "d2h_bytes_per_step": 2 * elems * 4},
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": 3 * steps,
         "roofline": {"bound": "hbm", "achieved": ach_b, "peak": peak, "unit": "GB/s",
                      "frac": ach_b / peak, "traffic": profiled_traffic("scan_bwd_tma_config3"),
                      "algorithmic_bytes": 20 * elems,
@@ -706,12 +707,13 @@ def dtn_workload(args, world, rank):
 
     for _ in range(args.warmup):
         step()
+    steps = steps_for(step, args.steps, world)
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
-    ms = time_steps(step, args.steps, world)
+    ms = time_steps(step, steps, world)
     clk = clocks.stop()
     tokens = B * L * world
-    value = tokens / (ms / args.steps / 1e3)
+    value = tokens / (ms / steps / 1e3)
     # dominant kernels (about 40% of the step): the STE backward of a tropical
     # projection (M=B*64, N=K=256): its stats pass and the one-pass gx + gW
     # kernel each evaluate one exponential per (m, n, k) term -> 2*M*N*K per
@@ -765,8 +767,8 @@ def dtn_workload(args, world, rank):
         per_step = None
     return {
         "metric": "DTN tropical attention block tokens/s (fwd+bwd, train mode)",
-        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True,
         "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: x ~ N(0,1), upstream grad ~ N(0,1), Q/K weights N(0,0.02), "
                 "tau_h ~ U(0.1,1) (seeded)",
@@ -777,7 +779,7 @@ def dtn_workload(args, world, rank):
                    "l2": "activations 8 MiB (fit L2); the tropical kernels are compute-bound"},
         "e2e": {"value": tokens / (e2e_ms / 3 / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hgx.numel() * 4},
-        "gpu_launches": per_step * args.steps if per_step is not None else None,
+        "gpu_launches": per_step * steps if per_step is not None else None,
         "roofline": {"bound": "sfu (ex2)", "achieved": achieved, "peak": peak,
                      "unit": "T exp/s", "frac": achieved / peak, "traffic": None,
                      "kernel": f"STE backward of the Q projection (M={B * L}, N=K=256): stats "
@@ -853,6 +855,7 @@ def linear_workload(args, world, rank):
         timed = graph.replay
     for _ in range(max(args.warmup, 10)):
         timed()
+    steps = steps_for(timed, steps, world)
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
     ms = time_steps(timed, steps, world)
@@ -974,17 +977,18 @@ def tsrn_attn_workload(args, world, rank):
 
     for _ in range(args.warmup):
         step()
+    steps = steps_for(step, args.steps, world)
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
-    ms = time_steps(step, args.steps, world)
+    ms = time_steps(step, steps, world)
     clk = clocks.stop()
     tokens = B * T * world
-    value = tokens / (ms / args.steps / 1e3)
+    value = tokens / (ms / steps / 1e3)
     # roofline: the score dot products (causal: sum over rows of (i+1) keys, dh FMAs
     # each) against the measured fp32 FMA rate
     fmas = B * H * dh * T * (T + 1) / 2
     peak = ffma_peak()
-    achieved = 2.0 * fmas / (ms / args.steps / 1e3) / 1e12
+    achieved = 2.0 * fmas / (ms / steps / 1e3) / 1e12
     hout = torch.empty(B, H, T, dh).pin_memory()
 
     def e2e_step():   # the host entry: sequence groups' copies overlap the computation
@@ -1000,8 +1004,8 @@ def tsrn_attn_workload(args, world, rank):
         per_step = None
     return {
         "metric": "TSRN tropical top-k attention tokens/s (fused fwd, inference)",
-        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True,
         "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: Q, K, V ~ N(0,1) (seeded; the statistics of LayerNorm'd, rotated "
                 "Q/K), ALiBi slopes 2^(-8(h+1)/H)",
@@ -1011,7 +1015,7 @@ def tsrn_attn_workload(args, world, rank):
                    "l2": f"Q/K/V 3 x {B * H * T * dh * 4 >> 20} MiB"},
         "e2e": {"value": tokens / (e2e_ms / e2e_steps / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": 3 * hQ.numel() * 4, "d2h_bytes_per_step": hout.numel() * 4},
-        "gpu_launches": per_step * args.steps if per_step is not None else None,
+        "gpu_launches": per_step * steps if per_step is not None else None,
         "roofline": {"bound": "cuda-core fp32 FMA (score dot products) + selection",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": None,
@@ -1078,15 +1082,16 @@ def esn_workload(args, world, rank):
 
     for _ in range(args.warmup):
         step()
+    steps = steps_for(step, args.steps, world)
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
-    ms = time_steps(step, args.steps, world)
+    ms = time_steps(step, steps, world)
     clk = clocks.stop()
     tokens = B * T * world
-    value = tokens / (ms / args.steps / 1e3)
+    value = tokens / (ms / steps / 1e3)
     gates = 1 if mode == "leaky" else 3
     peak = ffma_peak()
-    achieved = 2.0 * gates * B * T * dr * dr / (ms / args.steps / 1e3) / 1e12
+    achieved = 2.0 * gates * B * T * dr * dr / (ms / steps / 1e3) / 1e12
     hH = torch.empty(B, T, dr).pin_memory()
 
     def e2e_step():   # the host entry: time windows' copies overlap the recurrence
@@ -1108,8 +1113,8 @@ def esn_workload(args, world, rank):
             else "GRU-gated EchoStateReservoir (research/tsrn_dml.py)")
     return {
         "metric": f"echo-state reservoir tokens/s ({mode}, fused recurrence, inference)",
-        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True,
         "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded): U with the statistics of W_in(LayerNorm(x)), sparse "
                 "W_res scaled to spectral radius 0.75" + ("" if mode == "leaky" else
@@ -1120,7 +1125,7 @@ def esn_workload(args, world, rank):
                    "l2": f"U and H {B * T * dr * 4 / 2**20:.0f} MiB each"},
         "e2e": {"value": tokens / (e2e_ms / e2e_steps / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": hU.numel() * 4, "d2h_bytes_per_step": hH.numel() * 4},
-        "gpu_launches": per_step * args.steps if per_step is not None else None,
+        "gpu_launches": per_step * steps if per_step is not None else None,
         "roofline": {"bound": "cuda-core fp32 FMA (recurrent mat-vec products); the "
                               "recurrence is latency-bound per step",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -1199,15 +1204,16 @@ def tsrn_block_workload(args, world, rank):
             raise RuntimeError(f"TSRN block tropical path differs from the reference port ({err})")
     for _ in range(args.warmup):
         step()
+    steps = steps_for(step, args.steps, world)
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
-    ms = time_steps(lambda: step(True), args.steps, world)
+    ms = time_steps(lambda: step(True), steps, world)
     clk = clocks.stop()
     tokens = B * T * world
-    value = tokens / (ms / args.steps / 1e3)
+    value = tokens / (ms / steps / 1e3)
     share = {n: max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in branch_ms[n]),
                                world) for n in names}
-    step_ms = ms / args.steps
+    step_ms = ms / steps
     # the two recurrent / selection kernels timed alone on this step's inputs
     with torch.no_grad():
         xa = m.ln_attn(x)
@@ -1258,7 +1264,7 @@ def tsrn_block_workload(args, world, rank):
         per_step = None
     return {
         "metric": "TSRN block tropical path tokens/s (attention + reservoir + SSM, inference)",
-        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
         "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: x ~ N(0,1) residual stream (seeded), reference initialisation "
@@ -1275,7 +1281,7 @@ def tsrn_block_workload(args, world, rank):
                    "l2": f"residual stream {B * T * d * 4 >> 20} MiB"},
         "e2e": {"value": tokens / (e2e_ms / e2e_steps / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4},
-        "gpu_launches": per_step * args.steps if per_step is not None else None,
+        "gpu_launches": per_step * steps if per_step is not None else None,
         "roofline": {"bound": "cuda-core fp32 FMA (dominant kernel)", "achieved": dom["achieved"],
                      "peak": peak, "unit": "TFLOP/s", "frac": dom["achieved"] / peak,
                      "traffic": None, "kernel": dom["kernel"], "kernel_ms": dom["kernel_ms"],

@@ -61,7 +61,7 @@ def test_validation_rejects_before_launch():
     # empty problems are a no-op success
     assert lib.tp_maxplus_fwd(0, 0, 4, 4, None, 4, None, 4, None, None, 4, None, 0, None) == 0
     assert lib.tp_scan_fwd(0, 4, 4, None, None, None, 0.0, None, None, None, None) == 0
-    assert lib.tp_probe_addmax(9, 1, 256, 1, None, None) == -1
+    assert lib.tp_probe_addmax(10, 1, 256, 1, None, None) == -1
 
 
 def test_null_pointer_rejected_without_pointer_checks():
