@@ -112,6 +112,14 @@ struct Cfg {
 };
 
 using DefaultCfg = Cfg<TP_TMA_TM, TP_TMA_TN, TP_TMA_CHUNK>;
+// argmax problems with K <= TP_TMA_SMALLK_MAX use narrower chunks
+#ifndef TP_TMA_SMALLK_CHUNK
+#define TP_TMA_SMALLK_CHUNK 32
+#endif
+#ifndef TP_TMA_SMALLK_MAX
+#define TP_TMA_SMALLK_MAX 4096
+#endif
+using SmallKCfg = Cfg<TP_TMA_TM, TP_TMA_TN, TP_TMA_SMALLK_CHUNK>;
 
 constexpr int MAX_DESTS = 8;   // output copies (the ranks of one NVLink domain)
 
@@ -1315,6 +1323,102 @@ bool maxplus_tma_eligible(const StridedMaxPlus& p) {
   return tiles >= 16 && tiles < (int64_t)INT32_MAX;
 }
 
+// The fp32 schedule (whole tiles / stream-K / k-aligned pieces) and launch
+// for one chunk width C.
+template <class C>
+int launch_fp32_sched(const StridedMaxPlus& p, const CUtensorMap& xmap, const CUtensorMap& wmap,
+                      TmaParams tp_, cudaStream_t stream) {
+  // Stream-K when the tiles leave the last wave partly idle (every CTA must
+  // cover at least one tile's chunks) and K is long (K >= 4096: shorter tiles
+  // do not repay the split -- 2048^3 with argmax measured 1.07 ms whole-tile
+  // vs 1.17 ms split), unless the stream is being captured (the workspace is
+  // allocated on the stream).  With argmax only when the idle share is at
+  // least 5% of the run: below it the split tiles cost about what they save
+  // (measured: 8192 x 1024 x 8192, 3.46 waves, 5.62 -> 5.27 ms; 8192 x 2048 x
+  // 8192, 6.92 waves, 9.72 -> 9.97 ms; value-only gains in both).
+  const int grid = std::min(num_sms(), tp_.num_tiles);
+  const int mode = g_stream_k.load(std::memory_order_relaxed);
+  const int waves = (int)ceil_div(tp_.num_tiles, grid);
+  const double idle = (double)(waves * grid - tp_.num_tiles) / ((double)waves * grid);
+  bool sk = mode != 0 && tp_.num_tiles >= grid && grid > 1 &&
+            (mode >= 2 || (tp_.num_tiles % grid != 0 && p.K >= 4096 &&
+                           (!p.am || idle >= 0.05)));
+  // The remainder after the whole-tile waves (rem tiles, grid <= rem < 2 grid)
+  // as whole tiles (2 rounds), an even split of its chunks (rem / grid
+  // tile-times), or tiles cut into S k-aligned pieces of whole 64-k chunks
+  // (ceil(S rem / grid) / S).  Forced mode 3 takes the S in {2, 4} with the
+  // fewest rounds.  Auto mode, argmax kernel: the cheapest of the three with
+  // S = 2, each split charged its measured overhead in tile-times at
+  // K = 8192 (even split 0.34: 8192 x 1024 x 8192 took 5.28 ms for an ideal
+  // 4.81; halves 0.10: 5.11 ms for 4.97; quarters were dearer still,
+  // 2048^2 x 8192 2.95 ms against 2.89 ms whole); value-only: the even split
+  // (no measurable overhead).
+  const int sk_dp = std::max(0, tp_.num_tiles / grid - 1);
+  const int rem = tp_.num_tiles - sk_dp * grid;
+  int split = 0;
+  if (sk && p.am && mode == 3) {
+    double best = 1e30;
+    for (int S = 2; S <= 4; S *= 2) {
+      if (tp_.k_tiles % (S * C::KT_PER_CHUNK) != 0) continue;
+      const double cost = (double)ceil_div((int64_t)S * rem, (int64_t)grid) / S;
+      if (cost < best - 1e-9) {
+        best = cost;
+        split = S;
+      }
+    }
+  } else if (sk && p.am && mode == 1) {
+    const double whole = (double)ceil_div(rem, grid);
+    const double even = (double)rem / grid + 0.34;
+    const double halves = tp_.k_tiles % (2 * C::KT_PER_CHUNK) == 0
+                              ? (double)ceil_div((int64_t)2 * rem, (int64_t)grid) / 2 + 0.10
+                              : 1e30;
+    if (whole <= even && whole <= halves) sk = false;
+    else if (halves < even) split = 2;
+  }
+  void* ws = nullptr;
+  if (sk) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    int dev = 0;
+    cudaMemPool_t pool = nullptr;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone ||
+        cudaGetDevice(&dev) != cudaSuccess || (pool = sk_pool(dev)) == nullptr) {
+      (void)cudaGetLastError();
+      sk = false;
+    } else {
+      const size_t slot = (size_t)C::OUTS * C::CT;
+      const size_t nslots = split ? (size_t)(split - 1) * rem : (size_t)grid;
+      const size_t bytes = nslots * slot * (p.am ? 8 : 4) + nslots * 4 + 256;
+      if (cudaMallocFromPoolAsync(&ws, bytes, pool, stream) != cudaSuccess) {
+        (void)cudaGetLastError();
+        sk = false;
+      } else {
+        // whole-tile waves for all but the last full wave; stream-K over that
+        // wave and the remainder (at least one tile's chunks per CTA)
+        tp_.sk = split ? 2 : 1;
+        tp_.sk_cpt = (int)ceil_div(tp_.k_tiles, C::KT_PER_CHUNK);
+        tp_.sk_dp = sk_dp;
+        tp_.sk_units = (int64_t)rem * tp_.sk_cpt;
+        tp_.sk_split = split;
+        tp_.sk_rem = rem;
+        tp_.sk_max = (float*)ws;
+        tp_.sk_cid = p.am ? (int32_t*)(tp_.sk_max + nslots * slot) : nullptr;
+        tp_.sk_flag = (unsigned*)((char*)ws + nslots * slot * (p.am ? 8 : 4));
+        const cudaError_t e = cudaMemsetAsync(tp_.sk_flag, 0, nslots * 4, stream);
+        if (e != cudaSuccess) {
+          (void)cudaFreeAsync(ws, stream);
+          return (int)e;
+        }
+      }
+    }
+  }
+  const int st = p.am ? launch_cfg<C, true>(xmap, wmap, tp_, stream)
+                      : launch_cfg<C, false>(xmap, wmap, tp_, stream);
+  if (ws != nullptr) {
+    const cudaError_t e = cudaFreeAsync(ws, stream);
+    if (st == TP_OK && e != cudaSuccess) return (int)e;
+  }
+  return st;
+}
 int launch_maxplus_fwd_tma(const StridedMaxPlus& p, cudaStream_t stream) {
   return launch_maxplus_fwd_tma_dests(p, nullptr, nullptr, 0, 0, stream);
 }
@@ -1372,96 +1476,14 @@ int launch_maxplus_fwd_tma_dests(const StridedMaxPlus& p, float* const* ydst,
     if (p.am) return launch_cfg16<DefaultCfg, true>(xmap, wmap, tp_, stream);
     return launch_cfg16<DefaultCfg, false>(xmap, wmap, tp_, stream);
   }
-  // Stream-K when the tiles leave the last wave partly idle (every CTA must
-  // cover at least one tile's chunks) and K is long (K >= 4096: shorter tiles
-  // do not repay the split -- 2048^3 with argmax measured 1.07 ms whole-tile
-  // vs 1.17 ms split), unless the stream is being captured (the workspace is
-  // allocated on the stream).  With argmax only when the idle share is at
-  // least 5% of the run: below it the split tiles cost about what they save
-  // (measured: 8192 x 1024 x 8192, 3.46 waves, 5.62 -> 5.27 ms; 8192 x 2048 x
-  // 8192, 6.92 waves, 9.72 -> 9.97 ms; value-only gains in both).
-  const int grid = std::min(num_sms(), tp_.num_tiles);
-  const int mode = g_stream_k.load(std::memory_order_relaxed);
-  const int waves = (int)ceil_div(tp_.num_tiles, grid);
-  const double idle = (double)(waves * grid - tp_.num_tiles) / ((double)waves * grid);
-  bool sk = mode != 0 && tp_.num_tiles >= grid && grid > 1 &&
-            (mode >= 2 || (tp_.num_tiles % grid != 0 && p.K >= 4096 &&
-                           (!p.am || idle >= 0.05)));
-  // The remainder after the whole-tile waves (rem tiles, grid <= rem < 2 grid)
-  // as whole tiles (2 rounds), an even split of its chunks (rem / grid
-  // tile-times), or tiles cut into S k-aligned pieces of whole 64-k chunks
-  // (ceil(S rem / grid) / S).  Forced mode 3 takes the S in {2, 4} with the
-  // fewest rounds.  Auto mode, argmax kernel: the cheapest of the three with
-  // S = 2, each split charged its measured overhead in tile-times at
-  // K = 8192 (even split 0.34: 8192 x 1024 x 8192 took 5.28 ms for an ideal
-  // 4.81; halves 0.10: 5.11 ms for 4.97; quarters were dearer still,
-  // 2048^2 x 8192 2.95 ms against 2.89 ms whole); value-only: the even split
-  // (no measurable overhead).
-  const int sk_dp = std::max(0, tp_.num_tiles / grid - 1);
-  const int rem = tp_.num_tiles - sk_dp * grid;
-  int split = 0;
-  if (sk && p.am && mode == 3) {
-    double best = 1e30;
-    for (int S = 2; S <= 4; S *= 2) {
-      if (tp_.k_tiles % (S * DefaultCfg::KT_PER_CHUNK) != 0) continue;
-      const double cost = (double)ceil_div((int64_t)S * rem, (int64_t)grid) / S;
-      if (cost < best - 1e-9) {
-        best = cost;
-        split = S;
-      }
-    }
-  } else if (sk && p.am && mode == 1) {
-    const double whole = (double)ceil_div(rem, grid);
-    const double even = (double)rem / grid + 0.34;
-    const double halves = tp_.k_tiles % (2 * DefaultCfg::KT_PER_CHUNK) == 0
-                              ? (double)ceil_div((int64_t)2 * rem, (int64_t)grid) / 2 + 0.10
-                              : 1e30;
-    if (whole <= even && whole <= halves) sk = false;
-    else if (halves < even) split = 2;
-  }
-  void* ws = nullptr;
-  if (sk) {
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    int dev = 0;
-    cudaMemPool_t pool = nullptr;
-    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone ||
-        cudaGetDevice(&dev) != cudaSuccess || (pool = sk_pool(dev)) == nullptr) {
-      (void)cudaGetLastError();
-      sk = false;
-    } else {
-      const size_t slot = (size_t)DefaultCfg::OUTS * DefaultCfg::CT;
-      const size_t nslots = split ? (size_t)(split - 1) * rem : (size_t)grid;
-      const size_t bytes = nslots * slot * (p.am ? 8 : 4) + nslots * 4 + 256;
-      if (cudaMallocFromPoolAsync(&ws, bytes, pool, stream) != cudaSuccess) {
-        (void)cudaGetLastError();
-        sk = false;
-      } else {
-        // whole-tile waves for all but the last full wave; stream-K over that
-        // wave and the remainder (at least one tile's chunks per CTA)
-        tp_.sk = split ? 2 : 1;
-        tp_.sk_cpt = (int)ceil_div(tp_.k_tiles, DefaultCfg::KT_PER_CHUNK);
-        tp_.sk_dp = sk_dp;
-        tp_.sk_units = (int64_t)rem * tp_.sk_cpt;
-        tp_.sk_split = split;
-        tp_.sk_rem = rem;
-        tp_.sk_max = (float*)ws;
-        tp_.sk_cid = p.am ? (int32_t*)(tp_.sk_max + nslots * slot) : nullptr;
-        tp_.sk_flag = (unsigned*)((char*)ws + nslots * slot * (p.am ? 8 : 4));
-        const cudaError_t e = cudaMemsetAsync(tp_.sk_flag, 0, nslots * 4, stream);
-        if (e != cudaSuccess) {
-          (void)cudaFreeAsync(ws, stream);
-          return (int)e;
-        }
-      }
-    }
-  }
-  const int st = p.am ? launch_cfg<DefaultCfg, true>(xmap, wmap, tp_, stream)
-                      : launch_cfg<DefaultCfg, false>(xmap, wmap, tp_, stream);
-  if (ws != nullptr) {
-    const cudaError_t e = cudaFreeAsync(ws, stream);
-    if (st == TP_OK && e != cudaSuccess) return (int)e;
-  }
-  return st;
+  // Argmax chunk width: 64-k chunks at K > 4096, 32 below (measured with
+  // argmax: 4096^3 5.57 -> 5.05 ms, 2048^3 1.07 -> 0.87 ms with 32; 8192^3
+  // 37.5 ms with 64 against 38.1 with 32): the deferred search re-reads one
+  // chunk of x and W per output from L2, which matters more when a CTA has
+  // few tiles, while narrower chunks cost snapshot compares in the main loop.
+  if (p.am && p.K <= TP_TMA_SMALLK_MAX) return launch_fp32_sched<SmallKCfg>(p, xmap, wmap, tp_, stream);
+  return launch_fp32_sched<DefaultCfg>(p, xmap, wmap, tp_, stream);
 }
+
 
 }  // namespace tp

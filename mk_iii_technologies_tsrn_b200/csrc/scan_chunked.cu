@@ -76,7 +76,7 @@ struct ChunkArgs {
   float* cout;
   float* cin;
   float* gap;
-  uint8_t* tflag;
+  int* tflag;                      // 1: no input won in the chunk
 };
 
 template <int V>
@@ -278,33 +278,39 @@ __device__ float chunk_compose(float h, float beta, float a, int rows, const Chu
   return hh;
 }
 
-// forward pass 2: the exact starting state of every chunk.  The chunk states
-// beta do not depend on the walk: they are read 16 at a time (all loads in
-// flight together) ahead of the dependent composes.
-constexpr int kWalkGroup = 16;
+// forward pass 2: the exact starting state of every chunk.  One warp per
+// block, one (b, c) lane per thread.  The chunk states beta do not depend on
+// the walk: a window of up to kWin of them is copied into shared memory with
+// cp.async (all in flight together) before the dependent composes.
+constexpr int kWin = 128;
+constexpr int kWalkGroup = 16;   // values read together by the ga reduction
 
-__global__ void __launch_bounds__(128) chunk_fwd_carry_kernel(const ChunkArgs p) {
-  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= p.B * p.C) return;
-  const int64_t b = e / p.C, c = e % p.C;
-  const float a = p.a[c];
-  float h = p.h0 ? p.h0[b * p.C + c] : p.h_init;
-  const float* __restrict__ beta = p.beta + b * p.nch * p.C + c;
-  float* __restrict__ hs = p.hs + b * p.nch * p.C + c;
-  for (int j0 = 0; j0 < p.nch; j0 += kWalkGroup) {
-    float cur[kWalkGroup];
-#pragma unroll
-    for (int k = 0; k < kWalkGroup; ++k)
-      cur[k] = __ldcg(beta + (int64_t)min(j0 + k, p.nch - 1) * p.C);
-#pragma unroll 1
-    for (int k = 0; k < kWalkGroup; ++k) {
-      const int jj = j0 + k;
-      if (jj >= p.nch) break;
-      hs[(int64_t)jj * p.C] = h;
-      const int64_t t0 = (int64_t)jj * p.L;
-      const int rows = (int)((p.T - t0) < p.L ? (p.T - t0) : p.L);
-      h = chunk_compose(h, cur[k], a, rows, p, b, c, t0);
+__global__ void __launch_bounds__(32) chunk_fwd_carry_kernel(const ChunkArgs p) {
+  __shared__ float s_beta[kWin][32];
+  const int lane = threadIdx.x;
+  const int64_t e = (int64_t)blockIdx.x * 32 + lane;
+  const bool live = e < p.B * p.C;
+  const int64_t b = live ? e / p.C : 0, c = live ? e % p.C : 0;
+  const float a = live ? p.a[c] : 0.0f;
+  float h = (live && p.h0) ? p.h0[b * p.C + c] : p.h_init;
+  const float* beta = p.beta + b * p.nch * p.C + c;
+  float* hs = p.hs + b * p.nch * p.C + c;
+  for (int w0 = 0; w0 < p.nch; w0 += kWin) {
+    const int n = min(kWin, p.nch - w0);
+    if (live)
+      for (int k = 0; k < n; ++k) tp_cp_async4(&s_beta[k][lane], beta + (int64_t)(w0 + k) * p.C, 4);
+    tp_cp_async_commit();
+    tp_cp_async_wait<0>();
+    if (live) {
+      for (int k = 0; k < n; ++k) {
+        const int jj = w0 + k;
+        hs[(int64_t)jj * p.C] = h;
+        const int64_t t0 = (int64_t)jj * p.L;
+        const int rows = (int)((p.T - t0) < p.L ? (p.T - t0) : p.L);
+        h = chunk_compose(h, s_beta[k][lane], a, rows, p, b, c, t0);
+      }
     }
+    __syncwarp();
   }
 }
 
@@ -421,84 +427,68 @@ __global__ void __launch_bounds__(kPassThreads) chunk_bwd_kernel(const ChunkArgs
   }
 }
 
-// backward pass B: the exact carry entering every chunk (from the end).  A
-// run of consecutive chunks without a winner passes the carry through all of
-// their gradients in order: one chain over the run's rows, loaded kRowBatch
-// rows at a time (all loads issued before the adds, row indices clamped so
-// that no load is predicated), the entering carry of each chunk of the run
-// recorded as the chain crosses its boundary.  The per-chunk words (winner
-// flags, carries out) do not depend on the walk and are read 16 at a time.
-constexpr int kRowBatch = 64;
+// backward pass B: the exact carry entering every chunk (from the end).  One
+// warp per block, one (b, c) lane per thread.  The per-chunk words (no-winner
+// flag, carry out) do not depend on the walk: a window of up to kWin chunks is
+// copied into shared memory with cp.async before it is walked.  A chunk with
+// no winner passes the carry through all of its gradients in order (one add
+// per step); its rows stream through a two-slot ring of kRing rows in shared
+// memory, the next slot's copies in flight while the current slot is added.
+constexpr int kRing = 32;
 
-__global__ void __launch_bounds__(128) chunk_bwd_carry_kernel(const ChunkArgs p) {
-  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= p.B * p.C) return;
-  const int64_t b = e / p.C, c = e % p.C;
+__global__ void __launch_bounds__(32) chunk_bwd_carry_kernel(const ChunkArgs p) {
+  __shared__ int s_tf[kWin][32];
+  __shared__ float s_co[kWin][32];
+  __shared__ float s_g[2][kRing][32];
+  const int lane = threadIdx.x;
+  const int64_t e = (int64_t)blockIdx.x * 32 + lane;
+  const bool live = e < p.B * p.C;
+  const int64_t b = live ? e / p.C : 0, c = live ? e % p.C : 0;
   const int64_t base = b * p.nch * p.C + c;
   const float* g = p.gh + b * p.T * p.C + c;
   float carry = 0.0f;
-  int j = p.nch - 1;
-  while (j >= 0) {
-    // the next group of chunk words, read together
-    uint8_t tf[kWalkGroup];
-    float co[kWalkGroup];
-#pragma unroll
-    for (int k = 0; k < kWalkGroup; ++k) {
-      const int64_t o = base + (int64_t)max(j - k, 0) * p.C;
-      tf[k] = __ldcg(p.tflag + o);
-      co[k] = __ldcg(p.cout + o);
+  for (int w1 = p.nch; w1 > 0; w1 -= kWin) {          // window of chunks [w0, w1)
+    const int w0 = max(0, w1 - kWin);
+    if (live) {
+      for (int j = w0; j < w1; ++j) {
+        tp_cp_async4(&s_tf[j - w0][lane], p.tflag + base + (int64_t)j * p.C, 4);
+        tp_cp_async4(&s_co[j - w0][lane], p.cout + base + (int64_t)j * p.C, 4);
+      }
     }
-    int k = 0;
-    while (k < kWalkGroup && j - k >= 0) {
-      const int jj = j - k;
-      if (!tf[k]) {
-        p.cin[base + (int64_t)jj * p.C] = carry;
-        carry = co[k];
-        ++k;
+    tp_cp_async_commit();
+    tp_cp_async_wait<0>();
+    if (!live) continue;
+    for (int j = w1 - 1; j >= w0; --j) {
+      p.cin[base + (int64_t)j * p.C] = carry;
+      if (!s_tf[j - w0][lane]) {
+        carry = s_co[j - w0][lane];
         continue;
       }
-      // a run of chunks without a winner: jj down to jlo (may leave the group)
-      int jlo = jj;
-      int kk = k;
-      while (jlo - 1 >= 0) {
-        const bool next = (kk + 1 < kWalkGroup) ? (tf[kk + 1] != 0)
-                                                 : (__ldcg(p.tflag + base +
-                                                           (int64_t)(jlo - 1) * p.C) != 0);
-        if (!next) break;
-        --jlo;
-        ++kk;
-      }
-      p.cin[base + (int64_t)jj * p.C] = carry;
-      const int64_t t_hi = min(p.T, (int64_t)(jj + 1) * p.L) - 1;
-      const int64_t t_lo = (int64_t)jlo * p.L;
-      for (int64_t t = t_hi; t >= t_lo; t -= kRowBatch) {
-        float gv[kRowBatch];
-#pragma unroll
-        for (int q = 0; q < kRowBatch; ++q)
-          gv[q] = __ldg(g + max(t - q, t_lo) * p.C);
-#pragma unroll
-        for (int q = 0; q < kRowBatch; ++q) {
-          const int64_t tq = t - q;
-          if (tq >= t_lo) {
-            carry = gv[q] + carry;
-            // leaving the first row of a chunk of the run: the carry enters
-            // the chunk below
-            if (tq % p.L == 0 && tq > t_lo) p.cin[base + (tq / p.L - 1) * p.C] = carry;
-          }
+      // no winner in chunk j: carry <- g_t + carry for t from its last row down
+      const int64_t t0 = (int64_t)j * p.L;
+      const int rows = (int)((p.T - t0) < p.L ? (p.T - t0) : p.L);
+      const int nb = (rows + kRing - 1) / kRing;
+      auto issue = [&](int bi) {        // ring slot bi & 1 <- rows of batch bi
+        const int top = rows - 1 - bi * kRing;
+        for (int q = 0; q < kRing; ++q)
+          tp_cp_async4(&s_g[bi & 1][q][lane], g + (t0 + max(top - q, 0)) * p.C, 4);
+        tp_cp_async_commit();
+      };
+      issue(0);
+      for (int bi = 0; bi < nb; ++bi) {
+        if (bi + 1 < nb) {
+          issue(bi + 1);
+          tp_cp_async_wait<1>();
+        } else {
+          tp_cp_async_wait<0>();
         }
-      }
-      // continue after the run
-      const int consumed = jj - jlo + 1;
-      k += consumed;
-      if (k >= kWalkGroup) {          // the run left this group: restart below it
-        j = jlo - 1;
-        k = -1;
-        break;
+        const int top = rows - 1 - bi * kRing;
+        const int cnt = min(kRing, top + 1);
+        for (int q = 0; q < cnt; ++q) carry = s_g[bi & 1][q][lane] + carry;
       }
     }
-    if (k >= 0) j -= k;
   }
-  if (p.gh0) p.gh0[b * p.C + c] = carry;
+  if (live && p.gh0) p.gh0[b * p.C + c] = carry;
 }
 
 // ga[c] = sum over b (ascending) of the chunk partials summed in descending
@@ -545,7 +535,7 @@ int64_t scan_chunked_workspace_bytes(int64_t B, int64_t T, int64_t C, int chunk)
   if (B <= 0 || T <= 0 || C <= 0) return 0;
   const int L = chunk > 0 ? chunk : scan_chunk_pick(B, T, C);
   const int64_t plane = B * ceil_div(T, L) * C;
-  return 3 * align256(plane * 4) + align256(plane);
+  return 4 * align256(plane * 4);
 }
 
 static int prepare(ChunkArgs& p, int chunk, void* ws, int64_t ws_bytes) {
@@ -561,14 +551,14 @@ static int prepare(ChunkArgs& p, int chunk, void* ws, int64_t ws_bytes) {
   float* f0 = reinterpret_cast<float*>(w);
   float* f1 = reinterpret_cast<float*>(w + align256(plane * 4));
   float* f2 = reinterpret_cast<float*>(w + 2 * align256(plane * 4));
-  uint8_t* u0 = reinterpret_cast<uint8_t*>(w + 3 * align256(plane * 4));
+  int* i0 = reinterpret_cast<int*>(w + 3 * align256(plane * 4));
   // forward: beta, hs; backward: cout, cin, gap, tflag
   p.beta = f0;
   p.hs = f1;
   p.cout = f0;
   p.cin = f1;
   p.gap = f2;
-  p.tflag = u0;
+  p.tflag = i0;
   return TP_OK;
 }
 
@@ -593,7 +583,6 @@ int launch_scan_fwd_chunked(const ScanArgs& q, int chunk, void* ws, int64_t ws_b
   const int V = v4 ? 4 : 1;
   const int64_t slots = p.B * p.nch * (p.C / V);
   const unsigned g1 = blocks_for(slots, kPassThreads);
-  const unsigned g2 = blocks_for(p.B * p.C, 128);
 #define TP_FWD1(VV, HX) chunk_fwd_kernel<VV, HX, false, false><<<g1, kPassThreads, 0, stream>>>(p)
 #define TP_FWD3(VV, HX, MK) chunk_fwd_kernel<VV, HX, true, MK><<<g1, kPassThreads, 0, stream>>>(p)
   if (v4) {
@@ -602,7 +591,7 @@ int launch_scan_fwd_chunked(const ScanArgs& q, int chunk, void* ws, int64_t ws_b
     if (p.xx) TP_FWD1(1, true); else TP_FWD1(1, false);
   }
   if ((s = launch_status()) != TP_OK) return s;
-  chunk_fwd_carry_kernel<<<g2, 128, 0, stream>>>(p);
+  chunk_fwd_carry_kernel<<<blocks_for(p.B * p.C, 32), 32, 0, stream>>>(p);
   if ((s = launch_status()) != TP_OK) return s;
   const bool mk = p.win != nullptr;
   if (v4) {
@@ -639,7 +628,6 @@ int launch_scan_bwd_chunked(const ScanArgs& q, int chunk, void* ws, int64_t ws_b
   const bool v4 = vec4_ok(p, ptrs, 8);
   const int64_t slots = p.B * p.nch * (p.C / (v4 ? 4 : 1));
   const unsigned g1 = blocks_for(slots, kPassThreads);
-  const unsigned g2 = blocks_for(p.B * p.C, 128);
   const bool hx = !mk && p.xx != nullptr;
 #define TP_BWD(VV, OUT)                                                              \
   do {                                                                               \
@@ -649,7 +637,7 @@ int launch_scan_bwd_chunked(const ScanArgs& q, int chunk, void* ws, int64_t ws_b
   } while (0)
   if (v4) TP_BWD(4, false); else TP_BWD(1, false);
   if ((s = launch_status()) != TP_OK) return s;
-  chunk_bwd_carry_kernel<<<g2, 128, 0, stream>>>(p);
+  chunk_bwd_carry_kernel<<<blocks_for(p.B * p.C, 32), 32, 0, stream>>>(p);
   if ((s = launch_status()) != TP_OK) return s;
   if (v4) TP_BWD(4, true); else TP_BWD(1, true);
 #undef TP_BWD
