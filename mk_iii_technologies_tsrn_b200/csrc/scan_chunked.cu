@@ -262,7 +262,12 @@ __device__ float chunk_compose(float h, float beta, float a, int rows, const Chu
     if (ub < beta) return beta;
   }
   float ch = h;
-  for (int k = 0; k < rows; ++k) ch = a + ch;
+  int k = 0;
+  for (; k + 8 <= rows; k += 8) {        // dependent adds, unrolled
+#pragma unroll
+    for (int q = 0; q < 8; ++q) ch = a + ch;
+  }
+  for (; k < rows; ++k) ch = a + ch;
   if (ch != ch) return ch;
   if (ch > beta) return ch;
   if (ch < beta) return beta;
@@ -283,7 +288,7 @@ __device__ float chunk_compose(float h, float beta, float a, int rows, const Chu
 // the walk: a window of up to kWin of them is copied into shared memory with
 // cp.async (all in flight together) before the dependent composes.
 constexpr int kWin = 128;
-constexpr int kWalkGroup = 16;   // values read together by the ga reduction
+constexpr int kWalkGroup = 64;   // values read together by the ga reduction
 
 __global__ void __launch_bounds__(32) chunk_fwd_carry_kernel(const ChunkArgs p) {
   __shared__ float s_beta[kWin][32];
@@ -429,17 +434,19 @@ __global__ void __launch_bounds__(kPassThreads) chunk_bwd_kernel(const ChunkArgs
 
 // backward pass B: the exact carry entering every chunk (from the end).  One
 // warp per block, one (b, c) lane per thread.  The per-chunk words (no-winner
-// flag, carry out) do not depend on the walk: a window of up to kWin chunks is
+// flag, carry out) do not depend on the walk: a window of up to kBwdWin chunks is
 // copied into shared memory with cp.async before it is walked.  A chunk with
 // no winner passes the carry through all of its gradients in order (one add
 // per step); its rows stream through a two-slot ring of kRing rows in shared
-// memory, the next slot's copies in flight while the current slot is added.
+// memory, up to kSlots - 1 slots' copies in flight while one slot is added.
 constexpr int kRing = 32;
+constexpr int kSlots = 8;
+constexpr int kBwdWin = 64;      // chunk words per window (48 KB of shared memory in all)
 
 __global__ void __launch_bounds__(32) chunk_bwd_carry_kernel(const ChunkArgs p) {
-  __shared__ int s_tf[kWin][32];
-  __shared__ float s_co[kWin][32];
-  __shared__ float s_g[2][kRing][32];
+  __shared__ int s_tf[kBwdWin][32];
+  __shared__ float s_co[kBwdWin][32];
+  __shared__ float s_g[kSlots][kRing][32];
   const int lane = threadIdx.x;
   const int64_t e = (int64_t)blockIdx.x * 32 + lane;
   const bool live = e < p.B * p.C;
@@ -447,8 +454,8 @@ __global__ void __launch_bounds__(32) chunk_bwd_carry_kernel(const ChunkArgs p) 
   const int64_t base = b * p.nch * p.C + c;
   const float* g = p.gh + b * p.T * p.C + c;
   float carry = 0.0f;
-  for (int w1 = p.nch; w1 > 0; w1 -= kWin) {          // window of chunks [w0, w1)
-    const int w0 = max(0, w1 - kWin);
+  for (int w1 = p.nch; w1 > 0; w1 -= kBwdWin) {          // window of chunks [w0, w1)
+    const int w0 = max(0, w1 - kBwdWin);
     if (live) {
       for (int j = w0; j < w1; ++j) {
         tp_cp_async4(&s_tf[j - w0][lane], p.tflag + base + (int64_t)j * p.C, 4);
@@ -468,24 +475,31 @@ __global__ void __launch_bounds__(32) chunk_bwd_carry_kernel(const ChunkArgs p) 
       const int64_t t0 = (int64_t)j * p.L;
       const int rows = (int)((p.T - t0) < p.L ? (p.T - t0) : p.L);
       const int nb = (rows + kRing - 1) / kRing;
-      auto issue = [&](int bi) {        // ring slot bi & 1 <- rows of batch bi
-        const int top = rows - 1 - bi * kRing;
-        for (int q = 0; q < kRing; ++q)
-          tp_cp_async4(&s_g[bi & 1][q][lane], g + (t0 + max(top - q, 0)) * p.C, 4);
+      // ring slot bi % kSlots <- rows of batch bi (one commit group per batch;
+      // batches past the end commit empty groups so that the wait count holds)
+      auto issue = [&](int bi) {
+        if (bi < nb) {
+          const int top = rows - 1 - bi * kRing;
+          for (int q = 0; q < kRing; ++q)
+            tp_cp_async4(&s_g[bi % kSlots][q][lane], g + (t0 + max(top - q, 0)) * p.C, 4);
+        }
         tp_cp_async_commit();
       };
-      issue(0);
+      for (int bi = 0; bi < kSlots - 1; ++bi) issue(bi);
       for (int bi = 0; bi < nb; ++bi) {
-        if (bi + 1 < nb) {
-          issue(bi + 1);
-          tp_cp_async_wait<1>();
-        } else {
-          tp_cp_async_wait<0>();
-        }
+        issue(bi + kSlots - 1);
+        tp_cp_async_wait<kSlots - 1>();       // batch bi has landed
         const int top = rows - 1 - bi * kRing;
         const int cnt = min(kRing, top + 1);
-        for (int q = 0; q < cnt; ++q) carry = s_g[bi & 1][q][lane] + carry;
+        const float* sg = &s_g[bi % kSlots][0][lane];
+        if (cnt == kRing) {
+#pragma unroll
+          for (int q = 0; q < kRing; ++q) carry = sg[q * 32] + carry;
+        } else {
+          for (int q = 0; q < cnt; ++q) carry = sg[q * 32] + carry;
+        }
       }
+      tp_cp_async_wait<0>();
     }
   }
   if (live && p.gh0) p.gh0[b * p.C + c] = carry;
