@@ -56,6 +56,14 @@ namespace {
 #ifndef TP_TMA_SEARCH
 #define TP_TMA_SEARCH 128
 #endif
+// fp32 argmax kernel: TMA ring depth, and whether a dedicated producer warp
+// (rather than compute thread 0, inline) issues the loads
+#ifndef TP_TMA_ARGMAX_STAGES
+#define TP_TMA_ARGMAX_STAGES 3
+#endif
+#ifndef TP_TMA_ARGMAX_PRODUCER
+#define TP_TMA_ARGMAX_PRODUCER 0
+#endif
 #ifndef TP_TMA_CHUNK
 #define TP_TMA_CHUNK 64
 #endif
@@ -71,7 +79,7 @@ constexpr int BK = 32;           // fp32 per TMA row: 128 bytes (one swizzle ato
 // which leaves more of the SM's L1 to the argmax search's global loads (the
 // search re-reads x and w row chunks that neighbouring outputs share).
 template <bool kArgmax>
-constexpr int stages() { return kArgmax ? 3 : 4; }
+constexpr int stages() { return kArgmax ? TP_TMA_ARGMAX_STAGES : 4; }
 constexpr int TILE_BYTES = BM * BK * 4;                                  // 16 KB
 constexpr int STAGE_BYTES = 2 * TILE_BYTES;
 constexpr int SNAP_BYTES = BM * BN * 4;                                  // 64 KB
@@ -101,7 +109,11 @@ struct Cfg {
   // behind the shorter tiles.)
   static constexpr int SEARCH_THREADS = TP_TMA_SEARCH;   // a divisor of BN, multiple of 32
   template <bool kArgmax>
-  static constexpr int threads32() { return kArgmax ? CT + SEARCH_THREADS : THREADS; }
+  static constexpr int threads32() {
+    return kArgmax ? CT + SEARCH_THREADS + (TP_TMA_ARGMAX_PRODUCER ? 32 : 0) : THREADS;
+  }
+  // the argmax kernel's producer warp (when it has one) follows the search warps
+  static constexpr int ARGMAX_PRODUCER_WARP = (CT + SEARCH_THREADS) / 32;
   static constexpr int OUTS = TM * TN;     // outputs per compute thread
   static constexpr int KT_PER_CHUNK = CHUNK / BK;
   static constexpr int64_t MAX_K = (int64_t)CHUNK * 65535;  // 16-bit chunk index
@@ -425,6 +437,16 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
       }
       return;
     }
+  } else if (TP_TMA_ARGMAX_PRODUCER) {
+    if (warp == C::ARGMAX_PRODUCER_WARP) {
+      if (lane == 0) {
+        tp_prefetch_tensormap(&xmap);
+        tp_prefetch_tensormap(&wmap);
+        for (uint32_t j = 0; j < sch_total_kt; ++j)
+          if (!produce(j)) return;
+      }
+      return;
+    }
   } else {
     // thread 0 fills all but one stage now, then one stage per k-tile: at
     // k-tile j it refills the stage of k-tile j-1 with k-tile j+STAGES-1
@@ -441,7 +463,7 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
   const int Mc = (int)p.M, Nc = (int)p.N;
 
   if constexpr (kArgmax) {
-    if (threadIdx.x >= CT) {
+    if (threadIdx.x >= CT && threadIdx.x < CT + C::SEARCH_THREADS) {
       // ---------------------------------------------------- search warpgroup
       // This CTA's finished tiles but the last, each once its raw maxima and
       // chunks are stored; thread sid walks column sid of the tile row by
@@ -549,7 +571,8 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
     for (int kt = kb0; kt < ke0; ++kt, ++it) {
       const uint32_t s = it % STAGES;
       const uint32_t ph = (it / STAGES) & 1u;
-      if (kArgmax && threadIdx.x == 0 && it + STAGES - 1 < sch_total_kt)
+      if (kArgmax && !TP_TMA_ARGMAX_PRODUCER && threadIdx.x == 0 &&
+          it + STAGES - 1 < sch_total_kt)
         if (!produce(it + STAGES - 1)) return;
       if (!tp_mbar_wait(&full[s], ph, p.err)) return;
       const uint32_t xbase = stage_addr + s * STAGE_BYTES;
