@@ -242,6 +242,32 @@ __global__ void __launch_bounds__(kPassThreads) chunk_fwd_kernel(const ChunkArgs
   if (!kOut) stv<V>(p.beta + o, h);
 }
 
+// chain_L(h) = L rounded additions of a, when it can be had in one step:
+// while h and every sum stay inside one binade [2^(e-1), 2^e) (one sign, a
+// spacing of ulp = 2^(e-24) between floats), fl(f + a) = f + m ulp with
+// m = a / ulp rounded to the nearest integer -- unless a / ulp lies exactly
+// halfway, when ties-to-even makes the step depend on f's last bit.  Then
+// chain_L(h) = h + L m ulp exactly.  Returns false (nothing decided) when a
+// condition fails; the caller runs the adds.
+__device__ __forceinline__ bool chain_by_binade(float h, float a, int L, float& out) {
+  if (!isfinite(h) || !isfinite(a) || h == 0.0f) return false;
+  int e;
+  (void)frexpf(h, &e);                       // |h| in [2^(e-1), 2^e)
+  if (e < -100 || e > 100) return false;     // keep ulp and its multiples normal
+  const float ulp = ldexpf(1.0f, e - 24);
+  const float q = a / ulp;                   // exact: a power-of-two scaling
+  const float m = rintf(q);
+  if (fabsf(q - m) == 0.5f) return false;    // a tie: parity-dependent rounding
+  if (fabsf(m) * (float)L >= 8388608.0f) return false;
+  const float end = h + (float)L * m * ulp;  // exact when it stays in the binade
+  const float lo = ldexpf(1.0f, e - 1), hi = ldexpf(1.0f, e);
+  const float mag = fabsf(end);
+  // strictly inside: every exact intermediate sum keeps the binade's spacing
+  if ((end < 0.0f) != (h < 0.0f) || !(mag >= lo + ulp) || !(mag <= hi - ulp)) return false;
+  out = end;
+  return true;
+}
+
 // state after a chunk of `rows` steps entered with h, given the chunk's own
 // state from -inf (beta); exact (see the file comment).
 __device__ float chunk_compose(float h, float beta, float a, int rows, const ChunkArgs& p,
@@ -262,12 +288,15 @@ __device__ float chunk_compose(float h, float beta, float a, int rows, const Chu
     if (ub < beta) return beta;
   }
   float ch = h;
-  int k = 0;
-  for (; k + 8 <= rows; k += 8) {        // dependent adds, unrolled
+  if (!chain_by_binade(h, a, rows, ch)) {
+    ch = h;
+    int k = 0;
+    for (; k + 8 <= rows; k += 8) {      // dependent adds, unrolled
 #pragma unroll
-    for (int q = 0; q < 8; ++q) ch = a + ch;
+      for (int q = 0; q < 8; ++q) ch = a + ch;
+    }
+    for (; k < rows; ++k) ch = a + ch;
   }
-  for (; k < rows; ++k) ch = a + ch;
   if (ch != ch) return ch;
   if (ch > beta) return ch;
   if (ch < beta) return beta;
@@ -480,8 +509,10 @@ __global__ void __launch_bounds__(32) chunk_bwd_carry_kernel(const ChunkArgs p) 
       auto issue = [&](int bi) {
         if (bi < nb) {
           const int top = rows - 1 - bi * kRing;
-          for (int q = 0; q < kRing; ++q)
-            tp_cp_async4(&s_g[bi % kSlots][q][lane], g + (t0 + max(top - q, 0)) * p.C, 4);
+          const float* src = g + (t0 + top) * p.C;     // row top, then upwards
+          float* dst = &s_g[bi % kSlots][0][lane];
+          const int cnt = min(kRing, top + 1);
+          for (int q = 0; q < cnt; ++q, src -= p.C, dst += 32) tp_cp_async4(dst, src, 4);
         }
         tp_cp_async_commit();
       };
@@ -576,8 +607,12 @@ static int prepare(ChunkArgs& p, int chunk, void* ws, int64_t ws_bytes) {
   return TP_OK;
 }
 
+// Four channels per thread (128-bit loads) when that still leaves 32 warps of
+// threads per SM; else one channel per thread, for 4x the threads (at B = 2,
+// C = 1024, 64-step chunks the 4-channel passes filled 11% of the warp slots).
 static bool vec4_ok(const ChunkArgs& p, const void* const* ptrs, int n) {
   if (p.C % 4 != 0) return false;
+  if (p.B * (int64_t)p.nch * (p.C / 4) < (int64_t)num_sms() * 1024) return false;
   for (int i = 0; i < n; ++i)
     if (ptrs[i] && !aligned16(ptrs[i])) return false;
   return true;

@@ -178,3 +178,27 @@ def test_workspace_and_arguments(cuda):
     torch.cuda.synchronize()
     rh, _ = oscan.scan_fwd(b.cpu().numpy(), a.cpu().numpy(), 0.0)
     np.testing.assert_array_equal(h.cpu().numpy(), rh)
+
+
+def test_forward_carry_chains_at_binade_edges(cuda):
+    # inputs that never win (the carry decides every chunk), decays that are
+    # exact half-ulps (ties), fractions of an ulp, and starts just above and
+    # below binade boundaries of both signs: the chunk states come from the
+    # one-step chain (inside a binade) or the step-by-step adds (ties,
+    # crossings), and must equal the recurrence bit for bit either way
+    B, T = 2, 2048
+    a = np.array([-2.0 ** -24, -3 * 2.0 ** -24, -2.0 ** -25, -1e-7, -0.49e-7, 0.0, -1.0,
+                  -2.0 ** -23, 2.0 ** -24, 3e-8, -7.3e-6, -2.0 ** -20], np.float32)
+    C = a.size
+    u = np.full((B, T, C), -np.inf, np.float32)
+    u[1, 700, 3] = 0.5                       # one late winner
+    h0 = np.array([[1.0000001, 2.0 - 2.0 ** -22, 1.5, -1.5, 1e-30, 3.0e38,
+                    1.0, 1.0 + 2.0 ** -22, -2.0 + 2.0 ** -22, 0.75, 1024.0, -0.1],
+                   [2.0 ** -126, -2.0 ** -126, 4.0, 4.0 - 2.0 ** -21, -1.0, 8.0,
+                    0.3, 1.0 - 2.0 ** -24, 5.0, -5.0, 1e-3, 1.0]], np.float32)
+    ops = _ops()
+    for chunk in (32, 64, 256):
+        h, mask = _fwd(ops, u, None, a, 0.0, h0=h0, chunk=chunk)
+        rh, win = oscan.scan_fwd(u, a, 0.0, h0)
+        np.testing.assert_array_equal(h.view(np.uint32), rh.view(np.uint32))
+        np.testing.assert_array_equal(mask, oscan.win_mask_words(win))
