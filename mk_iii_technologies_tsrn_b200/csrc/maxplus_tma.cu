@@ -197,13 +197,28 @@ __device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, 
 }
 
 // acc = max.NaN(acc, x0 + w0, x1 + w1) with both sums from one add.rn.f32x2.
+// Two terms: their sums (each one IEEE-rounded fp32 add) folded into acc by a
+// 3-input NaN-propagating max.  TP_TMA_SCALAR_ADD selects two scalar adds
+// instead of one packed add.f32x2 (same results; a different issue mix).
+#ifndef TP_TMA_SCALAR_ADD
+#define TP_TMA_SCALAR_ADD 0
+#endif
 __device__ __forceinline__ void mp_pair(float& acc, uint64_t xa, uint64_t wb) {
+#if TP_TMA_SCALAR_ADD
+  asm("{\n\t.reg .f32 x0, x1, w0, w1, lo, hi;\n\t"
+      "mov.b64 {x0, x1}, %1;\n\tmov.b64 {w0, w1}, %2;\n\t"
+      "add.rn.f32 lo, x0, w0;\n\tadd.rn.f32 hi, x1, w1;\n\t"
+      "max.NaN.f32 %0, %0, lo, hi;\n\t}"
+      : "+f"(acc)
+      : "l"(xa), "l"(wb));
+#else
   asm("{\n\t.reg .b64 s;\n\t.reg .f32 lo, hi;\n\t"
       "add.rn.f32x2 s, %1, %2;\n\t"
       "mov.b64 {lo, hi}, s;\n\t"
       "max.NaN.f32 %0, %0, lo, hi;\n\t}"
       : "+f"(acc)
       : "l"(xa), "l"(wb));
+#endif
 }
 
 __device__ __forceinline__ void lds128(uint32_t addr, uint64_t& a, uint64_t& b) {

@@ -249,18 +249,24 @@ __global__ void __launch_bounds__(kPassThreads) chunk_fwd_kernel(const ChunkArgs
 // halfway, when ties-to-even makes the step depend on f's last bit.  Then
 // chain_L(h) = h + L m ulp exactly.  Returns false (nothing decided) when a
 // condition fails; the caller runs the adds.
+__device__ __forceinline__ float pow2f(int k) {          // 2^k for -126 <= k <= 127
+  return __int_as_float((k + 127) << 23);
+}
+
 __device__ __forceinline__ bool chain_by_binade(float h, float a, int L, float& out) {
-  if (!isfinite(h) || !isfinite(a) || h == 0.0f) return false;
-  int e;
-  (void)frexpf(h, &e);                       // |h| in [2^(e-1), 2^e)
-  if (e < -100 || e > 100) return false;     // keep ulp and its multiples normal
-  const float ulp = ldexpf(1.0f, e - 24);
-  const float q = a / ulp;                   // exact: a power-of-two scaling
+  const int bits = __float_as_int(h);
+  const int be = (bits >> 23) & 0xff;                    // biased exponent of h
+  // normal h away from both ends of the range (ulp and its multiples stay
+  // normal and finite); excludes 0, subnormals, inf and NaN
+  if (be < 30 || be > 225 || !isfinite(a)) return false;
+  const int e = be - 126;                                // |h| in [2^(e-1), 2^e)
+  const float ulp = pow2f(e - 24);
+  const float q = a * pow2f(24 - e);                     // a / ulp, exact
   const float m = rintf(q);
-  if (fabsf(q - m) == 0.5f) return false;    // a tie: parity-dependent rounding
+  if (fabsf(q - m) == 0.5f) return false;                // a tie: parity-dependent
   if (fabsf(m) * (float)L >= 8388608.0f) return false;
-  const float end = h + (float)L * m * ulp;  // exact when it stays in the binade
-  const float lo = ldexpf(1.0f, e - 1), hi = ldexpf(1.0f, e);
+  const float end = h + (float)L * m * ulp;              // exact inside the binade
+  const float lo = pow2f(e - 1), hi = pow2f(e);
   const float mag = fabsf(end);
   // strictly inside: every exact intermediate sum keeps the binade's spacing
   if ((end < 0.0f) != (h < 0.0f) || !(mag >= lo + ulp) || !(mag <= hi - ulp)) return false;
