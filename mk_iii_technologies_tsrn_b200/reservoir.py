@@ -171,7 +171,10 @@ class EchoStateReservoir(nn.Module):
         U = self.W_in(x)
         Wzh, Wzu = self.W_z.weight.split(dr, dim=1)
         Wrh, Wru = self.W_r.weight.split(dr, dim=1)
-        return U, F.linear(U, Wzu, self.W_z.bias), F.linear(U, Wru, self.W_r.bias), Wzh, Wrh, Ws
+        # both gates' input terms as one GEMM on the stacked input halves
+        Uzr = F.linear(U, torch.cat((Wzu, Wru), dim=0), torch.cat((self.W_z.bias, self.W_r.bias)))
+        Uz, Ur = Uzr.split(dr, dim=-1)
+        return U, Uz.contiguous(), Ur.contiguous(), Wzh, Wrh, Ws
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         U, Uz, Ur, Wzh, Wrh, Ws = self.recurrence_inputs(x)

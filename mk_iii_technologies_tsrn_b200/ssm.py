@@ -2,17 +2,20 @@
 
 Same constructor, parameters and initialisation (``A``, ``B_proj``, ``C_proj``,
 ``gate_B``, ``gate_out``, ``mix``), so reference checkpoints load unchanged.
-Only the scan (research/tsrn_dml.py:961-972) changes: the reference evaluates
+The scan (research/tsrn_dml.py:961-972) changes: the reference evaluates
 ``h_t = max(A_c + h_{t-1}, u_t)`` (h_{-1} = 0, A_c = clamp(A, max=0)) through
 the closed form ``t*A_c + cummax(u - t*A_c)``; here the recurrence itself runs
 as one fused kernel (bit-exact with the sequential recurrence; it differs from
 the closed form by O(T ulp) rounding).  Gradients follow the same argmax path
-(input wins ties, as torch.cummax's last-index rule does).
+(input wins ties, as torch.cummax's last-index rule does).  The three
+projections of the input (gate_B, B_proj, gate_out) run as one GEMM on the
+stacked weights.
 """
 from __future__ import annotations
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 from torch import Tensor
 
 from .ops import tropical_scan
@@ -36,8 +39,14 @@ class TropicalSSM(nn.Module):
         self.mix = nn.Parameter(torch.tensor(0.0))
 
     def forward(self, x: Tensor) -> Tensor:
-        u = torch.sigmoid(self.gate_B(x)) * self.B_proj(x)
+        # the three projections of x (gate_B, B_proj, gate_out) as one GEMM on
+        # the stacked weights; x is read once
+        ds, d = self.ds, x.shape[-1]
+        w = torch.cat((self.gate_B.weight, self.B_proj.weight, self.gate_out.weight), dim=0)
+        b = torch.cat((self.gate_B.bias, self.gate_B.bias.new_zeros(ds), self.gate_out.bias))
+        gb, bp, go = F.linear(x, w, b).split((ds, ds, d), dim=-1)
+        u = torch.sigmoid(gb) * bp
         A_c = self.A.clamp(max=0)
         H = tropical_scan(u.contiguous(), None, A_c, 0.0)
-        out = torch.sigmoid(self.gate_out(x)) * self.C_proj(H)
+        out = torch.sigmoid(go) * self.C_proj(H)
         return torch.sigmoid(self.mix) * out
