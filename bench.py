@@ -5,14 +5,25 @@ Default workload (``--workload gemm``): the fp32 max-plus GEMM with int32 argmax
 at M = N = K = 8192 -- ``y[m,n] = max_k(x[m,k] + W[n,k])`` -- on synthetic
 N(0,1) inputs with 5% of W set to -inf (seeded).  A step is one pass of the hot
 path over the whole problem: at N GPUs each rank computes its output-column
-shard W[r*N/P:(r+1)*N/P] and the shards of y and argmax are all-gathered over
-NCCL (strong scaling: the total problem is fixed).  The metric is max-plus
-Gop/s = 2*M*N*K / step time (one add and one max per term).
+shard W[r*N/P:(r+1)*N/P] and the shards of y and argmax are exchanged (peer
+stores fused into the GEMM epilogue, or NCCL with ``--exchange nccl``; strong
+scaling: the total problem is fixed).  The metric is max-plus Gop/s =
+2*M*N*K / step time (one add and one max per term).  Every run checks the
+result bit for bit against the oracle on sampled rows x the first and last 64
+columns of every rank's range, on every rank, and exits non-zero on a
+mismatch.  The end-to-end number runs the public host entry: ``ops.maxplus_host``
+on one GPU, ``dist.maxplus_host_sharded`` on several (each rank's row block
+of x and its W shard over PCIe, x gathered over NVLink).  The JSON line also
+carries a ``secondary`` list: every workload below measured in the same run.
 
-``--workload scan``: the tropical SSM scan at B=16, T=4096, C=1024 (per rank,
-weak scaling): forward (read b, x; write h: 12 B/elem) plus argmax-path
-backward recomputing the winners (read g, h, b, x; write gu: 20 B/elem);
-metric GB/s of those algorithmic bytes.
+Batch workloads split the configuration's batch over the ranks
+(``--scaling strong``, default; ``--scaling weak`` gives every rank all of it):
+
+``--workload scan``: the tropical SSM scan at B=16, T=4096, C=1024: forward
+(read b, x; write h: 12 B/elem) plus argmax-path backward recomputing the
+winners (read g, h, b, x; write gu: 20 B/elem); metric GB/s of those
+algorithmic bytes.  Few lanes per GPU (B=2 at 8 GPUs) run the chunk-parallel
+scan.
 
 ``--workload linear``: config 1, the tropical linear x [1024,256] (x) W [256,256]
 forward with int32 argmax and the argmax backward; Gop/s of forward ops.
@@ -22,23 +33,22 @@ T=1024, d_h=80, top_k=16, causal) through the fused kernel; tokens/s.
 
 ``--workload esn``: the echo-state reservoir recurrence of config 5's first
 TSRN block (research/tsrn_dml.py:1073: GRU-gated, d_reservoir = d_model / 2 =
-320; B=64, T=1024 per rank) in one fused launch from the input projections to
-the state sequence H; ``--esn-mode leaky`` runs the leaky reservoir of
-tsrn_gpu.py (d_reservoir = d_model = 640) instead.  Metric tokens/s.
+320; B=64, T=1024) in one fused launch from the input projections to the state
+sequence H; ``--esn-mode leaky`` runs the leaky reservoir of tsrn_gpu.py
+(d_reservoir = d_model = 640) instead.  Metric tokens/s.
 
 ``--workload tsrn_block``: config 5's hot path, the tropical branches of the first
 TSRN block (research/tsrn_dml.py:1096-1106: fused top-k attention, GRU reservoir,
 tropical SSM, with their LayerNorms and projections) on B=64 sequences of
 T=1024 tokens, d=640; tokens/s and each branch's share of the step.
 
-Batch workloads (scan, dtn, linear, tsrn_attn, esn, tsrn_block) split the
-configuration's batch over the ranks by default (``--scaling strong``); the
-default GEMM line also carries a ``secondary`` list with each of them measured
-in the same run.
-
 ``--workload dtn``: config 2, the drop-in DTNAttention(256, 8) block
 (tropical Q/K projections with the STE backward, tropical score, Maslov
-softmax) forward + backward at B=128, L=64 per rank; metric tokens/s.
+softmax) forward + backward at B=128, L=64; metric tokens/s.
+
+Every timed region lasts at least 0.6 s (short steps are repeated) so that the
+clock sampler sees it; a kernel's timed-out device-side wait raises after each
+timed region.
 
 ``--dtype bf16`` stores the GEMM operands in bf16 (widened exactly on the GPU;
 the arithmetic stays fp32); with ``--arith bf16`` every sum is rounded to bf16

@@ -49,7 +49,11 @@ namespace tp {
 
 namespace {
 
-constexpr int kRowBlock = 8;     // rows whose loads are issued together
+// rows whose loads are issued together: 8 with four channels per thread
+// (128-bit loads), 16 with one channel per thread (keeps ~100 KB of loads in
+// flight per SM at 40% occupancy)
+template <int V>
+constexpr int row_block() { return V == 4 ? 8 : 16; }
 constexpr int kPassThreads = 128;   // threads per block of the chunk-parallel passes
 
 struct ChunkArgs {
@@ -188,6 +192,7 @@ __global__ void __launch_bounds__(kPassThreads) chunk_fwd_kernel(const ChunkArgs
   const float* pb = p.bb + base;
   const float* px = kHasX ? p.xx + base : nullptr;
   float* ph = kOut ? p.h + base : nullptr;
+  constexpr int kRowBlock = row_block<V>();
   uint32_t bits[V];
 #pragma unroll
   for (int v = 0; v < V; ++v) bits[v] = 0u;
@@ -410,6 +415,7 @@ __global__ void __launch_bounds__(kPassThreads) chunk_bwd_kernel(const ChunkArgs
     }
     if (kOut) stv_stream<V>(p.gu + base + (int64_t)t * p.C, out);
   };
+  constexpr int kRowBlock = row_block<V>();
   int t = s.rows - 1;
   for (; t + 1 >= kRowBlock; t -= kRowBlock) {
     float g[kRowBlock][V], u[kRowBlock][V], hp[kRowBlock][V];
