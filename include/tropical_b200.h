@@ -295,10 +295,17 @@ TP_API int tp_tsrn_attention_prologue(int64_t B, int64_t T, int64_t H, int64_t d
  *    out[i] = sum over {j : S[i,j] >= thr_i} of softmax(S[i,:])_j * V[j]
  *  Q [B,H,T,dh], K and V [B,H,Tkv,dh] contiguous fp32; keys j < Tc are the
  *  cross-window cached keys (positions j - Tc < 0), Tkv = Tc + T when they
- *  are used.  alibi_slopes [H].  dh <= 128, top_k <= 64, Tkv <= 6144.  The
- *  scores match the reference's fp32 log-sum-exp within 1e-5; rows whose
- *  top_k-th and next scores lie within that distance may select differently.
- *  workspace: tp_tsrn_attention_workspace_bytes(...) bytes, 16-byte aligned.
+ *  are used.  alibi_slopes [H].  Two kernels:
+ *    tensor cores (dh <= 96, top_k <= 16, any Tkv): the exp-feature dots as
+ *      3xTF32 tcgen05 MMAs into tensor memory, two passes over the keys;
+ *    CUDA cores (dh <= 128, top_k <= 64, Tkv <= 6144): fp32 FMA dots, the
+ *      score block of 16 rows in shared memory.
+ *  tp_tsrn_attention_set_path selects; the default takes the tensor-core
+ *  kernel whenever the shape allows.  The scores match the reference's fp32
+ *  log-sum-exp within 1e-5; rows whose top_k-th and next scores lie within
+ *  that distance may select differently.
+ *  workspace: tp_tsrn_attention_workspace_bytes(...) bytes (enough for either
+ *  kernel), 16-byte aligned.
  * ======================================================================== */
 TP_API int64_t tp_tsrn_attention_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t Tkv,
                                                  int64_t dh);
@@ -306,6 +313,16 @@ TP_API int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, i
                                  int64_t dh, const float* Q, const float* K, const float* V,
                                  const float* alibi_slopes, int top_k, int causal, float* out,
                                  void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Kernel choice of tp_tsrn_attention_fwd for this process: TP_ATT_PATH_AUTO
+ * (tensor cores where supported, else CUDA cores), TP_ATT_PATH_CUDA_CORES,
+ * or TP_ATT_PATH_TENSOR_CORES (shapes it does not support then return
+ * TP_ERR_UNSUPPORTED).  Stores the previous choice in *previous when it is
+ * not NULL.  (No reference counterpart.) */
+#define TP_ATT_PATH_AUTO 0
+#define TP_ATT_PATH_CUDA_CORES 1
+#define TP_ATT_PATH_TENSOR_CORES 2
+TP_API int tp_tsrn_attention_set_path(int path, int* previous);
 
 /* ======================================================================== *
  *  Echo-state reservoir recurrences, forward (inference), whole sequence in

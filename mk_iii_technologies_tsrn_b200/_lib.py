@@ -141,6 +141,7 @@ SIGNATURES: dict[str, tuple] = {
         [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_int, _c_int,
          _c_p, _c_p, _c_i64, _c_p],
     ),
+    "tp_tsrn_attention_set_path": (_c_int, [_c_int, _c_p]),
     "tp_maslov_softmax_fwd": (
         _c_int,
         [_c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64,
@@ -166,6 +167,9 @@ TP_BWD_STE = 1
 TP_BWD_LSE = 2
 TP_DEVERR_BARRIER_TIMEOUT = 1
 TP_DEVERR_FLAG_TIMEOUT = 2
+TP_ATT_PATH_AUTO = 0
+TP_ATT_PATH_CUDA_CORES = 1
+TP_ATT_PATH_TENSOR_CORES = 2
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

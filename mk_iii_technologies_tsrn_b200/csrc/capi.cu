@@ -553,6 +553,15 @@ int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t 
                                        causal, out, (float*)workspace, as_stream(stream));
 }
 
+int tp_tsrn_attention_set_path(int path, int* previous) {
+  TP_RETURN_IF(path != TP_ATT_PATH_AUTO && path != TP_ATT_PATH_CUDA_CORES &&
+                   path != TP_ATT_PATH_TENSOR_CORES,
+               TP_ERR_INVALID_ARG);
+  if (previous) *previous = tp::tsrn_attention_path();
+  tp::tsrn_attention_path() = path;
+  return TP_OK;
+}
+
 int tp_esn_gru_fwd(int64_t B, int64_t T, int64_t dr, const float* U, const float* Uz,
                    const float* Ur, const float* Wzh, int64_t ld_wzh, const float* Wrh,
                    int64_t ld_wrh, const float* Ws, int64_t ld_ws, float* H, void* stream) {

@@ -208,6 +208,14 @@ int launch_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int6
                               const float* slopes, int top_k, int causal, float* out,
                               float* ws, cudaStream_t stream);
 
+// tsrn_attention_tc.cu: the same forward with the score contraction on tcgen05
+int& tsrn_attention_path();   // TP_ATT_PATH_*
+bool tsrn_attention_tc_supported(int64_t dh, int top_k);
+int64_t tsrn_attention_tc_workspace_floats(int64_t B, int64_t H, int64_t T, int64_t Tkv);
+int launch_tsrn_attention_tc(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc, int64_t dh,
+                             const float* Q, const float* K, const float* V, const float* slopes,
+                             int top_k, int causal, float* out, float* ws, cudaStream_t stream);
+
 // tsrn_prologue.cu: QK LayerNorm + rotary embedding + head-major layout of Q/K/V
 int launch_tsrn_prologue(int64_t B, int64_t T, int64_t H, int64_t dh, const float* qkv, int64_t ld,
                          int64_t koff, int64_t voff, const float* qg, const float* qb,

@@ -523,8 +523,13 @@ static inline int64_t round4(int64_t n) { return (n + 3) & ~(int64_t)3; }
 
 // workspace: query features, query maxima, key features, key maxima; each
 // region starts on a 16-byte boundary
+// (the larger of this kernel's and the tensor-core kernel's, so that one
+// workspace serves whichever path runs)
 int64_t tsrn_attention_workspace_floats(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t dh) {
-  return round4(B * H * T * dh) + round4(B * H * T) + round4(B * H * Tkv * dh) + round4(B * H * Tkv);
+  const int64_t cc =
+      round4(B * H * T * dh) + round4(B * H * T) + round4(B * H * Tkv * dh) + round4(B * H * Tkv);
+  const int64_t tc = tsrn_attention_tc_workspace_floats(B, H, T, Tkv);
+  return cc > tc ? cc : tc;
 }
 
 int launch_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc, int64_t dh,
@@ -532,6 +537,14 @@ int launch_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int6
                               const float* slopes, int top_k, int causal, float* out,
                               float* ws, cudaStream_t stream) {
   if (B * H * T == 0) return TP_OK;
+  const int path = tsrn_attention_path();
+  const bool tc_ok = tsrn_attention_tc_supported(dh, top_k);
+  if (path == TP_ATT_PATH_TENSOR_CORES && !tc_ok) return TP_ERR_UNSUPPORTED;
+  if (tc_ok && path != TP_ATT_PATH_CUDA_CORES) {
+    if (Tc < 0 || Tc > Tkv || Tkv < 1) return TP_ERR_INVALID_ARG;
+    return launch_tsrn_attention_tc(B, H, T, Tkv, Tc, dh, Q, K, V, slopes, top_k, causal, out, ws,
+                                    stream);
+  }
   if (dh < 1 || dh > ATT_MAX_DH || top_k < 1 || top_k > ATT_MAX_TOPK) return TP_ERR_UNSUPPORTED;
   if (Tkv < 1 || Tkv > ATT_MAX_TKV) return TP_ERR_UNSUPPORTED;
   if (Tc < 0 || Tc > Tkv) return TP_ERR_INVALID_ARG;

@@ -1,0 +1,583 @@
+// tsrn_attention_tc.cu -- the fused TSRN tropical top-k attention forward
+// (research/tsrn_dml.py:438-460 score, :509-524 ALiBi / causal mask / top-k /
+// softmax / V) with the score contraction on the 5th-generation tensor cores.
+//
+// The log-sum-exp over channels factorises into a dot product of exp features
+// (each in (0, 1]; see tsrn_attention.cu):
+//   S[i,j] = log( F_Q[i,:] . F_K[j,:] ) + qmax_i + kmax_j - slope_h |i - (j - Tc)|
+// so the scores of a 128-query tile against a 64-key tile are one 128 x 64
+// GEMM with K = dh.  fp32 accuracy from TF32 operands by the 3xTF32 split:
+// F = hi + lo with hi = F with its low 13 mantissa bits cleared (exact in
+// TF32) and lo = F - hi (exact in fp32; its TF32 rounding costs ~2^-22 of F),
+//   F_Q . F_K ~= hi_Q . hi_K + hi_Q . lo_K + lo_Q . hi_K
+// (the dropped lo . lo term is below 2^-22 of the product): three
+// tcgen05.mma kind::tf32 chains into one fp32 accumulator in tensor memory.
+//
+// Pre-pass: one warp per row writes hi and lo as row-major [rows_pad, 96]
+// planes (channels past dh and rows past the sequence are zero) plus the row
+// maxima.  Main kernel: one CTA per (b, h, 128-query tile), 6 warps:
+//   warp 0   TMA producer: the query tile once (hi, lo: 96 KB), then key tiles
+//            (hi, lo: 48 KB) through a 2-stage ring; 128-byte swizzle, the
+//            K-major layout tcgen05 reads;
+//   warp 1   allocates 128 TMEM columns and issues the MMAs of each key tile
+//            (M = 128, N = 64, K = 8 per instruction) into one of two
+//            64-column accumulators; tcgen05.commit frees the key stage and
+//            publishes the accumulator;
+//   warps 2-5 one query row per thread (TMEM lane = row): tcgen05.ld the 64
+//            scores of the tile, release the accumulator, finish the scores.
+// Selection in two passes over the key tiles:
+//   pass 1 (tiles nearest the diagonal first) keeps each row's 16 largest
+//          scores (a sorted register list, NaN never enters): rowmax = the
+//          first, thr = the top_k-th, ties counted as torch.topk counts them;
+//   pass 2 recomputes the same MMAs (same operands, same order: the same
+//          bits) and lists the kept keys {j : !(S < thr), S != -inf}, with
+//          the softmax normaliser, in shared memory (ascending j).
+// Then each warp gathers the V rows of its 32 rows' kept keys (lanes split
+// the channels).  A row with more than TC_KCAP kept keys (ties at the
+// threshold) accumulates its V rows itself into the output.
+// A dot below 1e-30 is recomputed exactly from the raw rows, as in the
+// CUDA-core kernel.
+#include "maxplus_internal.cuh"
+
+namespace tp {
+
+namespace {
+
+constexpr int TC_M = 128;           // query rows per CTA = TMEM lanes
+constexpr int TC_N = 64;            // keys per tile = accumulator columns
+constexpr int TC_KP = 96;           // feature channels, padded: 3 swizzle atoms
+constexpr int TC_ATOM = 32;         // fp32 channels per 128-byte swizzled row
+constexpr int TC_LIST = 16;         // per-row score list (top_k <= 16)
+constexpr int TC_KCAP = 24;         // kept keys listed per row in shared memory
+constexpr int TC_THREADS = 192;
+constexpr int TC_TMEM_COLS = 128;   // two accumulators of TC_N columns
+constexpr int TC_MAX_DH = 96;
+
+constexpr uint32_t TC_Q_ATOM_FLOATS = TC_M * TC_ATOM;     // 16 KB
+constexpr uint32_t TC_K_ATOM_FLOATS = TC_N * TC_ATOM;     // 8 KB
+constexpr uint32_t TC_Q_BYTES = 2 * 3 * TC_Q_ATOM_FLOATS * 4;   // hi + lo
+constexpr uint32_t TC_K_STAGE_BYTES = 2 * 3 * TC_K_ATOM_FLOATS * 4;
+constexpr size_t TC_SMEM_BYTES = 1024                          // alignment slack
+                                 + TC_Q_BYTES + 2 * TC_K_STAGE_BYTES
+                                 + (size_t)TC_KCAP * TC_M * 8  // kept lists (j, S)
+                                 + (size_t)TC_M * 8            // per-row count, normaliser
+                                 + 16 * 8;                     // barriers, TMEM address, flags
+
+// instruction descriptor of tcgen05.mma kind::tf32: fp32 accumulator, TF32 A
+// and B, both K-major, N = TC_N, M = TC_M
+constexpr uint32_t TC_IDESC = (1u << 4) | (2u << 7) | (2u << 10) |
+                              ((uint32_t)(TC_N >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+
+// shared-memory matrix descriptor: K-major, 128-byte swizzle (8-row groups
+// 1024 bytes apart), descriptor version 1
+__device__ __forceinline__ uint64_t tc_desc(const float* p) {
+  const uint32_t a = tp_smem_addr(p);
+  return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(TC_IDESC), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   tp_smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 consecutive accumulator columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tc_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// pre-pass: exp features split into TF32 hi / lo planes [S][rows_pad][96]
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) att_tc_feat_kernel(const float* __restrict__ X,
+                                                          int64_t rows, int64_t rows_pad, int dh,
+                                                          float* __restrict__ Fhi,
+                                                          float* __restrict__ Flo,
+                                                          float* __restrict__ mx,
+                                                          int64_t mx_ld) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t slice = blockIdx.y;
+  const int64_t r = (int64_t)blockIdx.x * 8 + warp;
+  if (r >= rows_pad) return;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  const bool live = r < rows;
+  const float* xr = X + (slice * rows + (live ? r : 0)) * dh;
+  float v[3];
+  float m = NEG_INF;
+#pragma unroll
+  for (int u = 0; u < 3; ++u) {
+    const int c = lane + 32 * u;
+    v[u] = (live && c < dh) ? xr[c] : NEG_INF;
+    m = fmaxf(m, v[u]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const int64_t o = (slice * rows_pad + r) * TC_KP;
+#pragma unroll
+  for (int u = 0; u < 3; ++u) {
+    const int c = lane + 32 * u;
+    const float f = (live && c < dh) ? expf(v[u] - m) : 0.0f;
+    const float hi = __uint_as_float(__float_as_uint(f) & 0xffffe000u);
+    Fhi[o + c] = hi;
+    Flo[o + c] = f - hi;
+  }
+  if (lane == 0 && r < mx_ld) mx[slice * mx_ld + r] = live ? m : 0.0f;
+}
+
+struct TcArgs {
+  int64_t S, H, T, Tkv, Tc;
+  int64_t Tp, Kp;         // query rows / keys per slice in the feature planes
+  int dh, top_k, causal, nk;
+  const float* Q;
+  const float* K;
+  const float* V;
+  const float* slopes;
+  const float* qmx;       // [S][T]
+  const float* kmx;       // [S][Kp]
+  float* out;             // [S][T][dh]
+  int* err;
+};
+
+// the score of row i against key j from the accumulated dot d -- the same
+// expression in both passes, so both see the same bits
+__device__ __forceinline__ float tc_score(float d, int64_t i, int64_t j, float qm, float km,
+                                          float slope, const TcArgs& p, int64_t slice) {
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  float s;
+  if (d >= 1e-30f) {
+    s = __fadd_rn(__fadd_rn(__logf(d), qm), km);
+  } else {
+    // exact max-shifted log-sum-exp from the raw rows (rare)
+    const float* qr = p.Q + (slice * p.T + i) * p.dh;
+    const float* kr = p.K + (slice * p.Tkv + j) * p.dh;
+    float m = NEG_INF;
+    for (int c = 0; c < p.dh; ++c) m = fmaxf(m, qr[c] + kr[c]);
+    float z = 0.0f;
+    if (m > NEG_INF)
+      for (int c = 0; c < p.dh; ++c) z += expf(qr[c] + kr[c] - m);
+    s = (m > NEG_INF) ? m + logf(z) : NEG_INF;
+  }
+  const float dist = fabsf((float)(i - (j - p.Tc)));
+  return __fmaf_rn(-slope, dist, s);
+}
+
+// insert s into the descending list L (drops the smallest); s > L[TC_LIST-1]
+__device__ __forceinline__ void tc_insert(float (&L)[TC_LIST], float s) {
+#pragma unroll
+  for (int k = TC_LIST - 1; k >= 1; --k) L[k] = fmaxf(L[k], fminf(L[k - 1], s));
+  L[0] = fmaxf(L[0], s);
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    att_tc_kernel(const __grid_constant__ CUtensorMap map_qh,
+                  const __grid_constant__ CUtensorMap map_ql,
+                  const __grid_constant__ CUtensorMap map_kh,
+                  const __grid_constant__ CUtensorMap map_kl, const TcArgs p) {
+  extern __shared__ uint8_t tc_raw[];
+  float* sQ = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) &
+                                       ~(uintptr_t)1023);
+  float* sK = sQ + 2 * 3 * TC_Q_ATOM_FLOATS;                       // [stage][hi/lo][atom]
+  int* s_kj = reinterpret_cast<int*>(sK + 2 * 2 * 3 * TC_K_ATOM_FLOATS);   // [TC_KCAP][TC_M]
+  float* s_ks = reinterpret_cast<float*>(s_kj + TC_KCAP * TC_M);          // [TC_KCAP][TC_M]
+  int* s_cnt = reinterpret_cast<int*>(s_ks + TC_KCAP * TC_M);             // [TC_M]
+  float* s_z = reinterpret_cast<float*>(s_cnt + TC_M);                    // [TC_M]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_z + TC_M);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;        // [2]
+  uint64_t* k_empty = bars + 3;       // [2]
+  uint64_t* acc_full = bars + 5;      // [2]
+  uint64_t* acc_empty = bars + 7;     // [2]
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 9);
+  int* s_flag = reinterpret_cast<int*>(bars + 10);     // [1]: a bounded wait gave up
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t nqt = p.Tp / TC_M;
+  const int64_t cta = blockIdx.x;
+  const int64_t qt = nqt - 1 - cta / p.S;                // heaviest (causal) tiles first
+  const int64_t slice = cta % p.S;
+  const int64_t i0 = qt * TC_M;
+  int64_t kv_end = p.Tkv;
+  if (p.causal) {
+    const int64_t last = (i0 + TC_M - 1 < p.T) ? i0 + TC_M - 1 : p.T - 1;
+    kv_end = last + p.Tc + 1 < p.Tkv ? last + p.Tc + 1 : p.Tkv;
+  }
+  const int nt = (int)((kv_end + TC_N - 1) / TC_N);
+
+  if (threadIdx.x == 0) {
+    tp_mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      tp_mbar_init(&k_full[s], 1);
+      tp_mbar_init(&k_empty[s], 1);
+      tp_mbar_init(&acc_full[s], 1);
+      tp_mbar_init(&acc_empty[s], 4);
+    }
+    s_flag[0] = 0;
+    s_flag[1] = 0;
+    tp_fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     tp_smem_addr(s_tmem)),
+                 "r"(TC_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  // epilogue state (warps 2-5): row r of the tile
+  const int quarter = warp & 3;
+  const int r = quarter * 32 + lane;
+  const int64_t i = i0 + r;
+  const bool row_ok = warp >= 2 && i < p.T;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  const float slope = p.slopes[slice % p.H];
+  const float qm = row_ok ? p.qmx[slice * p.T + i] : 0.0f;
+  // keys this row may see: j < jlim
+  int64_t jlim = p.Tkv;
+  if (p.causal) jlim = (i + p.Tc + 1 < p.Tkv) ? i + p.Tc + 1 : p.Tkv;
+  float L[TC_LIST];
+#pragma unroll
+  for (int k = 0; k < TC_LIST; ++k) L[k] = NEG_INF;
+  float thr = NEG_INF, rowmax = NEG_INF, z = 0.0f;
+  int cnt = 0;
+  bool serial = false;              // more than TC_KCAP kept keys: accumulate into out
+  float* orow = p.out + (slice * p.T + (row_ok ? i : 0)) * p.dh;
+  const float* Vs = p.V + slice * p.Tkv * p.dh;
+
+  // the producer and MMA threads remember what they issued last, so that an
+  // aborted CTA can wait for its own copies and MMAs before it exits
+  int last_load = -1, last_mma = -1;
+
+  for (int round = 0; round < 2; ++round) {
+    if (round == 1) {
+      __syncthreads();
+      if (s_flag[1] != 0) break;
+    }
+    const int it0 = round * nt;
+    if (warp == 0) {
+      if (lane == 0 && s_flag[1] == 0) {
+        if (round == 0) {
+          tp_prefetch_tensormap(&map_qh);
+          tp_prefetch_tensormap(&map_ql);
+          tp_prefetch_tensormap(&map_kh);
+          tp_prefetch_tensormap(&map_kl);
+          tp_mbar_arrive_expect_tx(q_full, TC_Q_BYTES);
+          const int32_t y = (int32_t)(slice * p.Tp + i0);
+          for (int a = 0; a < 3; ++a) {
+            tp_tma_load_2d(sQ + a * TC_Q_ATOM_FLOATS, &map_qh, a * TC_ATOM, y, q_full);
+            tp_tma_load_2d(sQ + (3 + a) * TC_Q_ATOM_FLOATS, &map_ql, a * TC_ATOM, y, q_full);
+          }
+        }
+        for (int n = 0; n < nt; ++n) {
+          const int it = it0 + n, st = it & 1, use = it >> 1;
+          const int t = round == 0 ? nt - 1 - n : n;
+          if (!tp_mbar_wait(&k_empty[st], (use & 1) ^ 1, p.err)) {
+            s_flag[1] = 1;
+            break;
+          }
+          tp_mbar_arrive_expect_tx(&k_full[st], TC_K_STAGE_BYTES);
+          const int32_t y = (int32_t)(slice * p.Kp + (int64_t)t * TC_N);
+          float* dst = sK + st * 2 * 3 * TC_K_ATOM_FLOATS;
+          for (int a = 0; a < 3; ++a) {
+            tp_tma_load_2d(dst + a * TC_K_ATOM_FLOATS, &map_kh, a * TC_ATOM, y, &k_full[st]);
+            tp_tma_load_2d(dst + (3 + a) * TC_K_ATOM_FLOATS, &map_kl, a * TC_ATOM, y,
+                           &k_full[st]);
+          }
+          last_load = it;
+        }
+      }
+      __syncwarp();
+    } else if (warp == 1) {
+      if (lane == 0 && s_flag[1] == 0) {
+        bool ok = round == 1 || tp_mbar_wait(q_full, 0, p.err);
+        if (!ok) s_flag[1] = 1;
+        for (int n = 0; ok && n < nt; ++n) {
+          const int it = it0 + n, st = it & 1, use = it >> 1;
+          if (!tp_mbar_wait(&acc_empty[st], (use & 1) ^ 1, p.err) ||
+              !tp_mbar_wait(&k_full[st], use & 1, p.err)) {
+            s_flag[1] = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + (uint32_t)(st * TC_N);
+          const float* kb = sK + st * 2 * 3 * TC_K_ATOM_FLOATS;
+          uint32_t acc = 0;
+          // hi.hi, hi.lo, lo.hi
+#pragma unroll 1
+          for (int prod = 0; prod < 3; ++prod) {
+            const float* qa = sQ + (prod == 2 ? 3 : 0) * TC_Q_ATOM_FLOATS;
+            const float* kbb = kb + (prod == 1 ? 3 : 0) * TC_K_ATOM_FLOATS;
+            for (int ks = 0; ks < p.nk; ++ks) {
+              const int a = ks >> 2, kk = (ks & 3) * 8;
+              tc_mma(d, tc_desc(qa + a * TC_Q_ATOM_FLOATS + kk),
+                     tc_desc(kbb + a * TC_K_ATOM_FLOATS + kk), acc);
+              acc = 1;
+            }
+          }
+          tc_commit(&k_empty[st]);
+          tc_commit(&acc_full[st]);
+          last_mma = it;
+        }
+      }
+      __syncwarp();
+    } else {
+      // ---- scores: one row per thread
+      for (int n = 0; n < nt; ++n) {
+        const int it = it0 + n, st = it & 1, use = it >> 1;
+        const int t = round == 0 ? nt - 1 - n : n;
+        // the whole warp leaves together (tcgen05.ld is warp-collective)
+        const bool got = tp_mbar_wait(&acc_full[st], use & 1, p.err);
+        if (!__all_sync(0xffffffffu, got)) {
+          s_flag[1] = 1;
+          break;
+        }
+        tc_fence_after();
+        uint32_t v0[32], v1[32];
+        const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(st * TC_N);
+        tc_ld32(ta, v0);
+        tc_ld32(ta + 32, v1);
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tp_mbar_arrive(&acc_empty[st]);
+        const int64_t j0 = (int64_t)t * TC_N;
+        const float km0 = p.kmx[slice * p.Kp + j0 + lane];
+        const float km1 = p.kmx[slice * p.Kp + j0 + 32 + lane];
+        auto one = [&](int c, uint32_t bits) {
+          const int64_t j = j0 + c;
+          const float km = __shfl_sync(0xffffffffu, c < 32 ? km0 : km1, c & 31);
+          float s = NEG_INF;
+          if (row_ok && j < jlim) s = tc_score(__uint_as_float(bits), i, j, qm, km, slope, p, slice);
+          if (round == 0) {
+            if (__any_sync(0xffffffffu, s > L[TC_LIST - 1]))
+              if (s > L[TC_LIST - 1]) tc_insert(L, s);
+          } else if (!(s < thr) && s != NEG_INF) {
+            const float e = expf(s - rowmax);
+            z += e;
+            if (!serial && cnt < TC_KCAP) {
+              s_kj[cnt * TC_M + r] = (int)j;
+              s_ks[cnt * TC_M + r] = s;
+            } else {
+              if (!serial) {
+                // overflow: accumulate the listed keys, then this one, into
+                // the output row (normalised at the end)
+                serial = true;
+                for (int c2 = 0; c2 < p.dh; ++c2) orow[c2] = 0.0f;
+                for (int e2 = 0; e2 < TC_KCAP; ++e2) {
+                  const float w2 = expf(s_ks[e2 * TC_M + r] - rowmax);
+                  const float* vr = Vs + (int64_t)s_kj[e2 * TC_M + r] * p.dh;
+                  for (int c2 = 0; c2 < p.dh; ++c2) orow[c2] = fmaf(w2, vr[c2], orow[c2]);
+                }
+              }
+              const float* vr = Vs + j * p.dh;
+              for (int c2 = 0; c2 < p.dh; ++c2) orow[c2] = fmaf(e, vr[c2], orow[c2]);
+            }
+            ++cnt;
+          }
+        };
+#pragma unroll
+        for (int c = 0; c < 32; ++c) one(c, v0[c]);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) one(32 + c, v1[c]);
+      }
+      if (round == 0) {
+        rowmax = L[0];
+        thr = L[0];
+#pragma unroll
+        for (int k = 1; k < TC_LIST; ++k)
+          if (k < p.top_k) thr = L[k];
+      }
+    }
+  }
+
+  // ---- gather: each warp forms the outputs of its 32 rows (lanes split the
+  // channels), from the kept-key lists
+  if (warp >= 2 && s_flag[1] == 0) {
+    if (row_ok) {
+      s_cnt[r] = serial ? -1 : cnt;
+      s_z[r] = z;
+    }
+    __syncwarp();
+    for (int rr = 0; rr < 32; ++rr) {
+      const int row = quarter * 32 + rr;
+      const int64_t ii = i0 + row;
+      if (ii >= p.T) break;
+      const int n = s_cnt[row];
+      const float rmax = __shfl_sync(0xffffffffu, rowmax, rr);
+      const float invz = 1.0f / s_z[row];
+      float* orr = p.out + (slice * p.T + ii) * p.dh;
+      if (n < 0) {
+        // listed and accumulated by the row's own thread: normalise
+        __syncwarp();
+        for (int c = lane; c < p.dh; c += 32) orr[c] = orr[c] * invz;
+        continue;
+      }
+      float oacc[3] = {0.0f, 0.0f, 0.0f};
+      for (int e0 = 0; e0 < n; e0 += 4) {
+        int jj[4];
+        float wv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const bool ok = e0 + e < n;
+          jj[e] = ok ? s_kj[(e0 + e) * TC_M + row] : -1;
+          wv[e] = ok ? expf(s_ks[(e0 + e) * TC_M + row] - rmax) * invz : 0.0f;
+        }
+        float val[4][3];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+#pragma unroll
+          for (int q = 0; q < 3; ++q) {
+            const int c = lane + 32 * q;
+            val[e][q] = (jj[e] >= 0 && c < p.dh) ? __ldg(Vs + (int64_t)jj[e] * p.dh + c) : 0.0f;
+          }
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (jj[e] >= 0)
+#pragma unroll
+            for (int q = 0; q < 3; ++q) oacc[q] = fmaf(wv[e], val[e][q], oacc[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < 3; ++q) {
+        const int c = lane + 32 * q;
+        if (c < p.dh) orr[c] = oacc[q];
+      }
+    }
+  }
+
+  // ---- teardown: an aborted CTA first waits (bounded) for its own copies and
+  // MMAs in flight; then TMEM is released
+  if (warp == 0 && lane == 0 && last_load >= 0) {
+    for (int it = last_load; it >= 0 && it > last_load - 2; --it)
+      tp_mbar_wait(&k_full[it & 1], (it >> 1) & 1, p.err);
+  }
+  if (warp == 1 && lane == 0 && last_mma >= 0)
+    tp_mbar_wait(&acc_full[last_mma & 1], (last_mma >> 1) & 1, p.err);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(TC_TMEM_COLS)
+                 : "memory");
+  }
+}
+
+bool make_feat_map(CUtensorMap* map, const float* base, int64_t rows, uint32_t box_rows) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)TC_KP, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)TC_KP * 4};
+  cuuint32_t box[2] = {(cuuint32_t)TC_ATOM, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+inline int64_t round64(int64_t n) { return (n + 63) & ~(int64_t)63; }
+
+struct TcLayout {
+  int64_t Tp, Kp;
+  int64_t qhi, qlo, khi, klo, qmx, kmx, total;   // float offsets
+};
+
+TcLayout tc_layout(int64_t B, int64_t H, int64_t T, int64_t Tkv) {
+  TcLayout l;
+  const int64_t S = B * H;
+  l.Tp = ceil_div(T, TC_M) * TC_M;
+  l.Kp = ceil_div(Tkv, TC_N) * TC_N;
+  l.qhi = 0;
+  l.qlo = l.qhi + round64(S * l.Tp * TC_KP);
+  l.khi = l.qlo + round64(S * l.Tp * TC_KP);
+  l.klo = l.khi + round64(S * l.Kp * TC_KP);
+  l.qmx = l.klo + round64(S * l.Kp * TC_KP);
+  l.kmx = l.qmx + round64(S * T);
+  l.total = l.kmx + round64(S * l.Kp);
+  return l;
+}
+
+}  // namespace
+
+int& tsrn_attention_path() {
+  static int mode = TP_ATT_PATH_AUTO;
+  return mode;
+}
+
+bool tsrn_attention_tc_supported(int64_t dh, int top_k) {
+  return dh >= 1 && dh <= TC_MAX_DH && top_k >= 1 && top_k <= TC_LIST;
+}
+
+int64_t tsrn_attention_tc_workspace_floats(int64_t B, int64_t H, int64_t T, int64_t Tkv) {
+  return tc_layout(B, H, T, Tkv).total;
+}
+
+int launch_tsrn_attention_tc(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc, int64_t dh,
+                             const float* Q, const float* K, const float* V, const float* slopes,
+                             int top_k, int causal, float* out, float* ws, cudaStream_t stream) {
+  const TcLayout l = tc_layout(B, H, T, Tkv);
+  const int64_t S = B * H;
+  if (S * (l.Tp > l.Kp ? l.Tp : l.Kp) >= ((int64_t)1 << 31)) return TP_ERR_TOO_LARGE;
+  if (S * (l.Tp / TC_M) >= ((int64_t)1 << 31)) return TP_ERR_TOO_LARGE;
+  if (S > 65535) return TP_ERR_TOO_LARGE;
+  float* qhi = ws + l.qhi;
+  float* qlo = ws + l.qlo;
+  float* khi = ws + l.khi;
+  float* klo = ws + l.klo;
+  float* qmx = ws + l.qmx;
+  float* kmx = ws + l.kmx;
+  att_tc_feat_kernel<<<dim3((unsigned)ceil_div(l.Tp, 8), (unsigned)S), 256, 0, stream>>>(
+      Q, T, l.Tp, (int)dh, qhi, qlo, qmx, T);
+  att_tc_feat_kernel<<<dim3((unsigned)ceil_div(l.Kp, 8), (unsigned)S), 256, 0, stream>>>(
+      K, Tkv, l.Kp, (int)dh, khi, klo, kmx, l.Kp);
+  int s = launch_status();
+  if (s != TP_OK) return s;
+  CUtensorMap mqh, mql, mkh, mkl;
+  if (!make_feat_map(&mqh, qhi, S * l.Tp, TC_M) || !make_feat_map(&mql, qlo, S * l.Tp, TC_M) ||
+      !make_feat_map(&mkh, khi, S * l.Kp, TC_N) || !make_feat_map(&mkl, klo, S * l.Kp, TC_N))
+    return TP_ERR_UNSUPPORTED;
+  TcArgs a{S, H, T, Tkv, Tc, l.Tp, l.Kp, (int)dh, top_k, causal, (int)ceil_div(dh, 8),
+           Q, K, V, slopes, qmx, kmx, out, device_error_ptr()};
+  cudaError_t e = cudaFuncSetAttribute(att_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)TC_SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_status(e);
+  att_tc_kernel<<<(unsigned)(S * (l.Tp / TC_M)), TC_THREADS, TC_SMEM_BYTES, stream>>>(mqh, mql, mkh,
+                                                                                     mkl, a);
+  return launch_status();
+}
+
+}  // namespace tp

@@ -788,6 +788,22 @@ def _attention_shapes(Q, K, V, slopes):
         raise ValueError("slopes must be [H]")
 
 
+ATTENTION_PATHS = {"auto": 0, "cuda_cores": 1, "tensor_cores": 2}
+
+
+def set_attention_path(path: str) -> str:
+    """Kernel of the fused TSRN attention for this process: ``"auto"`` (the
+    tcgen05 kernel where the shape allows -- dh <= 96, top_k <= 16 -- else the
+    CUDA-core kernel), ``"cuda_cores"`` or ``"tensor_cores"``.  Returns the
+    previous choice."""
+    if path not in ATTENTION_PATHS:
+        raise ValueError(f"path must be one of {sorted(ATTENTION_PATHS)}, got {path!r}")
+    prev = ctypes.c_int(0)
+    _lib.check(_lib.load().tp_tsrn_attention_set_path(ATTENTION_PATHS[path], ctypes.byref(prev)),
+               "tp_tsrn_attention_set_path")
+    return {v: k for k, v in ATTENTION_PATHS.items()}[prev.value]
+
+
 def tsrn_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, slopes: torch.Tensor,
                    top_k: int, causal: bool = True, Tc: int = 0) -> torch.Tensor:
     """Fused TSRN tropical top-k attention forward (research/tsrn_dml.py:462-548 after RoPE):

@@ -139,3 +139,25 @@ def test_chunked_scan_validates_on_the_host():
                                    None, 0, None) == -2
     assert lib.tp_scan_bwd_chunked(2, 64, 8, None, None, None, None, 0.0, None, None, None,
                                    None, None, None, 32, None, 0, None) == -2
+
+
+def test_attention_path_selector_and_workspace():
+    from mk_iii_technologies_tsrn_b200 import _lib
+    lib = _lib.load()
+    prev = ctypes.c_int(-1)
+    assert lib.tp_tsrn_attention_set_path(3, None) == -1
+    assert lib.tp_tsrn_attention_set_path(-1, None) == -1
+    assert lib.tp_tsrn_attention_set_path(_lib.TP_ATT_PATH_CUDA_CORES, ctypes.byref(prev)) == 0
+    assert prev.value == _lib.TP_ATT_PATH_AUTO
+    assert lib.tp_tsrn_attention_set_path(_lib.TP_ATT_PATH_AUTO, ctypes.byref(prev)) == 0
+    assert prev.value == _lib.TP_ATT_PATH_CUDA_CORES
+    # the workspace covers the tensor-core kernel's padded hi/lo feature planes
+    # (128-row query tiles, 64-key tiles, 96 channels) as well as the CUDA-core
+    # kernel's transposed features
+    B, H, T, Tkv, dh = 2, 3, 200, 260, 80
+    tp, kp = 256, 320
+    tc_floats = 2 * B * H * tp * 96 + 2 * B * H * kp * 96 + B * H * T + B * H * kp
+    assert lib.tp_tsrn_attention_workspace_bytes(B, H, T, Tkv, dh) >= 4 * tc_floats
+    cc_floats = B * H * (T + Tkv) * (dh + 1)
+    assert lib.tp_tsrn_attention_workspace_bytes(1, 1, 8, 8, 128) >= 4 * 16 * 129
+    assert lib.tp_tsrn_attention_workspace_bytes(B, H, T, Tkv, dh) >= 4 * cc_floats
