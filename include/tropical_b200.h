@@ -300,8 +300,9 @@ TP_API int tp_tsrn_attention_prologue(int64_t B, int64_t T, int64_t H, int64_t d
  *      3xTF32 tcgen05 MMAs into tensor memory, two passes over the keys;
  *    CUDA cores (dh <= 128, top_k <= 64, Tkv <= 6144): fp32 FMA dots, the
  *      score block of 16 rows in shared memory.
- *  tp_tsrn_attention_set_path selects; the default takes the tensor-core
- *  kernel whenever the shape allows.  The scores match the reference's fp32
+ *  tp_tsrn_attention_set_path selects; the default takes the CUDA-core
+ *  kernel wherever its limits allow and the tensor-core kernel beyond them
+ *  (Tkv > 6144).  The scores match the reference's fp32
  *  log-sum-exp within 1e-5; rows whose top_k-th and next scores lie within
  *  that distance may select differently.
  *  workspace: tp_tsrn_attention_workspace_bytes(...) bytes (enough for either
@@ -315,7 +316,7 @@ TP_API int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, i
                                  void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Kernel choice of tp_tsrn_attention_fwd for this process: TP_ATT_PATH_AUTO
- * (tensor cores where supported, else CUDA cores), TP_ATT_PATH_CUDA_CORES,
+ * (CUDA cores within their limits, else tensor cores), TP_ATT_PATH_CUDA_CORES,
  * or TP_ATT_PATH_TENSOR_CORES (shapes it does not support then return
  * TP_ERR_UNSUPPORTED).  Stores the previous choice in *previous when it is
  * not NULL.  (No reference counterpart.) */

@@ -793,9 +793,9 @@ ATTENTION_PATHS = {"auto": 0, "cuda_cores": 1, "tensor_cores": 2}
 
 def set_attention_path(path: str) -> str:
     """Kernel of the fused TSRN attention for this process: ``"auto"`` (the
-    tcgen05 kernel where the shape allows -- dh <= 96, top_k <= 16 -- else the
-    CUDA-core kernel), ``"cuda_cores"`` or ``"tensor_cores"``.  Returns the
-    previous choice."""
+    CUDA-core kernel within its limits -- dh <= 128, top_k <= 64, Tkv <= 6144 --
+    else the tcgen05 kernel, which takes dh <= 96, top_k <= 16 and any Tkv),
+    ``"cuda_cores"`` or ``"tensor_cores"``.  Returns the previous choice."""
     if path not in ATTENTION_PATHS:
         raise ValueError(f"path must be one of {sorted(ATTENTION_PATHS)}, got {path!r}")
     prev = ctypes.c_int(0)

@@ -82,6 +82,8 @@ def test_long_cached_keys_beyond_the_cuda_core_limit(cuda, path):
     path("cuda_cores")
     with pytest.raises(RuntimeError):
         _run(cuda, Q, K, V, slopes, top_k, True, Tc)
+    path("auto")                         # beyond the CUDA-core limit auto takes tensor cores
+    np.testing.assert_array_equal(_run(cuda, Q, K, V, slopes, top_k, True, Tc), out)
 
 
 @pytest.mark.parametrize("causal", [True, False])
