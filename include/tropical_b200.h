@@ -300,9 +300,9 @@ TP_API int tp_tsrn_attention_prologue(int64_t B, int64_t T, int64_t H, int64_t d
  *      3xTF32 tcgen05 MMAs into tensor memory, two passes over the keys;
  *    CUDA cores (dh <= 128, top_k <= 64, Tkv <= 6144): fp32 FMA dots, the
  *      score block of 16 rows in shared memory.
- *  tp_tsrn_attention_set_path selects; the default takes the CUDA-core
- *  kernel wherever its limits allow and the tensor-core kernel beyond them
- *  (Tkv > 6144).  The scores match the reference's fp32
+ *  tp_tsrn_attention_set_path selects; the default takes the tensor-core
+ *  kernel where it applies and T >= 128, else the CUDA-core kernel (and
+ *  tensor cores again beyond the CUDA-core limits).  The scores match the reference's fp32
  *  log-sum-exp within 1e-5; rows whose top_k-th and next scores lie within
  *  that distance may select differently.
  *  workspace: tp_tsrn_attention_workspace_bytes(...) bytes (enough for either
@@ -316,7 +316,8 @@ TP_API int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, i
                                  void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Kernel choice of tp_tsrn_attention_fwd for this process: TP_ATT_PATH_AUTO
- * (CUDA cores within their limits, else tensor cores), TP_ATT_PATH_CUDA_CORES,
+ * (tensor cores where supported and T >= 128, else CUDA cores within their
+ * limits, else tensor cores), TP_ATT_PATH_CUDA_CORES,
  * or TP_ATT_PATH_TENSOR_CORES (shapes it does not support then return
  * TP_ERR_UNSUPPORTED).  Stores the previous choice in *previous when it is
  * not NULL.  (No reference counterpart.) */
@@ -371,6 +372,32 @@ TP_API int tp_esn_leaky_fwd_seg(int64_t B, int64_t T, int64_t t_stride, int64_t 
                                 const float* U, const float* Ws, int64_t ld_ws,
                                 const float* leak, const float* h0, int64_t ld_h0, float* H,
                                 void* stream);
+
+/* Backward through time of both recurrences (training), one launch each:
+ * the reverse-time loops of reservoir autograd (research/tsrn_dml.py:834-840
+ * and tsrn_gpu.py:480-484 differentiated), with the per-step factors formed
+ * beforehand for all steps.  g = 0 after the last step; for t = T-1 .. 0:
+ *   GRU (tp_esn_gru_bwd):   dh = dH_t + g;  dAh_t = dh fa_t;
+ *     dm = dAh_t Ws;  dAr_t = dm fr_t;  dAz_t = dh fz_t;
+ *     g = dh keep_t + dm r_t + dAz_t Wzh + dAr_t Wrh
+ *   with fa = z (1 - h~^2), fz = (h~ - h_{t-1}) z (1 - z),
+ *   fr = h_{t-1} r (1 - r), keep = 1 - z and r the reset gate; dAh, dAz, dAr
+ *   are the gradients of the pre-activations of h~, z and r.
+ *   leaky (tp_esn_leaky_bwd): dh = dH_t + g;  dA_t = dh fa_t;
+ *     g = dh (1 - lk) + dA_t Ws;  dHs_t = dh   (fa = lk (1 - s^2)).
+ * Weights are passed TRANSPOSED (WzhT = Wzh^T etc., [dr, dr], row stride
+ * ld >= dr).  All [B, T, dr] tensors contiguous fp32.  Same cluster layout,
+ * limits and bounded waits as the forward; matches the reference loop
+ * within fp32 rounding of the dot products.  (No reference counterpart: the
+ * reference differentiates its Python loop with autograd.) */
+TP_API int tp_esn_gru_bwd(int64_t B, int64_t T, int64_t dr, const float* dH, const float* fa,
+                          const float* fz, const float* fr, const float* keep, const float* r,
+                          const float* WzhT, int64_t ld_wz, const float* WrhT, int64_t ld_wr,
+                          const float* WsT, int64_t ld_ws, float* dAh, float* dAz, float* dAr,
+                          void* stream);
+TP_API int tp_esn_leaky_bwd(int64_t B, int64_t T, int64_t dr, const float* dH, const float* fa,
+                            const float* WsT, int64_t ld_ws, const float* leak, float* dA,
+                            float* dHs, void* stream);
 
 /* Copy `rows` rows of width_bytes from src (row pitch src_pitch bytes) to dst
  * (pitch dst_pitch), host or device memory on either side (pinned host memory

@@ -540,11 +540,14 @@ int launch_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int6
   const int path = tsrn_attention_path();
   const bool tc_ok = tsrn_attention_tc_supported(dh, top_k);
   if (path == TP_ATT_PATH_TENSOR_CORES && !tc_ok) return TP_ERR_UNSUPPORTED;
-  // auto: the CUDA-core kernel wherever its limits allow (it measured faster
-  // at the model's shapes), the tensor-core kernel for longer key ranges
+  // auto: the tensor-core kernel where it applies and its 128-query tiles
+  // are filled (T >= 128; at B = 64, T = 1024, dh = 80 it measured 3.27 ms
+  // against 5.16 ms on CUDA cores), else the CUDA-core kernel (16-row tiles),
+  // and the tensor-core kernel again beyond the CUDA-core key limit
   const bool cc_ok = dh >= 1 && dh <= ATT_MAX_DH && top_k >= 1 && top_k <= ATT_MAX_TOPK &&
                      Tkv >= 1 && Tkv <= ATT_MAX_TKV;
-  if (tc_ok && (path == TP_ATT_PATH_TENSOR_CORES || (path == TP_ATT_PATH_AUTO && !cc_ok))) {
+  const bool auto_tc = T >= 128 || !cc_ok;
+  if (tc_ok && (path == TP_ATT_PATH_TENSOR_CORES || (path == TP_ATT_PATH_AUTO && auto_tc))) {
     if (Tc < 0 || Tc > Tkv || Tkv < 1) return TP_ERR_INVALID_ARG;
     return launch_tsrn_attention_tc(B, H, T, Tkv, Tc, dh, Q, K, V, slopes, top_k, causal, out, ws,
                                     stream);

@@ -15,7 +15,7 @@
 //
 // Pre-pass: one warp per row writes hi and lo as row-major [rows_pad, 96]
 // planes (channels past dh and rows past the sequence are zero) plus the row
-// maxima.  Main kernel: one CTA per (b, h, 128-query tile), 6 warps:
+// maxima.  Main kernel: one CTA per (b, h, 128-query tile), 10 warps:
 //   warp 0   TMA producer: the query tile once (hi, lo: 96 KB), then key tiles
 //            (hi, lo: 48 KB) through a 2-stage ring; 128-byte swizzle, the
 //            K-major layout tcgen05 reads;
@@ -23,20 +23,27 @@
 //            (M = 128, N = 64, K = 8 per instruction) into one of two
 //            64-column accumulators; tcgen05.commit frees the key stage and
 //            publishes the accumulator;
-//   warps 2-5 one query row per thread (TMEM lane = row): tcgen05.ld the 64
-//            scores of the tile, release the accumulator, finish the scores.
+//   warps 2-9 two threads per query row (TMEM lane = row; a warp reads the
+//            lanes of its quarter, warp % 4): the thread of half h takes the
+//            tile's columns 2c + h (interleaved, so that keys clustered near
+//            the diagonal split evenly), tcgen05.ld's the 64 scores, releases
+//            the accumulator and finishes its 32.
 // Selection in two passes over the key tiles:
-//   pass 1 (tiles nearest the diagonal first) keeps each row's 16 largest
-//          scores (a sorted register list, NaN never enters): rowmax = the
+//   pass 1 (tiles nearest the diagonal first): each thread keeps the 16
+//          largest of its scores (a sorted register list, NaN never enters);
+//          the two lists of a row are merged in shared memory: rowmax = the
 //          first, thr = the top_k-th, ties counted as torch.topk counts them;
 //   pass 2 recomputes the same MMAs (same operands, same order: the same
-//          bits) and lists the kept keys {j : !(S < thr), S != -inf}, with
-//          the softmax normaliser, in shared memory (ascending j).
-// Then each warp gathers the V rows of its 32 rows' kept keys (lanes split
-// the channels).  A row with more than TC_KCAP kept keys (ties at the
-// threshold) accumulates its V rows itself into the output.
+//          bits) and lists each half's kept keys {j : !(S < thr), S != -inf}
+//          (ascending j) with its part of the softmax normaliser in shared
+//          memory.
+// Then each warp gathers the V rows of 16 rows' kept keys (lanes split the
+// channels).  Kept keys beyond a half's TC_KCAP list entries (ties at the
+// threshold) are accumulated by their thread into a scratch row -- the
+// output row for half 0, the CTA's own (already consumed) query-feature row
+// for half 1 -- and added in by the gather.
 // A dot below 1e-30 is recomputed exactly from the raw rows, as in the
-// CUDA-core kernel.
+// CUDA-core kernel (out of line: rare).
 #include "maxplus_internal.cuh"
 
 namespace tp {
@@ -47,9 +54,10 @@ constexpr int TC_M = 128;           // query rows per CTA = TMEM lanes
 constexpr int TC_N = 64;            // keys per tile = accumulator columns
 constexpr int TC_KP = 96;           // feature channels, padded: 3 swizzle atoms
 constexpr int TC_ATOM = 32;         // fp32 channels per 128-byte swizzled row
-constexpr int TC_LIST = 16;         // per-row score list (top_k <= 16)
-constexpr int TC_KCAP = 24;         // kept keys listed per row in shared memory
-constexpr int TC_THREADS = 192;
+constexpr int TC_LIST = 16;         // per-thread score list (top_k <= 16)
+constexpr int TC_KCAP = 12;         // kept keys listed per row half in shared memory
+constexpr int TC_EPI_WARPS = 8;     // two per TMEM lane quarter
+constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
 constexpr int TC_TMEM_COLS = 128;   // two accumulators of TC_N columns
 constexpr int TC_MAX_DH = 96;
 
@@ -57,10 +65,12 @@ constexpr uint32_t TC_Q_ATOM_FLOATS = TC_M * TC_ATOM;     // 16 KB
 constexpr uint32_t TC_K_ATOM_FLOATS = TC_N * TC_ATOM;     // 8 KB
 constexpr uint32_t TC_Q_BYTES = 2 * 3 * TC_Q_ATOM_FLOATS * 4;   // hi + lo
 constexpr uint32_t TC_K_STAGE_BYTES = 2 * 3 * TC_K_ATOM_FLOATS * 4;
+constexpr size_t TC_LIST_BYTES = (size_t)2 * TC_KCAP * TC_M * 8;   // kept lists (j, S) per half
+static_assert((size_t)2 * TC_LIST * TC_M * 4 <= TC_LIST_BYTES,
+              "pass-1 score lists are merged in the kept-list space");
 constexpr size_t TC_SMEM_BYTES = 1024                          // alignment slack
-                                 + TC_Q_BYTES + 2 * TC_K_STAGE_BYTES
-                                 + (size_t)TC_KCAP * TC_M * 8  // kept lists (j, S)
-                                 + (size_t)TC_M * 8            // per-row count, normaliser
+                                 + TC_Q_BYTES + 2 * TC_K_STAGE_BYTES + TC_LIST_BYTES
+                                 + (size_t)TC_M * 4 * 5        // counts, normalisers, row max
                                  + 16 * 8;                     // barriers, TMEM address, flags
 
 // instruction descriptor of tcgen05.mma kind::tf32: fp32 accumulator, TF32 A
@@ -166,30 +176,20 @@ struct TcArgs {
   const float* qmx;       // [S][T]
   const float* kmx;       // [S][Kp]
   float* out;             // [S][T][dh]
+  float* qlo;             // [S][Tp][TC_KP]: query-feature lo plane (overflow scratch of half 1)
   int* err;
 };
 
-// the score of row i against key j from the accumulated dot d -- the same
-// expression in both passes, so both see the same bits
-__device__ __forceinline__ float tc_score(float d, int64_t i, int64_t j, float qm, float km,
-                                          float slope, const TcArgs& p, int64_t slice) {
+// exact max-shifted log-sum-exp of query row i and key j from the raw rows,
+// for dots below 1e-30 (out of line: rare)
+__device__ __noinline__ float tc_exact_lse(const float* qr, const float* kr, int dh) {
   const float NEG_INF = -__int_as_float(0x7f800000);
-  float s;
-  if (d >= 1e-30f) {
-    s = __fadd_rn(__fadd_rn(__logf(d), qm), km);
-  } else {
-    // exact max-shifted log-sum-exp from the raw rows (rare)
-    const float* qr = p.Q + (slice * p.T + i) * p.dh;
-    const float* kr = p.K + (slice * p.Tkv + j) * p.dh;
-    float m = NEG_INF;
-    for (int c = 0; c < p.dh; ++c) m = fmaxf(m, qr[c] + kr[c]);
-    float z = 0.0f;
-    if (m > NEG_INF)
-      for (int c = 0; c < p.dh; ++c) z += expf(qr[c] + kr[c] - m);
-    s = (m > NEG_INF) ? m + logf(z) : NEG_INF;
-  }
-  const float dist = fabsf((float)(i - (j - p.Tc)));
-  return __fmaf_rn(-slope, dist, s);
+  float m = NEG_INF;
+  for (int c = 0; c < dh; ++c) m = fmaxf(m, qr[c] + kr[c]);
+  float z = 0.0f;
+  if (m > NEG_INF)
+    for (int c = 0; c < dh; ++c) z += expf(qr[c] + kr[c] - m);
+  return (m > NEG_INF) ? m + logf(z) : NEG_INF;
 }
 
 // insert s into the descending list L (drops the smallest); s > L[TC_LIST-1]
@@ -197,6 +197,17 @@ __device__ __forceinline__ void tc_insert(float (&L)[TC_LIST], float s) {
 #pragma unroll
   for (int k = TC_LIST - 1; k >= 1; --k) L[k] = fmaxf(L[k], fminf(L[k - 1], s));
   L[0] = fmaxf(L[0], s);
+}
+
+// a kept key beyond the half's list: weight e times V row j into the
+// scratch row (zeroed at the first such key)
+__device__ __noinline__ void tc_overflow_add(float* dst, bool first, float e, const float* vr,
+                                             int dh) {
+  for (int c = 0; c < dh; ++c) dst[c] = fmaf(e, vr[c], first ? 0.0f : dst[c]);
+}
+
+__device__ __forceinline__ void tc_epi_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * TC_EPI_WARPS) : "memory");
 }
 
 __global__ void __launch_bounds__(TC_THREADS, 1)
@@ -208,11 +219,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   float* sQ = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) &
                                        ~(uintptr_t)1023);
   float* sK = sQ + 2 * 3 * TC_Q_ATOM_FLOATS;                       // [stage][hi/lo][atom]
-  int* s_kj = reinterpret_cast<int*>(sK + 2 * 2 * 3 * TC_K_ATOM_FLOATS);   // [TC_KCAP][TC_M]
-  float* s_ks = reinterpret_cast<float*>(s_kj + TC_KCAP * TC_M);          // [TC_KCAP][TC_M]
-  int* s_cnt = reinterpret_cast<int*>(s_ks + TC_KCAP * TC_M);             // [TC_M]
-  float* s_z = reinterpret_cast<float*>(s_cnt + TC_M);                    // [TC_M]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_z + TC_M);
+  uint8_t* lists = reinterpret_cast<uint8_t*>(sK + 2 * 2 * 3 * TC_K_ATOM_FLOATS);
+  int* s_kj = reinterpret_cast<int*>(lists);                       // [half][TC_KCAP][TC_M]
+  float* s_ks = reinterpret_cast<float*>(s_kj + 2 * TC_KCAP * TC_M);   // [half][TC_KCAP][TC_M]
+  float* s_lst = reinterpret_cast<float*>(lists);                  // pass 1: [half][TC_LIST][TC_M]
+  int* s_cnt = reinterpret_cast<int*>(lists + TC_LIST_BYTES);      // [half][TC_M]
+  float* s_z = reinterpret_cast<float*>(s_cnt + 2 * TC_M);         // [half][TC_M]
+  float* s_rmax = s_z + 2 * TC_M;                                  // [TC_M]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_rmax + TC_M);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;        // [2]
   uint64_t* k_empty = bars + 3;       // [2]
@@ -226,13 +240,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int64_t cta = blockIdx.x;
   const int64_t qt = nqt - 1 - cta / p.S;                // heaviest (causal) tiles first
   const int64_t slice = cta % p.S;
-  const int64_t i0 = qt * TC_M;
-  int64_t kv_end = p.Tkv;
+  const int i0 = (int)(qt * TC_M);
+  int kv_end = (int)p.Tkv;
   if (p.causal) {
-    const int64_t last = (i0 + TC_M - 1 < p.T) ? i0 + TC_M - 1 : p.T - 1;
-    kv_end = last + p.Tc + 1 < p.Tkv ? last + p.Tc + 1 : p.Tkv;
+    const int last = (i0 + TC_M - 1 < p.T) ? i0 + TC_M - 1 : (int)p.T - 1;
+    kv_end = last + (int)p.Tc + 1 < p.Tkv ? last + (int)p.Tc + 1 : (int)p.Tkv;
   }
-  const int nt = (int)((kv_end + TC_N - 1) / TC_N);
+  const int nt = (kv_end + TC_N - 1) / TC_N;
 
   if (threadIdx.x == 0) {
     tp_mbar_init(q_full, 1);
@@ -240,7 +254,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tp_mbar_init(&k_full[s], 1);
       tp_mbar_init(&k_empty[s], 1);
       tp_mbar_init(&acc_full[s], 1);
-      tp_mbar_init(&acc_empty[s], 4);
+      tp_mbar_init(&acc_empty[s], TC_EPI_WARPS);
     }
     s_flag[0] = 0;
     s_flag[1] = 0;
@@ -258,24 +272,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
-  // epilogue state (warps 2-5): row r of the tile
+  // epilogue state (warps 2-9): row r of the tile, columns 2c + half of each key tile
   const int quarter = warp & 3;
+  const int half = (warp - 2) >> 2;
   const int r = quarter * 32 + lane;
-  const int64_t i = i0 + r;
+  const int i = i0 + r;
   const bool row_ok = warp >= 2 && i < p.T;
   const float NEG_INF = -__int_as_float(0x7f800000);
   const float slope = p.slopes[slice % p.H];
   const float qm = row_ok ? p.qmx[slice * p.T + i] : 0.0f;
   // keys this row may see: j < jlim
-  int64_t jlim = p.Tkv;
-  if (p.causal) jlim = (i + p.Tc + 1 < p.Tkv) ? i + p.Tc + 1 : p.Tkv;
+  int jlim = (int)p.Tkv;
+  if (p.causal) jlim = (i + (int)p.Tc + 1 < p.Tkv) ? i + (int)p.Tc + 1 : (int)p.Tkv;
   float L[TC_LIST];
 #pragma unroll
   for (int k = 0; k < TC_LIST; ++k) L[k] = NEG_INF;
   float thr = NEG_INF, rowmax = NEG_INF, z = 0.0f;
   int cnt = 0;
-  bool serial = false;              // more than TC_KCAP kept keys: accumulate into out
-  float* orow = p.out + (slice * p.T + (row_ok ? i : 0)) * p.dh;
+  // scratch row of this thread's kept keys beyond its list
+  float* ovf_row = half == 0 ? p.out + (slice * p.T + (row_ok ? i : 0)) * p.dh
+                             : p.qlo + (slice * p.Tp + i0 + r) * TC_KP;
   const float* Vs = p.V + slice * p.Tkv * p.dh;
 
   // the producer and MMA threads remember what they issued last, so that an
@@ -355,10 +371,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       __syncwarp();
     } else {
-      // ---- scores: one row per thread
+      // ---- scores: two threads per row, 32 interleaved columns each per tile
+      float kmn0 = 0.0f, kmn1 = 0.0f;   // key maxima of the next tile (prefetched)
+      {
+        const int t = round == 0 ? nt - 1 : 0;
+        kmn0 = p.kmx[slice * p.Kp + t * TC_N + lane];
+        kmn1 = p.kmx[slice * p.Kp + t * TC_N + 32 + lane];
+      }
       for (int n = 0; n < nt; ++n) {
         const int it = it0 + n, st = it & 1, use = it >> 1;
         const int t = round == 0 ? nt - 1 - n : n;
+        const float km0 = kmn0, km1 = kmn1;
+        if (n + 1 < nt) {
+          const int tn = round == 0 ? t - 1 : t + 1;
+          kmn0 = p.kmx[slice * p.Kp + tn * TC_N + lane];
+          kmn1 = p.kmx[slice * p.Kp + tn * TC_N + 32 + lane];
+        }
         // the whole warp leaves together (tcgen05.ld is warp-collective)
         const bool got = tp_mbar_wait(&acc_full[st], use & 1, p.err);
         if (!__all_sync(0xffffffffu, got)) {
@@ -366,114 +394,169 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           break;
         }
         tc_fence_after();
-        uint32_t v0[32], v1[32];
+        const int j0 = t * TC_N;
+        // all 32 scores first (independent: the compiler can overlap them);
+        // dots below 1e-30 (or NaN) are marked and recomputed exactly below.
+        // The tile's two 32-column halves are read one after the other.
+        float sc[32];
+        uint32_t slow = 0;
+        const float fbase = (float)(i - j0 - half + (int)p.Tc);   // i - j for cc = 0
         const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(st * TC_N);
-        tc_ld32(ta, v0);
-        tc_ld32(ta + 32, v1);
-        tc_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tp_mbar_arrive(&acc_empty[st]);
-        const int64_t j0 = (int64_t)t * TC_N;
-        const float km0 = p.kmx[slice * p.Kp + j0 + lane];
-        const float km1 = p.kmx[slice * p.Kp + j0 + 32 + lane];
-        auto one = [&](int c, uint32_t bits) {
-          const int64_t j = j0 + c;
-          const float km = __shfl_sync(0xffffffffu, c < 32 ? km0 : km1, c & 31);
-          float s = NEG_INF;
-          if (row_ok && j < jlim) s = tc_score(__uint_as_float(bits), i, j, qm, km, slope, p, slice);
-          if (round == 0) {
-            if (__any_sync(0xffffffffu, s > L[TC_LIST - 1]))
-              if (s > L[TC_LIST - 1]) tc_insert(L, s);
-          } else if (!(s < thr) && s != NEG_INF) {
-            const float e = expf(s - rowmax);
-            z += e;
-            if (!serial && cnt < TC_KCAP) {
-              s_kj[cnt * TC_M + r] = (int)j;
-              s_ks[cnt * TC_M + r] = s;
-            } else {
-              if (!serial) {
-                // overflow: accumulate the listed keys, then this one, into
-                // the output row (normalised at the end)
-                serial = true;
-                for (int c2 = 0; c2 < p.dh; ++c2) orow[c2] = 0.0f;
-                for (int e2 = 0; e2 < TC_KCAP; ++e2) {
-                  const float w2 = expf(s_ks[e2 * TC_M + r] - rowmax);
-                  const float* vr = Vs + (int64_t)s_kj[e2 * TC_M + r] * p.dh;
-                  for (int c2 = 0; c2 < p.dh; ++c2) orow[c2] = fmaf(w2, vr[c2], orow[c2]);
-                }
-              }
-              const float* vr = Vs + j * p.dh;
-              for (int c2 = 0; c2 < p.dh; ++c2) orow[c2] = fmaf(e, vr[c2], orow[c2]);
-            }
-            ++cnt;
+#pragma unroll
+        for (int hv = 0; hv < 2; ++hv) {
+          uint32_t v[32];
+          tc_ld32(ta + 32 * hv, v);
+          tc_wait_ld();
+          if (hv == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tp_mbar_arrive(&acc_empty[st]);
           }
-        };
+          const float km = hv == 0 ? km0 : km1;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) one(c, v0[c]);
+          for (int q = 0; q < 16; ++q) {
+            const int cc = 16 * hv + q;
+            const int c = 2 * cc + half;
+            const float kmc = __shfl_sync(0xffffffffu, km, c & 31);
+            const float d = __uint_as_float(half ? v[2 * q + 1] : v[2 * q]);
+            const bool valid = row_ok && j0 + c < jlim;
+            float l2;
+            asm("lg2.approx.f32 %0, %1;" : "=f"(l2) : "f"(d));
+            const float s0 = __fadd_rn(__fadd_rn(__fmul_rn(l2, 0.6931471805599453f), qm), kmc);
+            const float dist = fabsf(fbase - (float)(2 * cc));
+            if (valid && !(d >= 1e-30f)) slow |= 1u << cc;
+            sc[cc] = valid ? __fmaf_rn(-slope, dist, s0) : NEG_INF;
+          }
+        }
+        if (__any_sync(0xffffffffu, slow != 0)) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) one(32 + c, v1[c]);
+          for (int cc = 0; cc < 32; ++cc)
+            if ((slow >> cc) & 1u) {
+              const int j = j0 + 2 * cc + half;
+              const float e = tc_exact_lse(p.Q + (slice * p.T + i) * p.dh,
+                                           p.K + (slice * p.Tkv + j) * p.dh, p.dh);
+              sc[cc] = __fmaf_rn(-slope, fabsf(fbase - (float)(2 * cc)), e);
+            }
+        }
+        if (round == 0) {
+          // candidates against the list's last entry before this tile (it only
+          // grows, so no later candidate is missed); columns where no lane
+          // has one are skipped with a warp-uniform branch
+          const float l15 = L[TC_LIST - 1];
+          uint32_t cand = 0;
+#pragma unroll
+          for (int cc = 0; cc < 32; ++cc) cand |= (sc[cc] > l15 ? 1u : 0u) << cc;
+          const uint32_t wm = __reduce_or_sync(0xffffffffu, cand);
+          if (wm != 0) {
+#pragma unroll
+            for (int cc = 0; cc < 32; ++cc)
+              if ((wm >> cc) & 1u)
+                if (sc[cc] > L[TC_LIST - 1]) tc_insert(L, sc[cc]);
+          }
+        } else {
+          uint32_t kept = 0;
+#pragma unroll
+          for (int cc = 0; cc < 32; ++cc)
+            kept |= ((!(sc[cc] < thr) && sc[cc] != NEG_INF) ? 1u : 0u) << cc;
+          const uint32_t wm = __reduce_or_sync(0xffffffffu, kept);
+          if (wm != 0) {
+#pragma unroll
+            for (int cc = 0; cc < 32; ++cc)
+              if (((wm >> cc) & 1u) && ((kept >> cc) & 1u)) {
+                const int j = j0 + 2 * cc + half;
+                const float e = expf(sc[cc] - rowmax);
+                z += e;
+                if (cnt < TC_KCAP) {
+                  s_kj[(half * TC_KCAP + cnt) * TC_M + r] = j;
+                  s_ks[(half * TC_KCAP + cnt) * TC_M + r] = sc[cc];
+                } else {
+                  tc_overflow_add(ovf_row, cnt == TC_KCAP, e, Vs + (int64_t)j * p.dh, p.dh);
+                }
+                ++cnt;
+              }
+          }
+        }
       }
       if (round == 0) {
-        rowmax = L[0];
-        thr = L[0];
+        // merge the row's two lists: rowmax and the top_k-th largest
 #pragma unroll
-        for (int k = 1; k < TC_LIST; ++k)
-          if (k < p.top_k) thr = L[k];
+        for (int k = 0; k < TC_LIST; ++k) s_lst[(half * TC_LIST + k) * TC_M + r] = L[k];
+        tc_epi_sync();
+        int a = 0, b = 0;
+        for (int k = 0; k < p.top_k; ++k) {
+          const float x = s_lst[a * TC_M + r], y = s_lst[(TC_LIST + b) * TC_M + r];
+          if (x >= y) {
+            thr = x;
+            ++a;
+          } else {
+            thr = y;
+            ++b;
+          }
+        }
+        rowmax = fmaxf(s_lst[r], s_lst[TC_LIST * TC_M + r]);
+        tc_epi_sync();          // the lists' space is the kept-key lists' of pass 2
       }
     }
   }
 
-  // ---- gather: each warp forms the outputs of its 32 rows (lanes split the
+  // ---- gather: each warp forms the outputs of 16 rows (lanes split the
   // channels), from the kept-key lists
-  if (warp >= 2 && s_flag[1] == 0) {
+  if (warp >= 2) {
     if (row_ok) {
-      s_cnt[r] = serial ? -1 : cnt;
-      s_z[r] = z;
+      s_cnt[half * TC_M + r] = cnt;
+      s_z[half * TC_M + r] = z;
+      if (half == 0) s_rmax[r] = rowmax;
     }
-    __syncwarp();
-    for (int rr = 0; rr < 32; ++rr) {
-      const int row = quarter * 32 + rr;
-      const int64_t ii = i0 + row;
-      if (ii >= p.T) break;
-      const int n = s_cnt[row];
-      const float rmax = __shfl_sync(0xffffffffu, rowmax, rr);
-      const float invz = 1.0f / s_z[row];
-      float* orr = p.out + (slice * p.T + ii) * p.dh;
-      if (n < 0) {
-        // listed and accumulated by the row's own thread: normalise
-        __syncwarp();
-        for (int c = lane; c < p.dh; c += 32) orr[c] = orr[c] * invz;
-        continue;
-      }
-      float oacc[3] = {0.0f, 0.0f, 0.0f};
-      for (int e0 = 0; e0 < n; e0 += 4) {
-        int jj[4];
-        float wv[4];
+    tc_epi_sync();
+    if (s_flag[1] == 0) {
+      const int e8 = warp - 2;
+      for (int rr = 0; rr < TC_M / TC_EPI_WARPS; ++rr) {
+        const int row = e8 * (TC_M / TC_EPI_WARPS) + rr;
+        const int ii = i0 + row;
+        if (ii >= p.T) break;
+        const int c0 = s_cnt[row], c1 = s_cnt[TC_M + row];
+        const float rmax = s_rmax[row];
+        const float invz = 1.0f / (s_z[row] + s_z[TC_M + row]);
+        float* orr = p.out + (slice * p.T + ii) * p.dh;
+        float oacc[3] = {0.0f, 0.0f, 0.0f};
+        for (int hh = 0; hh < 2; ++hh) {
+          const int n = min(hh ? c1 : c0, TC_KCAP);
+          for (int e0 = 0; e0 < n; e0 += 4) {
+            int jj[4];
+            float wv[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const bool ok = e0 + e < n;
-          jj[e] = ok ? s_kj[(e0 + e) * TC_M + row] : -1;
-          wv[e] = ok ? expf(s_ks[(e0 + e) * TC_M + row] - rmax) * invz : 0.0f;
-        }
-        float val[4][3];
+            for (int e = 0; e < 4; ++e) {
+              const bool ok = e0 + e < n;
+              const int slot = (hh * TC_KCAP + e0 + e) * TC_M + row;
+              jj[e] = ok ? s_kj[slot] : -1;
+              wv[e] = ok ? expf(s_ks[slot] - rmax) * invz : 0.0f;
+            }
+            float val[4][3];
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
+            for (int e = 0; e < 4; ++e)
 #pragma unroll
-          for (int q = 0; q < 3; ++q) {
-            const int c = lane + 32 * q;
-            val[e][q] = (jj[e] >= 0 && c < p.dh) ? __ldg(Vs + (int64_t)jj[e] * p.dh + c) : 0.0f;
+              for (int q = 0; q < 3; ++q) {
+                const int c = lane + 32 * q;
+                val[e][q] = (jj[e] >= 0 && c < p.dh) ? __ldg(Vs + (int64_t)jj[e] * p.dh + c) : 0.0f;
+              }
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (jj[e] >= 0)
+#pragma unroll
+                for (int q = 0; q < 3; ++q) oacc[q] = fmaf(wv[e], val[e][q], oacc[q]);
           }
+        }
+        // kept keys past the lists, accumulated (unnormalised) in scratch rows
+        const float* ov1 = p.qlo + (slice * p.Tp + ii) * TC_KP;
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (jj[e] >= 0)
-#pragma unroll
-            for (int q = 0; q < 3; ++q) oacc[q] = fmaf(wv[e], val[e][q], oacc[q]);
-      }
-#pragma unroll
-      for (int q = 0; q < 3; ++q) {
-        const int c = lane + 32 * q;
-        if (c < p.dh) orr[c] = oacc[q];
+        for (int q = 0; q < 3; ++q) {
+          const int c = lane + 32 * q;
+          if (c >= p.dh) continue;
+          float o = oacc[q];
+          if (c0 > TC_KCAP) o = fmaf(orr[c], invz, o);
+          if (c1 > TC_KCAP) o = fmaf(ov1[c], invz, o);
+          orr[c] = o;
+        }
       }
     }
   }
@@ -571,7 +654,7 @@ int launch_tsrn_attention_tc(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64
       !make_feat_map(&mkh, khi, S * l.Kp, TC_N) || !make_feat_map(&mkl, klo, S * l.Kp, TC_N))
     return TP_ERR_UNSUPPORTED;
   TcArgs a{S, H, T, Tkv, Tc, l.Tp, l.Kp, (int)dh, top_k, causal, (int)ceil_div(dh, 8),
-           Q, K, V, slopes, qmx, kmx, out, device_error_ptr()};
+           Q, K, V, slopes, qmx, kmx, out, qlo, device_error_ptr()};
   cudaError_t e = cudaFuncSetAttribute(att_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)TC_SMEM_BYTES);
   if (e != cudaSuccess) return cuda_status(e);

@@ -793,9 +793,10 @@ ATTENTION_PATHS = {"auto": 0, "cuda_cores": 1, "tensor_cores": 2}
 
 def set_attention_path(path: str) -> str:
     """Kernel of the fused TSRN attention for this process: ``"auto"`` (the
-    CUDA-core kernel within its limits -- dh <= 128, top_k <= 64, Tkv <= 6144 --
-    else the tcgen05 kernel, which takes dh <= 96, top_k <= 16 and any Tkv),
-    ``"cuda_cores"`` or ``"tensor_cores"``.  Returns the previous choice."""
+    tcgen05 kernel -- dh <= 96, top_k <= 16, any Tkv -- when T >= 128 fills its
+    128-query tiles, else the CUDA-core kernel within its limits -- dh <= 128,
+    top_k <= 64, Tkv <= 6144), ``"cuda_cores"`` or ``"tensor_cores"``.
+    Returns the previous choice."""
     if path not in ATTENTION_PATHS:
         raise ValueError(f"path must be one of {sorted(ATTENTION_PATHS)}, got {path!r}")
     prev = ctypes.c_int(0)
@@ -979,6 +980,51 @@ def esn_leaky_fwd(U: torch.Tensor, Ws: torch.Tensor, lk: torch.Tensor,
     H = torch.empty_like(U)
     _esn_call(False, U, None, None, [_rows(Ws, dr)], lk, h0, H, T, T, dev)
     return H
+
+
+def esn_gru_bwd(dH: torch.Tensor, fa: torch.Tensor, fz: torch.Tensor, fr: torch.Tensor,
+                keep: torch.Tensor, r: torch.Tensor, Wzh: torch.Tensor, Wrh: torch.Tensor,
+                Ws: torch.Tensor):
+    """Backward through time of the GRU-gated recurrence in one launch: the
+    reverse-time loop of the reference's autograd over research/tsrn_dml.py:834-840.
+    dH and the per-step factors fa, fz, fr, keep, r are [B, T, dr] (see
+    ``reservoir.GRUReservoirFunction``); returns (dAh, dAz, dAr), the gradients
+    of the candidate's and both gates' pre-activations at every step."""
+    dev = _require_cuda(dH, fa, fz, fr, keep, r, Wzh, Wrh, Ws)
+    dH, fa, fz, fr, keep, r = (_f32(t).contiguous() for t in (dH, fa, fz, fr, keep, r))
+    B, T, dr = dH.shape
+    for t in (fa, fz, fr, keep, r):
+        if t.shape != dH.shape:
+            raise ValueError("esn_gru_bwd: every factor must have dH's shape [B, T, dr]")
+    WT = [_rows(w.t().contiguous(), dr) for w in (Wzh, Wrh, Ws)]
+    out = [torch.empty_like(dH) for _ in range(3)]
+    with torch.cuda.device(dev):
+        st = _lib.load().tp_esn_gru_bwd(B, T, dr, _ptr(dH), _ptr(fa), _ptr(fz), _ptr(fr),
+                                         _ptr(keep), _ptr(r), _ptr(WT[0][0]), WT[0][1],
+                                         _ptr(WT[1][0]), WT[1][1], _ptr(WT[2][0]), WT[2][1],
+                                         _ptr(out[0]), _ptr(out[1]), _ptr(out[2]), _stream(dev))
+    _lib.check(st, "tp_esn_gru_bwd")
+    return tuple(out)
+
+
+def esn_leaky_bwd(dH: torch.Tensor, fa: torch.Tensor, Ws: torch.Tensor, lk: torch.Tensor):
+    """Backward through time of the leaky recurrence in one launch (the reverse
+    loop of autograd over tsrn_gpu.py:480-484): dH and fa = lk (1 - s^2) are
+    [B, T, dr], ``lk`` the device scalar.  Returns (dA, dHs): the gradient of
+    each step's pre-activation and of each step's state h_t."""
+    dev = _require_cuda(dH, fa, Ws, lk)
+    dH, fa = (_f32(t).contiguous() for t in (dH, fa))
+    B, T, dr = dH.shape
+    if fa.shape != dH.shape:
+        raise ValueError("esn_leaky_bwd: fa must have dH's shape [B, T, dr]")
+    lk = _f32(lk).reshape(1).contiguous()
+    WsT, ld = _rows(Ws.t().contiguous(), dr)
+    dA, dHs = torch.empty_like(dH), torch.empty_like(dH)
+    with torch.cuda.device(dev):
+        st = _lib.load().tp_esn_leaky_bwd(B, T, dr, _ptr(dH), _ptr(fa), _ptr(WsT), ld, _ptr(lk),
+                                           _ptr(dA), _ptr(dHs), _stream(dev))
+    _lib.check(st, "tp_esn_leaky_bwd")
+    return dA, dHs
 
 
 def _copy_rows(dst: torch.Tensor, src: torch.Tensor, stream) -> None:

@@ -145,3 +145,14 @@ def test_path_selection(cuda, path):
     np.testing.assert_allclose(out[ok], ref[ok], rtol=1e-4, atol=2e-5)
     with pytest.raises(ValueError):
         ops.set_attention_path("fast")
+
+
+@pytest.mark.parametrize("T,expect", [(200, "tensor_cores"), (100, "cuda_cores")])
+def test_auto_choice(cuda, path, T, expect):
+    # auto takes tensor cores when T fills a 128-query tile, CUDA cores below
+    Q, K, V, slopes = _case(1, 2, T, 0, 32, seed=T)
+    outs = {}
+    for p in ("auto", "tensor_cores", "cuda_cores"):
+        path(p)
+        outs[p] = _run(cuda, Q, K, V, slopes, 8, True, 0)
+    np.testing.assert_array_equal(outs["auto"], outs[expect])
