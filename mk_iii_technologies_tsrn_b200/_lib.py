@@ -119,6 +119,15 @@ SIGNATURES: dict[str, tuple] = {
         [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p,
          _c_p],
     ),
+    "tp_esn_gru_bwd": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_i64,
+         _c_p, _c_i64, _c_p, _c_p, _c_p, _c_p],
+    ),
+    "tp_esn_leaky_bwd": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_p, _c_p],
+    ),
     "tp_esn_leaky_fwd": (
         _c_int, [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_p]),
     "tp_esn_gru_fwd_seg": (

@@ -580,6 +580,52 @@ int tp_esn_gru_fwd(int64_t B, int64_t T, int64_t dr, const float* U, const float
   return tp::launch_esn_fwd(true, B, T, dr, U, Uz, Ur, W, ld, nullptr, H, as_stream(stream));
 }
 
+int tp_esn_gru_bwd(int64_t B, int64_t T, int64_t dr, const float* dH, const float* fa,
+                   const float* fz, const float* fr, const float* keep, const float* r,
+                   const float* WzhT, int64_t ld_wz, const float* WrhT, int64_t ld_wr,
+                   const float* WsT, int64_t ld_ws, float* dAh, float* dAz, float* dAr,
+                   void* stream) {
+  TP_RETURN_IF(B < 0 || T < 0 || dr < 0, TP_ERR_INVALID_ARG);
+  if (B * T * dr == 0) return TP_OK;
+  TP_RETURN_IF(ld_wz < dr || ld_wr < dr || ld_ws < dr, TP_ERR_INVALID_ARG);
+  TP_CHECK_PTR(dH);
+  TP_CHECK_PTR(fa);
+  TP_CHECK_PTR(fz);
+  TP_CHECK_PTR(fr);
+  TP_CHECK_PTR(keep);
+  TP_CHECK_PTR(r);
+  TP_CHECK_PTR(WzhT);
+  TP_CHECK_PTR(WrhT);
+  TP_CHECK_PTR(WsT);
+  TP_CHECK_PTR(dAh);
+  TP_CHECK_PTR(dAz);
+  TP_CHECK_PTR(dAr);
+  const float* F[5] = {fa, fz, fr, keep, r};
+  const float* W[3] = {WzhT, WrhT, WsT};
+  const int64_t ld[3] = {ld_wz, ld_wr, ld_ws};
+  float* out[3] = {dAh, dAz, dAr};
+  return tp::launch_esn_bwd(true, B, T, dr, dH, F, W, ld, nullptr, out, as_stream(stream));
+}
+
+int tp_esn_leaky_bwd(int64_t B, int64_t T, int64_t dr, const float* dH, const float* fa,
+                     const float* WsT, int64_t ld_ws, const float* leak, float* dA, float* dHs,
+                     void* stream) {
+  TP_RETURN_IF(B < 0 || T < 0 || dr < 0, TP_ERR_INVALID_ARG);
+  if (B * T * dr == 0) return TP_OK;
+  TP_RETURN_IF(ld_ws < dr, TP_ERR_INVALID_ARG);
+  TP_CHECK_PTR(dH);
+  TP_CHECK_PTR(fa);
+  TP_CHECK_PTR(WsT);
+  TP_CHECK_PTR(leak);
+  TP_CHECK_PTR(dA);
+  TP_CHECK_PTR(dHs);
+  const float* F[5] = {fa, nullptr, nullptr, nullptr, nullptr};
+  const float* W[3] = {WsT, nullptr, nullptr};
+  const int64_t ld[3] = {ld_ws, 0, 0};
+  float* out[3] = {dA, dHs, nullptr};
+  return tp::launch_esn_bwd(false, B, T, dr, dH, F, W, ld, leak, out, as_stream(stream));
+}
+
 int tp_esn_leaky_fwd(int64_t B, int64_t T, int64_t dr, const float* U, const float* Ws,
                      int64_t ld_ws, const float* leak, float* H, void* stream) {
   TP_RETURN_IF(B < 0 || T < 0 || dr < 0, TP_ERR_INVALID_ARG);

@@ -319,6 +319,202 @@ __global__ void __launch_bounds__(ESN_MAX_NT, 1) esn_kernel(EsnParams p) {
   esn_cluster_sync();
 }
 
+
+// ---------------------------------------------------------------------------
+// Backward through time of both recurrences, one launch (same cluster layout,
+// exchanges and input ring as the forward; time runs from T-1 down to 0).
+// With g the state gradient carried from step t+1 (0 after the last step):
+//   GRU:   dh = dH_t + g,  dah = dh fa_t                    (exchanged)
+//          dm = dah Ws,   dar = dm fr_t,  daz = dh fz_t    (both exchanged)
+//          g  = dh keep_t + dm r_t + daz Wzh + dar Wrh
+//   leaky: dh = dH_t + g,  da = dh fa_t                     (exchanged)
+//          g  = dh (1 - lk) + da Ws
+// fa = z (1 - h~^2), fz = (h~ - h_{t-1}) z (1 - z), fr = h_{t-1} r (1 - r),
+// keep = 1 - z (GRU); fa = lk (1 - s^2) (leaky): per-step factors formed
+// for all steps beforehand.  Column k of a product v W is the dot of v with
+// row k of W^T, so the kernel takes the transposed weights and reads them
+// like the forward reads its own.  Outputs per step: GRU dah, daz, dar (the
+// gradients of the three pre-activations); leaky da and dh.
+// ---------------------------------------------------------------------------
+struct EsnBwdParams {
+  int B, T, dr, dr4;
+  const float* dH;    // [B][T][dr]
+  const float* F[5];  // GRU: fa, fz, fr, keep, r; leaky: fa
+  const float* W[3];  // transposed weights: GRU WzhT, WrhT, WsT; leaky WsT
+  int64_t ld[3];
+  const float* leak;  // leaky: device scalar lk
+  float* out[3];      // GRU: dAh, dAz, dAr; leaky: dA, dHs
+  int* err;
+  int ncl;
+  int off_x, off_pre; // shared-memory offsets in floats
+};
+
+template <bool kGru, bool kSmemW, int RB>
+__global__ void __launch_bounds__(ESN_MAX_NT, 1) esn_bwd_kernel(EsnBwdParams p) {
+  extern __shared__ __align__(16) float esn_sm[];
+  constexpr int G = kGru ? 3 : 1;  // weight matrices
+  constexpr int P = kGru ? 6 : 2;  // streamed inputs per step: dH and the factors
+  constexpr int PARTS = ESN_KS / RB;
+  const uint32_t crank = esn_cluster_rank();
+  const uint32_t csize = esn_cluster_size();
+  const int b0 = (int)(blockIdx.x / csize) * RB;
+  const int ncl = p.ncl, dr = p.dr, dr4 = p.dr4, NG = dr4 >> 2;
+  const int c0 = (int)crank * ncl;
+  const int items = RB * ncl;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int cl = tid / ESN_KS, ks = tid % ESN_KS;
+  const int row = ks % RB, part = ks / RB;
+  const bool col_ok = cl < ncl && c0 + cl < dr;
+  const bool row_ok = b0 + row < p.B;
+  float* wsm = esn_sm;
+  // exchange buffers: GRU dah, daz, dar [RB][dr4] each; leaky da [2][RB][dr4]
+  float* xs = esn_sm + p.off_x;
+  float* pre = esn_sm + p.off_pre;  // [3][P][RB][ncl], ring of step inputs
+
+  if (kSmemW) {
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      for (int e = tid; e < ncl * dr4; e += nt) {
+        const int c = e / dr4, k = e - c * dr4;
+        float v = 0.0f;
+        if (c0 + c < dr && k < dr) v = p.W[g][(int64_t)(c0 + c) * p.ld[g] + k];
+        wsm[(g * ncl + c) * dr4 + k] = v;
+      }
+  }
+  for (int e = tid; e < 3 * RB * dr4; e += nt) xs[e] = 0.0f;
+
+  // stage step s's inputs (time T-1-s) into ring slot s % 3
+  auto prefetch = [&](int s) {
+    float* dst = pre + (s % 3) * P * items;
+    const int t = p.T - 1 - s;
+    for (int e = tid; s < p.T && e < P * items; e += nt) {
+      const int pi = e / items, it = e - pi * items;
+      const int bl = it / ncl, c = it - bl * ncl;
+      const int b = b0 + bl, cg = c0 + c;
+      const float* src = pi == 0 ? p.dH : p.F[pi - 1];
+      const bool ok = b < p.B && cg < dr;
+      tp_cp_async4(dst + e, ok ? src + ((int64_t)b * p.T + t) * dr + cg : src, ok ? 4 : 0);
+    }
+    tp_cp_async_commit();
+  };
+  auto wrow = [&](int g) -> const float4* {
+    const int c = min(cl, ncl - 1);
+    if (kSmemW) return reinterpret_cast<const float4*>(wsm + (g * ncl + c) * dr4);
+    const int cg = min(c0 + c, dr - 1);
+    return reinterpret_cast<const float4*>(p.W[g] + (int64_t)cg * p.ld[g]);
+  };
+  const float4* w_s = wrow(G - 1);
+  const float4* w_z = kGru ? wrow(0) : w_s;
+  const float4* w_r = kGru ? wrow(1) : w_s;
+  const int pidx = row * ncl + min(cl, ncl - 1);
+  const float lk = kGru ? 0.0f : *p.leak;
+  float g = 0.0f;   // state gradient from the step after
+
+  // receive barriers: GRU mb[0] dah, mb[1] daz + dar; leaky mb[b] for the da
+  // buffer b (step s writes buffer s & 1).  Re-armed by thread 0 after each
+  // wait, as in the forward.
+  __shared__ __align__(8) uint64_t mb[2];
+  const uint32_t xbytes = (uint32_t)(min(RB, p.B - b0) * dr * (int)sizeof(float));
+  const uint32_t xb1 = kGru ? 2 * xbytes : xbytes;
+  if (tid == 0) {
+    tp_mbar_init(&mb[0], 1);
+    tp_mbar_init(&mb[1], 1);
+    tp_fence_mbar_init();
+    tp_mbar_arrive_expect_tx(&mb[0], xbytes);
+    tp_mbar_arrive_expect_tx(&mb[1], xb1);
+  }
+  bool failed = false;
+  auto recv = [&](int b, uint32_t parity) {
+    if (!failed && !tp_mbar_wait(&mb[b], parity, p.err)) failed = true;
+    if (tid == 0) tp_mbar_arrive_expect_tx(&mb[b], b == 1 ? xb1 : xbytes);
+  };
+  auto dot = [&](const float4* w, const float* v) -> float {
+    float2 acc[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) acc[r] = make_float2(0.0f, 0.0f);
+    for (int q = ks; q < NG; q += ESN_KS) {
+      const float4 wv = esn_wload<kSmemW>(w, q);
+#pragma unroll
+      for (int r = 0; r < RB; ++r)
+        acc[r] = esn_dot4(reinterpret_cast<const float4*>(v + r * dr4)[q], wv, acc[r]);
+    }
+    float va[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) va[r] = acc[r].x + acc[r].y;
+    return esn_reduce_rows<RB>(va, ks);
+  };
+
+  prefetch(0);
+  prefetch(1);
+  tp_cp_async_wait<1>();
+  esn_cluster_sync();  // every CTA of the cluster is running; barriers, weights, step 0
+
+  for (int s = 0; s < p.T; ++s) {
+    const int t = p.T - 1 - s;
+    prefetch(s + 2);
+    const float* pin = pre + (s % 3) * P * items;
+    // every input of this step into registers now: the slot is refilled at
+    // the start of step s + 3, which a thread may reach while this one is
+    // still in the step's second half
+    float f[P];
+#pragma unroll
+    for (int q = 0; q < P; ++q) f[q] = pin[q * items + pidx];
+    const float dh = f[0] + g;
+    const int64_t o = ((int64_t)(b0 + row) * p.T + t) * dr + c0 + cl;
+    if (kGru) {
+      float* dahs = xs;
+      float* dazs = xs + RB * dr4;
+      float* dars = xs + 2 * RB * dr4;
+      const float dah = dh * f[1];
+      __syncthreads();  // every thread has seen the last phase before any send
+      if (col_ok && row_ok)
+        for (uint32_t rk = part; rk < csize; rk += PARTS)
+          esn_st_async(dahs + row * dr4 + c0 + cl, &mb[0], rk, dah);
+      recv(0, (uint32_t)s & 1u);
+      const float dm = dot(w_s, dahs);
+      const float dar = dm * f[3];
+      const float daz = dh * f[2];
+      // the next step's inputs landed; the barrier publishes them and orders
+      // every thread's view of the last phase before the sends below
+      tp_cp_async_wait<1>();
+      __syncthreads();
+      if (col_ok && row_ok) {
+        for (uint32_t rk = part; rk < csize; rk += PARTS) {
+          esn_st_async(dazs + row * dr4 + c0 + cl, &mb[1], rk, daz);
+          esn_st_async(dars + row * dr4 + c0 + cl, &mb[1], rk, dar);
+        }
+        if (part == 0) {
+          p.out[0][o] = dah;
+          p.out[1][o] = daz;
+          p.out[2][o] = dar;
+        }
+      }
+      recv(1, (uint32_t)s & 1u);
+      const float gz = dot(w_z, dazs);
+      const float gr = dot(w_r, dars);
+      g = dh * f[4] + dm * f[5] + gz + gr;
+    } else {
+      float* das = xs + (s & 1) * RB * dr4;
+      const float da = dh * f[1];
+      tp_cp_async_wait<1>();
+      __syncthreads();
+      if (col_ok && row_ok) {
+        for (uint32_t rk = part; rk < csize; rk += PARTS)
+          esn_st_async(das + row * dr4 + c0 + cl, &mb[s & 1], rk, da);
+        if (part == 0) {
+          p.out[0][o] = da;
+          p.out[1][o] = dh;
+        }
+      }
+      recv(s & 1, (uint32_t)(s >> 1) & 1u);
+      g = dh * (1.0f - lk) + dot(w_s, das);
+    }
+  }
+  // every exchange was received inside its step; the cluster barrier keeps
+  // each CTA alive until all have left the loop
+  esn_cluster_sync();
+}
+
 struct EsnPlan {
   int CS, ncl, RB, nt;
   bool smemW;
@@ -326,17 +522,31 @@ struct EsnPlan {
   int clusters;
 };
 
-size_t esn_smem_bytes(bool gru, bool smemW, int dr4, int ncl, int RB) {
-  const int G = gru ? 3 : 1, P = gru ? 3 : 1;
+size_t esn_smem_bytes(bool gru, bool smemW, int dr4, int ncl, int RB, bool bwd = false) {
+  const int G = gru ? 3 : 1;
+  const int P = bwd ? (gru ? 6 : 2) : (gru ? 3 : 1);
   const size_t w = smemW ? (size_t)G * ncl * dr4 : 0;
-  const size_t state = (size_t)2 * RB * dr4;
+  const size_t state = (size_t)(bwd ? 3 : 2) * RB * dr4;
   const size_t pre = (size_t)3 * P * RB * ncl;
   return (w + state + pre) * sizeof(float);
 }
 
+// the kernel of a (direction, recurrence, weight placement, rows) choice, and
+// its parameter block
+template <bool kBwd, bool kGru, bool kSmemW, int RB>
+struct EsnKernel {
+  using Params = EsnParams;
+  static constexpr auto fn = esn_kernel<kGru, kSmemW, RB>;
+};
 template <bool kGru, bool kSmemW, int RB>
+struct EsnKernel<true, kGru, kSmemW, RB> {
+  using Params = EsnBwdParams;
+  static constexpr auto fn = esn_bwd_kernel<kGru, kSmemW, RB>;
+};
+
+template <class Kn>
 int esn_configure(const EsnPlan& pl, cudaLaunchConfig_t* cfg, cudaLaunchAttribute* attr) {
-  auto kern = esn_kernel<kGru, kSmemW, RB>;
+  auto kern = Kn::fn;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
   if (e != cudaSuccess) return (int)e;
@@ -358,46 +568,54 @@ int esn_configure(const EsnPlan& pl, cudaLaunchConfig_t* cfg, cudaLaunchAttribut
 }
 
 // kind 0: occupancy query (max active clusters into *out); kind 1: launch
-template <bool kGru, bool kSmemW, int RB>
-int esn_run(int kind, const EsnPlan& pl, const EsnParams& p, cudaStream_t stream, int* out) {
+// (params: the kernel's parameter block; unused for kind 0)
+template <class Kn>
+int esn_run(int kind, const EsnPlan& pl, const void* params, cudaStream_t stream, int* out) {
   cudaLaunchConfig_t cfg;
   cudaLaunchAttribute attr[1];
-  int st = esn_configure<kGru, kSmemW, RB>(pl, &cfg, attr);
+  int st = esn_configure<Kn>(pl, &cfg, attr);
   if (st != TP_OK) return st;
   if (kind == 0) {
     cfg.gridDim = dim3((unsigned)pl.CS);
-    return (int)cudaOccupancyMaxActiveClusters(out, (const void*)esn_kernel<kGru, kSmemW, RB>,
-                                               &cfg);
+    return (int)cudaOccupancyMaxActiveClusters(out, (const void*)Kn::fn, &cfg);
   }
   cfg.stream = stream;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, esn_kernel<kGru, kSmemW, RB>, p);
+  const typename Kn::Params& p = *static_cast<const typename Kn::Params*>(params);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, Kn::fn, p);
   if (e != cudaSuccess) return (int)e;
   return launch_status();
 }
 
-template <bool kGru, bool kSmemW>
-int esn_run_rb(int kind, const EsnPlan& pl, const EsnParams& p, cudaStream_t s, int* out) {
+template <bool kBwd, bool kGru, bool kSmemW>
+int esn_run_rb(int kind, const EsnPlan& pl, const void* p, cudaStream_t s, int* out) {
   switch (pl.RB) {
-    case 1: return esn_run<kGru, kSmemW, 1>(kind, pl, p, s, out);
-    case 2: return esn_run<kGru, kSmemW, 2>(kind, pl, p, s, out);
-    case 4: return esn_run<kGru, kSmemW, 4>(kind, pl, p, s, out);
-    default: return esn_run<kGru, kSmemW, 8>(kind, pl, p, s, out);
+    case 1: return esn_run<EsnKernel<kBwd, kGru, kSmemW, 1>>(kind, pl, p, s, out);
+    case 2: return esn_run<EsnKernel<kBwd, kGru, kSmemW, 2>>(kind, pl, p, s, out);
+    case 4: return esn_run<EsnKernel<kBwd, kGru, kSmemW, 4>>(kind, pl, p, s, out);
+    default: return esn_run<EsnKernel<kBwd, kGru, kSmemW, 8>>(kind, pl, p, s, out);
   }
 }
 
-int esn_dispatch(bool gru, int kind, const EsnPlan& pl, const EsnParams& p, cudaStream_t s,
+template <bool kBwd>
+int esn_dispatch_dir(bool gru, int kind, const EsnPlan& pl, const void* p, cudaStream_t s,
+                     int* out) {
+  if (gru) return pl.smemW ? esn_run_rb<kBwd, true, true>(kind, pl, p, s, out)
+                           : esn_run_rb<kBwd, true, false>(kind, pl, p, s, out);
+  return pl.smemW ? esn_run_rb<kBwd, false, true>(kind, pl, p, s, out)
+                  : esn_run_rb<kBwd, false, false>(kind, pl, p, s, out);
+}
+
+int esn_dispatch(bool bwd, bool gru, int kind, const EsnPlan& pl, const void* p, cudaStream_t s,
                  int* out) {
-  if (gru) return pl.smemW ? esn_run_rb<true, true>(kind, pl, p, s, out)
-                           : esn_run_rb<true, false>(kind, pl, p, s, out);
-  return pl.smemW ? esn_run_rb<false, true>(kind, pl, p, s, out)
-                  : esn_run_rb<false, false>(kind, pl, p, s, out);
+  return bwd ? esn_dispatch_dir<true>(gru, kind, pl, p, s, out)
+             : esn_dispatch_dir<false>(gru, kind, pl, p, s, out);
 }
 
 // Plan: over cluster sizes CS (at most cs_cap CTAs, <= 64 columns each) and
 // rows per cluster RB (power of two <= 8), the candidate with the lowest
 // waves x (2 + RB) score (below); weights stay in shared memory when they
 // fit, else they are read from L2 (global_ok).
-int esn_plan(bool gru, int B, int dr, bool global_ok, int cs_cap, EsnPlan* pl) {
+int esn_plan(bool bwd, bool gru, int B, int dr, bool global_ok, int cs_cap, EsnPlan* pl) {
   const int dr4 = (dr + 3) & ~3;
   int dev = 0, smem_max = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -409,19 +627,19 @@ int esn_plan(bool gru, int B, int dr, bool global_ok, int cs_cap, EsnPlan* pl) {
   auto make = [&](int CS, int RB, EsnPlan* out, int* maxc) -> int {
     const int ncl = (dr + CS - 1) / CS;
     if (ncl > ESN_MAX_NCL) return -1;
-    bool smemW = esn_smem_bytes(gru, true, dr4, ncl, RB) <= (size_t)smem_max;
-    if (!smemW && (!global_ok || esn_smem_bytes(gru, false, dr4, ncl, RB) > (size_t)smem_max))
+    bool smemW = esn_smem_bytes(gru, true, dr4, ncl, RB, bwd) <= (size_t)smem_max;
+    if (!smemW &&
+        (!global_ok || esn_smem_bytes(gru, false, dr4, ncl, RB, bwd) > (size_t)smem_max))
       return -1;
     out->CS = CS;
     out->ncl = ncl;
     out->RB = RB;
     out->nt = ((ncl + 3) / 4) * 4 * ESN_KS;
     out->smemW = smemW;
-    out->smem = esn_smem_bytes(gru, smemW, dr4, ncl, RB);
+    out->smem = esn_smem_bytes(gru, smemW, dr4, ncl, RB, bwd);
     out->clusters = (B + RB - 1) / RB;
-    EsnParams dummy{};
     *maxc = 0;
-    const int st = esn_dispatch(gru, 0, *out, dummy, nullptr, maxc);
+    const int st = esn_dispatch(bwd, gru, 0, *out, nullptr, nullptr, maxc);
     if (st != TP_OK) {
       (void)cudaGetLastError();
       return -1;
@@ -466,20 +684,21 @@ int esn_plan(bool gru, int B, int dr, bool global_ok, int cs_cap, EsnPlan* pl) {
 // plans are cached per (mode, B, dr, global_ok, device): planning runs
 // several occupancy queries
 struct EsnPlanKey {
-  bool gru, global_ok;
+  bool bwd, gru, global_ok;
   int B, dr, dev;
   bool operator==(const EsnPlanKey& o) const {
-    return gru == o.gru && global_ok == o.global_ok && B == o.B && dr == o.dr && dev == o.dev;
+    return bwd == o.bwd && gru == o.gru && global_ok == o.global_ok && B == o.B && dr == o.dr &&
+           dev == o.dev;
   }
 };
 std::mutex esn_plan_mu;
 std::vector<std::pair<EsnPlanKey, EsnPlan>> esn_plan_cache;
 
-int esn_plan_cached(bool gru, int B, int dr, bool global_ok, EsnPlan* pl) {
+int esn_plan_cached(bool bwd, bool gru, int B, int dr, bool global_ok, EsnPlan* pl) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return (int)e;
-  const EsnPlanKey key{gru, global_ok, B, dr, dev};
+  const EsnPlanKey key{bwd, gru, global_ok, B, dr, dev};
   {
     std::lock_guard<std::mutex> lk(esn_plan_mu);
     for (auto& kv : esn_plan_cache)
@@ -490,10 +709,10 @@ int esn_plan_cached(bool gru, int B, int dr, bool global_ok, EsnPlan* pl) {
   }
   // clusters of 16 CTAs (a non-portable size) when the device schedules
   // them, else at most 8
-  int st = esn_plan(gru, B, dr, global_ok, 16, pl);
+  int st = esn_plan(bwd, gru, B, dr, global_ok, 16, pl);
   if (st != TP_OK) {
     (void)cudaGetLastError();
-    st = esn_plan(gru, B, dr, global_ok, 8, pl);
+    st = esn_plan(bwd, gru, B, dr, global_ok, 8, pl);
   }
   if (st != TP_OK) return st;
   std::lock_guard<std::mutex> lk(esn_plan_mu);
@@ -520,7 +739,7 @@ int launch_esn_fwd(bool gru, int64_t B, int64_t T, int64_t dr, const float* U, c
   bool global_ok = true;
   for (int g = 0; g < G; ++g) global_ok = global_ok && esn_vec_ok(W[g], ld[g], (int)dr);
   EsnPlan pl{};
-  const int st = esn_plan_cached(gru, (int)B, (int)dr, global_ok, &pl);
+  const int st = esn_plan_cached(false, gru, (int)B, (int)dr, global_ok, &pl);
   if (st != TP_OK) return st;
   if ((int64_t)pl.clusters * pl.CS > INT32_MAX) return TP_ERR_TOO_LARGE;
   EsnParams p{};
@@ -544,7 +763,40 @@ int launch_esn_fwd(bool gru, int64_t B, int64_t T, int64_t dr, const float* U, c
   p.ncl = pl.ncl;
   p.off_h = pl.smemW ? G * pl.ncl * p.dr4 : 0;
   p.off_pre = p.off_h + 2 * pl.RB * p.dr4;
-  return esn_dispatch(gru, 1, pl, p, stream, nullptr);
+  return esn_dispatch(false, gru, 1, pl, &p, stream, nullptr);
+}
+
+int launch_esn_bwd(bool gru, int64_t B, int64_t T, int64_t dr, const float* dH,
+                   const float* const F[5], const float* const WT[3], const int64_t ld[3],
+                   const float* leak, float* const out[3], cudaStream_t stream) {
+  if (B * T * dr == 0) return TP_OK;
+  if (B > INT32_MAX / 2 || T > INT32_MAX / 2) return TP_ERR_TOO_LARGE;
+  if (dr > 16 * ESN_MAX_NCL) return TP_ERR_UNSUPPORTED;
+  const int G = gru ? 3 : 1;
+  bool global_ok = true;
+  for (int g = 0; g < G; ++g) global_ok = global_ok && esn_vec_ok(WT[g], ld[g], (int)dr);
+  EsnPlan pl{};
+  const int st = esn_plan_cached(true, gru, (int)B, (int)dr, global_ok, &pl);
+  if (st != TP_OK) return st;
+  if ((int64_t)pl.clusters * pl.CS > INT32_MAX) return TP_ERR_TOO_LARGE;
+  EsnBwdParams p{};
+  p.B = (int)B;
+  p.T = (int)T;
+  p.dr = (int)dr;
+  p.dr4 = ((int)dr + 3) & ~3;
+  p.dH = dH;
+  for (int q = 0; q < 5; ++q) p.F[q] = (gru || q == 0) ? F[q] : nullptr;
+  for (int g = 0; g < 3; ++g) {
+    p.W[g] = g < G ? WT[g] : nullptr;
+    p.ld[g] = g < G ? ld[g] : 0;
+  }
+  p.leak = leak;
+  for (int q = 0; q < 3; ++q) p.out[q] = (gru || q < 2) ? out[q] : nullptr;
+  p.err = device_error_ptr();
+  p.ncl = pl.ncl;
+  p.off_x = pl.smemW ? G * pl.ncl * p.dr4 : 0;
+  p.off_pre = p.off_x + 3 * pl.RB * p.dr4;
+  return esn_dispatch(true, gru, 1, pl, &p, stream, nullptr);
 }
 
 }  // namespace tp

@@ -9,8 +9,9 @@ recurrent matrix.  The recurrence over T steps runs as one launch
 (``ops.esn_gru_fwd`` / ``ops.esn_leaky_fwd``) in inference and in training;
 for training, :class:`GRUReservoirFunction` / :class:`LeakyReservoirFunction`
 add a backward through time: every step's gates are recomputed at once from the
-saved states (batched GEMMs), a single reverse-time loop carries the state
-gradient, and the weight gradients are batched GEMMs over all steps.  CUDA
+saved states (batched GEMMs), one launch (``ops.esn_gru_bwd`` /
+``ops.esn_leaky_bwd``) carries the state gradient backwards through all steps,
+and the weight gradients are batched GEMMs over all steps.  CUDA
 tensors only (no CPU fallback).
 """
 from __future__ import annotations
@@ -63,21 +64,8 @@ class GRUReservoirFunction(torch.autograd.Function):
         fz = (hc - Hp) * z * (1.0 - z)        # d h / d a_z
         fr = Hp * r * (1.0 - r)               # d m / d a_r
         keep = 1.0 - z
-        Wzr = torch.cat((Wzh, Wrh), dim=0)    # [2 dr, dr]
-        dA = torch.empty(B, T, 3, dr, device=H.device, dtype=H.dtype)   # a_h, a_z, a_r
-        dH = dH.contiguous()
-        g = torch.zeros(B, dr, device=H.device, dtype=H.dtype)
-        for t in range(T - 1, -1, -1):
-            dh = dH[:, t] + g
-            dah = dh * fa[:, t]
-            dm = dah @ Ws
-            dar = dm * fr[:, t]
-            daz = dh * fz[:, t]
-            dzr = torch.stack((daz, dar), dim=1)                 # [B, 2, dr]
-            g = dh * keep[:, t] + dm * r[:, t] + dzr.reshape(B, 2 * dr) @ Wzr
-            dA[:, t, 0] = dah
-            dA[:, t, 1:] = dzr
-        dAh, dAz, dAr = dA.unbind(2)
+        # the reverse-time loop over the state gradient: one launch
+        dAh, dAz, dAr = ops.esn_gru_bwd(dH, fa, fz, fr, keep, r, Wzh, Wrh, Ws)
         flat = lambda t: t.reshape(B * T, dr)   # noqa: E731
         dWs = flat(dAh).T @ flat(m)
         dWzh = flat(dAz).T @ flat(Hp)
@@ -102,16 +90,8 @@ class LeakyReservoirFunction(torch.autograd.Function):
         Hp = _previous_states(H)
         s = torch.tanh(Hp @ Ws.T + U)
         fa = lk * (1.0 - s * s)
-        dA = torch.empty_like(H)
-        dHs = torch.empty_like(H)
-        dH = dH.contiguous()
-        g = torch.zeros(B, dr, device=H.device, dtype=H.dtype)
-        for t in range(T - 1, -1, -1):
-            dh = dH[:, t] + g
-            da = dh * fa[:, t]
-            g = dh * (1.0 - lk) + da @ Ws
-            dA[:, t] = da
-            dHs[:, t] = dh
+        # the reverse-time loop over the state gradient: one launch
+        dA, dHs = ops.esn_leaky_bwd(dH, fa, Ws, lk)
         flat = lambda t: t.reshape(B * T, dr)   # noqa: E731
         dWs = flat(dA).T @ flat(Hp)
         dlk = (dHs * (s - Hp)).sum().reshape(lk.shape)
