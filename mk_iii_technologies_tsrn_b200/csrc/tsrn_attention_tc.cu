@@ -519,32 +519,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const float invz = 1.0f / (s_z[row] + s_z[TC_M + row]);
         float* orr = p.out + (slice * p.T + ii) * p.dh;
         float oacc[3] = {0.0f, 0.0f, 0.0f};
+        // each half's listed keys at once: every V load of the half in flight
+        // together (one L2 round trip per half instead of one per 4 keys);
+        // accumulated in list order (ascending key), half 0 first
         for (int hh = 0; hh < 2; ++hh) {
           const int n = min(hh ? c1 : c0, TC_KCAP);
-          for (int e0 = 0; e0 < n; e0 += 4) {
-            int jj[4];
-            float wv[4];
+          if (n == 0) continue;
+          int jj[TC_KCAP];
+          float val[TC_KCAP][3];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const bool ok = e0 + e < n;
-              const int slot = (hh * TC_KCAP + e0 + e) * TC_M + row;
-              jj[e] = ok ? s_kj[slot] : -1;
-              wv[e] = ok ? expf(s_ks[slot] - rmax) * invz : 0.0f;
+          for (int e = 0; e < TC_KCAP; ++e) {
+            jj[e] = e < n ? s_kj[(hh * TC_KCAP + e) * TC_M + row] : -1;
+#pragma unroll
+            for (int q = 0; q < 3; ++q) {
+              const int c = lane + 32 * q;
+              val[e][q] = (jj[e] >= 0 && c < p.dh) ? __ldg(Vs + (int64_t)jj[e] * p.dh + c) : 0.0f;
             }
-            float val[4][3];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-#pragma unroll
-              for (int q = 0; q < 3; ++q) {
-                const int c = lane + 32 * q;
-                val[e][q] = (jj[e] >= 0 && c < p.dh) ? __ldg(Vs + (int64_t)jj[e] * p.dh + c) : 0.0f;
-              }
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (jj[e] >= 0)
-#pragma unroll
-                for (int q = 0; q < 3; ++q) oacc[q] = fmaf(wv[e], val[e][q], oacc[q]);
           }
+#pragma unroll
+          for (int e = 0; e < TC_KCAP; ++e)
+            if (jj[e] >= 0) {
+              const float wv = expf(s_ks[(hh * TC_KCAP + e) * TC_M + row] - rmax) * invz;
+#pragma unroll
+              for (int q = 0; q < 3; ++q) oacc[q] = fmaf(wv, val[e][q], oacc[q]);
+            }
         }
         // kept keys past the lists, accumulated (unnormalised) in scratch rows
         const float* ov1 = p.qlo + (slice * p.Tp + ii) * TC_KP;
