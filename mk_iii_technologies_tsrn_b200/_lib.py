@@ -150,6 +150,21 @@ SIGNATURES: dict[str, tuple] = {
         [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_int, _c_int,
          _c_p, _c_p, _c_i64, _c_p],
     ),
+    "tp_tsrn_attention_fwd_lists": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_int, _c_int,
+         _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p],
+    ),
+    "tp_tsrn_attention_bwd_rows": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
+         _c_p, _c_p],
+    ),
+    "tp_tsrn_attention_bwd_keys": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
+         _c_p, _c_p],
+    ),
     "tp_tsrn_attention_set_path": (_c_int, [_c_int, _c_p]),
     "tp_maslov_softmax_fwd": (
         _c_int,
@@ -179,6 +194,7 @@ TP_DEVERR_FLAG_TIMEOUT = 2
 TP_ATT_PATH_AUTO = 0
 TP_ATT_PATH_CUDA_CORES = 1
 TP_ATT_PATH_TENSOR_CORES = 2
+TP_ATT_LIST = 32
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

@@ -553,6 +553,81 @@ int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t 
                                        causal, out, (float*)workspace, as_stream(stream));
 }
 
+int tp_tsrn_attention_fwd_lists(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc,
+                                int64_t dh, const float* Q, const float* K, const float* V,
+                                const float* alibi_slopes, int top_k, int causal, float* out,
+                                int32_t* kept_keys, float* kept_weights, int32_t* kept_count,
+                                void* workspace, int64_t workspace_bytes, void* stream) {
+  TP_RETURN_IF(B < 0 || H < 0 || T < 0 || Tkv < 0 || Tc < 0 || dh < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(Tc > Tkv, TP_ERR_INVALID_ARG);
+  if (B * H * T == 0) return TP_OK;
+  TP_RETURN_IF(Tkv == 0 || dh == 0 || top_k < 1, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(!tp::tsrn_attention_tc_supported(dh, top_k), TP_ERR_UNSUPPORTED);
+  TP_CHECK_PTR(Q);
+  TP_CHECK_PTR(K);
+  TP_CHECK_PTR(V);
+  TP_CHECK_PTR(alibi_slopes);
+  TP_CHECK_PTR(out);
+  TP_CHECK_PTR(kept_keys);
+  TP_CHECK_PTR(kept_weights);
+  TP_CHECK_PTR(kept_count);
+  TP_RETURN_IF(workspace == nullptr ||
+                   workspace_bytes < tp_tsrn_attention_workspace_bytes(B, H, T, Tkv, dh),
+               TP_ERR_WORKSPACE);
+  TP_RETURN_IF(!aligned16(workspace), TP_ERR_MISALIGNED);
+  TP_CHECK_PTR(workspace);
+  return tp::launch_tsrn_attention_tc(B, H, T, Tkv, Tc, dh, Q, K, V, alibi_slopes, top_k, causal,
+                                      out, (float*)workspace, as_stream(stream), kept_keys,
+                                      kept_weights, kept_count);
+}
+
+int tp_tsrn_attention_bwd_rows(int64_t S, int64_t T, int64_t Tkv, int64_t dh, const float* Q,
+                               const float* K, const float* V, const float* dO,
+                               const int32_t* kept_keys, const float* kept_weights,
+                               const int32_t* kept_count, float* dQ, float* entry_ds,
+                               float* entry_lse, void* stream) {
+  TP_RETURN_IF(S < 0 || T < 0 || Tkv < 0 || dh < 0, TP_ERR_INVALID_ARG);
+  if (S * T == 0) return TP_OK;
+  TP_RETURN_IF(Tkv == 0 || dh == 0, TP_ERR_INVALID_ARG);
+  TP_CHECK_PTR(Q);
+  TP_CHECK_PTR(K);
+  TP_CHECK_PTR(V);
+  TP_CHECK_PTR(dO);
+  TP_CHECK_PTR(kept_keys);
+  TP_CHECK_PTR(kept_weights);
+  TP_CHECK_PTR(kept_count);
+  TP_CHECK_PTR(dQ);
+  TP_CHECK_PTR(entry_ds);
+  TP_CHECK_PTR(entry_lse);
+  return tp::launch_tsrn_attention_bwd_rows(S, T, Tkv, dh, Q, K, V, dO, kept_keys, kept_weights,
+                                            kept_count, dQ, entry_ds, entry_lse,
+                                            as_stream(stream));
+}
+
+int tp_tsrn_attention_bwd_keys(int64_t S, int64_t T, int64_t Tkv, int64_t dh, const float* Q,
+                               const float* K, const float* dO, const float* kept_weights,
+                               const float* entry_ds, const float* entry_lse,
+                               const int32_t* order, const int64_t* offsets, float* dK,
+                               float* dV, void* stream) {
+  TP_RETURN_IF(S < 0 || T < 0 || Tkv < 0 || dh < 0, TP_ERR_INVALID_ARG);
+  if (S * Tkv == 0) return TP_OK;
+  TP_RETURN_IF(dh == 0, TP_ERR_INVALID_ARG);
+  TP_CHECK_PTR(K);
+  TP_CHECK_PTR(offsets);
+  TP_CHECK_PTR(dK);
+  TP_CHECK_PTR(dV);
+  if (S * T > 0) {
+    TP_CHECK_PTR(Q);
+    TP_CHECK_PTR(dO);
+    TP_CHECK_PTR(kept_weights);
+    TP_CHECK_PTR(entry_ds);
+    TP_CHECK_PTR(entry_lse);
+    TP_CHECK_PTR(order);
+  }
+  return tp::launch_tsrn_attention_bwd_keys(S, T, Tkv, dh, Q, K, dO, kept_weights, entry_ds,
+                                            entry_lse, order, offsets, dK, dV, as_stream(stream));
+}
+
 int tp_tsrn_attention_set_path(int path, int* previous) {
   TP_RETURN_IF(path != TP_ATT_PATH_AUTO && path != TP_ATT_PATH_CUDA_CORES &&
                    path != TP_ATT_PATH_TENSOR_CORES,

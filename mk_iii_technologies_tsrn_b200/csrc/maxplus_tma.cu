@@ -70,6 +70,11 @@ namespace {
 #ifndef TP_TMA_QUNROLL
 #define TP_TMA_QUNROLL 8
 #endif
+// search warpgroup: packed-add units in two alternating buffers (1) or the
+// scalar units with a one-deep prefetch (0)
+#ifndef TP_TMA_LEAN_SEARCH
+#define TP_TMA_LEAN_SEARCH 0
+#endif
 
 constexpr int QUNROLL = TP_TMA_QUNROLL;
 constexpr int BM = 128;
@@ -283,6 +288,81 @@ __device__ __forceinline__ void load_unit(const float* xr, const float* wr, int 
     b0 = make_float4(wv[0], wv[1], wv[2], wv[3]);
     b1 = make_float4(wv[4], wv[5], wv[6], wv[7]);
   }
+}
+
+// Packed form of a search unit: x and w of 8 consecutive k as four 64-bit
+// pairs each; the eight sums come from four add.rn.f32x2 (each sum one
+// rounded fp32 add, as in the main loop) and the max tree from three 3-input
+// and one 2-input NaN-propagating max.
+struct Unit8 {
+  ulonglong2 x0, x1, w0, w1;
+};
+
+__device__ __forceinline__ void load_unit8(const float* xr, const float* wr, int k, int K,
+                                           Unit8& u) {
+  if (k + 8 <= K) {
+    u.x0 = __ldg(reinterpret_cast<const ulonglong2*>(xr));
+    u.x1 = __ldg(reinterpret_cast<const ulonglong2*>(xr + 4));
+    u.w0 = __ldg(reinterpret_cast<const ulonglong2*>(wr));
+    u.w1 = __ldg(reinterpret_cast<const ulonglong2*>(wr + 4));
+  } else {
+    float4 a0, a1, b0, b1;
+    load_unit(xr, wr, k, K, a0, a1, b0, b1);
+    u.x0 = *reinterpret_cast<const ulonglong2*>(&a0);
+    u.x1 = *reinterpret_cast<const ulonglong2*>(&a1);
+    u.w0 = *reinterpret_cast<const ulonglong2*>(&b0);
+    u.w1 = *reinterpret_cast<const ulonglong2*>(&b1);
+  }
+}
+
+__device__ __forceinline__ void add2_split(uint64_t a, uint64_t b, float& lo, float& hi) {
+  asm("{\n\t.reg .b64 s;\n\tadd.rn.f32x2 s, %2, %3;\n\tmov.b64 {%0, %1}, s;\n\t}"
+      : "=f"(lo), "=f"(hi)
+      : "l"(a), "l"(b));
+}
+
+__device__ __forceinline__ int unit8_first_hit(float tv, bool tnan, int k, int K, const Unit8& u) {
+  float s[8];
+  add2_split(u.x0.x, u.w0.x, s[0], s[1]);
+  add2_split(u.x0.y, u.w0.y, s[2], s[3]);
+  add2_split(u.x1.x, u.w1.x, s[4], s[5]);
+  add2_split(u.x1.y, u.w1.y, s[6], s[7]);
+  float mx = tp_max3_nan(s[0], s[1], s[2]);
+  mx = tp_max3_nan(mx, s[3], s[4]);
+  mx = tp_max3_nan(mx, s[5], s[6]);
+  mx = tp_max_nan(mx, s[7]);
+  int best = kBestNone;
+  if (tnan ? (mx != mx) : (mx == tv)) {
+#pragma unroll
+    for (int e = 7; e >= 0; --e) {
+      const bool hit = (k + e < K) && (tnan ? (s[e] != s[e]) : (s[e] == tv));
+      if (hit) best = k + e;
+    }
+  }
+  return best;
+}
+
+// first k of the chunk [kc, kc + 8 * UPO) of output row xr / wr whose sum
+// equals tv (NaN: is NaN), or kBestNone; two units in flight, alternating
+// between two buffers (no register copies)
+template <int UPO>
+__device__ __forceinline__ int search_chunk(const float* xr, const float* wr, int kc, int K,
+                                            float tv) {
+  const bool tnan = tv != tv;
+  Unit8 A, B;
+  load_unit8(xr, wr, kc, K, A);
+#pragma unroll
+  for (int u = 0; u < UPO; u += 2) {
+    if (u + 1 < UPO) load_unit8(xr + 8 * (u + 1), wr + 8 * (u + 1), kc + 8 * (u + 1), K, B);
+    int best = unit8_first_hit(tv, tnan, kc + 8 * u, K, A);
+    if (best != kBestNone) return best;
+    if (u + 1 < UPO) {
+      if (u + 2 < UPO) load_unit8(xr + 8 * (u + 2), wr + 8 * (u + 2), kc + 8 * (u + 2), K, A);
+      best = unit8_first_hit(tv, tnan, kc + 8 * (u + 1), K, B);
+      if (best != kBestNone) return best;
+    }
+  }
+  return kBestNone;
 }
 
 // final value (bias, scale) and argmax of output (m, n), to y/argmax and to
@@ -516,6 +596,9 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
           }
           const float* xr = p.x + (int64_t)m * p.ldx + kc;
           const float* wr = wrow + kc;
+#if TP_TMA_LEAN_SEARCH
+          const int best = search_chunk<UPO>(xr, wr, kc, Kc, tv);
+#else
           float4 a0, a1, b0, b1;
           load_unit(xr, wr, kc, Kc, a0, a1, b0, b1);
           int best = kBestNone;
@@ -530,6 +613,7 @@ __global__ void __launch_bounds__(C::template threads32<kArgmax>(), 1)
             b0 = d0;
             b1 = d1;
           }
+#endif
           store_output(p, m, n, tv, best != kBestNone ? best : kc);
           tv = ntv;
           kc = nkc;

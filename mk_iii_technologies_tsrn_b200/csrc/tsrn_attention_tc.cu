@@ -55,11 +55,13 @@ constexpr int TC_N = 64;            // keys per tile = accumulator columns
 constexpr int TC_KP = 96;           // feature channels, padded: 3 swizzle atoms
 constexpr int TC_ATOM = 32;         // fp32 channels per 128-byte swizzled row
 constexpr int TC_LIST = 16;         // per-thread score list (top_k <= 16)
-constexpr int TC_KCAP = 12;         // kept keys listed per row half in shared memory
+constexpr int TC_KCAP = 16;         // kept keys listed per row half in shared memory (>= top_k)
 constexpr int TC_EPI_WARPS = 8;     // two per TMEM lane quarter
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
 constexpr int TC_TMEM_COLS = 128;   // two accumulators of TC_N columns
 constexpr int TC_MAX_DH = 96;
+constexpr int TC_LISTS_OUT = 2 * TC_KCAP;   // kept keys per row saved for the backward
+static_assert(TC_LISTS_OUT == TSRN_ATT_LIST, "saved list width");
 
 constexpr uint32_t TC_Q_ATOM_FLOATS = TC_M * TC_ATOM;     // 16 KB
 constexpr uint32_t TC_K_ATOM_FLOATS = TC_N * TC_ATOM;     // 8 KB
@@ -68,9 +70,11 @@ constexpr uint32_t TC_K_STAGE_BYTES = 2 * 3 * TC_K_ATOM_FLOATS * 4;
 constexpr size_t TC_LIST_BYTES = (size_t)2 * TC_KCAP * TC_M * 8;   // kept lists (j, S) per half
 static_assert((size_t)2 * TC_LIST * TC_M * 4 <= TC_LIST_BYTES,
               "pass-1 score lists are merged in the kept-list space");
+// (the per-row counts, normalisers and maxima of the gather live in the query
+// tile's space, free once the last MMA has read it)
+static_assert((size_t)TC_M * 4 * 5 <= TC_Q_BYTES, "gather state fits the query tile");
 constexpr size_t TC_SMEM_BYTES = 1024                          // alignment slack
                                  + TC_Q_BYTES + 2 * TC_K_STAGE_BYTES + TC_LIST_BYTES
-                                 + (size_t)TC_M * 4 * 5        // counts, normalisers, row max
                                  + 16 * 8;                     // barriers, TMEM address, flags
 
 // instruction descriptor of tcgen05.mma kind::tf32: fp32 accumulator, TF32 A
@@ -177,6 +181,12 @@ struct TcArgs {
   const float* kmx;       // [S][Kp]
   float* out;             // [S][T][dh]
   float* qlo;             // [S][Tp][TC_KP]: query-feature lo plane (overflow scratch of half 1)
+  // optional (training): each row's kept keys and softmax weights, half 0's
+  // list then half 1's, [S][T][TC_LISTS_OUT] (j = -1 past the end), and the
+  // count per row [S][T] (-1 when a half overflowed its list)
+  int* kj;
+  float* kp;
+  int* kn;
   int* err;
 };
 
@@ -223,10 +233,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   int* s_kj = reinterpret_cast<int*>(lists);                       // [half][TC_KCAP][TC_M]
   float* s_ks = reinterpret_cast<float*>(s_kj + 2 * TC_KCAP * TC_M);   // [half][TC_KCAP][TC_M]
   float* s_lst = reinterpret_cast<float*>(lists);                  // pass 1: [half][TC_LIST][TC_M]
-  int* s_cnt = reinterpret_cast<int*>(lists + TC_LIST_BYTES);      // [half][TC_M]
+  // gather state, written after the last MMA: in the query tile's space
+  int* s_cnt = reinterpret_cast<int*>(sQ);                         // [half][TC_M]
   float* s_z = reinterpret_cast<float*>(s_cnt + 2 * TC_M);         // [half][TC_M]
   float* s_rmax = s_z + 2 * TC_M;                                  // [TC_M]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_rmax + TC_M);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(lists + TC_LIST_BYTES);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;        // [2]
   uint64_t* k_empty = bars + 3;       // [2]
@@ -544,6 +555,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               for (int q = 0; q < 3; ++q) oacc[q] = fmaf(wv, val[e][q], oacc[q]);
             }
         }
+        if (p.kj != nullptr) {
+          // the row's kept keys and weights for the backward: lane e writes
+          // entry e (half 0's list, then half 1's)
+          const int64_t lrow = slice * p.T + ii;
+          const bool over = c0 > TC_KCAP || c1 > TC_KCAP;
+          if (lane < TC_LISTS_OUT) {
+            const int hh = lane >= c0 ? 1 : 0;
+            const int e = hh ? lane - c0 : lane;
+            const bool ok = !over && e < (hh ? c1 : c0);
+            const int slot = (hh * TC_KCAP + (ok ? e : 0)) * TC_M + row;
+            p.kj[lrow * TC_LISTS_OUT + lane] = ok ? s_kj[slot] : -1;
+            p.kp[lrow * TC_LISTS_OUT + lane] = ok ? expf(s_ks[slot] - rmax) * invz : 0.0f;
+          }
+          if (lane == 0) p.kn[lrow] = over ? -1 : c0 + c1;
+        }
         // kept keys past the lists, accumulated (unnormalised) in scratch rows
         const float* ov1 = p.qlo + (slice * p.Tp + ii) * TC_KP;
 #pragma unroll
@@ -629,7 +655,8 @@ int64_t tsrn_attention_tc_workspace_floats(int64_t B, int64_t H, int64_t T, int6
 
 int launch_tsrn_attention_tc(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc, int64_t dh,
                              const float* Q, const float* K, const float* V, const float* slopes,
-                             int top_k, int causal, float* out, float* ws, cudaStream_t stream) {
+                             int top_k, int causal, float* out, float* ws, cudaStream_t stream,
+                             int* kj, float* kp, int* kn) {
   const TcLayout l = tc_layout(B, H, T, Tkv);
   const int64_t S = B * H;
   if (S * (l.Tp > l.Kp ? l.Tp : l.Kp) >= ((int64_t)1 << 31)) return TP_ERR_TOO_LARGE;
@@ -652,7 +679,7 @@ int launch_tsrn_attention_tc(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64
       !make_feat_map(&mkh, khi, S * l.Kp, TC_N) || !make_feat_map(&mkl, klo, S * l.Kp, TC_N))
     return TP_ERR_UNSUPPORTED;
   TcArgs a{S, H, T, Tkv, Tc, l.Tp, l.Kp, (int)dh, top_k, causal, (int)ceil_div(dh, 8),
-           Q, K, V, slopes, qmx, kmx, out, qlo, device_error_ptr()};
+           Q, K, V, slopes, qmx, kmx, out, qlo, kj, kp, kn, device_error_ptr()};
   cudaError_t e = cudaFuncSetAttribute(att_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)TC_SMEM_BYTES);
   if (e != cudaSuccess) return cuda_status(e);

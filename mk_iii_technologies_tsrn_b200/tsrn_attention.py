@@ -11,11 +11,11 @@ state dict loads unchanged.  The computation is this library's:
 * one kernel (``tp_tsrn_attention_fwd``) computes the log-sum-exp tropical
   score, ALiBi, the causal mask, the top-k threshold, the softmax and @V
   without materialising the T x T scores;
-* in training, :class:`TopKAttentionFunction` keeps that forward and supplies
-  an analytic backward (scores recomputed by the LSE kernel, softmax and top-k
-  mask differentiated in closed form, Q/K gradients by the LSE backward
-  kernel); with attention dropout the forward runs densely so that the
-  dropped weights are the ones differentiated.
+* in training, :class:`TopKAttentionFunction` keeps that forward (saving each
+  row's kept keys) and supplies a sparse analytic backward over the kept
+  (query, key) pairs (``ops.tsrn_attention_sparse_bwd``); with attention
+  dropout the forward runs densely so that the dropped weights are the ones
+  differentiated, and the backward recomputes the dense scores.
 """
 from __future__ import annotations
 
@@ -120,7 +120,14 @@ class TopKAttentionFunction(torch.autograd.Function):
     """Tropical top-k attention core: Q, K, V [B, H, T(kv), dh] (rotated) ->
     context [B, H, T, dh].  The top-k cut is not differentiated (the reference
     detaches its threshold).  ``drop_p`` > 0 draws an attention-dropout mask
-    (scaled by 1 / (1 - p)) over the kept weights."""
+    (scaled by 1 / (1 - p)) over the kept weights.
+
+    Without dropout, on shapes the tensor-core kernel takes (dh <= 96,
+    top_k <= 16), the forward saves each row's kept keys and weights and the
+    backward is sparse: two kernels over the ~top_k kept (i, j) of each row
+    (``ops.tsrn_attention_sparse_bwd``).  Otherwise -- dropout, other shapes,
+    or ties that kept more keys than the lists hold -- the backward recomputes
+    the dense scores."""
 
     @staticmethod
     def forward(ctx, Q, K, V, slopes, top_k: int, causal: bool, Tc: int, drop_p: float):
@@ -128,15 +135,22 @@ class TopKAttentionFunction(torch.autograd.Function):
         if drop_p > 0.0:
             P = torch.softmax(_masked_scores(Q, K, slopes, top_k, causal, Tc), dim=-1)
             keep = (torch.rand_like(P) >= drop_p).to(P.dtype) / (1.0 - drop_p)
-            ctx.save_for_backward(Q, K, V, slopes, keep)
+            ctx.save_for_backward(Q, K, V, slopes, keep, None, None, None)
             return (P * keep) @ V
-        ctx.save_for_backward(Q, K, V, slopes, None)
+        if ops.tsrn_attention_supports_lists(Q.shape[-1], top_k):
+            out, kj, kp, kn = ops.tsrn_attention_train_fwd(Q, K, V, slopes, top_k, causal, Tc)
+            ctx.save_for_backward(Q, K, V, slopes, None, kj, kp, kn)
+            return out
+        ctx.save_for_backward(Q, K, V, slopes, None, None, None, None)
         return ops.tsrn_attention(Q, K, V, slopes, top_k, causal, Tc)
 
     @staticmethod
     def backward(ctx, dO):
-        Q, K, V, slopes, keep = ctx.saved_tensors
+        Q, K, V, slopes, keep, kj, kp, kn = ctx.saved_tensors
         top_k, causal, Tc, _ = ctx.args
+        if kj is not None and (kn.numel() == 0 or int(kn.min()) >= 0):
+            dQ, dK, dV = ops.tsrn_attention_sparse_bwd(Q, K, V, dO, kj, kp, kn)
+            return dQ, dK, dV, None, None, None, None, None
         P = torch.softmax(_masked_scores(Q, K, slopes, top_k, causal, Tc), dim=-1)
         Pd = P * keep if keep is not None else P
         dV = Pd.transpose(-1, -2) @ dO

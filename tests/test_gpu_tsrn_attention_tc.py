@@ -89,7 +89,7 @@ def test_long_cached_keys_beyond_the_cuda_core_limit(cuda, path):
 @pytest.mark.parametrize("causal", [True, False])
 def test_exact_ties_keep_every_tied_key(cuda, path, causal):
     # equal keys and no ALiBi: every score of a row ties, so every visible key
-    # is kept (in the tensor-core kernel, rows with more than 12 kept keys in
+    # is kept (in the tensor-core kernel, rows with more than 16 kept keys in
     # either half of the key columns overflow the shared-memory lists and
     # accumulate those V rows in scratch rows)
     B, H, T, dh, top_k = 1, 2, 100, 32, 8
