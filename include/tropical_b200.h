@@ -323,37 +323,47 @@ TP_API int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, i
  *   kernel (dh <= 96, top_k <= 16; else TP_ERR_UNSUPPORTED) that also saves,
  *   per query row (b, h, i), its kept keys and softmax weights:
  *   kept_keys [B*H*T][TP_ATT_LIST] int32 (-1 past the row's entries),
- *   kept_weights [B*H*T][TP_ATT_LIST] fp32, kept_count [B*H*T] int32 (-1 when
- *   ties kept more keys than the lists hold: use a dense backward then).
- * tp_tsrn_attention_bwd_rows: per row, dP = dO_i . V_j, dS = P (dP - sum P dP),
- *   L = logsumexp_c(Q_i + K_j) for every kept j, and
- *   dQ_i = sum_j dS_ij exp(Q_i + K_j - L_ij); stores dS and L per entry
- *   (entry_ds, entry_lse: [B*H*T][TP_ATT_LIST]).  S = B*H.
+ *   kept_weights [B*H*T][TP_ATT_LIST] fp32, kept_lse [B*H*T][TP_ATT_LIST] fp32
+ *   (L_ij = logsumexp_c(Q_ic + K_jc): the kernel's score with its ALiBi term
+ *   added back), kept_count [B*H*T] int32 (-1 when ties kept more keys than
+ *   the lists hold: use a dense backward then).
+ * tp_tsrn_attention_bwd_rows: per row, dP = dO_i . V_j and
+ *   dS = P (dP - sum P dP) for every kept j, and
+ *   dQ_i = sum_j dS_ij exp(Q_i + K_j - L_ij); stores dS per entry (entry_ds
+ *   [B*H*T][TP_ATT_LIST]).  S = B*H.
+ * tp_tsrn_attention_bwd_group: groups the entries of each slice by key,
+ *   rows ascending inside a key (a stable counting sort, one CTA per slice;
+ *   Tkv up to 17000 keys, else TP_ERR_TOO_LARGE): entry ids
+ *   (row * TP_ATT_LIST + slot) into order [S*T*TP_ATT_LIST] (slice s's in its
+ *   own segment from s*T*TP_ATT_LIST), and per key (slice * Tkv + j) the start
+ *   key_begin and length key_count of its run.
  * tp_tsrn_attention_bwd_keys: dK_j = sum_i dS_ij exp(Q_i + K_j - L_ij) and
- *   dV_j = sum_i P_ij dO_i over the entries that kept key j: `order` lists the
- *   entry ids (row * TP_ATT_LIST + slot) sorted by key (slice * Tkv + j) with
- *   rows ascending within a key (a stable sort of the row-major entries);
- *   offsets [S*Tkv + 1] bound each key's run.  Every key of every slice is
- *   written (zero when nothing kept it).  Both backward kernels add in a fixed
- *   order: results repeat bit for bit. */
+ *   dV_j = sum_i P_ij dO_i over each key's run.  Every key of every slice is
+ *   written (zero when nothing kept it).  All three backward kernels add in a
+ *   fixed order: results repeat bit for bit. */
 #define TP_ATT_LIST 32
 TP_API int tp_tsrn_attention_fwd_lists(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc,
                                        int64_t dh, const float* Q, const float* K,
                                        const float* V, const float* alibi_slopes, int top_k,
                                        int causal, float* out, int32_t* kept_keys,
-                                       float* kept_weights, int32_t* kept_count,
-                                       void* workspace, int64_t workspace_bytes, void* stream);
+                                       float* kept_weights, float* kept_lse,
+                                       int32_t* kept_count, void* workspace,
+                                       int64_t workspace_bytes, void* stream);
 TP_API int tp_tsrn_attention_bwd_rows(int64_t S, int64_t T, int64_t Tkv, int64_t dh,
                                       const float* Q, const float* K, const float* V,
                                       const float* dO, const int32_t* kept_keys,
-                                      const float* kept_weights, const int32_t* kept_count,
-                                      float* dQ, float* entry_ds, float* entry_lse, void* stream);
+                                      const float* kept_weights, const float* kept_lse,
+                                      const int32_t* kept_count, float* dQ, float* entry_ds,
+                                      void* stream);
+TP_API int tp_tsrn_attention_bwd_group(int64_t S, int64_t T, int64_t Tkv,
+                                       const int32_t* kept_keys, int32_t* order,
+                                       int32_t* key_begin, int32_t* key_count, void* stream);
 TP_API int tp_tsrn_attention_bwd_keys(int64_t S, int64_t T, int64_t Tkv, int64_t dh,
                                       const float* Q, const float* K, const float* dO,
-                                      const float* kept_weights, const float* entry_ds,
-                                      const float* entry_lse, const int32_t* order,
-                                      const int64_t* offsets, float* dK, float* dV,
-                                      void* stream);
+                                      const float* kept_weights, const float* kept_lse,
+                                      const float* entry_ds, const int32_t* order,
+                                      const int32_t* key_begin, const int32_t* key_count,
+                                      float* dK, float* dV, void* stream);
 
 /* Kernel choice of tp_tsrn_attention_fwd for this process: TP_ATT_PATH_AUTO
  * (tensor cores where supported and T >= 128, else CUDA cores within their

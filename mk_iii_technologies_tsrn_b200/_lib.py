@@ -153,17 +153,21 @@ SIGNATURES: dict[str, tuple] = {
     "tp_tsrn_attention_fwd_lists": (
         _c_int,
         [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_int, _c_int,
-         _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p],
+         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p],
     ),
     "tp_tsrn_attention_bwd_rows": (
         _c_int,
         [_c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
          _c_p, _c_p],
     ),
+    "tp_tsrn_attention_bwd_group": (
+        _c_int,
+        [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p],
+    ),
     "tp_tsrn_attention_bwd_keys": (
         _c_int,
         [_c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
-         _c_p, _c_p],
+         _c_p, _c_p, _c_p],
     ),
     "tp_tsrn_attention_set_path": (_c_int, [_c_int, _c_p]),
     "tp_maslov_softmax_fwd": (

@@ -556,8 +556,9 @@ int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t 
 int tp_tsrn_attention_fwd_lists(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc,
                                 int64_t dh, const float* Q, const float* K, const float* V,
                                 const float* alibi_slopes, int top_k, int causal, float* out,
-                                int32_t* kept_keys, float* kept_weights, int32_t* kept_count,
-                                void* workspace, int64_t workspace_bytes, void* stream) {
+                                int32_t* kept_keys, float* kept_weights, float* kept_lse,
+                                int32_t* kept_count, void* workspace, int64_t workspace_bytes,
+                                void* stream) {
   TP_RETURN_IF(B < 0 || H < 0 || T < 0 || Tkv < 0 || Tc < 0 || dh < 0, TP_ERR_INVALID_ARG);
   TP_RETURN_IF(Tc > Tkv, TP_ERR_INVALID_ARG);
   if (B * H * T == 0) return TP_OK;
@@ -570,6 +571,7 @@ int tp_tsrn_attention_fwd_lists(int64_t B, int64_t H, int64_t T, int64_t Tkv, in
   TP_CHECK_PTR(out);
   TP_CHECK_PTR(kept_keys);
   TP_CHECK_PTR(kept_weights);
+  TP_CHECK_PTR(kept_lse);
   TP_CHECK_PTR(kept_count);
   TP_RETURN_IF(workspace == nullptr ||
                    workspace_bytes < tp_tsrn_attention_workspace_bytes(B, H, T, Tkv, dh),
@@ -578,14 +580,14 @@ int tp_tsrn_attention_fwd_lists(int64_t B, int64_t H, int64_t T, int64_t Tkv, in
   TP_CHECK_PTR(workspace);
   return tp::launch_tsrn_attention_tc(B, H, T, Tkv, Tc, dh, Q, K, V, alibi_slopes, top_k, causal,
                                       out, (float*)workspace, as_stream(stream), kept_keys,
-                                      kept_weights, kept_count);
+                                      kept_weights, kept_lse, kept_count);
 }
 
 int tp_tsrn_attention_bwd_rows(int64_t S, int64_t T, int64_t Tkv, int64_t dh, const float* Q,
                                const float* K, const float* V, const float* dO,
                                const int32_t* kept_keys, const float* kept_weights,
-                               const int32_t* kept_count, float* dQ, float* entry_ds,
-                               float* entry_lse, void* stream) {
+                               const float* kept_lse, const int32_t* kept_count, float* dQ,
+                               float* entry_ds, void* stream) {
   TP_RETURN_IF(S < 0 || T < 0 || Tkv < 0 || dh < 0, TP_ERR_INVALID_ARG);
   if (S * T == 0) return TP_OK;
   TP_RETURN_IF(Tkv == 0 || dh == 0, TP_ERR_INVALID_ARG);
@@ -595,37 +597,54 @@ int tp_tsrn_attention_bwd_rows(int64_t S, int64_t T, int64_t Tkv, int64_t dh, co
   TP_CHECK_PTR(dO);
   TP_CHECK_PTR(kept_keys);
   TP_CHECK_PTR(kept_weights);
+  TP_CHECK_PTR(kept_lse);
   TP_CHECK_PTR(kept_count);
   TP_CHECK_PTR(dQ);
   TP_CHECK_PTR(entry_ds);
-  TP_CHECK_PTR(entry_lse);
   return tp::launch_tsrn_attention_bwd_rows(S, T, Tkv, dh, Q, K, V, dO, kept_keys, kept_weights,
-                                            kept_count, dQ, entry_ds, entry_lse,
+                                            kept_lse, kept_count, dQ, entry_ds,
                                             as_stream(stream));
+}
+
+int tp_tsrn_attention_bwd_group(int64_t S, int64_t T, int64_t Tkv, const int32_t* kept_keys,
+                                int32_t* order, int32_t* key_begin, int32_t* key_count,
+                                void* stream) {
+  TP_RETURN_IF(S < 0 || T < 0 || Tkv < 0, TP_ERR_INVALID_ARG);
+  if (S * Tkv == 0) return TP_OK;
+  TP_CHECK_PTR(key_begin);
+  TP_CHECK_PTR(key_count);
+  if (S * T > 0) {
+    TP_CHECK_PTR(kept_keys);
+    TP_CHECK_PTR(order);
+  }
+  return tp::launch_tsrn_attention_bwd_group(S, T, Tkv, kept_keys, order, key_begin, key_count,
+                                             as_stream(stream));
 }
 
 int tp_tsrn_attention_bwd_keys(int64_t S, int64_t T, int64_t Tkv, int64_t dh, const float* Q,
                                const float* K, const float* dO, const float* kept_weights,
-                               const float* entry_ds, const float* entry_lse,
-                               const int32_t* order, const int64_t* offsets, float* dK,
-                               float* dV, void* stream) {
+                               const float* kept_lse, const float* entry_ds,
+                               const int32_t* order, const int32_t* key_begin,
+                               const int32_t* key_count, float* dK, float* dV, void* stream) {
   TP_RETURN_IF(S < 0 || T < 0 || Tkv < 0 || dh < 0, TP_ERR_INVALID_ARG);
   if (S * Tkv == 0) return TP_OK;
   TP_RETURN_IF(dh == 0, TP_ERR_INVALID_ARG);
   TP_CHECK_PTR(K);
-  TP_CHECK_PTR(offsets);
+  TP_CHECK_PTR(key_begin);
+  TP_CHECK_PTR(key_count);
   TP_CHECK_PTR(dK);
   TP_CHECK_PTR(dV);
   if (S * T > 0) {
     TP_CHECK_PTR(Q);
     TP_CHECK_PTR(dO);
     TP_CHECK_PTR(kept_weights);
+    TP_CHECK_PTR(kept_lse);
     TP_CHECK_PTR(entry_ds);
-    TP_CHECK_PTR(entry_lse);
     TP_CHECK_PTR(order);
   }
   return tp::launch_tsrn_attention_bwd_keys(S, T, Tkv, dh, Q, K, dO, kept_weights, entry_ds,
-                                            entry_lse, order, offsets, dK, dV, as_stream(stream));
+                                            kept_lse, order, key_begin, key_count, dK, dV,
+                                            as_stream(stream));
 }
 
 int tp_tsrn_attention_set_path(int path, int* previous) {

@@ -215,17 +215,20 @@ int64_t tsrn_attention_tc_workspace_floats(int64_t B, int64_t H, int64_t T, int6
 int launch_tsrn_attention_tc(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc, int64_t dh,
                              const float* Q, const float* K, const float* V, const float* slopes,
                              int top_k, int causal, float* out, float* ws, cudaStream_t stream,
-                             int* kj = nullptr, float* kp = nullptr, int* kn = nullptr);
+                             int* kj = nullptr, float* kp = nullptr, float* kl = nullptr,
+                             int* kn = nullptr);
 constexpr int TSRN_ATT_LIST = 32;   // kept keys per row in the saved lists (two halves of 16)
 int launch_tsrn_attention_bwd_rows(int64_t S, int64_t T, int64_t Tkv, int64_t dh, const float* Q,
                                    const float* K, const float* V, const float* dO,
-                                   const int* kj, const float* kp, const int* kn, float* dQ,
-                                   float* eds, float* eL, cudaStream_t stream);
+                                   const int* kj, const float* kp, const float* kl,
+                                   const int* kn, float* dQ, float* eds, cudaStream_t stream);
+int launch_tsrn_attention_bwd_group(int64_t S, int64_t T, int64_t Tkv, const int* kj, int* order,
+                                    int* key_begin, int* key_count, cudaStream_t stream);
 int launch_tsrn_attention_bwd_keys(int64_t S, int64_t T, int64_t Tkv, int64_t dh, const float* Q,
                                    const float* K, const float* dO, const float* kp,
-                                   const float* eds, const float* eL, const int* order,
-                                   const int64_t* offsets, float* dK, float* dV,
-                                   cudaStream_t stream);
+                                   const float* eds, const float* kl, const int* order,
+                                   const int* key_begin, const int* key_count, float* dK,
+                                   float* dV, cudaStream_t stream);
 
 // tsrn_prologue.cu: QK LayerNorm + rotary embedding + head-major layout of Q/K/V
 int launch_tsrn_prologue(int64_t B, int64_t T, int64_t H, int64_t dh, const float* qkv, int64_t ld,

@@ -186,6 +186,7 @@ struct TcArgs {
   // count per row [S][T] (-1 when a half overflowed its list)
   int* kj;
   float* kp;
+  float* kl;              // [S][T][TC_LISTS_OUT]: the entry's log-sum-exp score before ALiBi
   int* kn;
   int* err;
 };
@@ -530,30 +531,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const float invz = 1.0f / (s_z[row] + s_z[TC_M + row]);
         float* orr = p.out + (slice * p.T + ii) * p.dh;
         float oacc[3] = {0.0f, 0.0f, 0.0f};
-        // each half's listed keys at once: every V load of the half in flight
-        // together (one L2 round trip per half instead of one per 4 keys);
-        // accumulated in list order (ascending key), half 0 first
+        // each half's listed keys eight at a time: the eight V rows' loads in
+        // flight together (one L2 round trip per eight keys); accumulated in
+        // list order (ascending key), half 0 first
         for (int hh = 0; hh < 2; ++hh) {
           const int n = min(hh ? c1 : c0, TC_KCAP);
-          if (n == 0) continue;
-          int jj[TC_KCAP];
-          float val[TC_KCAP][3];
+          for (int e0 = 0; e0 < n; e0 += 8) {
+            int jj[8];
+            float val[8][3];
 #pragma unroll
-          for (int e = 0; e < TC_KCAP; ++e) {
-            jj[e] = e < n ? s_kj[(hh * TC_KCAP + e) * TC_M + row] : -1;
+            for (int e = 0; e < 8; ++e) {
+              jj[e] = e0 + e < n ? s_kj[(hh * TC_KCAP + e0 + e) * TC_M + row] : -1;
 #pragma unroll
-            for (int q = 0; q < 3; ++q) {
-              const int c = lane + 32 * q;
-              val[e][q] = (jj[e] >= 0 && c < p.dh) ? __ldg(Vs + (int64_t)jj[e] * p.dh + c) : 0.0f;
+              for (int q = 0; q < 3; ++q) {
+                const int c = lane + 32 * q;
+                val[e][q] =
+                    (jj[e] >= 0 && c < p.dh) ? __ldg(Vs + (int64_t)jj[e] * p.dh + c) : 0.0f;
+              }
             }
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              if (jj[e] >= 0) {
+                const float wv = expf(s_ks[(hh * TC_KCAP + e0 + e) * TC_M + row] - rmax) * invz;
+#pragma unroll
+                for (int q = 0; q < 3; ++q) oacc[q] = fmaf(wv, val[e][q], oacc[q]);
+              }
           }
-#pragma unroll
-          for (int e = 0; e < TC_KCAP; ++e)
-            if (jj[e] >= 0) {
-              const float wv = expf(s_ks[(hh * TC_KCAP + e) * TC_M + row] - rmax) * invz;
-#pragma unroll
-              for (int q = 0; q < 3; ++q) oacc[q] = fmaf(wv, val[e][q], oacc[q]);
-            }
         }
         if (p.kj != nullptr) {
           // the row's kept keys and weights for the backward: lane e writes
@@ -565,8 +568,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int e = hh ? lane - c0 : lane;
             const bool ok = !over && e < (hh ? c1 : c0);
             const int slot = (hh * TC_KCAP + (ok ? e : 0)) * TC_M + row;
-            p.kj[lrow * TC_LISTS_OUT + lane] = ok ? s_kj[slot] : -1;
-            p.kp[lrow * TC_LISTS_OUT + lane] = ok ? expf(s_ks[slot] - rmax) * invz : 0.0f;
+            const int jk = ok ? s_kj[slot] : -1;
+            const float sk = s_ks[slot];
+            p.kj[lrow * TC_LISTS_OUT + lane] = jk;
+            p.kp[lrow * TC_LISTS_OUT + lane] = ok ? expf(sk - rmax) * invz : 0.0f;
+            // the score with its ALiBi term added back: the log-sum-exp of
+            // (Q_i + K_j) over the channels, which the backward differentiates
+            p.kl[lrow * TC_LISTS_OUT + lane] =
+                ok ? __fmaf_rn(slope, fabsf((float)(ii - jk + (int)p.Tc)), sk) : 0.0f;
           }
           if (lane == 0) p.kn[lrow] = over ? -1 : c0 + c1;
         }
@@ -656,7 +665,7 @@ int64_t tsrn_attention_tc_workspace_floats(int64_t B, int64_t H, int64_t T, int6
 int launch_tsrn_attention_tc(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc, int64_t dh,
                              const float* Q, const float* K, const float* V, const float* slopes,
                              int top_k, int causal, float* out, float* ws, cudaStream_t stream,
-                             int* kj, float* kp, int* kn) {
+                             int* kj, float* kp, float* kl, int* kn) {
   const TcLayout l = tc_layout(B, H, T, Tkv);
   const int64_t S = B * H;
   if (S * (l.Tp > l.Kp ? l.Tp : l.Kp) >= ((int64_t)1 << 31)) return TP_ERR_TOO_LARGE;
@@ -679,7 +688,7 @@ int launch_tsrn_attention_tc(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64
       !make_feat_map(&mkh, khi, S * l.Kp, TC_N) || !make_feat_map(&mkl, klo, S * l.Kp, TC_N))
     return TP_ERR_UNSUPPORTED;
   TcArgs a{S, H, T, Tkv, Tc, l.Tp, l.Kp, (int)dh, top_k, causal, (int)ceil_div(dh, 8),
-           Q, K, V, slopes, qmx, kmx, out, qlo, kj, kp, kn, device_error_ptr()};
+           Q, K, V, slopes, qmx, kmx, out, qlo, kj, kp, kl, kn, device_error_ptr()};
   cudaError_t e = cudaFuncSetAttribute(att_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)TC_SMEM_BYTES);
   if (e != cudaSuccess) return cuda_status(e);

@@ -821,17 +821,21 @@ def tsrn_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, slopes: to
     return out
 
 
-def tsrn_attention_supports_lists(dh: int, top_k: int) -> bool:
-    """Whether ``tsrn_attention_train_fwd`` (the tensor-core kernel) takes this shape."""
-    return 1 <= dh <= 96 and 1 <= top_k <= 16
+def tsrn_attention_supports_lists(dh: int, top_k: int, Tkv: int = 0) -> bool:
+    """Whether ``tsrn_attention_train_fwd`` (the tensor-core kernel) and the sparse
+    backward (whose grouping kernel holds 3 words per key in shared memory) take
+    this shape."""
+    return 1 <= dh <= 96 and 1 <= top_k <= 16 and Tkv <= 16384
 
 
 def tsrn_attention_train_fwd(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
                              slopes: torch.Tensor, top_k: int, causal: bool = True, Tc: int = 0):
     """``tsrn_attention`` on the tensor-core kernel, also returning what the sparse
     backward needs: per query row its kept keys [B*H*T, 32] (int32, -1 past the
-    row's entries), their softmax weights [B*H*T, 32] and the count [B*H*T]
-    (-1 when ties kept more keys than the lists hold).  dh <= 96, top_k <= 16."""
+    row's entries), their softmax weights and log-sum-exp scores before ALiBi
+    (both [B*H*T, 32]) and the count [B*H*T] (-1 when ties kept more keys than
+    the lists hold).  Returns (out, keys, weights, lse, count).  dh <= 96,
+    top_k <= 16."""
     dev = _require_cuda(Q, K, V, slopes)
     _attention_shapes(Q, K, V, slopes)
     Q, K, V = (_f32(t).contiguous() for t in (Q, K, V))
@@ -842,6 +846,7 @@ def tsrn_attention_train_fwd(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
     rows = B * H * T
     kj = torch.empty(rows, _lib.TP_ATT_LIST, device=dev, dtype=torch.int32)
     kp = torch.empty(rows, _lib.TP_ATT_LIST, device=dev, dtype=torch.float32)
+    kl = torch.empty(rows, _lib.TP_ATT_LIST, device=dev, dtype=torch.float32)
     kn = torch.empty(rows, device=dev, dtype=torch.int32)
     lib = _lib.load()
     ws_bytes = int(lib.tp_tsrn_attention_workspace_bytes(B, H, T, Tkv, dh))
@@ -849,21 +854,21 @@ def tsrn_attention_train_fwd(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
     with torch.cuda.device(dev):
         st = lib.tp_tsrn_attention_fwd_lists(B, H, T, Tkv, int(Tc), dh, _ptr(Q), _ptr(K), _ptr(V),
                                              _ptr(slopes), int(top_k), 1 if causal else 0,
-                                             _ptr(out), _ptr(kj), _ptr(kp), _ptr(kn), _ptr(ws),
-                                             ws.numel() * 4, _stream(dev))
+                                             _ptr(out), _ptr(kj), _ptr(kp), _ptr(kl), _ptr(kn),
+                                             _ptr(ws), ws.numel() * 4, _stream(dev))
     _lib.check(st, "tp_tsrn_attention_fwd_lists")
-    return out, kj, kp, kn
+    return out, kj, kp, kl, kn
 
 
 def tsrn_attention_sparse_bwd(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
                               dO: torch.Tensor, kj: torch.Tensor, kp: torch.Tensor,
-                              kn: torch.Tensor):
+                              kl: torch.Tensor, kn: torch.Tensor):
     """Gradients (dQ, dK, dV) of the fused attention from the kept-key lists of
     ``tsrn_attention_train_fwd`` (every kn >= 0): the backward of
     research/tsrn_dml.py:438-460, :509-524 with the top-k threshold detached.
-    Two kernels; the entries are grouped by key with a stable sort in between,
-    so every gradient is summed in a fixed order."""
-    dev = _require_cuda(Q, K, V, dO, kj, kp, kn)
+    Three kernels (rows: dQ; group: a stable counting sort of the entries by
+    key; keys: dK, dV): every gradient is summed in a fixed order."""
+    dev = _require_cuda(Q, K, V, dO, kj, kp, kl, kn)
     Q, K, V, dO = (_f32(t).contiguous() for t in (Q, K, V, dO))
     B, H, T, dh = Q.shape
     Tkv = K.shape[2]
@@ -872,26 +877,22 @@ def tsrn_attention_sparse_bwd(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,
     dK = torch.empty_like(K)
     dV = torch.empty_like(V)
     eds = torch.empty(S * T, L, device=dev, dtype=torch.float32)
-    eL = torch.empty(S * T, L, device=dev, dtype=torch.float32)
     lib = _lib.load()
     with torch.cuda.device(dev):
         st = lib.tp_tsrn_attention_bwd_rows(S, T, Tkv, dh, _ptr(Q), _ptr(K), _ptr(V), _ptr(dO),
-                                            _ptr(kj), _ptr(kp), _ptr(kn), _ptr(dQ), _ptr(eds),
-                                            _ptr(eL), _stream(dev))
+                                            _ptr(kj), _ptr(kp), _ptr(kl), _ptr(kn), _ptr(dQ),
+                                            _ptr(eds), _stream(dev))
         _lib.check(st, "tp_tsrn_attention_bwd_rows")
-        # entries grouped by key (slice * Tkv + j), rows ascending inside a group
-        keys = kj.view(S, T * L).to(torch.int64)
-        flat = torch.where(keys >= 0,
-                           keys + torch.arange(S, device=dev, dtype=torch.int64)[:, None] * Tkv,
-                           torch.full_like(keys, S * Tkv)).reshape(-1)
-        sorted_keys, order = torch.sort(flat, stable=True)
-        counts = torch.bincount(sorted_keys, minlength=S * Tkv + 1)[:S * Tkv]
-        offsets = torch.zeros(S * Tkv + 1, device=dev, dtype=torch.int64)
-        torch.cumsum(counts, 0, out=offsets[1:])
-        order = order.to(torch.int32)
+        # entries grouped by key (slice * Tkv + j), rows ascending inside a key
+        order = torch.empty(S * T * L, device=dev, dtype=torch.int32)
+        key_begin = torch.empty(S * Tkv, device=dev, dtype=torch.int32)
+        key_count = torch.empty(S * Tkv, device=dev, dtype=torch.int32)
+        st = lib.tp_tsrn_attention_bwd_group(S, T, Tkv, _ptr(kj), _ptr(order), _ptr(key_begin),
+                                             _ptr(key_count), _stream(dev))
+        _lib.check(st, "tp_tsrn_attention_bwd_group")
         st = lib.tp_tsrn_attention_bwd_keys(S, T, Tkv, dh, _ptr(Q), _ptr(K), _ptr(dO), _ptr(kp),
-                                            _ptr(eds), _ptr(eL), _ptr(order), _ptr(offsets),
-                                            _ptr(dK), _ptr(dV), _stream(dev))
+                                            _ptr(kl), _ptr(eds), _ptr(order), _ptr(key_begin),
+                                            _ptr(key_count), _ptr(dK), _ptr(dV), _stream(dev))
         _lib.check(st, "tp_tsrn_attention_bwd_keys")
     return dQ, dK, dV
 

@@ -135,21 +135,21 @@ class TopKAttentionFunction(torch.autograd.Function):
         if drop_p > 0.0:
             P = torch.softmax(_masked_scores(Q, K, slopes, top_k, causal, Tc), dim=-1)
             keep = (torch.rand_like(P) >= drop_p).to(P.dtype) / (1.0 - drop_p)
-            ctx.save_for_backward(Q, K, V, slopes, keep, None, None, None)
+            ctx.save_for_backward(Q, K, V, slopes, keep, None, None, None, None)
             return (P * keep) @ V
-        if ops.tsrn_attention_supports_lists(Q.shape[-1], top_k):
-            out, kj, kp, kn = ops.tsrn_attention_train_fwd(Q, K, V, slopes, top_k, causal, Tc)
-            ctx.save_for_backward(Q, K, V, slopes, None, kj, kp, kn)
+        if ops.tsrn_attention_supports_lists(Q.shape[-1], top_k, K.shape[-2]):
+            out, kj, kp, kl, kn = ops.tsrn_attention_train_fwd(Q, K, V, slopes, top_k, causal, Tc)
+            ctx.save_for_backward(Q, K, V, slopes, None, kj, kp, kl, kn)
             return out
-        ctx.save_for_backward(Q, K, V, slopes, None, None, None, None)
+        ctx.save_for_backward(Q, K, V, slopes, None, None, None, None, None)
         return ops.tsrn_attention(Q, K, V, slopes, top_k, causal, Tc)
 
     @staticmethod
     def backward(ctx, dO):
-        Q, K, V, slopes, keep, kj, kp, kn = ctx.saved_tensors
+        Q, K, V, slopes, keep, kj, kp, kl, kn = ctx.saved_tensors
         top_k, causal, Tc, _ = ctx.args
         if kj is not None and (kn.numel() == 0 or int(kn.min()) >= 0):
-            dQ, dK, dV = ops.tsrn_attention_sparse_bwd(Q, K, V, dO, kj, kp, kn)
+            dQ, dK, dV = ops.tsrn_attention_sparse_bwd(Q, K, V, dO, kj, kp, kl, kn)
             return dQ, dK, dV, None, None, None, None, None
         P = torch.softmax(_masked_scores(Q, K, slopes, top_k, causal, Tc), dim=-1)
         Pd = P * keep if keep is not None else P

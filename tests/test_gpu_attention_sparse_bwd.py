@@ -90,10 +90,10 @@ def test_sparse_backward_repeats_bit_for_bit(cuda):
     B, H, T, dh, k = 2, 4, 256, 80, 16
     Q, K, V, dO = (torch.randn(B, H, T, dh, device=cuda, generator=g) for _ in range(4))
     slopes = 2.0 ** (-8.0 * torch.arange(1, H + 1, device=cuda, dtype=torch.float32) / H)
-    _, kj, kp, kn = ops.tsrn_attention_train_fwd(Q, K, V, slopes, k)
+    _, kj, kp, kl, kn = ops.tsrn_attention_train_fwd(Q, K, V, slopes, k)
     assert int(kn.min()) >= 0
-    first = ops.tsrn_attention_sparse_bwd(Q, K, V, dO, kj, kp, kn)
-    second = ops.tsrn_attention_sparse_bwd(Q, K, V, dO, kj, kp, kn)
+    first = ops.tsrn_attention_sparse_bwd(Q, K, V, dO, kj, kp, kl, kn)
+    second = ops.tsrn_attention_sparse_bwd(Q, K, V, dO, kj, kp, kl, kn)
     for x, y in zip(first, second):
         assert torch.equal(x, y)
 
@@ -106,7 +106,7 @@ def test_lists_match_the_forward(cuda):
     B, H, T, dh, k = 1, 2, 180, 40, 8
     Q, K, V = (torch.randn(B, H, T, dh, device=cuda, generator=g) for _ in range(3))
     slopes = torch.tensor([0.5, 0.01], device=cuda)
-    out, kj, kp, kn = ops.tsrn_attention_train_fwd(Q, K, V, slopes, k)
+    out, kj, kp, kl, kn = ops.tsrn_attention_train_fwd(Q, K, V, slopes, k)
     assert int(kn.min()) >= 0
     assert torch.equal((kj >= 0).sum(dim=1).to(torch.int32), kn)
     torch.testing.assert_close(kp.sum(dim=1), torch.ones(B * H * T, device=cuda),
@@ -116,6 +116,12 @@ def test_lists_match_the_forward(cuda):
     gathered = Vr[rows[:, None], kj.clamp(min=0).long()]          # [rows, 32, dh]
     recon = (kp[..., None] * gathered).sum(dim=1).reshape(B, H, T, dh)
     torch.testing.assert_close(recon, out, rtol=1e-4, atol=1e-5)
+    # the saved scores before ALiBi are logsumexp_c(Q_i + K_j) of the kept pairs
+    Qr, Kr = Q.reshape(B * H * T, dh).double(), K.reshape(B * H, T, dh).double()
+    Kg = Kr[rows[:, None], kj.clamp(min=0).long()]                 # [rows, 32, dh]
+    lse = torch.logsumexp(Qr[:, None, :] + Kg, dim=-1)
+    valid = kj >= 0
+    torch.testing.assert_close(kl.double()[valid], lse[valid], rtol=0, atol=2e-5)
 
 
 def test_tie_overflow_falls_back_to_dense(cuda):
@@ -128,8 +134,8 @@ def test_tie_overflow_falls_back_to_dense(cuda):
     K = torch.randn(B, H, 1, dh, generator=gen).expand(B, H, T, dh).contiguous()
     V = torch.randn(B, H, T, dh, generator=gen)
     slopes = torch.zeros(H)
-    _, _, _, kn = ops.tsrn_attention_train_fwd(Q.to(cuda), K.to(cuda), V.to(cuda),
-                                               slopes.to(cuda), k)
+    _, _, _, _, kn = ops.tsrn_attention_train_fwd(Q.to(cuda), K.to(cuda), V.to(cuda),
+                                                  slopes.to(cuda), k)
     assert int(kn.min()) == -1
     gout = torch.randn(Q.shape, generator=torch.Generator().manual_seed(5))
     out, gq, gk, gv = _grads(cuda, Q, K, V, slopes, k, True, gout)
@@ -144,5 +150,5 @@ def test_tie_overflow_falls_back_to_dense(cuda):
 def test_empty(cuda):
     ops = _ops()
     z = torch.zeros(1, 2, 0, 16, device=cuda)
-    out, kj, kp, kn = ops.tsrn_attention_train_fwd(z, z, z, torch.ones(2, device=cuda), 4)
+    out, kj, kp, kl, kn = ops.tsrn_attention_train_fwd(z, z, z, torch.ones(2, device=cuda), 4)
     assert out.shape == z.shape and kn.numel() == 0
