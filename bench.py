@@ -239,6 +239,17 @@ def parallelism(total: int, local: int, world: int, what: str = "batch") -> str:
     return f"{what}-sharded x{world} (strong: {local} of {total} per rank, no exchange)"
 
 
+TF32_PEAK_SOURCE = ("dense TF32 rate taken as half of MEASURED_PEAKS.json bf16_tflops "
+                    "(cuBLAS bf16 burst; the tensor cores run TF32 at half the bf16 rate); "
+                    "of measured")
+
+
+def tf32_peak():
+    """Dense TF32 tensor-core rate (TFLOP/s): half the measured bf16 GEMM burst rate
+    (fallback 1590 TFLOP/s bf16 when the file is absent)."""
+    return measured_peaks().get("bf16_tflops", 1590.0) / 2.0
+
+
 def ffma_peak():
     """fp32 FMA rate (TFLOP/s) of the register-only probe: the better of scalar
     FFMA (form 7) and packed fma.f32x2 (form 9), measured in this run."""
@@ -994,11 +1005,12 @@ def tsrn_attn_workload(args, world, rank):
     clk = clocks.stop()
     tokens = B * T * world
     value = tokens / (ms / steps / 1e3)
-    # roofline: the score dot products (causal: sum over rows of (i+1) keys, dh FMAs
-    # each) against the measured fp32 FMA rate
-    fmas = B * H * dh * T * (T + 1) / 2
-    peak = ffma_peak()
-    achieved = 2.0 * fmas / (ms / steps / 1e3) / 1e12
+    # roofline: the score contraction on the tensor cores (causal: sum over rows of
+    # (i+1) keys; three TF32 products of dh multiply-adds each, the 3xTF32 split)
+    # against the dense TF32 rate (half the measured bf16 GEMM rate)
+    tf32_flops = 3 * 2.0 * B * H * dh * T * (T + 1) / 2
+    peak = tf32_peak()
+    achieved = tf32_flops / (ms / steps / 1e3) / 1e12
     hout = torch.empty(B, H, T, dh).pin_memory()
 
     def e2e_step():   # the host entry: sequence groups' copies overlap the computation
@@ -1026,13 +1038,13 @@ def tsrn_attn_workload(args, world, rank):
         "e2e": {"value": tokens / (e2e_ms / e2e_steps / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": 3 * hQ.numel() * 4, "d2h_bytes_per_step": hout.numel() * 4},
         "gpu_launches": per_step * steps if per_step is not None else None,
-        "roofline": {"bound": "cuda-core fp32 FMA (score dot products) + selection",
-                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": None,
-                     "kernel": "att_fwd_kernel (score dots, causal) incl. its top-k selection",
-                     "peak_source": "in-repo register-only FMA probe (tp_probe_addmax: best "
-                                    "of scalar FFMA form 7 and packed f32x2 form 9), this "
-                                    "run; of measured"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                     "kernel": "att_tc_kernel (tcgen05 kind::tf32 score contraction, 3xTF32, "
+                               "causal) incl. its two-pass top-k selection and V gather",
+                     "limiter": "the per-score selection epilogue, not the tensor pipe "
+                                "(ncu at B=8: issue active 39%, tensor pipe 9.6%)",
+                     "peak_source": TF32_PEAK_SOURCE},
         "clocks": clk,
     }
 
@@ -1245,15 +1257,20 @@ def tsrn_block_workload(args, world, rank):
         torch.cuda.synchronize()
         esn_ms = e0.elapsed_time(e1) / 3
         del Q, K, V, esn_in, xa
-    peak = ffma_peak()
     dr = d // 2
-    att_flops = 2.0 * B * H * (d // H) * T * (T + 1) / 2
+    att_flops = 3 * 2.0 * B * H * (d // H) * T * (T + 1) / 2
     esn_flops = 2.0 * 3 * B * T * dr * dr
     if att_ms >= esn_ms:
-        dom = {"kernel": "att_fwd_kernel (fused top-k LSE attention; score dot products, causal)",
+        dom = {"kernel": "att_tc_kernel (tcgen05 3xTF32 score contraction, causal, with its "
+                         "top-k selection)", "bound": "tensor", "peak": tf32_peak(),
+               "peak_source": TF32_PEAK_SOURCE,
                "achieved": att_flops / (att_ms / 1e3) / 1e12, "kernel_ms": att_ms}
     else:
         dom = {"kernel": "esn_kernel (GRU reservoir recurrence; latency-bound per step)",
+               "bound": "cuda-core fp32 FMA", "peak": ffma_peak(),
+               "peak_source": "in-repo register-only FMA probe (tp_probe_addmax: best of "
+                              "scalar FFMA form 7 and packed f32x2 form 9), this run; of "
+                              "measured",
                "achieved": esn_flops / (esn_ms / 1e3) / 1e12, "kernel_ms": esn_ms}
     hy = torch.empty(B, T, d).pin_memory()
     dx = torch.empty_like(x)
@@ -1292,12 +1309,10 @@ def tsrn_block_workload(args, world, rank):
         "e2e": {"value": tokens / (e2e_ms / e2e_steps / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": hx.numel() * 4, "d2h_bytes_per_step": hy.numel() * 4},
         "gpu_launches": per_step * steps if per_step is not None else None,
-        "roofline": {"bound": "cuda-core fp32 FMA (dominant kernel)", "achieved": dom["achieved"],
-                     "peak": peak, "unit": "TFLOP/s", "frac": dom["achieved"] / peak,
+        "roofline": {"bound": dom["bound"] + " (dominant kernel)", "achieved": dom["achieved"],
+                     "peak": dom["peak"], "unit": "TFLOP/s", "frac": dom["achieved"] / dom["peak"],
                      "traffic": None, "kernel": dom["kernel"], "kernel_ms": dom["kernel_ms"],
-                     "peak_source": "in-repo register-only FMA probe (tp_probe_addmax: best "
-                                    "of scalar FFMA form 7 and packed f32x2 form 9), this "
-                                    "run; of measured"},
+                     "peak_source": dom["peak_source"]},
         "clocks": clk,
     }
 
