@@ -449,6 +449,14 @@ TP_API int tp_esn_leaky_bwd(int64_t B, int64_t T, int64_t dr, const float* dH, c
                             const float* WsT, int64_t ld_ws, const float* leak, float* dA,
                             float* dHs, void* stream);
 
+/* x = hi + lo for n fp32 values: hi = x with its 13 low mantissa bits cleared
+ * (exact in TF32), lo = x - hi (exact; 0 where x is not finite).  x, hi, lo
+ * 16-byte aligned.  With it, three TF32 tensor-core GEMMs (hi.hi + hi.lo +
+ * lo.hi) reproduce an fp32 GEMM to ~2e-6 relative: the nn.Linear projections
+ * around the tropical branches (research/tsrn_dml.py:462-548, 808-843,
+ * 917-980) run that way in inference.  (Utility; no reference counterpart.) */
+TP_API int tp_split_tf32(const float* x, int64_t n, float* hi, float* lo, void* stream);
+
 /* Copy `rows` rows of width_bytes from src (row pitch src_pitch bytes) to dst
  * (pitch dst_pitch), host or device memory on either side (pinned host memory
  * for an asynchronous copy), on `stream`: the strided time windows the

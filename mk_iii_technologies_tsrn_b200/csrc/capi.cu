@@ -674,6 +674,16 @@ int tp_esn_gru_fwd(int64_t B, int64_t T, int64_t dr, const float* U, const float
   return tp::launch_esn_fwd(true, B, T, dr, U, Uz, Ur, W, ld, nullptr, H, as_stream(stream));
 }
 
+int tp_split_tf32(const float* x, int64_t n, float* hi, float* lo, void* stream) {
+  TP_RETURN_IF(n < 0, TP_ERR_INVALID_ARG);
+  if (n == 0) return TP_OK;
+  TP_CHECK_PTR(x);
+  TP_CHECK_PTR(hi);
+  TP_CHECK_PTR(lo);
+  TP_RETURN_IF(!aligned16(x) || !aligned16(hi) || !aligned16(lo), TP_ERR_MISALIGNED);
+  return tp::launch_split_tf32(x, n, hi, lo, as_stream(stream));
+}
+
 int tp_esn_gru_bwd(int64_t B, int64_t T, int64_t dr, const float* dH, const float* fa,
                    const float* fz, const float* fr, const float* keep, const float* r,
                    const float* WzhT, int64_t ld_wz, const float* WrhT, int64_t ld_wr,

@@ -18,7 +18,6 @@ from __future__ import annotations
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from . import ops
 
@@ -148,11 +147,11 @@ class EchoStateReservoir(nn.Module):
         """(U, Uz, Ur, Wzh, Wrh, Ws) of ``ops.esn_gru_fwd`` for x [B, T, d_model]."""
         dr = self.dr
         Ws = self._scaled_recurrent()
-        U = self.W_in(x)
+        U = ops.linear(x, self.W_in.weight)
         Wzh, Wzu = self.W_z.weight.split(dr, dim=1)
         Wrh, Wru = self.W_r.weight.split(dr, dim=1)
         # both gates' input terms as one GEMM on the stacked input halves
-        Uzr = F.linear(U, torch.cat((Wzu, Wru), dim=0), torch.cat((self.W_z.bias, self.W_r.bias)))
+        Uzr = ops.linear(U, torch.cat((Wzu, Wru), dim=0), torch.cat((self.W_z.bias, self.W_r.bias)))
         Uz, Ur = Uzr.split(dr, dim=-1)
         return U, Uz.contiguous(), Ur.contiguous(), Wzh, Wrh, Ws
 
@@ -162,7 +161,7 @@ class EchoStateReservoir(nn.Module):
             H = GRUReservoirFunction.apply(U, Uz, Ur, Wzh, Wrh, Ws)
         else:
             H = ops.esn_gru_fwd(U, Uz, Ur, Wzh, Wrh, Ws.detach())
-        return self.readout(H)
+        return ops.linear(H, self.readout.weight)
 
 
 class LeakyEchoStateReservoir(nn.Module):
@@ -185,9 +184,9 @@ class LeakyEchoStateReservoir(nn.Module):
         radius = torch.linalg.eigvals(self.W_res).abs().max().real.clamp(min=1e-6)
         Ws = self.W_res * (torch.sigmoid(self.log_rho) * 1.5 / radius)
         lk = torch.sigmoid(self.leak)
-        U = self.W_in(x)
+        U = ops.linear(x, self.W_in.weight)
         if _needs_graph(x, self):
             H = LeakyReservoirFunction.apply(U, Ws, lk.reshape(1))
         else:
             H = ops.esn_leaky_fwd(U, Ws.detach(), lk.detach())
-        return self.readout(H)
+        return ops.linear(H, self.readout.weight)

@@ -9,15 +9,16 @@ as one fused kernel (bit-exact with the sequential recurrence; it differs from
 the closed form by O(T ulp) rounding).  Gradients follow the same argmax path
 (input wins ties, as torch.cummax's last-index rule does).  The three
 projections of the input (gate_B, B_proj, gate_out) run as one GEMM on the
-stacked weights.
+stacked weights (in inference an fp32-accurate 3xTF32 tensor-core GEMM,
+``ops.linear``).
 """
 from __future__ import annotations
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 from torch import Tensor
 
+from . import ops
 from .ops import tropical_scan
 
 
@@ -44,9 +45,9 @@ class TropicalSSM(nn.Module):
         ds, d = self.ds, x.shape[-1]
         w = torch.cat((self.gate_B.weight, self.B_proj.weight, self.gate_out.weight), dim=0)
         b = torch.cat((self.gate_B.bias, self.gate_B.bias.new_zeros(ds), self.gate_out.bias))
-        gb, bp, go = F.linear(x, w, b).split((ds, ds, d), dim=-1)
+        gb, bp, go = ops.linear(x, w, b).split((ds, ds, d), dim=-1)
         u = torch.sigmoid(gb) * bp
         A_c = self.A.clamp(max=0)
         H = tropical_scan(u.contiguous(), None, A_c, 0.0)
-        out = torch.sigmoid(go) * self.C_proj(H)
+        out = torch.sigmoid(go) * ops.linear(H, self.C_proj.weight)
         return torch.sigmoid(self.mix) * out

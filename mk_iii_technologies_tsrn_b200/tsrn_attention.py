@@ -5,7 +5,9 @@ The module keeps the reference's constructor and its parameter / buffer names
 ``alibi_slopes``, ``cross_window_mem.cached_k`` / ``cached_v``), so a reference
 state dict loads unchanged.  The computation is this library's:
 
-* one GEMM projects Q, K and V together (the three weights stacked);
+* one GEMM projects Q, K and V together (the three weights stacked; in
+  inference the projections run as fp32-accurate 3xTF32 tensor-core GEMMs,
+  ``ops.linear``);
 * one kernel (``tp_tsrn_attention_prologue``) applies the per-head QK
   LayerNorm and the rotary embedding and lays Q/K/V out head-major;
 * one kernel (``tp_tsrn_attention_fwd``) computes the log-sum-exp tropical
@@ -196,7 +198,7 @@ class TropicalAttention(nn.Module):
         """Rotated, normalised Q, K and V [B, H, T, dh] of x [B, T, d] (inference:
         one stacked GEMM and the fused prologue kernel)."""
         B, T, d = x.shape
-        qkv = F.linear(x, self._qkv_weight()).reshape(B * T, 3 * d)
+        qkv = ops.linear(x, self._qkv_weight()).reshape(B * T, 3 * d)
         cos, sin = self.rope.tables(T, x.device)
         return ops.tsrn_attention_prologue(qkv, B, T, self.H, self.dh, self.q_norm, self.k_norm,
                                            cos, sin)
@@ -229,4 +231,4 @@ class TropicalAttention(nn.Module):
             ctx = ops.tsrn_attention(Q, K.contiguous(), V.contiguous(), slopes, k, causal, Tc)
         if use_cache:
             self.cross_window_mem.store(Kn, Vn)
-        return self.Wo(ctx.transpose(1, 2).reshape(B, T, d))
+        return ops.linear(ctx.transpose(1, 2).reshape(B, T, d), self.Wo.weight)
