@@ -32,8 +32,17 @@ namespace tp {
 
 namespace {
 
-constexpr int ESN_KS = 8;          // lanes per column (k split)
-constexpr int ESN_MAX_NCL = 64;    // columns per CTA
+// lanes per column (k split) and the most columns a CTA owns (their product is
+// the largest block); build parameters
+#ifndef TP_ESN_KS
+#define TP_ESN_KS 8
+#endif
+#ifndef TP_ESN_MAX_NCL
+#define TP_ESN_MAX_NCL 64
+#endif
+constexpr int ESN_KS = TP_ESN_KS;
+constexpr int ESN_MAX_NCL = TP_ESN_MAX_NCL;
+static_assert(ESN_KS * ESN_MAX_NCL <= 1024, "one CTA holds at most 1024 threads");
 constexpr int ESN_MAX_NT = ESN_MAX_NCL * ESN_KS;
 constexpr int ESN_MAX_RB = 8;      // batch rows per cluster
 
