@@ -42,6 +42,11 @@ TSRN block (research/tsrn_dml.py:1096-1106: fused top-k attention, GRU reservoir
 tropical SSM, with their LayerNorms and projections) on B=64 sequences of
 T=1024 tokens, d=640; tokens/s and each branch's share of the step.
 
+``--workload tsrn_train``: the same branches in training (forward + backward of
+every parameter and the input under autograd: the attention's sparse backward,
+the reservoir's one-launch backward through time, the scan's argmax-path
+backward); tokens/s.
+
 ``--workload dtn``: config 2, the drop-in DTNAttention(256, 8) block
 (tropical Q/K projections with the STE backward, tropical score, Maslov
 softmax) forward + backward at B=128, L=64; metric tokens/s.
@@ -89,7 +94,8 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload",
-                   choices=["gemm", "scan", "dtn", "linear", "tsrn_attn", "esn", "tsrn_block"],
+                   choices=["gemm", "scan", "dtn", "linear", "tsrn_attn", "esn", "tsrn_block",
+                            "tsrn_train"],
                    default="gemm")
     p.add_argument("--size", type=int, default=8192, help="M = N = K of the GEMM workload")
     p.add_argument("--dtype", choices=["f32", "bf16"], default="f32",
@@ -1317,6 +1323,156 @@ def tsrn_block_workload(args, world, rank):
     }
 
 
+def tsrn_train_workload(args, world, rank):
+    """Config 5's tropical branches in training: the first TSRN block's attention
+    (tensor-core forward saving each row's kept keys, sparse backward), GRU
+    reservoir (one-launch forward and backward through time) and tropical SSM
+    (scan forward, argmax-path backward) with their LayerNorms and fp32
+    projections under autograd -- forward + backward of B=64 sequences of
+    T=1024 tokens (split over the ranks), gradients for every parameter and the
+    input."""
+    from mk_iii_technologies_tsrn_b200 import ops, _lib
+
+    _lib.load().tp_set_pointer_checks(0)
+    B = local_batch(TSRN_BLOCK["B"], world, args)
+    T, d, H, k = TSRN_BLOCK["T"], TSRN_BLOCK["d"], TSRN_BLOCK["H"], TSRN_BLOCK["top_k"]
+    dev = torch.device("cuda")
+    m = _tsrn_block_module(dev, 30).train()
+    gen = torch.Generator().manual_seed(50 + rank)
+    hx = torch.randn(B, T, d, generator=gen).pin_memory()
+    hg = torch.randn(B, T, d, generator=gen).pin_memory()
+    x = hx.to(dev).requires_grad_(True)
+    gy = hg.to(dev)
+
+    def step():
+        m.zero_grad(set_to_none=True)
+        x.grad = None
+        y = m(x)
+        y.backward(gy)
+        return y
+
+    # before timing: the training forward agrees with the inference forward on a
+    # slice (fp32 against 3xTF32 projections, the PyTorch prologue against the
+    # fused one: rounding, and near-ties at the top-k cut), and every gradient is
+    # finite
+    if rank == 0:
+        xs = x[:1, :256].detach().clone().requires_grad_(True)
+        ys = m(xs)
+        with torch.no_grad():
+            ye = m(xs.detach())
+        ys.sum().backward()
+        err = ((ys.detach() - ye).abs().max() / ye.abs().max()).item()
+        bad = [n for n, prm in m.named_parameters()
+               if prm.grad is None or not torch.isfinite(prm.grad).all()]
+        if not err < 2e-3 or bad or not torch.isfinite(xs.grad).all():
+            raise RuntimeError(f"TSRN training step check failed ({err}, {bad[:3]})")
+        m.zero_grad(set_to_none=True)
+    for _ in range(args.warmup):
+        step()
+    steps = steps_for(step, args.steps, world)
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    ms = time_steps(step, steps, world)
+    clk = clocks.stop()
+    tokens = B * T * world
+    value = tokens / (ms / steps / 1e3)
+    # the dominant kernel, timed alone on this step's inputs: the reservoir's
+    # backward through time (three dr x dr products per step, as the forward)
+    dr = d // 2
+    with torch.no_grad():
+        U, Uz, Ur, Wzh, Wrh, Ws = m.reservoir.recurrence_inputs(m.ln_res(x.detach()))
+        Hs = ops.esn_gru_fwd(U, Uz, Ur, Wzh, Wrh, Ws)
+        fac = [torch.rand_like(Hs) * 0.25 for _ in range(5)]
+        dH = torch.randn_like(Hs)
+        ops.esn_gru_bwd(dH, *fac, Wzh, Wrh, Ws)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(3):
+            ops.esn_gru_bwd(dH, *fac, Wzh, Wrh, Ws)
+        e1.record()
+        torch.cuda.synchronize()
+        bptt_ms = e0.elapsed_time(e1) / 3
+        del U, Uz, Ur, Hs, fac, dH
+    peak = ffma_peak()
+    achieved = 2.0 * 3 * B * T * dr * dr / (bptt_ms / 1e3) / 1e12
+    hdx = torch.empty(B, T, d).pin_memory()
+
+    def e2e_step():   # inputs and the upstream gradient from host, dL/dx back to host
+        with torch.no_grad():
+            x.copy_(hx, non_blocking=True)
+            gy.copy_(hg, non_blocking=True)
+        step()
+        hdx.copy_(x.grad, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_steps = max(3, min(args.steps, 5))
+    e2e_ms = time_steps(e2e_step, e2e_steps, world)
+    try:
+        per_step = count_library_kernels(step)
+    except Exception:   # profiler unavailable: leave the count out rather than guess
+        per_step = None
+    return {
+        "metric": "TSRN block tropical path training tokens/s (attention + reservoir + SSM, "
+                  "fwd + bwd)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: x and the upstream gradient ~ N(0,1) (seeded), reference "
+                "initialisation (zero-initialised output projections drawn N(0,0.02))",
+        "config": {"workload": f"TSRN block-0 tropical branches, training step, B={B * world} "
+                               f"T={T} d={d} H={H} top_k={k} d_reservoir={dr} (config 5)",
+                   "parallelism": parallelism(TSRN_BLOCK["B"], B, world),
+                   "bptt_kernel_ms": bptt_ms,
+                   "l2": f"residual stream {B * T * d * 4 >> 20} MiB"},
+        "e2e": {"value": tokens / (e2e_ms / e2e_steps / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": 2 * hx.numel() * 4, "d2h_bytes_per_step": hdx.numel() * 4},
+        "gpu_launches": per_step * steps if per_step is not None else None,
+        "roofline": {"bound": "cuda-core fp32 FMA (dominant kernel)", "achieved": achieved,
+                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                     "kernel": "esn_bwd_kernel (GRU reservoir backward through time; "
+                               "latency-bound per step)", "kernel_ms": bptt_ms,
+                     "peak_source": "in-repo register-only FMA probe (tp_probe_addmax: best "
+                                    "of scalar FFMA form 7 and packed f32x2 form 9), this "
+                                    "run; of measured"},
+        "clocks": clk,
+    }
+
+
+def cpu_tsrn_train_rate(target_s: float = 10.0):
+    """The reference block's tropical branches on CPU torch (oracle/torch_ref.py) with
+    autograd: forward + backward of one sequence of T=1024 tokens."""
+    from oracle.torch_ref import tsrn_block_torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    m = _tsrn_block_module(torch.device("cpu"), 30)
+    params = {n for n, _ in m.named_parameters()}
+    T, d, H, k = TSRN_BLOCK["T"], TSRN_BLOCK["d"], TSRN_BLOCK["H"], TSRN_BLOCK["top_k"]
+    gen = torch.Generator().manual_seed(50)
+    x = torch.randn(1, T, d, generator=gen)
+    gy = torch.randn(1, T, d, generator=gen)
+
+    def one():
+        sd = {n: v.detach().clone().requires_grad_(n in params)
+              for n, v in m.state_dict().items()}
+        xx = x.clone().requires_grad_(True)
+        tsrn_block_torch(xx, sd, H, k).backward(gy)
+
+    t0 = time.perf_counter()
+    one()
+    dt = time.perf_counter() - t0
+    reps = int(max(1, min(10, target_s / max(dt, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        one()
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": T / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"1 of {TSRN_BLOCK['B']} sequences (T={T}) through the reference "
+                      f"block's tropical branches on CPU torch, forward + autograd backward, "
+                      f"{reps} reps, {dt:.2f} s each"}
+
+
 def cpu_tsrn_block_rate(target_s: float = 10.0):
     """The reference block's tropical branches on CPU torch (oracle/torch_ref.py, pinned
     to the reference module) on one sequence of T=1024 tokens."""
@@ -1455,6 +1611,12 @@ def reference_arm(args, world, rank):
         metric = "TSRN block tropical path tokens/s (attention + reservoir + SSM, inference)"
         cfg = {"workload": "TSRN block-0 tropical branches d=640 H=8 top_k=16 d_reservoir=320 "
                            "T=1024 (torch CPU)"}
+    elif args.workload == "tsrn_train":
+        cb = cpu_tsrn_train_rate(target_s=max(3.0, 2.0 * args.steps))
+        metric = ("TSRN block tropical path training tokens/s (attention + reservoir + SSM, "
+                  "fwd + bwd)")
+        cfg = {"workload": "TSRN block-0 tropical branches, training step, d=640 H=8 top_k=16 "
+                           "d_reservoir=320 T=1024 (torch CPU, autograd)"}
     elif args.workload == "tsrn_attn":
         cb = cpu_tsrn_attn_rate(target_s=max(3.0, 2.0 * args.steps))
         metric = "TSRN tropical top-k attention tokens/s (fused fwd, inference)"
@@ -1508,6 +1670,7 @@ def secondary_workloads(args, world, rank):
             ("tsrn_attn", tsrn_attn_workload, lambda: cpu_tsrn_attn_rate(target_s=5.0)),
             ("esn", esn_workload, lambda: cpu_esn_rate("gru", target_s=5.0)),
             ("tsrn_block", tsrn_block_workload, lambda: cpu_tsrn_block_rate(target_s=5.0)),
+            ("tsrn_train", tsrn_train_workload, lambda: cpu_tsrn_train_rate(target_s=5.0)),
             ("linear", linear_workload, lambda: cpu_linear_rate(target_s=3.0))]
     for name, fn, cpu in plan:
         sub = copy.copy(args)
@@ -1547,6 +1710,8 @@ def main():
             res = esn_workload(args, world, rank)
         elif args.workload == "tsrn_block":
             res = tsrn_block_workload(args, world, rank)
+        elif args.workload == "tsrn_train":
+            res = tsrn_train_workload(args, world, rank)
         else:
             res = scan_workload(args, world, rank)
         if res is not None and args.impl == "ours" and rank == 0 and world == 1 \
@@ -1564,6 +1729,8 @@ def main():
                 res["cpu_baseline"] = cpu_esn_rate(args.esn_mode)
             elif args.workload == "tsrn_block":
                 res["cpu_baseline"] = cpu_tsrn_block_rate()
+            elif args.workload == "tsrn_train":
+                res["cpu_baseline"] = cpu_tsrn_train_rate()
             else:
                 res["cpu_baseline"] = cpu_scan_rate(16, 4096, 1024)
         if args.impl == "ours" and args.workload == "gemm" and not args.no_secondary \

@@ -852,16 +852,41 @@ def _tf32_matmuls():
 LINEAR_TF32X3_MIN_ROWS = 4096
 
 
+def _mm3(ah, al, bh, bl):
+    """ah @ bh + ah @ bl + al @ bh on the TF32 tensor cores (2-D operands, any
+    strides; the parts from ``split_tf32``)."""
+    with _tf32_matmuls():
+        y = ah @ bh
+        y.addmm_(ah, bl).addmm_(al, bh)
+    return y
+
+
+def matmul_tf32x3(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``a @ b`` (2-D fp32 CUDA tensors) at fp32 accuracy on the TF32 tensor cores:
+    both split into TF32 hi and lo parts, three GEMMs (hi.hi + hi.lo + lo.hi)."""
+    ah, al = split_tf32(a)
+    bh, bl = split_tf32(b)
+    return _mm3(ah, al, bh, bl)
+
+
+def matmul_tn_tf32x3(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``a.T @ b`` for row-major a [R, M] and b [R, N] (a weight gradient over R
+    rows) at fp32 accuracy on the TF32 tensor cores; a is split in its own
+    layout and read transposed."""
+    ah, al = split_tf32(a)
+    bh, bl = split_tf32(b)
+    return _mm3(ah.t(), al.t(), bh, bl)
+
+
 def linear_tf32x3(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None):
     """``x @ w.T (+ b)`` at fp32 accuracy on the TF32 tensor cores: x and w are
     split into TF32 hi and lo parts (``split_tf32``) and three cuBLAS TF32 GEMMs
     sum hi.hi + hi.lo + lo.hi (the lo.lo term is below 2^-22 of the product):
     ~2e-6 relative against ~1.5e-6 for fp32 SGEMM at K = 640, 3.3x faster on
     B200 at [65536 x 640] x [640 x 1920].  A non-finite x or w entry gives NaN
-    where fp32 may give +-inf.  No autograd (inference)."""
+    where fp32 may give +-inf.  No autograd (``LinearTF32x3Function`` adds it)."""
     K = x.shape[-1]
-    xs = x.reshape(-1, K)
-    xh, xl = split_tf32(xs)
+    xh, xl = split_tf32(x.reshape(-1, K))
     wh, wl = split_tf32(w)
     with _tf32_matmuls():
         y = torch.addmm(b, xh, wh.t()) if b is not None else xh @ wh.t()
@@ -869,19 +894,51 @@ def linear_tf32x3(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = 
     return y.reshape(*x.shape[:-1], w.shape[0])
 
 
+class LinearTF32x3Function(torch.autograd.Function):
+    """``linear_tf32x3`` with its backward in the same form: dx = dy @ w and
+    dw = dy^T @ x as 3xTF32 GEMMs (the splits recomputed, not saved), db = the
+    column sums of dy."""
+
+    @staticmethod
+    def forward(ctx, x, w, b):
+        ctx.save_for_backward(x, w)
+        ctx.has_bias = b is not None
+        return linear_tf32x3(x, w, b)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        K, N = x.shape[-1], w.shape[0]
+        gh, gl = split_tf32(dy.reshape(-1, N))
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            wh, wl = split_tf32(w)
+            dx = _mm3(gh, gl, wh, wl).reshape(x.shape)
+        if ctx.needs_input_grad[1]:
+            xh, xl = split_tf32(x.reshape(-1, K))
+            dw = _mm3(gh.t(), gl.t(), xh, xl)
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            db = dy.reshape(-1, N).sum(0)
+        return dx, dw, db
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None):
-    """``F.linear`` of the drop-in modules: ``linear_tf32x3`` in inference on CUDA
-    tensors with at least LINEAR_TF32X3_MIN_ROWS rows, plain fp32 otherwise
-    (training keeps fp32 autograd)."""
+    """``F.linear`` of the drop-in modules: fp32-accurate 3xTF32 tensor-core GEMMs
+    (``linear_tf32x3``; with autograd ``LinearTF32x3Function``) for CUDA fp32
+    inputs of at least LINEAR_TF32X3_MIN_ROWS rows, the plain fp32 GEMM
+    otherwise."""
     rows = x.numel() // max(x.shape[-1], 1)
-    needs_grad = torch.is_grad_enabled() and (
-        x.requires_grad or w.requires_grad or (b is not None and b.requires_grad))
-    if needs_grad or rows < LINEAR_TF32X3_MIN_ROWS or not x.is_cuda or x.dtype != torch.float32:
+    if rows < LINEAR_TF32X3_MIN_ROWS or not x.is_cuda or x.dtype != torch.float32 or \
+            w.dtype != torch.float32:
         return torch.nn.functional.linear(x, w, b)
     try:
         torch.backends.cuda.matmul.allow_tf32
     except RuntimeError:     # the caller set TF32 through the newer API: keep fp32 GEMMs
         return torch.nn.functional.linear(x, w, b)
+    needs_grad = torch.is_grad_enabled() and (
+        x.requires_grad or w.requires_grad or (b is not None and b.requires_grad))
+    if needs_grad:
+        return LinearTF32x3Function.apply(x, w, b)
     return linear_tf32x3(x, w.detach(), None if b is None else b.detach())
 
 

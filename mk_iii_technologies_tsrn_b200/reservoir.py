@@ -11,8 +11,9 @@ for training, :class:`GRUReservoirFunction` / :class:`LeakyReservoirFunction`
 add a backward through time: every step's gates are recomputed at once from the
 saved states (batched GEMMs), one launch (``ops.esn_gru_bwd`` /
 ``ops.esn_leaky_bwd``) carries the state gradient backwards through all steps,
-and the weight gradients are batched GEMMs over all steps.  CUDA
-tensors only (no CPU fallback).
+and the weight gradients are batched GEMMs over all steps (the gate
+recomputation and the weight gradients as fp32-accurate 3xTF32 tensor-core
+GEMMs).  CUDA tensors only (no CPU fallback).
 """
 from __future__ import annotations
 
@@ -54,10 +55,12 @@ class GRUReservoirFunction(torch.autograd.Function):
         U, Uz, Ur, Wzh, Wrh, Ws, H = ctx.saved_tensors
         B, T, dr = H.shape
         Hp = _previous_states(H)
-        z = torch.sigmoid(Hp @ Wzh.T + Uz)
-        r = torch.sigmoid(Hp @ Wrh.T + Ur)
+        flat = lambda t: t.reshape(B * T, dr)   # noqa: E731
+        # every step's gates at once (fp32-accurate 3xTF32 GEMMs)
+        z = torch.sigmoid(ops.matmul_tf32x3(flat(Hp), Wzh.t()).view(B, T, dr) + Uz)
+        r = torch.sigmoid(ops.matmul_tf32x3(flat(Hp), Wrh.t()).view(B, T, dr) + Ur)
         m = r * Hp
-        hc = torch.tanh(m @ Ws.T + U)
+        hc = torch.tanh(ops.matmul_tf32x3(flat(m), Ws.t()).view(B, T, dr) + U)
         # per-step factors, all steps at once
         fa = z * (1.0 - hc * hc)              # d h / d a_h  (a_h = m Ws^T + U)
         fz = (hc - Hp) * z * (1.0 - z)        # d h / d a_z
@@ -65,10 +68,9 @@ class GRUReservoirFunction(torch.autograd.Function):
         keep = 1.0 - z
         # the reverse-time loop over the state gradient: one launch
         dAh, dAz, dAr = ops.esn_gru_bwd(dH, fa, fz, fr, keep, r, Wzh, Wrh, Ws)
-        flat = lambda t: t.reshape(B * T, dr)   # noqa: E731
-        dWs = flat(dAh).T @ flat(m)
-        dWzh = flat(dAz).T @ flat(Hp)
-        dWrh = flat(dAr).T @ flat(Hp)
+        dWs = ops.matmul_tn_tf32x3(flat(dAh), flat(m))
+        dWzh = ops.matmul_tn_tf32x3(flat(dAz), flat(Hp))
+        dWrh = ops.matmul_tn_tf32x3(flat(dAr), flat(Hp))
         return dAh, dAz, dAr, dWzh, dWrh, dWs
 
 
@@ -87,12 +89,12 @@ class LeakyReservoirFunction(torch.autograd.Function):
         U, Ws, lk, H = ctx.saved_tensors
         B, T, dr = H.shape
         Hp = _previous_states(H)
-        s = torch.tanh(Hp @ Ws.T + U)
+        flat = lambda t: t.reshape(B * T, dr)   # noqa: E731
+        s = torch.tanh(ops.matmul_tf32x3(flat(Hp), Ws.t()).view(B, T, dr) + U)
         fa = lk * (1.0 - s * s)
         # the reverse-time loop over the state gradient: one launch
         dA, dHs = ops.esn_leaky_bwd(dH, fa, Ws, lk)
-        flat = lambda t: t.reshape(B * T, dr)   # noqa: E731
-        dWs = flat(dA).T @ flat(Hp)
+        dWs = ops.matmul_tn_tf32x3(flat(dA), flat(Hp))
         dlk = (dHs * (s - Hp)).sum().reshape(lk.shape)
         return dA, dWs, dlk
 

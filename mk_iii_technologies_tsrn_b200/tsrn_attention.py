@@ -25,7 +25,6 @@ from typing import Dict, Optional, Tuple
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from . import ops
 
@@ -205,7 +204,7 @@ class TropicalAttention(nn.Module):
 
     def _project_differentiable(self, x: torch.Tensor):
         B, T, d = x.shape
-        q, k, v = F.linear(x, self._qkv_weight()).view(B, T, 3, self.H, self.dh).unbind(2)
+        q, k, v = ops.linear(x, self._qkv_weight()).view(B, T, 3, self.H, self.dh).unbind(2)
         cos, sin = self.rope.tables(T, x.device)
         cos, sin = cos[:T], sin[:T]
         heads = lambda t: t.permute(0, 2, 1, 3)   # noqa: E731

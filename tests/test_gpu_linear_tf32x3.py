@@ -64,10 +64,47 @@ def test_linear_dispatch_and_tf32_setting(cuda):
     with torch.no_grad():
         y = ops.linear(big, w)
     assert torch.equal(y, ops.linear_tf32x3(big, w))
-    # autograd: the fp32 GEMM with its gradient
+    # autograd: the same products, with a 3xTF32 backward
     wg = w.clone().requires_grad_(True)
     yg = ops.linear(big, wg)
     assert yg.requires_grad
-    assert torch.equal(yg.detach(), torch.nn.functional.linear(big, w))
+    assert torch.equal(yg.detach(), ops.linear_tf32x3(big, w))
+    # few rows under autograd: the plain fp32 GEMM
+    ys = ops.linear(small, wg)
+    assert torch.equal(ys.detach(), torch.nn.functional.linear(small, w))
     # the caller's TF32 setting is left as it was
     assert m.allow_tf32 == prev
+
+
+def test_linear_autograd_vs_float64(cuda):
+    ops = _ops()
+    g = torch.Generator(device=cuda).manual_seed(11)
+    M, K, N = 6000, 320, 192
+    x = torch.randn(M, K, device=cuda, generator=g)
+    w = torch.randn(N, K, device=cuda, generator=g) / K ** 0.5
+    b = torch.randn(N, device=cuda, generator=g)
+    dy = torch.randn(M, N, device=cuda, generator=g)
+    xr, wr, br = (t.clone().requires_grad_(True) for t in (x, w, b))
+    y = ops.linear(xr, wr, br)
+    assert y.grad_fn is not None and "LinearTF32x3" in type(y.grad_fn).__name__
+    y.backward(dy)
+    xd, wd, bd = (t.double().requires_grad_(True) for t in (x, w, b))
+    (torch.nn.functional.linear(xd, wd, bd) * dy.double()).sum().backward()
+    # the output and dx reduce over K = 320, dW and db over M = 6000 rows (fp32
+    # accumulation over that many rows: a few 1e-5 of the scale, as for SGEMM)
+    for got, ref, tol in ((y, xd.double() @ wd.double().T + bd, 1e-5), (xr.grad, xd.grad, 1e-5),
+                          (wr.grad, wd.grad, 5e-5), (br.grad, bd.grad, 5e-5)):
+        err = ((got.double() - ref).abs().max() / ref.abs().max()).item()
+        assert err < tol, err
+
+
+def test_matmul_helpers(cuda):
+    ops = _ops()
+    g = torch.Generator(device=cuda).manual_seed(12)
+    a = torch.randn(700, 96, device=cuda, generator=g)
+    b = torch.randn(96, 50, device=cuda, generator=g)
+    c = torch.randn(700, 50, device=cuda, generator=g)
+    for got, ref in ((ops.matmul_tf32x3(a, b), a.double() @ b.double()),
+                     (ops.matmul_tn_tf32x3(a, c), a.double().T @ c.double())):
+        err = ((got.double() - ref).abs().max() / ref.abs().max()).item()
+        assert err < 1e-5, err
