@@ -29,14 +29,18 @@
 //            the diagonal split evenly), tcgen05.ld's the 64 scores, releases
 //            the accumulator and finishes its 32.
 // Selection in two passes over the key tiles:
-//   pass 1 (tiles nearest the diagonal first): each thread keeps the 16
-//          largest of its scores (a sorted register list, NaN never enters);
+//   pass 1 (keys nearest the diagonal first: tiles in descending order, a
+//          tile's columns too): each thread keeps the 16 largest of its scores
+//          (a sorted register list, NaN never enters);
 //          the two lists of a row are merged in shared memory: rowmax = the
 //          first, thr = the top_k-th, ties counted as torch.topk counts them;
-//   pass 2 recomputes the same MMAs (same operands, same order: the same
-//          bits) and lists each half's kept keys {j : !(S < thr), S != -inf}
-//          (ascending j) with its part of the softmax normaliser in shared
-//          memory.
+//          every score that reached the list's last entry when it was seen is
+//          also logged (key, score) in global memory: a superset of the kept
+//          keys {j : !(S < thr), S != -inf}, which are then listed from the
+//          log with the softmax normaliser, in logged order;
+//   pass 2 runs only when a log overflowed (or a score was NaN): it
+//          recomputes the same MMAs (same operands, same order: the same bits)
+//          and lists each half's kept keys in ascending j.
 // Then each warp gathers the V rows of 16 rows' kept keys (lanes split the
 // channels).  Kept keys beyond a half's TC_KCAP list entries (ties at the
 // threshold) are accumulated by their thread into a scratch row -- the
@@ -61,6 +65,7 @@ constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
 constexpr int TC_TMEM_COLS = 128;   // two accumulators of TC_N columns
 constexpr int TC_MAX_DH = 96;
 constexpr int TC_LISTS_OUT = 2 * TC_KCAP;   // kept keys per row saved for the backward
+constexpr int TC_LOGCAP = 48;      // pass-1 candidates logged per row half (else pass 2 runs)
 static_assert(TC_LISTS_OUT == TSRN_ATT_LIST, "saved list width");
 
 constexpr uint32_t TC_Q_ATOM_FLOATS = TC_M * TC_ATOM;     // 16 KB
@@ -188,6 +193,7 @@ struct TcArgs {
   float* kp;
   float* kl;              // [S][T][TC_LISTS_OUT]: the entry's log-sum-exp score before ALiBi
   int* kn;
+  float2* log;            // [grid][2][TC_LOGCAP][TC_M]: pass-1 candidates (key bits, score)
   int* err;
 };
 
@@ -301,6 +307,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   for (int k = 0; k < TC_LIST; ++k) L[k] = NEG_INF;
   float thr = NEG_INF, rowmax = NEG_INF, z = 0.0f;
   int cnt = 0;
+  // pass-1 candidate log of this thread (row r, its half of the key columns):
+  // every score that reached the list's last entry when it was seen -- a
+  // superset of the kept keys, since that entry only grows up to the
+  // threshold.  A log that overflows, or a NaN score, sends the CTA through
+  // pass 2 instead.
+  float2* lg = p.log + ((int64_t)blockIdx.x * 2 + (half > 0 ? 1 : 0)) * TC_LOGCAP * TC_M + r;
+  int lcnt = 0;
+  bool lbad = false;
   // scratch row of this thread's kept keys beyond its list
   float* ovf_row = half == 0 ? p.out + (slice * p.T + (row_ok ? i : 0)) * p.dh
                              : p.qlo + (slice * p.Tp + i0 + r) * TC_KP;
@@ -313,7 +327,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   for (int round = 0; round < 2; ++round) {
     if (round == 1) {
       __syncthreads();
-      if (s_flag[1] != 0) break;
+      // pass 2 only when some thread could not log all its candidates
+      if (s_flag[1] != 0 || s_flag[0] == 0) break;
+      cnt = 0;            // it rebuilds every row's kept list
+      z = 0.0f;
     }
     const int it0 = round * nt;
     if (warp == 0) {
@@ -453,17 +470,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (round == 0) {
           // candidates against the list's last entry before this tile (it only
           // grows, so no later candidate is missed); columns where no lane
-          // has one are skipped with a warp-uniform branch
+          // has one are skipped with a warp-uniform branch.  A candidate at
+          // least equal to the current last entry is logged (ties included),
+          // one strictly above it enters the list.
           const float l15 = L[TC_LIST - 1];
           uint32_t cand = 0;
 #pragma unroll
-          for (int cc = 0; cc < 32; ++cc) cand |= (sc[cc] > l15 ? 1u : 0u) << cc;
+          for (int cc = 0; cc < 32; ++cc) {
+            cand |= ((sc[cc] >= l15 && sc[cc] != NEG_INF) ? 1u : 0u) << cc;
+            lbad |= sc[cc] != sc[cc];
+          }
           const uint32_t wm = __reduce_or_sync(0xffffffffu, cand);
           if (wm != 0) {
+            // keys nearest the diagonal first (the tiles run that way too):
+            // with ALiBi the large scores come early and later keys rarely
+            // reach the list, which keeps both the insertions and the log short
 #pragma unroll
-            for (int cc = 0; cc < 32; ++cc)
-              if ((wm >> cc) & 1u)
-                if (sc[cc] > L[TC_LIST - 1]) tc_insert(L, sc[cc]);
+            for (int cc = 31; cc >= 0; --cc)
+              if ((wm >> cc) & 1u) {
+                const float sv = sc[cc];
+                if (sv >= L[TC_LIST - 1] && sv != NEG_INF) {
+                  if (lcnt < TC_LOGCAP)
+                    lg[lcnt * TC_M] = make_float2(__int_as_float(j0 + 2 * cc + half), sv);
+                  ++lcnt;
+                  if (sv > L[TC_LIST - 1]) tc_insert(L, sv);
+                }
+              }
           }
         } else {
           uint32_t kept = 0;
@@ -507,6 +539,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         rowmax = fmaxf(s_lst[r], s_lst[TC_LIST * TC_M + r]);
         tc_epi_sync();          // the lists' space is the kept-key lists' of pass 2
+        // the kept keys from the log, in logged order (pass 2 is not needed
+        // unless some thread of the CTA could not log all its candidates)
+        if (lbad || lcnt > TC_LOGCAP) {
+          s_flag[0] = 1;
+        } else if (row_ok) {
+          for (int e = 0; e < lcnt; ++e) {
+            const float2 ent = lg[e * TC_M];
+            const float sv = ent.y;
+            if (sv < thr) continue;
+            const int j = __float_as_int(ent.x);
+            const float ev = expf(sv - rowmax);
+            z += ev;
+            if (cnt < TC_KCAP) {
+              s_kj[(half * TC_KCAP + cnt) * TC_M + r] = j;
+              s_ks[(half * TC_KCAP + cnt) * TC_M + r] = sv;
+            } else {
+              tc_overflow_add(ovf_row, cnt == TC_KCAP, ev, Vs + (int64_t)j * p.dh, p.dh);
+            }
+            ++cnt;
+          }
+        }
       }
     }
   }
@@ -629,7 +682,7 @@ inline int64_t round64(int64_t n) { return (n + 63) & ~(int64_t)63; }
 
 struct TcLayout {
   int64_t Tp, Kp;
-  int64_t qhi, qlo, khi, klo, qmx, kmx, total;   // float offsets
+  int64_t qhi, qlo, khi, klo, qmx, kmx, log, total;   // float offsets
 };
 
 TcLayout tc_layout(int64_t B, int64_t H, int64_t T, int64_t Tkv) {
@@ -643,7 +696,8 @@ TcLayout tc_layout(int64_t B, int64_t H, int64_t T, int64_t Tkv) {
   l.klo = l.khi + round64(S * l.Kp * TC_KP);
   l.qmx = l.klo + round64(S * l.Kp * TC_KP);
   l.kmx = l.qmx + round64(S * T);
-  l.total = l.kmx + round64(S * l.Kp);
+  l.log = l.kmx + round64(S * l.Kp);
+  l.total = l.log + round64(S * (l.Tp / TC_M) * 2 * TC_LOGCAP * TC_M * 2);
   return l;
 }
 
@@ -688,7 +742,8 @@ int launch_tsrn_attention_tc(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64
       !make_feat_map(&mkh, khi, S * l.Kp, TC_N) || !make_feat_map(&mkl, klo, S * l.Kp, TC_N))
     return TP_ERR_UNSUPPORTED;
   TcArgs a{S, H, T, Tkv, Tc, l.Tp, l.Kp, (int)dh, top_k, causal, (int)ceil_div(dh, 8),
-           Q, K, V, slopes, qmx, kmx, out, qlo, kj, kp, kl, kn, device_error_ptr()};
+           Q, K, V, slopes, qmx, kmx, out, qlo, kj, kp, kl, kn,
+           reinterpret_cast<float2*>(ws + l.log), device_error_ptr()};
   cudaError_t e = cudaFuncSetAttribute(att_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)TC_SMEM_BYTES);
   if (e != cudaSuccess) return cuda_status(e);
