@@ -1045,7 +1045,9 @@ def tsrn_attn_workload(args, world, rank):
                 "h2d_bytes_per_step": 3 * hQ.numel() * 4, "d2h_bytes_per_step": hout.numel() * 4},
         "gpu_launches": per_step * steps if per_step is not None else None,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
-                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                     "unit": "TFLOP/s", "frac": achieved / peak,
+                     "traffic": (profiled_traffic("att_tc_kernel_b64") * B // 64
+                                 if profiled_traffic("att_tc_kernel_b64") else None),
                      "kernel": "att_tc_kernel (tcgen05 kind::tf32 score contraction, 3xTF32, "
                                "causal) incl. its two-pass top-k selection and V gather",
                      "limiter": "the per-score selection epilogue, not the tensor pipe "
@@ -1429,7 +1431,9 @@ def tsrn_train_workload(args, world, rank):
                 "h2d_bytes_per_step": 2 * hx.numel() * 4, "d2h_bytes_per_step": hdx.numel() * 4},
         "gpu_launches": per_step * steps if per_step is not None else None,
         "roofline": {"bound": "cuda-core fp32 FMA (dominant kernel)", "achieved": achieved,
-                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "traffic": (profiled_traffic("esn_bwd_kernel_b64") * B // 64
+                                 if profiled_traffic("esn_bwd_kernel_b64") else None),
                      "kernel": "esn_bwd_kernel (GRU reservoir backward through time; "
                                "latency-bound per step)", "kernel_ms": bptt_ms,
                      "peak_source": "in-repo register-only FMA probe (tp_probe_addmax: best "
