@@ -330,7 +330,8 @@ TP_API int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, i
  * tp_tsrn_attention_bwd_rows: per row, dP = dO_i . V_j and
  *   dS = P (dP - sum P dP) for every kept j, and
  *   dQ_i = sum_j dS_ij exp(Q_i + K_j - L_ij); stores dS per entry (entry_ds
- *   [B*H*T][TP_ATT_LIST]).  S = B*H.
+ *   [B*H*T][TP_ATT_LIST]).  S = B*H.  Keys outside [0, Tkv) (in these and in
+ *   tp_tsrn_attention_bwd_group) count as empty slots.
  * tp_tsrn_attention_bwd_group: groups the entries of each slice by key,
  *   rows ascending inside a key (a stable counting sort, one CTA per slice;
  *   Tkv up to 17000 keys, else TP_ERR_TOO_LARGE): entry ids

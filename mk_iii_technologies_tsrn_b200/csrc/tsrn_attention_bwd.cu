@@ -90,7 +90,8 @@ __global__ void __launch_bounds__(256) att_bwd_rows_kernel(const AttBwdArgs a) {
     float part[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int j = e0 + e < n ? jr[e0 + e] : -1;
+      int j = e0 + e < n ? jr[e0 + e] : -1;
+      if (j >= a.Tkv) j = -1;     // a key past the slice (not from the forward): no entry
       float d = 0.0f;
 #pragma unroll
       for (int q = 0; q < 3; ++q) {
@@ -116,7 +117,8 @@ __global__ void __launch_bounds__(256) att_bwd_rows_kernel(const AttBwdArgs a) {
     float kv[4][3];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int j = e0 + e < n ? jr[e0 + e] : -1;
+      int j = e0 + e < n ? jr[e0 + e] : -1;
+      if (j >= a.Tkv) j = -1;
 #pragma unroll
       for (int q = 0; q < 3; ++q) {
         const int c = lane + 32 * q;
@@ -231,7 +233,7 @@ __global__ void __launch_bounds__(AB_GROUP_THREADS) att_bwd_group_kernel(
   __syncthreads();
   for (int64_t e = tid; e < T * AB_L; e += AB_GROUP_THREADS) {
     const int j = kjs[e];
-    if (j >= 0) atomicAdd(&cnt[j], 1);      // counts do not depend on the order
+    if (j >= 0 && j < Tkv) atomicAdd(&cnt[j], 1);   // counts do not depend on the order
   }
   __syncthreads();
   // exclusive scan of cnt: each thread a contiguous run of keys, then the
@@ -274,7 +276,8 @@ __global__ void __launch_bounds__(AB_GROUP_THREADS) att_bwd_group_kernel(
     for (int64_t k = tid; k < Tkv; k += AB_GROUP_THREADS) msk[k] = 0u;
     __syncthreads();
     const int64_t row = r0 + rr;
-    const int j = row < T ? kjs[row * AB_L + slot] : -1;
+    int j = row < T ? kjs[row * AB_L + slot] : -1;
+    if (j >= Tkv) j = -1;               // a key past the slice: not an entry
     if (j >= 0) atomicOr(&msk[j], 1u << rr);
     __syncthreads();
     unsigned m = 0u;

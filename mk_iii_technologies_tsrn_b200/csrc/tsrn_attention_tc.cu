@@ -586,7 +586,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         float oacc[3] = {0.0f, 0.0f, 0.0f};
         // each half's listed keys eight at a time: the eight V rows' loads in
         // flight together (one L2 round trip per eight keys); accumulated in
-        // list order (ascending key), half 0 first
+        // list order (the order pass 1 logged them, or ascending key after a
+        // pass 2), half 0 first
         for (int hh = 0; hh < 2; ++hh) {
           const int n = min(hh ? c1 : c0, TC_KCAP);
           for (int e0 = 0; e0 < n; e0 += 8) {

@@ -152,3 +152,20 @@ def test_empty(cuda):
     z = torch.zeros(1, 2, 0, 16, device=cuda)
     out, kj, kp, kl, kn = ops.tsrn_attention_train_fwd(z, z, z, torch.ones(2, device=cuda), 4)
     assert out.shape == z.shape and kn.numel() == 0
+
+
+def test_keys_out_of_range_are_empty_slots(cuda):
+    # a caller's lists with keys past the slice: those slots contribute nothing
+    # (and are not read), the other entries are unchanged
+    ops = _ops()
+    g = torch.Generator(device=cuda).manual_seed(6)
+    B, H, T, dh, k = 1, 2, 140, 24, 8
+    Q, K, V, dO = (torch.randn(B, H, T, dh, device=cuda, generator=g) for _ in range(4))
+    slopes = torch.tensor([0.5, 0.1], device=cuda)
+    _, kj, kp, kl, kn = ops.tsrn_attention_train_fwd(Q, K, V, slopes, k)
+    ref = ops.tsrn_attention_sparse_bwd(Q, K, V, dO, kj, kp, kl, kn)
+    bad = kj.clone()
+    bad[kj < 0] = T + 1000            # padding slots pointing past the slice
+    got = ops.tsrn_attention_sparse_bwd(Q, K, V, dO, bad, kp, kl, kn)
+    for x, y in zip(got, ref):
+        assert torch.equal(x, y)
