@@ -282,6 +282,27 @@ TP_API int tp_tsrn_attention_prologue(int64_t B, int64_t T, int64_t H, int64_t d
                                       int64_t npos, int64_t pos0, float* Q, float* K, float* V,
                                       void* stream);
 
+/* Backward of tp_tsrn_attention_prologue (training): from the gradients of Q,
+ * K, V ([B, H, T, dh] contiguous) and the projections qkv, the gradient of qkv
+ * (dqkv, same [B*T, ld] layout: Q, K, V columns at 0, koff, voff) and of the
+ * four LayerNorm parameters, dparams [4][dh] = d q_gamma, d q_beta,
+ * d k_gamma, d k_beta (the autograd of research/tsrn_dml.py:472-500; the
+ * LayerNorm statistics are recomputed, the rotation transposed).  workspace:
+ * tp_tsrn_attention_prologue_bwd_workspace_bytes(B, T, H, dh) bytes for the
+ * parameter gradients' per-block partials, summed in a fixed order
+ * (deterministic).  (Replaces the reference's PyTorch chain; no C counterpart.) */
+TP_API int64_t tp_tsrn_attention_prologue_bwd_workspace_bytes(int64_t B, int64_t T, int64_t H,
+                                                              int64_t dh);
+TP_API int tp_tsrn_attention_prologue_bwd(int64_t B, int64_t T, int64_t H, int64_t dh,
+                                          const float* qkv, int64_t ld, int64_t koff,
+                                          int64_t voff, const float* q_gamma,
+                                          const float* k_gamma, float eps,
+                                          const float* cos_table, const float* sin_table,
+                                          int64_t npos, int64_t pos0, const float* dQ,
+                                          const float* dK, const float* dV, float* dqkv,
+                                          float* dparams, void* workspace,
+                                          int64_t workspace_bytes, void* stream);
+
 /* ======================================================================== *
  *  Fused TSRN tropical top-k attention, forward (inference)
  *  Replaces research/tsrn_dml.py:462-548 (TropicalAttention.forward) from the

@@ -531,6 +531,47 @@ int64_t tp_tsrn_attention_workspace_bytes(int64_t B, int64_t H, int64_t T, int64
   return tp::tsrn_attention_workspace_floats(B, H, T, Tkv, dh) * (int64_t)sizeof(float);
 }
 
+int64_t tp_tsrn_attention_prologue_bwd_workspace_bytes(int64_t B, int64_t T, int64_t H,
+                                                       int64_t dh) {
+  if (B < 0 || T < 0 || H < 0 || dh <= 0) return -1;
+  return (int64_t)tp::tsrn_prologue_bwd_blocks(B, T, H) * 4 * dh * (int64_t)sizeof(float);
+}
+
+int tp_tsrn_attention_prologue_bwd(int64_t B, int64_t T, int64_t H, int64_t dh, const float* qkv,
+                                   int64_t ld, int64_t koff, int64_t voff, const float* q_gamma,
+                                   const float* k_gamma, float eps, const float* cos_table,
+                                   const float* sin_table, int64_t npos, int64_t pos0,
+                                   const float* dQ, const float* dK, const float* dV, float* dqkv,
+                                   float* dparams, void* workspace, int64_t workspace_bytes,
+                                   void* stream) {
+  TP_RETURN_IF(B < 0 || T < 0 || H < 0 || dh <= 0 || npos < 0 || pos0 < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(dh % 2 != 0 || dh > 128, TP_ERR_UNSUPPORTED);
+  TP_RETURN_IF(koff < 0 || voff < 0 || ld < 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(B * T * H > 0 &&
+                   (ld < H * dh || koff + H * dh > ld || voff + H * dh > ld || pos0 + T > npos),
+               TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(!(eps >= 0.0f), TP_ERR_INVALID_ARG);
+  TP_CHECK_PTR(dparams);
+  TP_RETURN_IF(workspace == nullptr ||
+                   workspace_bytes < tp_tsrn_attention_prologue_bwd_workspace_bytes(B, T, H, dh),
+               TP_ERR_WORKSPACE);
+  TP_CHECK_PTR(workspace);
+  if (B * T * H > 0) {
+    TP_CHECK_PTR(qkv);
+    TP_CHECK_PTR(q_gamma);
+    TP_CHECK_PTR(k_gamma);
+    TP_CHECK_PTR(cos_table);
+    TP_CHECK_PTR(sin_table);
+    TP_CHECK_PTR(dQ);
+    TP_CHECK_PTR(dK);
+    TP_CHECK_PTR(dV);
+    TP_CHECK_PTR(dqkv);
+  }
+  return tp::launch_tsrn_prologue_bwd(B, T, H, dh, qkv, ld, koff, voff, q_gamma, k_gamma, eps,
+                                      cos_table, sin_table, pos0, dQ, dK, dV, dqkv, dparams,
+                                      (float*)workspace, as_stream(stream));
+}
+
 int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc, int64_t dh,
                           const float* Q, const float* K, const float* V,
                           const float* alibi_slopes, int top_k, int causal, float* out,

@@ -236,6 +236,12 @@ int launch_tsrn_prologue(int64_t B, int64_t T, int64_t H, int64_t dh, const floa
                          const float* kg, const float* kb, float eps, const float* cosb,
                          const float* sinb, int64_t pos0, float* Q, float* K, float* V,
                          cudaStream_t stream);
+int tsrn_prologue_bwd_blocks(int64_t B, int64_t T, int64_t H);
+int launch_tsrn_prologue_bwd(int64_t B, int64_t T, int64_t H, int64_t dh, const float* qkv,
+                             int64_t ld, int64_t koff, int64_t voff, const float* qg,
+                             const float* kg, float eps, const float* cosb, const float* sinb,
+                             int64_t pos0, const float* dQ, const float* dK, const float* dV,
+                             float* dqkv, float* dparams, float* part, cudaStream_t stream);
 
 // esn.cu: echo-state reservoir recurrences (GRU-gated when gru, else leaky);
 // W[0..2] = Wzh, Wrh, Ws for GRU, W[0] = Ws for leaky

@@ -1027,13 +1027,6 @@ def tsrn_attention_prologue(qkv: torch.Tensor, B: int, T: int, H: int, dh: int,
     [positions, dh/2]) on Q and K, head-major layout for all three -- the
     prologue of research/tsrn_dml.py:472-477 in one kernel (inference)."""
     dev = _require_cuda(qkv, cos, sin)
-    qkv = _f32(qkv)
-    d = H * dh
-    if qkv.dim() != 2 or qkv.shape[0] != B * T or qkv.shape[1] < 3 * d or qkv.stride(1) != 1:
-        raise ValueError(f"qkv must be [B*T, >= 3*H*dh] with unit column stride, "
-                         f"got {tuple(qkv.shape)}")
-    if cos.shape != sin.shape or cos.dim() != 2 or cos.shape[1] * 2 != dh:
-        raise ValueError("cos / sin tables must be [positions, dh/2]")
 
     def affine(ln):
         if ln.weight is None:
@@ -1044,15 +1037,67 @@ def tsrn_attention_prologue(qkv: torch.Tensor, B: int, T: int, H: int, dh: int,
     kg, kb = affine(k_norm)
     if q_norm.eps != k_norm.eps:
         raise ValueError("q_norm and k_norm must share eps")
+    return tsrn_attention_prologue_raw(qkv, B, T, H, dh, qg, qb, kg, kb, float(q_norm.eps),
+                                       cos, sin, pos0)
+
+
+def _prologue_checks(qkv, B, T, H, dh, cos, sin):
+    d = H * dh
+    if qkv.dim() != 2 or qkv.shape[0] != B * T or qkv.shape[1] < 3 * d or qkv.stride(1) != 1:
+        raise ValueError(f"qkv must be [B*T, >= 3*H*dh] with unit column stride, "
+                         f"got {tuple(qkv.shape)}")
+    if cos.shape != sin.shape or cos.dim() != 2 or cos.shape[1] * 2 != dh:
+        raise ValueError("cos / sin tables must be [positions, dh/2]")
+
+
+def tsrn_attention_prologue_raw(qkv: torch.Tensor, B: int, T: int, H: int, dh: int,
+                                qg: torch.Tensor, qb: torch.Tensor, kg: torch.Tensor,
+                                kb: torch.Tensor, eps: float, cos: torch.Tensor,
+                                sin: torch.Tensor, pos0: int = 0):
+    """``tsrn_attention_prologue`` with the LayerNorm parameters as tensors."""
+    dev = _require_cuda(qkv, qg, qb, kg, kb, cos, sin)
+    qkv = _f32(qkv)
+    _prologue_checks(qkv, B, T, H, dh, cos, sin)
+    d = H * dh
+    qg, qb, kg, kb = (_f32(t.detach()).contiguous() for t in (qg, qb, kg, kb))
     cos, sin = _f32(cos).contiguous(), _f32(sin).contiguous()
     Q, K, V = (torch.empty(B, H, T, dh, device=dev) for _ in range(3))
     with torch.cuda.device(dev):
         st = _lib.load().tp_tsrn_attention_prologue(
             B, T, H, dh, _ptr(qkv), qkv.stride(0), d, 2 * d, _ptr(qg), _ptr(qb), _ptr(kg),
-            _ptr(kb), float(q_norm.eps), _ptr(cos), _ptr(sin), cos.shape[0], int(pos0),
+            _ptr(kb), float(eps), _ptr(cos), _ptr(sin), cos.shape[0], int(pos0),
             _ptr(Q), _ptr(K), _ptr(V), _stream(dev))
     _lib.check(st, "tp_tsrn_attention_prologue")
     return Q, K, V
+
+
+def tsrn_attention_prologue_bwd(qkv: torch.Tensor, B: int, T: int, H: int, dh: int,
+                                qg: torch.Tensor, kg: torch.Tensor, eps: float,
+                                cos: torch.Tensor, sin: torch.Tensor, dQ: torch.Tensor,
+                                dK: torch.Tensor, dV: torch.Tensor, pos0: int = 0):
+    """Backward of ``tsrn_attention_prologue_raw``: (dqkv [B*T, 3*H*dh], dq_gamma,
+    dq_beta, dk_gamma, dk_beta) from the gradients of Q, K, V; one kernel over the
+    rows plus an ordered sum of the parameter gradients (deterministic)."""
+    dev = _require_cuda(qkv, qg, kg, cos, sin, dQ, dK, dV)
+    qkv = _f32(qkv)
+    _prologue_checks(qkv, B, T, H, dh, cos, sin)
+    d = H * dh
+    qg, kg = (_f32(t.detach()).contiguous() for t in (qg, kg))
+    cos, sin = _f32(cos).contiguous(), _f32(sin).contiguous()
+    dQ, dK, dV = (_f32(t).contiguous() for t in (dQ, dK, dV))
+    dqkv = torch.zeros(B * T, qkv.shape[1], device=dev) if qkv.shape[1] != 3 * d else \
+        torch.empty(B * T, 3 * d, device=dev)
+    dp = torch.empty(4, dh, device=dev)
+    lib = _lib.load()
+    ws_bytes = int(lib.tp_tsrn_attention_prologue_bwd_workspace_bytes(B, T, H, dh))
+    ws = torch.empty(max(ws_bytes // 4, 4), device=dev)
+    with torch.cuda.device(dev):
+        st = lib.tp_tsrn_attention_prologue_bwd(
+            B, T, H, dh, _ptr(qkv), qkv.stride(0), d, 2 * d, _ptr(qg), _ptr(kg), float(eps),
+            _ptr(cos), _ptr(sin), cos.shape[0], int(pos0), _ptr(dQ), _ptr(dK), _ptr(dV),
+            _ptr(dqkv), _ptr(dp), _ptr(ws), ws.numel() * 4, _stream(dev))
+    _lib.check(st, "tp_tsrn_attention_prologue_bwd")
+    return dqkv, dp[0], dp[1], dp[2], dp[3]
 
 
 def tsrn_attention_host(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,

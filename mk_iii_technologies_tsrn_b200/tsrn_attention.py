@@ -13,8 +13,9 @@ state dict loads unchanged.  The computation is this library's:
 * one kernel (``tp_tsrn_attention_fwd``) computes the log-sum-exp tropical
   score, ALiBi, the causal mask, the top-k threshold, the softmax and @V
   without materialising the T x T scores;
-* in training, :class:`TopKAttentionFunction` keeps that forward (saving each
-  row's kept keys) and supplies a sparse analytic backward over the kept
+* in training, :class:`PrologueFunction` runs the same prologue kernel with a
+  fused backward, and :class:`TopKAttentionFunction` keeps the attention
+  forward (saving each row's kept keys) and supplies a sparse analytic backward over the kept
   (query, key) pairs (``ops.tsrn_attention_sparse_bwd``); with attention
   dropout the forward runs densely so that the dropped weights are the ones
   differentiated, and the backward recomputes the dense scores.
@@ -117,6 +118,31 @@ def _masked_scores(Q, K, slopes, top_k: int, causal: bool, Tc: int) -> torch.Ten
     return S.masked_fill(S < cut, float("-inf"))
 
 
+class PrologueFunction(torch.autograd.Function):
+    """The attention prologue (per-head QK LayerNorm, rotary embedding, head
+    layout) with autograd: the fused forward kernel and its fused backward
+    (``ops.tsrn_attention_prologue_bwd``): qkv [B*T, 3*H*dh] and the four
+    LayerNorm parameters get gradients."""
+
+    @staticmethod
+    def forward(ctx, qkv, qg, qb, kg, kb, cos, sin, B: int, T: int, H: int, dh: int, eps: float):
+        ctx.dims = (B, T, H, dh, eps)
+        ctx.save_for_backward(qkv, qg, kg, cos, sin)
+        return ops.tsrn_attention_prologue_raw(qkv, B, T, H, dh, qg, qb, kg, kb, eps, cos, sin)
+
+    @staticmethod
+    def backward(ctx, dQ, dK, dV):
+        qkv, qg, kg, cos, sin = ctx.saved_tensors
+        B, T, H, dh, eps = ctx.dims
+        zero = None
+        if dQ is None or dK is None or dV is None:
+            zero = torch.zeros(B, H, T, dh, device=qkv.device)
+        dqkv, dqg, dqb, dkg, dkb = ops.tsrn_attention_prologue_bwd(
+            qkv, B, T, H, dh, qg, kg, eps, cos, sin, zero if dQ is None else dQ,
+            zero if dK is None else dK, zero if dV is None else dV)
+        return dqkv, dqg, dqb, dkg, dkb, None, None, None, None, None, None, None
+
+
 class TopKAttentionFunction(torch.autograd.Function):
     """Tropical top-k attention core: Q, K, V [B, H, T(kv), dh] (rotated) ->
     context [B, H, T, dh].  The top-k cut is not differentiated (the reference
@@ -202,6 +228,20 @@ class TropicalAttention(nn.Module):
         return ops.tsrn_attention_prologue(qkv, B, T, self.H, self.dh, self.q_norm, self.k_norm,
                                            cos, sin)
 
+    def _project_train(self, x: torch.Tensor):
+        """Q, K, V with autograd: the stacked projection (3xTF32 GEMMs) and the
+        fused prologue kernel with its fused backward; the PyTorch chain
+        (``_project_differentiable``) where the kernel does not apply."""
+        qn, kn = self.q_norm, self.k_norm
+        if qn.weight is None or kn.weight is None or qn.eps != kn.eps or self.dh % 2 or \
+                self.dh > 128 or not x.is_cuda:
+            return self._project_differentiable(x)
+        B, T, d = x.shape
+        qkv = ops.linear(x, self._qkv_weight()).reshape(B * T, 3 * d)
+        cos, sin = self.rope.tables(T, x.device)
+        return PrologueFunction.apply(qkv, qn.weight, qn.bias, kn.weight, kn.bias, cos, sin,
+                                      B, T, self.H, self.dh, float(qn.eps))
+
     def _project_differentiable(self, x: torch.Tensor):
         B, T, d = x.shape
         q, k, v = ops.linear(x, self._qkv_weight()).view(B, T, 3, self.H, self.dh).unbind(2)
@@ -217,7 +257,7 @@ class TropicalAttention(nn.Module):
         k = min(self.top_k, T)
         grad = torch.is_grad_enabled() and (x.requires_grad or any(
             p.requires_grad for p in self.parameters()))
-        Q, K, V = self._project_differentiable(x) if grad else self.project(x)
+        Q, K, V = self._project_train(x) if grad else self.project(x)
         use_cache = not self.training and self.cross_window_mem.enabled
         Kn, Vn, Tc = K, V, 0
         if use_cache and self.cross_window_mem.has():

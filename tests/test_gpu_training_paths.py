@@ -177,3 +177,49 @@ def test_attention_prologue_matches_torch(cuda):
             ref = m._project_differentiable(x)
         for a, b in zip(got, ref):
             torch.testing.assert_close(a, b.contiguous(), rtol=2e-6, atol=2e-6)
+
+
+@pytest.mark.parametrize("d,H,B,T", [(640, 8, 2, 50), (64, 4, 3, 33), (96, 2, 1, 129)])
+def test_attention_prologue_backward_matches_autograd(cuda, d, H, B, T):
+    # the fused prologue with its fused backward (PrologueFunction) against the
+    # module's differentiable PyTorch chain: outputs and every gradient
+    from mk_iii_technologies_tsrn_b200.tsrn_attention import TropicalAttention
+    torch.manual_seed(7)
+    m = TropicalAttention(d, top_k=4, n_heads=H).to(cuda)
+    with torch.no_grad():
+        for ln in (m.q_norm, m.k_norm):
+            ln.weight.uniform_(0.5, 1.5)
+            ln.bias.uniform_(-0.3, 0.3)
+    x = torch.randn(B, T, d, device=cuda)
+    g = [torch.randn(B, H, T, d // H, device=cuda) for _ in range(3)]
+    results = []
+    for fn in (m._project_train, m._project_differentiable):
+        m.zero_grad(set_to_none=True)
+        xr = x.clone().requires_grad_(True)
+        outs = fn(xr)
+        sum((o * gg).sum() for o, gg in zip(outs, g)).backward()
+        grads = [xr.grad] + [p.grad for p in (m.Wq.weight, m.Wk.weight, m.Wv.weight,
+                                             m.q_norm.weight, m.q_norm.bias,
+                                             m.k_norm.weight, m.k_norm.bias)]
+        results.append(([o.detach() for o in outs], grads))
+    (o1, g1), (o2, g2) = results
+    for a, b in zip(o1, o2):
+        torch.testing.assert_close(a, b, rtol=1e-5, atol=2e-6)
+    for a, b in zip(g1, g2):
+        _close(a, b.double().cpu(), rtol=1e-4, atol=1e-5)
+
+
+def test_attention_prologue_backward_repeats(cuda):
+    from mk_iii_technologies_tsrn_b200 import ops
+    g = torch.Generator(device=cuda).manual_seed(3)
+    B, T, H, dh = 2, 70, 4, 80
+    qkv = torch.randn(B * T, 3 * H * dh, device=cuda, generator=g)
+    qg, kg = (torch.rand(dh, device=cuda, generator=g) + 0.5 for _ in range(2))
+    ang = torch.outer(torch.arange(T, dtype=torch.float32),
+                      torch.rand(dh // 2, generator=torch.Generator().manual_seed(1)))
+    cos, sin = ang.cos().to(cuda), ang.sin().to(cuda)
+    dQ, dK, dV = (torch.randn(B, H, T, dh, device=cuda, generator=g) for _ in range(3))
+    a = ops.tsrn_attention_prologue_bwd(qkv, B, T, H, dh, qg, kg, 1e-5, cos, sin, dQ, dK, dV)
+    b = ops.tsrn_attention_prologue_bwd(qkv, B, T, H, dh, qg, kg, 1e-5, cos, sin, dQ, dK, dV)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
