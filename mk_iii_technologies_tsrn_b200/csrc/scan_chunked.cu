@@ -10,17 +10,20 @@
 // ? u_t : fl(a + h_{t-1}):
 //   1. beta: every chunk runs the recurrence from h = -inf (its own inputs
 //      only) and keeps its last state beta_j.
-//   2. carry: one thread per (b, c) walks the chunks in order.  The state
-//      after chunk j from any start h is max(chain_L(h), beta_j), where
-//      chain_L is L rounded additions of a (rounding is monotone, so
-//      fl(a + max(p, q)) = max(fl(a+p), fl(a+q)) and the carry and the
-//      chunk's own winners separate).  Which side wins decides the bits: a
-//      carry that never loses gives chain_L(h) exactly, a carry that loses
-//      once gives beta_j exactly (from the step it loses, the run equals the
-//      chunk's own run).  A rounding-error bound on chain_L settles most
-//      chunks without the L dependent adds; an exact tie at zero (where +0
-//      and -0 differ) replays the chunk.  The walk writes each chunk's
-//      exact starting state.
+//   2. carry: the state after chunk j from any start h is max(chain_L(h),
+//      beta_j), where chain_L is L rounded additions of a (rounding is
+//      monotone, so fl(a + max(p, q)) = max(fl(a+p), fl(a+q)) and the carry
+//      and the chunk's own winners separate).  Which side wins decides the
+//      bits: a carry that never loses gives chain_L(h) exactly, a carry that
+//      loses once gives beta_j exactly (from the step it loses, the run
+//      equals the chunk's own run).  Runs of chunks compose the same way,
+//      (n1, G1) then (n2, G2) -> (n1 + n2, max(chain_n2(G1), G2)), so one
+//      block per (b, c) scans its chunks in parallel (warp shuffles, log
+//      depth); chain_n is evaluated exactly in a few steps per binade
+//      (chain_exact.cuh) after a rounding-error bound has settled most
+//      comparisons.  An exact tie at zero (where +0 and -0 differ) sends the
+//      lane to a chunk-by-chunk walk that replays the chunk.  The pass writes
+//      each chunk's exact starting state.
 //   3. output: every chunk reruns the recurrence from its exact starting
 //      state and writes h and the win-mask words -- the same bits as the
 //      sequential kernel.
@@ -37,12 +40,15 @@
 //      an order that differs from one sequential sum over T: ga agrees with
 //      the sequential kernel to rounding, gu and gh0 bit for bit.
 //
-// Memory: pass 1 reads b, x once and pass 3 reads them again; between the
-// two they stay in L2 when B*T*C is small (the case this mode exists for:
-// 2 x 32 MiB at B=2).  Loads are 128-bit across 4 channels (C % 4 == 0 and
-// 16-byte aligned tensors; otherwise one channel per thread).
+// Memory: pass 1 reads b, x once and pass 3 reads them again; pass 1 marks
+// the lines evict-last in L2 and pass 3 evict-first, so that at the sizes this
+// mode exists for (2 x 32 MiB at B=2) the second read comes from L2; the
+// backward's passes A and C do the same.  Loads are 128-bit across 4 channels
+// (C % 4 == 0 and 16-byte aligned tensors and enough threads; otherwise one
+// channel per thread).
 #include <math.h>
 
+#include "chain_exact.cuh"
 #include "maxplus_internal.cuh"
 
 namespace tp {
@@ -93,14 +99,35 @@ __device__ __forceinline__ void ldv(float (&d)[V], const float* p) {
   }
 }
 
-// last use of an input: evict-first loads
+// L2 eviction policies: the first pass over an input keeps its lines in L2
+// (evict_last) for the second pass, which reads them for the last time
+// (evict_first); at the sizes this mode serves the inputs fit in L2
+__device__ __forceinline__ uint64_t l2_policy(bool keep) {
+  uint64_t pol;
+  if (keep) asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  else asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 template <int V>
-__device__ __forceinline__ void ldv_last(float (&d)[V], const float* p) {
+__device__ __forceinline__ void ldv_pol(float (&d)[V], const float* p, uint64_t pol) {
   if constexpr (V == 4) {
-    const float4 t = __ldcs(reinterpret_cast<const float4*>(p));
-    d[0] = t.x; d[1] = t.y; d[2] = t.z; d[3] = t.w;
+    asm("ld.global.nc.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "l"(p), "l"(pol));
   } else {
-    d[0] = __ldcs(p);
+    asm("ld.global.nc.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(d[0]) : "l"(p), "l"(pol));
+  }
+}
+
+template <int V>
+__device__ __forceinline__ void ldw_pol(uint32_t (&d)[V], const uint32_t* p, uint64_t pol) {
+  if constexpr (V == 4) {
+    asm("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "l"(p), "l"(pol));
+  } else {
+    asm("ld.global.nc.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(d[0]) : "l"(p), "l"(pol));
   }
 }
 
@@ -128,16 +155,6 @@ __device__ __forceinline__ void stw(uint32_t* p, const uint32_t (&s)[V]) {
     *reinterpret_cast<uint4*>(p) = make_uint4(s[0], s[1], s[2], s[3]);
   } else {
     p[0] = s[0];
-  }
-}
-
-template <int V>
-__device__ __forceinline__ void ldw(uint32_t (&d)[V], const uint32_t* p) {
-  if constexpr (V == 4) {
-    const uint4 t = __ldg(reinterpret_cast<const uint4*>(p));
-    d[0] = t.x; d[1] = t.y; d[2] = t.z; d[3] = t.w;
-  } else {
-    d[0] = __ldg(p);
   }
 }
 
@@ -191,6 +208,7 @@ __global__ void __launch_bounds__(kPassThreads) chunk_fwd_kernel(const ChunkArgs
   const int64_t base = (s.b * p.T + s.t0) * p.C + s.c;
   const float* pb = p.bb + base;
   const float* px = kHasX ? p.xx + base : nullptr;
+  const uint64_t pol = l2_policy(!kOut);
   float* ph = kOut ? p.h + base : nullptr;
   constexpr int kRowBlock = row_block<V>();
   uint32_t bits[V];
@@ -202,10 +220,10 @@ __global__ void __launch_bounds__(kPassThreads) chunk_fwd_kernel(const ChunkArgs
 #pragma unroll
     for (int k = 0; k < kRowBlock; ++k) {
       const int64_t off = (int64_t)(t + k) * p.C;
-      if (kOut) ldv_last<V>(u[k], pb + off); else ldv<V>(u[k], pb + off);
+      ldv_pol<V>(u[k], pb + off, pol);
       if (kHasX) {
         float xv[V];
-        if (kOut) ldv_last<V>(xv, px + off); else ldv<V>(xv, px + off);
+        ldv_pol<V>(xv, px + off, pol);
 #pragma unroll
         for (int v = 0; v < V; ++v) u[k][v] = u[k][v] + xv[v];
       }
@@ -228,10 +246,10 @@ __global__ void __launch_bounds__(kPassThreads) chunk_fwd_kernel(const ChunkArgs
   for (; t < s.rows; ++t) {
     const int64_t off = (int64_t)t * p.C;
     float u[V];
-    if (kOut) ldv_last<V>(u, pb + off); else ldv<V>(u, pb + off);
+    ldv_pol<V>(u, pb + off, pol);
     if (kHasX) {
       float xv[V];
-      if (kOut) ldv_last<V>(xv, px + off); else ldv<V>(xv, px + off);
+      ldv_pol<V>(xv, px + off, pol);
 #pragma unroll
       for (int v = 0; v < V; ++v) u[v] = u[v] + xv[v];
     }
@@ -247,67 +265,33 @@ __global__ void __launch_bounds__(kPassThreads) chunk_fwd_kernel(const ChunkArgs
   if (!kOut) stv<V>(p.beta + o, h);
 }
 
-// chain_L(h) = L rounded additions of a, when it can be had in one step:
-// while h and every sum stay inside one binade [2^(e-1), 2^e) (one sign, a
-// spacing of ulp = 2^(e-24) between floats), fl(f + a) = f + m ulp with
-// m = a / ulp rounded to the nearest integer -- unless a / ulp lies exactly
-// halfway, when ties-to-even makes the step depend on f's last bit.  Then
-// chain_L(h) = h + L m ulp exactly.  Returns false (nothing decided) when a
-// condition fails; the caller runs the adds.
-__device__ __forceinline__ float pow2f(int k) {          // 2^k for -126 <= k <= 127
-  return __int_as_float((k + 127) << 23);
-}
-
-__device__ __forceinline__ bool chain_by_binade(float h, float a, int L, float& out) {
-  const int bits = __float_as_int(h);
-  const int be = (bits >> 23) & 0xff;                    // biased exponent of h
-  // normal h away from both ends of the range (ulp and its multiples stay
-  // normal and finite); excludes 0, subnormals, inf and NaN
-  if (be < 30 || be > 225 || !isfinite(a)) return false;
-  const int e = be - 126;                                // |h| in [2^(e-1), 2^e)
-  const float ulp = pow2f(e - 24);
-  const float q = a * pow2f(24 - e);                     // a / ulp, exact
-  const float m = rintf(q);
-  if (fabsf(q - m) == 0.5f) return false;                // a tie: parity-dependent
-  if (fabsf(m) * (float)L >= 8388608.0f) return false;
-  const float end = h + (float)L * m * ulp;              // exact inside the binade
-  const float lo = pow2f(e - 1), hi = pow2f(e);
-  const float mag = fabsf(end);
-  // strictly inside: every exact intermediate sum keeps the binade's spacing
-  if ((end < 0.0f) != (h < 0.0f) || !(mag >= lo + ulp) || !(mag <= hi - ulp)) return false;
-  out = end;
-  return true;
+// The carry after n steps in which it keeps winning is chain_exact(h, a, n).
+// A cheap upper bound settles the usual case first: chain_n(h) <= h + n a +
+// n 2^-24 max_k |f_k| (+ 2^-150 per add below the normal range), and every
+// |f_k| <= |h| + n |a| up to the same errors.  The margin n 2^-20 (|h| + n |a|)
+// + n 2^-126 exceeds that bound together with the rounding of these few fp32
+// operations (each at most 2^-24 of |h| + n |a| + margin), so a bound below g
+// proves the chain ends below g; an overflow makes the bound infinite and
+// merely skips the shortcut.
+__device__ __forceinline__ bool chain_below(float h, float a, float nf, float g) {
+  if (!isfinite(a) || !isfinite(h)) return false;
+  const float mag = fabsf(h) + nf * fabsf(a);
+  const float ub = fmaf(nf, a, h) + nf * 0x1p-20f * mag + nf * 0x1p-126f;
+  return ub < g;
 }
 
 // state after a chunk of `rows` steps entered with h, given the chunk's own
 // state from -inf (beta); exact (see the file comment).
 __device__ float chunk_compose(float h, float beta, float a, int rows, const ChunkArgs& p,
                                int64_t b, int64_t c, int64_t t0) {
+  // a = +inf: -inf + a is NaN, so the chunk's own state is NaN, yet any other
+  // entering state becomes +inf and stays there
+  if (a == INFINITY) return (h == -INFINITY || h != h) ? beta : a;
   if (beta != beta) return beta;          // NaN inside the chunk whatever enters
   if (h != h) return h;                   // a NaN state stays NaN
   if (h == -INFINITY) return beta;
-  if (isfinite(a) && isfinite(h)) {
-    // chain_L(h) <= h + L a + L 2^-24 max_k |f_k| (+ 2^-150 per add below the
-    // normal range), and every |f_k| <= |h| + L |a| up to the same errors.  The
-    // margin L 2^-20 (|h| + L |a|) + L 2^-126 exceeds that bound together
-    // with the rounding of these few fp32 operations (each at most 2^-24 of
-    // |h| + L |a| + margin), so ub < beta proves the chain loses; an
-    // overflow makes ub infinite and merely skips the shortcut.
-    const float Lf = (float)rows;
-    const float mag = fabsf(h) + Lf * fabsf(a);
-    const float ub = fmaf(Lf, a, h) + Lf * 0x1p-20f * mag + Lf * 0x1p-126f;
-    if (ub < beta) return beta;
-  }
-  float ch = h;
-  if (!chain_by_binade(h, a, rows, ch)) {
-    ch = h;
-    int k = 0;
-    for (; k + 8 <= rows; k += 8) {      // dependent adds, unrolled
-#pragma unroll
-      for (int q = 0; q < 8; ++q) ch = a + ch;
-    }
-    for (; k < rows; ++k) ch = a + ch;
-  }
+  if (chain_below(h, a, (float)rows, beta)) return beta;
+  const float ch = chain_exact(h, a, rows);
   if (ch != ch) return ch;
   if (ch > beta) return ch;
   if (ch < beta) return beta;
@@ -323,41 +307,98 @@ __device__ float chunk_compose(float h, float beta, float a, int rows, const Chu
   return hh;
 }
 
-// forward pass 2: the exact starting state of every chunk.  One warp per
-// block, one (b, c) lane per thread.  The chunk states beta do not depend on
-// the walk: a window of up to kWin of them is copied into shared memory with
-// cp.async (all in flight together) before the dependent composes.
-constexpr int kWin = 128;
-constexpr int kWalkGroup = 64;   // values read together by the ga reduction
+// max(chain_n(g0), g1): a stretch of n steps with own state g1 (from -inf),
+// entered with g0; NaN wins; equal zeros (signs may differ) set tie0.
+// Needs a != +inf (see chunk_compose).
+__device__ __forceinline__ float join_chain(float g0, float g1, float a, int64_t n, bool& tie0) {
+  if (g1 != g1) return g1;
+  if (g0 != g0) return g0;
+  if (g0 == -INFINITY || chain_below(g0, a, (float)n, g1)) return g1;
+  const float ch = chain_exact(g0, a, n);
+  if (ch != ch) return ch;
+  if (ch > g1) return ch;
+  if (ch < g1) return g1;
+  if (ch == 0.0f) tie0 = true;            // equal nonzero values have equal bits
+  return g1;
+}
 
-__global__ void __launch_bounds__(32) chunk_fwd_carry_kernel(const ChunkArgs p) {
-  __shared__ float s_beta[kWin][32];
-  const int lane = threadIdx.x;
-  const int64_t e = (int64_t)blockIdx.x * 32 + lane;
-  const bool live = e < p.B * p.C;
-  const int64_t b = live ? e / p.C : 0, c = live ? e % p.C : 0;
-  const float a = live ? p.a[c] : 0.0f;
-  float h = (live && p.h0) ? p.h0[b * p.C + c] : p.h_init;
+// forward pass 2: the exact starting state of every chunk, by a parallel
+// scan over the chunks of one (b, c) lane per block.  The run through chunks
+// i..j from any entering state h is max(chain_n(h), G) with n their steps and
+// G their state from -inf, so runs compose as (n1, G1) then (n2, G2) ->
+// (n1 + n2, max(chain_n2(G1), G2)) -- associative, exact with chain_exact.
+// Each warp scans 32 chunks with shuffles (5 levels); warp totals chain in
+// order; a tile of blockDim.x chunks at a time.  Equal zeros anywhere (their
+// sign bits are not decided by the values) send the lane to the chunk-by-
+// chunk walk, which replays such chunks.
+constexpr int kScanWarps = 4;
+
+__global__ void __launch_bounds__(kScanWarps * 32) chunk_fwd_scan_kernel(const ChunkArgs p) {
+  __shared__ int64_t s_n[kScanWarps];
+  __shared__ float s_g[kScanWarps];
+  __shared__ float s_carry;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t b = blockIdx.x / p.C, c = blockIdx.x % p.C;
+  const float a = p.a[c];
+  const float e0 = p.h0 ? p.h0[b * p.C + c] : p.h_init;
   const float* beta = p.beta + b * p.nch * p.C + c;
   float* hs = p.hs + b * p.nch * p.C + c;
-  for (int w0 = 0; w0 < p.nch; w0 += kWin) {
-    const int n = min(kWin, p.nch - w0);
-    if (live)
-      for (int k = 0; k < n; ++k) tp_cp_async4(&s_beta[k][lane], beta + (int64_t)(w0 + k) * p.C, 4);
-    tp_cp_async_commit();
-    tp_cp_async_wait<0>();
-    if (live) {
-      for (int k = 0; k < n; ++k) {
-        const int jj = w0 + k;
-        hs[(int64_t)jj * p.C] = h;
-        const int64_t t0 = (int64_t)jj * p.L;
-        const int rows = (int)((p.T - t0) < p.L ? (p.T - t0) : p.L);
-        h = chunk_compose(h, s_beta[k][lane], a, rows, p, b, c, t0);
+  if (a == INFINITY) {                    // see chunk_compose
+    const float later = (e0 == -INFINITY || e0 != e0) ? __int_as_float(0x7fc00000) : a;
+    for (int j = threadIdx.x; j < p.nch; j += blockDim.x) hs[(int64_t)j * p.C] = j == 0 ? e0 : later;
+    return;
+  }
+  if (threadIdx.x == 0) s_carry = e0;
+  bool tie0 = false;
+  for (int j0 = 0; j0 < p.nch; j0 += blockDim.x) {
+    const int j = j0 + threadIdx.x;
+    const bool in = j < p.nch;
+    const int64_t t0 = (int64_t)j * p.L;
+    int64_t n = in ? ((p.T - t0) < p.L ? (p.T - t0) : p.L) : 0;
+    float g = in ? __ldcg(beta + (int64_t)j * p.C) : -INFINITY;
+#pragma unroll
+    for (int d = 1; d < 32; d *= 2) {     // inclusive scan of the warp's chunks
+      const int64_t np = __shfl_up_sync(0xffffffffu, n, d);
+      const float gp = __shfl_up_sync(0xffffffffu, g, d);
+      if (lane >= d) {
+        g = join_chain(gp, g, a, n, tie0);
+        n += np;
       }
     }
-    __syncwarp();
+    if (lane == 31) {
+      s_n[warp] = n;
+      s_g[warp] = g;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {               // state entering each warp's first chunk
+      float st = s_carry;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+        const float enter = st;
+        if (s_n[w] > 0) st = join_chain(st, s_g[w], a, s_n[w], tie0);
+        s_g[w] = enter;
+      }
+      s_carry = st;
+    }
+    __syncthreads();
+    const int64_t ne = __shfl_up_sync(0xffffffffu, n, 1);
+    const float ge = __shfl_up_sync(0xffffffffu, g, 1);
+    const float enter = s_g[warp];
+    const float start = lane == 0 ? enter : join_chain(enter, ge, a, ne, tie0);
+    if (in) hs[(int64_t)j * p.C] = start;
+    __syncthreads();                      // s_g is rewritten by the next tile
+  }
+  if (__syncthreads_or(tie0) && threadIdx.x == 0) {
+    float h = e0;
+    for (int j = 0; j < p.nch; ++j) {
+      hs[(int64_t)j * p.C] = h;
+      const int64_t t0 = (int64_t)j * p.L;
+      const int rows = (int)((p.T - t0) < p.L ? (p.T - t0) : p.L);
+      h = chunk_compose(h, __ldcg(beta + (int64_t)j * p.C), a, rows, p, b, c, t0);
+    }
   }
 }
+
+constexpr int kWalkGroup = 64;   // values read together by the ga reduction
 
 // ---------------------------------------------------------------------------
 // backward: pass A (kOut = false: carry leaving the chunk from carry 0, and
@@ -390,13 +431,14 @@ __global__ void __launch_bounds__(kPassThreads) chunk_bwd_kernel(const ChunkArgs
     any[v] = false;
   }
   const int64_t base = (s.b * p.T + s.t0) * p.C + s.c;
+  const uint64_t pol = l2_policy(!kOut);
   uint32_t word[V];
   int cur_w = -1;
   auto step_row = [&](int t, const float (&g)[V], const float (&u)[V], const float (&hp)[V]) {
     if (kMask) {
       const int w = (int)((s.t0 + t) / 32);
       if (w != cur_w) {
-        ldw<V>(word, p.win_in + (s.b * p.nw + w) * p.C + s.c);
+        ldw_pol<V>(word, p.win_in + (s.b * p.nw + w) * p.C + s.c, pol);
         cur_w = w;
       }
     }
@@ -423,12 +465,12 @@ __global__ void __launch_bounds__(kPassThreads) chunk_bwd_kernel(const ChunkArgs
     for (int k = 0; k < kRowBlock; ++k) {
       const int tt = t - k;
       const int64_t off = base + (int64_t)tt * p.C;
-      ldv<V>(g[k], p.gh + off);
+      ldv_pol<V>(g[k], p.gh + off, pol);
       if (!kMask) {
-        ldv<V>(u[k], p.bb + off);
+        ldv_pol<V>(u[k], p.bb + off, pol);
         if (kHasX) {
           float xv[V];
-          ldv<V>(xv, p.xx + off);
+          ldv_pol<V>(xv, p.xx + off, pol);
 #pragma unroll
           for (int v = 0; v < V; ++v) u[k][v] = u[k][v] + xv[v];
         }
@@ -436,7 +478,7 @@ __global__ void __launch_bounds__(kPassThreads) chunk_bwd_kernel(const ChunkArgs
 #pragma unroll
           for (int v = 0; v < V; ++v) hp[k][v] = hm1[v];
         } else {
-          ldv<V>(hp[k], p.hin + off - p.C);
+          ldv_pol<V>(hp[k], p.hin + off - p.C, pol);
         }
       }
     }
@@ -446,12 +488,12 @@ __global__ void __launch_bounds__(kPassThreads) chunk_bwd_kernel(const ChunkArgs
   for (; t >= 0; --t) {
     float g[V], u[V], hp[V];
     const int64_t off = base + (int64_t)t * p.C;
-    ldv<V>(g, p.gh + off);
+    ldv_pol<V>(g, p.gh + off, pol);
     if (!kMask) {
-      ldv<V>(u, p.bb + off);
+      ldv_pol<V>(u, p.bb + off, pol);
       if (kHasX) {
         float xv[V];
-        ldv<V>(xv, p.xx + off);
+        ldv_pol<V>(xv, p.xx + off, pol);
 #pragma unroll
         for (int v = 0; v < V; ++v) u[v] = u[v] + xv[v];
       }
@@ -459,7 +501,7 @@ __global__ void __launch_bounds__(kPassThreads) chunk_bwd_kernel(const ChunkArgs
 #pragma unroll
         for (int v = 0; v < V; ++v) hp[v] = hm1[v];
       } else {
-        ldv<V>(hp, p.hin + off - p.C);
+        ldv_pol<V>(hp, p.hin + off - p.C, pol);
       }
     }
     step_row(t, g, u, hp);
@@ -579,10 +621,11 @@ unsigned blocks_for(int64_t threads, int per_block) {
 }  // namespace
 
 int scan_chunk_pick(int64_t B, int64_t T, int64_t C) {
-  // 64-step chunks: measured best at T = 4096, C = 1024 for B = 1, 2 and 4
-  // (B = 2: forward 0.058 ms at 64 against 0.067 at 32 and 0.069 at 128;
+  // 64-step chunks: measured best at T = 4096, C = 1024 for B = 2 and 4
+  // (B = 2: forward 0.044 ms at 64 against 0.052 at 32 and 0.055 at 128;
   // backward 0.186 / 0.218 / 0.244 ms) -- shorter chunks lengthen the
-  // per-lane walks, longer ones leave the parallel passes too few threads
+  // backward's per-lane walks, longer ones leave the parallel passes too few
+  // threads
   (void)B;
   (void)C;
   return T >= 128 ? 64 : 32;
@@ -652,7 +695,11 @@ int launch_scan_fwd_chunked(const ScanArgs& q, int chunk, void* ws, int64_t ws_b
     if (p.xx) TP_FWD1(1, true); else TP_FWD1(1, false);
   }
   if ((s = launch_status()) != TP_OK) return s;
-  chunk_fwd_carry_kernel<<<blocks_for(p.B * p.C, 32), 32, 0, stream>>>(p);
+  {
+    const int64_t want = ceil_div((int64_t)p.nch, 32) * 32;
+    const int threads = want < kScanWarps * 32 ? (int)want : kScanWarps * 32;
+    chunk_fwd_scan_kernel<<<(unsigned)(p.B * p.C), threads, 0, stream>>>(p);
+  }
   if ((s = launch_status()) != TP_OK) return s;
   const bool mk = p.win != nullptr;
   if (v4) {

@@ -88,9 +88,12 @@ def test_forward_special_values(cuda):
     a[6] = -0.0
     u[:, :, 7] = 0.0
     a[7] = 0.0
+    a[8] = np.inf                            # -inf + inf is NaN, finite + inf stays +inf
+    u[0, :, 8] = -np.inf                     # no finite input before t = 40 in row 0
+    u[0, 40:, 8] = rng.standard_normal(T - 40)
     ops = _ops()
     for h_init in (0.0, -0.0, float("-inf")):
-        for chunk in (32, 96):
+        for chunk in (32, 64, 96):
             h, mask = _fwd(ops, u, None, a, h_init, chunk=chunk)
             rh, win = oscan.scan_fwd(u, a, h_init)
             np.testing.assert_array_equal(h.view(np.uint32)[~np.isnan(rh)],
@@ -202,3 +205,25 @@ def test_forward_carry_chains_at_binade_edges(cuda):
         rh, win = oscan.scan_fwd(u, a, 0.0, h0)
         np.testing.assert_array_equal(h.view(np.uint32), rh.view(np.uint32))
         np.testing.assert_array_equal(mask, oscan.win_mask_words(win))
+
+
+def test_forward_scan_over_many_chunks(cuda):
+    # the chunks' starting states come from a parallel scan over the chunks of
+    # each (b, c) lane, 128 chunks per tile: 313 / 625 / 157 chunks (several
+    # tiles, a partial last chunk and warp), slow channels whose carry
+    # survives many chunks in a row, C not a multiple of 4 (one channel per
+    # thread); bit-exact with the recurrence, also when called again
+    B, T, C = 2, 20000, 130
+    rng = np.random.default_rng(11)
+    a = -rng.random(C).astype(np.float32)
+    a[::5] = -(10.0 ** rng.uniform(-7, -3, a[::5].size)).astype(np.float32)
+    u = rng.standard_normal((B, T, C)).astype(np.float32)
+    h0 = rng.standard_normal((B, C)).astype(np.float32)
+    rh, win = oscan.scan_fwd(u, a, 0.0, h0)
+    words = oscan.win_mask_words(win)
+    ops = _ops()
+    for chunk in (64, 32, 64, 128):
+        h, mask = _fwd(ops, u, None, a, 0.0, h0=h0, chunk=chunk)
+        np.testing.assert_array_equal(h.view(np.uint32), rh.view(np.uint32))
+        np.testing.assert_array_equal(mask, words)
+    ops.check_device_error()
