@@ -282,6 +282,23 @@ TP_API int tp_tsrn_attention_prologue(int64_t B, int64_t T, int64_t H, int64_t d
                                       int64_t npos, int64_t pos0, float* Q, float* K, float* V,
                                       void* stream);
 
+/* Backward of LayerNorm over rows of D channels (training): the pre-norms of
+ * the TSRN block's tropical branches (research/tsrn_dml.py:1096-1106,
+ * nn.LayerNorm(d_model) before the attention, the reservoir and the SSM).
+ * x [rows, D] is the LayerNorm's input, dy the gradient of its output; writes
+ * dx [rows, D] and, when not NULL, dgamma [D] and dbeta [D] (the row
+ * statistics are recomputed; gamma NULL means ones).  D a multiple of 128, at
+ * most 1024; x, dy, dx, gamma 16-byte aligned.  workspace:
+ * tp_layernorm_bwd_workspace_bytes(rows, D) bytes (-1: unsupported D) for the
+ * parameter gradients' per-block partials, summed in a fixed order
+ * (deterministic).  (Replaces PyTorch's LayerNorm backward; no C counterpart
+ * in the reference.) */
+TP_API int64_t tp_layernorm_bwd_workspace_bytes(int64_t rows, int64_t D);
+TP_API int tp_layernorm_bwd(int64_t rows, int64_t D, const float* x, const float* dy,
+                            const float* gamma, float eps, float* dx, float* dgamma,
+                            float* dbeta, void* workspace, int64_t workspace_bytes,
+                            void* stream);
+
 /* Backward of tp_tsrn_attention_prologue (training): from the gradients of Q,
  * K, V ([B, H, T, dh] contiguous) and the projections qkv, the gradient of qkv
  * (dqkv, same [B*T, ld] layout: Q, K, V columns at 0, koff, voff) and of the

@@ -151,6 +151,11 @@ SIGNATURES: dict[str, tuple] = {
         [_c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_int, _c_int,
          _c_p, _c_p, _c_i64, _c_p],
     ),
+    "tp_layernorm_bwd_workspace_bytes": (_c_i64, [_c_i64, _c_i64]),
+    "tp_layernorm_bwd": (
+        _c_int,
+        [_c_i64, _c_i64, _c_p, _c_p, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p],
+    ),
     "tp_tsrn_attention_prologue_bwd_workspace_bytes": (_c_i64, [_c_i64, _c_i64, _c_i64, _c_i64]),
     "tp_tsrn_attention_prologue_bwd": (
         _c_int,

@@ -572,6 +572,32 @@ int tp_tsrn_attention_prologue_bwd(int64_t B, int64_t T, int64_t H, int64_t dh, 
                                       (float*)workspace, as_stream(stream));
 }
 
+int64_t tp_layernorm_bwd_workspace_bytes(int64_t rows, int64_t D) {
+  if (rows < 0 || !tp::layernorm_bwd_supported(D)) return -1;
+  return (int64_t)tp::layernorm_bwd_blocks(rows) * 2 * D * (int64_t)sizeof(float);
+}
+
+int tp_layernorm_bwd(int64_t rows, int64_t D, const float* x, const float* dy,
+                     const float* gamma, float eps, float* dx, float* dgamma, float* dbeta,
+                     void* workspace, int64_t workspace_bytes, void* stream) {
+  TP_RETURN_IF(rows < 0 || D <= 0, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(!tp::layernorm_bwd_supported(D), TP_ERR_UNSUPPORTED);
+  TP_RETURN_IF(!(eps >= 0.0f), TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(workspace == nullptr ||
+                   workspace_bytes < tp_layernorm_bwd_workspace_bytes(rows, D),
+               TP_ERR_WORKSPACE);
+  TP_CHECK_PTR(workspace);
+  if (gamma != nullptr) TP_RETURN_IF(!aligned16(gamma), TP_ERR_MISALIGNED);
+  if (rows > 0) {
+    TP_CHECK_PTR(x);
+    TP_CHECK_PTR(dy);
+    TP_CHECK_PTR(dx);
+    TP_RETURN_IF(!aligned16(x) || !aligned16(dy) || !aligned16(dx), TP_ERR_MISALIGNED);
+  }
+  return tp::launch_layernorm_bwd(rows, D, x, dy, gamma, eps, dx, dgamma, dbeta,
+                                  (float*)workspace, as_stream(stream));
+}
+
 int tp_tsrn_attention_fwd(int64_t B, int64_t H, int64_t T, int64_t Tkv, int64_t Tc, int64_t dh,
                           const float* Q, const float* K, const float* V,
                           const float* alibi_slopes, int top_k, int causal, float* out,

@@ -236,6 +236,11 @@ int launch_tsrn_prologue(int64_t B, int64_t T, int64_t H, int64_t dh, const floa
                          const float* kg, const float* kb, float eps, const float* cosb,
                          const float* sinb, int64_t pos0, float* Q, float* K, float* V,
                          cudaStream_t stream);
+int layernorm_bwd_blocks(int64_t rows);
+bool layernorm_bwd_supported(int64_t D);
+int launch_layernorm_bwd(int64_t rows, int64_t D, const float* x, const float* dy,
+                         const float* gamma, float eps, float* dx, float* dgamma, float* dbeta,
+                         float* part, cudaStream_t stream);
 int tsrn_prologue_bwd_blocks(int64_t B, int64_t T, int64_t H);
 int launch_tsrn_prologue_bwd(int64_t B, int64_t T, int64_t H, int64_t dh, const float* qkv,
                              int64_t ld, int64_t koff, int64_t voff, const float* qg,

@@ -878,6 +878,14 @@ def matmul_tn_tf32x3(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return _mm3(ah.t(), al.t(), bh, bl)
 
 
+def _linear3(xh, xl, wh, wl, b):
+    """hi.hi + hi.lo + lo.hi (+ b) as three cuBLAS TF32 GEMMs on split parts."""
+    with _tf32_matmuls():
+        y = torch.addmm(b, xh, wh.t()) if b is not None else xh @ wh.t()
+        y.addmm_(xh, wl.t()).addmm_(xl, wh.t())
+    return y
+
+
 def linear_tf32x3(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None):
     """``x @ w.T (+ b)`` at fp32 accuracy on the TF32 tensor cores: x and w are
     split into TF32 hi and lo parts (``split_tf32``) and three cuBLAS TF32 GEMMs
@@ -888,34 +896,34 @@ def linear_tf32x3(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = 
     K = x.shape[-1]
     xh, xl = split_tf32(x.reshape(-1, K))
     wh, wl = split_tf32(w)
-    with _tf32_matmuls():
-        y = torch.addmm(b, xh, wh.t()) if b is not None else xh @ wh.t()
-        y.addmm_(xh, wl.t()).addmm_(xl, wh.t())
-    return y.reshape(*x.shape[:-1], w.shape[0])
+    return _linear3(xh, xl, wh, wl, b).reshape(*x.shape[:-1], w.shape[0])
 
 
 class LinearTF32x3Function(torch.autograd.Function):
     """``linear_tf32x3`` with its backward in the same form: dx = dy @ w and
-    dw = dy^T @ x as 3xTF32 GEMMs (the splits recomputed, not saved), db = the
-    column sums of dy."""
+    dw = dy^T @ x as 3xTF32 GEMMs, db = the column sums of dy.  The forward's
+    split parts of x and w are kept for the backward (x's parts instead of x:
+    twice its bytes, one read and two writes of x fewer per step)."""
 
     @staticmethod
     def forward(ctx, x, w, b):
-        ctx.save_for_backward(x, w)
+        K = x.shape[-1]
+        xh, xl = split_tf32(x.reshape(-1, K))
+        wh, wl = split_tf32(w)
+        ctx.save_for_backward(xh, xl, wh, wl)
+        ctx.x_shape = x.shape
         ctx.has_bias = b is not None
-        return linear_tf32x3(x, w, b)
+        return _linear3(xh, xl, wh, wl, b).reshape(*x.shape[:-1], w.shape[0])
 
     @staticmethod
     def backward(ctx, dy):
-        x, w = ctx.saved_tensors
-        K, N = x.shape[-1], w.shape[0]
+        xh, xl, wh, wl = ctx.saved_tensors
+        N = wh.shape[0]
         gh, gl = split_tf32(dy.reshape(-1, N))
         dx = dw = db = None
         if ctx.needs_input_grad[0]:
-            wh, wl = split_tf32(w)
-            dx = _mm3(gh, gl, wh, wl).reshape(x.shape)
+            dx = _mm3(gh, gl, wh, wl).reshape(ctx.x_shape)
         if ctx.needs_input_grad[1]:
-            xh, xl = split_tf32(x.reshape(-1, K))
             dw = _mm3(gh.t(), gl.t(), xh, xl)
         if ctx.has_bias and ctx.needs_input_grad[2]:
             db = dy.reshape(-1, N).sum(0)
@@ -1098,6 +1106,71 @@ def tsrn_attention_prologue_bwd(qkv: torch.Tensor, B: int, T: int, H: int, dh: i
             _ptr(dqkv), _ptr(dp), _ptr(ws), ws.numel() * 4, _stream(dev))
     _lib.check(st, "tp_tsrn_attention_prologue_bwd")
     return dqkv, dp[0], dp[1], dp[2], dp[3]
+
+
+def layer_norm_supported(D: int) -> bool:
+    """Whether :func:`layer_norm_bwd` takes rows of ``D`` channels (a multiple of
+    128, at most 1024)."""
+    return 128 <= D <= 1024 and D % 128 == 0
+
+
+def layer_norm_bwd(x: torch.Tensor, dy: torch.Tensor, weight: Optional[torch.Tensor],
+                   eps: float):
+    """Backward of ``F.layer_norm(x, (D,), weight, bias, eps)`` over the last
+    dimension: (dx, dweight, dbias), one pass over x and dy with the row
+    statistics recomputed; the parameter gradients are summed per block and then
+    over blocks in a fixed order (the same bits on every call).  The pre-norms of
+    the TSRN block's branches (research/tsrn_dml.py:1096-1106) in training."""
+    dev = _require_cuda(x, dy, weight)
+    D = x.shape[-1]
+    if not layer_norm_supported(D):
+        raise ValueError(f"layer_norm_bwd takes D a multiple of 128 up to 1024, got {D}")
+    x2 = _f32(x).reshape(-1, D).contiguous()
+    dy2 = _f32(dy).reshape(-1, D).contiguous()
+    rows = x2.shape[0]
+    w = _f32(weight.detach()).contiguous() if weight is not None else None
+    dx = torch.empty_like(x2)
+    dw = torch.empty(D, device=dev)
+    db = torch.empty(D, device=dev)
+    lib = _lib.load()
+    ws_bytes = int(lib.tp_layernorm_bwd_workspace_bytes(rows, D))
+    ws = torch.empty(max(ws_bytes // 4, 4), device=dev)
+    with torch.cuda.device(dev):
+        st = lib.tp_layernorm_bwd(rows, D, _ptr(x2), _ptr(dy2), _ptr(w), float(eps), _ptr(dx),
+                                  _ptr(dw), _ptr(db), _ptr(ws), ws.numel() * 4, _stream(dev))
+    _lib.check(st, "tp_layernorm_bwd")
+    return dx.reshape(x.shape), dw, db
+
+
+class LayerNormFunction(torch.autograd.Function):
+    """LayerNorm over the last dimension: PyTorch's forward kernel, the backward
+    of :func:`layer_norm_bwd`."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps: float):
+        ctx.save_for_backward(x, weight)
+        ctx.eps = eps
+        ctx.has_bias = bias is not None
+        return torch.nn.functional.layer_norm(x, (x.shape[-1],), weight, bias, eps)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight = ctx.saved_tensors
+        dx, dw, db = layer_norm_bwd(x, dy, weight, ctx.eps)
+        return (dx, dw if weight is not None else None, db if ctx.has_bias else None, None)
+
+
+def layer_norm(x: torch.Tensor, weight: Optional[torch.Tensor], bias: Optional[torch.Tensor],
+               eps: float = 1e-5) -> torch.Tensor:
+    """``F.layer_norm`` over the last dimension with the backward of
+    :func:`layer_norm_bwd` when autograd records on a supported CUDA fp32 shape
+    (else PyTorch's own)."""
+    needs = torch.is_grad_enabled() and (x.requires_grad or (
+        weight is not None and weight.requires_grad) or (bias is not None and bias.requires_grad))
+    if (needs and x.is_cuda and x.dtype == torch.float32 and layer_norm_supported(x.shape[-1])
+            and (weight is None or weight.dtype == torch.float32)):
+        return LayerNormFunction.apply(x, weight, bias, float(eps))
+    return torch.nn.functional.layer_norm(x, (x.shape[-1],), weight, bias, eps)
 
 
 def tsrn_attention_host(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor,

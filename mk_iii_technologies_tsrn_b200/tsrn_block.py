@@ -28,6 +28,7 @@ from typing import Dict, Optional
 import torch
 import torch.nn as nn
 
+from . import ops
 from .reservoir import EchoStateReservoir
 from .ssm import TropicalSSM
 from .tsrn_attention import TropicalAttention
@@ -57,7 +58,7 @@ class TSRNTropicalPath(nn.Module):
         def branch(name, ln, mod, h):
             if events is not None and name in events:
                 events[name][0].record()
-            out = h + mod(ln(h))
+            out = h + mod(ops.layer_norm(h, ln.weight, ln.bias, ln.eps))
             if events is not None and name in events:
                 events[name][1].record()
             return out

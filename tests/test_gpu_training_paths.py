@@ -223,3 +223,51 @@ def test_attention_prologue_backward_repeats(cuda):
     b = ops.tsrn_attention_prologue_bwd(qkv, B, T, H, dh, qg, kg, 1e-5, cos, sin, dQ, dK, dV)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("rows,D", [(3000, 640), (517, 128), (64, 1024), (1, 384)])
+def test_layer_norm_backward_matches_autograd(cuda, rows, D):
+    # the pre-norms of the block's branches (research/tsrn_dml.py:1096-1106)
+    # with this library's backward, against float64 autograd
+    from mk_iii_technologies_tsrn_b200 import ops
+    gen = torch.Generator().manual_seed(rows + D)
+    x = torch.randn(rows, D, generator=gen) * 3.0 + 1.5
+    w = torch.randn(D, generator=gen)
+    b = torch.randn(D, generator=gen)
+    gy = torch.randn(rows, D, generator=gen)
+    xs, ws, bs = (t.to(cuda).requires_grad_(True) for t in (x, w, b))
+    y = ops.layer_norm(xs, ws, bs, 1e-5)
+    assert "LayerNormFunction" in type(y.grad_fn).__name__
+    (y * gy.to(cuda)).sum().backward()
+    xd, wd, bd = (t.double().requires_grad_(True) for t in (x, w, b))
+    yd = torch.nn.functional.layer_norm(xd, (D,), wd, bd, 1e-5)
+    (yd * gy.double()).sum().backward()
+    _close(y, yd, rtol=1e-5, atol=1e-6)
+    _close(xs.grad, xd.grad, rtol=1e-4, atol=1e-6)
+    _close(ws.grad, wd.grad, rtol=1e-4, atol=1e-6)
+    _close(bs.grad, bd.grad, rtol=1e-4, atol=1e-6)
+
+
+def test_layer_norm_backward_repeats_and_edges(cuda):
+    from mk_iii_technologies_tsrn_b200 import ops
+    gen = torch.Generator(device=cuda).manual_seed(5)
+    x = torch.randn(4099, 640, device=cuda, generator=gen)
+    dy = torch.randn(4099, 640, device=cuda, generator=gen)
+    w = torch.randn(640, device=cuda, generator=gen)
+    first = ops.layer_norm_bwd(x, dy, w, 1e-5)
+    second = ops.layer_norm_bwd(x, dy, w, 1e-5)
+    for a, b in zip(first, second):
+        assert torch.equal(a, b)
+    # no weight: gamma = 1 (dx equals the weighted form at w = 1)
+    ones = torch.ones(640, device=cuda)
+    for a, b in zip(ops.layer_norm_bwd(x, dy, None, 1e-5), ops.layer_norm_bwd(x, dy, ones, 1e-5)):
+        assert torch.equal(a, b)
+    # no rows: zero parameter gradients
+    dx, dw, db = ops.layer_norm_bwd(x[:0], dy[:0], w, 1e-5)
+    assert dx.shape == (0, 640) and not dw.any() and not db.any()
+    # unsupported width: PyTorch's own backward through ops.layer_norm
+    xs = torch.randn(10, 100, device=cuda, requires_grad=True)
+    y = ops.layer_norm(xs, None, None)
+    assert "LayerNormFunction" not in type(y.grad_fn).__name__
+    with pytest.raises(ValueError):
+        ops.layer_norm_bwd(xs.detach(), xs.detach(), None, 1e-5)
