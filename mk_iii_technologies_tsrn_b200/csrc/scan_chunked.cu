@@ -87,6 +87,7 @@ struct ChunkArgs {
   float* cin;
   float* gap;
   int* tflag;                      // 1: no input won in the chunk
+  int* err;                        // device status block (bounded waits)
 };
 
 template <int V>
@@ -590,6 +591,135 @@ __global__ void __launch_bounds__(32) chunk_bwd_carry_kernel(const ChunkArgs p) 
   if (live && p.gh0) p.gh0[b * p.C + c] = carry;
 }
 
+// backward pass B with the gradient rows staged by TMA (C % 4 == 0, aligned
+// gh): one warp per (b, 32 channels).  The rows of every chunk in which some
+// lane has no winner arrive as boxes of kWalkBox rows x 32 channels, one copy
+// instruction per box, kWalkSlots boxes in flight across chunk boundaries;
+// the lanes then only add (the row copies of the plain walk above cost one
+// instruction per row and a memory round trip per chunk).  With few boxes in
+// flight the warp waits on each copy's latency: 24 slots (96 KB of dynamic
+// shared memory) keep it adding.
+constexpr int kWalkBox = 32;
+constexpr int kWalkSlots = 24;
+constexpr int kTmaWin = 64;      // chunk words per window
+
+struct WalkSmem {
+  float g[kWalkSlots][kWalkBox][32];
+  int tf[kTmaWin][32];
+  float co[kTmaWin][32];
+  int need[kTmaWin];
+  uint64_t full[kWalkSlots];
+};
+
+bool make_walk_map(CUtensorMap* map, const float* base, int64_t rows, int64_t C) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)C, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)C * 4};
+  cuuint32_t box[2] = {32, kWalkBox};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+__global__ void __launch_bounds__(32)
+    chunk_bwd_carry_tma_kernel(const __grid_constant__ CUtensorMap gmap, const ChunkArgs p,
+                               int cgroups) {
+  extern __shared__ __align__(128) unsigned char walk_smem[];
+  WalkSmem& sm = *reinterpret_cast<WalkSmem*>(walk_smem);
+  auto& s_g = sm.g;
+  auto& s_tf = sm.tf;
+  auto& s_co = sm.co;
+  auto& s_need = sm.need;
+  auto& full = sm.full;
+  const unsigned all = 0xffffffffu;
+  const int lane = threadIdx.x;
+  const int64_t b = blockIdx.x / cgroups;
+  const int64_t c0 = (int64_t)(blockIdx.x % cgroups) * 32;
+  const int64_t c = c0 + lane;
+  const bool live = c < p.C;
+  const int64_t base = b * p.nch * p.C + c;
+  const int64_t row0 = b * p.T;
+  auto boxes_of = [&](int j) {
+    const int64_t t0 = (int64_t)j * p.L;
+    const int rows = (int)((p.T - t0) < p.L ? (p.T - t0) : p.L);
+    return (rows + kWalkBox - 1) / kWalkBox;
+  };
+  if (lane == 0) {
+    for (int s = 0; s < kWalkSlots; ++s) tp_mbar_init(&full[s], 1);
+    tp_fence_mbar_init();
+  }
+  __syncwarp();
+  uint32_t issued = 0, used = 0;      // boxes copied / added so far (lane 0 counts the first)
+  float carry = 0.0f;
+  for (int w1 = p.nch; w1 > 0; w1 -= kTmaWin) {            // window of chunks [w0, w1)
+    const int w0 = max(0, w1 - kTmaWin);
+    if (live) {
+      for (int j = w0; j < w1; ++j) {
+        tp_cp_async4(&s_tf[j - w0][lane], p.tflag + base + (int64_t)j * p.C, 4);
+        tp_cp_async4(&s_co[j - w0][lane], p.cout + base + (int64_t)j * p.C, 4);
+      }
+    }
+    tp_cp_async_commit();
+    tp_cp_async_wait<0>();
+    __syncwarp();
+    // chunks in which some lane has no winner, last first
+    int nneed = 0;
+    for (int j = w1 - 1; j >= w0; --j) {
+      if (__any_sync(all, live && s_tf[j - w0][lane] != 0)) {
+        if (lane == 0) s_need[nneed] = j;
+        ++nneed;
+      }
+    }
+    __syncwarp();
+    // lane 0's copy cursor: needed chunk pn, box pq of it (top box first)
+    int pn = 0, pq = nneed > 0 ? boxes_of(s_need[0]) - 1 : 0;
+    auto issue_next = [&]() {
+      if (pn >= nneed) return;
+      const int j = s_need[pn];
+      const uint32_t s = issued % kWalkSlots;
+      tp_mbar_arrive_expect_tx(&full[s], kWalkBox * 32 * (uint32_t)sizeof(float));
+      tp_tma_load_2d(&s_g[s][0][0], &gmap, (int32_t)c0,
+                     (int32_t)(row0 + (int64_t)j * p.L + (int64_t)pq * kWalkBox), &full[s]);
+      ++issued;
+      if (--pq < 0 && ++pn < nneed) pq = boxes_of(s_need[pn]) - 1;
+    };
+    if (lane == 0)
+      for (int k = 0; k < kWalkSlots; ++k) issue_next();
+    int ni = 0;
+    for (int j = w1 - 1; j >= w0; --j) {
+      if (live) p.cin[base + (int64_t)j * p.C] = carry;
+      const bool needed = ni < nneed && s_need[ni] == j;
+      const bool adds = live && s_tf[j - w0][lane] != 0;
+      if (live && !adds) carry = s_co[j - w0][lane];
+      if (!needed) continue;                 // every lane has a winner in chunk j
+      ++ni;
+      const int64_t t0 = (int64_t)j * p.L;
+      const int rows = (int)((p.T - t0) < p.L ? (p.T - t0) : p.L);
+      for (int q = boxes_of(j) - 1; q >= 0; --q) {
+        const uint32_t s = used % kWalkSlots;
+        if (!tp_mbar_wait(&full[s], (used / kWalkSlots) & 1u, p.err)) return;
+        const int cnt = min(kWalkBox, rows - q * kWalkBox);   // the box's rows inside the chunk
+        if (adds) {                          // carry <- g_t + carry, t from the box's top down
+          const float* sg = &s_g[s][0][lane];
+          if (cnt == kWalkBox) {
+#pragma unroll
+            for (int r = kWalkBox - 1; r >= 0; --r) carry = sg[r * 32] + carry;
+          } else {
+            for (int r = cnt - 1; r >= 0; --r) carry = sg[r * 32] + carry;
+          }
+        }
+        ++used;
+        __syncwarp();                        // every lane is done with slot s
+        if (lane == 0) issue_next();
+      }
+    }
+  }
+  if (live && p.gh0) p.gh0[b * p.C + c] = carry;
+}
+
 // ga[c] = sum over b (ascending) of the chunk partials summed in descending
 // chunk order
 __global__ void chunk_ga_reduce_kernel(const ChunkArgs p) {
@@ -655,6 +785,7 @@ static int prepare(ChunkArgs& p, int chunk, void* ws, int64_t ws_bytes) {
   // forward: beta, hs; backward: cout, cin, gap, tflag
   p.beta = f0;
   p.hs = f1;
+  p.err = device_error_ptr();
   p.cout = f0;
   p.cin = f1;
   p.gap = f2;
@@ -745,7 +876,22 @@ int launch_scan_bwd_chunked(const ScanArgs& q, int chunk, void* ws, int64_t ws_b
   } while (0)
   if (v4) TP_BWD(4, false); else TP_BWD(1, false);
   if ((s = launch_status()) != TP_OK) return s;
-  chunk_bwd_carry_kernel<<<blocks_for(p.B * p.C, 32), 32, 0, stream>>>(p);
+  {
+    const int64_t cgroups = ceil_div(p.C, 32);
+    CUtensorMap gmap;
+    const int smem = (int)sizeof(WalkSmem);
+    const bool attr_set = cudaFuncSetAttribute(chunk_bwd_carry_tma_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               smem) == cudaSuccess;
+    if (!attr_set) cudaGetLastError();
+    if (attr_set && p.C % 4 == 0 && aligned16(p.gh) &&
+        p.B * p.T + kWalkBox < (int64_t)INT32_MAX && p.B * cgroups < (int64_t)INT32_MAX &&
+        make_walk_map(&gmap, p.gh, p.B * p.T, p.C))
+      chunk_bwd_carry_tma_kernel<<<(unsigned)(p.B * cgroups), 32, smem, stream>>>(gmap, p,
+                                                                                 (int)cgroups);
+    else
+      chunk_bwd_carry_kernel<<<blocks_for(p.B * p.C, 32), 32, 0, stream>>>(p);
+  }
   if ((s = launch_status()) != TP_OK) return s;
   if (v4) TP_BWD(4, true); else TP_BWD(1, true);
 #undef TP_BWD
