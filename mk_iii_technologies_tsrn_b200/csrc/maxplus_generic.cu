@@ -58,15 +58,45 @@ __device__ __forceinline__ void load_slab(float (*dst)[GB_M + 4], const T* base,
   }
 }
 
+// load_slab for a tile of ROWS rows loaded by THREADS threads
+template <typename T, int ROWS, int THREADS>
+__device__ __forceinline__ void load_slab_rows(float (*dst)[ROWS + 4], const T* base,
+                                               int64_t s_row, int64_t s_k, int64_t rows,
+                                               int64_t K, int64_t r0, int64_t k0, float kfill) {
+  static_assert((ROWS * GB_K) % THREADS == 0, "slab must split evenly over the threads");
+#pragma unroll
+  for (int r = 0; r < (ROWS * GB_K) / THREADS; ++r) {
+    const int e = threadIdx.x + r * THREADS;
+    const int rr = e / GB_K;
+    const int kk = e % GB_K;
+    const int64_t gr = r0 + rr;
+    const int64_t gk = k0 + kk;
+    float v;
+    if (gk >= K) {
+      v = kfill;
+    } else if (gr >= rows) {
+      v = 0.0f;
+    } else {
+      v = tp_load_as_f32<T>(base + gr * s_row + gk * s_k);
+    }
+    dst[kk][rr] = v;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // forward (hard max, optional argmax)
 // ---------------------------------------------------------------------------
+// TYR rows of 16 threads, 4 x 4 outputs each: tiles of (4 TYR) x 64.  Shapes
+// with few tiles take TYR = 8 or 4 (32- or 16-row tiles) so that more CTAs
+// share the work (config 1's 1024 x 256 output: 64 CTAs at TYR = 16, 256 at
+// TYR = 4).
 // kBf16Sum: every sum is rounded to bf16 (ties to even) before the max, the
 // arithmetic torch applies to bf16 tensors (TP_DTYPE_BF16_ARITH).
-template <typename T, bool kArgmax, bool kBf16Sum = false>
-__global__ void __launch_bounds__(G_THREADS)
+template <typename T, bool kArgmax, bool kBf16Sum = false, int TYR = 16>
+__global__ void __launch_bounds__(16 * TYR)
     maxplus_fwd_generic_kernel(StridedMaxPlus p) {
-  __shared__ float xs[GB_K][GB_M + 4];
+  constexpr int ROWS = 4 * TYR, THREADS = 16 * TYR;
+  __shared__ float xs[GB_K][ROWS + 4];
   __shared__ float ws[GB_K][GB_N + 4];
   __shared__ float lf_sm[64];
   if (!kArgmax && p.act.mode >= 0) {
@@ -75,7 +105,7 @@ __global__ void __launch_bounds__(G_THREADS)
   }
   const int tx = threadIdx.x % 16;
   const int ty = threadIdx.x / 16;
-  const int64_t m0 = (int64_t)blockIdx.y * GB_M;
+  const int64_t m0 = (int64_t)blockIdx.y * ROWS;
   const int64_t n0 = (int64_t)blockIdx.x * GB_N;
   const T* xg = static_cast<const T*>(p.x);
   const T* wg = static_cast<const T*>(p.w);
@@ -99,14 +129,14 @@ __global__ void __launch_bounds__(G_THREADS)
 
     for (int64_t k0 = 0; k0 < p.K; k0 += GB_K) {
       __syncthreads();
-      load_slab<T>(xs, xb, p.sx_m, p.sx_k, p.M, p.K, m0, k0, NEG_INF);
-      load_slab<T>(ws, wb, p.sw_n, p.sw_k, p.N, p.K, n0, k0, 0.0f);
+      load_slab_rows<T, ROWS, THREADS>(xs, xb, p.sx_m, p.sx_k, p.M, p.K, m0, k0, NEG_INF);
+      load_slab_rows<T, GB_N, THREADS>(ws, wb, p.sw_n, p.sw_k, p.N, p.K, n0, k0, 0.0f);
       __syncthreads();
 #pragma unroll
       for (int kk = 0; kk < GB_K; ++kk) {
         float a[4], b[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) a[i] = xs[kk][ty + 16 * i];
+        for (int i = 0; i < 4; ++i) a[i] = xs[kk][ty + TYR * i];
 #pragma unroll
         for (int j = 0; j < 4; ++j) b[j] = ws[kk][tx + 16 * j];
         const int k = (int)(k0 + kk);
@@ -131,7 +161,7 @@ __global__ void __launch_bounds__(G_THREADS)
     int32_t* ab = kArgmax ? p.am + b1 * p.sa_b1 + b2 * p.sa_b2 : nullptr;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      int64_t m = m0 + ty + 16 * i;
+      int64_t m = m0 + ty + TYR * i;
       if (m >= p.M) continue;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -1073,25 +1103,43 @@ inline unsigned flat_grid(int64_t total, int threads) {
 
 }  // namespace
 
-int launch_maxplus_fwd_generic(const StridedMaxPlus& p, cudaStream_t stream) {
-  dim3 grid = generic_grid(p.M, p.N, p.B1 * p.B2);
-  if (grid.x > 2147483647u || grid.y > 65535u) return TP_ERR_TOO_LARGE;
+template <int TYR>
+void launch_fwd_generic_tyr(const StridedMaxPlus& p, dim3 grid, cudaStream_t stream) {
   const bool am = p.am != nullptr;
+  const int t = 16 * TYR;
   if (p.dtype == TP_DTYPE_F32) {
     if (am)
-      maxplus_fwd_generic_kernel<float, true><<<grid, G_THREADS, 0, stream>>>(p);
+      maxplus_fwd_generic_kernel<float, true, false, TYR><<<grid, t, 0, stream>>>(p);
     else
-      maxplus_fwd_generic_kernel<float, false><<<grid, G_THREADS, 0, stream>>>(p);
+      maxplus_fwd_generic_kernel<float, false, false, TYR><<<grid, t, 0, stream>>>(p);
   } else if (p.dtype == TP_DTYPE_BF16) {
     if (am)
-      maxplus_fwd_generic_kernel<uint16_t, true><<<grid, G_THREADS, 0, stream>>>(p);
+      maxplus_fwd_generic_kernel<uint16_t, true, false, TYR><<<grid, t, 0, stream>>>(p);
     else
-      maxplus_fwd_generic_kernel<uint16_t, false><<<grid, G_THREADS, 0, stream>>>(p);
+      maxplus_fwd_generic_kernel<uint16_t, false, false, TYR><<<grid, t, 0, stream>>>(p);
   } else {
     if (am)
-      maxplus_fwd_generic_kernel<uint16_t, true, true><<<grid, G_THREADS, 0, stream>>>(p);
+      maxplus_fwd_generic_kernel<uint16_t, true, true, TYR><<<grid, t, 0, stream>>>(p);
     else
-      maxplus_fwd_generic_kernel<uint16_t, false, true><<<grid, G_THREADS, 0, stream>>>(p);
+      maxplus_fwd_generic_kernel<uint16_t, false, true, TYR><<<grid, t, 0, stream>>>(p);
+  }
+}
+
+int launch_maxplus_fwd_generic(const StridedMaxPlus& p, cudaStream_t stream) {
+  // the tallest tile that still gives every SM two CTAs (16-row tiles at least)
+  const int64_t batches = p.B1 * p.B2;
+  const int64_t want = 2 * (int64_t)num_sms();
+  int tyr = 16;
+  while (tyr > 4 && ceil_div(p.M, (int64_t)(4 * tyr)) * ceil_div(p.N, (int64_t)GB_N) *
+                            (batches < 65535 ? batches : 65535) < want)
+    tyr /= 2;
+  dim3 grid = generic_grid(p.M, p.N, batches);
+  grid.y = (unsigned)ceil_div(p.M, (int64_t)(4 * tyr));
+  if (grid.x > 2147483647u || ceil_div(p.M, (int64_t)(4 * tyr)) > 65535) return TP_ERR_TOO_LARGE;
+  if (tyr == 16) launch_fwd_generic_tyr<16>(p, grid, stream);
+  else if (tyr == 8) launch_fwd_generic_tyr<8>(p, grid, stream);
+  else {
+    launch_fwd_generic_tyr<4>(p, grid, stream);
   }
   return launch_status();
 }
