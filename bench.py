@@ -22,8 +22,13 @@ Batch workloads split the configuration's batch over the ranks
 ``--workload scan``: the tropical SSM scan at B=16, T=4096, C=1024: forward
 (read b, x; write h: 12 B/elem) plus argmax-path backward recomputing the
 winners (read g, h, b, x; write gu: 20 B/elem); metric GB/s of those
-algorithmic bytes.  Few lanes per GPU (B=2 at 8 GPUs) run the chunk-parallel
-scan.
+algorithmic bytes.  Few lanes per GPU (B=2 at 8 GPUs, or ``--scan-batch 2``
+on one) run the chunk-parallel scan.
+
+Workloads whose data fit in L2 (config 1, the DTN block, the scan at B <= 2
+per GPU) overwrite a 256 MiB buffer before every timed step, outside that
+step's CUDA events, and report the sum of the steps' device times; the other
+workloads read inputs larger than L2 every step.
 
 ``--workload linear``: config 1, the tropical linear x [1024,256] (x) W [256,256]
 forward with int32 argmax and the argmax backward; Gop/s of forward ops.
