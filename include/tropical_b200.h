@@ -496,6 +496,17 @@ TP_API int tp_esn_leaky_bwd(int64_t B, int64_t T, int64_t dr, const float* dH, c
  * 917-980) run that way in inference.  (Utility; no reference counterpart.) */
 TP_API int tp_split_tf32(const float* x, int64_t n, float* hi, float* lo, void* stream);
 
+/* The same split written row-concatenated: for x [rows, cols] (row-major,
+ * cols a multiple of 4), out [rows, nparts cols] (nparts 1 to 3) holds the
+ * parts of each row side by side, part p the lo part where bit p of lo_mask is
+ * set, else the hi part.  With A = [xh | xl] (lo_mask 2) and B = [wl | wh]
+ * (lo_mask 1), A B^T is the two correction products hi.lo + lo.hi as one
+ * TF32 GEMM of depth 2 cols, accumulated onto hi.hi (its own GEMM: the small
+ * terms are not summed inside the tensor cores' accumulation of the large
+ * ones).  x, out 16-byte aligned.  (Utility; no reference counterpart.) */
+TP_API int tp_split_tf32_cat(const float* x, int64_t rows, int64_t cols, float* out,
+                             int nparts, int lo_mask, void* stream);
+
 /* Copy `rows` rows of width_bytes from src (row pitch src_pitch bytes) to dst
  * (pitch dst_pitch), host or device memory on either side (pinned host memory
  * for an asynchronous copy), on `stream`: the strided time windows the

@@ -120,6 +120,7 @@ SIGNATURES: dict[str, tuple] = {
          _c_p],
     ),
     "tp_split_tf32": (_c_int, [_c_p, _c_i64, _c_p, _c_p, _c_p]),
+    "tp_split_tf32_cat": (_c_int, [_c_p, _c_i64, _c_i64, _c_p, _c_int, _c_int, _c_p]),
     "tp_esn_gru_bwd": (
         _c_int,
         [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_p, _c_i64,

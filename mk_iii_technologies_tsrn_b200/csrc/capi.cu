@@ -751,6 +751,18 @@ int tp_split_tf32(const float* x, int64_t n, float* hi, float* lo, void* stream)
   return tp::launch_split_tf32(x, n, hi, lo, as_stream(stream));
 }
 
+int tp_split_tf32_cat(const float* x, int64_t rows, int64_t cols, float* out, int nparts,
+                      int lo_mask, void* stream) {
+  TP_RETURN_IF(rows < 0 || cols < 0 || nparts < 1 || nparts > 3, TP_ERR_INVALID_ARG);
+  TP_RETURN_IF(lo_mask < 0 || lo_mask >= (1 << nparts), TP_ERR_INVALID_ARG);
+  if (rows * cols == 0) return TP_OK;
+  TP_RETURN_IF(cols % 4 != 0, TP_ERR_UNSUPPORTED);
+  TP_CHECK_PTR(x);
+  TP_CHECK_PTR(out);
+  TP_RETURN_IF(!aligned16(x) || !aligned16(out), TP_ERR_MISALIGNED);
+  return tp::launch_split_tf32_cat(x, rows, cols, out, nparts, lo_mask, as_stream(stream));
+}
+
 int tp_esn_gru_bwd(int64_t B, int64_t T, int64_t dr, const float* dH, const float* fa,
                    const float* fz, const float* fr, const float* keep, const float* r,
                    const float* WzhT, int64_t ld_wz, const float* WrhT, int64_t ld_wr,

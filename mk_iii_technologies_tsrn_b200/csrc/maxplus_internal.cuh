@@ -255,6 +255,8 @@ int launch_esn_fwd(bool gru, int64_t B, int64_t T, int64_t dr, const float* U, c
                    const float* leak, float* H, cudaStream_t stream, int64_t ts = 0,
                    const float* h0 = nullptr, int64_t ld_h0 = 0);
 int launch_split_tf32(const float* x, int64_t n, float* hi, float* lo, cudaStream_t stream);
+int launch_split_tf32_cat(const float* x, int64_t rows, int64_t cols, float* out, int nparts,
+                          int lo_mask, cudaStream_t stream);
 int launch_esn_bwd(bool gru, int64_t B, int64_t T, int64_t dr, const float* dH,
                    const float* const F[5], const float* const WT[3], const int64_t ld[3],
                    const float* leak, float* const out[3], cudaStream_t stream);

@@ -878,6 +878,21 @@ def matmul_tn_tf32x3(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return _mm3(ah.t(), al.t(), bh, bl)
 
 
+def split_tf32_cat(x: torch.Tensor, nparts: int, lo_mask: int) -> torch.Tensor:
+    """The parts of ``split_tf32`` row-concatenated: x [R, C] (C a multiple of 4)
+    -> [R, nparts C], part p (columns p C .. (p+1) C) the lo part where bit p of
+    ``lo_mask`` is set, else the hi part; one kernel."""
+    dev = _require_cuda(x)
+    x = _f32(x).contiguous()
+    R, C = x.shape
+    out = torch.empty(R, nparts * C, device=dev)
+    with torch.cuda.device(dev):
+        st = _lib.load().tp_split_tf32_cat(_ptr(x), R, C, _ptr(out), int(nparts), int(lo_mask),
+                                           _stream(dev))
+    _lib.check(st, "tp_split_tf32_cat")
+    return out
+
+
 def _linear3(xh, xl, wh, wl, b):
     """hi.hi + hi.lo + lo.hi (+ b) as three cuBLAS TF32 GEMMs on split parts."""
     with _tf32_matmuls():
@@ -886,14 +901,35 @@ def _linear3(xh, xl, wh, wl, b):
     return y
 
 
+def _linear2cat(A, Bm, b):
+    """A = [xh | xl], Bm = [wl | wh]: hi.hi (+ b) as one TF32 GEMM, then the two
+    correction products as one GEMM of depth 2K accumulated onto it -- the
+    output is read and written once for both (three GEMMs read and write it
+    twice), and the small terms are summed apart from the large one."""
+    K = A.shape[1] // 2
+    xh, wh = A[:, :K], Bm[:, K:]
+    with _tf32_matmuls():
+        y = torch.addmm(b, xh, wh.t()) if b is not None else xh @ wh.t()
+        y.addmm_(A, Bm.t())
+    return y
+
+
 def linear_tf32x3(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None):
     """``x @ w.T (+ b)`` at fp32 accuracy on the TF32 tensor cores: x and w are
-    split into TF32 hi and lo parts (``split_tf32``) and three cuBLAS TF32 GEMMs
-    sum hi.hi + hi.lo + lo.hi (the lo.lo term is below 2^-22 of the product):
+    split into TF32 hi and lo parts (``split_tf32``) and cuBLAS TF32 GEMMs sum
+    hi.hi + hi.lo + lo.hi (the lo.lo term is below 2^-22 of the product):
     ~2e-6 relative against ~1.5e-6 for fp32 SGEMM at K = 640, 3.3x faster on
-    B200 at [65536 x 640] x [640 x 1920].  A non-finite x or w entry gives NaN
-    where fp32 may give +-inf.  No autograd (``LinearTF32x3Function`` adds it)."""
+    B200 at [65536 x 640] x [640 x 1920].  With K a multiple of 4 the parts
+    are row-concatenated (``split_tf32_cat``) and the two correction products
+    run as one GEMM of depth 2K; else three GEMMs.  (One GEMM of depth 3K for
+    all three products measured ~1e-5 relative: the tensor cores' accumulation
+    drops bits of the small terms beside the large one.)  A non-finite x or w
+    entry gives NaN where fp32 may give +-inf.  No autograd
+    (``LinearTF32x3Function`` adds it)."""
     K = x.shape[-1]
+    if K % 4 == 0:
+        y = _linear2cat(split_tf32_cat(x.reshape(-1, K), 2, 2), split_tf32_cat(w, 2, 1), b)
+        return y.reshape(*x.shape[:-1], w.shape[0])
     xh, xl = split_tf32(x.reshape(-1, K))
     wh, wl = split_tf32(w)
     return _linear3(xh, xl, wh, wl, b).reshape(*x.shape[:-1], w.shape[0])
@@ -902,29 +938,53 @@ def linear_tf32x3(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = 
 class LinearTF32x3Function(torch.autograd.Function):
     """``linear_tf32x3`` with its backward in the same form: dx = dy @ w and
     dw = dy^T @ x as 3xTF32 GEMMs, db = the column sums of dy.  The forward's
-    split parts of x and w are kept for the backward (x's parts instead of x:
-    twice its bytes, one read and two writes of x fewer per step)."""
+    split parts of x and w are kept for the backward.  With K and N multiples
+    of 4 the parts are row-concatenated: the forward and dx each take a hi.hi
+    GEMM and one GEMM of depth 2K / 2N for the two corrections (dw, a small
+    output, three GEMMs on views of the parts)."""
 
     @staticmethod
     def forward(ctx, x, w, b):
-        K = x.shape[-1]
+        K, N = x.shape[-1], w.shape[0]
+        ctx.x_shape = x.shape
+        ctx.has_bias = b is not None
+        ctx.cat = K % 4 == 0 and N % 4 == 0
+        if ctx.cat:
+            A = split_tf32_cat(x.reshape(-1, K), 2, 2)      # [xh | xl]
+            Bm = split_tf32_cat(w, 2, 1)                    # [wl | wh]
+            ctx.save_for_backward(A, Bm)
+            return _linear2cat(A, Bm, b).reshape(*x.shape[:-1], N)
         xh, xl = split_tf32(x.reshape(-1, K))
         wh, wl = split_tf32(w)
         ctx.save_for_backward(xh, xl, wh, wl)
-        ctx.x_shape = x.shape
-        ctx.has_bias = b is not None
-        return _linear3(xh, xl, wh, wl, b).reshape(*x.shape[:-1], w.shape[0])
+        return _linear3(xh, xl, wh, wl, b).reshape(*x.shape[:-1], N)
 
     @staticmethod
     def backward(ctx, dy):
-        xh, xl, wh, wl = ctx.saved_tensors
-        N = wh.shape[0]
-        gh, gl = split_tf32(dy.reshape(-1, N))
+        K = ctx.x_shape[-1]
         dx = dw = db = None
-        if ctx.needs_input_grad[0]:
-            dx = _mm3(gh, gl, wh, wl).reshape(ctx.x_shape)
-        if ctx.needs_input_grad[1]:
-            dw = _mm3(gh.t(), gl.t(), xh, xl)
+        if ctx.cat:
+            A, Bm = ctx.saved_tensors
+            N = Bm.shape[0]
+            xh, xl, wl, wh = A[:, :K], A[:, K:], Bm[:, :K], Bm[:, K:]
+            G = split_tf32_cat(dy.reshape(-1, N), 2, 2)     # [gh | gl]
+            gh, gl = G[:, :N], G[:, N:]
+            if ctx.needs_input_grad[0]:
+                Bw = torch.cat((wl, wh), 0)                  # [wl; wh]: gh.wl + gl.wh
+                with _tf32_matmuls():
+                    dx = gh @ wh
+                    dx.addmm_(G, Bw)
+                dx = dx.reshape(ctx.x_shape)
+            if ctx.needs_input_grad[1]:
+                dw = _mm3(gh.t(), gl.t(), xh, xl)
+        else:
+            xh, xl, wh, wl = ctx.saved_tensors
+            N = wh.shape[0]
+            gh, gl = split_tf32(dy.reshape(-1, N))
+            if ctx.needs_input_grad[0]:
+                dx = _mm3(gh, gl, wh, wl).reshape(ctx.x_shape)
+            if ctx.needs_input_grad[1]:
+                dw = _mm3(gh.t(), gl.t(), xh, xl)
         if ctx.has_bias and ctx.needs_input_grad[2]:
             db = dy.reshape(-1, N).sum(0)
         return dx, dw, db

@@ -108,3 +108,34 @@ def test_matmul_helpers(cuda):
                      (ops.matmul_tn_tf32x3(a, c), a.double().T @ c.double())):
         err = ((got.double() - ref).abs().max() / ref.abs().max()).item()
         assert err < 1e-5, err
+
+
+@pytest.mark.parametrize("R,C", [(1, 4), (37, 640), (4099, 1920)])
+def test_split_cat_parts(cuda, R, C):
+    ops = _ops()
+    g = torch.Generator(device=cuda).manual_seed(R + C)
+    x = torch.randn(R, C, device=cuda, generator=g) * 100.0
+    x[0, 0] = float("inf")
+    hi, lo = ops.split_tf32(x)
+    for nparts in (1, 2, 3):
+        for mask in range(1 << nparts):
+            out = ops.split_tf32_cat(x, nparts, mask)
+            assert out.shape == (R, nparts * C)
+            for part in range(nparts):
+                want = lo if (mask >> part) & 1 else hi
+                assert torch.equal(out[:, part * C:(part + 1) * C], want)
+
+
+@pytest.mark.parametrize("M,K,N", [(5000, 640, 324), (5000, 640, 320), (4099, 320, 640)])
+def test_linear_forms_agree(cuda, M, K, N):
+    # K a multiple of 4: hi.hi and the two corrections as one GEMM of depth 2K;
+    # three GEMMs otherwise -- both within 1e-5 of float64 (fp32 SGEMM: ~1e-6)
+    ops = _ops()
+    g = torch.Generator(device=cuda).manual_seed(M + K + N)
+    x = torch.randn(M, K, device=cuda, generator=g)
+    w = torch.randn(N, K, device=cuda, generator=g) / K ** 0.5
+    ref = x.double() @ w.double().T
+    xh, xl = ops.split_tf32(x)
+    wh, wl = ops.split_tf32(w)
+    for y in (ops.linear_tf32x3(x, w), ops._linear3(xh, xl, wh, wl, None)):
+        assert ((y.double() - ref).abs().max() / ref.abs().max()).item() < 5e-6
