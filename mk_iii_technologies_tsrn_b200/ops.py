@@ -863,9 +863,19 @@ def _mm3(ah, al, bh, bl):
 
 def matmul_tf32x3(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """``a @ b`` (2-D fp32 CUDA tensors) at fp32 accuracy on the TF32 tensor cores:
-    both split into TF32 hi and lo parts, three GEMMs (hi.hi + hi.lo + lo.hi)."""
-    ah, al = split_tf32(a)
+    both split into TF32 hi and lo parts, hi.hi + hi.lo + lo.hi.  With a's
+    width a multiple of 4 the two corrections are one GEMM of depth 2K on
+    [ah | al] and [bl; bh] (the output read and written once for both), else
+    three GEMMs."""
+    K = a.shape[1]
     bh, bl = split_tf32(b)
+    if K % 4 == 0:
+        A = split_tf32_cat(a, 2, 2)                         # [ah | al]
+        with _tf32_matmuls():
+            y = A[:, :K] @ bh
+            y.addmm_(A, torch.cat((bl, bh), 0))
+        return y
+    ah, al = split_tf32(a)
     return _mm3(ah, al, bh, bl)
 
 

@@ -57,8 +57,10 @@ class GRUReservoirFunction(torch.autograd.Function):
         Hp = _previous_states(H)
         flat = lambda t: t.reshape(B * T, dr)   # noqa: E731
         # every step's gates at once (fp32-accurate 3xTF32 GEMMs)
-        z = torch.sigmoid(ops.matmul_tf32x3(flat(Hp), Wzh.t()).view(B, T, dr) + Uz)
-        r = torch.sigmoid(ops.matmul_tf32x3(flat(Hp), Wrh.t()).view(B, T, dr) + Ur)
+        # both gates' recurrent terms from one product with the stacked weights
+        hz, hr = ops.matmul_tf32x3(flat(Hp), torch.cat((Wzh, Wrh), 0).t()).split(dr, dim=1)
+        z = torch.sigmoid(hz.reshape(B, T, dr) + Uz)
+        r = torch.sigmoid(hr.reshape(B, T, dr) + Ur)
         m = r * Hp
         hc = torch.tanh(ops.matmul_tf32x3(flat(m), Ws.t()).view(B, T, dr) + U)
         # per-step factors, all steps at once
