@@ -35,7 +35,9 @@
 //      no winner passes the entering carry through its L rounded adds of g
 //      (in order, exact).  gh0 is the carry leaving chunk 0.
 //   C. output: every chunk reruns its reverse walk from its exact entering
-//      carry and writes gu -- bit-exact -- and its partial sum of the lost
+//      carry (from b, x, h: on the winners pass A recomputed and stored as
+//      mask words, one bit per element read instead of b, x and h again)
+//      and writes gu -- bit-exact -- and its partial sum of the lost
 //      gradients; ga sums the partials (ascending batch, descending chunk),
 //      an order that differs from one sequential sum over T: ga agrees with
 //      the sequential kernel to rounding, gu and gh0 bit for bit.
@@ -88,6 +90,7 @@ struct ChunkArgs {
   float* gap;
   int* tflag;                      // 1: no input won in the chunk
   int* err;                        // device status block (bounded waits)
+  uint32_t* wmask;                 // backward from b, x, h: pass A's winners [B, nw, C]
 };
 
 template <int V>
@@ -406,8 +409,12 @@ constexpr int kWalkGroup = 64;   // values read together by the ga reduction
 // whether an input won in it) and pass C (kOut = true: from the exact
 // entering carry, writing gu and the chunk's partial ga)
 // ---------------------------------------------------------------------------
-template <int V, bool kMask, bool kHasX, bool kOut>
+// kSave (pass A from b, x, h): the winners it recomputes are also stored as
+// mask words (p.wmask, the forward's layout), so that pass C reads gh and the
+// mask instead of gh, b, x and h again.
+template <int V, bool kMask, bool kHasX, bool kOut, bool kSave = false>
 __global__ void __launch_bounds__(kPassThreads) chunk_bwd_kernel(const ChunkArgs p) {
+  static_assert(!kSave || (!kMask && !kOut), "pass A from b, x, h saves the winners");
   Slot s;
   if (!slot_of<V>(p, s)) return;
   const int64_t o = (s.b * p.nch + s.j) * p.C + s.c;
@@ -433,7 +440,9 @@ __global__ void __launch_bounds__(kPassThreads) chunk_bwd_kernel(const ChunkArgs
   }
   const int64_t base = (s.b * p.T + s.t0) * p.C + s.c;
   const uint64_t pol = l2_policy(!kOut);
-  uint32_t word[V];
+  uint32_t word[V], wbits[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) wbits[v] = 0u;
   int cur_w = -1;
   auto step_row = [&](int t, const float (&g)[V], const float (&u)[V], const float (&hp)[V]) {
     if (kMask) {
@@ -455,8 +464,14 @@ __global__ void __launch_bounds__(kPassThreads) chunk_bwd_kernel(const ChunkArgs
       part[v] += lost;
       carry[v] = lost;
       any[v] |= win;
+      if (kSave) wbits[v] |= (uint32_t)win << ((s.t0 + t) & 31);
     }
     if (kOut) stv_stream<V>(p.gu + base + (int64_t)t * p.C, out);
+    if (kSave && ((s.t0 + t) & 31) == 0) {   // the word's lowest row: it is complete
+      stw<V>(p.wmask + (s.b * p.nw + (s.t0 + t) / 32) * p.C + s.c, wbits);
+#pragma unroll
+      for (int v = 0; v < V; ++v) wbits[v] = 0u;
+    }
   };
   constexpr int kRowBlock = row_block<V>();
   int t = s.rows - 1;
@@ -765,7 +780,8 @@ int64_t scan_chunked_workspace_bytes(int64_t B, int64_t T, int64_t C, int chunk)
   if (B <= 0 || T <= 0 || C <= 0) return 0;
   const int L = chunk > 0 ? chunk : scan_chunk_pick(B, T, C);
   const int64_t plane = B * ceil_div(T, L) * C;
-  return 4 * align256(plane * 4);
+  const int64_t mask = B * ceil_div(T, (int64_t)32) * C;      // uint32 words
+  return 4 * align256(plane * 4) + align256(mask * 4);
 }
 
 static int prepare(ChunkArgs& p, int chunk, void* ws, int64_t ws_bytes) {
@@ -782,9 +798,11 @@ static int prepare(ChunkArgs& p, int chunk, void* ws, int64_t ws_bytes) {
   float* f1 = reinterpret_cast<float*>(w + align256(plane * 4));
   float* f2 = reinterpret_cast<float*>(w + 2 * align256(plane * 4));
   int* i0 = reinterpret_cast<int*>(w + 3 * align256(plane * 4));
-  // forward: beta, hs; backward: cout, cin, gap, tflag
+  // forward: beta, hs; backward: cout, cin, gap, tflag (+ the winners' mask
+  // when they are recomputed from b, x, h)
   p.beta = f0;
   p.hs = f1;
+  p.wmask = reinterpret_cast<uint32_t*>(w + 4 * align256(plane * 4));
   p.err = device_error_ptr();
   p.cout = f0;
   p.cin = f1;
@@ -868,13 +886,17 @@ int launch_scan_bwd_chunked(const ScanArgs& q, int chunk, void* ws, int64_t ws_b
   const int64_t slots = p.B * p.nch * (p.C / (v4 ? 4 : 1));
   const unsigned g1 = blocks_for(slots, kPassThreads);
   const bool hx = !mk && p.xx != nullptr;
-#define TP_BWD(VV, OUT)                                                              \
-  do {                                                                               \
-    if (mk) chunk_bwd_kernel<VV, true, false, OUT><<<g1, kPassThreads, 0, stream>>>(p);       \
-    else if (hx) chunk_bwd_kernel<VV, false, true, OUT><<<g1, kPassThreads, 0, stream>>>(p);  \
-    else chunk_bwd_kernel<VV, false, false, OUT><<<g1, kPassThreads, 0, stream>>>(p);         \
+  // pass A; from b, x, h it also saves the winners, which pass C then reads
+  // as a mask (one bit per element instead of three fp32 values)
+#define TP_BWD_A(VV)                                                                          \
+  do {                                                                                        \
+    if (mk) chunk_bwd_kernel<VV, true, false, false><<<g1, kPassThreads, 0, stream>>>(p);     \
+    else if (hx)                                                                              \
+      chunk_bwd_kernel<VV, false, true, false, true><<<g1, kPassThreads, 0, stream>>>(p);     \
+    else chunk_bwd_kernel<VV, false, false, false, true><<<g1, kPassThreads, 0, stream>>>(p); \
   } while (0)
-  if (v4) TP_BWD(4, false); else TP_BWD(1, false);
+  if (v4) TP_BWD_A(4); else TP_BWD_A(1);
+#undef TP_BWD_A
   if ((s = launch_status()) != TP_OK) return s;
   {
     const int64_t cgroups = ceil_div(p.C, 32);
@@ -893,8 +915,12 @@ int launch_scan_bwd_chunked(const ScanArgs& q, int chunk, void* ws, int64_t ws_b
       chunk_bwd_carry_kernel<<<blocks_for(p.B * p.C, 32), 32, 0, stream>>>(p);
   }
   if ((s = launch_status()) != TP_OK) return s;
-  if (v4) TP_BWD(4, true); else TP_BWD(1, true);
-#undef TP_BWD
+  {
+    ChunkArgs pc = p;
+    if (!mk) pc.win_in = p.wmask;
+    if (v4) chunk_bwd_kernel<4, true, false, true><<<g1, kPassThreads, 0, stream>>>(pc);
+    else chunk_bwd_kernel<1, true, false, true><<<g1, kPassThreads, 0, stream>>>(pc);
+  }
   if ((s = launch_status()) != TP_OK) return s;
   if (p.ga) {
     chunk_ga_reduce_kernel<<<blocks_for(p.C, 128), 128, 0, stream>>>(p);
